@@ -1,0 +1,418 @@
+"""Generate golden fixtures by running the reference G2PTQ code on CPU.
+
+Usage (needs a checkout of the reference; not available on GPU boxes)::
+
+    python tests/golden/make_golden.py --reference <path-to-G2PTQ-checkout>
+
+The reference's quantizer modules import third-party packages that are not
+installed here (fast_hadamard_transform, llmcompressor, accelerate and
+compressed_tensors.distributed).  None of them takes part in the arithmetic
+captured below, so they are replaced by empty module stubs.  The CUDA-only
+tensor validator and ``torch.cuda.synchronize`` are neutralised and the
+shared-offload write-back is replaced by a plain ``weight.data.copy_`` so the
+reference's torch path runs unchanged on CPU.
+
+Each fixture file holds the inputs and the reference's outputs for one family
+of calls; ``tests/test_oracle_golden.py`` replays the inputs through the numpy
+oracle and the GPU tests replay them through the CUDA library.
+"""
+
+import argparse
+import contextlib
+import copy
+import importlib.machinery
+import os
+import sys
+import types
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _stub(name, **attrs):
+    m = types.ModuleType(name)
+    m.__spec__ = importlib.machinery.ModuleSpec(name, None)
+    m.__dict__.update(attrs)
+    sys.modules[name] = m
+    return m
+
+
+def import_reference(root):
+    sys.path.insert(0, root)
+    import transformers  # noqa: F401  (must precede the llmcompressor stubs)
+    _stub("fast_hadamard_transform", hadamard_transform=lambda *a, **k: None)
+    _stub("compressed_tensors.distributed", greedy_bin_packing=None,
+          wait_for_comms=lambda c: [x.wait() for x in c],
+          is_distributed=lambda: False, is_source_process=lambda: True)
+    for n in ["llmcompressor", "llmcompressor.utils", "llmcompressor.modeling",
+              "llmcompressor.modeling.moe"]:
+        _stub(n)
+    _stub("llmcompressor.utils.dev", skip_weights_initialize=None)
+    _stub("llmcompressor.modeling.moe.conversion_mappings", ARCH_TO_2D_MAPPINGS={},
+          get_linearize_load_mappings=None, has_linearize_load_mappings=None,
+          set_save_conversion_mapping=None)
+    _stub("llmcompressor.modeling.moe.linear_experts", LinearExperts2D=None)
+    _stub("llmcompressor.modeling.moe.linearize", linearize_moe=None)
+    _stub("accelerate", dispatch_model=None, infer_auto_device_map=None)
+    _stub("accelerate.utils", get_balanced_memory=None)
+    import compressed_tensors.offload.utils as _u
+    import compressed_tensors.offload.load as _l
+    _u.as_single_threaded = getattr(_u, "as_single_threaded", contextlib.nullcontext)
+    for n in ["_get_cpu_memory", "_get_device_memory", "_estimate_tensor_count"]:
+        if not hasattr(_l, n):
+            setattr(_l, n, None)
+    from utils import dist_utils  # noqa: F401
+    from gptq_utils import gptq_utils, g2ptq_utils, gptaq_utils, gptq_guided_utils
+    from utils import quant_utils, offload_utils
+    torch.cuda.synchronize = lambda *a, **k: None
+    offload_utils.update_shared_offload_parameter = (
+        lambda layer, name, data, **k: layer.weight.data.copy_(data))
+    for m in (gptq_utils, g2ptq_utils, gptaq_utils, gptq_guided_utils):
+        m.validate_tensors = lambda *a, **k: None
+        m.offload_utils = offload_utils
+    return types.SimpleNamespace(gptq=gptq_utils, g2ptq=g2ptq_utils, gptaq=gptaq_utils,
+                                 guided=gptq_guided_utils, quant=quant_utils)
+
+
+def npy(t):
+    return t.detach().cpu().numpy().copy()
+
+
+def save(name, **arrays):
+    path = os.path.join(HERE, name)
+    np.savez_compressed(path, **arrays)
+    print("wrote", path, sum(a.nbytes for a in arrays.values()) // 1024, "KB")
+
+
+def activations(gen, shape, outliers=(), outlier_scale=20.0):
+    x = torch.randn(shape, generator=gen)
+    for c in outliers:
+        x[..., c] *= outlier_scale
+    return x
+
+
+# ---------------------------------------------------------------------------
+# add_batch families
+# ---------------------------------------------------------------------------
+
+def gen_hessians(ref):
+    gen = torch.Generator().manual_seed(43)
+    C, R = 96, 32
+    out = {}
+    # GPTQ: three 3-D calls (b=1,2,1) then one 2-D call; BF16 and FP32 inputs.
+    for tag, dtype in (("f32", torch.float32), ("bf16", torch.bfloat16)):
+        lin = torch.nn.Linear(C, R, bias=False)
+        g = ref.gptq.GPTQ([lin])
+        calls = [activations(gen, (1, 40, C), outliers=(3, 50)),
+                 activations(gen, (2, 40, C), outliers=(3, 50)),
+                 activations(gen, (1, 24, C)),
+                 activations(gen, (56, C))]
+        for i, x in enumerate(calls):
+            x = x.to(dtype)
+            g.add_batch(0, x, None)
+            out[f"gptq_{tag}_x{i}"] = npy(x.float())
+        out[f"gptq_{tag}_H"] = npy(g.H[0])
+        out[f"gptq_{tag}_n"] = np.array(int(g.nsamples[0]))
+    # G2PTQ: per-call [t, C] input with [t, 4] saliency.
+    lin = torch.nn.Linear(C, R, bias=False)
+    sals = [torch.rand(48, 4, generator=gen) for _ in range(3)]
+    g2 = ref.g2ptq.G2PTQ([lin], [list(sals)], [torch.zeros(R, C)], num_groups=4)
+    for i in range(3):
+        x = activations(gen, (48, C), outliers=(7,))
+        g2.add_batch(0, x, None)
+        out[f"g2ptq_x{i}"] = npy(x)
+        out[f"g2ptq_s{i}"] = npy(sals[i])
+    out["g2ptq_H"] = npy(g2.H[0])
+    out["g2ptq_act_square"] = npy(g2.act_square[0])
+    out["g2ptq_index"] = np.array(int(g2.index[0]))
+    out["g2ptq_total_tokens"] = np.array(int(g2.total_tokens[0]))
+    # GPTAQ: quantized-path input plus FP input per call.
+    lin = torch.nn.Linear(C, R, bias=False)
+    ga = ref.gptaq.GPTAQ([lin])
+    for i in range(3):
+        x = activations(gen, (1, 32, C))
+        xf = x + 0.05 * torch.randn(x.shape, generator=gen)
+        ga.fp_inp[0].append(xf[0])
+        ga.add_batch(0, x, None)
+        out[f"gptaq_x{i}"] = npy(x)
+        out[f"gptaq_fp{i}"] = npy(xf)
+    out["gptaq_H"] = npy(ga.H[0])
+    out["gptaq_dXXT"] = npy(ga.dXXT[0])
+    out["gptaq_n"] = np.array(int(ga.nsamples[0]))
+    # GuidedQuant: saliency [N, S, G] sliced by index.
+    lin = torch.nn.Linear(C, R, bias=False)
+    sal = torch.rand(3, 16, 4, generator=gen)
+    gq = ref.guided.GPTQGuided([lin], [sal], num_groups=4)
+    xs = [activations(gen, (1, 16, C)), activations(gen, (2, 16, C))]
+    for i, x in enumerate(xs):
+        gq.add_batch(0, x, None)
+        out[f"guided_x{i}"] = npy(x)
+    out["guided_sal"] = npy(sal)
+    out["guided_H"] = npy(gq.H[0])
+    out["guided_act_square"] = npy(gq.act_square[0])
+    save("hessians.npz", **out)
+
+
+# ---------------------------------------------------------------------------
+# Compensation block kernels (the reference's kernel boundary ``run_eager``)
+# ---------------------------------------------------------------------------
+
+BLOCK_CASES = (
+    # name, batch, columns, rows, maxq, asymmetric, seed  (the reference's CASES)
+    ("symmetric_2bit_tail", 1, 7, 37, 1, False, 101),
+    ("asymmetric_2bit_tail", 1, 7, 37, 1, True, 102),
+    ("symmetric_4bit_batched", 2, 16, 193, 7, False, 201),
+    ("asymmetric_4bit_batched", 2, 16, 193, 7, True, 202),
+    ("symmetric_8bit_small", 3, 5, 11, 127, False, 301),
+    ("asymmetric_8bit_small", 3, 5, 11, 127, True, 302),
+    ("asymmetric_3bit_fullblock", 1, 128, 72, 3, True, 401),
+    ("symmetric_4bit_fullblock", 1, 128, 40, 7, False, 402),
+)
+
+
+def block_inputs(batch, columns, rows, maxq, asymmetric, seed):
+    """Same construction as the reference test fixture (away from ties)."""
+    gen = torch.Generator().manual_seed(seed)
+    shape = (batch, columns, rows)
+    minq = -(maxq + 1)
+    scale = torch.rand(shape, generator=gen).mul_(0.15).add_(0.05)
+    zero = (torch.randint(minq, maxq + 1, shape, generator=gen).float() if asymmetric
+            else torch.zeros(shape))
+    target = torch.randint(minq, maxq + 1, shape, generator=gen).float()
+    frac = torch.randint(0, 2, shape, generator=gen).float().mul_(0.5).sub_(0.25)
+    weight = (target - zero + frac) * scale
+    hinv = torch.triu(torch.randn(batch, columns, columns, generator=gen).mul_(0.002), 1)
+    torch.diagonal(hinv, dim1=1, dim2=2).copy_(
+        torch.rand(batch, columns, generator=gen).mul_(0.5).add_(0.75))
+    z = torch.randn(shape, generator=gen).mul_(scale * 0.002)
+    ghinv = torch.randn(shape, generator=gen).mul_(scale * 0.002)
+    p = torch.triu(torch.randn(batch, columns, columns, generator=gen).mul_(0.002), 1)
+    return weight, hinv, scale, zero, z, ghinv, p
+
+
+def gen_blocks(ref):
+    out = {}
+    for name, batch, columns, rows, maxq, asym, seed in BLOCK_CASES:
+        weight, hinv, scale, zero, z, ghinv, p = block_inputs(batch, columns, rows, maxq,
+                                                              asym, seed)
+        for k, v in (("weight", weight), ("hinv", hinv), ("scale", scale), ("zero", zero),
+                     ("z", z), ("ghinv", ghinv), ("p", p)):
+            out[f"{name}__{k}"] = npy(v)
+        out[f"{name}__maxq"] = np.array(maxq)
+        w, qi, err = weight.clone(), torch.empty_like(weight), torch.empty_like(weight)
+        ref.gptq._run_torch_compensation(w, hinv.clone(), scale, zero, qi, err, maxq)
+        out[f"{name}__gptq_q"], out[f"{name}__gptq_int"], out[f"{name}__gptq_err"] = \
+            npy(w), npy(qi), npy(err)
+        w, gh = weight.clone(), ghinv.clone()
+        qi, err = torch.empty_like(weight), torch.empty_like(weight)
+        ref.g2ptq._run_torch_compensation(w, hinv.clone(), scale, zero, z.clone(), gh, qi,
+                                          err, maxq)
+        out[f"{name}__g2ptq_q"], out[f"{name}__g2ptq_int"] = npy(w), npy(qi)
+        out[f"{name}__g2ptq_err"], out[f"{name}__g2ptq_ghinv"] = npy(err), npy(gh)
+        w = weight.clone()
+        cw = torch.empty(batch, rows)
+        qi, err = torch.empty_like(weight), torch.empty_like(weight)
+        ref.gptaq._run_torch_compensation(w, hinv.clone(), p.clone(), scale, zero, cw, qi,
+                                          err, maxq)
+        out[f"{name}__gptaq_q"], out[f"{name}__gptaq_int"], out[f"{name}__gptaq_err"] = \
+            npy(w), npy(qi), npy(err)
+    save("blocks.npz", **out)
+
+
+# ---------------------------------------------------------------------------
+# Whole fasterquant pipelines
+# ---------------------------------------------------------------------------
+
+FQ_CASES = (
+    # name, bits, sym, groupsize, actorder(=static_groups), B, R, C, blocksize
+    ("w4_sym_ungrouped", 4, True, -1, False, 2, 32, 160, 128),
+    ("w4_sym_g40_actorder", 4, True, 40, True, 1, 32, 160, 128),
+    ("w3_asym_g40_dynamic", 3, False, 40, False, 1, 32, 160, 64),
+    ("w2_asym_g64_dynamic", 2, False, 64, False, 1, 32, 192, 128),
+    ("w4_asym_g128_actorder", 4, False, 128, True, 1, 32, 256, 128),
+)
+
+
+def make_quantizers(ref, bits, sym, C, groupsize, mse=False, hclip=False):
+    q = ref.quant.WeightQuantizer()
+    q.configure(bits, perchannel=True, sym=sym, mse=mse, hclip=hclip)
+    from gptq_utils.common_utils import make_group_quantizers
+    return make_group_quantizers(q, C, groupsize)
+
+
+def hessian_from(gen, C, T, dead=()):
+    x = activations(gen, (T, C), outliers=(1, C // 2))
+    x[:, list(dead)] = 0
+    return x
+
+
+def gen_fasterquant(ref):
+    out = {}
+    gen = torch.Generator().manual_seed(42)
+    for name, bits, sym, gs, act, B, R, C, blk in FQ_CASES:
+        layers = [torch.nn.Linear(C, R, bias=False) for _ in range(B)]
+        for l in layers:
+            l.weight.data = torch.randn(R, C, generator=gen) * 0.02
+        W0 = torch.stack([l.weight.data.clone() for l in layers])
+        # -- GPTQ
+        g = ref.gptq.GPTQ(layers)
+        g.quantizer = make_quantizers(ref, bits, sym, C, gs)
+        xs = []
+        for b in range(B):
+            x = hessian_from(gen, C, 300, dead=(5,) if b == 0 else ())
+            xs.append(x)
+            g.add_batch(b, x.unsqueeze(0), None)
+        H = g.H.clone()
+        g.fasterquant(blocksize=blk, percdamp=0.01, groupsize=gs, actorder=act,
+                      static_groups=act)
+        out[f"{name}__W"] = npy(W0)
+        out[f"{name}__H"] = npy(H)
+        out[f"{name}__gptq_Q"] = npy(torch.stack([l.weight.data for l in layers]))
+        # capture codes/scales through the export staging hook
+        for l, w in zip(layers, W0):
+            l.weight.data = w.clone()
+        g = ref.gptq.GPTQ(layers)
+        g.quantizer = make_quantizers(ref, bits, sym, C, gs)
+        g.H = H.clone()
+        g.nsamples = torch.ones(B, dtype=torch.long)
+        cap = {}
+        orig = ref.gptq.compressed_tensors_utils.compress
+
+        def grab(layer, Scale, W_int, bits, groupsize, cap=cap):
+            cap.setdefault("Scale", []).append(Scale.clone())
+            cap.setdefault("W_int", []).append(W_int.clone())
+
+        ref.gptq.compressed_tensors_utils.compress = grab
+        try:
+            g.fasterquant(blocksize=blk, percdamp=0.01, groupsize=gs, actorder=act,
+                          static_groups=act, export_compressed_tensors=True)
+        finally:
+            ref.gptq.compressed_tensors_utils.compress = orig
+        out[f"{name}__gptq_W_int"] = npy(torch.stack(cap["W_int"]))
+        out[f"{name}__gptq_Scale"] = npy(torch.stack(cap["Scale"]))
+        # -- GPTAQ (same H, synthetic dXXT from a perturbed FP input)
+        for l, w in zip(layers, W0):
+            l.weight.data = w.clone()
+        ga = ref.gptaq.GPTAQ(layers)
+        ga.quantizer = make_quantizers(ref, bits, sym, C, gs)
+        for b in range(B):
+            xf = xs[b] + 0.05 * torch.randn(xs[b].shape, generator=gen)
+            ga.fp_inp[b].append(xf)
+            ga.add_batch(b, xs[b].unsqueeze(0), None)
+        assert torch.equal(ga.H, H), "GPTAQ H differs from GPTQ H on the same inputs"
+        out[f"{name}__gptaq_dXXT"] = npy(ga.dXXT)
+        ga.fasterquant(blocksize=blk, percdamp=0.01, groupsize=gs, actorder=act,
+                       static_groups=act)
+        out[f"{name}__gptaq_Q"] = npy(torch.stack([l.weight.data for l in layers]))
+        # -- G2PTQ (4 row groups, saliency-weighted Hessians, gradients, alpha 1.0)
+        for l, w in zip(layers, W0):
+            l.weight.data = w.clone()
+        G = 4
+        sal = [[torch.rand(300, G, generator=gen)] for _ in range(B)]
+        grads = [torch.randn(R, C, generator=gen) * 1e-3 for _ in range(B)]
+        g2 = ref.g2ptq.G2PTQ(layers, [list(s) for s in sal], grads, num_groups=G)
+        g2.quantizer = make_quantizers(ref, bits, sym, C, gs)
+        for b in range(B):
+            g2.add_batch(b, xs[b], None)
+        out[f"{name}__g2_sal"] = npy(torch.stack([s[0] for s in sal]))
+        out[f"{name}__g2_grad"] = npy(torch.stack(grads))
+        out[f"{name}__g2_H"] = npy(g2.H)
+        out[f"{name}__g2_act_square"] = npy(g2.act_square)
+        g2.fasterquant(blocksize=blk, percdamp=0.01, groupsize=gs, actorder=act,
+                       static_groups=act, enable_gradient_update=True, alpha=1.0)
+        out[f"{name}__g2ptq_Q"] = npy(torch.stack([l.weight.data for l in layers]))
+        # -- GuidedQuant
+        for l, w in zip(layers, W0):
+            l.weight.data = w.clone()
+        gsal = [torch.rand(1, 300, G, generator=gen) for _ in range(B)]
+        gq = ref.guided.GPTQGuided(layers, gsal, num_groups=G)
+        gq.quantizer = make_quantizers(ref, bits, sym, C, gs)
+        for b in range(B):
+            gq.add_batch(b, xs[b].unsqueeze(0), None)
+        out[f"{name}__guided_sal"] = npy(torch.stack(gsal))
+        out[f"{name}__guided_H"] = npy(gq.H)
+        out[f"{name}__guided_act_square"] = npy(gq.act_square)
+        gq.fasterquant(blocksize=blk, percdamp=0.01, groupsize=gs, actorder=act,
+                       static_groups=act)
+        out[f"{name}__guided_Q"] = npy(torch.stack([l.weight.data for l in layers]))
+    save("fasterquant.npz", **out)
+
+
+# ---------------------------------------------------------------------------
+# find_params, Cholesky chain, export packing
+# ---------------------------------------------------------------------------
+
+def gen_misc(ref):
+    from compressed_tensors.compressors import pack_to_int32
+    out = {}
+    gen = torch.Generator().manual_seed(44)
+    x = torch.randn(24, 64, generator=gen) * 0.02
+    x[3] = 0.0
+    x[3, 5] = 0.01
+    x[4] = x[4].abs()
+    out["fp_x"] = npy(x)
+    hd = torch.rand(4, 64, generator=gen) + 0.5
+    out["fp_hdiag"] = npy(hd)
+    for bits in (2, 3, 4, 8):
+        for sym in (True, False):
+            for mse, hclip in ((False, False), (True, False), (True, True)):
+                if mse and bits == 8:
+                    continue
+                q = ref.quant.WeightQuantizer()
+                q.configure(bits, perchannel=True, sym=sym, mse=mse, hclip=hclip)
+                q.find_params(x, hd.repeat_interleave(6, 0) if hclip else None)
+                tag = f"fp_b{bits}_{'sym' if sym else 'asym'}_{int(mse)}{int(hclip)}"
+                out[tag + "_scale"] = npy(q.scale)
+                out[tag + "_zero"] = npy(q.zero)
+                fq, qi, _ = q.fake_quantize(x)
+                out[tag + "_fq"] = npy(fq)
+                out[tag + "_q"] = npy(qi)
+    # Cholesky chain: a well-conditioned H and a rank-deficient one that
+    # needs the damp auto-increment.
+    for tag, T in (("pd", 400), ("lowrank", 12)):
+        xx = torch.randn(T, 80, generator=gen)
+        H = (2 / T) * xx.t() @ xx
+        if tag == "lowrank":
+            H[7, :] = 0
+            H[:, 7] = 0
+            H -= 1e-3 * torch.eye(80) * H.diag().mean()
+        out[f"chol_{tag}_H"] = npy(H)
+        damp = 0.01
+        while 1 > damp > 0:
+            try:
+                Ht = H.clone()
+                Ht.diagonal().add_(damp * torch.mean(torch.diag(H)))
+                L = torch.linalg.cholesky(Ht)
+                Hinv = torch.cholesky_inverse(L)
+                U = torch.linalg.cholesky(Hinv, upper=True)
+                if torch.isnan(U).any():
+                    raise torch._C._LinAlgError
+                break
+            except torch._C._LinAlgError:
+                damp += 0.0015
+        out[f"chol_{tag}_U"] = npy(U)
+        out[f"chol_{tag}_damp"] = np.array(damp)
+    for bits in (2, 3, 4, 8):
+        lo, hi = -(2 ** (bits - 1)), 2 ** (bits - 1) - 1
+        codes = torch.randint(lo, hi + 1, (6, 37), generator=gen).to(torch.int8)
+        out[f"pack_b{bits}_codes"] = npy(codes)
+        out[f"pack_b{bits}_packed"] = npy(pack_to_int32(codes, bits))
+    save("misc.npz", **out)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", required=True, help="path of the reference checkout")
+    args = ap.parse_args()
+    torch.set_num_threads(min(8, os.cpu_count() or 1))
+    ref = import_reference(os.path.abspath(args.reference))
+    gen_hessians(ref)
+    gen_blocks(ref)
+    gen_fasterquant(ref)
+    gen_misc(ref)
+
+
+if __name__ == "__main__":
+    main()
