@@ -1,0 +1,465 @@
+"""Benchmark of the per-layer quantization hot path (see the driver contract).
+
+Workload: one Llama-3-8B decoder layer -- q/k/v/o/gate/up/
+down linears (4096x4096, 1024x4096 x2, 4096x4096, 14336x4096 x2, 4096x14336),
+GPTQ W4 symmetric, group 128, damp 0.01, act-order with static groups,
+compressed-tensors export on, calibrated on 128 sequences x 2048 tokens.  One
+step = every ``add_batch`` call of the calibration pass (one per sequence and
+linear, ``--bsz 1``) followed by ``fasterquant`` of all seven linears.
+Activations are seeded synthetic BF16 hidden states N(0, 1) with 4 outlier
+channels x20 per linear input (the stand-in for the model forward over
+uniform random token ids); weights are random N(0, 0.02) BF16.
+
+Metric: linear layers quantized per second (whole job); ``config`` also
+reports the implied end-to-end calibration seconds of the 32-layer model.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl native|reference]
+"""
+
+import argparse
+import json
+import os
+import subprocess
+import threading
+import time
+
+import numpy as np
+
+HIDDEN, INTER, HEADS, KV_HEADS, HEAD_DIM, N_LAYERS = 4096, 14336, 32, 8, 128, 32
+LINEARS = [  # name, rows, columns, input group
+    ("self_attn.q_proj", HEADS * HEAD_DIM, HIDDEN, "attn"),
+    ("self_attn.k_proj", KV_HEADS * HEAD_DIM, HIDDEN, "attn"),
+    ("self_attn.v_proj", KV_HEADS * HEAD_DIM, HIDDEN, "attn"),
+    ("self_attn.o_proj", HIDDEN, HEADS * HEAD_DIM, "o"),
+    ("mlp.gate_proj", INTER, HIDDEN, "mlp"),
+    ("mlp.up_proj", INTER, HIDDEN, "mlp"),
+    ("mlp.down_proj", HIDDEN, INTER, "down"),
+]
+GROUP_COLS = {"attn": HIDDEN, "o": HEADS * HEAD_DIM, "mlp": HIDDEN, "down": INTER}
+BITS, GROUPSIZE, PERCDAMP, BLOCKSIZE = 4, 128, 0.01, 128
+METRIC = "linear layers quantized/sec"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="native", choices=["native", "reference"])
+    ap.add_argument("--seqs", type=int, default=128)
+    ap.add_argument("--seq-len", type=int, default=2048)
+    ap.add_argument("--precision", type=int, default=None,
+                    help="0: fp32 CUDA-core products, 1: tcgen05 tensor cores")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def load_peaks():
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return p["hbm_gbs"], p["bf16_tflops"], "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle samples during the timed region."""
+
+    def __init__(self, index):
+        self.index = index
+        self.samples = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def start(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+
+    def _run(self):
+        q = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
+                                      "--format=csv,noheader,nounits"], capture_output=True,
+                                     text=True, timeout=5).stdout.strip()
+                if out:
+                    self.samples.append([x.strip() for x in out.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def stop(self):
+        self._stop.set()
+        if self._t:
+            self._t.join(timeout=10)
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
+        mx = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4)
+                          if len(s) > 2 + i and s[2 + i].lower() == "active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------
+# native arm
+# ---------------------------------------------------------------------------
+
+def make_inputs(torch, dev, rank, world, seqs, seq_len):
+    """Per-rank shard of the calibration activations (the reference splits the
+    calibration set by rank, gptq_utils/main.py:32-37)."""
+    lo, hi = seqs * rank // world, seqs * (rank + 1) // world
+    n = hi - lo
+    g = torch.Generator(device=dev).manual_seed(43 + rank)
+    acts = {}
+    for grp, C in GROUP_COLS.items():
+        out = torch.empty(n, seq_len, C, device=dev, dtype=torch.bfloat16)
+        idx = torch.randperm(C, device=dev, generator=g)[:4]
+        for s in range(0, n, 8):
+            x = torch.randn(min(8, n - s), seq_len, C, device=dev, generator=g)
+            x[..., idx] *= 20.0
+            out[s:s + 8] = x.to(torch.bfloat16)
+        acts[grp] = out
+    return acts, n
+
+
+def make_layers(torch, dev):
+    g = torch.Generator(device=dev).manual_seed(42)
+    layers = {}
+    for name, rows, cols, _ in LINEARS:
+        lin = torch.nn.Linear(cols, rows, bias=False, device=dev, dtype=torch.bfloat16)
+        lin.weight.data = (torch.randn(rows, cols, device=dev, generator=g) * 0.02).to(
+            torch.bfloat16)
+        layers[name] = lin
+    return layers
+
+
+def one_step(torch, layers, acts, n_local, world, rank, dist, obj2rank=None, h2d=None):
+    """add_batch over the rank's sequences, reduce to owners, fasterquant, broadcast."""
+    from g2ptq_b200.gptq_utils import gptq_utils, common_utils
+    from g2ptq_b200.utils.quant_utils import WeightQuantizer
+    objs = {}
+    for name, rows, cols, grp in LINEARS:
+        obj = gptq_utils.GPTQ([layers[name]])
+        q = WeightQuantizer()
+        q.configure(BITS, perchannel=True, sym=True, mse=False)
+        obj.quantizer = common_utils.make_group_quantizers(q, cols, GROUPSIZE)
+        objs[name] = obj
+    for s in range(n_local):
+        xs = acts(s) if callable(acts) else {g: acts[g][s:s + 1] for g in acts}
+        for name, rows, cols, grp in LINEARS:
+            objs[name].add_batch(0, xs[grp], None)
+    owners = objs
+    if world > 1:
+        specs = list(objs.values())
+        _, _, obj2rank = common_utils.partition_layers(specs, world)
+        gptq_utils.reduce_to_target_rank(specs, obj2rank)
+        owners = {k: o for k, o in objs.items() if obj2rank[o] == rank}
+    for name, obj in owners.items():
+        obj.fasterquant(blocksize=BLOCKSIZE, percdamp=PERCDAMP, groupsize=GROUPSIZE,
+                        actorder=True, static_groups=True, export_compressed_tensors=True)
+    if world > 1:
+        common_utils.broadcast_quantized_param(list(objs.values()), obj2rank,
+                                               export_compressed_tensors=True)
+    for o in objs.values():
+        o.free()
+    return objs
+
+
+class GramTimer:
+    """CUDA-event time and algorithmic flops of every Hessian (Gram) launch."""
+
+    def __init__(self, torch):
+        self.torch = torch
+        self.events = []
+        self.flops = 0.0
+
+    def install(self):
+        from g2ptq_b200 import ops
+        orig = ops.gram_update
+        timer = self
+
+        def timed(D, A, B=None, row_scale=None, alpha=1.0, beta=1.0, symmetric=None,
+                  precision=0):
+            s = timer.torch.cuda.Event(enable_timing=True)
+            e = timer.torch.cuda.Event(enable_timing=True)
+            s.record()
+            orig(D, A, B, row_scale, alpha, beta, symmetric, precision)
+            e.record()
+            T, M = A.shape
+            N = (B if B is not None else A).shape[1]
+            sym = symmetric if symmetric is not None else (B is None or B is A)
+            # algorithmic work: T*C*(C+1) for the symmetric update, 2*T*M*N otherwise
+            timer.flops += T * M * (M + 1) if sym else 2.0 * T * M * N
+            timer.events.append((s, e))
+
+        ops.gram_update = timed
+        self._orig = orig
+
+    def uninstall(self):
+        from g2ptq_b200 import ops
+        ops.gram_update = self._orig
+
+    def total_ms(self):
+        return sum(s.elapsed_time(e) for s, e in self.events)
+
+
+def native(args):
+    import torch
+    import torch.distributed as dist
+    from g2ptq_b200 import _lib
+    from g2ptq_b200.gptq_utils import _engine
+    if args.precision is not None:
+        _engine.PRECISION = args.precision
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=dev)
+    lib = _lib.load()
+    layers = make_layers(torch, dev)
+    acts, n_local = make_inputs(torch, dev, rank, world, args.seqs, args.seq_len)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        one_step(torch, layers, acts, n_local, world, rank, dist)
+    barrier()
+    timer = GramTimer(torch)
+    timer.install()
+    clocks = ClockSampler(local)
+    clocks.start()
+    launches0 = lib.g2q_launch_count()
+    barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        one_step(torch, layers, acts, n_local, world, rank, dist)
+    t1.record()
+    barrier()
+    clk = clocks.stop()
+    timer.uninstall()
+    launches = lib.g2q_launch_count() - launches0
+    ms = t0.elapsed_time(t1) / args.steps
+    if world > 1:
+        m = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(m, op=dist.ReduceOp.MAX)
+        ms = float(m.item())
+    gram_ms = timer.total_ms() / args.steps
+    gram_tflops = timer.flops / args.steps / (gram_ms * 1e-3) / 1e12 if gram_ms > 0 else 0.0
+
+    e2e = None
+    if not args.no_e2e:
+        e2e = native_e2e(torch, dist, args, layers, world, rank, dev, n_local, acts)
+    del acts
+    hbm, bf16, peak_kind = load_peaks()
+    value = len(LINEARS) / (ms * 1e-3)
+    line = {
+        "metric": METRIC, "value": round(value, 4), "unit": "linears/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16-in/f32", "data": "synthetic",
+        "config": {
+            "workload": "Llama-3-8B decoder layer (7 linears) GPTQ W4 sym g128 act-order, "
+                        f"{args.seqs}x{args.seq_len} calibration tokens",
+            "parallelism": f"tokens dp{world} + linear ownership (LPT)",
+            "calibration_seconds_32_layers": round(N_LAYERS * ms * 1e-3, 3),
+            "precision": "tcgen05" if _engine.PRECISION == 1 else "fp32-cuda-core",
+            "l2": "inputs larger than L2 (GBs of activations per step)",
+        },
+        "gpu_launches": int(launches // args.steps) * args.steps,
+        "clocks": clk,
+        "roofline": {
+            "kernel": "Hessian Gram update (g2q_gram_update)",
+            "bound": "tensor", "achieved": round(gram_tflops, 2),
+            "peak": bf16, "unit": "TFLOP/s",
+            "frac": round(gram_tflops / bf16, 4), "traffic": None,
+            "peak_kind": f"{peak_kind} bf16 dense",
+            "share_of_step": round(gram_ms / ms, 3) if ms else None,
+        },
+    }
+    if e2e is not None:
+        line["e2e"] = e2e
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def native_e2e(torch, dist, args, layers, world, rank, dev, n_local, dev_acts):
+    """Same steps through the public API with host-resident inputs: every step
+    copies its activations from pinned host memory (double-buffered on a side
+    stream, as the reference's prefetch_generator overlaps its H2D copies) and
+    reads the quantized weights and packed codes back to the host."""
+    host = {grp: torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
+            for grp, x in dev_acts.items()}
+    for grp in host:
+        host[grp].copy_(dev_acts[grp])
+    side = torch.cuda.Stream(device=dev)
+    bufs = [{grp: torch.empty(1, args.seq_len, C, dtype=torch.bfloat16, device=dev)
+             for grp, C in GROUP_COLS.items()} for _ in range(2)]
+    ready = [torch.cuda.Event() for _ in range(2)]
+    free_ev = [torch.cuda.Event() for _ in range(2)]
+    h2d_bytes = sum(h.numel() * h.element_size() for h in host.values())
+    outs = {name: torch.empty(rows, cols, dtype=torch.bfloat16, pin_memory=True)
+            for name, rows, cols, _ in LINEARS}
+    packed = {name: torch.empty(rows, cols * BITS // 32, dtype=torch.int32, pin_memory=True)
+              for name, rows, cols, _ in LINEARS}
+
+    def prefetch(s):
+        k = s & 1
+        with torch.cuda.stream(side):
+            side.wait_event(free_ev[k])
+            for grp in GROUP_COLS:
+                bufs[k][grp].copy_(host[grp][s:s + 1], non_blocking=True)
+            ready[k].record(side)
+
+    def step():
+        prefetch(0)
+        state = {"prev": None}
+
+        def feed(s):
+            if state["prev"] is not None:
+                free_ev[state["prev"] & 1].record()  # previous buffer's users are enqueued
+            state["prev"] = s
+            torch.cuda.current_stream().wait_event(ready[s & 1])
+            if s + 1 < n_local:
+                prefetch(s + 1)
+            return bufs[s & 1]
+
+        one_step(torch, layers, feed, n_local, world, rank, dist)
+        free_ev[state["prev"] & 1].record()
+        d2h = 0
+        for name, rows, cols, _ in LINEARS:
+            outs[name].copy_(layers[name].weight.data, non_blocking=True)
+            qp = layers[name].__dict__.get("_export_qparams")
+            d2h += rows * cols * 2
+            if qp is not None:
+                packed[name].copy_(qp["weight_packed"], non_blocking=True)
+                d2h += packed[name].numel() * 4
+        return d2h
+
+    for _ in range(max(1, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    d2h = 0
+    for _ in range(args.steps):
+        d2h = step()
+    ev1.record()
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    if world > 1:
+        m = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(m, op=dist.ReduceOp.MAX)
+        ms = float(m.item())
+    return {"value": round(len(LINEARS) / (ms * 1e-3), 4), "unit": "linears/s",
+            "ms_per_step": round(ms, 3), "h2d_bytes_per_step": int(h2d_bytes),
+            "d2h_bytes_per_step": int(d2h)}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline / reference arm: the numpy oracle of the reference's torch path
+# ---------------------------------------------------------------------------
+
+SAMPLE_TOKENS = 8192
+SAMPLE_LINEAR = (1024, 4096)  # k_proj-shaped sample: rows x columns
+
+
+def cpu_sample(threads=None):
+    """Time the oracle pipeline on one k_proj-shaped linear with 4 sequences of
+    2048 tokens, then scale each stage to the full step (Hessian by T*C^2,
+    factorization by C^3, compensation by R*C^2) -> seconds per step."""
+    from oracle import compensation as comp, fasterquant as fq, hessian
+    rows, cols = SAMPLE_LINEAR
+    rng = np.random.default_rng(0)
+    W = (rng.standard_normal((1, rows, cols)) * 0.02).astype(np.float32)
+    X = rng.standard_normal((SAMPLE_TOKENS, cols)).astype(np.float32)
+    X[:, :4] *= 20
+    t0 = time.perf_counter()
+    H = np.zeros((cols, cols), np.float32)
+    n = 0
+    for s in range(0, SAMPLE_TOKENS, 2048):
+        H, n = hessian.gptq_add_batch(H, n, X[None, s:s + 2048])
+    t_hess = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    qz = comp.make_group_quantizers(comp.Quantizer(BITS, True), cols, GROUPSIZE)
+    fq.gptq_fasterquant(W, H[None], qz, BLOCKSIZE, PERCDAMP, GROUPSIZE, True, True)
+    t_fq = time.perf_counter() - t0
+    total_tokens = 128 * 2048
+    hess_units = sum(total_tokens * c * c for _, r, c, _ in LINEARS)
+    comp_units = sum(r * c * c for _, r, c, _ in LINEARS)
+    step_s = (t_hess * hess_units / (SAMPLE_TOKENS * cols * cols) +
+              t_fq * comp_units / (rows * cols * cols))
+    return step_s, t_hess + t_fq
+
+
+def cpu_baseline():
+    step_s, wall = cpu_sample()
+    return {"value": round(len(LINEARS) / step_s, 6), "unit": "linears/s",
+            "cores": os.cpu_count(), "kind": "port",
+            "sample": f"numpy oracle of the reference torch path: one {SAMPLE_LINEAR[0]}x"
+                      f"{SAMPLE_LINEAR[1]} linear, {SAMPLE_TOKENS} tokens, add_batch + "
+                      f"fasterquant ({wall:.1f} s), scaled per stage to the 7-linear, "
+                      f"262144-token step"}
+
+
+def reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    for _ in range(args.warmup):
+        cpu_sample()
+    vals = []
+    walls = []
+    for _ in range(args.steps):
+        s, w = cpu_sample()
+        vals.append(s)
+        walls.append(w)
+    step_s = float(np.mean(vals))
+    value = len(LINEARS) / step_s
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 6),
+            "unit": "linears/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(step_s * 1e3, 1), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "Llama-3-8B decoder layer (7 linears) GPTQ W4 sym g128 "
+                                   "act-order, 128x2048 calibration tokens"},
+            "cpu_baseline": {"value": round(value, 6), "unit": "linears/s",
+                             "cores": os.cpu_count(), "kind": "port",
+                             "sample": "one 1024x4096 linear, 8192 tokens per step, scaled "
+                                       "per stage to the full step"},
+            "e2e": {"value": round(value, 6), "unit": "linears/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    a = parse()
+    if a.impl == "reference":
+        reference(a)
+    else:
+        native(a)

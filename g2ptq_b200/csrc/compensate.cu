@@ -1,0 +1,501 @@
+// Lazy-batch column compensation (GPTQ / G2PTQ / GPTAQ) and quantization
+// parameters.
+//
+// Rows of W are independent in the compensation: every row walks the block's
+// columns in order, quantizes, and pushes its error onto the remaining
+// columns through the shared row U[c, c+1:].  One thread therefore owns one
+// row and keeps the block's 128 values of that row in registers; the block
+// of U (and of P for GPTAQ) sits in shared memory and every U[c][j] read is a
+// warp-wide broadcast.  The trailing update of the columns after the block is
+// a GEMM (gemm_simt.cu or gemm_tc.cu).
+#include "gemm_simt.cuh"
+
+namespace g2q {
+
+constexpr int BLK = 128;  // maximum block width handled by one launch
+
+struct BlockParams {
+  float* W;  // row-major rows x ncols per batch entry, updated in place to Q
+  long long ldw, w_bs;
+  long long rows;
+  int ncols;
+  const float* hinv;
+  long long ldh, h_bs;
+  const float* scale;
+  const float* zero;
+  long long param_ld;
+  const int* colmap;
+  int maxq;
+  int8_t* codes;  // row-major (ldq, q_bs)
+  long long ldq, q_bs;
+  float* err;  // optional fp32 error, column-major: (c * lde + r) + b * e_bs
+  long long lde, e_bs;
+  float* erra;  // optional trailing-update operand, column-major (ldea, ea_bs)
+  long long ldea, ea_bs;
+  __nv_bfloat16* erra_hi;  // optional split copy of erra (same layout)
+  __nv_bfloat16* erra_lo;
+  const float* z;  // G2PTQ, row-major (ldz, z_bs)
+  float* gh;
+  long long ldz, z_bs;
+  const float* p;  // GPTAQ, layout (ldh, h_bs)
+  int dfact;       // G2PTQ distance factor (the traversal's blocksize)
+};
+
+constexpr int WIN = 32;       // columns held in registers at a time
+constexpr int LDS_ROW = BLK + 1;  // padded shared-memory row of a W / gh tile
+
+// Shared-memory layout (floats): U block, W tile, [gh tile | P block], codes.
+__host__ __device__ constexpr int smem_floats(int method) {
+  return BLK * BLK + BLK * LDS_ROW +
+         (method == G2Q_METHOD_G2PTQ ? BLK * LDS_ROW : 0) +
+         (method == G2Q_METHOD_GPTAQ ? BLK * BLK : 0);
+}
+constexpr int CODE_ROW = BLK + 4;
+
+template <int METHOD>
+__global__ void __launch_bounds__(128) block_kernel(BlockParams P) {
+  extern __shared__ __align__(16) float smem[];
+  float* Us = smem;                       // [BLK][BLK]
+  float* Ws = Us + BLK * BLK;             // [BLK rows][LDS_ROW]
+  float* Xs = Ws + BLK * LDS_ROW;         // G2PTQ gh tile [BLK][LDS_ROW] / GPTAQ P [BLK][BLK]
+  int8_t* Qs = reinterpret_cast<int8_t*>(smem + smem_floats(METHOD));  // [BLK][CODE_ROW]
+  int* cmap = reinterpret_cast<int*>(Qs + BLK * CODE_ROW);
+  const int b = blockIdx.y;
+  const int t = threadIdx.x;
+  const int lane = t & 31, warp = t >> 5;
+  const long long row0 = (long long)blockIdx.x * BLK;
+  const long long r = row0 + t;
+  const int nc = P.ncols;
+  const long long nrows_here = (P.rows - row0) < BLK ? (P.rows - row0) : BLK;
+
+  const float* hb = P.hinv + (long long)b * P.h_bs;
+  for (int idx = t; idx < BLK * BLK; idx += BLK) {
+    const int i = idx >> 7, j = idx & (BLK - 1);
+    Us[idx] = (i < nc && j < nc) ? hb[i * P.ldh + j] : 0.f;
+  }
+  if (METHOD == G2Q_METHOD_GPTAQ) {
+    const float* pb = P.p + (long long)b * P.h_bs;
+    for (int idx = t; idx < BLK * BLK; idx += BLK) {
+      const int i = idx >> 7, j = idx & (BLK - 1);
+      Xs[idx] = (i < nc && j < nc) ? pb[i * P.ldh + j] : 0.f;
+    }
+  }
+  // W (and gh) tiles: one warp per row, lanes along the row (coalesced)
+  for (int rr = warp; rr < BLK; rr += 4) {
+    const bool ok = rr < nrows_here;
+    const float* src = P.W + (long long)b * P.w_bs + (row0 + rr) * P.ldw;
+    const float* gsrc = (METHOD == G2Q_METHOD_G2PTQ)
+                            ? P.gh + (long long)b * P.z_bs + (row0 + rr) * P.ldz : nullptr;
+    for (int c = lane; c < BLK; c += 32) {
+      Ws[rr * LDS_ROW + c] = (ok && c < nc) ? src[c] : 0.f;
+      if (METHOD == G2Q_METHOD_G2PTQ) Xs[rr * LDS_ROW + c] = (ok && c < nc) ? gsrc[c] : 0.f;
+    }
+  }
+  cmap[t] = t < nc ? P.colmap[t] : 0;
+  __syncthreads();
+
+  const bool active = r < P.rows;
+  if (active) {
+    float* wsr = Ws + t * LDS_ROW;
+    float* gsr = Xs + t * LDS_ROW;  // G2PTQ only
+    int8_t* qsr = Qs + t * CODE_ROW;
+    const long long prow = ((long long)b * P.rows + r) * P.param_ld;
+    const float* zrow =
+        (METHOD == G2Q_METHOD_G2PTQ) ? P.z + (long long)b * P.z_bs + r * P.ldz : nullptr;
+    const float qlo = -(float)(P.maxq + 1), qhi = (float)P.maxq;
+
+    for (int w0 = 0; w0 < nc; w0 += WIN) {
+      float wv[WIN], gv[WIN], ev[WIN], xv[WIN];  // xv: GPTAQ pre-quant w / G2PTQ z
+#pragma unroll
+      for (int k = 0; k < WIN; ++k) {
+        wv[k] = wsr[w0 + k];
+        gv[k] = (METHOD == G2Q_METHOD_G2PTQ) ? gsr[w0 + k] : 0.f;
+        ev[k] = 0.f;
+        xv[k] = 0.f;
+      }
+#pragma unroll
+      for (int c = 0; c < WIN; ++c) {
+        const int cc = w0 + c;
+        if (cc < nc) {
+          const int pc = cmap[cc];
+          const float s = P.scale[prow + pc];
+          const float zz = P.zero[prow + pc];
+          const float d = Us[cc * BLK + cc];
+          const float wc = wv[c];
+          float q = rintf(wc / s) + zz;
+          q = fminf(fmaxf(q, qlo), qhi);
+          const float qv = s * (q - zz);
+          float e;
+          if (METHOD == G2Q_METHOD_G2PTQ) {
+            xv[c] = zrow[cc];
+            e = (wc - qv - gv[c]) / d;
+          } else {
+            e = (wc - qv) / d;
+          }
+          if (METHOD == G2Q_METHOD_GPTAQ) xv[c] = wc;
+          ev[c] = e;
+          wv[c] = qv;
+          qsr[cc] = (int8_t)(int)q;
+          const float ea =
+              (METHOD == G2Q_METHOD_G2PTQ) ? e - xv[c] * (float)(P.dfact - 1 - cc) : e;
+          const long long co = (long long)cc;
+          if (P.err) P.err[(long long)b * P.e_bs + co * P.lde + r] = e;
+          if (P.erra) P.erra[(long long)b * P.ea_bs + co * P.ldea + r] = ea;
+          if (P.erra_hi) {
+            __nv_bfloat16 h, l;
+            split_bf16(ea, &h, &l);
+            P.erra_hi[(long long)b * P.ea_bs + co * P.ldea + r] = h;
+            P.erra_lo[(long long)b * P.ea_bs + co * P.ldea + r] = l;
+          }
+          // in-window update of columns c+1 .. WIN-1
+#pragma unroll
+          for (int j = c + 1; j < WIN; ++j) {
+            const float u = Us[cc * BLK + w0 + j];
+            if (METHOD == G2Q_METHOD_G2PTQ) {
+              wv[j] = fmaf(-e, u, wv[j] - gv[j]);
+              gv[j] = fmaf(-xv[c], u, gv[j]);
+            } else if (METHOD == G2Q_METHOD_GPTAQ) {
+              wv[j] = fmaf(Xs[cc * BLK + w0 + j], wc, fmaf(-e, u, wv[j]));
+            } else {
+              wv[j] = fmaf(-e, u, wv[j]);
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < WIN; ++k) {
+        wsr[w0 + k] = wv[k];
+        if (METHOD == G2Q_METHOD_G2PTQ) gsr[w0 + k] = gv[k];
+      }
+      // deferred update of the block columns after this window, applied in
+      // column order so each element sees the same sequence of operations
+      const int jend = (nc + 3) & ~3;
+      for (int j0 = w0 + WIN; j0 < jend; j0 += 4) {
+        float x4[4], g4[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          x4[k] = wsr[j0 + k];
+          g4[k] = (METHOD == G2Q_METHOD_G2PTQ) ? gsr[j0 + k] : 0.f;
+        }
+#pragma unroll
+        for (int c = 0; c < WIN; ++c) {
+          const float4 u4 = *reinterpret_cast<const float4*>(&Us[(w0 + c) * BLK + j0]);
+          const float uu[4] = {u4.x, u4.y, u4.z, u4.w};
+          float pp[4] = {0.f, 0.f, 0.f, 0.f};
+          if (METHOD == G2Q_METHOD_GPTAQ) {
+            const float4 p4 = *reinterpret_cast<const float4*>(&Xs[(w0 + c) * BLK + j0]);
+            pp[0] = p4.x; pp[1] = p4.y; pp[2] = p4.z; pp[3] = p4.w;
+          }
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            if (METHOD == G2Q_METHOD_G2PTQ) {
+              x4[k] = fmaf(-ev[c], uu[k], x4[k] - g4[k]);
+              g4[k] = fmaf(-xv[c], uu[k], g4[k]);
+            } else if (METHOD == G2Q_METHOD_GPTAQ) {
+              x4[k] = fmaf(pp[k], xv[c], fmaf(-ev[c], uu[k], x4[k]));
+            } else {
+              x4[k] = fmaf(-ev[c], uu[k], x4[k]);
+            }
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          wsr[j0 + k] = x4[k];
+          if (METHOD == G2Q_METHOD_G2PTQ) gsr[j0 + k] = g4[k];
+        }
+      }
+    }
+  }
+  __syncthreads();
+  // coalesced write-back of Q, codes (and gh)
+  for (int rr = warp; rr < nrows_here; rr += 4) {
+    float* dst = P.W + (long long)b * P.w_bs + (row0 + rr) * P.ldw;
+    int8_t* qdst = P.codes ? P.codes + (long long)b * P.q_bs + (row0 + rr) * P.ldq : nullptr;
+    float* gdst = (METHOD == G2Q_METHOD_G2PTQ)
+                      ? P.gh + (long long)b * P.z_bs + (row0 + rr) * P.ldz : nullptr;
+    for (int c = lane; c < nc; c += 32) {
+      dst[c] = Ws[rr * LDS_ROW + c];
+      if (qdst) qdst[c] = Qs[rr * CODE_ROW + c];
+      if (METHOD == G2Q_METHOD_G2PTQ) gdst[c] = Xs[rr * LDS_ROW + c];
+    }
+  }
+}
+
+static size_t block_smem(int method) {
+  return (size_t)smem_floats(method) * sizeof(float) + BLK * CODE_ROW + BLK * sizeof(int);
+}
+
+template <int METHOD>
+static int launch_block_t(const BlockParams& P, long long batch, cudaStream_t st) {
+  static int attr_done[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return G2Q_ERR_CUDA;
+  const size_t smem = block_smem(METHOD);
+  if (dev >= 64 || !attr_done[dev]) {
+    if (cudaFuncSetAttribute(block_kernel<METHOD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem) != cudaSuccess)
+      return G2Q_ERR_CUDA;
+    if (dev < 64) attr_done[dev] = 1;
+  }
+  dim3 grid(cdiv(P.rows, BLK), (unsigned)batch);
+  if (grid.y > 65535u) return G2Q_ERR_INVALID_ARG;
+  block_kernel<METHOD><<<grid, BLK, smem, st>>>(P);
+  G2Q_CHECK_LAUNCH();
+  return G2Q_OK;
+}
+
+int launch_block(int method, const BlockParams& P, long long batch, cudaStream_t st) {
+  if (P.rows <= 0 || batch <= 0 || P.ncols <= 0) return G2Q_OK;
+  switch (method) {
+    case G2Q_METHOD_GPTQ: return launch_block_t<G2Q_METHOD_GPTQ>(P, batch, st);
+    case G2Q_METHOD_G2PTQ: return launch_block_t<G2Q_METHOD_G2PTQ>(P, batch, st);
+    case G2Q_METHOD_GPTAQ: return launch_block_t<G2Q_METHOD_GPTAQ>(P, batch, st);
+  }
+  return G2Q_ERR_INVALID_ARG;
+}
+
+// ---------------------------------------------------------------------------
+// Quantization parameters: one warp per (row, group).
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ void params_from_range(float xmin, float xmax, int bits, int sym,
+                                                  float* s_out, float* z_out) {
+  const int maxq = (1 << (bits - 1)) - 1;
+  const int minq = -(maxq + 1);
+  const float bit_range = (float)(maxq - minq);
+  xmin = fminf(xmin, 0.f);
+  xmax = fmaxf(xmax, 0.f);
+  float s, z;
+  if (sym) {
+    s = fmaxf(fabsf(xmin), xmax) / (bit_range / 2.f);
+    z = 0.f;
+  } else {
+    s = (xmax - xmin) / bit_range;
+    z = rintf((float)minq - xmin / s);
+    z = fminf(fmaxf(z, (float)minq), (float)maxq);
+  }
+  *s_out = s;
+  *z_out = rintf(z);
+}
+
+__global__ void find_params_kernel(float* scale, float* zero, long long param_ld,
+                                   const float* W, long long rows, long long cols,
+                                   long long ldw, int bits, int sym, int* status,
+                                   long long first_start, int groupsize, long long C) {
+  const long long warp = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const long long r = warp;
+  const int gi = blockIdx.y;
+  if (r >= rows) return;
+  long long c0 = 0, nc = cols;
+  long long pc = 0;
+  if (first_start >= 0) {
+    c0 = first_start + (long long)gi * groupsize;
+    nc = (C - c0) < groupsize ? (C - c0) : groupsize;
+    pc = c0 / groupsize;
+  }
+  const float* x = W + r * ldw + c0;
+  float mn = INFINITY, mx = -INFINITY;
+  for (long long c = lane; c < nc; c += 32) {
+    const float v = x[c];
+    mn = fminf(mn, v);
+    mx = fmaxf(mx, v);
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  }
+  if (lane == 0) {
+    float s, z;
+    params_from_range(mn, mx, bits, sym, &s, &z);
+    scale[r * param_ld + pc] = s;
+    zero[r * param_ld + pc] = z;
+    if (!(s > 0.f)) record_error(status, G2Q_ERR_BAD_SCALE);
+  }
+}
+
+static int launch_find_params(float* scale, float* zero, long long param_ld, const float* W,
+                              long long rows, long long cols, long long ldw, int bits, int sym,
+                              int* status, long long first_start, int ngs, int groupsize,
+                              long long C, cudaStream_t st) {
+  if (rows <= 0) return G2Q_OK;
+  const int warps_per_block = 8;
+  dim3 grid(cdiv(rows, warps_per_block), first_start >= 0 ? ngs : 1);
+  find_params_kernel<<<grid, 32 * warps_per_block, 0, st>>>(
+      scale, zero, param_ld, W, rows, cols, ldw, bits, sym, status, first_start, groupsize, C);
+  G2Q_CHECK_LAUNCH();
+  return G2Q_OK;
+}
+
+__global__ void fake_quantize_kernel(float* out, long long ldo, int8_t* codes, long long ldq,
+                                     const float* W, long long ldw, long long rows,
+                                     long long cols, const float* scale, const float* zero,
+                                     long long param_ld, const int* colmap, int maxq) {
+  const long long n = rows * cols;
+  const float qlo = -(float)(maxq + 1), qhi = (float)maxq;
+  for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < n;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const long long r = idx / cols, c = idx - r * cols;
+    const long long pi = r * param_ld + (colmap ? colmap[c] : 0);
+    const float s = scale[pi], z = zero[pi];
+    const float w = W[r * ldw + c];
+    float q = rintf(w / s) + z;
+    q = fminf(fmaxf(q, qlo), qhi);
+    if (out) out[r * ldo + c] = s * (q - z);
+    if (codes) codes[r * ldq + c] = (int8_t)(int)q;
+  }
+}
+
+// W[b][:, c] -= f * G[b][:, c] over a column range (G2PTQ gradient term).
+__global__ void sub_scaled_kernel(float* W, const float* G, long long nl_rows, long long C,
+                                  long long c0, float f) {
+  const long long w = C - c0;
+  const long long n = nl_rows * w;
+  for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < n;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const long long r = idx / w, c = c0 + (idx - r * w);
+    W[r * C + c] -= f * G[r * C + c];
+  }
+}
+
+static int grid_for(long long n) {
+  long long b = (n + 255) / 256;
+  if (b > 148 * 64) b = 148 * 64;
+  if (b < 1) b = 1;
+  return (int)b;
+}
+
+}  // namespace g2q
+
+using namespace g2q;
+
+extern "C" int g2q_find_params(float* scale, float* zero, int64_t param_ld, const float* W,
+                               int64_t rows, int64_t cols, int64_t ldw, int bits, int sym,
+                               int* status, void* stream) {
+  if (!scale || !zero || !W || rows < 0 || cols <= 0 || ldw < cols || bits < 1 || bits > 16)
+    return G2Q_ERR_INVALID_ARG;
+  return launch_find_params(scale, zero, param_ld, W, rows, cols, ldw, bits, sym, status,
+                            -1, 1, 0, cols, (cudaStream_t)stream);
+}
+
+extern "C" int g2q_fake_quantize(float* out, int64_t ldo, int8_t* codes, int64_t ldq,
+                                 const float* W, int64_t ldw, int64_t rows, int64_t cols,
+                                 const float* scale, const float* zero, int64_t param_ld,
+                                 const int* colmap, int maxq, void* stream) {
+  if (!W || !scale || !zero || rows < 0 || cols < 0) return G2Q_ERR_INVALID_ARG;
+  if (rows * cols == 0) return G2Q_OK;
+  fake_quantize_kernel<<<grid_for(rows * cols), 256, 0, (cudaStream_t)stream>>>(
+      out, ldo, codes, ldq, W, ldw, rows, cols, scale, zero, param_ld, colmap, maxq);
+  G2Q_CHECK_LAUNCH();
+  return G2Q_OK;
+}
+
+extern "C" int g2q_compensate_block(int method, float* W, int64_t ldw, int64_t w_bstride,
+                                    int64_t batch, int64_t rows, int64_t ncols,
+                                    const float* hinv, int64_t ldh, int64_t h_bstride,
+                                    const float* scale, const float* zero, int64_t param_ld,
+                                    const int* colmap, int maxq, int8_t* codes, float* err,
+                                    const float* z, float* ghinv, const float* p,
+                                    void* stream) {
+  if (!W || !hinv || !scale || !zero || !colmap || ncols <= 0 || ncols > BLK || rows < 0 ||
+      batch < 0 || maxq < 0)
+    return G2Q_ERR_INVALID_ARG;
+  if (method == G2Q_METHOD_G2PTQ && (!z || !ghinv)) return G2Q_ERR_INVALID_ARG;
+  if (method == G2Q_METHOD_GPTAQ && !p) return G2Q_ERR_INVALID_ARG;
+  BlockParams P{};
+  P.W = W; P.ldw = ldw; P.w_bs = w_bstride;
+  P.rows = rows; P.ncols = (int)ncols;
+  P.hinv = hinv; P.ldh = ldh; P.h_bs = h_bstride;
+  P.scale = scale; P.zero = zero; P.param_ld = param_ld; P.colmap = colmap; P.maxq = maxq;
+  P.codes = codes; P.ldq = ldw; P.q_bs = w_bstride;
+  P.err = err; P.lde = rows; P.e_bs = ncols * rows;
+  P.z = z; P.gh = ghinv; P.ldz = ldw; P.z_bs = w_bstride;
+  P.p = p;
+  P.dfact = (int)ncols;
+  return launch_block(method, P, batch, (cudaStream_t)stream);
+}
+
+
+extern "C" size_t g2q_compensate_workspace_bytes(int method, int64_t nl, int64_t rows,
+                                                 int64_t C, int precision) {
+  size_t b = (size_t)nl * rows * BLK * sizeof(float) + 256;
+  if (precision == 1) {
+    b += 2 * (size_t)nl * rows * BLK * sizeof(__nv_bfloat16) + 256;  // erra hi/lo
+    b += 2 * (size_t)nl * C * C * sizeof(__nv_bfloat16) + 256;       // U hi/lo
+    if (method != G2Q_METHOD_GPTQ)
+      b += 2 * (size_t)nl * rows * C * sizeof(__nv_bfloat16) + 256;  // Z or -Q/P operands
+  }
+  return b;
+}
+
+static char* align_up(char* p, size_t a) {
+  return (char*)(((uintptr_t)p + a - 1) / a * a);
+}
+
+extern "C" int g2q_compensate(int method, float* W, int64_t nl, int64_t rows, int64_t C,
+                              const float* U, float* scale, float* zero, int64_t ngroups,
+                              const int* colgroup, int dynamic_groups, int groupsize, int bits,
+                              int sym, int blocksize, int8_t* codes, const float* z, float* gh,
+                              const float* p, int precision, void* workspace,
+                              size_t workspace_bytes, int* status, void* stream) {
+  if (!W || !U || !scale || !zero || !colgroup || !codes || nl <= 0 || rows <= 0 || C <= 0 ||
+      blocksize <= 0 || blocksize > BLK || bits < 1 || bits > 8 || !workspace)
+    return G2Q_ERR_INVALID_ARG;
+  if (dynamic_groups && groupsize <= 0) return G2Q_ERR_INVALID_ARG;
+  if (method == G2Q_METHOD_G2PTQ && (!z || !gh)) return G2Q_ERR_INVALID_ARG;
+  if (method == G2Q_METHOD_GPTAQ && !p) return G2Q_ERR_INVALID_ARG;
+  if (precision != 0) return G2Q_ERR_UNSUPPORTED;
+  if (workspace_bytes < g2q_compensate_workspace_bytes(method, nl, rows, C, precision))
+    return G2Q_ERR_INVALID_ARG;
+  cudaStream_t st = (cudaStream_t)stream;
+  char* wsp = align_up((char*)workspace, 256);
+  float* erra = (float*)wsp;
+  const int maxq = (1 << (bits - 1)) - 1;
+  for (long long i1 = 0; i1 < C; i1 += blocksize) {
+    const long long i2 = (i1 + blocksize < C) ? i1 + blocksize : C;
+    const int nc = (int)(i2 - i1);
+    if (dynamic_groups) {
+      // group starts c0 with i1 <= c0 < i2 and c0 % groupsize == 0
+      const long long first = (i1 + groupsize - 1) / groupsize * groupsize;
+      const int cnt = first < i2 ? (int)((i2 - 1 - first) / groupsize + 1) : 0;
+      if (cnt > 0)
+        G2Q_TRY(launch_find_params(scale, zero, ngroups, W, nl * rows, 0, C, bits, sym, status,
+                                   first, cnt, groupsize, C, st));
+    }
+    BlockParams P{};
+    P.W = W + i1; P.ldw = C; P.w_bs = rows * C;
+    P.rows = rows; P.ncols = nc;
+    P.hinv = U + i1 * C + i1; P.ldh = C; P.h_bs = C * C;
+    P.scale = scale; P.zero = zero; P.param_ld = ngroups; P.colmap = colgroup + i1;
+    P.maxq = maxq;
+    P.codes = codes + i1; P.ldq = C; P.q_bs = rows * C;
+    P.erra = erra; P.ldea = rows; P.ea_bs = rows * BLK;
+    if (method == G2Q_METHOD_G2PTQ) {
+      P.z = z + i1; P.gh = gh + i1; P.ldz = C; P.z_bs = rows * C;
+    }
+    if (method == G2Q_METHOD_GPTAQ) P.p = p + i1 * C + i1;
+    P.dfact = blocksize;
+    G2Q_TRY(launch_block(method, P, nl, st));
+    if (i2 >= C) break;
+    const long long N = C - i2;
+    if (method == G2Q_METHOD_G2PTQ) {
+      sub_scaled_kernel<<<grid_for(nl * rows * N), 256, 0, st>>>(W, gh, nl * rows, C, i2,
+                                                                 (float)blocksize);
+      G2Q_CHECK_LAUNCH();
+    }
+    // W[:, i2:] -= Erra @ U[i1:i2, i2:]
+    G2Q_TRY(simt_gemm_f32(W + i2, C, erra, rows, true, U + i1 * C + i2, C, false, rows, N, nc,
+                          1.f, -1.f, G2Q_MASK_FULL, st, nl, rows * BLK, C * C, rows * C));
+    if (method == G2Q_METHOD_G2PTQ) {
+      // GH[:, i2:] -= Z[:, i1:i2] @ U[i1:i2, i2:]
+      G2Q_TRY(simt_gemm_f32(gh + i2, C, z + i1, C, false, U + i1 * C + i2, C, false, rows, N,
+                            nc, 1.f, -1.f, G2Q_MASK_FULL, st, nl, rows * C, C * C, rows * C));
+    }
+    if (method == G2Q_METHOD_GPTAQ) {
+      // W[:, i2:] += Q1 @ P[i1:i2, i2:]
+      G2Q_TRY(simt_gemm_f32(W + i2, C, W + i1, C, false, p + i1 * C + i2, C, false, rows, N, nc,
+                            1.f, 1.f, G2Q_MASK_FULL, st, nl, rows * C, C * C, rows * C));
+    }
+  }
+  return G2Q_OK;
+}

@@ -1,0 +1,263 @@
+"""Shared machinery of the quantizer objects: token staging for ``add_batch``
+and the device pipeline behind ``fasterquant``.
+
+Staging.  The reference updates the running Hessian on every hook call
+(``H <- H n/(n+b) + (2/(n+b)) X^T X``, gptq_utils.py:123-126), i.e. a full
+read-modify-write of the C x C matrix per 2048-token sequence at the default
+``--bsz 1``, which costs as much HBM time as the product itself.  Here each
+call only copies its tokens into a per-layer staging buffer; the buffer is
+folded into ``H`` by one Gram launch when it fills up or when ``H`` is read.
+Folding b pending samples at once applies the same rescale the reference
+applies call by call: ``H <- H n_old/n_new + (2/n_new) sum X^T X``.
+
+fasterquant.  Everything between the stacked weights and the written-back
+quantized weights runs on the device (find_params, dead columns, act-order
+permutation, damped inverse-Cholesky, compensation, un-permutation, cast and
+NaN count).  The host reads back one small status vector per call; the
+damp auto-increment of the reference (gptq_utils.py:291-311) re-runs only
+when a layer's factorization failed.
+"""
+
+import logging
+import os
+
+import torch
+
+from .. import ops, _lib
+from ..utils import compressed_tensors_utils
+
+DAMP_INCREMENT = 0.0015
+STAGE_TOKENS = int(os.environ.get("G2PTQ_B200_STAGE_TOKENS", "16384"))
+STAGE_BYTES = int(os.environ.get("G2PTQ_B200_STAGE_BYTES", str(512 << 20)))
+# 0 = fp32 CUDA cores, 1 = tcgen05 tensor cores (Gram products and trailing updates)
+PRECISION = int(os.environ.get("G2PTQ_B200_PRECISION", "0"))
+
+
+class TokenStage:
+    """Pending calibration tokens of one layer, folded into a Gram matrix lazily.
+
+    ``buf`` holds the tokens (bf16 for bf16 inputs, else fp32), ``sub_buf``
+    an optional fp32 second operand (GPTAQ's ``X_fp - X``), ``scale_buf`` optional
+    per-token weights ``[cap, groups]`` (G2PTQ / GuidedQuant saliencies).
+    """
+
+    def __init__(self, columns, device, groups=0):
+        self.columns = columns
+        self.device = device
+        self.groups = groups
+        self.buf = None
+        self.sub_buf = None
+        self.scale_buf = None
+        self.rows = 0
+        self.dtype = None
+
+    def capacity(self, elem):
+        return max(1, min(STAGE_TOKENS, STAGE_BYTES // (self.columns * elem)))
+
+    def _ensure(self, dtype, with_sub):
+        if self.buf is None or self.buf.dtype != dtype or (with_sub and self.sub_buf is None):
+            cap = self.capacity(torch.tensor([], dtype=dtype).element_size() +
+                                (4 if with_sub else 0))
+            self.buf = torch.empty(cap, self.columns, dtype=dtype, device=self.device)
+            self.sub_buf = (torch.empty(cap, self.columns, dtype=torch.float32,
+                                        device=self.device) if with_sub else None)
+            self.scale_buf = (torch.empty(cap, self.groups, dtype=torch.float32,
+                                          device=self.device) if self.groups else None)
+            self.dtype = dtype
+
+    def cap(self):
+        return self.buf.shape[0]
+
+    def free(self):
+        self.buf = None
+        self.sub_buf = None
+        self.scale_buf = None
+        self.rows = 0
+
+
+def stage_dtype(x):
+    return torch.bfloat16 if x.dtype == torch.bfloat16 else torch.float32
+
+
+def as_rows(x, columns):
+    x = x.reshape(-1, columns)
+    if x.stride(1) != 1:
+        x = x.contiguous()
+    return x
+
+
+def sync_check(*tensors):
+    """One device->host read of several small int tensors."""
+    flat = torch.cat([t.reshape(-1).to(torch.int64) for t in tensors])
+    return flat.cpu().tolist()
+
+
+def factor_with_retry(H, percdamp, info=None):
+    """Damped inverse-Cholesky of every ``H[b]``; the reference's damp
+    auto-increment runs for each failing ``b`` (one host read per attempt).
+
+    Returns ``(U, damps)``.
+    """
+    nl = H.shape[0]
+    damps = [float(percdamp)] * nl
+    if not (1 > percdamp > 0):
+        raise ValueError(f"Quantization: `damp_percent` must between 0 and 1. current is "
+                         f"{percdamp}")
+    U, info = ops.chol_upper_inverse(H, damps, info)
+    return U, info, damps
+
+
+def retry_failed(H, U, info_list, damps):
+    """Re-factor failing layers with the damp auto-increment."""
+    for b, inf in enumerate(info_list):
+        if inf == 0:
+            continue
+        d = damps[b]
+        while True:
+            logging.warning(f"Quantization: Current `damp_percent = {d:.5f}` is too low, "
+                            f"auto-incrementing by `{DAMP_INCREMENT:.5f}`")
+            d += DAMP_INCREMENT
+            if not (1 > d > 0):
+                raise ValueError(
+                    f"Quantization: `damp_percent` must between 0 and 1. current is {d}")
+            Ub, ib = ops.chol_upper_inverse(H[b:b + 1].contiguous(), [d])
+            if int(ib.item()) == 0:
+                U[b].copy_(Ub[0])
+                break
+        damps[b] = d
+    return U
+
+
+class ParamSet:
+    """Quantization parameters of a layer batch: ``[nl*rows, ngroups]`` scale
+    and zero arrays plus the column -> parameter-column map.  Each group
+    quantizer's ``scale`` / ``zero`` becomes a ``[nl*rows, 1]`` view of one
+    column, so callers reading the quantizers see the final values."""
+
+    def __init__(self, quantizers, total_rows, columns, groupsize, device):
+        self.quantizers = quantizers
+        self.ng = len(quantizers)
+        self.groupsize = groupsize
+        self.scale = torch.zeros(total_rows, self.ng, dtype=torch.float32, device=device)
+        self.zero = torch.zeros_like(self.scale)
+        self.status = torch.zeros(1, dtype=torch.int32, device=device)
+        self.columns = columns
+
+    def init_static(self, W_flat, H_diag=None):
+        """gptq_utils.py:259-270 for ungrouped / static-group quantizers."""
+        gs = self.groupsize
+        for i, q in enumerate(self.quantizers):
+            sv = self.scale[:, i:i + 1]
+            zv = self.zero[:, i:i + 1]
+            if not q.ready():
+                cols = slice(None) if gs == -1 else slice(i * gs, (i + 1) * gs)
+                q.find_params(W_flat[:, cols],
+                              None if H_diag is None else H_diag[:, cols], out=(sv, zv))
+            else:
+                sv.copy_(q.scale.reshape(-1, 1).to(sv))
+                zv.copy_(q.zero.reshape(-1, 1).to(zv))
+            q.scale, q.zero = sv, zv
+
+    def bind_dynamic(self):
+        for i, q in enumerate(self.quantizers):
+            q.scale = self.scale[:, i:i + 1]
+            q.zero = self.zero[:, i:i + 1]
+            q._ready = True
+
+    def statuses(self):
+        out = [self.status]
+        for q in self.quantizers:
+            if getattr(q, "_status", None) is not None:
+                out.append(q._status)
+        return out
+
+    def colgroup(self, perm, static_groups, device):
+        C = self.columns
+        if self.groupsize == -1:
+            return torch.zeros(C, dtype=torch.int32, device=device)
+        idx = perm if (perm is not None and static_groups) else torch.arange(C, device=device)
+        return (idx // self.groupsize).to(torch.int32).contiguous()
+
+
+def act_order_perm(key):
+    """``torch.argsort(key, descending=True)`` (stable) and its inverse."""
+    perm = ops.argsort_desc(key.contiguous())
+    invperm = torch.empty_like(perm)
+    invperm[perm] = torch.arange(perm.numel(), device=perm.device)
+    return perm, invperm
+
+
+def write_back(layers, Q, codes, params, bits, groupsize, columns, export, perm_dynamic=None):
+    """Cast, NaN check and hand-over of the quantized weights (gptq_utils.py:329-353).
+
+    Returns the list of device tensors to check on the host; ``finish`` applies them."""
+    nan = torch.zeros(1, dtype=torch.int32, device=Q.device)
+    outs = []
+    for b, layer in enumerate(layers):
+        outs.append(ops.cast_check(Q[b].contiguous(), layer.weight.dtype, nan))
+    return nan, outs
+
+
+def finish(layers, outs, codes, params, bits, groupsize, columns, export, rows):
+    for b, layer in enumerate(layers):
+        if export:
+            if groupsize == -1:
+                gscale = params.scale[b * rows:(b + 1) * rows, :1]
+            else:
+                gscale = params.scale[b * rows:(b + 1) * rows]
+            compressed_tensors_utils.compress_grouped(layer, gscale, codes[b], bits)
+        layer.weight.data.copy_(outs[b].reshape(layer.weight.shape))
+
+
+class StagingMixin:
+    """``add_batch`` plumbing shared by the quantizer objects.
+
+    Subclasses provide ``_fold(idx, X, sub, scales)``, which folds staged
+    tokens into their statistics using the counts recorded so far.  Because
+    every fold rescales by (counts already folded) / (counts now), any split
+    of the pending tokens into folds gives the same statistics.
+    """
+
+    def _init_stages(self, groups=0):
+        self._stages = [TokenStage(self.columns, self.dev, groups)
+                        for _ in range(self.num_layers)]
+
+    def _append(self, idx, x, sub=None, scales=None):
+        st = self._stages[idx]
+        dt = stage_dtype(x)
+        if st.rows and st.dtype != dt:
+            self._flush(idx)
+        st._ensure(dt, sub is not None)
+        cap = st.cap()
+        t = x.shape[0]
+        for s in range(0, t, cap):
+            e = min(t, s + cap)
+            if st.rows + (e - s) > cap:
+                self._flush(idx)
+            ops.stage_tokens(st.buf, st.rows, x[s:e])
+            if sub is not None:
+                ops.stage_tokens(st.sub_buf, st.rows, sub[s:e], x[s:e])
+            if scales is not None:
+                st.scale_buf[st.rows:st.rows + (e - s)].copy_(scales[s:e])
+            st.rows += e - s
+
+    def _flush(self, idx):
+        st = self._stages[idx]
+        if st.rows == 0:
+            return
+        self._fold(idx, st.buf[:st.rows],
+                   None if st.sub_buf is None else st.sub_buf[:st.rows],
+                   None if st.scale_buf is None else st.scale_buf[:st.rows])
+        st.rows = 0
+
+    def _flush_all(self):
+        if getattr(self, "_stages", None) is None:
+            return
+        for i in range(self.num_layers):
+            self._flush(i)
+
+    def _require_device_stats(self, t):
+        if t.device.type != "cuda":
+            raise RuntimeError("add_batch needs the statistics on the device; wrap the "
+                               "calibration forward in the object's onload context when "
+                               "offload_hessians=True")

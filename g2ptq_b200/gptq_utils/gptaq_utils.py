@@ -1,0 +1,209 @@
+"""GPTAQ quantizer object, a drop-in for gptq_utils/gptaq_utils.py of the reference
+(``GPTAQ`` gptaq_utils.py:103-399, ``run_eager`` :74-100, ``reduce_to_target_rank``
+:402-439).
+
+Statistics: ``H`` as GPTQ and ``dXX^T <- dXX^T n/(n+b) + (2/(n+b)) (X_fp - X)^T X``
+(gptaq_utils.py:139-146), staged as ``X`` plus the fp32 difference ``X_fp - X``.
+Compensation adds ``+ w_c * P[c, c+1:]`` with
+``P = alpha * triu(dXX^T U^T, 1) U`` (gptaq_utils.py:349-352).
+"""
+
+import contextlib
+
+import torch
+import torch.distributed as dist
+
+from .. import ops, _lib
+from . import _engine
+from .graph_utils import validate_tensors
+from .gptq_utils import _onload
+
+
+def run_eager(weight, hinv, p, scale, zero, maxq, backend="torch", column_weight=None,
+              int_weight=None, error=None):
+    """One GPTAQ compensation block, reference layout ``[B, blk, R]``
+    (gptaq_utils.py:74-100)."""
+    validate_tensors("GPTAQ", weight, hinv, p, scale, zero, int_weight, error)
+    B, blk, R = weight.shape
+    W = weight.transpose(1, 2).contiguous()
+    S = scale.transpose(1, 2).contiguous().reshape(B * R, blk)
+    Z = zero.transpose(1, 2).contiguous().reshape(B * R, blk)
+    colmap = torch.arange(blk, dtype=torch.int32, device=weight.device)
+    codes = torch.empty(B, R, blk, dtype=torch.int8, device=weight.device)
+    err = torch.empty(B, blk, R, dtype=torch.float32, device=weight.device)
+    ops.compensate_block(_lib.METHOD_GPTAQ, W, hinv.contiguous(), S, Z, colmap, maxq,
+                         codes=codes, err=err, p=p.contiguous())
+    weight.copy_(W.transpose(1, 2))
+    int_weight.copy_(codes.transpose(1, 2))
+    error.copy_(err)
+    return weight, int_weight, error
+
+
+class GPTAQ(_engine.StagingMixin):
+    def __init__(self, layers, offload_hessians: bool = False):
+        self.layers = layers
+        self.num_layers = len(layers)
+        self.offload_hessians = offload_hessians
+        weight = layers[0].weight
+        self.dev = weight.device
+        if self.dev.type != "cuda":
+            raise RuntimeError("g2ptq_b200 GPTAQ requires layers on a CUDA device")
+        self.rows, self.columns = weight.shape
+        H_device = "cpu" if offload_hessians else self.dev
+        self._H = torch.zeros((self.num_layers, self.columns, self.columns),
+                              dtype=torch.float32, device=H_device)
+        self._dXXT = torch.zeros_like(self._H)
+        self.nsamples = torch.tensor([0] * self.num_layers, device=self.dev)
+        self.fp_inp = [[] for _ in range(self.num_layers)]
+        self._n = [0] * self.num_layers
+        self._n_folded = [0] * self.num_layers
+        self._init_stages()
+
+    @property
+    def H(self):
+        self._flush_all()
+        return self._H
+
+    @H.setter
+    def H(self, value):
+        self._H = value
+
+    @property
+    def dXXT(self):
+        self._flush_all()
+        return self._dXXT
+
+    @dXXT.setter
+    def dXXT(self, value):
+        self._dXXT = value
+
+    def _maybe_onload_hessian(self):
+        """gptaq_utils.py:123-128."""
+        if not self.offload_hessians:
+            return contextlib.nullcontext()
+        return _onload(self, ("_H", "_dXXT"))
+
+    def add_batch(self, idx, inp, out):
+        """gptaq_utils.py:130-148."""
+        fp = self.fp_inp[idx][0].to(inp, non_blocking=True)
+        if len(inp.shape) == 2:
+            inp = inp.unsqueeze(0)
+        tmp = inp.shape[0]
+        x = _engine.as_rows(inp, self.columns)
+        fp = _engine.as_rows(fp, self.columns)
+        self._n[idx] += tmp
+        self.nsamples[idx] += tmp
+        self._append(idx, x, sub=fp)
+        del self.fp_inp[idx][0]
+
+    def _fold(self, idx, X, diff, scales):
+        n_old, n_new = self._n_folded[idx], self._n[idx]
+        self._require_device_stats(self._H)
+        a, b = n_old / n_new, 2.0 / n_new
+        ops.gram_update(self._H[idx], X, alpha=a, beta=b, precision=_engine.PRECISION)
+        ops.gram_update(self._dXXT[idx], diff, X, alpha=a, beta=b, symmetric=False,
+                        precision=_engine.PRECISION)
+        self._n_folded[idx] = n_new
+
+    def fasterquant(self, blocksize=128, percdamp=0.01, groupsize=-1, actorder=False,
+                    static_groups=False, alpha=0.25, export_compressed_tensors=False,
+                    backend="torch", graph=False):
+        """gptaq_utils.py:263-391 (``backend`` / ``graph`` accepted and ignored)."""
+        B, R, C = self.num_layers, self.rows, self.columns
+        q0 = self.quantizer[0]
+        if q0.hclip:
+            raise NotImplementedError("g2ptq_b200: --w_hclip needs the clip search")
+        with self._maybe_onload_hessian():
+            H = self.H
+            dX = self.dXXT
+            self.H = None
+        W = torch.stack([l.weight.data for l in self.layers]).float().contiguous()
+        params = _engine.ParamSet(self.quantizer, B * R, C, groupsize, self.dev)
+        dynamic = not (groupsize == -1 or static_groups)
+        if not dynamic:
+            params.init_static(W.view(B * R, C))
+        ops.prepare_hessian(H, W, extra=dX)
+        perm = invperm = None
+        if actorder:
+            perm, invperm = _engine.act_order_perm(ops.mean_diag(H))
+            W = ops.permute_cols(W, perm)
+            H = ops.permute_sym(H, perm)
+            dX = ops.permute_sym(dX, perm)
+        U, info, damps = _engine.factor_with_retry(H, percdamp)
+        colgroup = params.colgroup(perm, static_groups, self.dev)
+        W0 = W.clone()
+        codes = torch.empty(B, R, C, dtype=torch.int8, device=self.dev)
+
+        def compensate_and_cast(Wp):
+            T = ops.gemm(torch.empty_like(dX), dX, U, transB=True, mask=_lib.MASK_STRICT_UPPER)
+            P = ops.gemm(torch.empty_like(dX), T, U, beta=float(alpha))
+            ops.compensate(_lib.METHOD_GPTAQ, Wp, U, params.scale, params.zero, colgroup,
+                           dynamic, groupsize, q0.bits, q0.sym, blocksize, codes, p=P,
+                           status=params.status, precision=_engine.PRECISION)
+            Q, cq = Wp, codes
+            if actorder:
+                Q = ops.permute_cols(Wp, perm, inverse=True)
+                cq = ops.permute_cols(codes, perm, inverse=True)
+            nan, outs = _engine.write_back(self.layers, Q, cq, params, q0.bits, groupsize, C,
+                                           export_compressed_tensors)
+            return nan, outs, cq
+
+        nan, outs, cq = compensate_and_cast(W)
+        flags = _engine.sync_check(info, nan, *params.statuses())
+        if any(i != 0 for i in flags[:B]):
+            _engine.retry_failed(H, U, flags[:B], damps)
+            params.status.zero_()
+            nan, outs, cq = compensate_and_cast(W0)
+            flags = _engine.sync_check(info, nan, *params.statuses())
+            flags[:B] = [0] * B
+        if any(f != 0 for f in flags[B + 1:]):
+            raise RuntimeError("WeightQuantizer.find_params: non-positive scale")
+        if flags[B] != 0:
+            raise ValueError("NaN in weights")
+        if dynamic:
+            params.bind_dynamic()
+        if export_compressed_tensors and dynamic and actorder:
+            raise AssertionError("Scales in the same quantization group should be the same.")
+        _engine.finish(self.layers, outs, cq, params, q0.bits, groupsize, C,
+                       export_compressed_tensors, R)
+        self._last_damps = damps
+
+    def free(self):
+        self._H = None
+        self.Losses = None
+        self._dXXT = None
+        self.nsamples = None
+        self.fp_inp = None
+        self._stages = None
+
+
+def reduce_to_target_rank(gptqs, gptq2rank):
+    """gptaq_utils.py:402-439."""
+    rank = dist.get_rank()
+    dist.barrier()
+    for g in gptqs:
+        with g._maybe_onload_hessian():
+            H, dX = g.H, g.dXXT
+            pending = []
+            target = gptq2rank[g]
+            gn = g.nsamples.clone()
+            dist.all_reduce(gn, op=dist.ReduceOp.SUM)
+            gnl = gn.cpu().tolist()
+            for b in range(g.num_layers):
+                if gnl[b] == 0:
+                    H[b].zero_()
+                    dX[b].zero_()
+                    g.nsamples[b].zero_()
+                else:
+                    H[b] *= g._n[b] / gnl[b]
+                    dX[b] *= g._n[b] / gnl[b]
+                    pending.extend([
+                        dist.reduce(H[b], op=dist.ReduceOp.SUM, dst=target, async_op=True),
+                        dist.reduce(dX[b], op=dist.ReduceOp.SUM, dst=target, async_op=True),
+                    ])
+            if rank == target:
+                g.nsamples.copy_(gn)
+                g._n, g._n_folded = list(gnl), list(gnl)
+            for w in pending:
+                w.wait()
+    dist.barrier()

@@ -1,0 +1,212 @@
+"""GPTQ quantizer object, a drop-in for gptq_utils/gptq_utils.py of the reference.
+
+Same constructor, ``add_batch`` / ``fasterquant`` / ``free`` signatures,
+attributes (``H``, ``nsamples``, ``quantizer``, ``layers`` ...) and error
+behaviour (ValueError on an exhausted damp retry or NaN weights) as
+``GPTQ`` (gptq_utils.py:93-359), plus the kernel-level boundary ``run_eager``
+(gptq_utils.py:67-90) and ``reduce_to_target_rank`` (gptq_utils.py:362-391).
+All arithmetic runs in libg2ptq_b200's sm_100a kernels.
+"""
+
+import contextlib
+
+import torch
+import torch.distributed as dist
+
+from .. import ops, _lib
+from . import _engine
+from .common_utils import make_group_quantizers, merge_group_quantizers  # noqa: F401
+from .graph_utils import validate_tensors
+
+
+def run_eager(weight, hinv, scale, zero, maxq, backend="torch", int_weight=None, error=None):
+    """One prepared compensation block, reference layout ``[B, blk, R]``
+    (gptq_utils.py:67-90).  ``backend`` is accepted and ignored: there is a
+    single CUDA implementation.  Returns ``(weight, int_weight, error)``."""
+    validate_tensors("GPTQ", weight, hinv, scale, zero, int_weight, error)
+    B, blk, R = weight.shape
+    W = weight.transpose(1, 2).contiguous()
+    S = scale.transpose(1, 2).contiguous().reshape(B * R, blk)
+    Z = zero.transpose(1, 2).contiguous().reshape(B * R, blk)
+    colmap = torch.arange(blk, dtype=torch.int32, device=weight.device)
+    codes = torch.empty(B, R, blk, dtype=torch.int8, device=weight.device)
+    err = torch.empty(B, blk, R, dtype=torch.float32, device=weight.device)
+    ops.compensate_block(_lib.METHOD_GPTQ, W, hinv.contiguous(), S, Z, colmap, maxq,
+                         codes=codes, err=err)
+    weight.copy_(W.transpose(1, 2))
+    int_weight.copy_(codes.transpose(1, 2))
+    error.copy_(err)
+    return weight, int_weight, error
+
+
+class GPTQ(_engine.StagingMixin):
+    def __init__(self, layers, offload_hessians: bool = False):
+        self.layers = layers
+        self.num_layers = len(layers)
+        self.offload_hessians = offload_hessians
+        weight = layers[0].weight
+        self.dev = weight.device
+        if self.dev.type != "cuda":
+            raise RuntimeError("g2ptq_b200 GPTQ requires layers on a CUDA device")
+        self.rows, self.columns = weight.shape
+        H_device = "cpu" if offload_hessians else self.dev
+        self._H = torch.zeros((self.num_layers, self.columns, self.columns),
+                              dtype=torch.float32, device=H_device)
+        self.nsamples = torch.tensor([0] * self.num_layers, device=self.dev)
+        self._n = [0] * self.num_layers          # host copy of nsamples
+        self._n_folded = [0] * self.num_layers   # samples already folded into H
+        self._init_stages()
+
+    # -- Hessian ----------------------------------------------------------
+    @property
+    def H(self):
+        self._flush_all()
+        return self._H
+
+    @H.setter
+    def H(self, value):
+        self._H = value
+
+    def _maybe_onload_hessian(self, idx=None):
+        """Onload the Hessian for the duration of the context (gptq_utils.py:109-113)."""
+        if not self.offload_hessians:
+            return contextlib.nullcontext()
+        return _onload(self, ("_H",))
+
+    def add_batch(self, idx, inp, out):
+        """gptq_utils.py:115-126 (the product is folded in lazily, see _engine)."""
+        if len(inp.shape) == 2:
+            inp = inp.unsqueeze(0)
+        tmp = inp.shape[0]
+        self._n[idx] += tmp
+        self.nsamples[idx] += tmp
+        self._append(idx, _engine.as_rows(inp, self.columns))
+
+    def _fold(self, idx, X, sub, scales):
+        n_old, n_new = self._n_folded[idx], self._n[idx]
+        self._require_device_stats(self._H)
+        ops.gram_update(self._H[idx], X, alpha=n_old / n_new, beta=2.0 / n_new,
+                        precision=_engine.PRECISION)
+        self._n_folded[idx] = n_new
+
+    # -- quantization -------------------------------------------------------
+    def fasterquant(self, blocksize=128, percdamp=0.01, groupsize=-1, actorder=False,
+                    static_groups=False, export_compressed_tensors=False, backend="torch",
+                    graph=False):
+        """gptq_utils.py:234-353.  ``backend`` and ``graph`` are accepted and ignored."""
+        B, R, C = self.num_layers, self.rows, self.columns
+        q0 = self.quantizer[0]
+        hclip = q0.hclip
+        with self._maybe_onload_hessian():
+            H = self.H
+            self.H = None
+            H_diag = torch.diagonal(H, dim1=-2, dim2=-1).clone() if hclip else None
+            W = torch.stack([l.weight.data for l in self.layers]).float().contiguous()
+            params = _engine.ParamSet(self.quantizer, B * R, C, groupsize, self.dev)
+            dynamic = not (groupsize == -1 or static_groups)
+            if not dynamic:
+                params.init_static(W.view(B * R, C), H_diag)
+            ops.prepare_hessian(H, W)
+            perm = invperm = None
+            if actorder:
+                perm, invperm = _engine.act_order_perm(ops.mean_diag(H))
+                W = ops.permute_cols(W, perm)
+                H = ops.permute_sym(H, perm)
+            if H_diag is not None and actorder:
+                H_diag = H_diag[:, perm].contiguous()
+            if hclip and dynamic:
+                raise NotImplementedError("g2ptq_b200: --w_hclip needs the clip search")
+            U, info, damps = _engine.factor_with_retry(H, percdamp)
+        colgroup = params.colgroup(perm, static_groups, self.dev)
+        W0 = W.clone()
+        codes = torch.empty(B, R, C, dtype=torch.int8, device=self.dev)
+
+        def compensate_and_cast(Wp):
+            ops.compensate(_lib.METHOD_GPTQ, Wp, U, params.scale, params.zero, colgroup, dynamic,
+                           groupsize, q0.bits, q0.sym, blocksize, codes, status=params.status,
+                           precision=_engine.PRECISION)
+            Q, cq = Wp, codes
+            if actorder:
+                Q = ops.permute_cols(Wp, perm, inverse=True)
+                cq = ops.permute_cols(codes, perm, inverse=True)
+            nan, outs = _engine.write_back(self.layers, Q, cq, params, q0.bits, groupsize, C,
+                                           export_compressed_tensors)
+            return nan, outs, cq
+
+        nan, outs, cq = compensate_and_cast(W)
+        flags = _engine.sync_check(info, nan, *params.statuses())
+        info_list = flags[:B]
+        if any(i != 0 for i in info_list):
+            _engine.retry_failed(H, U, info_list, damps)
+            params.status.zero_()
+            nan, outs, cq = compensate_and_cast(W0)
+            flags = _engine.sync_check(info, nan, *params.statuses())
+            flags[:B] = [0] * B
+        if any(f != 0 for f in flags[B + 1:]):
+            raise RuntimeError("WeightQuantizer.find_params: non-positive scale")
+        if flags[B] != 0:
+            raise ValueError("NaN in weights")
+        if dynamic:
+            params.bind_dynamic()
+        if export_compressed_tensors and dynamic and actorder:
+            raise AssertionError("Scales in the same quantization group should be the same.")
+        _engine.finish(self.layers, outs, cq, params, q0.bits, groupsize, C,
+                       export_compressed_tensors, R)
+        self._last_damps = damps
+
+    def free(self):
+        self._H = None
+        self.Losses = None
+        self.nsamples = None
+        self._stages = None
+
+
+@contextlib.contextmanager
+def _onload(owner, names):
+    staged = {}
+    for n in names:
+        host = getattr(owner, n, None)
+        if host is not None:
+            staged[n] = host
+            setattr(owner, n, host.to(owner.dev, non_blocking=host.is_pinned()))
+    try:
+        yield
+    finally:
+        for n in names:
+            v = getattr(owner, n, None)
+            if v is None or v.device.type == "cpu":
+                continue
+            if hasattr(owner, "_flush_all") and n == "_H":
+                owner._flush_all()
+                v = getattr(owner, n)
+            setattr(owner, n, v.to("cpu"))
+
+
+def reduce_to_target_rank(gptqs, gptq2rank):
+    """gptq_utils.py:362-391: sum the rank-local Hessians, rescaled by their
+    sample share, onto each object's owner rank."""
+    rank = dist.get_rank()
+    dist.barrier()
+    for gptq in gptqs:
+        with gptq._maybe_onload_hessian():
+            H = gptq.H
+            pending = []
+            target = gptq2rank[gptq]
+            global_n = gptq.nsamples.clone()
+            dist.all_reduce(global_n, op=dist.ReduceOp.SUM)
+            gn = global_n.cpu().tolist()
+            for b in range(gptq.num_layers):
+                if gn[b] == 0:
+                    H[b].zero_()
+                    gptq.nsamples[b].zero_()
+                else:
+                    H[b] *= gptq._n[b] / gn[b]
+                    pending.append(dist.reduce(H[b], op=dist.ReduceOp.SUM, dst=target,
+                                               async_op=True))
+            if rank == target:
+                gptq.nsamples.copy_(global_n)
+                gptq._n = list(gn)
+                gptq._n_folded = list(gn)
+            for w in pending:
+                w.wait()
+    dist.barrier()

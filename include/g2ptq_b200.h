@@ -1,0 +1,258 @@
+/*
+ * g2ptq_b200 -- C ABI of the B200 (sm_100a) quantization hot path.
+ *
+ * Every entry point takes raw device pointers, sizes, leading dimensions and a
+ * cudaStream_t passed as void*, enqueues its kernels on that stream and
+ * returns an int status (G2Q_OK, or a negative G2Q_ERR_* code for an invalid
+ * argument or a failed launch).  Entry points never allocate or free device
+ * memory and never synchronise the device: callers pass the scratch space a
+ * call needs (the *_workspace_bytes queries give its size).  Conditions that
+ * are only known on the device (a non-positive Cholesky pivot, a NaN, a zero
+ * quantization scale) are written to caller-provided device int words.
+ *
+ * Matrices are row-major fp32 unless stated.  "Token-major" activations are
+ * [T, C] with the channel index contiguous, exactly as a linear layer's input
+ * arrives in the reference's forward hooks.
+ *
+ * Each declaration names the reference interface it replaces (paths are
+ * relative to the G2PTQ project root).
+ */
+#ifndef G2PTQ_B200_H
+#define G2PTQ_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define G2Q_OK 0
+#define G2Q_ERR_INVALID_ARG (-1)
+#define G2Q_ERR_CUDA (-2)
+#define G2Q_ERR_UNSUPPORTED (-3)
+#define G2Q_ERR_NONFINITE (-4)
+#define G2Q_ERR_TIMEOUT (-5)
+#define G2Q_ERR_BAD_SCALE (-6)
+
+/* element types of activation inputs */
+#define G2Q_DTYPE_BF16 0
+#define G2Q_DTYPE_F32 1
+#define G2Q_DTYPE_F16 2
+
+/* compensation methods */
+#define G2Q_METHOD_GPTQ 0
+#define G2Q_METHOD_G2PTQ 1
+#define G2Q_METHOD_GPTAQ 2
+
+/* output masks of g2q_gemm */
+#define G2Q_MASK_FULL 0
+#define G2Q_MASK_LOWER 1        /* i >= j */
+#define G2Q_MASK_UPPER 2        /* i <= j */
+#define G2Q_MASK_STRICT_UPPER 3 /* i <  j, others set to zero */
+
+/* ABI version; bumped on any signature change. */
+int g2q_abi_version(void);
+
+/* Number of kernels this library has launched in the process so far
+ * (host-side count of successful launch calls). */
+int64_t g2q_launch_count(void);
+
+/* Human-readable text for a status code (static storage). */
+const char* g2q_status_string(int status);
+
+/* Copies `t` token rows of `src` ([t, C], row stride src_ld, element type
+ * src_dtype) into rows [row0, row0 + t) of a staging buffer `dst`
+ * ([*, dst_ld], element type dst_dtype: BF16 only for a BF16 source, else
+ * F32), converting the element type.  When `sub` is non-NULL the staged value
+ * is src - sub (same layout and type as src), which is how GPTAQ's
+ * (X_fp - X) operand is formed.
+ * Replaces the input handling of GPTQ.add_batch, gptq_utils/gptq_utils.py:115-125,
+ * and GPTAQ.add_batch, gptq_utils/gptaq_utils.py:130-146. */
+int g2q_stage_tokens(void* dst, int dst_dtype, int64_t dst_ld, int64_t row0,
+                     const void* src, const void* sub, int src_dtype, int64_t src_ld,
+                     int64_t t, int64_t C, void* stream);
+
+/* Gram-matrix update over staged tokens:
+ *   D[i, j] <- alpha * D[i, j] + beta * sum_t A[t, i] * s[t] * B[t, j]
+ * A is [T, M] (lda), B is [T, N] (ldb), both token-major with element type
+ * G2Q_DTYPE_BF16 or G2Q_DTYPE_F32; s[t] = row_scale[t * scale_stride] when
+ * row_scale is non-NULL, else 1.  symmetric != 0 (A == B, M == N, no row
+ * scale asymmetry needed) computes the upper triangle and mirrors it, leaving
+ * a full symmetric D.  precision: 0 = fp32 CUDA cores, 1 = tensor cores
+ * (bf16 operands exact for BF16 input; FP32 input split into bf16 hi/lo
+ * pairs), which needs `workspace` of g2q_gram_workspace_bytes bytes.
+ * Replaces the Hessian products of GPTQ.add_batch (gptq_utils/gptq_utils.py:123-126),
+ * G2PTQ.add_batch (gptq_utils/g2ptq_utils.py:193-200), GPTAQ.add_batch
+ * (gptq_utils/gptaq_utils.py:139-146) and GPTQGuided.add_batch
+ * (gptq_utils/gptq_guided_utils.py:78-80). */
+int g2q_gram_update(float* D, int64_t ldd, int64_t M, int64_t N,
+                    const void* A, int a_dtype, int64_t lda,
+                    const void* B, int b_dtype, int64_t ldb,
+                    const float* row_scale, int64_t scale_stride,
+                    int64_t T, int symmetric, float alpha, float beta, int precision,
+                    void* workspace, size_t workspace_bytes, void* stream);
+size_t g2q_gram_workspace_bytes(int64_t M, int64_t N, int64_t T, int precision);
+
+/* Adds sum_t x[t, c]^2 * scale to acc[c] after acc *= keep: the running mean
+ * of squared activations kept by G2PTQ/GPTQGuided.add_batch
+ * (gptq_utils/g2ptq_utils.py:195,201; gptq_utils/gptq_guided_utils.py:81). */
+int g2q_sq_colsum(float* acc, float keep, float scale, const void* X, int x_dtype,
+                  int64_t ldx, int64_t T, int64_t C, void* stream);
+
+/* Batched fp32 GEMM  C <- alpha * C + beta * op(A) op(B)  with an output mask.
+ * op(A) is M x K (A stored K x M when transA), op(B) is K x N (B stored N x K
+ * when transB).  Replaces the torch.bmm / baddbmm_ products of fasterquant:
+ * gptq_utils/g2ptq_utils.py:462,475-476 (G2PTQ Z and GHinv) and
+ * gptq_utils/gptaq_utils.py:350-352 (GPTAQ P). */
+int g2q_gemm(float* C, int64_t ldc, int64_t strideC,
+             const float* A, int64_t lda, int64_t strideA, int transA,
+             const float* B, int64_t ldb, int64_t strideB, int transB,
+             int64_t M, int64_t N, int64_t K, int64_t batch,
+             float alpha, float beta, int out_mask, void* stream);
+
+/* Damped inverse-Cholesky factor.  For each of `batch` matrices H[b] (C x C,
+ * symmetric, row stride ldh, batch stride C*ldh) computes upper-triangular
+ * U[b] with U^T U = (H + d I)^-1, d = damp_percent[b] * mean(diag H[b]).
+ * info[b] (device int) receives 0, the 1-based index of the first
+ * non-positive pivot, or -1 when the factor holds a NaN.  Route: UL
+ * factorization H + dI = V V^T (V upper), U = V^-1 -- potrf + trtri, half the
+ * work of potrf + potri + potrf.  Needs g2q_chol_workspace_bytes(C) bytes.
+ * Replaces the damped Cholesky chain of gptq_utils/gptq_utils.py:291-311
+ * (and its copies g2ptq_utils.py:430-450, gptaq_utils.py:323-343,
+ * gptq_guided_utils.py:145-165); the damp auto-increment retry stays with the
+ * caller, which reads `info`. */
+int g2q_chol_upper_inverse(float* U, const float* H, int64_t C, int64_t ldh, int64_t batch,
+                           const float* damp_percent_host, int* info,
+                           void* workspace, size_t workspace_bytes, void* stream);
+size_t g2q_chol_workspace_bytes(int64_t C);
+
+/* Per-row quantization parameters over `cols` columns of W (row stride ldw):
+ * xmin = min(min(x), 0), xmax = max(max(x), 0); symmetric:
+ * scale = max(|xmin|, xmax) / ((2^bits - 1) / 2), zero = 0; asymmetric:
+ * scale = (xmax - xmin) / (2^bits - 1), zero = clamp(round(minq - xmin/scale)).
+ * Results go to scale[r * param_ld] / zero[r * param_ld].  A non-positive
+ * scale sets *status to G2Q_ERR_BAD_SCALE.
+ * Replaces WeightQuantizer.find_params without clip search,
+ * utils/quant_utils.py:377-433. */
+int g2q_find_params(float* scale, float* zero, int64_t param_ld,
+                    const float* W, int64_t rows, int64_t cols, int64_t ldw,
+                    int bits, int sym, int* status, void* stream);
+
+/* Fake quantization  q = clamp(round(w / s) + z, -(maxq+1), maxq),
+ * out = s * (q - z)  with per-element parameters s = scale[r*param_ld + colmap[c]].
+ * Writes out (fp32, row stride ldo) and, when codes is non-NULL, int8 codes.
+ * Replaces WeightQuantizer.fake_quantize (utils/quant_utils.py:435-459) and
+ * common_utils.fake_quantize_grouped (gptq_utils/common_utils.py:33-45). */
+int g2q_fake_quantize(float* out, int64_t ldo, int8_t* codes, int64_t ldq,
+                      const float* W, int64_t ldw, int64_t rows, int64_t cols,
+                      const float* scale, const float* zero, int64_t param_ld,
+                      const int* colmap, int maxq, void* stream);
+
+/* One lazy-batch compensation block (the reference's kernel boundary).
+ * W[b] is rows x ncols (row stride ldw, batch stride w_bstride), hinv[b] is
+ * the ncols x ncols upper block (row stride ldh, batch stride h_bstride).
+ * Quantization parameters of row r, column c are
+ * scale[(b*rows + r) * param_ld + colmap[c]] (same for zero).
+ * In place: W <- dequantized Q; codes (int8, optional), err (fp32, optional,
+ * same layout as W).  G2PTQ also reads z and updates ghinv (same layout as W);
+ * GPTAQ reads p (same layout as hinv).  ncols <= 128.
+ * Replaces run_eager / _run_torch_compensation / _run_triton_compensation of
+ * gptq_utils/gptq_utils.py:28-90, gptq_utils/g2ptq_utils.py:34-126 and
+ * gptq_utils/gptaq_utils.py:28-100 (reference layout [B, blk, R] is the
+ * transpose of this one). */
+int g2q_compensate_block(int method, float* W, int64_t ldw, int64_t w_bstride,
+                         int64_t batch, int64_t rows, int64_t ncols,
+                         const float* hinv, int64_t ldh, int64_t h_bstride,
+                         const float* scale, const float* zero, int64_t param_ld,
+                         const int* colmap, int maxq,
+                         int8_t* codes, float* err,
+                         const float* z, float* ghinv, const float* p,
+                         void* stream);
+
+/* Whole block traversal of fasterquant: for each block of `blocksize`
+ * columns (dynamic groups: find parameters at each group start from the
+ * current W), compensate the block, then apply the trailing update
+ * W[:, i2:] -= Err @ U[i1:i2, i2:] (plus the G2PTQ / GPTAQ terms).
+ * W: [nl, rows, C] fp32, overwritten with the dequantized weights.
+ * U: [nl, C, C] upper factors.  scale/zero: [nl*rows, ngroups] (static
+ * parameters are read, dynamic ones are written).  colgroup[c]: parameter
+ * column of (permuted) column c.  codes: [nl, rows, C] int8 output.
+ * G2PTQ: z [nl, rows, C] read, gh [nl, rows, C] updated.  GPTAQ: p [nl, C, C].
+ * precision: 0 = fp32 CUDA-core trailing update, 1 = tensor cores
+ * (bf16x3 split).  Needs g2q_compensate_workspace_bytes bytes; *status
+ * receives G2Q_ERR_BAD_SCALE on a non-positive dynamic scale.
+ * Replaces GPTQ._run_compensation (gptq_utils/gptq_utils.py:165-232),
+ * G2PTQ._run_compensation (gptq_utils/g2ptq_utils.py:252-347) and
+ * GPTAQ._run_compensation (gptq_utils/gptaq_utils.py:193-261). */
+int g2q_compensate(int method, float* W, int64_t nl, int64_t rows, int64_t C,
+                   const float* U, float* scale, float* zero, int64_t ngroups,
+                   const int* colgroup, int dynamic_groups, int groupsize, int bits, int sym,
+                   int blocksize, int8_t* codes,
+                   const float* z, float* gh, const float* p, int precision,
+                   void* workspace, size_t workspace_bytes, int* status, void* stream);
+size_t g2q_compensate_workspace_bytes(int method, int64_t nl, int64_t rows, int64_t C,
+                                      int precision);
+
+/* Hessian preparation of fasterquant for `nl` layers: an all-zero H[b]
+ * becomes the identity (RTN fallback); columns with H[b][c][c] == 0 get
+ * H[b][c][c] = 1 and W[b][:, c] = 0 (and, when extra != NULL, extra[b][:, c]
+ * = 0 with the same layout as W; when gzero != NULL and H[b] was all zero,
+ * gzero[b] is cleared, rows x C).  W is [nl, rows, C].
+ * Replaces gptq_utils/gptq_utils.py:272-277, gptaq_utils.py:302-308,
+ * g2ptq_utils.py:394-401. */
+int g2q_prepare_hessian(float* H, int64_t nl, int64_t C, float* W, int64_t rows,
+                        float* extra, int64_t extra_rows, float* gzero, void* stream);
+
+/* Stable descending argsort of key[0..n) (ties keep index order) into perm
+ * (int64).  Replaces torch.argsort(..., descending=True) of the act-order
+ * permutation, gptq_utils/gptq_utils.py:281-282. */
+int g2q_argsort_desc(int64_t* perm, const float* key, int64_t n, void* stream);
+
+/* key[c] = mean over nl layers of H[b][c][c]  (gptq_utils/gptq_utils.py:281). */
+int g2q_mean_diag(float* key, const float* H, int64_t nl, int64_t C, void* stream);
+
+/* dst[b][r][c] = src[b][r][perm[c]] for float (elem_bytes 4) or int8 (1).
+ * With inverse != 0: dst[b][r][perm[c]] = src[b][r][c]. */
+int g2q_permute_cols(void* dst, const void* src, int elem_bytes, int64_t nl, int64_t rows,
+                     int64_t C, const int64_t* perm, int inverse, void* stream);
+
+/* dst[b][i][j] = src[b][perm[i]][perm[j]]  (gptq_utils/gptq_utils.py:289). */
+int g2q_permute_sym(float* dst, const float* src, int64_t nl, int64_t C,
+                    const int64_t* perm, void* stream);
+
+/* Casts n fp32 values to dst_dtype (G2Q_DTYPE_BF16/F16/F32) and counts NaNs
+ * into *nan_count (device int, accumulated).  Replaces the write-back cast and
+ * NaN check of gptq_utils/gptq_utils.py:346-350. */
+int g2q_cast_check(void* dst, int dst_dtype, const float* src, int64_t n, int* nan_count,
+                   void* stream);
+
+/* compressed-tensors packing of int8 codes [rows, cols] into int32
+ * [rows, ceil(cols / (32/bits))]: value + 2^(bits-1), 32/bits values per
+ * word, first value in the lowest bits.  Replaces pack_to_int32 as called by
+ * utils/compressed_tensors_utils.py:39. */
+int g2q_pack_int32(int32_t* out, const int8_t* codes, int64_t rows, int64_t cols, int bits,
+                   void* stream);
+
+/* G2PTQ trust-region step size (gptq_utils/g2ptq_utils.py:459-470):
+ * with GH = grad @ Hinv, qe = Qsub - Wsub, d = diag(Hinv)[c]:
+ *   loss = |(qe*GH + qe^2/2) / d|,  c_ = sum_c(grad*GH) - GH^2/d
+ *   c_ = max(c_, 2 alpha loss, tiny);  beta = mean_c(1 - sqrt(max(1 - 2 alpha loss / c_, 0)))
+ * All of grad, GH, Qsub, Wsub are [nl, rows, C]; dinv is [nl, C];
+ * beta is [nl, rows]. */
+int g2q_trust_region_beta(float* beta, const float* grad, const float* GH,
+                          const float* Qsub, const float* Wsub, const float* dinv,
+                          int64_t nl, int64_t rows, int64_t C, float alpha, void* stream);
+
+/* dinv[b][c] = sum_k U[b][k][c]^2 = diag(U^T U)  -- the diagonal of H^-1. */
+int g2q_diag_of_utu(float* dinv, const float* U, int64_t nl, int64_t C, void* stream);
+
+/* X[b][r][c] *= s[b*rows + r]  (row scaling, G2PTQ Z = (G U^T) * beta). */
+int g2q_scale_rows(float* X, const float* s, int64_t nl, int64_t rows, int64_t C,
+                   void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* G2PTQ_B200_H */
