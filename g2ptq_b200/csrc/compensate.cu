@@ -428,6 +428,16 @@ extern "C" size_t g2q_compensate_workspace_bytes(int method, int64_t nl, int64_t
   return b;
 }
 
+namespace g2q {
+int tc_trailing_update(float* W, long long C, long long rows, long long batch, long long i1,
+                       long long i2, int nc, const __nv_bfloat16* err_hi,
+                       const __nv_bfloat16* err_lo, long long err_stride,
+                       const __nv_bfloat16* u_hi, const __nv_bfloat16* u_lo, int* status,
+                       cudaStream_t st);
+int split_bf16_2d(__nv_bfloat16* hi, __nv_bfloat16* lo, const float* src, long long n,
+                  cudaStream_t st);
+}  // namespace g2q
+
 static char* align_up(char* p, size_t a) {
   return (char*)(((uintptr_t)p + a - 1) / a * a);
 }
@@ -444,13 +454,30 @@ extern "C" int g2q_compensate(int method, float* W, int64_t nl, int64_t rows, in
   if (dynamic_groups && groupsize <= 0) return G2Q_ERR_INVALID_ARG;
   if (method == G2Q_METHOD_G2PTQ && (!z || !gh)) return G2Q_ERR_INVALID_ARG;
   if (method == G2Q_METHOD_GPTAQ && !p) return G2Q_ERR_INVALID_ARG;
-  if (precision != 0) return G2Q_ERR_UNSUPPORTED;
+  if (precision != 0 && precision != 1) return G2Q_ERR_INVALID_ARG;
   if (workspace_bytes < g2q_compensate_workspace_bytes(method, nl, rows, C, precision))
     return G2Q_ERR_INVALID_ARG;
   cudaStream_t st = (cudaStream_t)stream;
   char* wsp = align_up((char*)workspace, 256);
   float* erra = (float*)wsp;
+  wsp = align_up(wsp + (size_t)nl * rows * BLK * sizeof(float), 256);
   const int maxq = (1 << (bits - 1)) - 1;
+  // Tensor-core trailing update (GPTQ): bf16 hi/lo copies of the error block
+  // (column-major, written by the block kernel) and of U (split once here).
+  const bool use_tc = precision == 1 && method == G2Q_METHOD_GPTQ;
+  __nv_bfloat16 *ea_hi = nullptr, *ea_lo = nullptr, *u_hi = nullptr, *u_lo = nullptr;
+  if (use_tc) {
+    const size_t ne = (size_t)nl * rows * BLK, nu = (size_t)nl * C * C;
+    ea_hi = (__nv_bfloat16*)wsp;
+    wsp = align_up(wsp + ne * 2, 256);
+    ea_lo = (__nv_bfloat16*)wsp;
+    wsp = align_up(wsp + ne * 2, 256);
+    u_hi = (__nv_bfloat16*)wsp;
+    wsp = align_up(wsp + nu * 2, 256);
+    u_lo = (__nv_bfloat16*)wsp;
+    wsp = align_up(wsp + nu * 2, 256);
+    G2Q_TRY(split_bf16_2d(u_hi, u_lo, U, (long long)nu, st));
+  }
   for (long long i1 = 0; i1 < C; i1 += blocksize) {
     const long long i2 = (i1 + blocksize < C) ? i1 + blocksize : C;
     const int nc = (int)(i2 - i1);
@@ -470,6 +497,7 @@ extern "C" int g2q_compensate(int method, float* W, int64_t nl, int64_t rows, in
     P.maxq = maxq;
     P.codes = codes + i1; P.ldq = C; P.q_bs = rows * C;
     P.erra = erra; P.ldea = rows; P.ea_bs = rows * BLK;
+    P.erra_hi = ea_hi; P.erra_lo = ea_lo;
     if (method == G2Q_METHOD_G2PTQ) {
       P.z = z + i1; P.gh = gh + i1; P.ldz = C; P.z_bs = rows * C;
     }
@@ -484,6 +512,12 @@ extern "C" int g2q_compensate(int method, float* W, int64_t nl, int64_t rows, in
       G2Q_CHECK_LAUNCH();
     }
     // W[:, i2:] -= Erra @ U[i1:i2, i2:]
+    if (use_tc) {
+      const int s_tc = tc_trailing_update(W, C, rows, nl, i1, i2, nc, ea_hi, ea_lo, BLK, u_hi,
+                                          u_lo, status, st);
+      if (s_tc == G2Q_OK) continue;
+      if (s_tc != G2Q_ERR_UNSUPPORTED) return s_tc;
+    }
     G2Q_TRY(simt_gemm_f32(W + i2, C, erra, rows, true, U + i1 * C + i2, C, false, rows, N, nc,
                           1.f, -1.f, G2Q_MASK_FULL, st, nl, rows * BLK, C * C, rows * C));
     if (method == G2Q_METHOD_G2PTQ) {

@@ -1,15 +1,533 @@
-// Tensor-core (tcgen05) Gram / GEMM path.  Placeholder entry points until the
-// sm_100a kernel lands; the fp32 CUDA-core path serves every call meanwhile.
+// Tensor-core (tcgen05) Gram / GEMM for sm_100a.
+//
+//   D[m, n] <- alpha * D[m, n] + beta * sum_k A[k, m] * B[k, n]
+//
+// Both operands are "MN-major" in global memory: for every k, the m (or n)
+// index is contiguous.  That is how the two hot products arrive:
+//   * Hessian Gram  H += X^T X  with X token-major [T, C]  (k = token),
+//   * GPTQ trailing update  W[:, i2:] -= Err @ U[i1:i2, i2:]  with the block
+//     error stored column-major [blk, rows] by the compensation kernel and U
+//     row-major (k = block column).
+// Tiles of 128 x 64 (MN x K) bf16 are fed by TMA (two 64 x 64 boxes, 128-byte
+// swizzle) into a multi-stage shared-memory ring; one thread issues
+// tcgen05.mma (M = 128, N = 128, K = 16, bf16 in, fp32 accumulate in TMEM);
+// four epilogue warps read the accumulator with tcgen05.ld and apply
+// alpha / beta, the bounds and the symmetric mirror.
+// fp32 operands are carried as a bf16 hi/lo pair and multiplied as
+// hi*hi + hi*lo + lo*hi (three MMAs per K step).
+//
+// Warp roles (192 threads): warp 0 TMA producer, warp 1 TMEM owner + MMA
+// issuer, warps 2-5 epilogue (TMEM lane quadrant = warp % 4).
+// Every wait on an mbarrier is bounded; on expiry the CTA records
+// G2Q_ERR_TIMEOUT in the caller's status word and winds down.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "gemm_simt.cuh"
 
 namespace g2q {
+namespace tc {
 
-size_t tc_gram_workspace_bytes(long long, long long, long long) { return 0; }
+constexpr int BM = 128, BN = 128, BK = 64;
+constexpr int CHUNK_BYTES = 64 * BK * 2;     // one 64 (MN) x 64 (K) bf16 box
+constexpr int TILE_BYTES = 2 * CHUNK_BYTES;  // one 128 x 64 operand tile
+constexpr long long kWaitCycles = 4000000000LL;
 
-int tc_gram(float*, long long, long long, long long, const void*, int, long long, const void*,
-            int, long long, const float*, long long, long long, int, float, float, void*, size_t,
-            cudaStream_t) {
-  return G2Q_ERR_UNSUPPORTED;
+struct Params {
+  float* D;
+  long long ldd, d_bs;
+  long long M, N;
+  int num_kb;
+  long long ka_batch, kb_batch;  // per-batch row offset of A / B in their tensor maps
+  long long ka0, kb0;            // first K row of A / B
+  long long nb0;                 // first N coordinate of B
+  float alpha, beta;
+  int symmetric;
+  int* status;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t a, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(a), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t a, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(a), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_wait(uint32_t a, uint32_t parity, volatile int* abort_flag,
+                                          int* status) {
+  const long long t0 = clock64();
+  while (true) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > kWaitCycles) {
+      *abort_flag = 1;
+      record_error(status, G2Q_ERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                            uint32_t mbar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(mbar)
+      : "memory");
+}
+
+// Shared-memory matrix descriptor of an MN-major, 128-byte-swizzled operand:
+// 64-element MN chunks 8 KB apart (LBO), groups of 8 K rows 1 KB apart (SBO).
+__device__ __forceinline__ uint64_t desc_mn_sw128(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFF) >> 4);
+  d |= (uint64_t)(CHUNK_BYTES >> 4) << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+// kind::f16 instruction descriptor: bf16 x bf16 -> f32, both MN-major, M=128, N=BN.
+__host__ __device__ constexpr uint32_t idesc_bf16_mn() {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (1u << 15) | (1u << 16) |
+         ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void umma_commit(uint32_t mbar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   mbar)
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+template <int NA, int NB>
+struct Cfg {
+  static constexpr int STAGE_BYTES = (NA + NB) * TILE_BYTES;
+  static constexpr int STAGES = (NA + NB) == 2 ? 6 : ((NA + NB) == 3 ? 4 : 3);
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+  static constexpr int PRODUCTS = 1 + (NB == 2 ? 1 : 0) + (NA == 2 ? 1 : 0);
+};
+
+template <int NA, int NB>
+__global__ void __launch_bounds__(192, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap ma0, const __grid_constant__ CUtensorMap ma1,
+                   const __grid_constant__ CUtensorMap mb0, const __grid_constant__ CUtensorMap mb1,
+                   Params p) {
+  using K = Cfg<NA, NB>;
+  const int mt = blockIdx.y, nt = blockIdx.x;
+  const long long bz = blockIdx.z;
+  if (p.symmetric && nt < mt) return;  // tile holds no element of the upper triangle
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + K::STAGES * K::STAGE_BYTES);
+  // bars[0..S): full, bars[S..2S): empty, bars[2S]: accumulator ready
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * K::STAGES + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + K::STAGES);
+  const uint32_t accum_bar = smem_u32(bars + 2 * K::STAGES);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < K::STAGES; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    mbar_init(accum_bar, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_holder)),
+                 "r"(BN)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = *tmem_holder;
+  const int m0 = mt * BM, n0 = nt * BN;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int kb = 0; kb < p.num_kb; ++kb) {
+        const int s = kb % K::STAGES;
+        const uint32_t ph = (kb / K::STAGES) & 1;
+        if (!mbar_wait(empty0 + 8 * s, ph ^ 1, abort_flag, p.status)) break;
+        const uint32_t fb = full0 + 8 * s;
+        mbar_expect_tx(fb, K::STAGE_BYTES);
+        const uint32_t st = smem_u32(smem + s * K::STAGE_BYTES);
+        const int ya = (int)(p.ka_batch * bz + p.ka0 + (long long)kb * BK);
+        const int yb = (int)(p.kb_batch * bz + p.kb0 + (long long)kb * BK);
+        const int xb = (int)(p.nb0 + n0);
+        tma_load_2d(st, &ma0, m0, ya, fb);
+        tma_load_2d(st + CHUNK_BYTES, &ma0, m0 + 64, ya, fb);
+        if (NA == 2) {
+          tma_load_2d(st + TILE_BYTES, &ma1, m0, ya, fb);
+          tma_load_2d(st + TILE_BYTES + CHUNK_BYTES, &ma1, m0 + 64, ya, fb);
+        }
+        const uint32_t sb = st + NA * TILE_BYTES;
+        tma_load_2d(sb, &mb0, xb, yb, fb);
+        tma_load_2d(sb + CHUNK_BYTES, &mb0, xb + 64, yb, fb);
+        if (NB == 2) {
+          tma_load_2d(sb + TILE_BYTES, &mb1, xb, yb, fb);
+          tma_load_2d(sb + TILE_BYTES + CHUNK_BYTES, &mb1, xb + 64, yb, fb);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_mn();
+      bool ok = true;
+      for (int kb = 0; kb < p.num_kb; ++kb) {
+        const int s = kb % K::STAGES;
+        const uint32_t ph = (kb / K::STAGES) & 1;
+        if (!mbar_wait(full0 + 8 * s, ph, abort_flag, p.status)) {
+          ok = false;
+          break;
+        }
+        fence_after();
+        const uint32_t sa = smem_u32(smem + s * K::STAGE_BYTES);
+        const uint32_t sb = sa + NA * TILE_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk) {
+          const uint32_t off = kk * 2048;  // 16 K rows = two 8-row swizzle groups
+          const uint32_t acc0 = (kb > 0 || kk > 0) ? 1u : 0u;
+          umma_bf16(tmem, desc_mn_sw128(sa + off), desc_mn_sw128(sb + off), idesc, acc0);
+          if (NB == 2)
+            umma_bf16(tmem, desc_mn_sw128(sa + off), desc_mn_sw128(sb + TILE_BYTES + off), idesc,
+                      1u);
+          if (NA == 2)
+            umma_bf16(tmem, desc_mn_sw128(sa + TILE_BYTES + off), desc_mn_sw128(sb + off), idesc,
+                      1u);
+        }
+        umma_commit(empty0 + 8 * s);
+      }
+      if (ok) umma_commit(accum_bar);
+    }
+  } else {
+    // epilogue warps 2..5
+    const bool ok = mbar_wait(accum_bar, 0, abort_flag, p.status);
+    fence_after();
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const long long gm = m0 + row;
+    float* Db = p.D + bz * p.d_bs;
+    const bool vec_ok = ((p.ldd & 3) == 0) && ((reinterpret_cast<uintptr_t>(Db) & 15) == 0);
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t r[32];
+      tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32), r);
+      if (!ok || gm >= p.M) continue;
+      const long long nbase = n0 + c * 32;
+#pragma unroll
+      for (int j4 = 0; j4 < 8; ++j4) {
+        const long long gn = nbase + 4 * j4;
+        float v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) v[u] = p.beta * __uint_as_float(r[4 * j4 + u]);
+        float* dst = Db + gm * p.ldd + gn;
+        if (vec_ok && gn + 3 < p.N && (!p.symmetric || gn >= gm)) {
+          float4* d4 = reinterpret_cast<float4*>(dst);
+          if (p.alpha != 0.f) {
+            const float4 o = *d4;
+            v[0] = fmaf(p.alpha, o.x, v[0]);
+            v[1] = fmaf(p.alpha, o.y, v[1]);
+            v[2] = fmaf(p.alpha, o.z, v[2]);
+            v[3] = fmaf(p.alpha, o.w, v[3]);
+          }
+          *d4 = make_float4(v[0], v[1], v[2], v[3]);
+        } else {
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            if (gn + u >= p.N || (p.symmetric && gn + u < gm)) continue;
+            if (p.alpha != 0.f) v[u] = fmaf(p.alpha, dst[u], v[u]);
+            dst[u] = v[u];
+          }
+        }
+        if (p.symmetric) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            if (gn + u < p.N && gn + u > gm) Db[(gn + u) * p.ldd + gm] = v[u];
+        }
+      }
+    }
+  }
+  fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN)
+                 : "memory");
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// 2-D bf16 tensor [outer, inner] with row stride ld (elements), 64 x 64 boxes.
+static bool make_map(CUtensorMap* m, const void* base, long long inner, long long outer,
+                     long long ld) {
+  auto enc = encode_fn();
+  if (!enc) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || ((ld * 2) & 15) || inner <= 0 || outer <= 0)
+    return false;
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {64, (cuuint32_t)BK};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
+}
+
+template <int NA, int NB>
+static int launch(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b0,
+                  const CUtensorMap& b1, const Params& p, long long batch, cudaStream_t st) {
+  using K = Cfg<NA, NB>;
+  static int attr_done[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return G2Q_ERR_CUDA;
+  if (dev >= 64 || !attr_done[dev]) {
+    if (cudaFuncSetAttribute(tc_gemm_kernel<NA, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             K::SMEM) != cudaSuccess)
+      return G2Q_ERR_CUDA;
+    if (dev < 64) attr_done[dev] = 1;
+  }
+  dim3 grid(cdiv(p.N, BN), cdiv(p.M, BM), (unsigned)batch);
+  if (grid.y > 65535u || grid.z > 65535u) return G2Q_ERR_INVALID_ARG;
+  tc_gemm_kernel<NA, NB><<<grid, 192, K::SMEM, st>>>(a0, a1, b0, b1, p);
+  G2Q_CHECK_LAUNCH();
+  return G2Q_OK;
+}
+
+static int dispatch(int na, int nb, const CUtensorMap& a0, const CUtensorMap& a1,
+                    const CUtensorMap& b0, const CUtensorMap& b1, const Params& p,
+                    long long batch, cudaStream_t st) {
+  if (na == 1 && nb == 1) return launch<1, 1>(a0, a1, b0, b1, p, batch, st);
+  if (na == 1 && nb == 2) return launch<1, 2>(a0, a1, b0, b1, p, batch, st);
+  if (na == 2 && nb == 1) return launch<2, 1>(a0, a1, b0, b1, p, batch, st);
+  return launch<2, 2>(a0, a1, b0, b1, p, batch, st);
+}
+
+template <typename S>
+__global__ void split_rows_kernel(const S* X, long long ldx, long long T, long long C,
+                                  const float* s, long long sstride, __nv_bfloat16* hi,
+                                  __nv_bfloat16* lo, long long ldo) {
+  const long long n = T * C;
+  for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < n;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const long long t = idx / C, c = idx - t * C;
+    float v;
+    if constexpr (sizeof(S) == 2) v = __bfloat162float(X[t * ldx + c]);
+    else v = X[t * ldx + c];
+    if (s) v *= s[t * sstride];
+    __nv_bfloat16 h, l;
+    split_bf16(v, &h, &l);
+    hi[t * ldo + c] = h;
+    if (lo) lo[t * ldo + c] = l;
+  }
+}
+
+static int grid_for(long long n) {
+  long long b = (n + 255) / 256;
+  if (b > 148 * 64) b = 148 * 64;
+  return (int)(b < 1 ? 1 : b);
+}
+
+static int split_rows(const void* X, int dtype, long long ldx, long long T, long long C,
+                      const float* s, long long sstride, __nv_bfloat16* hi, __nv_bfloat16* lo,
+                      long long ldo, cudaStream_t st) {
+  if (T * C == 0) return G2Q_OK;
+  if (dtype == G2Q_DTYPE_BF16)
+    split_rows_kernel<__nv_bfloat16><<<grid_for(T * C), 256, 0, st>>>(
+        (const __nv_bfloat16*)X, ldx, T, C, s, sstride, hi, lo, ldo);
+  else
+    split_rows_kernel<float><<<grid_for(T * C), 256, 0, st>>>((const float*)X, ldx, T, C, s,
+                                                              sstride, hi, lo, ldo);
+  G2Q_CHECK_LAUNCH();
+  return G2Q_OK;
+}
+
+static long long round8(long long v) { return (v + 7) / 8 * 8; }
+
+}  // namespace tc
+
+size_t tc_gram_workspace_bytes(long long M, long long N, long long T) {
+  const long long w = tc::round8(M > N ? M : N);
+  return (size_t)(4 * T * w * 2 + 4 * 256);
+}
+
+int split_bf16_2d(__nv_bfloat16* hi, __nv_bfloat16* lo, const float* src, long long n,
+                  cudaStream_t st) {
+  return tc::split_rows(src, G2Q_DTYPE_F32, n, 1, n, nullptr, 0, hi, lo, n, st);
+}
+
+// Gram update on tensor cores (see g2q_gram_update).  Falls back to the fp32
+// CUDA-core kernel where TMA cannot describe the operands (row strides that
+// are not a multiple of 8 elements, misaligned bases) or there is no work.
+int tc_gram(float* D, long long ldd, long long M, long long N, const void* A, int a_dtype,
+            long long lda, const void* B, int b_dtype, long long ldb, const float* row_scale,
+            long long scale_stride, long long T, int symmetric, float alpha, float beta,
+            void* workspace, size_t workspace_bytes, cudaStream_t st) {
+  SimtArgs sa{};
+  sa.A = A; sa.B = B; sa.C = D;
+  sa.lda = lda; sa.ldb = ldb; sa.ldc = ldd;
+  sa.M = M; sa.N = N; sa.K = T;
+  sa.alpha = alpha; sa.beta = beta;
+  sa.kscale = row_scale; sa.kscale_stride = scale_stride;
+  sa.mirror = symmetric ? 1 : 0;
+  if (T == 0 || !tc::encode_fn()) return simt_gemm(sa, true, false, a_dtype, b_dtype, 1, st);
+  const long long w = tc::round8(M > N ? M : N);
+  char* ws = (char*)workspace;
+  auto take = [&](long long elems) -> __nv_bfloat16* {
+    uintptr_t p = ((uintptr_t)ws + 255) & ~(uintptr_t)255;
+    ws = (char*)p + elems * 2;
+    return (__nv_bfloat16*)p;
+  };
+  const void* a_terms[2] = {A, nullptr};
+  const void* b_terms[2] = {B, nullptr};
+  long long lda_t = lda, ldb_t = ldb;
+  int na = 1, nb = 1;
+  const bool same = (A == B) && (a_dtype == b_dtype) && !row_scale;
+  if (a_dtype != G2Q_DTYPE_BF16) {
+    if (!workspace || workspace_bytes < tc_gram_workspace_bytes(M, N, T))
+      return G2Q_ERR_INVALID_ARG;
+    __nv_bfloat16* hi = take(T * w);
+    __nv_bfloat16* lo = take(T * w);
+    G2Q_TRY(tc::split_rows(A, a_dtype, lda, T, M, nullptr, 0, hi, lo, w, st));
+    a_terms[0] = hi;
+    a_terms[1] = lo;
+    lda_t = w;
+    na = 2;
+  }
+  if (same) {
+    b_terms[0] = a_terms[0];
+    b_terms[1] = a_terms[1];
+    ldb_t = lda_t;
+    nb = na;
+  } else if (b_dtype != G2Q_DTYPE_BF16 || row_scale) {
+    if (!workspace || workspace_bytes < tc_gram_workspace_bytes(M, N, T))
+      return G2Q_ERR_INVALID_ARG;
+    __nv_bfloat16* hi = take(T * w);
+    __nv_bfloat16* lo = take(T * w);
+    G2Q_TRY(tc::split_rows(B, b_dtype, ldb, T, N, row_scale, scale_stride, hi, lo, w, st));
+    b_terms[0] = hi;
+    b_terms[1] = lo;
+    ldb_t = w;
+    nb = 2;
+  }
+  CUtensorMap ma[2], mb[2];
+  bool ok = tc::make_map(&ma[0], a_terms[0], M, T, lda_t) &&
+            tc::make_map(&mb[0], b_terms[0], N, T, ldb_t);
+  ok = ok && (na == 1 || tc::make_map(&ma[1], a_terms[1], M, T, lda_t));
+  ok = ok && (nb == 1 || tc::make_map(&mb[1], b_terms[1], N, T, ldb_t));
+  if (!ok) return simt_gemm(sa, true, false, a_dtype, b_dtype, 1, st);
+  if (na == 1) ma[1] = ma[0];
+  if (nb == 1) mb[1] = mb[0];
+  tc::Params p{};
+  p.D = D; p.ldd = ldd; p.d_bs = 0;
+  p.M = M; p.N = N;
+  p.num_kb = (int)((T + tc::BK - 1) / tc::BK);
+  p.alpha = alpha; p.beta = beta;
+  p.symmetric = symmetric ? 1 : 0;
+  p.status = nullptr;
+  return tc::dispatch(na, nb, ma[0], ma[1], mb[0], mb[1], p, 1, st);
+}
+
+// W[b][:, i2 + n] -= sum_k Err[b][k][m] * U[b][i1 + k][i2 + n] on tensor cores.
+// err_hi / err_lo: [batch][err_stride rows][rows] bf16 (column-major error
+// blocks), u_hi / u_lo: [batch][C][C] bf16.  Returns G2Q_ERR_UNSUPPORTED when
+// the shapes do not meet TMA's alignment rules (the caller then uses the
+// CUDA-core path).
+int tc_trailing_update(float* W, long long C, long long rows, long long batch, long long i1,
+                       long long i2, int nc, const __nv_bfloat16* err_hi,
+                       const __nv_bfloat16* err_lo, long long err_stride,
+                       const __nv_bfloat16* u_hi, const __nv_bfloat16* u_lo, int* status,
+                       cudaStream_t st) {
+  if ((nc % tc::BK) || (i2 % 8) || (rows % 8) || (C % 8) || !tc::encode_fn())
+    return G2Q_ERR_UNSUPPORTED;
+  CUtensorMap ma[2], mb[2];
+  bool ok = tc::make_map(&ma[0], err_hi, rows, batch * err_stride, rows) &&
+            tc::make_map(&ma[1], err_lo, rows, batch * err_stride, rows) &&
+            tc::make_map(&mb[0], u_hi, C, batch * C, C) &&
+            tc::make_map(&mb[1], u_lo, C, batch * C, C);
+  if (!ok) return G2Q_ERR_UNSUPPORTED;
+  tc::Params p{};
+  p.D = W + i2; p.ldd = C; p.d_bs = rows * C;
+  p.M = rows; p.N = C - i2;
+  p.num_kb = nc / tc::BK;
+  p.ka_batch = err_stride; p.ka0 = 0;
+  p.kb_batch = C; p.kb0 = i1;
+  p.nb0 = i2;
+  p.alpha = 1.f; p.beta = -1.f;
+  p.symmetric = 0;
+  p.status = status;
+  return tc::dispatch(2, 2, ma[0], ma[1], mb[0], mb[1], p, batch, st);
 }
 
 }  // namespace g2q

@@ -163,7 +163,7 @@ def fake_quantize(W, scale, zero, maxq, colmap=None, out=None, codes=None):
     ``scale[r, colmap[c]]`` (``colmap`` None: column 0 of the parameters)."""
     _cuda(W, scale, zero, colmap, out, codes)
     rows, cols = W.shape
-    if out is None and codes is None:
+    if out is None:
         out = torch.empty(rows, cols, dtype=torch.float32, device=W.device)
     pld = scale.stride(0) if scale.dim() == 2 else 1
     call("g2q_fake_quantize", _ptr(out), 0 if out is None else out.stride(0), _ptr(codes),

@@ -104,7 +104,7 @@ def test_gram_update_vs_torch(dtype, sym, scaled):
     Yd = (Y if not sym else X).double()
     w = torch.ones(T, device=DEV, dtype=torch.float64) if s is None else s[:, 1].double()
     ref = 0.75 * D0.double() + 0.125 * (Yd.T @ (Xd * w[:, None]))
-    assert rel_fro(D, ref) < 1e-6
+    assert rel_fro(D, ref) < 5e-6
 
 
 def test_chol_upper_inverse_matches_oracle(golden):
@@ -362,14 +362,15 @@ def test_guided_fasterquant_vs_reference(golden, case):
 # larger shapes against the numpy oracle
 # ---------------------------------------------------------------------------
 
-def synthetic_hessian(C, T, seed, outliers=4):
+def synthetic_hessian(C, T, seed, outliers=4, calls=4):
+    """Activations of ``calls`` sequences and the oracle's running Hessian over them."""
     rng = np.random.default_rng(seed)
-    X = rng.standard_normal((T, C)).astype(np.float32)
-    X[:, rng.choice(C, outliers, replace=False)] *= 20.0
+    X = rng.standard_normal((calls, T // calls, C)).astype(np.float32)
+    X[..., rng.choice(C, outliers, replace=False)] *= 20.0
     H = np.zeros((C, C), np.float32)
     n = 0
-    for s in range(0, T, 512):
-        H, n = ohess.gptq_add_batch(H, n, X[None, s:s + 512])
+    for s in range(calls):
+        H, n = ohess.gptq_add_batch(H, n, X[s:s + 1])
     return X, H
 
 
@@ -385,7 +386,8 @@ def test_gptq_pipeline_vs_oracle(rows, cols, bits, sym, gs, act):
     layers = [linear(W[0])]
     obj = gptq_utils.GPTQ(layers)
     obj.quantizer = quantizers(bits, sym, cols, gs)
-    obj.add_batch(0, t(X)[None], None)
+    for s in range(X.shape[0]):
+        obj.add_batch(0, t(X[s:s + 1]), None)
     assert rel_fro(obj.H[0], H) < 1e-5
     Hd = obj.H.clone()
     obj.fasterquant(blocksize=128, percdamp=0.01, groupsize=gs, actorder=act, static_groups=act)
