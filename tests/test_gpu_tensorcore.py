@@ -26,7 +26,8 @@ def rel_fro(a, b):
     return float((a - b).norm() / b.norm())
 
 
-@pytest.mark.parametrize("T,C", [(2048, 512), (1000, 200), (4096, 1376), (777, 4096)])
+@pytest.mark.parametrize("T,C", [(2048, 512), (1000, 200), (4096, 1376), (777, 4096),
+                                 (16384, 4096)])
 def test_tc_gram_bf16_symmetric(T, C):
     g = torch.Generator(device=DEV).manual_seed(T + C)
     X = torch.randn(T, C, device=DEV, generator=g)
@@ -37,7 +38,7 @@ def test_tc_gram_bf16_symmetric(T, C):
     D = D0.clone()
     ops.gram_update(D, X, alpha=0.5, beta=2.0 / 7, precision=1)
     ref = 0.5 * D0.double() + (2.0 / 7) * (X.double().T @ X.double())
-    assert rel_fro(D, ref) < 1e-6
+    assert rel_fro(D, ref) < 1e-5
     assert torch.equal(D, D.T)
 
 
