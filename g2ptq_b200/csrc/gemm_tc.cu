@@ -16,6 +16,14 @@
 // fp32 operands are carried as a bf16 hi/lo pair and multiplied as
 // hi*hi + hi*lo + lo*hi (three MMAs per K step).
 //
+// Accumulator promotion: the tensor core adds each MMA's partial sum into the
+// TMEM accumulator with a bias of about one fp32 ulp (measured: the relative
+// error of a long Gram product grows linearly with K, every diagonal entry
+// too small).  The MMA warp therefore accumulates at most `promote_kb` K
+// blocks into one of two TMEM buffers, and the epilogue warps drain each
+// finished buffer into an fp32 register accumulator with rounded adds while
+// the other buffer fills.  The bias stays below ~1e-6 relative for any K.
+//
 // Warp roles (192 threads): warp 0 TMA producer, warp 1 TMEM owner + MMA
 // issuer, warps 2-5 epilogue (TMEM lane quadrant = warp % 4).
 // Every wait on an mbarrier is bounded; on expiry the CTA records
@@ -43,6 +51,7 @@ struct Params {
   long long nb0;                 // first N coordinate of B
   float alpha, beta;
   int symmetric;
+  int promote_kb;  // K blocks accumulated in TMEM before the epilogue drains them
   int* status;
 };
 
@@ -123,6 +132,10 @@ __device__ __forceinline__ void umma_commit(uint32_t mbar) {
                : "memory");
 }
 
+__device__ __forceinline__ void mbar_arrive(uint32_t a) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(a) : "memory");
+}
+
 __device__ __forceinline__ void fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
@@ -150,6 +163,8 @@ struct Cfg {
   static constexpr int STAGES = (NA + NB) == 2 ? 6 : ((NA + NB) == 3 ? 4 : 3);
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
   static constexpr int PRODUCTS = 1 + (NB == 2 ? 1 : 0) + (NA == 2 ? 1 : 0);
+  // K blocks per TMEM accumulation group: 16 MMAs for one product, 24 for three
+  static constexpr int PROMOTE_KB = PRODUCTS == 1 ? 4 : 2;
 };
 
 template <int NA, int NB>
@@ -166,27 +181,32 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + K::STAGES * K::STAGE_BYTES);
-  // bars[0..S): full, bars[S..2S): empty, bars[2S]: accumulator ready
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * K::STAGES + 1);
+  // bars[0..S): full, [S..2S): empty, [2S..2S+2): accumulator full, [2S+2..2S+4): drained
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * K::STAGES + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + K::STAGES);
-  const uint32_t accum_bar = smem_u32(bars + 2 * K::STAGES);
+  const uint32_t accf0 = smem_u32(bars + 2 * K::STAGES);
+  const uint32_t acce0 = smem_u32(bars + 2 * K::STAGES + 2);
+  const int ngroups = (p.num_kb + p.promote_kb - 1) / p.promote_kb;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < K::STAGES; ++s) {
       mbar_init(full0 + 8 * s, 1);
       mbar_init(empty0 + 8 * s, 1);
     }
-    mbar_init(accum_bar, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(accf0 + 8 * b, 1);
+      mbar_init(acce0 + 8 * b, 128);
+    }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_holder)),
-                 "r"(BN)
+                 "r"(2 * BN)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -226,54 +246,78 @@ __global__ void __launch_bounds__(192, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_bf16_mn();
-      bool ok = true;
-      for (int kb = 0; kb < p.num_kb; ++kb) {
-        const int s = kb % K::STAGES;
-        const uint32_t ph = (kb / K::STAGES) & 1;
-        if (!mbar_wait(full0 + 8 * s, ph, abort_flag, p.status)) {
-          ok = false;
-          break;
-        }
+      int kb = 0;
+      for (int g = 0; g < ngroups; ++g) {
+        const int buf = g & 1;
+        const uint32_t use_ph = (uint32_t)((g >> 1) & 1);
+        if (!mbar_wait(acce0 + 8 * buf, use_ph ^ 1, abort_flag, p.status)) break;
         fence_after();
-        const uint32_t sa = smem_u32(smem + s * K::STAGE_BYTES);
-        const uint32_t sb = sa + NA * TILE_BYTES;
+        const uint32_t acc_t = tmem + (uint32_t)(buf * BN);
+        const int kend = (kb + p.promote_kb < p.num_kb) ? kb + p.promote_kb : p.num_kb;
+        const int kstart = kb;
+        bool ok = true;
+        for (; kb < kend; ++kb) {
+          const int s = kb % K::STAGES;
+          const uint32_t ph = (kb / K::STAGES) & 1;
+          if (!mbar_wait(full0 + 8 * s, ph, abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          fence_after();
+          const uint32_t sa = smem_u32(smem + s * K::STAGE_BYTES);
+          const uint32_t sb = sa + NA * TILE_BYTES;
 #pragma unroll
-        for (int kk = 0; kk < BK / 16; ++kk) {
-          const uint32_t off = kk * 2048;  // 16 K rows = two 8-row swizzle groups
-          const uint32_t acc0 = (kb > 0 || kk > 0) ? 1u : 0u;
-          umma_bf16(tmem, desc_mn_sw128(sa + off), desc_mn_sw128(sb + off), idesc, acc0);
-          if (NB == 2)
-            umma_bf16(tmem, desc_mn_sw128(sa + off), desc_mn_sw128(sb + TILE_BYTES + off), idesc,
-                      1u);
-          if (NA == 2)
-            umma_bf16(tmem, desc_mn_sw128(sa + TILE_BYTES + off), desc_mn_sw128(sb + off), idesc,
-                      1u);
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint32_t off = kk * 2048;  // 16 K rows = two 8-row swizzle groups
+            const uint32_t acc0 = (kb > kstart || kk > 0) ? 1u : 0u;
+            umma_bf16(acc_t, desc_mn_sw128(sa + off), desc_mn_sw128(sb + off), idesc, acc0);
+            if (NB == 2)
+              umma_bf16(acc_t, desc_mn_sw128(sa + off), desc_mn_sw128(sb + TILE_BYTES + off),
+                        idesc, 1u);
+            if (NA == 2)
+              umma_bf16(acc_t, desc_mn_sw128(sa + TILE_BYTES + off), desc_mn_sw128(sb + off),
+                        idesc, 1u);
+          }
+          umma_commit(empty0 + 8 * s);
         }
-        umma_commit(empty0 + 8 * s);
+        if (!ok) break;
+        umma_commit(accf0 + 8 * buf);
       }
-      if (ok) umma_commit(accum_bar);
     }
   } else {
-    // epilogue warps 2..5
-    const bool ok = mbar_wait(accum_bar, 0, abort_flag, p.status);
-    fence_after();
+    // epilogue warps 2..5: drain each accumulator buffer into registers
     const int q = warp & 3;
     const int row = q * 32 + lane;
     const long long gm = m0 + row;
+    float acc[BN];
+#pragma unroll
+    for (int j = 0; j < BN; ++j) acc[j] = 0.f;
+    bool ok = true;
+    for (int g = 0; g < ngroups; ++g) {
+      const int buf = g & 1;
+      const uint32_t use_ph = (uint32_t)((g >> 1) & 1);
+      if (ok) ok = mbar_wait(accf0 + 8 * buf, use_ph, abort_flag, p.status);
+      fence_after();
+      const uint32_t base = tmem + (uint32_t)(buf * BN) + ((uint32_t)(q * 32) << 16);
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(base + (uint32_t)(c * 32), r);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) acc[c * 32 + j] += __uint_as_float(r[j]);
+      }
+      fence_before();
+      mbar_arrive(acce0 + 8 * buf);
+    }
     float* Db = p.D + bz * p.d_bs;
     const bool vec_ok = ((p.ldd & 3) == 0) && ((reinterpret_cast<uintptr_t>(Db) & 15) == 0);
-#pragma unroll 1
-    for (int c = 0; c < BN / 32; ++c) {
-      uint32_t r[32];
-      tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32), r);
-      if (!ok || gm >= p.M) continue;
-      const long long nbase = n0 + c * 32;
+    if (ok && gm < p.M) {
 #pragma unroll
-      for (int j4 = 0; j4 < 8; ++j4) {
-        const long long gn = nbase + 4 * j4;
+      for (int j4 = 0; j4 < BN / 4; ++j4) {
+        const long long gn = n0 + 4 * j4;
         float v[4];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) v[u] = p.beta * __uint_as_float(r[4 * j4 + u]);
+        for (int u = 0; u < 4; ++u) v[u] = p.beta * acc[4 * j4 + u];
         float* dst = Db + gm * p.ldd + gn;
         if (vec_ok && gn + 3 < p.N && (!p.symmetric || gn >= gm)) {
           float4* d4 = reinterpret_cast<float4*>(dst);
@@ -306,7 +350,8 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 1) {
     __syncwarp();
     fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(2 * BN)
                  : "memory");
   }
 }
@@ -360,7 +405,9 @@ static int launch(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMa
   }
   dim3 grid(cdiv(p.N, BN), cdiv(p.M, BM), (unsigned)batch);
   if (grid.y > 65535u || grid.z > 65535u) return G2Q_ERR_INVALID_ARG;
-  tc_gemm_kernel<NA, NB><<<grid, 192, K::SMEM, st>>>(a0, a1, b0, b1, p);
+  Params q = p;
+  q.promote_kb = K::PROMOTE_KB;
+  tc_gemm_kernel<NA, NB><<<grid, 192, K::SMEM, st>>>(a0, a1, b0, b1, q);
   G2Q_CHECK_LAUNCH();
   return G2Q_OK;
 }
