@@ -70,24 +70,30 @@ def test_tc_gram_bf16_weighted_matches_fp32_path():
     assert rel_fro(D1, D0) < 1e-5
 
 
-def _gptq_layer(rows, cols, bits, sym, gs, act, seed, precision, monkeypatch):
+def _gptq_layer(W, X, bits, sym, gs, act, precision, monkeypatch, H=None):
+    """Calibrate (unless ``H`` is given) and quantize one linear with the chosen path."""
     monkeypatch.setattr(_engine, "PRECISION", precision)
-    g = torch.Generator(device=DEV).manual_seed(seed)
-    W = torch.randn(rows, cols, device=DEV, generator=g) * 0.02
-    X = torch.randn(4, 1024, cols, device=DEV, generator=g)
-    X[..., :4] *= 20
+    rows, cols = W.shape
     lin = torch.nn.Linear(cols, rows, bias=False, device=DEV)
     lin.weight.data = W.clone()
     obj = gptq_utils.GPTQ([lin])
     q = WeightQuantizer()
     q.configure(bits, perchannel=True, sym=sym)
     obj.quantizer = make_group_quantizers(q, cols, gs)
-    for s in range(4):
-        obj.add_batch(0, X[s:s + 1].to(torch.bfloat16), None)
-    H = obj.H[0].clone()
+    if H is None:
+        for s in range(X.shape[0]):
+            obj.add_batch(0, X[s:s + 1], None)
+    else:
+        obj.H = H[None].clone()
+    Hout = obj.H[0].clone()
     obj.fasterquant(blocksize=128, percdamp=0.01, groupsize=gs, actorder=act, static_groups=act,
                     export_compressed_tensors=True)
-    return W, H, lin.weight.data.clone(), lin._export_qparams["weight_packed"].clone()
+    return Hout, lin.weight.data.clone()
+
+
+def _proxy(W, Q, H):
+    d = (W - Q).double()
+    return float(torch.einsum("rc,cd,rd->", d, H.double(), d))
 
 
 @pytest.mark.parametrize("rows,cols,bits,sym,gs,act", [
@@ -96,15 +102,24 @@ def _gptq_layer(rows, cols, bits, sym, gs, act, seed, precision, monkeypatch):
     (768, 2048, 3, False, 128, False),
 ])
 def test_tc_pipeline_matches_fp32_path(rows, cols, bits, sym, gs, act, monkeypatch):
-    W, H1, Q1, P1 = _gptq_layer(rows, cols, bits, sym, gs, act, 5, 1, monkeypatch)
-    _, H0, Q0, P0 = _gptq_layer(rows, cols, bits, sym, gs, act, 5, 0, monkeypatch)
+    """Same Hessian -> codes identical on >= 99.9% (trailing-update precision).
+    Each path's own Hessian -> Hessians within 1e-5 and ||(W-Q)X||^2 within 1e-3.
+    (Codes are not compared across different Hessians: with outlier channels
+    the GPTQ recursion turns a 1e-7 relative change of H into ~1% of flipped
+    codes at an unchanged loss.)"""
+    g = torch.Generator(device=DEV).manual_seed(5)
+    W = torch.randn(rows, cols, device=DEV, generator=g) * 0.02
+    X = torch.randn(4, 1024, cols, device=DEV, generator=g)
+    X[..., :4] *= 20
+    X = X.to(torch.bfloat16)
+    H0, Q0 = _gptq_layer(W, X, bits, sym, gs, act, 0, monkeypatch)
+    H1, Q1 = _gptq_layer(W, X, bits, sym, gs, act, 1, monkeypatch)
     assert rel_fro(H1, H0) < 1e-5
-    same = float((Q1 == Q0).float().mean())
-    assert same >= 0.999, same
-    d1, d0 = (W - Q1).double(), (W - Q0).double()
-    l1 = float(torch.einsum("rc,cd,rd->", d1, H0.double(), d1))
-    l0 = float(torch.einsum("rc,cd,rd->", d0, H0.double(), d0))
+    l0, l1 = _proxy(W, Q0, H0), _proxy(W, Q1, H0)
     assert abs(l1 - l0) / l0 < 1e-3
+    _, Q1s = _gptq_layer(W, X, bits, sym, gs, act, 1, monkeypatch, H=H0)
+    same = float((Q1s == Q0).float().mean())
+    assert same >= 0.999, same
 
 
 def test_tc_trailing_update_direct():
