@@ -118,7 +118,10 @@ def test_tc_pipeline_matches_fp32_path(rows, cols, bits, sym, gs, act, monkeypat
     l0, l1 = _proxy(W, Q0, H0), _proxy(W, Q1, H0)
     assert abs(l1 - l0) / l0 < 1e-3
     _, Q1s = _gptq_layer(W, X, bits, sym, gs, act, 1, monkeypatch, H=H0)
-    same = float((Q1s == Q0).float().mean())
+    # dequantized weights compared at the reference tests' float tolerance:
+    # dynamic-group scales are recomputed from the updated W, so equal codes
+    # can carry scales an ulp apart
+    same = float(torch.isclose(Q1s, Q0, rtol=2e-5, atol=2e-5).float().mean())
     assert same >= 0.999, same
 
 
