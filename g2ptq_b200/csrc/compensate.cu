@@ -106,20 +106,24 @@ __global__ void __launch_bounds__(128) block_kernel(BlockParams P) {
 
     for (int w0 = 0; w0 < nc; w0 += WIN) {
       float wv[WIN], gv[WIN], ev[WIN], xv[WIN];  // xv: GPTAQ pre-quant w / G2PTQ z
+      float sv[WIN], zv[WIN];  // the window's quantization parameters, loaded up front
 #pragma unroll
       for (int k = 0; k < WIN; ++k) {
         wv[k] = wsr[w0 + k];
         gv[k] = (METHOD == G2Q_METHOD_G2PTQ) ? gsr[w0 + k] : 0.f;
         ev[k] = 0.f;
-        xv[k] = 0.f;
+        const bool in = w0 + k < nc;
+        const int pc = in ? cmap[w0 + k] : 0;
+        sv[k] = in ? P.scale[prow + pc] : 1.f;
+        zv[k] = in ? P.zero[prow + pc] : 0.f;
+        xv[k] = (METHOD == G2Q_METHOD_G2PTQ && in) ? zrow[w0 + k] : 0.f;
       }
 #pragma unroll
       for (int c = 0; c < WIN; ++c) {
         const int cc = w0 + c;
         if (cc < nc) {
-          const int pc = cmap[cc];
-          const float s = P.scale[prow + pc];
-          const float zz = P.zero[prow + pc];
+          const float s = sv[c];
+          const float zz = zv[c];
           const float d = Us[cc * BLK + cc];
           const float wc = wv[c];
           float q = rintf(wc / s) + zz;
@@ -127,7 +131,6 @@ __global__ void __launch_bounds__(128) block_kernel(BlockParams P) {
           const float qv = s * (q - zz);
           float e;
           if (METHOD == G2Q_METHOD_G2PTQ) {
-            xv[c] = zrow[cc];
             e = (wc - qv - gv[c]) / d;
           } else {
             e = (wc - qv) / d;

@@ -14,7 +14,9 @@
 // four epilogue warps read the accumulator with tcgen05.ld and apply
 // alpha / beta, the bounds and the symmetric mirror.
 // fp32 operands are carried as a bf16 hi/lo pair and multiplied as
-// hi*hi + hi*lo + lo*hi (three MMAs per K step).
+// hi*hi + hi*lo + lo*hi (three MMAs per K step), or -- where fp32 accuracy is
+// required (the Cholesky updates) -- as a hi/mid/lo triple multiplied with the
+// six products of order <= 2 (hh, hm, mh, hl, lh, mm).
 //
 // Accumulator promotion: the tensor core adds each MMA's partial sum into the
 // TMEM accumulator with a bias of about one fp32 ulp (measured: the relative
@@ -51,6 +53,7 @@ struct Params {
   long long nb0;                 // first N coordinate of B
   float alpha, beta;
   int symmetric;
+  int lower;       // write only the lower triangle (m >= n); skip tiles above it
   int promote_kb;  // K blocks accumulated in TMEM before the epilogue drains them
   int* status;
 };
@@ -160,22 +163,25 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 template <int NA, int NB>
 struct Cfg {
   static constexpr int STAGE_BYTES = (NA + NB) * TILE_BYTES;
-  static constexpr int STAGES = (NA + NB) == 2 ? 6 : ((NA + NB) == 3 ? 4 : 3);
+  static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
-  static constexpr int PRODUCTS = 1 + (NB == 2 ? 1 : 0) + (NA == 2 ? 1 : 0);
-  // K blocks per TMEM accumulation group: 16 MMAs for one product, 24 for three
-  static constexpr int PROMOTE_KB = PRODUCTS == 1 ? 4 : 2;
+  static constexpr int ORDER = (NA > NB ? NA : NB) - 1;  // products a_i b_j with i + j <= ORDER
+  static constexpr int PRODUCTS = (NA == 3 && NB == 3) ? 6 : (NA + NB - 1);
+  // K blocks per TMEM accumulation group: 16 MMAs for one product, 24 otherwise
+  static constexpr int PROMOTE_KB = PRODUCTS == 1 ? 4 : (PRODUCTS <= 3 ? 2 : 1);
 };
 
 template <int NA, int NB>
 __global__ void __launch_bounds__(192, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap ma0, const __grid_constant__ CUtensorMap ma1,
-                   const __grid_constant__ CUtensorMap mb0, const __grid_constant__ CUtensorMap mb1,
+                   const __grid_constant__ CUtensorMap ma2, const __grid_constant__ CUtensorMap mb0,
+                   const __grid_constant__ CUtensorMap mb1, const __grid_constant__ CUtensorMap mb2,
                    Params p) {
   using K = Cfg<NA, NB>;
   const int mt = blockIdx.y, nt = blockIdx.x;
   const long long bz = blockIdx.z;
   if (p.symmetric && nt < mt) return;  // tile holds no element of the upper triangle
+  if (p.lower && nt > mt) return;      // tile holds no element of the lower triangle
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -228,18 +234,18 @@ __global__ void __launch_bounds__(192, 1)
         const int ya = (int)(p.ka_batch * bz + p.ka0 + (long long)kb * BK);
         const int yb = (int)(p.kb_batch * bz + p.kb0 + (long long)kb * BK);
         const int xb = (int)(p.nb0 + n0);
-        tma_load_2d(st, &ma0, m0, ya, fb);
-        tma_load_2d(st + CHUNK_BYTES, &ma0, m0 + 64, ya, fb);
-        if (NA == 2) {
-          tma_load_2d(st + TILE_BYTES, &ma1, m0, ya, fb);
-          tma_load_2d(st + TILE_BYTES + CHUNK_BYTES, &ma1, m0 + 64, ya, fb);
+#pragma unroll
+        for (int i = 0; i < NA; ++i) {
+          const CUtensorMap* m = i == 0 ? &ma0 : (i == 1 ? &ma1 : &ma2);
+          tma_load_2d(st + i * TILE_BYTES, m, m0, ya, fb);
+          tma_load_2d(st + i * TILE_BYTES + CHUNK_BYTES, m, m0 + 64, ya, fb);
         }
         const uint32_t sb = st + NA * TILE_BYTES;
-        tma_load_2d(sb, &mb0, xb, yb, fb);
-        tma_load_2d(sb + CHUNK_BYTES, &mb0, xb + 64, yb, fb);
-        if (NB == 2) {
-          tma_load_2d(sb + TILE_BYTES, &mb1, xb, yb, fb);
-          tma_load_2d(sb + TILE_BYTES + CHUNK_BYTES, &mb1, xb + 64, yb, fb);
+#pragma unroll
+        for (int j = 0; j < NB; ++j) {
+          const CUtensorMap* m = j == 0 ? &mb0 : (j == 1 ? &mb1 : &mb2);
+          tma_load_2d(sb + j * TILE_BYTES, m, xb, yb, fb);
+          tma_load_2d(sb + j * TILE_BYTES + CHUNK_BYTES, m, xb + 64, yb, fb);
         }
       }
     }
@@ -270,13 +276,18 @@ __global__ void __launch_bounds__(192, 1)
           for (int kk = 0; kk < BK / 16; ++kk) {
             const uint32_t off = kk * 2048;  // 16 K rows = two 8-row swizzle groups
             const uint32_t acc0 = (kb > kstart || kk > 0) ? 1u : 0u;
-            umma_bf16(acc_t, desc_mn_sw128(sa + off), desc_mn_sw128(sb + off), idesc, acc0);
-            if (NB == 2)
-              umma_bf16(acc_t, desc_mn_sw128(sa + off), desc_mn_sw128(sb + TILE_BYTES + off),
-                        idesc, 1u);
-            if (NA == 2)
-              umma_bf16(acc_t, desc_mn_sw128(sa + TILE_BYTES + off), desc_mn_sw128(sb + off),
-                        idesc, 1u);
+            // products a_i * b_j with i + j <= ORDER, the leading one first
+#pragma unroll
+            for (int o = 0; o <= K::ORDER; ++o) {
+#pragma unroll
+              for (int i = 0; i < NA; ++i) {
+                const int j = o - i;
+                if (j < 0 || j >= NB) continue;
+                umma_bf16(acc_t, desc_mn_sw128(sa + i * TILE_BYTES + off),
+                          desc_mn_sw128(sb + j * TILE_BYTES + off), idesc,
+                          (o == 0) ? acc0 : 1u);
+              }
+            }
           }
           umma_commit(empty0 + 8 * s);
         }
@@ -319,7 +330,7 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
         for (int u = 0; u < 4; ++u) v[u] = p.beta * acc[4 * j4 + u];
         float* dst = Db + gm * p.ldd + gn;
-        if (vec_ok && gn + 3 < p.N && (!p.symmetric || gn >= gm)) {
+        if (vec_ok && gn + 3 < p.N && (!p.symmetric || gn >= gm) && (!p.lower || gn + 3 <= gm)) {
           float4* d4 = reinterpret_cast<float4*>(dst);
           if (p.alpha != 0.f) {
             const float4 o = *d4;
@@ -332,7 +343,8 @@ __global__ void __launch_bounds__(192, 1)
         } else {
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
-            if (gn + u >= p.N || (p.symmetric && gn + u < gm)) continue;
+            if (gn + u >= p.N || (p.symmetric && gn + u < gm) || (p.lower && gn + u > gm))
+              continue;
             if (p.alpha != 0.f) v[u] = fmaf(p.alpha, dst[u], v[u]);
             dst[u] = v[u];
           }
@@ -390,9 +402,12 @@ static bool make_map(CUtensorMap* m, const void* base, long long inner, long lon
          CUDA_SUCCESS;
 }
 
+struct Maps {
+  CUtensorMap a[3], b[3];
+};
+
 template <int NA, int NB>
-static int launch(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMap& b0,
-                  const CUtensorMap& b1, const Params& p, long long batch, cudaStream_t st) {
+static int launch(const Maps& m, const Params& p, long long batch, cudaStream_t st) {
   using K = Cfg<NA, NB>;
   static int attr_done[64] = {0};
   int dev = 0;
@@ -407,18 +422,22 @@ static int launch(const CUtensorMap& a0, const CUtensorMap& a1, const CUtensorMa
   if (grid.y > 65535u || grid.z > 65535u) return G2Q_ERR_INVALID_ARG;
   Params q = p;
   q.promote_kb = K::PROMOTE_KB;
-  tc_gemm_kernel<NA, NB><<<grid, 192, K::SMEM, st>>>(a0, a1, b0, b1, q);
+  tc_gemm_kernel<NA, NB><<<grid, 192, K::SMEM, st>>>(m.a[0], m.a[1], m.a[2], m.b[0], m.b[1],
+                                                      m.b[2], q);
   G2Q_CHECK_LAUNCH();
   return G2Q_OK;
 }
 
-static int dispatch(int na, int nb, const CUtensorMap& a0, const CUtensorMap& a1,
-                    const CUtensorMap& b0, const CUtensorMap& b1, const Params& p,
-                    long long batch, cudaStream_t st) {
-  if (na == 1 && nb == 1) return launch<1, 1>(a0, a1, b0, b1, p, batch, st);
-  if (na == 1 && nb == 2) return launch<1, 2>(a0, a1, b0, b1, p, batch, st);
-  if (na == 2 && nb == 1) return launch<2, 1>(a0, a1, b0, b1, p, batch, st);
-  return launch<2, 2>(a0, a1, b0, b1, p, batch, st);
+static int dispatch(int na, int nb, Maps& m, const Params& p, long long batch,
+                    cudaStream_t st) {
+  for (int i = na; i < 3; ++i) m.a[i] = m.a[0];
+  for (int j = nb; j < 3; ++j) m.b[j] = m.b[0];
+  if (na == 1 && nb == 1) return launch<1, 1>(m, p, batch, st);
+  if (na == 1 && nb == 2) return launch<1, 2>(m, p, batch, st);
+  if (na == 2 && nb == 1) return launch<2, 1>(m, p, batch, st);
+  if (na == 2 && nb == 2) return launch<2, 2>(m, p, batch, st);
+  if (na == 3 && nb == 3) return launch<3, 3>(m, p, batch, st);
+  return G2Q_ERR_UNSUPPORTED;
 }
 
 template <typename S>
@@ -528,14 +547,12 @@ int tc_gram(float* D, long long ldd, long long M, long long N, const void* A, in
     ldb_t = w;
     nb = 2;
   }
-  CUtensorMap ma[2], mb[2];
-  bool ok = tc::make_map(&ma[0], a_terms[0], M, T, lda_t) &&
-            tc::make_map(&mb[0], b_terms[0], N, T, ldb_t);
-  ok = ok && (na == 1 || tc::make_map(&ma[1], a_terms[1], M, T, lda_t));
-  ok = ok && (nb == 1 || tc::make_map(&mb[1], b_terms[1], N, T, ldb_t));
+  tc::Maps mp;
+  bool ok = tc::make_map(&mp.a[0], a_terms[0], M, T, lda_t) &&
+            tc::make_map(&mp.b[0], b_terms[0], N, T, ldb_t);
+  ok = ok && (na == 1 || tc::make_map(&mp.a[1], a_terms[1], M, T, lda_t));
+  ok = ok && (nb == 1 || tc::make_map(&mp.b[1], b_terms[1], N, T, ldb_t));
   if (!ok) return simt_gemm(sa, true, false, a_dtype, b_dtype, 1, st);
-  if (na == 1) ma[1] = ma[0];
-  if (nb == 1) mb[1] = mb[0];
   tc::Params p{};
   p.D = D; p.ldd = ldd; p.d_bs = 0;
   p.M = M; p.N = N;
@@ -543,7 +560,7 @@ int tc_gram(float* D, long long ldd, long long M, long long N, const void* A, in
   p.alpha = alpha; p.beta = beta;
   p.symmetric = symmetric ? 1 : 0;
   p.status = nullptr;
-  return tc::dispatch(na, nb, ma[0], ma[1], mb[0], mb[1], p, 1, st);
+  return tc::dispatch(na, nb, mp, p, 1, st);
 }
 
 // W[b][:, i2 + n] -= sum_k Err[b][k][m] * U[b][i1 + k][i2 + n] on tensor cores.
@@ -558,11 +575,11 @@ int tc_trailing_update(float* W, long long C, long long rows, long long batch, l
                        cudaStream_t st) {
   if ((nc % tc::BK) || (i2 % 8) || (rows % 8) || (C % 8) || !tc::encode_fn())
     return G2Q_ERR_UNSUPPORTED;
-  CUtensorMap ma[2], mb[2];
-  bool ok = tc::make_map(&ma[0], err_hi, rows, batch * err_stride, rows) &&
-            tc::make_map(&ma[1], err_lo, rows, batch * err_stride, rows) &&
-            tc::make_map(&mb[0], u_hi, C, batch * C, C) &&
-            tc::make_map(&mb[1], u_lo, C, batch * C, C);
+  tc::Maps mp;
+  bool ok = tc::make_map(&mp.a[0], err_hi, rows, batch * err_stride, rows) &&
+            tc::make_map(&mp.a[1], err_lo, rows, batch * err_stride, rows) &&
+            tc::make_map(&mp.b[0], u_hi, C, batch * C, C) &&
+            tc::make_map(&mp.b[1], u_lo, C, batch * C, C);
   if (!ok) return G2Q_ERR_UNSUPPORTED;
   tc::Params p{};
   p.D = W + i2; p.ldd = C; p.d_bs = rows * C;
@@ -574,7 +591,68 @@ int tc_trailing_update(float* W, long long C, long long rows, long long batch, l
   p.alpha = 1.f; p.beta = -1.f;
   p.symmetric = 0;
   p.status = status;
-  return tc::dispatch(2, 2, ma[0], ma[1], mb[0], mb[1], p, batch, st);
+  return tc::dispatch(2, 2, mp, p, batch, st);
+}
+
+// Three-way bf16 split (hi/mid/lo) of a rows x cols fp32 block (row stride
+// lds), written transposed (dst[c][r]) or not (dst[r][c]) with row stride ldd.
+__global__ void split3_kernel(const float* __restrict__ src, long long lds, long long rows,
+                              long long cols, __nv_bfloat16* h, __nv_bfloat16* m,
+                              __nv_bfloat16* l, long long ldd, int transpose) {
+  __shared__ float tile[32][33];
+  const long long r0 = (long long)blockIdx.y * 32, c0 = (long long)blockIdx.x * 32;
+  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
+    const long long r = r0 + k, c = c0 + threadIdx.x;
+    tile[k][threadIdx.x] = (r < rows && c < cols) ? src[r * lds + c] : 0.f;
+  }
+  __syncthreads();
+  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
+    // transposed: this thread writes dst[c0 + k][r0 + tx] from tile[tx][k]
+    const long long orow = transpose ? c0 + k : r0 + k;
+    const long long ocol = transpose ? r0 + threadIdx.x : c0 + threadIdx.x;
+    const bool ok = transpose ? (orow < cols && ocol < rows) : (orow < rows && ocol < cols);
+    if (!ok) continue;
+    const float v = transpose ? tile[threadIdx.x][k] : tile[k][threadIdx.x];
+    const __nv_bfloat16 hv = __float2bfloat16_rn(v);
+    const float r1 = v - __bfloat162float(hv);
+    const __nv_bfloat16 mv = __float2bfloat16_rn(r1);
+    const float r2 = r1 - __bfloat162float(mv);
+    h[orow * ldd + ocol] = hv;
+    m[orow * ldd + ocol] = mv;
+    l[orow * ldd + ocol] = __float2bfloat16_rn(r2);
+  }
+}
+
+int split3(const float* src, long long lds, long long rows, long long cols, __nv_bfloat16* h,
+           __nv_bfloat16* m, __nv_bfloat16* l, long long ldd, int transpose, cudaStream_t st) {
+  if (rows <= 0 || cols <= 0) return G2Q_OK;
+  dim3 grid(cdiv(cols, 32), cdiv(rows, 32));
+  if (grid.y > 65535u) return G2Q_ERR_INVALID_ARG;
+  split3_kernel<<<grid, dim3(32, 8), 0, st>>>(src, lds, rows, cols, h, m, l, ldd, transpose);
+  G2Q_CHECK_LAUNCH();
+  return G2Q_OK;
+}
+
+// fp32-accurate tensor-core update  D <- alpha D + beta * A^T B  for MN-major
+// three-term operands A[k][m] (terms a3, row stride lda) and B[k][n] (b3, ldb)
+// over K rows; lower != 0 writes only m >= n.  Returns G2Q_ERR_UNSUPPORTED when
+// TMA cannot describe the operands.
+int tc_update3(float* D, long long ldd, long long M, long long N, long long K,
+               __nv_bfloat16* const* a3, long long lda, __nv_bfloat16* const* b3, long long ldb,
+               int lower, float alpha, float beta, cudaStream_t st) {
+  if (M <= 0 || N <= 0 || K <= 0 || !tc::encode_fn()) return G2Q_ERR_UNSUPPORTED;
+  tc::Maps mp;
+  bool ok = true;
+  for (int i = 0; i < 3 && ok; ++i)
+    ok = tc::make_map(&mp.a[i], a3[i], M, K, lda) && tc::make_map(&mp.b[i], b3[i], N, K, ldb);
+  if (!ok) return G2Q_ERR_UNSUPPORTED;
+  tc::Params p{};
+  p.D = D; p.ldd = ldd; p.d_bs = 0;
+  p.M = M; p.N = N;
+  p.num_kb = (int)((K + tc::BK - 1) / tc::BK);
+  p.alpha = alpha; p.beta = beta;
+  p.lower = lower;
+  return tc::dispatch(3, 3, mp, p, 1, st);
 }
 
 }  // namespace g2q

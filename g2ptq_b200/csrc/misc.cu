@@ -252,7 +252,7 @@ void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 using namespace g2q;
 
-extern "C" int g2q_abi_version(void) { return 1; }
+extern "C" int g2q_abi_version(void) { return 2; }
 
 extern "C" int64_t g2q_launch_count(void) { return g2q::g_launches.load(); }
 
@@ -276,6 +276,15 @@ extern "C" int g2q_stage_tokens(void* dst, int dst_dtype, int64_t dst_ld, int64_
     return G2Q_ERR_INVALID_ARG;
   if (t == 0) return G2Q_OK;
   cudaStream_t st = (cudaStream_t)stream;
+  if (dst_dtype == src_dtype && !sub) {
+    // same element type: a strided device-to-device copy at copy bandwidth
+    const size_t es = dst_dtype == G2Q_DTYPE_BF16 || dst_dtype == G2Q_DTYPE_F16 ? 2 : 4;
+    if (cudaMemcpy2DAsync((char*)dst + (size_t)row0 * dst_ld * es, (size_t)dst_ld * es, src,
+                          (size_t)src_ld * es, (size_t)C * es, (size_t)t,
+                          cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+      return G2Q_ERR_CUDA;
+    return G2Q_OK;
+  }
   const int g = grid_for(t * C);
   if (dst_dtype == G2Q_DTYPE_BF16) {
     if (src_dtype != G2Q_DTYPE_BF16 || sub) return G2Q_ERR_INVALID_ARG;

@@ -103,7 +103,7 @@ def factor_with_retry(H, percdamp, info=None):
     if not (1 > percdamp > 0):
         raise ValueError(f"Quantization: `damp_percent` must between 0 and 1. current is "
                          f"{percdamp}")
-    U, info = ops.chol_upper_inverse(H, damps, info)
+    U, info = ops.chol_upper_inverse(H, damps, info, precision=PRECISION)
     return U, info, damps
 
 
@@ -120,7 +120,7 @@ def retry_failed(H, U, info_list, damps):
             if not (1 > d > 0):
                 raise ValueError(
                     f"Quantization: `damp_percent` must between 0 and 1. current is {d}")
-            Ub, ib = ops.chol_upper_inverse(H[b:b + 1].contiguous(), [d])
+            Ub, ib = ops.chol_upper_inverse(H[b:b + 1].contiguous(), [d], precision=PRECISION)
             if int(ib.item()) == 0:
                 U[b].copy_(Ub[0])
                 break

@@ -117,7 +117,7 @@ def gemm(C, A, B, transA=False, transB=False, alpha=0.0, beta=1.0, mask=_lib.MAS
     return C
 
 
-def chol_upper_inverse(H, damp_percent, info=None):
+def chol_upper_inverse(H, damp_percent, info=None, precision=0):
     """``U`` with ``U^T U = (H + d I)^-1`` per batch entry; returns ``(U, info)``.
 
     ``damp_percent`` is a float or a sequence (one per batch entry);
@@ -136,7 +136,7 @@ def chol_upper_inverse(H, damp_percent, info=None):
     ws_bytes = query("g2q_chol_workspace_bytes", C)
     ws = workspace(ws_bytes, H.device)
     call("g2q_chol_upper_inverse", U.data_ptr(), Hb.data_ptr(), C, C, B, damps, info.data_ptr(),
-         ws.data_ptr(), ws_bytes, _stream(H))
+         int(precision), ws.data_ptr(), ws_bytes, _stream(H))
     return (U if H.dim() == 3 else U[0]), info
 
 

@@ -117,13 +117,15 @@ int g2q_gemm(float* C, int64_t ldc, int64_t strideC,
  * info[b] (device int) receives 0, the 1-based index of the first
  * non-positive pivot, or -1 when the factor holds a NaN.  Route: UL
  * factorization H + dI = V V^T (V upper), U = V^-1 -- potrf + trtri, half the
- * work of potrf + potri + potrf.  Needs g2q_chol_workspace_bytes(C) bytes.
+ * work of potrf + potri + potrf.  precision: 0 = fp32 CUDA cores, 1 = trailing
+ * updates on tensor cores with a three-term bf16 split (fp32-level accuracy).
+ * Needs g2q_chol_workspace_bytes(C) bytes.
  * Replaces the damped Cholesky chain of gptq_utils/gptq_utils.py:291-311
  * (and its copies g2ptq_utils.py:430-450, gptaq_utils.py:323-343,
  * gptq_guided_utils.py:145-165); the damp auto-increment retry stays with the
  * caller, which reads `info`. */
 int g2q_chol_upper_inverse(float* U, const float* H, int64_t C, int64_t ldh, int64_t batch,
-                           const float* damp_percent_host, int* info,
+                           const float* damp_percent_host, int* info, int precision,
                            void* workspace, size_t workspace_bytes, void* stream);
 size_t g2q_chol_workspace_bytes(int64_t C);
 

@@ -152,3 +152,22 @@ def test_tc_trailing_update_direct():
     same = float((outs[0][1] == outs[1][1]).float().mean())
     assert same >= 0.999, same
     torch.testing.assert_close(outs[1][0], outs[0][0], rtol=0, atol=float(scale.max()) * 1.01)
+
+
+@pytest.mark.parametrize("C", [1152, 4096])
+def test_tc_cholesky_matches_fp32(C):
+    """Cholesky trailing updates on tensor cores (three-term split) vs fp32."""
+    g = torch.Generator(device=DEV).manual_seed(C)
+    X = torch.randn(2 * C, C, device=DEV, generator=g)
+    X[:, :4] *= 20
+    H = ((X.T @ X) / C)[None].contiguous()
+    U0, i0 = ops.chol_upper_inverse(H, 0.01, precision=0)
+    U1, i1 = ops.chol_upper_inverse(H, 0.01, precision=1)
+    assert int(i0.item()) == 0 and int(i1.item()) == 0
+    assert rel_fro(U1, U0) < 1e-5
+    Hd = H[0].double() + 0.01 * torch.diagonal(H[0]).double().mean() * torch.eye(
+        C, device=DEV, dtype=torch.float64)
+    resid = (U1[0].double().T @ U1[0].double()) @ Hd - torch.eye(C, device=DEV,
+                                                                dtype=torch.float64)
+    assert float(resid.abs().max()) < 1e-3
+    assert float(torch.tril(U1[0], -1).abs().max()) == 0.0
