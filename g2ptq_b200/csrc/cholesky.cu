@@ -54,60 +54,114 @@ __global__ void reverse_damp_kernel(const float* H, long long C, long long ldh,
 }
 
 // Factor the nb x nb diagonal block at (k0, k0) of A in place and write its
-// lower-triangular inverse to Linv (NB x NB, zero padded).  One pass over the
-// pivots computes both: after pivot j scales column j of L, the rows below
-// eliminate it from the trailing matrix (a[i][k] -= l_ij l_kj) and from the
-// forward substitution of L X = I (x[i][:j+1] -= l_ij x[j][:j+1]).  A 16 x 16
-// thread grid covers each trailing triangle.
+// lower-triangular inverse to Linv (NB x NB, zero padded).
+//
+// The block and its inverse live in registers: thread (ty, tx) of a 16 x 16
+// grid owns rows 8ty..8ty+7 x columns 8tx..8tx+7 of both L and X.  Pivot j
+// publishes column j of the working matrix and row j of X through shared
+// memory; every thread then applies the rank-1 update to its 8 x 8 tile of the
+// trailing matrix (a -= l l^T) and of the forward substitution of L X = I
+// (x_i -= l_ij x_j).  The pivot loop is unrolled by 8 so that every register
+// index is a compile-time constant.  Columns are scaled by 1/l_jj, as LAPACK's
+// unblocked spotf2 does.
 __global__ void __launch_bounds__(256) panel_kernel(float* A, long long C, long long k0, int nb,
                                                     float* Linv, int* info) {
-  extern __shared__ float panel_smem[];
-  float (*a)[NB + 1] = reinterpret_cast<float (*)[NB + 1]>(panel_smem);
-  float (*x)[NB + 1] = reinterpret_cast<float (*)[NB + 1]>(panel_smem + NB * (NB + 1));
+  __shared__ __align__(16) float col[NB];
+  __shared__ __align__(16) float row[NB];
   __shared__ int failed;
   const int t = threadIdx.x;
   const int ty = t >> 4, tx = t & 15;
-  for (int idx = t; idx < NB * NB; idx += blockDim.x) {
-    const int i = idx / NB, j = idx % NB;
-    a[i][j] = (i < nb && j < nb && j <= i) ? A[(k0 + i) * C + k0 + j] : 0.f;
-    x[i][j] = (i == j && i < nb) ? 1.f : 0.f;
-  }
+  const int r0 = ty * 8, c0 = tx * 8;
+  float a[8][8], x[8][8];
+#pragma unroll
+  for (int u = 0; u < 8; ++u)
+#pragma unroll
+    for (int v = 0; v < 8; ++v) {
+      const int r = r0 + u, c = c0 + v;
+      a[u][v] = (r < nb && c <= r) ? A[(k0 + r) * C + k0 + c] : 0.f;
+      x[u][v] = (r == c && r < nb) ? 1.f : 0.f;
+    }
   if (t == 0) failed = 0;
   __syncthreads();
 
-  for (int j = 0; j < nb; ++j) {
-    const float d = a[j][j];
-    if (!(d > 0.f)) {  // non-positive or NaN pivot (uniform across the block)
-      if (t == 0) {
-        failed = 1;
-        if (info) atomicCAS(info, 0, (int)(k0 + j + 1));
+  for (int jb = 0; jb < NB / 8; ++jb) {
+#pragma unroll
+    for (int jj = 0; jj < 8; ++jj) {
+      const int j = jb * 8 + jj;
+      if (j >= nb) break;
+      if (tx == jb) {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) col[r0 + u] = a[u][jj];
       }
-      break;
+      if (ty == jb) {
+#pragma unroll
+        for (int v = 0; v < 8; ++v) row[c0 + v] = x[jj][v];
+      }
+      __syncthreads();
+      const float d = col[j];
+      if (!(d > 0.f)) {  // non-positive or NaN pivot (uniform across the block)
+        if (t == 0) {
+          failed = 1;
+          if (info) atomicCAS(info, 0, (int)(k0 + j + 1));
+        }
+        goto done;
+      }
+      const float l = sqrtf(d);
+      const float rl = 1.f / l;
+      float lr[8], lc[8], xr[8];
+      {
+        const float4 p0 = *reinterpret_cast<const float4*>(&col[r0]);
+        const float4 p1 = *reinterpret_cast<const float4*>(&col[r0 + 4]);
+        const float4 q0 = *reinterpret_cast<const float4*>(&col[c0]);
+        const float4 q1 = *reinterpret_cast<const float4*>(&col[c0 + 4]);
+        const float4 s0 = *reinterpret_cast<const float4*>(&row[c0]);
+        const float4 s1 = *reinterpret_cast<const float4*>(&row[c0 + 4]);
+        const float pr[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+        const float pc[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+        const float ps[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          lr[u] = (r0 + u > j) ? pr[u] * rl : 0.f;
+          lc[u] = (c0 + u > j) ? pc[u] * rl : 0.f;
+          xr[u] = ps[u] * rl;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+#pragma unroll
+        for (int v = 0; v < 8; ++v) {
+          a[u][v] = fmaf(-lr[u], lc[v], a[u][v]);
+          x[u][v] = fmaf(-lr[u], xr[v], x[u][v]);
+        }
+      if (tx == jb) {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          if (r0 + u > j) a[u][jj] = lr[u];
+          else if (r0 + u == j) a[u][jj] = l;
+        }
+      }
+      if (ty == jb) {
+#pragma unroll
+        for (int v = 0; v < 8; ++v) x[jj][v] = xr[v];
+      }
+      __syncthreads();
     }
-    const float l = sqrtf(d);
-    __syncthreads();  // every thread has read a[j][j]
-    for (int i = j + 1 + t; i < nb; i += blockDim.x) a[i][j] = a[i][j] / l;
-    for (int c = t; c <= j; c += blockDim.x) x[j][c] = x[j][c] / l;
-    if (t == 0) a[j][j] = l;
-    __syncthreads();
-    for (int i = j + 1 + ty; i < nb; i += 16) {
-      const float lij = a[i][j];
-      for (int k = j + 1 + tx; k <= i; k += 16) a[i][k] = fmaf(-lij, a[k][j], a[i][k]);
-      for (int c = tx; c <= j; c += 16) x[i][c] = fmaf(-lij, x[j][c], x[i][c]);
-    }
-    __syncthreads();
   }
+done:
   __syncthreads();
   if (failed) {
     // mark the inverse as NaN so downstream products are visibly invalid
     for (int idx = t; idx < NB * NB; idx += blockDim.x) Linv[idx] = __int_as_float(0x7fc00000);
     return;
   }
-  for (int idx = t; idx < NB * NB; idx += blockDim.x) {
-    const int i = idx / NB, j = idx % NB;
-    Linv[idx] = (i < nb && j < nb) ? x[i][j] : 0.f;
-    if (i < nb && j <= i) A[(k0 + i) * C + k0 + j] = a[i][j];
-  }
+#pragma unroll
+  for (int u = 0; u < 8; ++u)
+#pragma unroll
+    for (int v = 0; v < 8; ++v) {
+      const int r = r0 + u, c = c0 + v;
+      Linv[r * NB + c] = (r < nb && c < nb) ? x[u][v] : 0.f;
+      if (r < nb && c <= r) A[(k0 + r) * C + k0 + c] = a[u][v];
+    }
 }
 
 // U[i][j] = X[C-1-i][C-1-j] for i <= j, 0 below; NaN -> info = -1.
@@ -133,19 +187,6 @@ static int gemm(float* Cp, long long ldc, const float* Ap, long long lda, bool t
   return simt_gemm_f32(Cp, ldc, Ap, lda, ta, Bp, ldb, tb, M, N, K, alpha, beta, mask, st);
 }
 
-static constexpr size_t kPanelSmem = 2 * NB * (NB + 1) * sizeof(float);
-
-static int ensure_panel_attr() {
-  static int done[64] = {0};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return G2Q_ERR_CUDA;
-  if (dev < 64 && done[dev]) return G2Q_OK;
-  if (cudaFuncSetAttribute(panel_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)kPanelSmem) != cudaSuccess)
-    return G2Q_ERR_CUDA;
-  if (dev < 64) done[dev] = 1;
-  return G2Q_OK;
-}
 
 int split3(const float* src, long long lds, long long rows, long long cols, __nv_bfloat16* h,
            __nv_bfloat16* m, __nv_bfloat16* l, long long ldd, int transpose, cudaStream_t st);
@@ -179,7 +220,6 @@ static int chol_one(float* U, const float* H, long long C, long long ldh, float 
   float* mdiag = Linv + NB * NB;
   __nv_bfloat16* lt = reinterpret_cast<__nv_bfloat16*>(mdiag + 64);
   __nv_bfloat16* xk = lt + 3 * (long long)NB * C;
-  G2Q_TRY(ensure_panel_attr());
   if (info && cudaMemsetAsync(info, 0, sizeof(int), st) != cudaSuccess) return G2Q_ERR_CUDA;
   mean_diag_kernel<<<1, 1024, 0, st>>>(H, C, ldh, mdiag);
   G2Q_CHECK_LAUNCH();
@@ -190,7 +230,7 @@ static int chol_one(float* U, const float* H, long long C, long long ldh, float 
   for (long long k0 = 0; k0 < C; k0 += NB) {
     const int nb = (int)((C - k0) < NB ? (C - k0) : NB);
     const long long rest = C - k0 - nb;
-    panel_kernel<<<1, 256, kPanelSmem, st>>>(A, C, k0, nb, Linv, info);
+    panel_kernel<<<1, 256, 0, st>>>(A, C, k0, nb, Linv, info);
     G2Q_CHECK_LAUNCH();
     // X_k: = Linv_kk Y_k:  (columns 0 .. k0+nb), in place in Y
     G2Q_TRY(gemm(Y + k0 * C, C, Linv, NB, false, Y + k0 * C, C, false, nb, k0 + nb, nb,
