@@ -41,8 +41,10 @@ struct BlockParams {
   int dfact;       // G2PTQ distance factor (the traversal's blocksize)
 };
 
-constexpr int WIN = 32;       // columns held in registers at a time
-constexpr int LDS_ROW = BLK + 1;  // padded shared-memory row of a W / gh tile
+constexpr int WIN = 32;           // columns held in registers at a time
+// Padded shared-memory row of a W / gh tile: rows stay 16-byte aligned, and the
+// 16-byte per-thread row accesses of a quarter warp cover all 32 banks.
+constexpr int LDS_ROW = BLK + 4;
 
 // Shared-memory layout (floats): U block, W tile, [gh tile | P block], codes.
 __host__ __device__ constexpr int smem_floats(int method) {
@@ -69,26 +71,53 @@ __global__ void __launch_bounds__(128) block_kernel(BlockParams P) {
   const long long nrows_here = (P.rows - row0) < BLK ? (P.rows - row0) : BLK;
 
   const float* hb = P.hinv + (long long)b * P.h_bs;
-  for (int idx = t; idx < BLK * BLK; idx += BLK) {
-    const int i = idx >> 7, j = idx & (BLK - 1);
-    Us[idx] = (i < nc && j < nc) ? hb[i * P.ldh + j] : 0.f;
-  }
-  if (METHOD == G2Q_METHOD_GPTAQ) {
-    const float* pb = P.p + (long long)b * P.h_bs;
+  const float* pb = (METHOD == G2Q_METHOD_GPTAQ) ? P.p + (long long)b * P.h_bs : nullptr;
+  // 16-byte loads with many in flight when the block is full width and aligned
+  const bool vec = (nc == BLK) && ((P.ldh & 3) == 0) && ((P.ldw & 3) == 0) &&
+                   (((uintptr_t)hb & 15) == 0) && (((uintptr_t)P.W & 15) == 0) &&
+                   (METHOD != G2Q_METHOD_G2PTQ ||
+                    (((P.ldz & 3) == 0) && (((uintptr_t)P.gh & 15) == 0))) &&
+                   (METHOD != G2Q_METHOD_GPTAQ || (((uintptr_t)pb & 15) == 0));
+  if (vec) {
+#pragma unroll 8
+    for (int q = t; q < BLK * BLK / 4; q += BLK) {
+      const int i = q >> 5, j4 = (q & 31) * 4;
+      *reinterpret_cast<float4*>(&Us[i * BLK + j4]) =
+          *reinterpret_cast<const float4*>(hb + i * P.ldh + j4);
+      if (METHOD == G2Q_METHOD_GPTAQ)
+        *reinterpret_cast<float4*>(&Xs[i * BLK + j4]) =
+            *reinterpret_cast<const float4*>(pb + i * P.ldh + j4);
+    }
+#pragma unroll 8
+    for (int q = t; q < BLK * BLK / 4; q += BLK) {
+      const int rr = q >> 5, c4 = (q & 31) * 4;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f), gv4 = v;
+      if (rr < nrows_here) {
+        v = *reinterpret_cast<const float4*>(P.W + (long long)b * P.w_bs +
+                                             (row0 + rr) * P.ldw + c4);
+        if (METHOD == G2Q_METHOD_G2PTQ)
+          gv4 = *reinterpret_cast<const float4*>(P.gh + (long long)b * P.z_bs +
+                                                 (row0 + rr) * P.ldz + c4);
+      }
+      *reinterpret_cast<float4*>(&Ws[rr * LDS_ROW + c4]) = v;
+      if (METHOD == G2Q_METHOD_G2PTQ) *reinterpret_cast<float4*>(&Xs[rr * LDS_ROW + c4]) = gv4;
+    }
+  } else {
     for (int idx = t; idx < BLK * BLK; idx += BLK) {
       const int i = idx >> 7, j = idx & (BLK - 1);
-      Xs[idx] = (i < nc && j < nc) ? pb[i * P.ldh + j] : 0.f;
+      Us[idx] = (i < nc && j < nc) ? hb[i * P.ldh + j] : 0.f;
+      if (METHOD == G2Q_METHOD_GPTAQ) Xs[idx] = (i < nc && j < nc) ? pb[i * P.ldh + j] : 0.f;
     }
-  }
-  // W (and gh) tiles: one warp per row, lanes along the row (coalesced)
-  for (int rr = warp; rr < BLK; rr += 4) {
-    const bool ok = rr < nrows_here;
-    const float* src = P.W + (long long)b * P.w_bs + (row0 + rr) * P.ldw;
-    const float* gsrc = (METHOD == G2Q_METHOD_G2PTQ)
-                            ? P.gh + (long long)b * P.z_bs + (row0 + rr) * P.ldz : nullptr;
-    for (int c = lane; c < BLK; c += 32) {
-      Ws[rr * LDS_ROW + c] = (ok && c < nc) ? src[c] : 0.f;
-      if (METHOD == G2Q_METHOD_G2PTQ) Xs[rr * LDS_ROW + c] = (ok && c < nc) ? gsrc[c] : 0.f;
+    // W (and gh) tiles: one warp per row, lanes along the row (coalesced)
+    for (int rr = warp; rr < BLK; rr += 4) {
+      const bool ok = rr < nrows_here;
+      const float* src = P.W + (long long)b * P.w_bs + (row0 + rr) * P.ldw;
+      const float* gsrc = (METHOD == G2Q_METHOD_G2PTQ)
+                              ? P.gh + (long long)b * P.z_bs + (row0 + rr) * P.ldz : nullptr;
+      for (int c = lane; c < BLK; c += 32) {
+        Ws[rr * LDS_ROW + c] = (ok && c < nc) ? src[c] : 0.f;
+        if (METHOD == G2Q_METHOD_G2PTQ) Xs[rr * LDS_ROW + c] = (ok && c < nc) ? gsrc[c] : 0.f;
+      }
     }
   }
   cmap[t] = t < nc ? P.colmap[t] : 0;
@@ -108,9 +137,18 @@ __global__ void __launch_bounds__(128) block_kernel(BlockParams P) {
       float wv[WIN], gv[WIN], ev[WIN], xv[WIN];  // xv: GPTAQ pre-quant w / G2PTQ z
       float sv[WIN], zv[WIN];  // the window's quantization parameters, loaded up front
 #pragma unroll
+      for (int k4 = 0; k4 < WIN; k4 += 4) {
+        const float4 a4 = *reinterpret_cast<const float4*>(&wsr[w0 + k4]);
+        wv[k4] = a4.x; wv[k4 + 1] = a4.y; wv[k4 + 2] = a4.z; wv[k4 + 3] = a4.w;
+        if (METHOD == G2Q_METHOD_G2PTQ) {
+          const float4 g4 = *reinterpret_cast<const float4*>(&gsr[w0 + k4]);
+          gv[k4] = g4.x; gv[k4 + 1] = g4.y; gv[k4 + 2] = g4.z; gv[k4 + 3] = g4.w;
+        } else {
+          gv[k4] = gv[k4 + 1] = gv[k4 + 2] = gv[k4 + 3] = 0.f;
+        }
+      }
+#pragma unroll
       for (int k = 0; k < WIN; ++k) {
-        wv[k] = wsr[w0 + k];
-        gv[k] = (METHOD == G2Q_METHOD_G2PTQ) ? gsr[w0 + k] : 0.f;
         ev[k] = 0.f;
         const bool in = w0 + k < nc;
         const int pc = in ? cmap[w0 + k] : 0;
@@ -166,19 +204,25 @@ __global__ void __launch_bounds__(128) block_kernel(BlockParams P) {
         }
       }
 #pragma unroll
-      for (int k = 0; k < WIN; ++k) {
-        wsr[w0 + k] = wv[k];
-        if (METHOD == G2Q_METHOD_G2PTQ) gsr[w0 + k] = gv[k];
+      for (int k4 = 0; k4 < WIN; k4 += 4) {
+        *reinterpret_cast<float4*>(&wsr[w0 + k4]) =
+            make_float4(wv[k4], wv[k4 + 1], wv[k4 + 2], wv[k4 + 3]);
+        if (METHOD == G2Q_METHOD_G2PTQ)
+          *reinterpret_cast<float4*>(&gsr[w0 + k4]) =
+              make_float4(gv[k4], gv[k4 + 1], gv[k4 + 2], gv[k4 + 3]);
       }
       // deferred update of the block columns after this window, applied in
       // column order so each element sees the same sequence of operations
       const int jend = (nc + 3) & ~3;
       for (int j0 = w0 + WIN; j0 < jend; j0 += 4) {
-        float x4[4], g4[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          x4[k] = wsr[j0 + k];
-          g4[k] = (METHOD == G2Q_METHOD_G2PTQ) ? gsr[j0 + k] : 0.f;
+        float x4[4], g4[4] = {0.f, 0.f, 0.f, 0.f};
+        {
+          const float4 a4 = *reinterpret_cast<const float4*>(&wsr[j0]);
+          x4[0] = a4.x; x4[1] = a4.y; x4[2] = a4.z; x4[3] = a4.w;
+          if (METHOD == G2Q_METHOD_G2PTQ) {
+            const float4 b4 = *reinterpret_cast<const float4*>(&gsr[j0]);
+            g4[0] = b4.x; g4[1] = b4.y; g4[2] = b4.z; g4[3] = b4.w;
+          }
         }
 #pragma unroll
         for (int c = 0; c < WIN; ++c) {
@@ -201,11 +245,9 @@ __global__ void __launch_bounds__(128) block_kernel(BlockParams P) {
             }
           }
         }
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          wsr[j0 + k] = x4[k];
-          if (METHOD == G2Q_METHOD_G2PTQ) gsr[j0 + k] = g4[k];
-        }
+        *reinterpret_cast<float4*>(&wsr[j0]) = make_float4(x4[0], x4[1], x4[2], x4[3]);
+        if (METHOD == G2Q_METHOD_G2PTQ)
+          *reinterpret_cast<float4*>(&gsr[j0]) = make_float4(g4[0], g4[1], g4[2], g4[3]);
       }
     }
   }
