@@ -20,45 +20,48 @@ __device__ __forceinline__ float ld_elem<__nv_bfloat16>(const __nv_bfloat16* p) 
   return __bfloat162float(*p);
 }
 
-constexpr int BM = 128, BN = 128, BK = 8;
+constexpr int BK = 8;
 
+// TILE x TILE output tile per CTA (TILE = 128: 8x8 per thread, 64: 4x4),
+// 256 threads, BK = 8, double-buffered shared memory.
 // TA: A stored [K, M] (element (m,k) at A[k*lda + m]); else [M, K].
 // TB: B stored [N, K] (element (k,n) at B[n*ldb + k]); else [K, N].
-template <bool TA, bool TB, typename TAe, typename TBe>
+template <bool TA, bool TB, typename TAe, typename TBe, int TILE>
 __global__ void __launch_bounds__(256) simt_gemm_kernel(SimtArgs p) {
-  const long long m0 = (long long)blockIdx.y * BM;
-  const long long n0 = (long long)blockIdx.x * BN;
+  constexpr int TT = TILE / 16;        // outputs per thread per dimension
+  constexpr int LPT = TILE * BK / 256;  // tile elements each thread loads per operand
+  const long long m0 = (long long)blockIdx.y * TILE;
+  const long long n0 = (long long)blockIdx.x * TILE;
   // Tiles that hold no element of the requested triangle do nothing.
-  if ((p.mask == G2Q_MASK_LOWER) && (m0 + BM - 1 < n0)) return;
-  if ((p.mask == G2Q_MASK_UPPER || p.mirror) && (n0 + BN - 1 < m0)) return;
+  if ((p.mask == G2Q_MASK_LOWER) && (m0 + TILE - 1 < n0)) return;
+  if ((p.mask == G2Q_MASK_UPPER || p.mirror) && (n0 + TILE - 1 < m0)) return;
 
   const long long bz = blockIdx.z;
   const TAe* A = reinterpret_cast<const TAe*>(p.A) + bz * p.sA;
   const TBe* B = reinterpret_cast<const TBe*>(p.B) + bz * p.sB;
   float* C = p.C + bz * p.sC;
 
-  __shared__ __align__(16) float As[2][BK][BM];
-  __shared__ __align__(16) float Bs[2][BK][BN];
+  __shared__ __align__(16) float As[2][BK][TILE];
+  __shared__ __align__(16) float Bs[2][BK][TILE];
 
   const int tid = threadIdx.x;
   const int tx = tid & 15, ty = tid >> 4;
 
-  float acc[8][8];
+  float acc[TT][TT];
 #pragma unroll
-  for (int i = 0; i < 8; ++i)
+  for (int i = 0; i < TT; ++i)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+    for (int j = 0; j < TT; ++j) acc[i][j] = 0.f;
 
-  float ra[4], rb[4];
-  // loader coordinates
-  // TA: k = tid/32, m = (tid%32)*4 + u ; !TA: m = tid/2, k = (tid%2)*4 + u
+  float ra[LPT], rb[LPT];
   auto load_a = [&](long long k0) {
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < LPT; ++u) {
+      const int idx = tid + 256 * u;
       long long m, k;
-      if (TA) { k = tid >> 5; m = (tid & 31) * 4 + u; }
-      else    { m = tid >> 1; k = (tid & 1) * 4 + u; }
-      long long gm = m0 + m, gk = k0 + k;
+      if (TA) { k = idx / TILE; m = idx % TILE; }
+      else    { m = idx / BK; k = idx % BK; }
+      const long long gm = m0 + m, gk = k0 + k;
       float v = 0.f;
       if (gm < p.M && gk < p.K) v = TA ? ld_elem(A + gk * p.lda + gm) : ld_elem(A + gm * p.lda + gk);
       ra[u] = v;
@@ -66,11 +69,12 @@ __global__ void __launch_bounds__(256) simt_gemm_kernel(SimtArgs p) {
   };
   auto load_b = [&](long long k0) {
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < LPT; ++u) {
+      const int idx = tid + 256 * u;
       long long n, k;
-      if (!TB) { k = tid >> 5; n = (tid & 31) * 4 + u; }
-      else     { n = tid >> 1; k = (tid & 1) * 4 + u; }
-      long long gn = n0 + n, gk = k0 + k;
+      if (!TB) { k = idx / TILE; n = idx % TILE; }
+      else     { n = idx / BK; k = idx % BK; }
+      const long long gn = n0 + n, gk = k0 + k;
       float v = 0.f;
       if (gn < p.N && gk < p.K) {
         v = TB ? ld_elem(B + gn * p.ldb + gk) : ld_elem(B + gk * p.ldb + gn);
@@ -81,13 +85,17 @@ __global__ void __launch_bounds__(256) simt_gemm_kernel(SimtArgs p) {
   };
   auto store_ab = [&](int buf) {
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      if (TA) As[buf][tid >> 5][(tid & 31) * 4 + u] = ra[u];
-      else    As[buf][(tid & 1) * 4 + u][tid >> 1] = ra[u];
-      if (!TB) Bs[buf][tid >> 5][(tid & 31) * 4 + u] = rb[u];
-      else     Bs[buf][(tid & 1) * 4 + u][tid >> 1] = rb[u];
+    for (int u = 0; u < LPT; ++u) {
+      const int idx = tid + 256 * u;
+      if (TA) As[buf][idx / TILE][idx % TILE] = ra[u];
+      else    As[buf][idx % BK][idx / BK] = ra[u];
+      if (!TB) Bs[buf][idx / TILE][idx % TILE] = rb[u];
+      else     Bs[buf][idx % BK][idx / BK] = rb[u];
     }
   };
+  // output rows / columns of this thread: four consecutive at ty*4 (and at
+  // TILE/2 + ty*4 for the 8 x 8 case)
+  auto off = [](int i, int base) { return i < 4 ? base * 4 + i : TILE / 2 + base * 4 + (i - 4); };
 
   const long long nk = (p.K + BK - 1) / BK;
   if (nk > 0) {
@@ -104,31 +112,30 @@ __global__ void __launch_bounds__(256) simt_gemm_kernel(SimtArgs p) {
     }
 #pragma unroll
     for (int k = 0; k < BK; ++k) {
-      float a[8], b[8];
-      float4 a0 = *reinterpret_cast<const float4*>(&As[buf][k][ty * 4]);
-      float4 a1 = *reinterpret_cast<const float4*>(&As[buf][k][64 + ty * 4]);
-      float4 b0 = *reinterpret_cast<const float4*>(&Bs[buf][k][tx * 4]);
-      float4 b1 = *reinterpret_cast<const float4*>(&Bs[buf][k][64 + tx * 4]);
-      a[0] = a0.x; a[1] = a0.y; a[2] = a0.z; a[3] = a0.w;
-      a[4] = a1.x; a[5] = a1.y; a[6] = a1.z; a[7] = a1.w;
-      b[0] = b0.x; b[1] = b0.y; b[2] = b0.z; b[3] = b0.w;
-      b[4] = b1.x; b[5] = b1.y; b[6] = b1.z; b[7] = b1.w;
+      float a[TT], b[TT];
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
+      for (int h = 0; h < TT / 4; ++h) {
+        const float4 a4 = *reinterpret_cast<const float4*>(&As[buf][k][off(4 * h, ty)]);
+        const float4 b4 = *reinterpret_cast<const float4*>(&Bs[buf][k][off(4 * h, tx)]);
+        a[4 * h] = a4.x; a[4 * h + 1] = a4.y; a[4 * h + 2] = a4.z; a[4 * h + 3] = a4.w;
+        b[4 * h] = b4.x; b[4 * h + 1] = b4.y; b[4 * h + 2] = b4.z; b[4 * h + 3] = b4.w;
+      }
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+      for (int i = 0; i < TT; ++i)
+#pragma unroll
+        for (int j = 0; j < TT; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
     }
     if (kt + 1 < nk) store_ab(buf ^ 1);
     __syncthreads();
   }
 
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const long long gm = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4));
+  for (int i = 0; i < TT; ++i) {
+    const long long gm = m0 + off(i, ty);
     if (gm >= p.M) continue;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const long long gn = n0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + (j - 4));
+    for (int j = 0; j < TT; ++j) {
+      const long long gn = n0 + off(j, tx);
       if (gn >= p.N) continue;
       bool inside = true;
       if (p.mask == G2Q_MASK_LOWER) inside = gm >= gn;
@@ -150,9 +157,17 @@ __global__ void __launch_bounds__(256) simt_gemm_kernel(SimtArgs p) {
 template <bool TA, bool TB, typename TAe, typename TBe>
 static int launch_simt(const SimtArgs& a, long long batch, cudaStream_t st) {
   if (a.M <= 0 || a.N <= 0 || batch <= 0) return G2Q_OK;
-  dim3 grid(cdiv(a.N, BN), cdiv(a.M, BM), (unsigned)batch);
-  if (grid.y > 65535u || grid.z > 65535u) return G2Q_ERR_INVALID_ARG;
-  simt_gemm_kernel<TA, TB, TAe, TBe><<<grid, 256, 0, st>>>(a);
+  // 64 x 64 tiles when 128 x 128 tiles would leave most SMs idle
+  const long long big = (long long)cdiv(a.N, 128) * cdiv(a.M, 128) * batch;
+  if (big < 2 * 148) {
+    dim3 grid(cdiv(a.N, 64), cdiv(a.M, 64), (unsigned)batch);
+    if (grid.y > 65535u || grid.z > 65535u) return G2Q_ERR_INVALID_ARG;
+    simt_gemm_kernel<TA, TB, TAe, TBe, 64><<<grid, 256, 0, st>>>(a);
+  } else {
+    dim3 grid(cdiv(a.N, 128), cdiv(a.M, 128), (unsigned)batch);
+    if (grid.y > 65535u || grid.z > 65535u) return G2Q_ERR_INVALID_ARG;
+    simt_gemm_kernel<TA, TB, TAe, TBe, 128><<<grid, 256, 0, st>>>(a);
+  }
   G2Q_CHECK_LAUNCH();
   return G2Q_OK;
 }

@@ -160,24 +160,60 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-template <int NA, int NB>
+// SMALL: short-K variant (K <= 4 blocks, no promotion needed): one accumulator,
+// the epilogue reads TMEM directly, and a single pipeline stage (up to three for
+// one-term operands) so that two or three CTAs share an SM and overlap one
+// CTA's epilogue with another's loads and MMAs.
+template <int NA, int NB, bool SMALL = false>
 struct Cfg {
   static constexpr int STAGE_BYTES = (NA + NB) * TILE_BYTES;
-  static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;
+  static constexpr int STAGES =
+      SMALL ? ((NA + NB) == 2 ? 3 : 1) : (192 * 1024) / STAGE_BYTES;
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+  static constexpr int MIN_BLOCKS = SMALL ? ((NA + NB) >= 6 ? 2 : 3) : 1;
+  static constexpr int ACC_COLS = SMALL ? BN : 2 * BN;
   static constexpr int ORDER = (NA > NB ? NA : NB) - 1;  // products a_i b_j with i + j <= ORDER
   static constexpr int PRODUCTS = (NA == 3 && NB == 3) ? 6 : (NA + NB - 1);
   // K blocks per TMEM accumulation group: 16 MMAs for one product, 24 otherwise
   static constexpr int PROMOTE_KB = PRODUCTS == 1 ? 4 : (PRODUCTS <= 3 ? 2 : 1);
 };
 
-template <int NA, int NB>
-__global__ void __launch_bounds__(192, 1)
+// Stores four consecutive accumulator columns v[0..3] of row gm starting at
+// column gn: alpha/beta, bounds, triangle masks and the symmetric mirror.
+#define EPILOGUE_STORE4                                                                        \
+  {                                                                                           \
+    float* dst = Db + gm * p.ldd + gn;                                                        \
+    if (vec_ok && gn + 3 < p.N && (!p.symmetric || gn >= gm) && (!p.lower || gn + 3 <= gm)) { \
+      float4* d4 = reinterpret_cast<float4*>(dst);                                            \
+      if (p.alpha != 0.f) {                                                                   \
+        const float4 o = *d4;                                                                 \
+        v[0] = fmaf(p.alpha, o.x, v[0]);                                                      \
+        v[1] = fmaf(p.alpha, o.y, v[1]);                                                      \
+        v[2] = fmaf(p.alpha, o.z, v[2]);                                                      \
+        v[3] = fmaf(p.alpha, o.w, v[3]);                                                      \
+      }                                                                                       \
+      *d4 = make_float4(v[0], v[1], v[2], v[3]);                                              \
+    } else {                                                                                  \
+      _Pragma("unroll") for (int u = 0; u < 4; ++u) {                                         \
+        if (gn + u >= p.N || (p.symmetric && gn + u < gm) || (p.lower && gn + u > gm))        \
+          continue;                                                                           \
+        if (p.alpha != 0.f) v[u] = fmaf(p.alpha, dst[u], v[u]);                               \
+        dst[u] = v[u];                                                                        \
+      }                                                                                       \
+    }                                                                                         \
+    if (p.symmetric) {                                                                        \
+      _Pragma("unroll") for (int u = 0; u < 4; ++u) if (gn + u < p.N && gn + u > gm)         \
+          Db[(gn + u) * p.ldd + gm] = v[u];                                                   \
+    }                                                                                         \
+  }
+
+template <int NA, int NB, bool SMALL>
+__global__ void __launch_bounds__(192, (Cfg<NA, NB, SMALL>::MIN_BLOCKS))
     tc_gemm_kernel(const __grid_constant__ CUtensorMap ma0, const __grid_constant__ CUtensorMap ma1,
                    const __grid_constant__ CUtensorMap ma2, const __grid_constant__ CUtensorMap mb0,
                    const __grid_constant__ CUtensorMap mb1, const __grid_constant__ CUtensorMap mb2,
                    Params p) {
-  using K = Cfg<NA, NB>;
+  using K = Cfg<NA, NB, SMALL>;
   const int mt = blockIdx.y, nt = blockIdx.x;
   const long long bz = blockIdx.z;
   if (p.symmetric && nt < mt) return;  // tile holds no element of the upper triangle
@@ -195,7 +231,9 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + K::STAGES);
   const uint32_t accf0 = smem_u32(bars + 2 * K::STAGES);
   const uint32_t acce0 = smem_u32(bars + 2 * K::STAGES + 2);
-  const int ngroups = (p.num_kb + p.promote_kb - 1) / p.promote_kb;
+  const int ngroups = SMALL ? (p.num_kb > 0 ? 1 : 0)
+                            : (p.num_kb + p.promote_kb - 1) / p.promote_kb;
+  const int promote_kb = SMALL ? p.num_kb : p.promote_kb;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < K::STAGES; ++s) {
@@ -212,7 +250,7 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_holder)),
-                 "r"(2 * BN)
+                 "r"(K::ACC_COLS)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -259,7 +297,7 @@ __global__ void __launch_bounds__(192, 1)
         if (!mbar_wait(acce0 + 8 * buf, use_ph ^ 1, abort_flag, p.status)) break;
         fence_after();
         const uint32_t acc_t = tmem + (uint32_t)(buf * BN);
-        const int kend = (kb + p.promote_kb < p.num_kb) ? kb + p.promote_kb : p.num_kb;
+        const int kend = (kb + promote_kb < p.num_kb) ? kb + promote_kb : p.num_kb;
         const int kstart = kb;
         bool ok = true;
         for (; kb < kend; ++kb) {
@@ -295,8 +333,41 @@ __global__ void __launch_bounds__(192, 1)
         umma_commit(accf0 + 8 * buf);
       }
     }
+  } else if (SMALL) {
+    // epilogue warps 2..5, short K: read the single accumulator chunk by chunk
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const long long gm = m0 + row;
+    bool ok = true;
+    if (ngroups > 0) ok = mbar_wait(accf0, 0, abort_flag, p.status);
+    fence_after();
+    float* Db = p.D + bz * p.d_bs;
+    const bool vec_ok = ((p.ldd & 3) == 0) && ((reinterpret_cast<uintptr_t>(Db) & 15) == 0);
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t r[32];
+      if (ngroups > 0) {
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32), r);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) r[j] = 0u;
+      }
+      if (!ok || gm >= p.M) continue;
+#pragma unroll
+      for (int j4 = 0; j4 < 8; ++j4) {
+        const long long gn = n0 + c * 32 + 4 * j4;
+        float v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) v[u] = p.beta * __uint_as_float(r[4 * j4 + u]);
+        EPILOGUE_STORE4
+      }
+    }
+    if (ngroups > 0) {
+      fence_before();
+      mbar_arrive(acce0);
+    }
   } else {
-    // epilogue warps 2..5: drain each accumulator buffer into registers
+    // epilogue warps 2..5, long K: drain each accumulator buffer into registers
     const int q = warp & 3;
     const int row = q * 32 + lane;
     const long long gm = m0 + row;
@@ -329,31 +400,7 @@ __global__ void __launch_bounds__(192, 1)
         float v[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) v[u] = p.beta * acc[4 * j4 + u];
-        float* dst = Db + gm * p.ldd + gn;
-        if (vec_ok && gn + 3 < p.N && (!p.symmetric || gn >= gm) && (!p.lower || gn + 3 <= gm)) {
-          float4* d4 = reinterpret_cast<float4*>(dst);
-          if (p.alpha != 0.f) {
-            const float4 o = *d4;
-            v[0] = fmaf(p.alpha, o.x, v[0]);
-            v[1] = fmaf(p.alpha, o.y, v[1]);
-            v[2] = fmaf(p.alpha, o.z, v[2]);
-            v[3] = fmaf(p.alpha, o.w, v[3]);
-          }
-          *d4 = make_float4(v[0], v[1], v[2], v[3]);
-        } else {
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            if (gn + u >= p.N || (p.symmetric && gn + u < gm) || (p.lower && gn + u > gm))
-              continue;
-            if (p.alpha != 0.f) v[u] = fmaf(p.alpha, dst[u], v[u]);
-            dst[u] = v[u];
-          }
-        }
-        if (p.symmetric) {
-#pragma unroll
-          for (int u = 0; u < 4; ++u)
-            if (gn + u < p.N && gn + u > gm) Db[(gn + u) * p.ldd + gm] = v[u];
-        }
+        EPILOGUE_STORE4
       }
     }
   }
@@ -363,7 +410,7 @@ __global__ void __launch_bounds__(192, 1)
     __syncwarp();
     fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                 "r"(2 * BN)
+                 "r"(K::ACC_COLS)
                  : "memory");
   }
 }
@@ -406,15 +453,15 @@ struct Maps {
   CUtensorMap a[3], b[3];
 };
 
-template <int NA, int NB>
+template <int NA, int NB, bool SMALL>
 static int launch(const Maps& m, const Params& p, long long batch, cudaStream_t st) {
-  using K = Cfg<NA, NB>;
+  using K = Cfg<NA, NB, SMALL>;
   static int attr_done[64] = {0};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return G2Q_ERR_CUDA;
   if (dev >= 64 || !attr_done[dev]) {
-    if (cudaFuncSetAttribute(tc_gemm_kernel<NA, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             K::SMEM) != cudaSuccess)
+    if (cudaFuncSetAttribute(tc_gemm_kernel<NA, NB, SMALL>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, K::SMEM) != cudaSuccess)
       return G2Q_ERR_CUDA;
     if (dev < 64) attr_done[dev] = 1;
   }
@@ -422,8 +469,8 @@ static int launch(const Maps& m, const Params& p, long long batch, cudaStream_t 
   if (grid.y > 65535u || grid.z > 65535u) return G2Q_ERR_INVALID_ARG;
   Params q = p;
   q.promote_kb = K::PROMOTE_KB;
-  tc_gemm_kernel<NA, NB><<<grid, 192, K::SMEM, st>>>(m.a[0], m.a[1], m.a[2], m.b[0], m.b[1],
-                                                      m.b[2], q);
+  tc_gemm_kernel<NA, NB, SMALL><<<grid, 192, K::SMEM, st>>>(m.a[0], m.a[1], m.a[2], m.b[0],
+                                                             m.b[1], m.b[2], q);
   G2Q_CHECK_LAUNCH();
   return G2Q_OK;
 }
@@ -432,11 +479,16 @@ static int dispatch(int na, int nb, Maps& m, const Params& p, long long batch,
                     cudaStream_t st) {
   for (int i = na; i < 3; ++i) m.a[i] = m.a[0];
   for (int j = nb; j < 3; ++j) m.b[j] = m.b[0];
-  if (na == 1 && nb == 1) return launch<1, 1>(m, p, batch, st);
-  if (na == 1 && nb == 2) return launch<1, 2>(m, p, batch, st);
-  if (na == 2 && nb == 1) return launch<2, 1>(m, p, batch, st);
-  if (na == 2 && nb == 2) return launch<2, 2>(m, p, batch, st);
-  if (na == 3 && nb == 3) return launch<3, 3>(m, p, batch, st);
+  const bool small = p.num_kb <= 4;
+  if (small) {
+    if (na == 2 && nb == 2) return launch<2, 2, true>(m, p, batch, st);
+    if (na == 3 && nb == 3) return launch<3, 3, true>(m, p, batch, st);
+  }
+  if (na == 1 && nb == 1) return launch<1, 1, false>(m, p, batch, st);
+  if (na == 1 && nb == 2) return launch<1, 2, false>(m, p, batch, st);
+  if (na == 2 && nb == 1) return launch<2, 1, false>(m, p, batch, st);
+  if (na == 2 && nb == 2) return launch<2, 2, false>(m, p, batch, st);
+  if (na == 3 && nb == 3) return launch<3, 3, false>(m, p, batch, st);
   return G2Q_ERR_UNSUPPORTED;
 }
 
