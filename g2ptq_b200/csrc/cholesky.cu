@@ -13,6 +13,9 @@
 //           Y_i: -= L_ik X_k:                (i > k)             (GEMM)
 // potrf + trtri = 2C^3/3 flops, where the reference chain
 // potrf -> cholesky_inverse -> potrf(upper) costs 4C^3/3.
+// The factorization (panel, TRSM, SYRK) runs on the caller's stream; the
+// inverse chain (X_k, Y update), which no later panel depends on, runs on a
+// library-owned side stream ordered by per-step events and joined at the end.
 #include "gemm_simt.cuh"
 
 namespace g2q {
@@ -181,11 +184,6 @@ __global__ void extract_u_kernel(const float* X, long long C, float* U, int* inf
   if (nan_seen && info) atomicCAS(info, 0, -1);
 }
 
-static int gemm(float* Cp, long long ldc, const float* Ap, long long lda, bool ta,
-                const float* Bp, long long ldb, bool tb, long long M, long long N, long long K,
-                float alpha, float beta, int mask, cudaStream_t st) {
-  return simt_gemm_f32(Cp, ldc, Ap, lda, ta, Bp, ldb, tb, M, N, K, alpha, beta, mask, st);
-}
 
 
 int split3(const float* src, long long lds, long long rows, long long cols, __nv_bfloat16* h,
@@ -194,64 +192,120 @@ int tc_update3(float* D, long long ldd, long long M, long long N, long long K,
                __nv_bfloat16* const* a3, long long lda, __nv_bfloat16* const* b3, long long ldb,
                int lower, float alpha, float beta, cudaStream_t st);
 
-// Trailing updates of step k on the tensor cores, fp32-accurate (three-term
-// bf16 split, six products): A_ij -= L_ik L_jk^T (lower) and Y_i: -= L_ik X_k:.
-// Returns G2Q_ERR_UNSUPPORTED when the shapes do not suit TMA.
-static int tc_trailing(float* A, float* Y, long long C, long long k0, int nb, long long rest,
-                       __nv_bfloat16* lt, __nv_bfloat16* xk, cudaStream_t st) {
-  if (C % 8) return G2Q_ERR_UNSUPPORTED;
-  const long long tsz = (long long)NB * C;
-  __nv_bfloat16* l3[3] = {lt, lt + tsz, lt + 2 * tsz};
-  __nv_bfloat16* x3[3] = {xk, xk + tsz, xk + 2 * tsz};
-  // L_ik^T (nb x rest, row stride C) and X_k: (nb x (k0 + nb), row stride C)
-  G2Q_TRY(split3(A + (k0 + nb) * C + k0, C, rest, nb, l3[0], l3[1], l3[2], C, 1, st));
-  G2Q_TRY(split3(Y + k0 * C, C, nb, k0 + nb, x3[0], x3[1], x3[2], C, 0, st));
-  int s = tc_update3(A + (k0 + nb) * C + (k0 + nb), C, rest, rest, nb, l3, C, l3, C, 1, 1.f,
-                     -1.f, st);
-  if (s != G2Q_OK) return s;
-  return tc_update3(Y + (k0 + nb) * C, C, rest, k0 + nb, nb, l3, C, x3, C, 0, 1.f, -1.f, st);
+// Side stream and per-step events of the inverse chain (one set per device).
+struct SideState {
+  cudaStream_t side = nullptr;
+  cudaEvent_t* ev = nullptr;  // [2 * cap]: factor-step-done, inverse-step-done
+  int cap = 0;
+};
+
+static int side_state(int steps, SideState** out) {
+  static SideState states[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64) return G2Q_ERR_CUDA;
+  SideState& s = states[dev];
+  if (!s.side && cudaStreamCreateWithFlags(&s.side, cudaStreamNonBlocking) != cudaSuccess)
+    return G2Q_ERR_CUDA;
+  if (s.cap < steps + 1) {
+    cudaEvent_t* ev = new cudaEvent_t[2 * (steps + 1)];
+    for (int i = 0; i < 2 * (steps + 1); ++i)
+      if (cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming) != cudaSuccess)
+        return G2Q_ERR_CUDA;
+    // events of the previous set may still be referenced by queued work; keep them
+    s.ev = ev;
+    s.cap = steps + 1;
+  }
+  *out = &s;
+  return G2Q_OK;
+}
+
+static bool tc_ok(long long C) { return C % 8 == 0; }
+
+// Workspace layout (floats unless noted): A [C*C], Y [C*C], diagonal inverses
+// [nblk][NB*NB], mean diag [64], then bf16: L21^T splits [2 buffers][3][NB*C],
+// X_k splits [3][NB*C].
+struct CholWs {
+  float *A, *Y, *linv, *mdiag;
+  __nv_bfloat16 *lt, *xk;
+};
+
+static CholWs carve(float* ws, long long C) {
+  CholWs w;
+  const long long nblk = (C + NB - 1) / NB;
+  w.A = ws;
+  w.Y = w.A + C * C;
+  w.linv = w.Y + C * C;
+  w.mdiag = w.linv + nblk * NB * NB;
+  w.lt = reinterpret_cast<__nv_bfloat16*>(w.mdiag + 64);
+  w.xk = w.lt + 2 * 3 * (long long)NB * C;
+  return w;
 }
 
 static int chol_one(float* U, const float* H, long long C, long long ldh, float damp_percent,
                     int* info, float* ws, int precision, cudaStream_t st) {
-  float* A = ws;
-  float* Y = A + C * C;
-  float* Linv = Y + C * C;
-  float* mdiag = Linv + NB * NB;
-  __nv_bfloat16* lt = reinterpret_cast<__nv_bfloat16*>(mdiag + 64);
-  __nv_bfloat16* xk = lt + 3 * (long long)NB * C;
+  CholWs w = carve(ws, C);
+  float* A = w.A;
+  float* Y = w.Y;
+  const long long nblk = (C + NB - 1) / NB;
+  const bool use_tc = precision == 1 && tc_ok(C);
+  SideState* ss = nullptr;
+  G2Q_TRY(side_state((int)nblk, &ss));
+  cudaStream_t side = ss->side;
+  cudaEvent_t* ev = ss->ev;  // ev[2k]: factor step k done, ev[2k+1]: inverse step k done
   if (info && cudaMemsetAsync(info, 0, sizeof(int), st) != cudaSuccess) return G2Q_ERR_CUDA;
-  mean_diag_kernel<<<1, 1024, 0, st>>>(H, C, ldh, mdiag);
+  mean_diag_kernel<<<1, 1024, 0, st>>>(H, C, ldh, w.mdiag);
   G2Q_CHECK_LAUNCH();
   int blocks = (int)((C * C + 255) / 256);
   if (blocks > 148 * 32) blocks = 148 * 32;
-  reverse_damp_kernel<<<blocks, 256, 0, st>>>(H, C, ldh, mdiag, damp_percent, A, Y);
+  reverse_damp_kernel<<<blocks, 256, 0, st>>>(H, C, ldh, w.mdiag, damp_percent, A, Y);
   G2Q_CHECK_LAUNCH();
-  for (long long k0 = 0; k0 < C; k0 += NB) {
+  const long long tsz = (long long)NB * C;
+  for (long long kb = 0; kb < nblk; ++kb) {
+    const long long k0 = kb * NB;
     const int nb = (int)((C - k0) < NB ? (C - k0) : NB);
     const long long rest = C - k0 - nb;
-    panel_kernel<<<1, 256, 0, st>>>(A, C, k0, nb, Linv, info);
+    float* linv = w.linv + kb * NB * NB;
+    __nv_bfloat16* lt = w.lt + (kb & 1) * 3 * tsz;
+    __nv_bfloat16* l3[3] = {lt, lt + tsz, lt + 2 * tsz};
+    __nv_bfloat16* x3[3] = {w.xk, w.xk + tsz, w.xk + 2 * tsz};
+    // ---- factorization (caller's stream): panel, TRSM, split, SYRK
+    panel_kernel<<<1, 256, 0, st>>>(A, C, k0, nb, linv, info);
     G2Q_CHECK_LAUNCH();
-    // X_k: = Linv_kk Y_k:  (columns 0 .. k0+nb), in place in Y
-    G2Q_TRY(gemm(Y + k0 * C, C, Linv, NB, false, Y + k0 * C, C, false, nb, k0 + nb, nb,
-                 0.f, 1.f, G2Q_MASK_FULL, st));
-    if (rest <= 0) break;
-    // L_ik = A_ik Linv_kk^T, in place in A
-    G2Q_TRY(gemm(A + (k0 + nb) * C + k0, C, A + (k0 + nb) * C + k0, C, false, Linv, NB, true,
-                 rest, nb, nb, 0.f, 1.f, G2Q_MASK_FULL, st));
-    if (precision == 1) {
-      const int s_tc = tc_trailing(A, Y, C, k0, nb, rest, lt, xk, st);
-      if (s_tc == G2Q_OK) continue;
-      if (s_tc != G2Q_ERR_UNSUPPORTED) return s_tc;
+    if (rest > 0) {
+      // L_ik = A_ik Linv_kk^T, in place in A
+      G2Q_TRY(simt_gemm_f32(A + (k0 + nb) * C + k0, C, A + (k0 + nb) * C + k0, C, false, linv,
+                            NB, true, rest, nb, nb, 0.f, 1.f, G2Q_MASK_FULL, st));
+      if (use_tc) {
+        // the inverse chain of step kb-2 used this L21^T buffer
+        if (kb >= 2 && cudaStreamWaitEvent(st, ev[2 * (kb - 2) + 1], 0) != cudaSuccess)
+          return G2Q_ERR_CUDA;
+        G2Q_TRY(split3(A + (k0 + nb) * C + k0, C, rest, nb, l3[0], l3[1], l3[2], C, 1, st));
+        G2Q_TRY(tc_update3(A + (k0 + nb) * C + (k0 + nb), C, rest, rest, nb, l3, C, l3, C, 1,
+                           1.f, -1.f, st));
+      } else {
+        G2Q_TRY(simt_gemm_f32(A + (k0 + nb) * C + (k0 + nb), C, A + (k0 + nb) * C + k0, C, false,
+                              A + (k0 + nb) * C + k0, C, true, rest, rest, nb, 1.f, -1.f,
+                              G2Q_MASK_LOWER, st));
+      }
     }
-    // A_ij -= L_ik L_jk^T (lower triangle of the trailing matrix)
-    G2Q_TRY(gemm(A + (k0 + nb) * C + (k0 + nb), C, A + (k0 + nb) * C + k0, C, false,
-                 A + (k0 + nb) * C + k0, C, true, rest, rest, nb, 1.f, -1.f, G2Q_MASK_LOWER,
-                 st));
-    // Y_i: -= L_ik X_k:
-    G2Q_TRY(gemm(Y + (k0 + nb) * C, C, A + (k0 + nb) * C + k0, C, false, Y + k0 * C, C, false,
-                 rest, k0 + nb, nb, 1.f, -1.f, G2Q_MASK_FULL, st));
+    if (cudaEventRecord(ev[2 * kb], st) != cudaSuccess) return G2Q_ERR_CUDA;
+    // ---- inverse chain (side stream): X_k: = Linv_kk Y_k:, then Y_i: -= L_ik X_k:
+    if (cudaStreamWaitEvent(side, ev[2 * kb], 0) != cudaSuccess) return G2Q_ERR_CUDA;
+    G2Q_TRY(simt_gemm_f32(Y + k0 * C, C, linv, NB, false, Y + k0 * C, C, false, nb, k0 + nb, nb,
+                          0.f, 1.f, G2Q_MASK_FULL, side));
+    if (rest > 0) {
+      if (use_tc) {
+        G2Q_TRY(split3(Y + k0 * C, C, nb, k0 + nb, x3[0], x3[1], x3[2], C, 0, side));
+        G2Q_TRY(tc_update3(Y + (k0 + nb) * C, C, rest, k0 + nb, nb, l3, C, x3, C, 0, 1.f, -1.f,
+                           side));
+      } else {
+        G2Q_TRY(simt_gemm_f32(Y + (k0 + nb) * C, C, A + (k0 + nb) * C + k0, C, false, Y + k0 * C,
+                              C, false, rest, k0 + nb, nb, 1.f, -1.f, G2Q_MASK_FULL, side));
+      }
+    }
+    if (cudaEventRecord(ev[2 * kb + 1], side) != cudaSuccess) return G2Q_ERR_CUDA;
   }
+  if (cudaStreamWaitEvent(st, ev[2 * (nblk - 1) + 1], 0) != cudaSuccess) return G2Q_ERR_CUDA;
   extract_u_kernel<<<blocks, 256, 0, st>>>(Y, C, U, info);
   G2Q_CHECK_LAUNCH();
   return G2Q_OK;
@@ -260,8 +314,9 @@ static int chol_one(float* U, const float* H, long long C, long long ldh, float 
 }  // namespace g2q
 
 extern "C" size_t g2q_chol_workspace_bytes(int64_t C) {
-  return (size_t)(2 * C * C + g2q::NB * g2q::NB + 64) * sizeof(float) +
-         (size_t)6 * g2q::NB * C * sizeof(__nv_bfloat16) + 256;
+  const int64_t nblk = (C + g2q::NB - 1) / g2q::NB;
+  return (size_t)(2 * C * C + nblk * g2q::NB * g2q::NB + 64) * sizeof(float) +
+         (size_t)9 * g2q::NB * C * sizeof(__nv_bfloat16) + 256;
 }
 
 extern "C" int g2q_chol_upper_inverse(float* U, const float* H, int64_t C, int64_t ldh,

@@ -54,7 +54,9 @@ struct Params {
   float alpha, beta;
   int symmetric;
   int lower;       // write only the lower triangle (m >= n); skip tiles above it
-  int promote_kb;  // K blocks accumulated in TMEM before the epilogue drains them
+  int promote_kb;
+  int raster;      // 1: 1-D grid over the needed tiles in groups of GROUP_M tile rows
+  int tiles_m, tiles_n;  // K blocks accumulated in TMEM before the epilogue drains them
   int* status;
 };
 
@@ -207,6 +209,41 @@ struct Cfg {
     }                                                                                         \
   }
 
+// Grouped rasterization for long-K products: consecutive CTAs walk GROUP_M tile
+// rows together, so a wave of CTAs reads a few dozen distinct operand column
+// blocks per K step instead of one per CTA and X stays in L2 between them.
+// Symmetric outputs enumerate only tiles with nt >= mt.
+constexpr int GROUP_M = 8;
+__device__ __forceinline__ bool decode_tile(long long id, int Tm, int Tn, bool sym, int& mt,
+                                            int& nt) {
+  for (int r0 = 0; r0 < Tm; r0 += GROUP_M) {
+    const int gsz = (Tm - r0) < GROUP_M ? (Tm - r0) : GROUP_M;
+    const long long tri = (long long)gsz * (gsz + 1) / 2;
+    const long long count = sym ? tri + (long long)(Tn - r0 - gsz) * gsz : (long long)gsz * Tn;
+    if (id < count) {
+      if (!sym) {
+        nt = (int)(id / gsz);
+        mt = r0 + (int)(id % gsz);
+      } else if (id < tri) {
+        int c = 0;
+        while (id >= c + 1) {
+          id -= c + 1;
+          ++c;
+        }
+        nt = r0 + c;
+        mt = r0 + (int)id;
+      } else {
+        id -= tri;
+        nt = r0 + gsz + (int)(id / gsz);
+        mt = r0 + (int)(id % gsz);
+      }
+      return true;
+    }
+    id -= count;
+  }
+  return false;
+}
+
 template <int NA, int NB, bool SMALL>
 __global__ void __launch_bounds__(192, (Cfg<NA, NB, SMALL>::MIN_BLOCKS))
     tc_gemm_kernel(const __grid_constant__ CUtensorMap ma0, const __grid_constant__ CUtensorMap ma1,
@@ -214,8 +251,9 @@ __global__ void __launch_bounds__(192, (Cfg<NA, NB, SMALL>::MIN_BLOCKS))
                    const __grid_constant__ CUtensorMap mb1, const __grid_constant__ CUtensorMap mb2,
                    Params p) {
   using K = Cfg<NA, NB, SMALL>;
-  const int mt = blockIdx.y, nt = blockIdx.x;
+  int mt = blockIdx.y, nt = blockIdx.x;
   const long long bz = blockIdx.z;
+  if (p.raster && !decode_tile(blockIdx.x, p.tiles_m, p.tiles_n, p.symmetric, mt, nt)) return;
   if (p.symmetric && nt < mt) return;  // tile holds no element of the upper triangle
   if (p.lower && nt > mt) return;      // tile holds no element of the lower triangle
 
@@ -465,10 +503,19 @@ static int launch(const Maps& m, const Params& p, long long batch, cudaStream_t 
       return G2Q_ERR_CUDA;
     if (dev < 64) attr_done[dev] = 1;
   }
-  dim3 grid(cdiv(p.N, BN), cdiv(p.M, BM), (unsigned)batch);
-  if (grid.y > 65535u || grid.z > 65535u) return G2Q_ERR_INVALID_ARG;
   Params q = p;
   q.promote_kb = K::PROMOTE_KB;
+  q.tiles_m = cdiv(p.M, BM);
+  q.tiles_n = cdiv(p.N, BN);
+  dim3 grid(q.tiles_n, q.tiles_m, (unsigned)batch);
+  if (q.raster) {
+    const long long tm = q.tiles_m, tn = q.tiles_n;
+    const long long n = q.symmetric ? tm * (tm + 1) / 2 : tm * tn;
+    if (q.symmetric && tm != tn) return G2Q_ERR_INVALID_ARG;
+    if (n > 0x7fffffffLL) return G2Q_ERR_INVALID_ARG;
+    grid = dim3((unsigned)n, 1, (unsigned)batch);
+  }
+  if (grid.y > 65535u || grid.z > 65535u) return G2Q_ERR_INVALID_ARG;
   tc_gemm_kernel<NA, NB, SMALL><<<grid, 192, K::SMEM, st>>>(m.a[0], m.a[1], m.a[2], m.b[0],
                                                              m.b[1], m.b[2], q);
   G2Q_CHECK_LAUNCH();
@@ -612,6 +659,7 @@ int tc_gram(float* D, long long ldd, long long M, long long N, const void* A, in
   p.alpha = alpha; p.beta = beta;
   p.symmetric = symmetric ? 1 : 0;
   p.status = nullptr;
+  p.raster = 1;
   return tc::dispatch(na, nb, mp, p, 1, st);
 }
 
