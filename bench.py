@@ -5,7 +5,8 @@ down linears (4096x4096, 1024x4096 x2, 4096x4096, 14336x4096 x2, 4096x14336),
 GPTQ W4 symmetric, group 128, damp 0.01, act-order with static groups,
 compressed-tensors export on, calibrated on 128 sequences x 2048 tokens.  One
 step = every ``add_batch`` call of the calibration pass (one per sequence and
-linear, ``--bsz 1``) followed by ``fasterquant`` of all seven linears.
+linear, ``--bsz 1``) followed by ``fasterquant`` of all seven linears (their
+device work overlapped on a small stream pool by ``fasterquant_all``).
 Activations are seeded synthetic BF16 hidden states N(0, 1) with 4 outlier
 channels x20 per linear input (the stand-in for the model forward over
 uniform random token ids); weights are random N(0, 0.02) BF16.
@@ -163,9 +164,9 @@ def one_step(torch, layers, acts, n_local, world, rank, dist, obj2rank=None, h2d
         _, _, obj2rank = common_utils.partition_layers(specs, world)
         gptq_utils.reduce_to_target_rank(specs, obj2rank)
         owners = {k: o for k, o in objs.items() if obj2rank[o] == rank}
-    for name, obj in owners.items():
-        obj.fasterquant(blocksize=BLOCKSIZE, percdamp=PERCDAMP, groupsize=GROUPSIZE,
-                        actorder=True, static_groups=True, export_compressed_tensors=True)
+    gptq_utils.fasterquant_all(list(owners.values()), blocksize=BLOCKSIZE, percdamp=PERCDAMP,
+                               groupsize=GROUPSIZE, actorder=True, static_groups=True,
+                               export_compressed_tensors=True)
     if world > 1:
         common_utils.broadcast_quantized_param(list(objs.values()), obj2rank,
                                                export_compressed_tensors=True)

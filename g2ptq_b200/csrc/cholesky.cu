@@ -192,30 +192,46 @@ int tc_update3(float* D, long long ldd, long long M, long long N, long long K,
                __nv_bfloat16* const* a3, long long lda, __nv_bfloat16* const* b3, long long ldb,
                int lower, float alpha, float beta, cudaStream_t st);
 
-// Side stream and per-step events of the inverse chain (one set per device).
+// Side stream and per-step events of the inverse chain, one set per (device,
+// caller stream) so that factorizations issued on different streams overlap.
 struct SideState {
+  int dev = -1;
+  cudaStream_t main = nullptr;
   cudaStream_t side = nullptr;
   cudaEvent_t* ev = nullptr;  // [2 * cap]: factor-step-done, inverse-step-done
   int cap = 0;
 };
 
-static int side_state(int steps, SideState** out) {
-  static SideState states[64];
+static int side_state(cudaStream_t main, int steps, SideState** out) {
+  constexpr int kSlots = 64;
+  static SideState states[kSlots];
+  static int next_slot = 0;
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64) return G2Q_ERR_CUDA;
-  SideState& s = states[dev];
-  if (!s.side && cudaStreamCreateWithFlags(&s.side, cudaStreamNonBlocking) != cudaSuccess)
-    return G2Q_ERR_CUDA;
-  if (s.cap < steps + 1) {
+  if (cudaGetDevice(&dev) != cudaSuccess) return G2Q_ERR_CUDA;
+  SideState* s = nullptr;
+  for (int i = 0; i < kSlots; ++i)
+    if (states[i].side && states[i].dev == dev && states[i].main == main) s = &states[i];
+  if (!s) {
+    s = &states[next_slot];
+    next_slot = (next_slot + 1) % kSlots;
+    if (s->side && s->dev != dev) {
+      *s = SideState();  // slot held a stream of another device: start over
+    }
+    if (!s->side && cudaStreamCreateWithFlags(&s->side, cudaStreamNonBlocking) != cudaSuccess)
+      return G2Q_ERR_CUDA;
+    s->dev = dev;
+    s->main = main;
+  }
+  if (s->cap < steps + 1) {
     cudaEvent_t* ev = new cudaEvent_t[2 * (steps + 1)];
     for (int i = 0; i < 2 * (steps + 1); ++i)
       if (cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming) != cudaSuccess)
         return G2Q_ERR_CUDA;
     // events of the previous set may still be referenced by queued work; keep them
-    s.ev = ev;
-    s.cap = steps + 1;
+    s->ev = ev;
+    s->cap = steps + 1;
   }
-  *out = &s;
+  *out = s;
   return G2Q_OK;
 }
 
@@ -249,7 +265,7 @@ static int chol_one(float* U, const float* H, long long C, long long ldh, float 
   const long long nblk = (C + NB - 1) / NB;
   const bool use_tc = precision == 1 && tc_ok(C);
   SideState* ss = nullptr;
-  G2Q_TRY(side_state((int)nblk, &ss));
+  G2Q_TRY(side_state(st, (int)nblk, &ss));
   cudaStream_t side = ss->side;
   cudaEvent_t* ev = ss->ev;  // ev[2k]: factor step k done, ev[2k+1]: inverse step k done
   if (info && cudaMemsetAsync(info, 0, sizeof(int), st) != cudaSuccess) return G2Q_ERR_CUDA;

@@ -30,7 +30,7 @@ DAMP_INCREMENT = 0.0015
 STAGE_TOKENS = int(os.environ.get("G2PTQ_B200_STAGE_TOKENS", "16384"))
 STAGE_BYTES = int(os.environ.get("G2PTQ_B200_STAGE_BYTES", str(512 << 20)))
 # 0 = fp32 CUDA cores, 1 = tcgen05 tensor cores (Gram products and trailing updates)
-PRECISION = int(os.environ.get("G2PTQ_B200_PRECISION", "0"))
+PRECISION = int(os.environ.get("G2PTQ_B200_PRECISION", "1"))
 
 
 class TokenStage:
@@ -261,3 +261,88 @@ class StagingMixin:
             raise RuntimeError("add_batch needs the statistics on the device; wrap the "
                                "calibration forward in the object's onload context when "
                                "offload_hessians=True")
+
+
+class Pending:
+    """A launched ``fasterquant`` whose results are still on the device.
+
+    ``run(W_init)`` enqueues compensation, un-permutation and the cast / NaN
+    count and returns ``(nan, outs, codes)``; ``finish()`` reads every status
+    word in one device-to-host copy, re-factors failing layers with the damp
+    auto-increment (re-running the compensation from ``W0``), raises where the
+    reference raises and hands the weights (and export qparams) to the layers.
+    """
+
+    def __init__(self, layers, nl, H, U, info, damps, params, run, W0, bits, groupsize,
+                 columns, rows, export, dynamic, actorder):
+        self.layers, self.nl, self.H, self.U, self.info = layers, nl, H, U, info
+        self.damps, self.params, self.run, self.W0 = damps, params, run, W0
+        self.bits, self.groupsize, self.columns, self.rows = bits, groupsize, columns, rows
+        self.export, self.dynamic, self.actorder = export, dynamic, actorder
+        self.nan, self.outs, self.codes = run(W0.clone())
+
+    def finish(self):
+        nl = self.nl
+        flags = sync_check(self.info, self.nan, *self.params.statuses())
+        if any(i != 0 for i in flags[:nl]):
+            retry_failed(self.H, self.U, flags[:nl], self.damps)
+            self.params.status.zero_()
+            self.nan, self.outs, self.codes = self.run(self.W0.clone())
+            flags = sync_check(self.info, self.nan, *self.params.statuses())
+            flags[:nl] = [0] * nl
+        if any(f != 0 for f in flags[nl + 1:]):
+            raise RuntimeError("WeightQuantizer.find_params: non-positive scale")
+        if flags[nl] != 0:
+            raise ValueError("NaN in weights")
+        if self.dynamic:
+            self.params.bind_dynamic()
+        if self.export and self.dynamic and self.actorder:
+            raise AssertionError("Scales in the same quantization group should be the same.")
+        finish(self.layers, self.outs, self.codes, self.params, self.bits, self.groupsize,
+               self.columns, self.export, self.rows)
+        return self.damps
+
+
+_STREAMS = {}
+
+
+def stream_pool(device, n=4):
+    key = (device.index if device.index is not None else torch.cuda.current_device(), n)
+    if key not in _STREAMS:
+        _STREAMS[key] = [torch.cuda.Stream(device=device) for _ in range(n)]
+    return _STREAMS[key]
+
+
+def fasterquant_all(objs, streams=4, **kwargs):
+    """Quantize several quantizer objects concurrently: each object's pipeline
+    is enqueued on one stream of a small pool, then every object is finished
+    (status read, retry, write-back) in order.  Equivalent to calling
+    ``obj.fasterquant(**kwargs)`` for each object in turn."""
+    if not objs:
+        return
+    cur = torch.cuda.current_stream(objs[0].dev)
+    pool = stream_pool(objs[0].dev, streams)
+    # Pending add_batch folds are large Gram products that fill the GPU on
+    # their own: run them in order on the caller's stream first, and overlap
+    # only the latency-bound factorization / compensation chains.
+    for o in objs:
+        if not getattr(o, "offload_hessians", False):
+            o._flush_all()
+    launched = []
+    for i, o in enumerate(objs):
+        s = pool[i % len(pool)]
+        s.wait_stream(cur)
+        with torch.cuda.stream(s):
+            launched.append((s, o, o._fq_launch(**kwargs)))
+    for s, o, pending in launched:
+        with torch.cuda.stream(s):
+            o._last_damps = pending.finish()
+        cur.wait_stream(s)
+        if pending.export:
+            # export buffers were allocated on the side stream and live on
+            # with the layer: tie their reuse to the caller's stream too
+            for layer in o.layers:
+                for name in compressed_tensors_utils.Q_PARAMS:
+                    buf = getattr(layer, name, None)
+                    if isinstance(buf, torch.Tensor) and buf.is_cuda:
+                        buf.record_stream(cur)

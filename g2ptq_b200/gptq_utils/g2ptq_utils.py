@@ -133,12 +133,20 @@ class G2PTQ(_engine.StagingMixin):
                     static_groups=False, enable_gradient_update=True, alpha=0.0,
                     export_compressed_tensors=False, backend="torch", graph=False):
         """g2ptq_utils.py:349-519 (``backend`` / ``graph`` accepted and ignored)."""
+        pending = self._fq_launch(blocksize=blocksize, percdamp=percdamp, groupsize=groupsize,
+                                  actorder=actorder, static_groups=static_groups,
+                                  enable_gradient_update=enable_gradient_update, alpha=alpha,
+                                  export_compressed_tensors=export_compressed_tensors)
+        self._last_damps = pending.finish()
+
+    def _fq_launch(self, blocksize=128, percdamp=0.01, groupsize=-1, actorder=False,
+                   static_groups=False, enable_gradient_update=True, alpha=0.0,
+                   export_compressed_tensors=False, backend="torch", graph=False):
         B, R, C, G = self.num_layers, self.rows, self.columns, self.num_groups
         rps = R // G
         nl = B * G
         q0 = self.quantizer[0]
-        hclip = q0.hclip
-        if hclip:
+        if q0.hclip:
             raise NotImplementedError("g2ptq_b200: --w_hclip needs the clip search")
         W = torch.stack([l.weight.data for l in self.layers]).float().contiguous()
         W_flat = W.view(B * R, C)
@@ -146,6 +154,7 @@ class G2PTQ(_engine.StagingMixin):
         with self._maybe_onload_hessian_grad(gradients=True):
             grad = self.gradients.to(self.dev, copy=True).view(nl, rps, C).contiguous()
             H = self.H.view(nl, C, C)
+            self.H = None
         params = _engine.ParamSet(self.quantizer, B * R, C, groupsize, self.dev)
         dynamic = not (groupsize == -1 or static_groups)
         if not dynamic:
@@ -159,9 +168,9 @@ class G2PTQ(_engine.StagingMixin):
                     q.find_params(W_sub[:, :, i * groupsize:(i + 1) * groupsize]
                                   .reshape(B * R, -1))
             Q_sub = fake_quantize_grouped(self.quantizer, W_sub, groupsize).contiguous()
-        perm = invperm = None
+        perm = None
         if actorder:
-            perm, invperm = _engine.act_order_perm(torch.mean(self.act_square, dim=0))
+            perm, _ = _engine.act_order_perm(torch.mean(self.act_square, dim=0))
             W_sub = ops.permute_cols(W_sub, perm)
             H = ops.permute_sym(H, perm)
             grad = ops.permute_cols(grad, perm)
@@ -169,10 +178,10 @@ class G2PTQ(_engine.StagingMixin):
                 Q_sub = ops.permute_cols(Q_sub, perm)
         U, info, damps = _engine.factor_with_retry(H, percdamp)
         colgroup = params.colgroup(perm, static_groups, self.dev)
-        W0 = W_sub.clone()
+        W0 = W_sub.contiguous()
         codes = torch.empty(nl, rps, C, dtype=torch.int8, device=self.dev)
 
-        def precompute():
+        def run(Wp):
             # Z = (G U^T) * beta, GHinv = Z U  (g2ptq_utils.py:459-476)
             T1 = ops.gemm(torch.empty_like(grad), grad, U, transB=True)
             if use_grad:
@@ -183,10 +192,6 @@ class G2PTQ(_engine.StagingMixin):
                 beta = torch.zeros(nl, rps, dtype=torch.float32, device=self.dev)
             Z = ops.scale_rows(T1, beta)
             GH = ops.gemm(torch.empty_like(grad), Z, U)
-            return Z, GH
-
-        def compensate_and_cast(Wp):
-            Z, GH = precompute()
             ops.compensate(_lib.METHOD_G2PTQ, Wp, U, params.scale, params.zero, colgroup,
                            dynamic, groupsize, q0.bits, q0.sym, blocksize, codes, z=Z, gh=GH,
                            status=params.status, precision=_engine.PRECISION)
@@ -194,33 +199,13 @@ class G2PTQ(_engine.StagingMixin):
             if actorder:
                 Q = ops.permute_cols(Wp, perm, inverse=True)
                 cq = ops.permute_cols(codes, perm, inverse=True)
-            Q = Q.view(B, R, C)
-            cq = cq.view(B, R, C)
+            Q, cq = Q.view(B, R, C), cq.view(B, R, C)
             nan, outs = _engine.write_back(self.layers, Q, cq, params, q0.bits, groupsize, C,
                                            export_compressed_tensors)
             return nan, outs, cq
 
-        Wp = W0.clone()
-        nan, outs, cq = compensate_and_cast(Wp)
-        flags = _engine.sync_check(info, nan, *params.statuses())
-        info_list = flags[:nl]
-        if any(i != 0 for i in info_list):
-            _engine.retry_failed(H, U, info_list, damps)
-            params.status.zero_()
-            nan, outs, cq = compensate_and_cast(W0.clone())
-            flags = _engine.sync_check(info, nan, *params.statuses())
-            flags[:nl] = [0] * nl
-        if any(f != 0 for f in flags[nl + 1:]):
-            raise RuntimeError("WeightQuantizer.find_params: non-positive scale")
-        if flags[nl] != 0:
-            raise ValueError("NaN in weights")
-        if dynamic:
-            params.bind_dynamic()
-        if export_compressed_tensors and dynamic and actorder:
-            raise AssertionError("Scales in the same quantization group should be the same.")
-        _engine.finish(self.layers, outs, cq, params, q0.bits, groupsize, C,
-                       export_compressed_tensors, R)
-        self._last_damps = damps
+        return _engine.Pending(self.layers, nl, H, U, info, damps, params, run, W0, q0.bits,
+                               groupsize, C, R, export_compressed_tensors, dynamic, actorder)
 
     def free(self):
         self._H = None

@@ -109,6 +109,14 @@ class GPTAQ(_engine.StagingMixin):
                     static_groups=False, alpha=0.25, export_compressed_tensors=False,
                     backend="torch", graph=False):
         """gptaq_utils.py:263-391 (``backend`` / ``graph`` accepted and ignored)."""
+        pending = self._fq_launch(blocksize=blocksize, percdamp=percdamp, groupsize=groupsize,
+                                  actorder=actorder, static_groups=static_groups, alpha=alpha,
+                                  export_compressed_tensors=export_compressed_tensors)
+        self._last_damps = pending.finish()
+
+    def _fq_launch(self, blocksize=128, percdamp=0.01, groupsize=-1, actorder=False,
+                   static_groups=False, alpha=0.25, export_compressed_tensors=False,
+                   backend="torch", graph=False):
         B, R, C = self.num_layers, self.rows, self.columns
         q0 = self.quantizer[0]
         if q0.hclip:
@@ -123,18 +131,17 @@ class GPTAQ(_engine.StagingMixin):
         if not dynamic:
             params.init_static(W.view(B * R, C))
         ops.prepare_hessian(H, W, extra=dX)
-        perm = invperm = None
+        perm = None
         if actorder:
-            perm, invperm = _engine.act_order_perm(ops.mean_diag(H))
+            perm, _ = _engine.act_order_perm(ops.mean_diag(H))
             W = ops.permute_cols(W, perm)
             H = ops.permute_sym(H, perm)
             dX = ops.permute_sym(dX, perm)
         U, info, damps = _engine.factor_with_retry(H, percdamp)
         colgroup = params.colgroup(perm, static_groups, self.dev)
-        W0 = W.clone()
         codes = torch.empty(B, R, C, dtype=torch.int8, device=self.dev)
 
-        def compensate_and_cast(Wp):
+        def run(Wp):
             T = ops.gemm(torch.empty_like(dX), dX, U, transB=True, mask=_lib.MASK_STRICT_UPPER)
             P = ops.gemm(torch.empty_like(dX), T, U, beta=float(alpha))
             ops.compensate(_lib.METHOD_GPTAQ, Wp, U, params.scale, params.zero, colgroup,
@@ -148,25 +155,8 @@ class GPTAQ(_engine.StagingMixin):
                                            export_compressed_tensors)
             return nan, outs, cq
 
-        nan, outs, cq = compensate_and_cast(W)
-        flags = _engine.sync_check(info, nan, *params.statuses())
-        if any(i != 0 for i in flags[:B]):
-            _engine.retry_failed(H, U, flags[:B], damps)
-            params.status.zero_()
-            nan, outs, cq = compensate_and_cast(W0)
-            flags = _engine.sync_check(info, nan, *params.statuses())
-            flags[:B] = [0] * B
-        if any(f != 0 for f in flags[B + 1:]):
-            raise RuntimeError("WeightQuantizer.find_params: non-positive scale")
-        if flags[B] != 0:
-            raise ValueError("NaN in weights")
-        if dynamic:
-            params.bind_dynamic()
-        if export_compressed_tensors and dynamic and actorder:
-            raise AssertionError("Scales in the same quantization group should be the same.")
-        _engine.finish(self.layers, outs, cq, params, q0.bits, groupsize, C,
-                       export_compressed_tensors, R)
-        self._last_damps = damps
+        return _engine.Pending(self.layers, B, H, U, info, damps, params, run, W, q0.bits,
+                               groupsize, C, R, export_compressed_tensors, dynamic, actorder)
 
     def free(self):
         self._H = None

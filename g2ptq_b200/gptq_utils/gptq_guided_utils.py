@@ -70,6 +70,14 @@ class GPTQGuided(GPTQ):
                     static_groups=False, export_compressed_tensors=False, backend="torch",
                     graph=False):
         """gptq_guided_utils.py:83-211."""
+        pending = self._fq_launch(blocksize=blocksize, percdamp=percdamp, groupsize=groupsize,
+                                  actorder=actorder, static_groups=static_groups,
+                                  export_compressed_tensors=export_compressed_tensors)
+        self._last_damps = pending.finish()
+
+    def _fq_launch(self, blocksize=128, percdamp=0.01, groupsize=-1, actorder=False,
+                   static_groups=False, export_compressed_tensors=False, backend="torch",
+                   graph=False):
         B, R, C, G = self.num_layers, self.rows, self.columns, self.num_groups
         rps = R // G
         nl = B * G
@@ -93,10 +101,9 @@ class GPTQGuided(GPTQ):
             H = ops.permute_sym(H, perm)
         U, info, damps = _engine.factor_with_retry(H, percdamp)
         colgroup = params.colgroup(perm, static_groups, self.dev)
-        W0 = W_sub.clone()
         codes = torch.empty(nl, rps, C, dtype=torch.int8, device=self.dev)
 
-        def compensate_and_cast(Wp):
+        def run(Wp):
             ops.compensate(_lib.METHOD_GPTQ, Wp, U, params.scale, params.zero, colgroup,
                            dynamic, groupsize, q0.bits, q0.sym, blocksize, codes,
                            status=params.status, precision=_engine.PRECISION)
@@ -109,23 +116,8 @@ class GPTQGuided(GPTQ):
                                            export_compressed_tensors)
             return nan, outs, cq
 
-        nan, outs, cq = compensate_and_cast(W0.clone())
-        flags = _engine.sync_check(info, nan, *params.statuses())
-        if any(i != 0 for i in flags[:nl]):
-            _engine.retry_failed(H, U, flags[:nl], damps)
-            params.status.zero_()
-            nan, outs, cq = compensate_and_cast(W0.clone())
-            flags = _engine.sync_check(info, nan, *params.statuses())
-            flags[:nl] = [0] * nl
-        if any(f != 0 for f in flags[nl + 1:]):
-            raise RuntimeError("WeightQuantizer.find_params: non-positive scale")
-        if flags[nl] != 0:
-            raise ValueError("NaN in weights")
-        if dynamic:
-            params.bind_dynamic()
-        _engine.finish(self.layers, outs, cq, params, q0.bits, groupsize, C,
-                       export_compressed_tensors, R)
-        self._last_damps = damps
+        return _engine.Pending(self.layers, nl, H, U, info, damps, params, run, W_sub, q0.bits,
+                               groupsize, C, R, export_compressed_tensors, dynamic, actorder)
 
     def free(self):
         self._H = None

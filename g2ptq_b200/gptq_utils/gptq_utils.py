@@ -94,34 +94,40 @@ class GPTQ(_engine.StagingMixin):
                     static_groups=False, export_compressed_tensors=False, backend="torch",
                     graph=False):
         """gptq_utils.py:234-353.  ``backend`` and ``graph`` are accepted and ignored."""
+        pending = self._fq_launch(blocksize=blocksize, percdamp=percdamp, groupsize=groupsize,
+                                  actorder=actorder, static_groups=static_groups,
+                                  export_compressed_tensors=export_compressed_tensors)
+        self._last_damps = pending.finish()
+
+    def _fq_launch(self, blocksize=128, percdamp=0.01, groupsize=-1, actorder=False,
+                   static_groups=False, export_compressed_tensors=False, backend="torch",
+                   graph=False):
+        """Enqueue the whole of fasterquant on the current stream (no host sync)."""
         B, R, C = self.num_layers, self.rows, self.columns
         q0 = self.quantizer[0]
         hclip = q0.hclip
         with self._maybe_onload_hessian():
             H = self.H
             self.H = None
-            H_diag = torch.diagonal(H, dim1=-2, dim2=-1).clone() if hclip else None
-            W = torch.stack([l.weight.data for l in self.layers]).float().contiguous()
-            params = _engine.ParamSet(self.quantizer, B * R, C, groupsize, self.dev)
-            dynamic = not (groupsize == -1 or static_groups)
-            if not dynamic:
-                params.init_static(W.view(B * R, C), H_diag)
-            ops.prepare_hessian(H, W)
-            perm = invperm = None
-            if actorder:
-                perm, invperm = _engine.act_order_perm(ops.mean_diag(H))
-                W = ops.permute_cols(W, perm)
-                H = ops.permute_sym(H, perm)
-            if H_diag is not None and actorder:
-                H_diag = H_diag[:, perm].contiguous()
-            if hclip and dynamic:
-                raise NotImplementedError("g2ptq_b200: --w_hclip needs the clip search")
-            U, info, damps = _engine.factor_with_retry(H, percdamp)
+        H_diag = torch.diagonal(H, dim1=-2, dim2=-1).clone() if hclip else None
+        W = torch.stack([l.weight.data for l in self.layers]).float().contiguous()
+        params = _engine.ParamSet(self.quantizer, B * R, C, groupsize, self.dev)
+        dynamic = not (groupsize == -1 or static_groups)
+        if not dynamic:
+            params.init_static(W.view(B * R, C), H_diag)
+        if hclip and dynamic:
+            raise NotImplementedError("g2ptq_b200: --w_hclip needs the clip search")
+        ops.prepare_hessian(H, W)
+        perm = None
+        if actorder:
+            perm, _ = _engine.act_order_perm(ops.mean_diag(H))
+            W = ops.permute_cols(W, perm)
+            H = ops.permute_sym(H, perm)
+        U, info, damps = _engine.factor_with_retry(H, percdamp)
         colgroup = params.colgroup(perm, static_groups, self.dev)
-        W0 = W.clone()
         codes = torch.empty(B, R, C, dtype=torch.int8, device=self.dev)
 
-        def compensate_and_cast(Wp):
+        def run(Wp):
             ops.compensate(_lib.METHOD_GPTQ, Wp, U, params.scale, params.zero, colgroup, dynamic,
                            groupsize, q0.bits, q0.sym, blocksize, codes, status=params.status,
                            precision=_engine.PRECISION)
@@ -133,26 +139,8 @@ class GPTQ(_engine.StagingMixin):
                                            export_compressed_tensors)
             return nan, outs, cq
 
-        nan, outs, cq = compensate_and_cast(W)
-        flags = _engine.sync_check(info, nan, *params.statuses())
-        info_list = flags[:B]
-        if any(i != 0 for i in info_list):
-            _engine.retry_failed(H, U, info_list, damps)
-            params.status.zero_()
-            nan, outs, cq = compensate_and_cast(W0)
-            flags = _engine.sync_check(info, nan, *params.statuses())
-            flags[:B] = [0] * B
-        if any(f != 0 for f in flags[B + 1:]):
-            raise RuntimeError("WeightQuantizer.find_params: non-positive scale")
-        if flags[B] != 0:
-            raise ValueError("NaN in weights")
-        if dynamic:
-            params.bind_dynamic()
-        if export_compressed_tensors and dynamic and actorder:
-            raise AssertionError("Scales in the same quantization group should be the same.")
-        _engine.finish(self.layers, outs, cq, params, q0.bits, groupsize, C,
-                       export_compressed_tensors, R)
-        self._last_damps = damps
+        return _engine.Pending(self.layers, B, H, U, info, damps, params, run, W, q0.bits,
+                               groupsize, C, R, export_compressed_tensors, dynamic, actorder)
 
     def free(self):
         self._H = None
@@ -180,6 +168,12 @@ def _onload(owner, names):
                 owner._flush_all()
                 v = getattr(owner, n)
             setattr(owner, n, v.to("cpu"))
+
+
+def fasterquant_all(gptqs, **kwargs):
+    """Run ``fasterquant(**kwargs)`` of several objects with their device work
+    overlapped on a small stream pool (same results as calling them in turn)."""
+    _engine.fasterquant_all(gptqs, **kwargs)
 
 
 def reduce_to_target_rank(gptqs, gptq2rank):
