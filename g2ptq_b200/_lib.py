@@ -20,6 +20,7 @@ G2Q_ERR_UNSUPPORTED = -3
 G2Q_ERR_NONFINITE = -4
 G2Q_ERR_TIMEOUT = -5
 G2Q_ERR_BAD_SCALE = -6
+G2Q_ERR_SCRATCH_LIMIT = -7
 
 DTYPE_BF16, DTYPE_F32, DTYPE_F16 = 0, 1, 2
 METHOD_GPTQ, METHOD_G2PTQ, METHOD_GPTAQ = 0, 1, 2
@@ -62,6 +63,9 @@ SIGNATURES = {
     "g2q_trust_region_beta": [P, P, P, P, P, P, I64, I64, I64, F32, P],
     "g2q_diag_of_utu": [P, P, I64, I64, P],
     "g2q_scale_rows": [P, P, I64, I64, I64, P],
+    "g2q_gram_update_noalloc": [P, I64, I64, I64, P, I32, I64, P, I32, I64, P, I64, I64, I32, F32,
+                                F32, P],
+    "g2q_gram_static_scratch_bytes": [],
 }
 _RESTYPES = {
     "g2q_launch_count": ctypes.c_int64,
@@ -69,6 +73,7 @@ _RESTYPES = {
     "g2q_gram_workspace_bytes": SZ,
     "g2q_chol_workspace_bytes": SZ,
     "g2q_compensate_workspace_bytes": SZ,
+    "g2q_gram_static_scratch_bytes": SZ,
 }
 
 _lib = None

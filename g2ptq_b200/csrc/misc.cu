@@ -265,6 +265,7 @@ extern "C" const char* g2q_status_string(int s) {
     case G2Q_ERR_NONFINITE: return "non-finite value";
     case G2Q_ERR_TIMEOUT: return "device wait timed out";
     case G2Q_ERR_BAD_SCALE: return "non-positive quantization scale";
+    case G2Q_ERR_SCRATCH_LIMIT: return "request exceeds the library-owned static scratch";
   }
   return s > 0 ? "non-positive Cholesky pivot" : "unknown status";
 }

@@ -34,6 +34,9 @@ extern "C" {
 #define G2Q_ERR_NONFINITE (-4)
 #define G2Q_ERR_TIMEOUT (-5)
 #define G2Q_ERR_BAD_SCALE (-6)
+/* the request needs more scratch than the library-owned array of
+ * g2q_gram_update_noalloc holds */
+#define G2Q_ERR_SCRATCH_LIMIT (-7)
 
 /* element types of activation inputs */
 #define G2Q_DTYPE_BF16 0
@@ -93,6 +96,26 @@ int g2q_gram_update(float* D, int64_t ldd, int64_t M, int64_t N,
                     int64_t T, int symmetric, float alpha, float beta, int precision,
                     void* workspace, size_t workspace_bytes, void* stream);
 size_t g2q_gram_workspace_bytes(int64_t M, int64_t N, int64_t T, int precision);
+
+/* g2q_gram_update at precision 1 (tensor cores) without caller-provided
+ * scratch: the bf16 splits of FP32 or row-scaled operands go to a file-scope
+ * device array of G2Q_GRAM_STATIC_SCRATCH_BYTES (40 MiB) owned by the library,
+ * so neither the caller nor the call allocates device memory.  Requests with
+ * g2q_gram_workspace_bytes(M, N, T, 1) above that size return
+ * G2Q_ERR_SCRATCH_LIMIT (e.g. T = 1024 tokens at C = 4096 fits; split longer
+ * token runs into several calls with alpha = 1 after the first).  BF16 inputs
+ * without row scale use no scratch.  The first call on a device looks the
+ * array up (set-up; make it before any stream capture).  One array per
+ * device: calls that overlap in time (several streams or host threads) race
+ * on it; calls on one stream are safe.  No counterpart in the reference,
+ * whose add_batch products allocate through torch. */
+#define G2Q_GRAM_STATIC_SCRATCH_BYTES (40u << 20)
+int g2q_gram_update_noalloc(float* D, int64_t ldd, int64_t M, int64_t N,
+                            const void* A, int a_dtype, int64_t lda,
+                            const void* B, int b_dtype, int64_t ldb,
+                            const float* row_scale, int64_t scale_stride,
+                            int64_t T, int symmetric, float alpha, float beta, void* stream);
+size_t g2q_gram_static_scratch_bytes(void);
 
 /* Adds sum_t x[t, c]^2 * scale to acc[c] after acc *= keep: the running mean
  * of squared activations kept by G2PTQ/GPTQGuided.add_batch
