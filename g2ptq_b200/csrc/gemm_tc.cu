@@ -116,10 +116,10 @@ __device__ __forceinline__ uint64_t desc_mn_sw128(uint32_t saddr) {
   return d;
 }
 
-// kind::f16 instruction descriptor: bf16 x bf16 -> f32, both MN-major, M=128, N=BN.
-__host__ __device__ constexpr uint32_t idesc_bf16_mn() {
+// kind::f16 instruction descriptor: bf16 x bf16 -> f32, both MN-major, M=128, N=n.
+__host__ __device__ constexpr uint32_t idesc_bf16_mn(int n) {
   return (1u << 4) | (1u << 7) | (1u << 10) | (1u << 15) | (1u << 16) |
-         ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+         ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 }
 
 __device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
@@ -166,14 +166,23 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 // the epilogue reads TMEM directly, and a single pipeline stage (up to three for
 // one-term operands) so that two or three CTAs share an SM and overlap one
 // CTA's epilogue with another's loads and MMAs.
-template <int NA, int NB, bool SMALL = false>
+// WIDE: 128 x 256 output tiles (N = 256 MMAs) for one-term long-K products.
+// A k-block then carries 512 tensor cycles of work, enough to hide the
+// full/empty barrier round trip that caps 128 x 128 k-blocks near half rate,
+// and each SM reads 48 KB per k-block instead of 64 KB for the same work.
+// Eight epilogue warps (two per TMEM lane quarter) drain the 256 columns.
+template <int NA, int NB, bool SMALL = false, bool WIDE = false>
 struct Cfg {
-  static constexpr int STAGE_BYTES = (NA + NB) * TILE_BYTES;
+  static constexpr int BN_T = WIDE ? 256 : BN;
+  static constexpr int B_BYTES = (BN_T / 64) * CHUNK_BYTES;  // one B term of a stage
+  static constexpr int STAGE_BYTES = NA * TILE_BYTES + NB * B_BYTES;
   static constexpr int STAGES =
       SMALL ? ((NA + NB) == 2 ? 3 : 1) : (192 * 1024) / STAGE_BYTES;
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
   static constexpr int MIN_BLOCKS = SMALL ? ((NA + NB) >= 6 ? 2 : 3) : 1;
-  static constexpr int ACC_COLS = SMALL ? BN : 2 * BN;
+  static constexpr int EPI_WARPS = WIDE ? 8 : 4;
+  static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+  static constexpr int ACC_COLS = SMALL ? BN : 2 * BN_T;
   static constexpr int ORDER = (NA > NB ? NA : NB) - 1;  // products a_i b_j with i + j <= ORDER
   static constexpr int PRODUCTS = (NA == 3 && NB == 3) ? 6 : (NA + NB - 1);
   // K blocks per TMEM accumulation group: 16 MMAs for one product, 24 otherwise
@@ -244,18 +253,66 @@ __device__ __forceinline__ bool decode_tile(long long id, int Tm, int Tn, bool s
   return false;
 }
 
-template <int NA, int NB, bool SMALL>
-__global__ void __launch_bounds__(192, (Cfg<NA, NB, SMALL>::MIN_BLOCKS))
+// Symmetric outputs with 128 x 256 tiles: tile (mt, nt) holds upper-triangle
+// elements when mt * 128 <= nt * 256 + 255, i.e. nt >= mt / 2.  Tile rows are
+// walked in groups of GROUP_M as above; inside a group the columns where only
+// part of the group's rows are needed come first.
+__host__ __device__ __forceinline__ long long wide_sym_group_count(int r0, int g, int Tn) {
+  long long c = 0;
+  for (int i = 0; i < g; ++i) {
+    const int lo = (r0 + i) / 2;
+    if (lo < Tn) c += Tn - lo;
+  }
+  return c;
+}
+
+__device__ __forceinline__ bool decode_tile_wide_sym(long long id, int Tm, int Tn, int& mt,
+                                                     int& nt) {
+  for (int r0 = 0; r0 < Tm; r0 += GROUP_M) {
+    const int g = (Tm - r0) < GROUP_M ? (Tm - r0) : GROUP_M;
+    const long long count = wide_sym_group_count(r0, g, Tn);
+    if (id < count) {
+      int n = r0 / 2;
+      while (true) {
+        const int rows = (2 * n + 2 - r0) < g ? (2 * n + 2 - r0) : g;
+        if (rows >= g) break;
+        if (id < rows) {
+          nt = n;
+          mt = r0 + (int)id;
+          return true;
+        }
+        id -= rows;
+        ++n;
+      }
+      nt = n + (int)(id / g);
+      mt = r0 + (int)(id % g);
+      return true;
+    }
+    id -= count;
+  }
+  return false;
+}
+
+template <int NA, int NB, bool SMALL, bool WIDE>
+__global__ void __launch_bounds__((Cfg<NA, NB, SMALL, WIDE>::THREADS),
+                                  (Cfg<NA, NB, SMALL, WIDE>::MIN_BLOCKS))
     tc_gemm_kernel(const __grid_constant__ CUtensorMap ma0, const __grid_constant__ CUtensorMap ma1,
                    const __grid_constant__ CUtensorMap ma2, const __grid_constant__ CUtensorMap mb0,
                    const __grid_constant__ CUtensorMap mb1, const __grid_constant__ CUtensorMap mb2,
                    Params p) {
-  using K = Cfg<NA, NB, SMALL>;
+  using K = Cfg<NA, NB, SMALL, WIDE>;
+  constexpr int BN_T = K::BN_T;
   int mt = blockIdx.y, nt = blockIdx.x;
   const long long bz = blockIdx.z;
-  if (p.raster && !decode_tile(blockIdx.x, p.tiles_m, p.tiles_n, p.symmetric, mt, nt)) return;
-  if (p.symmetric && nt < mt) return;  // tile holds no element of the upper triangle
-  if (p.lower && nt > mt) return;      // tile holds no element of the lower triangle
+  if (p.raster) {
+    const bool found = (WIDE && p.symmetric)
+                           ? decode_tile_wide_sym(blockIdx.x, p.tiles_m, p.tiles_n, mt, nt)
+                           : decode_tile(blockIdx.x, p.tiles_m, p.tiles_n, p.symmetric, mt, nt);
+    if (!found) return;
+  }
+  // tiles holding no element of the upper (symmetric) / lower triangle
+  if (p.symmetric && (long long)nt * BN_T + BN_T - 1 < (long long)mt * BM) return;
+  if (p.lower && (long long)nt * BN_T > (long long)mt * BM + BM - 1) return;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -280,7 +337,7 @@ __global__ void __launch_bounds__(192, (Cfg<NA, NB, SMALL>::MIN_BLOCKS))
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(accf0 + 8 * b, 1);
-      mbar_init(acce0 + 8 * b, 128);
+      mbar_init(acce0 + 8 * b, 32 * K::EPI_WARPS);
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -296,7 +353,7 @@ __global__ void __launch_bounds__(192, (Cfg<NA, NB, SMALL>::MIN_BLOCKS))
   __syncthreads();
   fence_after();
   const uint32_t tmem = *tmem_holder;
-  const int m0 = mt * BM, n0 = nt * BN;
+  const int m0 = mt * BM, n0 = nt * BN_T;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -320,21 +377,22 @@ __global__ void __launch_bounds__(192, (Cfg<NA, NB, SMALL>::MIN_BLOCKS))
 #pragma unroll
         for (int j = 0; j < NB; ++j) {
           const CUtensorMap* m = j == 0 ? &mb0 : (j == 1 ? &mb1 : &mb2);
-          tma_load_2d(sb + j * TILE_BYTES, m, xb, yb, fb);
-          tma_load_2d(sb + j * TILE_BYTES + CHUNK_BYTES, m, xb + 64, yb, fb);
+#pragma unroll
+          for (int c = 0; c < BN_T / 64; ++c)
+            tma_load_2d(sb + j * K::B_BYTES + c * CHUNK_BYTES, m, xb + 64 * c, yb, fb);
         }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16_mn();
+      constexpr uint32_t idesc = idesc_bf16_mn(BN_T);
       int kb = 0;
       for (int g = 0; g < ngroups; ++g) {
         const int buf = g & 1;
         const uint32_t use_ph = (uint32_t)((g >> 1) & 1);
         if (!mbar_wait(acce0 + 8 * buf, use_ph ^ 1, abort_flag, p.status)) break;
         fence_after();
-        const uint32_t acc_t = tmem + (uint32_t)(buf * BN);
+        const uint32_t acc_t = tmem + (uint32_t)(buf * BN_T);
         const int kend = (kb + promote_kb < p.num_kb) ? kb + promote_kb : p.num_kb;
         const int kstart = kb;
         bool ok = true;
@@ -360,7 +418,7 @@ __global__ void __launch_bounds__(192, (Cfg<NA, NB, SMALL>::MIN_BLOCKS))
                 const int j = o - i;
                 if (j < 0 || j >= NB) continue;
                 umma_bf16(acc_t, desc_mn_sw128(sa + i * TILE_BYTES + off),
-                          desc_mn_sw128(sb + j * TILE_BYTES + off), idesc,
+                          desc_mn_sw128(sb + j * K::B_BYTES + off), idesc,
                           (o == 0) ? acc0 : 1u);
               }
             }
@@ -405,8 +463,11 @@ __global__ void __launch_bounds__(192, (Cfg<NA, NB, SMALL>::MIN_BLOCKS))
       mbar_arrive(acce0);
     }
   } else {
-    // epilogue warps 2..5, long K: drain each accumulator buffer into registers
+    // epilogue warps, long K: drain each accumulator buffer into registers.
+    // Warp w reads TMEM lanes 32 (w % 4) .. + 31; with eight warps the second
+    // four take the upper 128 columns.
     const int q = warp & 3;
+    const int half = WIDE ? (warp - 2) / 4 : 0;
     const int row = q * 32 + lane;
     const long long gm = m0 + row;
     float acc[BN];
@@ -418,7 +479,8 @@ __global__ void __launch_bounds__(192, (Cfg<NA, NB, SMALL>::MIN_BLOCKS))
       const uint32_t use_ph = (uint32_t)((g >> 1) & 1);
       if (ok) ok = mbar_wait(accf0 + 8 * buf, use_ph, abort_flag, p.status);
       fence_after();
-      const uint32_t base = tmem + (uint32_t)(buf * BN) + ((uint32_t)(q * 32) << 16);
+      const uint32_t base =
+          tmem + (uint32_t)(buf * BN_T + half * BN) + ((uint32_t)(q * 32) << 16);
 #pragma unroll
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
@@ -434,7 +496,7 @@ __global__ void __launch_bounds__(192, (Cfg<NA, NB, SMALL>::MIN_BLOCKS))
     if (ok && gm < p.M) {
 #pragma unroll
       for (int j4 = 0; j4 < BN / 4; ++j4) {
-        const long long gn = n0 + 4 * j4;
+        const long long gn = n0 + half * BN + 4 * j4;
         float v[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) v[u] = p.beta * acc[4 * j4 + u];
@@ -491,14 +553,14 @@ struct Maps {
   CUtensorMap a[3], b[3];
 };
 
-template <int NA, int NB, bool SMALL>
+template <int NA, int NB, bool SMALL, bool WIDE = false>
 static int launch(const Maps& m, const Params& p, long long batch, cudaStream_t st) {
-  using K = Cfg<NA, NB, SMALL>;
+  using K = Cfg<NA, NB, SMALL, WIDE>;
   static int attr_done[64] = {0};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return G2Q_ERR_CUDA;
   if (dev >= 64 || !attr_done[dev]) {
-    if (cudaFuncSetAttribute(tc_gemm_kernel<NA, NB, SMALL>,
+    if (cudaFuncSetAttribute(tc_gemm_kernel<NA, NB, SMALL, WIDE>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, K::SMEM) != cudaSuccess)
       return G2Q_ERR_CUDA;
     if (dev < 64) attr_done[dev] = 1;
@@ -506,18 +568,26 @@ static int launch(const Maps& m, const Params& p, long long batch, cudaStream_t 
   Params q = p;
   q.promote_kb = K::PROMOTE_KB;
   q.tiles_m = cdiv(p.M, BM);
-  q.tiles_n = cdiv(p.N, BN);
+  q.tiles_n = cdiv(p.N, K::BN_T);
   dim3 grid(q.tiles_n, q.tiles_m, (unsigned)batch);
   if (q.raster) {
     const long long tm = q.tiles_m, tn = q.tiles_n;
-    const long long n = q.symmetric ? tm * (tm + 1) / 2 : tm * tn;
-    if (q.symmetric && tm != tn) return G2Q_ERR_INVALID_ARG;
+    long long n = q.symmetric ? tm * (tm + 1) / 2 : tm * tn;
+    if (WIDE && q.symmetric) {
+      if (p.M != p.N) return G2Q_ERR_INVALID_ARG;
+      n = 0;
+      for (int r0 = 0; r0 < q.tiles_m; r0 += GROUP_M)
+        n += wide_sym_group_count(r0, (q.tiles_m - r0) < GROUP_M ? (q.tiles_m - r0) : GROUP_M,
+                                  q.tiles_n);
+    } else if (q.symmetric && tm != tn) {
+      return G2Q_ERR_INVALID_ARG;
+    }
     if (n > 0x7fffffffLL) return G2Q_ERR_INVALID_ARG;
     grid = dim3((unsigned)n, 1, (unsigned)batch);
   }
   if (grid.y > 65535u || grid.z > 65535u) return G2Q_ERR_INVALID_ARG;
-  tc_gemm_kernel<NA, NB, SMALL><<<grid, 192, K::SMEM, st>>>(m.a[0], m.a[1], m.a[2], m.b[0],
-                                                             m.b[1], m.b[2], q);
+  tc_gemm_kernel<NA, NB, SMALL, WIDE><<<grid, K::THREADS, K::SMEM, st>>>(
+      m.a[0], m.a[1], m.a[2], m.b[0], m.b[1], m.b[2], q);
   G2Q_CHECK_LAUNCH();
   return G2Q_OK;
 }
@@ -531,7 +601,7 @@ static int dispatch(int na, int nb, Maps& m, const Params& p, long long batch,
     if (na == 2 && nb == 2) return launch<2, 2, true>(m, p, batch, st);
     if (na == 3 && nb == 3) return launch<3, 3, true>(m, p, batch, st);
   }
-  if (na == 1 && nb == 1) return launch<1, 1, false>(m, p, batch, st);
+  if (na == 1 && nb == 1) return launch<1, 1, false, true>(m, p, batch, st);
   if (na == 1 && nb == 2) return launch<1, 2, false>(m, p, batch, st);
   if (na == 2 && nb == 1) return launch<2, 1, false>(m, p, batch, st);
   if (na == 2 && nb == 2) return launch<2, 2, false>(m, p, batch, st);

@@ -27,7 +27,7 @@ def rel_fro(a, b):
 
 
 @pytest.mark.parametrize("T,C", [(2048, 512), (1000, 200), (4096, 1376), (777, 4096),
-                                 (16384, 4096)])
+                                 (16384, 4096), (300, 2200), (1024, 14336)])
 def test_tc_gram_bf16_symmetric(T, C):
     g = torch.Generator(device=DEV).manual_seed(T + C)
     X = torch.randn(T, C, device=DEV, generator=g)
@@ -40,6 +40,21 @@ def test_tc_gram_bf16_symmetric(T, C):
     ref = 0.5 * D0.double() + (2.0 / 7) * (X.double().T @ X.double())
     assert rel_fro(D, ref) < 1e-5
     assert torch.equal(D, D.T)
+
+
+@pytest.mark.parametrize("T,M,N", [(1000, 200, 328), (2048, 1376, 4096), (640, 4096, 136)])
+def test_tc_gram_bf16_cross(T, M, N):
+    """Non-symmetric BF16 products D <- a D + b Y^T X (one-term operands)."""
+    g = torch.Generator(device=DEV).manual_seed(T + M + N)
+    Y = torch.randn(T, M, device=DEV, generator=g).to(torch.bfloat16)
+    X = torch.randn(T, N, device=DEV, generator=g)
+    X[:, 1] *= 30
+    X = X.to(torch.bfloat16)
+    D0 = torch.randn(M, N, device=DEV, generator=g)
+    D = D0.clone()
+    ops.gram_update(D, Y, X, alpha=0.25, beta=1.0 / T, symmetric=False, precision=1)
+    ref = 0.25 * D0.double() + (1.0 / T) * (Y.double().T @ X.double())
+    assert rel_fro(D, ref) < 1e-5
 
 
 @pytest.mark.parametrize("sym,scaled", [(True, False), (True, True), (False, False)])
