@@ -54,9 +54,10 @@ struct Params {
   float alpha, beta;
   int symmetric;
   int lower;       // write only the lower triangle (m >= n); skip tiles above it
-  int promote_kb;
+  int promote_kb;  // K blocks accumulated in TMEM before the epilogue drains them
   int raster;      // 1: 1-D grid over the needed tiles in groups of GROUP_M tile rows
-  int tiles_m, tiles_n;  // K blocks accumulated in TMEM before the epilogue drains them
+  int tiles_m, tiles_n;
+  int red;         // short-K epilogue adds beta * acc into D with TMA reduce-add (alpha == 1)
   int* status;
 };
 
@@ -102,6 +103,30 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(mbar)
       : "memory");
+}
+
+// D[z][y .. y+31][x .. x+31] += the 32 x 32 fp32 box at smem (128-byte swizzled
+// rows), performed by the TMA unit in L2: the SM never reads D.
+__device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* map, uint32_t src, int x, int y,
+                                                  int z) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group"
+      " [%0, {%1, %2, %3}], [%4];" ::"l"(reinterpret_cast<uint64_t>(map)),
+      "r"(x), "r"(y), "r"(z), "r"(src)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// wait until at most one committed bulk group still reads shared memory
+__device__ __forceinline__ void bulk_wait_read_1() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+__device__ __forceinline__ void fence_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 // Shared-memory matrix descriptor of an MN-major, 128-byte-swizzled operand:
@@ -299,7 +324,7 @@ __global__ void __launch_bounds__((Cfg<NA, NB, SMALL, WIDE>::THREADS),
     tc_gemm_kernel(const __grid_constant__ CUtensorMap ma0, const __grid_constant__ CUtensorMap ma1,
                    const __grid_constant__ CUtensorMap ma2, const __grid_constant__ CUtensorMap mb0,
                    const __grid_constant__ CUtensorMap mb1, const __grid_constant__ CUtensorMap mb2,
-                   Params p) {
+                   const __grid_constant__ CUtensorMap md, Params p) {
   using K = Cfg<NA, NB, SMALL, WIDE>;
   constexpr int BN_T = K::BN_T;
   int mt = blockIdx.y, nt = blockIdx.x;
@@ -438,24 +463,69 @@ __global__ void __launch_bounds__((Cfg<NA, NB, SMALL, WIDE>::THREADS),
     if (ngroups > 0) ok = mbar_wait(accf0, 0, abort_flag, p.status);
     fence_after();
     float* Db = p.D + bz * p.d_bs;
-    const bool vec_ok = ((p.ldd & 3) == 0) && ((reinterpret_cast<uintptr_t>(Db) & 15) == 0);
+    if (p.red) {
+      // Every load has landed and every MMA has read its operands, so the stage
+      // buffers are free: each warp stages its 32 rows x 32 columns per chunk in
+      // two swizzled 4 KB buffers and the TMA unit adds them into D.
+      static_assert(K::STAGES * K::STAGE_BYTES >= 4 * 8192, "staging does not fit");
+      uint8_t* stg = smem + q * 8192;
 #pragma unroll 1
-    for (int c = 0; c < BN / 32; ++c) {
-      uint32_t r[32];
-      if (ngroups > 0) {
-        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32), r);
-      } else {
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        if (ngroups > 0) {
+          tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32), r);
+        } else {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) r[j] = 0u;
+          for (int j = 0; j < 32; ++j) r[j] = 0u;
+        }
+        if (c >= 2) {
+          if (lane == 0) bulk_wait_read_1();
+          __syncwarp();
+        }
+        float* buf = reinterpret_cast<float*>(stg + (c & 1) * 4096);
+#pragma unroll
+        for (int j4 = 0; j4 < 8; ++j4) {
+          const long long gn = n0 + c * 32 + 4 * j4;
+          float v[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            v[u] = p.beta * __uint_as_float(r[4 * j4 + u]);
+            if (p.lower && gn + u > gm) v[u] = 0.f;  // leave the upper triangle as it is
+          }
+          *reinterpret_cast<float4*>(buf + lane * 32 + ((j4 ^ (lane & 7)) << 2)) =
+              make_float4(v[0], v[1], v[2], v[3]);
+        }
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          // boxes starting inside D only; TMA clips the parts beyond M and N
+          if (ok && n0 + c * 32 < p.N && m0 + q * 32 < p.M)
+            tma_reduce_add_3d(&md, smem_u32(buf), n0 + c * 32, m0 + q * 32, (int)bz);
+          bulk_commit();
+        }
       }
-      if (!ok || gm >= p.M) continue;
+      if (lane == 0) bulk_wait_all();
+      __syncwarp();
+    } else {
+      const bool vec_ok = ((p.ldd & 3) == 0) && ((reinterpret_cast<uintptr_t>(Db) & 15) == 0);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        if (ngroups > 0) {
+          tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32), r);
+        } else {
 #pragma unroll
-      for (int j4 = 0; j4 < 8; ++j4) {
-        const long long gn = n0 + c * 32 + 4 * j4;
-        float v[4];
+          for (int j = 0; j < 32; ++j) r[j] = 0u;
+        }
+        if (!ok || gm >= p.M) continue;
 #pragma unroll
-        for (int u = 0; u < 4; ++u) v[u] = p.beta * __uint_as_float(r[4 * j4 + u]);
-        EPILOGUE_STORE4
+        for (int j4 = 0; j4 < 8; ++j4) {
+          const long long gn = n0 + c * 32 + 4 * j4;
+          float v[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) v[u] = p.beta * __uint_as_float(r[4 * j4 + u]);
+          EPILOGUE_STORE4
+        }
       }
     }
     if (ngroups > 0) {
@@ -551,7 +621,27 @@ static bool make_map(CUtensorMap* m, const void* base, long long inner, long lon
 
 struct Maps {
   CUtensorMap a[3], b[3];
+  CUtensorMap d;  // fp32 output for the reduce-add epilogue (Params::red)
 };
+
+// 3-D fp32 tensor [batch][M][N] (row stride ldd, batch stride d_bs elements),
+// 32 x 32 boxes with 128-byte swizzle: the target of the reduce-add epilogue.
+static bool make_map_out(CUtensorMap* m, float* D, long long N, long long M, long long batch,
+                         long long ldd, long long d_bs) {
+  auto enc = encode_fn();
+  if (!enc) return false;
+  if (batch <= 1) d_bs = M * ldd;
+  if ((reinterpret_cast<uintptr_t>(D) & 15) || ((ldd * 4) & 15) || ((d_bs * 4) & 15) || N <= 0 ||
+      M <= 0 || batch <= 0 || ldd < N || d_bs < M * ldd)
+    return false;
+  cuuint64_t dims[3] = {(cuuint64_t)N, (cuuint64_t)M, (cuuint64_t)batch};
+  cuuint64_t strides[2] = {(cuuint64_t)(ldd * 4), (cuuint64_t)(d_bs * 4)};
+  cuuint32_t box[3] = {32, 32, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, D, dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 
 template <int NA, int NB, bool SMALL, bool WIDE = false>
 static int launch(const Maps& m, const Params& p, long long batch, cudaStream_t st) {
@@ -586,8 +676,9 @@ static int launch(const Maps& m, const Params& p, long long batch, cudaStream_t 
     grid = dim3((unsigned)n, 1, (unsigned)batch);
   }
   if (grid.y > 65535u || grid.z > 65535u) return G2Q_ERR_INVALID_ARG;
+  if (!SMALL || q.symmetric || q.alpha != 1.f) q.red = 0;
   tc_gemm_kernel<NA, NB, SMALL, WIDE><<<grid, K::THREADS, K::SMEM, st>>>(
-      m.a[0], m.a[1], m.a[2], m.b[0], m.b[1], m.b[2], q);
+      m.a[0], m.a[1], m.a[2], m.b[0], m.b[1], m.b[2], m.d, q);
   G2Q_CHECK_LAUNCH();
   return G2Q_OK;
 }
@@ -716,7 +807,7 @@ int tc_gram(float* D, long long ldd, long long M, long long N, const void* A, in
     ldb_t = w;
     nb = 2;
   }
-  tc::Maps mp;
+  tc::Maps mp{};
   bool ok = tc::make_map(&mp.a[0], a_terms[0], M, T, lda_t) &&
             tc::make_map(&mp.b[0], b_terms[0], N, T, ldb_t);
   ok = ok && (na == 1 || tc::make_map(&mp.a[1], a_terms[1], M, T, lda_t));
@@ -745,7 +836,7 @@ int tc_trailing_update(float* W, long long C, long long rows, long long batch, l
                        cudaStream_t st) {
   if ((nc % tc::BK) || (i2 % 8) || (rows % 8) || (C % 8) || !tc::encode_fn())
     return G2Q_ERR_UNSUPPORTED;
-  tc::Maps mp;
+  tc::Maps mp{};
   bool ok = tc::make_map(&mp.a[0], err_hi, rows, batch * err_stride, rows) &&
             tc::make_map(&mp.a[1], err_lo, rows, batch * err_stride, rows) &&
             tc::make_map(&mp.b[0], u_hi, C, batch * C, C) &&
@@ -761,6 +852,7 @@ int tc_trailing_update(float* W, long long C, long long rows, long long batch, l
   p.alpha = 1.f; p.beta = -1.f;
   p.symmetric = 0;
   p.status = status;
+  p.red = tc::make_map_out(&mp.d, p.D, p.N, p.M, batch, p.ldd, p.d_bs) ? 1 : 0;
   return tc::dispatch(2, 2, mp, p, batch, st);
 }
 
@@ -811,7 +903,7 @@ int tc_update3(float* D, long long ldd, long long M, long long N, long long K,
                __nv_bfloat16* const* a3, long long lda, __nv_bfloat16* const* b3, long long ldb,
                int lower, float alpha, float beta, cudaStream_t st) {
   if (M <= 0 || N <= 0 || K <= 0 || !tc::encode_fn()) return G2Q_ERR_UNSUPPORTED;
-  tc::Maps mp;
+  tc::Maps mp{};
   bool ok = true;
   for (int i = 0; i < 3 && ok; ++i)
     ok = tc::make_map(&mp.a[i], a3[i], M, K, lda) && tc::make_map(&mp.b[i], b3[i], N, K, ldb);
@@ -822,6 +914,7 @@ int tc_update3(float* D, long long ldd, long long M, long long N, long long K,
   p.num_kb = (int)((K + tc::BK - 1) / tc::BK);
   p.alpha = alpha; p.beta = beta;
   p.lower = lower;
+  p.red = (alpha == 1.f && tc::make_map_out(&mp.d, D, N, M, 1, ldd, 0)) ? 1 : 0;
   return tc::dispatch(3, 3, mp, p, 1, st);
 }
 

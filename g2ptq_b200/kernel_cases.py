@@ -27,8 +27,10 @@ def _time(fn, warmup, reps):
     s = torch.cuda.Event(enable_timing=True)
     e = torch.cuda.Event(enable_timing=True)
     s.record()
+    torch.cuda.nvtx.range_push("timed")  # profilers can restrict a capture to these launches
     for _ in range(reps):
         fn()
+    torch.cuda.nvtx.range_pop()
     e.record()
     torch.cuda.synchronize()
     return s.elapsed_time(e) / reps
