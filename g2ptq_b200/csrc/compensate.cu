@@ -3,11 +3,9 @@
 //
 // Rows of W are independent in the compensation: every row walks the block's
 // columns in order, quantizes, and pushes its error onto the remaining
-// columns through the shared row U[c, c+1:].  One thread therefore owns one
-// row and keeps the block's 128 values of that row in registers; the block
-// of U (and of P for GPTAQ) sits in shared memory and every U[c][j] read is a
-// warp-wide broadcast.  The trailing update of the columns after the block is
-// a GEMM (gemm_simt.cu or gemm_tc.cu).
+// columns through the shared row U[c, c+1:].  The block of U (and of P for
+// GPTAQ) sits in shared memory; the trailing update of the columns after the
+// block is a GEMM (gemm_simt.cu or gemm_tc.cu).
 #include "gemm_simt.cuh"
 
 namespace g2q {
@@ -41,234 +39,188 @@ struct BlockParams {
   int dfact;       // G2PTQ distance factor (the traversal's blocksize)
 };
 
-constexpr int WIN = 32;           // columns held in registers at a time
-// Padded shared-memory row of a W / gh tile: rows stay 16-byte aligned, and the
-// 16-byte per-thread row accesses of a quarter warp cover all 32 banks.
-constexpr int LDS_ROW = BLK + 4;
+// Eight threads share a row and each keeps 16 of the block's columns in
+// registers.  At column i the owner of i quantizes it and broadcasts its error
+// to the other seven with a shuffle; every thread then applies that error to
+// its own columns after i.  The per-column chain is one quantization, one
+// shuffle and one update instead of a whole-row sweep per thread, and each
+// element still receives its updates in column order, as in the reference.
+// Errors are staged in shared memory and written out after the last column.
+constexpr int QT = 8;             // threads per row
+constexpr int SEG = BLK / QT;     // block columns per thread
+constexpr int USEG = SEG + 4;     // padded segment: a row's segments start on distinct banks
+constexpr int LDU = QT * USEG;    // shared-memory row of the U (and P) block
+constexpr int QROWS = 32;         // rows per CTA
+constexpr int LDE = BLK + 1;      // staged error row
 
-// Shared-memory layout (floats): U block, W tile, [gh tile | P block], codes.
-__host__ __device__ constexpr int smem_floats(int method) {
-  return BLK * BLK + BLK * LDS_ROW +
-         (method == G2Q_METHOD_G2PTQ ? BLK * LDS_ROW : 0) +
-         (method == G2Q_METHOD_GPTAQ ? BLK * BLK : 0);
+__host__ __device__ constexpr int block_smem_floats(int method) {
+  return BLK * LDU * (method == G2Q_METHOD_GPTAQ ? 2 : 1) +
+         QROWS * LDE * (method == G2Q_METHOD_G2PTQ ? 2 : 1);
 }
-constexpr int CODE_ROW = BLK + 4;
 
 template <int METHOD>
-__global__ void __launch_bounds__(128) block_kernel(BlockParams P) {
+__global__ void __launch_bounds__(QT * QROWS, 1) block_kernel(BlockParams P) {
   extern __shared__ __align__(16) float smem[];
-  float* Us = smem;                       // [BLK][BLK]
-  float* Ws = Us + BLK * BLK;             // [BLK rows][LDS_ROW]
-  float* Xs = Ws + BLK * LDS_ROW;         // G2PTQ gh tile [BLK][LDS_ROW] / GPTAQ P [BLK][BLK]
-  int8_t* Qs = reinterpret_cast<int8_t*>(smem + smem_floats(METHOD));  // [BLK][CODE_ROW]
-  int* cmap = reinterpret_cast<int*>(Qs + BLK * CODE_ROW);
+  float* Us = smem;              // [BLK][LDU], segment-padded
+  float* Ps = Us + BLK * LDU;    // GPTAQ P block, same layout
+  float* Es = smem + BLK * LDU * (METHOD == G2Q_METHOD_GPTAQ ? 2 : 1);  // [QROWS][LDE] errors
+  float* EAs = Es + QROWS * LDE;  // G2PTQ trailing-update errors
   const int b = blockIdx.y;
-  const int t = threadIdx.x;
-  const int lane = t & 31, warp = t >> 5;
-  const long long row0 = (long long)blockIdx.x * BLK;
-  const long long r = row0 + t;
+  const int tid = threadIdx.x;
+  const int t = tid & (QT - 1);
+  const int lane = tid & 31;
+  const int src0 = lane & ~(QT - 1);  // lane holding segment 0 of this row
+  const int rl = tid / QT;  // row within the CTA
+  const long long r = (long long)blockIdx.x * QROWS + rl;
   const int nc = P.ncols;
-  const long long nrows_here = (P.rows - row0) < BLK ? (P.rows - row0) : BLK;
+  const bool active = r < P.rows;
+  const long long rr = active ? r : 0;
 
   const float* hb = P.hinv + (long long)b * P.h_bs;
   const float* pb = (METHOD == G2Q_METHOD_GPTAQ) ? P.p + (long long)b * P.h_bs : nullptr;
-  // 16-byte loads with many in flight when the block is full width and aligned
-  const bool vec = (nc == BLK) && ((P.ldh & 3) == 0) && ((P.ldw & 3) == 0) &&
-                   (((uintptr_t)hb & 15) == 0) && (((uintptr_t)P.W & 15) == 0) &&
-                   (METHOD != G2Q_METHOD_G2PTQ ||
-                    (((P.ldz & 3) == 0) && (((uintptr_t)P.gh & 15) == 0))) &&
+  // 16-byte loads, many in flight, when the block is full width and aligned
+  const bool vec = (nc == BLK) && ((P.ldh & 3) == 0) && (((uintptr_t)hb & 15) == 0) &&
                    (METHOD != G2Q_METHOD_GPTAQ || (((uintptr_t)pb & 15) == 0));
   if (vec) {
 #pragma unroll 8
-    for (int q = t; q < BLK * BLK / 4; q += BLK) {
-      const int i = q >> 5, j4 = (q & 31) * 4;
-      *reinterpret_cast<float4*>(&Us[i * BLK + j4]) =
-          *reinterpret_cast<const float4*>(hb + i * P.ldh + j4);
+    for (int q = tid; q < BLK * BLK / 4; q += QT * QROWS) {
+      const int i = q / (BLK / 4), j = (q % (BLK / 4)) * 4;
+      const int o = i * LDU + (j / SEG) * USEG + (j % SEG);
+      *reinterpret_cast<float4*>(&Us[o]) = *reinterpret_cast<const float4*>(hb + i * P.ldh + j);
       if (METHOD == G2Q_METHOD_GPTAQ)
-        *reinterpret_cast<float4*>(&Xs[i * BLK + j4]) =
-            *reinterpret_cast<const float4*>(pb + i * P.ldh + j4);
-    }
-#pragma unroll 8
-    for (int q = t; q < BLK * BLK / 4; q += BLK) {
-      const int rr = q >> 5, c4 = (q & 31) * 4;
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f), gv4 = v;
-      if (rr < nrows_here) {
-        v = *reinterpret_cast<const float4*>(P.W + (long long)b * P.w_bs +
-                                             (row0 + rr) * P.ldw + c4);
-        if (METHOD == G2Q_METHOD_G2PTQ)
-          gv4 = *reinterpret_cast<const float4*>(P.gh + (long long)b * P.z_bs +
-                                                 (row0 + rr) * P.ldz + c4);
-      }
-      *reinterpret_cast<float4*>(&Ws[rr * LDS_ROW + c4]) = v;
-      if (METHOD == G2Q_METHOD_G2PTQ) *reinterpret_cast<float4*>(&Xs[rr * LDS_ROW + c4]) = gv4;
+        *reinterpret_cast<float4*>(&Ps[o]) =
+            *reinterpret_cast<const float4*>(pb + i * P.ldh + j);
     }
   } else {
-    for (int idx = t; idx < BLK * BLK; idx += BLK) {
-      const int i = idx >> 7, j = idx & (BLK - 1);
-      Us[idx] = (i < nc && j < nc) ? hb[i * P.ldh + j] : 0.f;
-      if (METHOD == G2Q_METHOD_GPTAQ) Xs[idx] = (i < nc && j < nc) ? pb[i * P.ldh + j] : 0.f;
-    }
-    // W (and gh) tiles: one warp per row, lanes along the row (coalesced)
-    for (int rr = warp; rr < BLK; rr += 4) {
-      const bool ok = rr < nrows_here;
-      const float* src = P.W + (long long)b * P.w_bs + (row0 + rr) * P.ldw;
-      const float* gsrc = (METHOD == G2Q_METHOD_G2PTQ)
-                              ? P.gh + (long long)b * P.z_bs + (row0 + rr) * P.ldz : nullptr;
-      for (int c = lane; c < BLK; c += 32) {
-        Ws[rr * LDS_ROW + c] = (ok && c < nc) ? src[c] : 0.f;
-        if (METHOD == G2Q_METHOD_G2PTQ) Xs[rr * LDS_ROW + c] = (ok && c < nc) ? gsrc[c] : 0.f;
-      }
+#pragma unroll 4
+    for (int idx = tid; idx < BLK * BLK; idx += QT * QROWS) {
+      const int i = idx / BLK, j = idx % BLK;
+      const int o = i * LDU + (j / SEG) * USEG + (j % SEG);
+      const bool in = i < nc && j < nc;
+      Us[o] = in ? hb[i * P.ldh + j] : 0.f;
+      if (METHOD == G2Q_METHOD_GPTAQ) Ps[o] = in ? pb[i * P.ldh + j] : 0.f;
     }
   }
-  cmap[t] = t < nc ? P.colmap[t] : 0;
+
+  // this thread's 32 columns of W (and of gh / z for G2PTQ) and their parameters
+  float wv[SEG], gv[SEG], xv[SEG], sv[SEG], zv[SEG];
+  float* wrow = P.W + (long long)b * P.w_bs + rr * P.ldw + t * SEG;
+  float* grow = (METHOD == G2Q_METHOD_G2PTQ)
+                    ? P.gh + (long long)b * P.z_bs + rr * P.ldz + t * SEG : nullptr;
+  const float* zrow = (METHOD == G2Q_METHOD_G2PTQ)
+                          ? P.z + (long long)b * P.z_bs + rr * P.ldz + t * SEG : nullptr;
+  const long long prow = ((long long)b * P.rows + rr) * P.param_ld;
+#pragma unroll
+  for (int k = 0; k < SEG; ++k) {
+    const int col = t * SEG + k;
+    const bool in = active && col < nc;
+    const int pc = in ? P.colmap[col] : 0;
+    wv[k] = in ? wrow[k] : 0.f;
+    sv[k] = in ? P.scale[prow + pc] : 1.f;
+    zv[k] = in ? P.zero[prow + pc] : 0.f;
+    gv[k] = (METHOD == G2Q_METHOD_G2PTQ && in) ? grow[k] : 0.f;
+    xv[k] = (METHOD == G2Q_METHOD_G2PTQ && in) ? zrow[k] : 0.f;
+  }
   __syncthreads();
 
-  const bool active = r < P.rows;
-  if (active) {
-    float* wsr = Ws + t * LDS_ROW;
-    float* gsr = Xs + t * LDS_ROW;  // G2PTQ only
-    int8_t* qsr = Qs + t * CODE_ROW;
-    const long long prow = ((long long)b * P.rows + r) * P.param_ld;
-    const float* zrow =
-        (METHOD == G2Q_METHOD_G2PTQ) ? P.z + (long long)b * P.z_bs + r * P.ldz : nullptr;
-    const float qlo = -(float)(P.maxq + 1), qhi = (float)P.maxq;
-
-    for (int w0 = 0; w0 < nc; w0 += WIN) {
-      float wv[WIN], gv[WIN], ev[WIN], xv[WIN];  // xv: GPTAQ pre-quant w / G2PTQ z
-      float sv[WIN], zv[WIN];  // the window's quantization parameters, loaded up front
+  uint32_t cw[SEG / 4];
 #pragma unroll
-      for (int k4 = 0; k4 < WIN; k4 += 4) {
-        const float4 a4 = *reinterpret_cast<const float4*>(&wsr[w0 + k4]);
-        wv[k4] = a4.x; wv[k4 + 1] = a4.y; wv[k4 + 2] = a4.z; wv[k4 + 3] = a4.w;
+  for (int k = 0; k < SEG / 4; ++k) cw[k] = 0u;
+  const float qlo = -(float)(P.maxq + 1), qhi = (float)P.maxq;
+
+#pragma unroll 1
+  for (int tw = 0; tw < QT; ++tw) {
+    if (tw * SEG >= nc) break;
+    const bool after = t >= tw;  // updates of columns j > k of segment tw
+    const bool later = t > tw;   // updates of columns j <= k (later segments only)
+#pragma unroll
+    for (int k = 0; k < SEG; ++k) {
+      const int i = tw * SEG + k;
+      if (i >= nc) break;
+      float e = 0.f, aux = 0.f;
+      if (t == tw) {
+        const float s = sv[k];
+        const float zz = zv[k];
+        const float d = Us[i * LDU + tw * USEG + k];
+        const float wc = wv[k];
+        float q = rintf(wc / s) + zz;
+        q = fminf(fmaxf(q, qlo), qhi);
+        const float qv = s * (q - zz);
         if (METHOD == G2Q_METHOD_G2PTQ) {
-          const float4 g4 = *reinterpret_cast<const float4*>(&gsr[w0 + k4]);
-          gv[k4] = g4.x; gv[k4 + 1] = g4.y; gv[k4 + 2] = g4.z; gv[k4 + 3] = g4.w;
+          e = (wc - qv - gv[k]) / d;
         } else {
-          gv[k4] = gv[k4 + 1] = gv[k4 + 2] = gv[k4 + 3] = 0.f;
+          e = (wc - qv) / d;
         }
+        aux = (METHOD == G2Q_METHOD_G2PTQ) ? xv[k] : wc;
+        wv[k] = qv;
+        cw[k / 4] |= ((uint32_t)(int)q & 0xffu) << (8 * (k % 4));
+        Es[rl * LDE + i] = e;
+        if (METHOD == G2Q_METHOD_G2PTQ)
+          EAs[rl * LDE + i] = e - xv[k] * (float)(P.dfact - 1 - i);
       }
+      e = __shfl_sync(0xffffffffu, e, src0 + tw);
+      if (METHOD != G2Q_METHOD_GPTQ) aux = __shfl_sync(0xffffffffu, aux, src0 + tw);
+      const float* urow = Us + i * LDU + t * USEG;
+      const float* prow_s = Ps + i * LDU + t * USEG;
 #pragma unroll
-      for (int k = 0; k < WIN; ++k) {
-        ev[k] = 0.f;
-        const bool in = w0 + k < nc;
-        const int pc = in ? cmap[w0 + k] : 0;
-        sv[k] = in ? P.scale[prow + pc] : 1.f;
-        zv[k] = in ? P.zero[prow + pc] : 0.f;
-        xv[k] = (METHOD == G2Q_METHOD_G2PTQ && in) ? zrow[w0 + k] : 0.f;
-      }
+      for (int j4 = 0; j4 < SEG; j4 += 4) {
+        const float4 u4 = *reinterpret_cast<const float4*>(urow + j4);
+        const float uu[4] = {u4.x, u4.y, u4.z, u4.w};
+        float pp[4] = {0.f, 0.f, 0.f, 0.f};
+        if (METHOD == G2Q_METHOD_GPTAQ) {
+          const float4 p4 = *reinterpret_cast<const float4*>(prow_s + j4);
+          pp[0] = p4.x; pp[1] = p4.y; pp[2] = p4.z; pp[3] = p4.w;
+        }
 #pragma unroll
-      for (int c = 0; c < WIN; ++c) {
-        const int cc = w0 + c;
-        if (cc < nc) {
-          const float s = sv[c];
-          const float zz = zv[c];
-          const float d = Us[cc * BLK + cc];
-          const float wc = wv[c];
-          float q = rintf(wc / s) + zz;
-          q = fminf(fmaxf(q, qlo), qhi);
-          const float qv = s * (q - zz);
-          float e;
-          if (METHOD == G2Q_METHOD_G2PTQ) {
-            e = (wc - qv - gv[c]) / d;
-          } else {
-            e = (wc - qv) / d;
-          }
-          if (METHOD == G2Q_METHOD_GPTAQ) xv[c] = wc;
-          ev[c] = e;
-          wv[c] = qv;
-          qsr[cc] = (int8_t)(int)q;
-          const float ea =
-              (METHOD == G2Q_METHOD_G2PTQ) ? e - xv[c] * (float)(P.dfact - 1 - cc) : e;
-          const long long co = (long long)cc;
-          if (P.err) P.err[(long long)b * P.e_bs + co * P.lde + r] = e;
-          if (P.erra) P.erra[(long long)b * P.ea_bs + co * P.ldea + r] = ea;
-          if (P.erra_hi) {
-            __nv_bfloat16 h, l;
-            split_bf16(ea, &h, &l);
-            P.erra_hi[(long long)b * P.ea_bs + co * P.ldea + r] = h;
-            P.erra_lo[(long long)b * P.ea_bs + co * P.ldea + r] = l;
-          }
-          // in-window update of columns c+1 .. WIN-1
-#pragma unroll
-          for (int j = c + 1; j < WIN; ++j) {
-            const float u = Us[cc * BLK + w0 + j];
+        for (int m = 0; m < 4; ++m) {
+          const int j = j4 + m;
+          if (j > k ? after : later) {
             if (METHOD == G2Q_METHOD_G2PTQ) {
-              wv[j] = fmaf(-e, u, wv[j] - gv[j]);
-              gv[j] = fmaf(-xv[c], u, gv[j]);
+              wv[j] = fmaf(-e, uu[m], wv[j] - gv[j]);
+              gv[j] = fmaf(-aux, uu[m], gv[j]);
             } else if (METHOD == G2Q_METHOD_GPTAQ) {
-              wv[j] = fmaf(Xs[cc * BLK + w0 + j], wc, fmaf(-e, u, wv[j]));
+              wv[j] = fmaf(pp[m], aux, fmaf(-e, uu[m], wv[j]));
             } else {
-              wv[j] = fmaf(-e, u, wv[j]);
+              wv[j] = fmaf(-e, uu[m], wv[j]);
             }
           }
         }
-      }
-#pragma unroll
-      for (int k4 = 0; k4 < WIN; k4 += 4) {
-        *reinterpret_cast<float4*>(&wsr[w0 + k4]) =
-            make_float4(wv[k4], wv[k4 + 1], wv[k4 + 2], wv[k4 + 3]);
-        if (METHOD == G2Q_METHOD_G2PTQ)
-          *reinterpret_cast<float4*>(&gsr[w0 + k4]) =
-              make_float4(gv[k4], gv[k4 + 1], gv[k4 + 2], gv[k4 + 3]);
-      }
-      // deferred update of the block columns after this window, applied in
-      // column order so each element sees the same sequence of operations
-      const int jend = (nc + 3) & ~3;
-      for (int j0 = w0 + WIN; j0 < jend; j0 += 4) {
-        float x4[4], g4[4] = {0.f, 0.f, 0.f, 0.f};
-        {
-          const float4 a4 = *reinterpret_cast<const float4*>(&wsr[j0]);
-          x4[0] = a4.x; x4[1] = a4.y; x4[2] = a4.z; x4[3] = a4.w;
-          if (METHOD == G2Q_METHOD_G2PTQ) {
-            const float4 b4 = *reinterpret_cast<const float4*>(&gsr[j0]);
-            g4[0] = b4.x; g4[1] = b4.y; g4[2] = b4.z; g4[3] = b4.w;
-          }
-        }
-#pragma unroll
-        for (int c = 0; c < WIN; ++c) {
-          const float4 u4 = *reinterpret_cast<const float4*>(&Us[(w0 + c) * BLK + j0]);
-          const float uu[4] = {u4.x, u4.y, u4.z, u4.w};
-          float pp[4] = {0.f, 0.f, 0.f, 0.f};
-          if (METHOD == G2Q_METHOD_GPTAQ) {
-            const float4 p4 = *reinterpret_cast<const float4*>(&Xs[(w0 + c) * BLK + j0]);
-            pp[0] = p4.x; pp[1] = p4.y; pp[2] = p4.z; pp[3] = p4.w;
-          }
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            if (METHOD == G2Q_METHOD_G2PTQ) {
-              x4[k] = fmaf(-ev[c], uu[k], x4[k] - g4[k]);
-              g4[k] = fmaf(-xv[c], uu[k], g4[k]);
-            } else if (METHOD == G2Q_METHOD_GPTAQ) {
-              x4[k] = fmaf(pp[k], xv[c], fmaf(-ev[c], uu[k], x4[k]));
-            } else {
-              x4[k] = fmaf(-ev[c], uu[k], x4[k]);
-            }
-          }
-        }
-        *reinterpret_cast<float4*>(&wsr[j0]) = make_float4(x4[0], x4[1], x4[2], x4[3]);
-        if (METHOD == G2Q_METHOD_G2PTQ)
-          *reinterpret_cast<float4*>(&gsr[j0]) = make_float4(g4[0], g4[1], g4[2], g4[3]);
       }
     }
   }
+
+  if (active) {
+    int8_t* qrow = P.codes ? P.codes + (long long)b * P.q_bs + r * P.ldq + t * SEG : nullptr;
+#pragma unroll
+    for (int k = 0; k < SEG; ++k) {
+      if (t * SEG + k >= nc) break;
+      wrow[k] = wv[k];
+      if (qrow) qrow[k] = (int8_t)((cw[k / 4] >> (8 * (k % 4))) & 0xffu);
+      if (METHOD == G2Q_METHOD_G2PTQ) grow[k] = gv[k];
+    }
+  }
+  // errors, column-major: consecutive threads take consecutive rows of a column
   __syncthreads();
-  // coalesced write-back of Q, codes (and gh)
-  for (int rr = warp; rr < nrows_here; rr += 4) {
-    float* dst = P.W + (long long)b * P.w_bs + (row0 + rr) * P.ldw;
-    int8_t* qdst = P.codes ? P.codes + (long long)b * P.q_bs + (row0 + rr) * P.ldq : nullptr;
-    float* gdst = (METHOD == G2Q_METHOD_G2PTQ)
-                      ? P.gh + (long long)b * P.z_bs + (row0 + rr) * P.ldz : nullptr;
-    for (int c = lane; c < nc; c += 32) {
-      dst[c] = Ws[rr * LDS_ROW + c];
-      if (qdst) qdst[c] = Qs[rr * CODE_ROW + c];
-      if (METHOD == G2Q_METHOD_G2PTQ) gdst[c] = Xs[rr * LDS_ROW + c];
+  const long long row0 = (long long)blockIdx.x * QROWS;
+  for (int idx = tid; idx < QROWS * nc; idx += QT * QROWS) {
+    const int i = idx / QROWS, q = idx % QROWS;
+    const long long rq = row0 + q;
+    if (rq >= P.rows) continue;
+    const float e = Es[q * LDE + i];
+    const float ea = (METHOD == G2Q_METHOD_G2PTQ) ? EAs[q * LDE + i] : e;
+    if (P.err) P.err[(long long)b * P.e_bs + (long long)i * P.lde + rq] = e;
+    const long long ao = (long long)b * P.ea_bs + (long long)i * P.ldea + rq;
+    if (P.erra) P.erra[ao] = ea;
+    if (P.erra_hi) {
+      __nv_bfloat16 h, l;
+      split_bf16(ea, &h, &l);
+      P.erra_hi[ao] = h;
+      P.erra_lo[ao] = l;
     }
   }
 }
 
-static size_t block_smem(int method) {
-  return (size_t)smem_floats(method) * sizeof(float) + BLK * CODE_ROW + BLK * sizeof(int);
-}
+static size_t block_smem(int method) { return (size_t)block_smem_floats(method) * sizeof(float); }
 
 template <int METHOD>
 static int launch_block_t(const BlockParams& P, long long batch, cudaStream_t st) {
@@ -282,9 +234,9 @@ static int launch_block_t(const BlockParams& P, long long batch, cudaStream_t st
       return G2Q_ERR_CUDA;
     if (dev < 64) attr_done[dev] = 1;
   }
-  dim3 grid(cdiv(P.rows, BLK), (unsigned)batch);
+  dim3 grid(cdiv(P.rows, QROWS), (unsigned)batch);
   if (grid.y > 65535u) return G2Q_ERR_INVALID_ARG;
-  block_kernel<METHOD><<<grid, BLK, smem, st>>>(P);
+  block_kernel<METHOD><<<grid, QT * QROWS, smem, st>>>(P);
   G2Q_CHECK_LAUNCH();
   return G2Q_OK;
 }

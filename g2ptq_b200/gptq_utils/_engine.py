@@ -315,13 +315,16 @@ def stream_pool(device, n=4):
 
 def fasterquant_all(objs, streams=4, **kwargs):
     """Quantize several quantizer objects concurrently: each object's pipeline
-    is enqueued on one stream of a small pool, then every object is finished
-    (status read, retry, write-back) in order.  Equivalent to calling
-    ``obj.fasterquant(**kwargs)`` for each object in turn."""
+    is enqueued on one stream of a small pool (longest first), then every
+    object is finished (status read, retry, write-back).  Equivalent to
+    calling ``obj.fasterquant(**kwargs)`` for each object in turn."""
     if not objs:
         return
     cur = torch.cuda.current_stream(objs[0].dev)
     pool = stream_pool(objs[0].dev, streams)
+    # launch the longest chains first (factorization ~ C^3, compensation ~ R C^2)
+    order = sorted(range(len(objs)), key=lambda i: -objs[i].num_layers * (
+        objs[i].columns ** 3 + objs[i].rows * objs[i].columns ** 2))
     # Pending add_batch folds are large Gram products that fill the GPU on
     # their own: run them in order on the caller's stream first, and overlap
     # only the latency-bound factorization / compensation chains.
@@ -329,8 +332,9 @@ def fasterquant_all(objs, streams=4, **kwargs):
         if not getattr(o, "offload_hessians", False):
             o._flush_all()
     launched = []
-    for i, o in enumerate(objs):
-        s = pool[i % len(pool)]
+    for n, i in enumerate(order):
+        o = objs[i]
+        s = pool[n % len(pool)]
         s.wait_stream(cur)
         with torch.cuda.stream(s):
             launched.append((s, o, o._fq_launch(**kwargs)))
