@@ -217,7 +217,11 @@ static int side_state(cudaStream_t main, int steps, SideState** out) {
     if (s->side && s->dev != dev) {
       *s = SideState();  // slot held a stream of another device: start over
     }
-    if (!s->side && cudaStreamCreateWithFlags(&s->side, cudaStreamNonBlocking) != cudaSuccess)
+    // the inverse chain runs at the caller's stream priority
+    int prio = 0;
+    if (!s->side && (cudaStreamGetPriority(main, &prio) != cudaSuccess ||
+                     cudaStreamCreateWithPriority(&s->side, cudaStreamNonBlocking, prio) !=
+                         cudaSuccess))
       return G2Q_ERR_CUDA;
     s->dev = dev;
     s->main = main;

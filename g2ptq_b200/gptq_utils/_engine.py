@@ -307,9 +307,12 @@ _STREAMS = {}
 
 
 def stream_pool(device, n=4):
+    """``n`` side streams of ``device``: the first at the highest priority the
+    device offers (it carries the longest chain), the others at the default."""
     key = (device.index if device.index is not None else torch.cuda.current_device(), n)
     if key not in _STREAMS:
-        _STREAMS[key] = [torch.cuda.Stream(device=device) for _ in range(n)]
+        _STREAMS[key] = [torch.cuda.Stream(device=device, priority=-16 if i == 0 else 0)
+                         for i in range(n)]
     return _STREAMS[key]
 
 
@@ -331,10 +334,12 @@ def fasterquant_all(objs, streams=4, **kwargs):
     for o in objs:
         if not getattr(o, "offload_hessians", False):
             o._flush_all()
+    # The longest chain takes the high-priority stream, so that its kernels go
+    # first whenever SMs free up; the shorter chains fill the gaps.
     launched = []
     for n, i in enumerate(order):
         o = objs[i]
-        s = pool[n % len(pool)]
+        s = pool[0] if n == 0 else pool[1 + (n - 1) % (len(pool) - 1)]
         s.wait_stream(cur)
         with torch.cuda.stream(s):
             launched.append((s, o, o._fq_launch(**kwargs)))
