@@ -57,13 +57,23 @@ def parse():
 
 
 def load_peaks():
+    """HBM GB/s and the dense bf16 TFLOP/s a kernel timed inside a long step can
+    reach (the sustained figure: the Gram launches run back to back for seconds)."""
     path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "MEASURED_PEAKS.json")
     try:
         with open(path) as f:
             p = json.load(f)
-        return p["hbm_gbs"], p["bf16_tflops"], "measured"
+        return p["hbm_gbs"], p.get("bf16_tflops_sustained", p["bf16_tflops"]), "measured"
     except Exception:
-        return 6650.0, 1590.0, "fallback"
+        return 6650.0, 1400.0, "fallback"
+
+
+# DRAM traffic of one Gram fold at the bench's 4096-column fold shape (16384 BF16
+# tokens), dram__bytes_read.sum + dram__bytes_write.sum from one ncu capture
+# (profiles/gram_tc_wide_c4096_t16384.md); the algorithmic bytes of that launch
+# are 268.4 MB (X once, H read and written once).
+GRAM_FOLD_TRAFFIC_BYTES = 310.19e6
+GRAM_FOLD_ALGORITHMIC_BYTES = 268.44e6
 
 
 class ClockSampler:
@@ -292,8 +302,10 @@ def native(args):
             "kernel": "Hessian Gram update (g2q_gram_update)",
             "bound": "tensor", "achieved": round(gram_tflops, 2),
             "peak": bf16, "unit": "TFLOP/s",
-            "frac": round(gram_tflops / bf16, 4), "traffic": None,
-            "peak_kind": f"{peak_kind} bf16 dense",
+            "frac": round(gram_tflops / bf16, 4), "traffic": GRAM_FOLD_TRAFFIC_BYTES,
+            "traffic_per": "launch, C=4096 x T=16384 fold "
+                           f"(algorithmic {GRAM_FOLD_ALGORITHMIC_BYTES:.4g} B)",
+            "peak_kind": f"{peak_kind} bf16 dense sustained",
             "share_of_step": round(gram_ms / ms, 3) if ms else None,
         },
     }
