@@ -60,17 +60,23 @@ __global__ void reverse_damp_kernel(const float* H, long long C, long long ldh,
 // lower-triangular inverse to Linv (NB x NB, zero padded).
 //
 // The block and its inverse live in registers: thread (ty, tx) of a 16 x 16
-// grid owns rows 8ty..8ty+7 x columns 8tx..8tx+7 of both L and X.  Pivot j
-// publishes column j of the working matrix and row j of X through shared
-// memory; every thread then applies the rank-1 update to its 8 x 8 tile of the
-// trailing matrix (a -= l l^T) and of the forward substitution of L X = I
-// (x_i -= l_ij x_j).  The pivot loop is unrolled by 8 so that every register
-// index is a compile-time constant.  Columns are scaled by 1/l_jj, as LAPACK's
-// unblocked spotf2 does.
+// grid owns rows 8ty..8ty+7 x columns 8tx..8tx+7 of both L and X = L^-1.
+// Blocked right-looking factorization, eight pivots at a time:
+//   1. the thread holding diagonal tile jb runs the unblocked factorization of
+//      that tile (columns scaled by 1/l_jj, as LAPACK's spotf2);
+//   2. the tiles under it apply the same eight pivots to their rows (the strip
+//      L_ij), and the tiles of block row jb of X run the forward substitution
+//      of L X = I for those eight rows;
+//   3. rank-8 updates A_ik -= L_ij L_kj^T of the lower trailing tiles and
+//      X_i: -= L_ij X_j: of X.
+// Every element sees the same operations in the same order as with one pivot
+// at a time, but with two block-wide barriers per eight pivots.
 __global__ void __launch_bounds__(256) panel_kernel(float* A, long long C, long long k0, int nb,
                                                     float* Linv, int* info) {
-  __shared__ __align__(16) float col[NB];
-  __shared__ __align__(16) float row[NB];
+  __shared__ __align__(16) float Ls[8][NB];  // strip L_ij, transposed (column k of the strip)
+  __shared__ __align__(16) float Xb[8][NB];  // finished rows of X in block row jb
+  __shared__ float Ld[8][8];                 // L_jj (scaled columns)
+  __shared__ float Rl[8];                    // 1 / l_jj
   __shared__ int failed;
   const int t = threadIdx.x;
   const int ty = t >> 4, tx = t & 15;
@@ -87,70 +93,114 @@ __global__ void __launch_bounds__(256) panel_kernel(float* A, long long C, long 
   if (t == 0) failed = 0;
   __syncthreads();
 
-  for (int jb = 0; jb < NB / 8; ++jb) {
+  for (int jb = 0; jb * 8 < nb; ++jb) {
+    const int j0 = jb * 8;
+    const int nbk = (nb - j0) < 8 ? (nb - j0) : 8;
+    // ---- 1. diagonal tile
+    if (ty == jb && tx == jb) {
+      bool ok = true;
 #pragma unroll
-    for (int jj = 0; jj < 8; ++jj) {
-      const int j = jb * 8 + jj;
-      if (j >= nb) break;
-      if (tx == jb) {
+      for (int j = 0; j < 8; ++j) {
+        float rl = 0.f;
+        if (j < nbk && ok) {
+          const float d = a[j][j];
+          if (!(d > 0.f)) {  // non-positive or NaN pivot
+            ok = false;
+            failed = 1;
+            if (info) atomicCAS(info, 0, (int)(k0 + j0 + j + 1));
+          } else {
+            const float l = sqrtf(d);
+            rl = 1.f / l;
+            a[j][j] = l;
 #pragma unroll
-        for (int u = 0; u < 8; ++u) col[r0 + u] = a[u][jj];
-      }
-      if (ty == jb) {
+            for (int u = j + 1; u < 8; ++u) a[u][j] *= rl;
 #pragma unroll
-        for (int v = 0; v < 8; ++v) row[c0 + v] = x[jj][v];
-      }
-      __syncthreads();
-      const float d = col[j];
-      if (!(d > 0.f)) {  // non-positive or NaN pivot (uniform across the block)
-        if (t == 0) {
-          failed = 1;
-          if (info) atomicCAS(info, 0, (int)(k0 + j + 1));
+            for (int u = j + 1; u < 8; ++u)
+#pragma unroll
+              for (int v = j + 1; v <= u; ++v) a[u][v] = fmaf(-a[u][j], a[v][j], a[u][v]);
+          }
         }
-        goto done;
-      }
-      const float l = sqrtf(d);
-      const float rl = 1.f / l;
-      float lr[8], lc[8], xr[8];
-      {
-        const float4 p0 = *reinterpret_cast<const float4*>(&col[r0]);
-        const float4 p1 = *reinterpret_cast<const float4*>(&col[r0 + 4]);
-        const float4 q0 = *reinterpret_cast<const float4*>(&col[c0]);
-        const float4 q1 = *reinterpret_cast<const float4*>(&col[c0 + 4]);
-        const float4 s0 = *reinterpret_cast<const float4*>(&row[c0]);
-        const float4 s1 = *reinterpret_cast<const float4*>(&row[c0 + 4]);
-        const float pr[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
-        const float pc[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-        const float ps[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          lr[u] = (r0 + u > j) ? pr[u] * rl : 0.f;
-          lc[u] = (c0 + u > j) ? pc[u] * rl : 0.f;
-          xr[u] = ps[u] * rl;
-        }
+        Rl[j] = rl;
       }
 #pragma unroll
       for (int u = 0; u < 8; ++u)
 #pragma unroll
-        for (int v = 0; v < 8; ++v) {
-          a[u][v] = fmaf(-lr[u], lc[v], a[u][v]);
-          x[u][v] = fmaf(-lr[u], xr[v], x[u][v]);
-        }
-      if (tx == jb) {
+        for (int v = 0; v < 8; ++v) Ld[u][v] = (v < u) ? a[u][v] : 0.f;
+    }
+    __syncthreads();
+    if (failed) break;  // uniform after the barrier
+    // ---- 2. the eight pivots on the strip, and on block row jb of X
+    if (tx == jb && ty > jb) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (j >= nbk) continue;
+        const float rl = Rl[j];
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
-          if (r0 + u > j) a[u][jj] = lr[u];
-          else if (r0 + u == j) a[u][jj] = l;
+          const float sv = a[u][j] * rl;
+          a[u][j] = sv;
+          Ls[j][r0 + u] = sv;
+#pragma unroll
+          for (int v = j + 1; v < 8; ++v) a[u][v] = fmaf(-sv, Ld[v][j], a[u][v]);
         }
       }
-      if (ty == jb) {
 #pragma unroll
-        for (int v = 0; v < 8; ++v) x[jj][v] = xr[v];
+      for (int j = 0; j < 8; ++j)
+        if (j >= nbk) {
+#pragma unroll
+          for (int u = 0; u < 8; ++u) Ls[j][r0 + u] = 0.f;
+        }
+    }
+    if (ty == jb && tx <= jb) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float rl = Rl[j];
+#pragma unroll
+        for (int v = 0; v < 8; ++v) {
+          const float xf = (j < nbk) ? x[j][v] * rl : 0.f;
+          x[j][v] = xf;
+          Xb[j][c0 + v] = xf;
+#pragma unroll
+          for (int u = j + 1; u < 8; ++u) x[u][v] = fmaf(-Ld[u][j], xf, x[u][v]);
+        }
       }
-      __syncthreads();
+    }
+    __syncthreads();
+    // ---- 3. rank-8 updates of the trailing lower tiles and of X
+    if (ty > jb) {
+      float lr[8][8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float4 p0 = *reinterpret_cast<const float4*>(&Ls[k][r0]);
+        const float4 p1 = *reinterpret_cast<const float4*>(&Ls[k][r0 + 4]);
+        lr[k][0] = p0.x; lr[k][1] = p0.y; lr[k][2] = p0.z; lr[k][3] = p0.w;
+        lr[k][4] = p1.x; lr[k][5] = p1.y; lr[k][6] = p1.z; lr[k][7] = p1.w;
+      }
+      if (tx > jb && tx <= ty) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float4 q0 = *reinterpret_cast<const float4*>(&Ls[k][c0]);
+          const float4 q1 = *reinterpret_cast<const float4*>(&Ls[k][c0 + 4]);
+          const float lc[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+#pragma unroll
+            for (int v = 0; v < 8; ++v) a[u][v] = fmaf(-lr[k][u], lc[v], a[u][v]);
+        }
+      } else if (tx <= jb) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float4 q0 = *reinterpret_cast<const float4*>(&Xb[k][c0]);
+          const float4 q1 = *reinterpret_cast<const float4*>(&Xb[k][c0 + 4]);
+          const float xc[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+#pragma unroll
+            for (int v = 0; v < 8; ++v) x[u][v] = fmaf(-lr[k][u], xc[v], x[u][v]);
+        }
+      }
     }
   }
-done:
   __syncthreads();
   if (failed) {
     // mark the inverse as NaN so downstream products are visibly invalid
