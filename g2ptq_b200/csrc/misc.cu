@@ -44,6 +44,35 @@ __global__ void stage_kernel(D* dst, long long dst_ld, long long row0, const S* 
   }
 }
 
+// Strided row copy in 16-byte words (rows of w16 words; pitches in words).
+__global__ void copy_rows16_kernel(uint4* __restrict__ dst, long long dst_pitch,
+                                   const uint4* __restrict__ src, long long src_pitch,
+                                   long long rows, long long w16) {
+  const long long n = rows * w16;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  // four independent words in flight per thread
+  for (; idx + 3 * stride < n; idx += 4 * stride) {
+    uint4 v[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const long long i = idx + k * stride;
+      const long long r = i / w16, c = i - r * w16;
+      v[k] = __ldcs(src + r * src_pitch + c);
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const long long i = idx + k * stride;
+      const long long r = i / w16, c = i - r * w16;
+      dst[r * dst_pitch + c] = v[k];
+    }
+  }
+  for (; idx < n; idx += stride) {
+    const long long r = idx / w16, c = idx - r * w16;
+    dst[r * dst_pitch + c] = __ldcs(src + r * src_pitch + c);
+  }
+}
+
 __global__ void scale_vec_kernel(float* acc, long long C, float keep) {
   const long long c = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (c < C) acc[c] *= keep;
@@ -278,8 +307,21 @@ extern "C" int g2q_stage_tokens(void* dst, int dst_dtype, int64_t dst_ld, int64_
   if (t == 0) return G2Q_OK;
   cudaStream_t st = (cudaStream_t)stream;
   if (dst_dtype == src_dtype && !sub) {
-    // same element type: a strided device-to-device copy at copy bandwidth
     const size_t es = dst_dtype == G2Q_DTYPE_BF16 || dst_dtype == G2Q_DTYPE_F16 ? 2 : 4;
+    char* d0 = (char*)dst + (size_t)row0 * dst_ld * es;
+    if ((((uintptr_t)d0 | (uintptr_t)src) & 15) == 0 && ((size_t)C * es) % 16 == 0 &&
+        ((size_t)dst_ld * es) % 16 == 0 && ((size_t)src_ld * es) % 16 == 0) {
+      // 16-byte words on the SMs: reads and writes at HBM speed
+      const long long w16 = (long long)((size_t)C * es / 16);
+      long long blocks = (t * w16 + 1023) / 1024;
+      if (blocks > 148 * 16) blocks = 148 * 16;
+      copy_rows16_kernel<<<(int)blocks, 256, 0, st>>>(
+          (uint4*)d0, (long long)((size_t)dst_ld * es / 16), (const uint4*)src,
+          (long long)((size_t)src_ld * es / 16), t, w16);
+      G2Q_CHECK_LAUNCH();
+      return G2Q_OK;
+    }
+    // unaligned rows: a strided device-to-device copy
     if (cudaMemcpy2DAsync((char*)dst + (size_t)row0 * dst_ld * es, (size_t)dst_ld * es, src,
                           (size_t)src_ld * es, (size_t)C * es, (size_t)t,
                           cudaMemcpyDeviceToDevice, st) != cudaSuccess)
