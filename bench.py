@@ -73,6 +73,8 @@ def load_peaks():
 # (profiles/gram_tc_wide_c4096_t16384.md); the algorithmic bytes of that launch
 # are 268.4 MB (X once, H read and written once).
 GRAM_FOLD_TRAFFIC_BYTES = 310.19e6
+# device buffers (one calibration sequence each) of the host-input copy ring
+E2E_RING = 48
 GRAM_FOLD_ALGORITHMIC_BYTES = 268.44e6
 
 
@@ -322,47 +324,53 @@ def native(args):
 
 def native_e2e(torch, dist, args, layers, world, rank, dev, n_local, dev_acts):
     """Same steps through the public API with host-resident inputs: every step
-    copies its activations from pinned host memory (double-buffered on a side
-    stream, as the reference's prefetch_generator overlaps its H2D copies) and
-    reads the quantized weights and packed codes back to the host."""
+    copies its activations from pinned host memory and reads the quantized
+    weights and packed codes back to the host.  The copies stream through a ring
+    of sequence buffers on a side stream (as the reference's prefetch_generator
+    overlaps its H2D copies), running ahead into the next step's sequences while
+    the current step factors and compensates."""
     host = {grp: torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
             for grp, x in dev_acts.items()}
     for grp in host:
         host[grp].copy_(dev_acts[grp])
     side = torch.cuda.Stream(device=dev)
+    ring = max(2, min(n_local, E2E_RING))
     bufs = [{grp: torch.empty(1, args.seq_len, C, dtype=torch.bfloat16, device=dev)
-             for grp, C in GROUP_COLS.items()} for _ in range(2)]
-    ready = [torch.cuda.Event() for _ in range(2)]
-    free_ev = [torch.cuda.Event() for _ in range(2)]
+             for grp, C in GROUP_COLS.items()} for _ in range(ring)]
+    ready = [torch.cuda.Event() for _ in range(ring)]
+    free_ev = [torch.cuda.Event() for _ in range(ring)]
     h2d_bytes = sum(h.numel() * h.element_size() for h in host.values())
     outs = {name: torch.empty(rows, cols, dtype=torch.bfloat16, pin_memory=True)
             for name, rows, cols, _ in LINEARS}
     packed = {name: torch.empty(rows, cols * BITS // 32, dtype=torch.int32, pin_memory=True)
               for name, rows, cols, _ in LINEARS}
+    state = {"issued": 0, "consumed": 0}  # sequences copied / handed to add_batch so far
 
-    def prefetch(s):
-        k = s & 1
-        with torch.cuda.stream(side):
-            side.wait_event(free_ev[k])
-            for grp in GROUP_COLS:
-                bufs[k][grp].copy_(host[grp][s:s + 1], non_blocking=True)
-            ready[k].record(side)
+    def prefetch_upto(g_end):
+        while state["issued"] < g_end:
+            g = state["issued"]
+            k, s = g % ring, g % n_local
+            with torch.cuda.stream(side):
+                side.wait_event(free_ev[k])
+                for grp in GROUP_COLS:
+                    bufs[k][grp].copy_(host[grp][s:s + 1], non_blocking=True)
+                ready[k].record(side)
+            state["issued"] += 1
+
+    def feed(s):
+        g = state["consumed"]
+        if g > 0:
+            free_ev[(g - 1) % ring].record()  # users of the previous buffer are enqueued
+        prefetch_upto(g + ring)  # the slot of g - 1 is free again
+        torch.cuda.current_stream().wait_event(ready[g % ring])
+        state["consumed"] += 1
+        return bufs[g % ring]
 
     def step():
-        prefetch(0)
-        state = {"prev": None}
-
-        def feed(s):
-            if state["prev"] is not None:
-                free_ev[state["prev"] & 1].record()  # previous buffer's users are enqueued
-            state["prev"] = s
-            torch.cuda.current_stream().wait_event(ready[s & 1])
-            if s + 1 < n_local:
-                prefetch(s + 1)
-            return bufs[s & 1]
-
         one_step(torch, layers, feed, n_local, world, rank, dist)
-        free_ev[state["prev"] & 1].record()
+        # free the last buffer and keep the copies running into the next step
+        free_ev[(state["consumed"] - 1) % ring].record()
+        prefetch_upto(state["consumed"] + ring)
         d2h = 0
         for name, rows, cols, _ in LINEARS:
             outs[name].copy_(layers[name].weight.data, non_blocking=True)
