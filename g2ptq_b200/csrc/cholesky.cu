@@ -16,6 +16,8 @@
 // The factorization (panel, TRSM, SYRK) runs on the caller's stream; the
 // inverse chain (X_k, Y update), which no later panel depends on, runs on a
 // library-owned side stream ordered by per-step events and joined at the end.
+#include <cuda_fp16.h>
+
 #include "gemm_simt.cuh"
 
 namespace g2q {
@@ -236,11 +238,12 @@ __global__ void extract_u_kernel(const float* X, long long C, float* U, int* inf
 
 
 
-int split3(const float* src, long long lds, long long rows, long long cols, __nv_bfloat16* h,
-           __nv_bfloat16* m, __nv_bfloat16* l, long long ldd, int transpose, cudaStream_t st);
-int tc_update3(float* D, long long ldd, long long M, long long N, long long K,
-               __nv_bfloat16* const* a3, long long lda, __nv_bfloat16* const* b3, long long ldb,
-               int lower, float alpha, float beta, cudaStream_t st);
+int split2h(const float* src, long long lds, long long n, int K, __half* hi, __half* lo,
+            long long ldd, float* scale, int transpose, cudaStream_t st);
+int tc_update2h(float* D, long long ldd, long long M, long long N, long long K,
+                __half* const* a2, const float* sa, long long lda, __half* const* b2,
+                const float* sb, long long ldb, int lower, float alpha, float beta,
+                cudaStream_t st);
 
 // Side stream and per-step events of the inverse chain, one set per (device,
 // caller stream) so that factorizations issued on different streams overlap.
@@ -292,11 +295,12 @@ static int side_state(cudaStream_t main, int steps, SideState** out) {
 static bool tc_ok(long long C) { return C % 8 == 0; }
 
 // Workspace layout (floats unless noted): A [C*C], Y [C*C], diagonal inverses
-// [nblk][NB*NB], mean diag [64], then bf16: L21^T splits [2 buffers][3][NB*C],
-// X_k splits [3][NB*C].
+// [nblk][NB*NB], mean diag [64], then fp16: L21^T splits [2 buffers][2][NB*C],
+// X_k splits [2][NB*C], then the splits' scales: L21 [2 buffers][C], X_k [C].
 struct CholWs {
   float *A, *Y, *linv, *mdiag;
-  __nv_bfloat16 *lt, *xk;
+  __half *lt, *xk;
+  float *lsc, *xsc;
 };
 
 static CholWs carve(float* ws, long long C) {
@@ -306,8 +310,10 @@ static CholWs carve(float* ws, long long C) {
   w.Y = w.A + C * C;
   w.linv = w.Y + C * C;
   w.mdiag = w.linv + nblk * NB * NB;
-  w.lt = reinterpret_cast<__nv_bfloat16*>(w.mdiag + 64);
-  w.xk = w.lt + 2 * 3 * (long long)NB * C;
+  w.lt = reinterpret_cast<__half*>(w.mdiag + 64);
+  w.xk = w.lt + 2 * 2 * (long long)NB * C;
+  w.lsc = reinterpret_cast<float*>(w.xk + 2 * (long long)NB * C);
+  w.xsc = w.lsc + 2 * C;
   return w;
 }
 
@@ -335,9 +341,10 @@ static int chol_one(float* U, const float* H, long long C, long long ldh, float 
     const int nb = (int)((C - k0) < NB ? (C - k0) : NB);
     const long long rest = C - k0 - nb;
     float* linv = w.linv + kb * NB * NB;
-    __nv_bfloat16* lt = w.lt + (kb & 1) * 3 * tsz;
-    __nv_bfloat16* l3[3] = {lt, lt + tsz, lt + 2 * tsz};
-    __nv_bfloat16* x3[3] = {w.xk, w.xk + tsz, w.xk + 2 * tsz};
+    __half* lt = w.lt + (kb & 1) * 2 * tsz;
+    __half* l2[2] = {lt, lt + tsz};
+    float* lsc = w.lsc + (kb & 1) * C;
+    __half* x2[2] = {w.xk, w.xk + tsz};
     // ---- factorization (caller's stream): panel, TRSM, split, SYRK
     panel_kernel<<<1, 256, 0, st>>>(A, C, k0, nb, linv, info);
     G2Q_CHECK_LAUNCH();
@@ -349,9 +356,9 @@ static int chol_one(float* U, const float* H, long long C, long long ldh, float 
         // the inverse chain of step kb-2 used this L21^T buffer
         if (kb >= 2 && cudaStreamWaitEvent(st, ev[2 * (kb - 2) + 1], 0) != cudaSuccess)
           return G2Q_ERR_CUDA;
-        G2Q_TRY(split3(A + (k0 + nb) * C + k0, C, rest, nb, l3[0], l3[1], l3[2], C, 1, st));
-        G2Q_TRY(tc_update3(A + (k0 + nb) * C + (k0 + nb), C, rest, rest, nb, l3, C, l3, C, 1,
-                           1.f, -1.f, st));
+        G2Q_TRY(split2h(A + (k0 + nb) * C + k0, C, rest, nb, l2[0], l2[1], C, lsc, 1, st));
+        G2Q_TRY(tc_update2h(A + (k0 + nb) * C + (k0 + nb), C, rest, rest, nb, l2, lsc, C, l2,
+                            lsc, C, 1, 1.f, -1.f, st));
       } else {
         G2Q_TRY(simt_gemm_f32(A + (k0 + nb) * C + (k0 + nb), C, A + (k0 + nb) * C + k0, C, false,
                               A + (k0 + nb) * C + k0, C, true, rest, rest, nb, 1.f, -1.f,
@@ -365,9 +372,9 @@ static int chol_one(float* U, const float* H, long long C, long long ldh, float 
                           0.f, 1.f, G2Q_MASK_FULL, side));
     if (rest > 0) {
       if (use_tc) {
-        G2Q_TRY(split3(Y + k0 * C, C, nb, k0 + nb, x3[0], x3[1], x3[2], C, 0, side));
-        G2Q_TRY(tc_update3(Y + (k0 + nb) * C, C, rest, k0 + nb, nb, l3, C, x3, C, 0, 1.f, -1.f,
-                           side));
+        G2Q_TRY(split2h(Y + k0 * C, C, k0 + nb, nb, x2[0], x2[1], C, w.xsc, 0, side));
+        G2Q_TRY(tc_update2h(Y + (k0 + nb) * C, C, rest, k0 + nb, nb, l2, lsc, C, x2, w.xsc, C, 0,
+                            1.f, -1.f, side));
       } else {
         G2Q_TRY(simt_gemm_f32(Y + (k0 + nb) * C, C, A + (k0 + nb) * C + k0, C, false, Y + k0 * C,
                               C, false, rest, k0 + nb, nb, 1.f, -1.f, G2Q_MASK_FULL, side));
@@ -386,7 +393,7 @@ static int chol_one(float* U, const float* H, long long C, long long ldh, float 
 extern "C" size_t g2q_chol_workspace_bytes(int64_t C) {
   const int64_t nblk = (C + g2q::NB - 1) / g2q::NB;
   return (size_t)(2 * C * C + nblk * g2q::NB * g2q::NB + 64) * sizeof(float) +
-         (size_t)9 * g2q::NB * C * sizeof(__nv_bfloat16) + 256;
+         (size_t)6 * g2q::NB * C * sizeof(__half) + (size_t)3 * C * sizeof(float) + 256;
 }
 
 extern "C" int g2q_chol_upper_inverse(float* U, const float* H, int64_t C, int64_t ldh,

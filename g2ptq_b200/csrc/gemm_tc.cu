@@ -8,16 +8,17 @@
 //   * GPTQ trailing update  W[:, i2:] -= Err @ U[i1:i2, i2:]  with the block
 //     error stored column-major [blk, rows] by the compensation kernel and U
 //     row-major (k = block column).
-// Tiles of 128 x 64 (MN x K) bf16 are fed by TMA (two 64 x 64 boxes, 128-byte
-// swizzle) into a multi-stage shared-memory ring; one thread issues
-// tcgen05.mma (M = 128, N = 128, K = 16, bf16 in, fp32 accumulate in TMEM);
-// four epilogue warps read the accumulator with tcgen05.ld and apply
-// alpha / beta, the bounds and the symmetric mirror.
-// fp32 operands are carried as a bf16 hi/lo pair and multiplied as
-// hi*hi + hi*lo + lo*hi (three MMAs per K step), or -- where fp32 accuracy is
-// required (the Cholesky updates) -- as a hi/mid/lo triple multiplied with the
-// six products of order <= 2 (hh, hm, mh, hl, lh, mm).
-//
+// Tiles of 128 x 64 (MN x K) 16-bit values are fed by TMA (64 x 64 boxes,
+// 128-byte swizzle) into a multi-stage shared-memory ring; one thread issues
+// tcgen05.mma (M = 128, N = 128 or 256, K = 16, bf16 or fp16 in, fp32
+// accumulate in TMEM); the epilogue warps read the accumulator with tcgen05.ld
+// and apply alpha / beta, the bounds and the symmetric mirror.
+// fp32 operands are carried as a hi/lo pair and multiplied as
+// hi*hi + hi*lo + lo*hi (three MMAs per K step): bf16 pairs for the trailing
+// update and fp32 Grams, and -- where fp32 accuracy is required (the Cholesky
+// updates) -- fp16 pairs of rows scaled by powers of two (22 significant bits,
+// the scales applied exactly in the epilogue).
+
 // Accumulator promotion: the tensor core adds each MMA's partial sum into the
 // TMEM accumulator with a bias of about one fp32 ulp (measured: the relative
 // error of a long Gram product grows linearly with K, every diagonal entry
@@ -26,12 +27,15 @@
 // finished buffer into an fp32 register accumulator with rounded adds while
 // the other buffer fills.  The bias stays below ~1e-6 relative for any K.
 //
-// Warp roles (192 threads): warp 0 TMA producer, warp 1 TMEM owner + MMA
-// issuer, warps 2-5 epilogue (TMEM lane quadrant = warp % 4).
+// Warp roles (192 threads, 320 for 128 x 256 tiles): warp 0 TMA producer,
+// warp 1 TMEM owner + MMA issuer, the rest epilogue (TMEM lane quadrant =
+// warp % 4).
 // Every wait on an mbarrier is bounded; on expiry the CTA records
 // G2Q_ERR_TIMEOUT in the caller's status word and winds down.
 #include <cuda.h>
 #include <cudaTypedefs.h>
+
+#include <cuda_fp16.h>
 
 #include "gemm_simt.cuh"
 
@@ -58,6 +62,9 @@ struct Params {
   int raster;      // 1: 1-D grid over the needed tiles in groups of GROUP_M tile rows
   int tiles_m, tiles_n;
   int red;         // short-K epilogue adds beta * acc into D with TMA reduce-add (alpha == 1)
+  int f16;         // operands are fp16 (else bf16)
+  const float* sa;  // optional per-row (M) and per-column (N) output scales, powers of two
+  const float* sb;
   int* status;
 };
 
@@ -141,10 +148,14 @@ __device__ __forceinline__ uint64_t desc_mn_sw128(uint32_t saddr) {
   return d;
 }
 
-// kind::f16 instruction descriptor: bf16 x bf16 -> f32, both MN-major, M=128, N=n.
+// kind::f16 instruction descriptor: bf16 x bf16 (or f16 x f16) -> f32, both
+// MN-major, M=128, N=n.
 __host__ __device__ constexpr uint32_t idesc_bf16_mn(int n) {
   return (1u << 4) | (1u << 7) | (1u << 10) | (1u << 15) | (1u << 16) |
          ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+__host__ __device__ constexpr uint32_t idesc_f16_mn(int n) {
+  return idesc_bf16_mn(n) & ~((7u << 7) | (7u << 10));
 }
 
 __device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc,
@@ -209,7 +220,7 @@ struct Cfg {
   static constexpr int THREADS = 64 + 32 * EPI_WARPS;
   static constexpr int ACC_COLS = SMALL ? BN : 2 * BN_T;
   static constexpr int ORDER = (NA > NB ? NA : NB) - 1;  // products a_i b_j with i + j <= ORDER
-  static constexpr int PRODUCTS = (NA == 3 && NB == 3) ? 6 : (NA + NB - 1);
+  static constexpr int PRODUCTS = NA + NB - 1;
   // K blocks per TMEM accumulation group: 16 MMAs for one product, 24 otherwise
   static constexpr int PROMOTE_KB = PRODUCTS == 1 ? 4 : (PRODUCTS <= 3 ? 2 : 1);
 };
@@ -410,7 +421,7 @@ __global__ void __launch_bounds__((Cfg<NA, NB, SMALL, WIDE>::THREADS),
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16_mn(BN_T);
+      const uint32_t idesc = p.f16 ? idesc_f16_mn(BN_T) : idesc_bf16_mn(BN_T);
       int kb = 0;
       for (int g = 0; g < ngroups; ++g) {
         const int buf = g & 1;
@@ -490,6 +501,7 @@ __global__ void __launch_bounds__((Cfg<NA, NB, SMALL, WIDE>::THREADS),
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             v[u] = p.beta * __uint_as_float(r[4 * j4 + u]);
+            if (p.sa) v[u] *= (gm < p.M ? p.sa[gm] : 1.f) * (gn + u < p.N ? p.sb[gn + u] : 1.f);
             if (p.lower && gn + u > gm) v[u] = 0.f;  // leave the upper triangle as it is
           }
           *reinterpret_cast<float4*>(buf + lane * 32 + ((j4 ^ (lane & 7)) << 2)) =
@@ -523,7 +535,10 @@ __global__ void __launch_bounds__((Cfg<NA, NB, SMALL, WIDE>::THREADS),
           const long long gn = n0 + c * 32 + 4 * j4;
           float v[4];
 #pragma unroll
-          for (int u = 0; u < 4; ++u) v[u] = p.beta * __uint_as_float(r[4 * j4 + u]);
+          for (int u = 0; u < 4; ++u) {
+            v[u] = p.beta * __uint_as_float(r[4 * j4 + u]);
+            if (p.sa) v[u] *= p.sa[gm] * (gn + u < p.N ? p.sb[gn + u] : 1.f);
+          }
           EPILOGUE_STORE4
         }
       }
@@ -569,7 +584,10 @@ __global__ void __launch_bounds__((Cfg<NA, NB, SMALL, WIDE>::THREADS),
         const long long gn = n0 + half * BN + 4 * j4;
         float v[4];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) v[u] = p.beta * acc[4 * j4 + u];
+        for (int u = 0; u < 4; ++u) {
+          v[u] = p.beta * acc[4 * j4 + u];
+          if (p.sa) v[u] *= p.sa[gm] * (gn + u < p.N ? p.sb[gn + u] : 1.f);
+        }
         EPILOGUE_STORE4
       }
     }
@@ -604,7 +622,7 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 // 2-D bf16 tensor [outer, inner] with row stride ld (elements), 64 x 64 boxes.
 static bool make_map(CUtensorMap* m, const void* base, long long inner, long long outer,
-                     long long ld) {
+                     long long ld, bool f16 = false) {
   auto enc = encode_fn();
   if (!enc) return false;
   if ((reinterpret_cast<uintptr_t>(base) & 15) || ((ld * 2) & 15) || inner <= 0 || outer <= 0)
@@ -613,7 +631,8 @@ static bool make_map(CUtensorMap* m, const void* base, long long inner, long lon
   cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
   cuuint32_t box[2] = {64, (cuuint32_t)BK};
   cuuint32_t estr[2] = {1, 1};
-  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+  return enc(m, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+             const_cast<void*>(base), dims, strides, box,
              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
          CUDA_SUCCESS;
@@ -690,13 +709,11 @@ static int dispatch(int na, int nb, Maps& m, const Params& p, long long batch,
   const bool small = p.num_kb <= 4;
   if (small) {
     if (na == 2 && nb == 2) return launch<2, 2, true>(m, p, batch, st);
-    if (na == 3 && nb == 3) return launch<3, 3, true>(m, p, batch, st);
   }
   if (na == 1 && nb == 1) return launch<1, 1, false, true>(m, p, batch, st);
   if (na == 1 && nb == 2) return launch<1, 2, false>(m, p, batch, st);
   if (na == 2 && nb == 1) return launch<2, 1, false>(m, p, batch, st);
   if (na == 2 && nb == 2) return launch<2, 2, false>(m, p, batch, st);
-  if (na == 3 && nb == 3) return launch<3, 3, false>(m, p, batch, st);
   return G2Q_ERR_UNSUPPORTED;
 }
 
@@ -856,57 +873,92 @@ int tc_trailing_update(float* W, long long C, long long rows, long long batch, l
   return tc::dispatch(2, 2, mp, p, batch, st);
 }
 
-// Three-way bf16 split (hi/mid/lo) of a rows x cols fp32 block (row stride
-// lds), written transposed (dst[c][r]) or not (dst[r][c]) with row stride ldd.
-__global__ void split3_kernel(const float* __restrict__ src, long long lds, long long rows,
-                              long long cols, __nv_bfloat16* h, __nv_bfloat16* m,
-                              __nv_bfloat16* l, long long ldd, int transpose) {
-  __shared__ float tile[32][33];
-  const long long r0 = (long long)blockIdx.y * 32, c0 = (long long)blockIdx.x * 32;
-  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
-    const long long r = r0 + k, c = c0 + threadIdx.x;
-    tile[k][threadIdx.x] = (r < rows && c < cols) ? src[r * lds + c] : 0.f;
+// Two-term fp16 split of a K x (rows or cols) fp32 block for the fp32-accurate
+// updates of the Cholesky chain.  Each output row (M or N index) is scaled by a
+// power of two that puts its largest magnitude in [2^14, 2^15), so both terms
+// keep 11 significant bits each (22 together) whatever the row's scale; the
+// inverse scale is written to `scale` and applied exactly in the epilogue.
+//   transpose != 0: src is [rows][K] (row stride lds), dst [K][rows], one scale
+//                   per src row (the operand L21 of the SYRK and of the Y update);
+//   transpose == 0: src is [K][cols] (row stride lds), dst [K][cols], one scale
+//                   per column (the operand X_k of the Y update).
+// One block handles 32 rows (or columns) and all K <= 128 of them.
+__global__ void __launch_bounds__(256) split2h_kernel(const float* __restrict__ src,
+                                                      long long lds, long long n, int K,
+                                                      __half* hi, __half* lo, long long ldd,
+                                                      float* scale, int transpose) {
+  __shared__ float tile[128][33];
+  __shared__ float smax[8][32];
+  __shared__ float sfac[32];
+  const int x = threadIdx.x, y = threadIdx.y;
+  const long long n0 = (long long)blockIdx.x * 32;
+  const long long ni = n0 + x;
+  if (transpose) {
+    // source rows n0..n0+31, K long each: lanes walk k (coalesced), warp y takes
+    // rows y, y+8, ...
+    for (int rr = y; rr < 32; rr += 8) {
+      const long long r = n0 + rr;
+      for (int k = x; k < K; k += 32) tile[k][rr] = (r < n) ? src[r * lds + k] : 0.f;
+    }
+  } else {
+    for (int k = y; k < K; k += 8) tile[k][x] = (ni < n) ? src[(long long)k * lds + ni] : 0.f;
   }
   __syncthreads();
-  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
-    // transposed: this thread writes dst[c0 + k][r0 + tx] from tile[tx][k]
-    const long long orow = transpose ? c0 + k : r0 + k;
-    const long long ocol = transpose ? r0 + threadIdx.x : c0 + threadIdx.x;
-    const bool ok = transpose ? (orow < cols && ocol < rows) : (orow < rows && ocol < cols);
-    if (!ok) continue;
-    const float v = transpose ? tile[threadIdx.x][k] : tile[k][threadIdx.x];
-    const __nv_bfloat16 hv = __float2bfloat16_rn(v);
-    const float r1 = v - __bfloat162float(hv);
-    const __nv_bfloat16 mv = __float2bfloat16_rn(r1);
-    const float r2 = r1 - __bfloat162float(mv);
-    h[orow * ldd + ocol] = hv;
-    m[orow * ldd + ocol] = mv;
-    l[orow * ldd + ocol] = __float2bfloat16_rn(r2);
+  float m = 0.f;
+  for (int k = y; k < K; k += 8) m = fmaxf(m, fabsf(tile[k][x]));
+  smax[y][x] = m;
+  __syncthreads();
+  if (y == 0) {
+    float mm = smax[0][x];
+#pragma unroll
+    for (int q = 1; q < 8; ++q) mm = fmaxf(mm, smax[q][x]);
+    float f = 1.f, inv = 1.f;
+    if (mm > 0.f && mm <= 3.0e38f) {
+      int e;
+      frexpf(mm, &e);  // mm in [2^(e-1), 2^e)
+      f = ldexpf(1.f, 15 - e);
+      inv = ldexpf(1.f, e - 15);
+    }
+    sfac[x] = f;
+    if (ni < n) scale[ni] = inv;
+  }
+  __syncthreads();
+  const float f = sfac[x];
+  if (ni < n) {
+    for (int k = y; k < K; k += 8) {
+      const float v = tile[k][x] * f;
+      const __half h = __float2half_rn(v);
+      hi[(long long)k * ldd + ni] = h;
+      lo[(long long)k * ldd + ni] = __float2half_rn(v - __half2float(h));
+    }
   }
 }
 
-int split3(const float* src, long long lds, long long rows, long long cols, __nv_bfloat16* h,
-           __nv_bfloat16* m, __nv_bfloat16* l, long long ldd, int transpose, cudaStream_t st) {
-  if (rows <= 0 || cols <= 0) return G2Q_OK;
-  dim3 grid(cdiv(cols, 32), cdiv(rows, 32));
-  if (grid.y > 65535u) return G2Q_ERR_INVALID_ARG;
-  split3_kernel<<<grid, dim3(32, 8), 0, st>>>(src, lds, rows, cols, h, m, l, ldd, transpose);
+int split2h(const float* src, long long lds, long long n, int K, __half* hi, __half* lo,
+            long long ldd, float* scale, int transpose, cudaStream_t st) {
+  if (n <= 0 || K <= 0) return G2Q_OK;
+  if (K > 128) return G2Q_ERR_INVALID_ARG;
+  split2h_kernel<<<cdiv(n, 32), dim3(32, 8), 0, st>>>(src, lds, n, K, hi, lo, ldd, scale,
+                                                      transpose);
   G2Q_CHECK_LAUNCH();
   return G2Q_OK;
 }
 
-// fp32-accurate tensor-core update  D <- alpha D + beta * A^T B  for MN-major
-// three-term operands A[k][m] (terms a3, row stride lda) and B[k][n] (b3, ldb)
-// over K rows; lower != 0 writes only m >= n.  Returns G2Q_ERR_UNSUPPORTED when
-// TMA cannot describe the operands.
-int tc_update3(float* D, long long ldd, long long M, long long N, long long K,
-               __nv_bfloat16* const* a3, long long lda, __nv_bfloat16* const* b3, long long ldb,
-               int lower, float alpha, float beta, cudaStream_t st) {
+// fp32-accurate tensor-core update  D <- alpha D + beta * diag(sa) A^T B diag(sb)
+// for MN-major two-term fp16 operands A[k][m] (terms a2, row stride lda) and
+// B[k][n] (b2, ldb) over K rows (three products: hi*hi, hi*lo, lo*hi); lower != 0
+// writes only m >= n.  Returns G2Q_ERR_UNSUPPORTED when TMA cannot describe the
+// operands.
+int tc_update2h(float* D, long long ldd, long long M, long long N, long long K,
+                __half* const* a2, const float* sa, long long lda, __half* const* b2,
+                const float* sb, long long ldb, int lower, float alpha, float beta,
+                cudaStream_t st) {
   if (M <= 0 || N <= 0 || K <= 0 || !tc::encode_fn()) return G2Q_ERR_UNSUPPORTED;
   tc::Maps mp{};
   bool ok = true;
-  for (int i = 0; i < 3 && ok; ++i)
-    ok = tc::make_map(&mp.a[i], a3[i], M, K, lda) && tc::make_map(&mp.b[i], b3[i], N, K, ldb);
+  for (int i = 0; i < 2 && ok; ++i)
+    ok = tc::make_map(&mp.a[i], a2[i], M, K, lda, true) &&
+         tc::make_map(&mp.b[i], b2[i], N, K, ldb, true);
   if (!ok) return G2Q_ERR_UNSUPPORTED;
   tc::Params p{};
   p.D = D; p.ldd = ldd; p.d_bs = 0;
@@ -914,8 +966,10 @@ int tc_update3(float* D, long long ldd, long long M, long long N, long long K,
   p.num_kb = (int)((K + tc::BK - 1) / tc::BK);
   p.alpha = alpha; p.beta = beta;
   p.lower = lower;
+  p.f16 = 1;
+  p.sa = sa; p.sb = sb;
   p.red = (alpha == 1.f && tc::make_map_out(&mp.d, D, N, M, 1, ldd, 0)) ? 1 : 0;
-  return tc::dispatch(3, 3, mp, p, 1, st);
+  return tc::dispatch(2, 2, mp, p, 1, st);
 }
 
 }  // namespace g2q
