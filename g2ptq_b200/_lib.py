@@ -11,7 +11,7 @@ import os
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.environ.get("G2PTQ_B200_LIB", os.path.join(_HERE, "_lib", "libg2ptq_b200.so"))
 
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 G2Q_OK = 0
 G2Q_ERR_INVALID_ARG = -1
@@ -32,6 +32,14 @@ I32 = ctypes.c_int
 F32 = ctypes.c_float
 SZ = ctypes.c_size_t
 
+
+class ClipConfig(ctypes.Structure):
+    """``g2q_clip_t``: the clip search of ``find_params`` (--w_clip / --w_hclip)."""
+    _fields_ = [("grid", ctypes.c_int), ("maxshrink", ctypes.c_float),
+                ("norm", ctypes.c_float), ("hdiag", ctypes.c_void_p),
+                ("hdiag_ld", ctypes.c_int64), ("rows_per_block", ctypes.c_int64)]
+
+
 # name -> argtypes (every entry point returns int unless listed in _RESTYPES)
 SIGNATURES = {
     "g2q_abi_version": [],
@@ -47,11 +55,12 @@ SIGNATURES = {
     "g2q_chol_upper_inverse": [P, P, I64, I64, I64, P, P, I32, P, SZ, P],
     "g2q_chol_workspace_bytes": [I64],
     "g2q_find_params": [P, P, I64, P, I64, I64, I64, I32, I32, P, P],
+    "g2q_find_params_clip": [P, P, I64, P, I64, I64, I64, I32, I32, P, P, P],
     "g2q_fake_quantize": [P, I64, P, I64, P, I64, I64, I64, P, P, I64, P, I32, P],
     "g2q_compensate_block": [I32, P, I64, I64, I64, I64, I64, P, I64, I64, P, P, I64, P, I32, P,
                              P, P, P, P, P],
     "g2q_compensate": [I32, P, I64, I64, I64, P, P, P, I64, P, I32, I32, I32, I32, I32, P, P, P,
-                       P, I32, P, SZ, P, P],
+                       P, P, I32, P, SZ, P, P],
     "g2q_compensate_workspace_bytes": [I32, I64, I64, I64, I32],
     "g2q_prepare_hessian": [P, I64, I64, P, I64, P, I64, P, P],
     "g2q_argsort_desc": [P, P, I64, P],

@@ -311,17 +311,183 @@ __global__ void find_params_kernel(float* scale, float* zero, long long param_ld
   }
 }
 
+// WeightQuantizer.find_params with the clip search (quant_utils.py:406-425):
+// the range [xmin, xmax] of a (row, group) is shrunk on a grid,
+// xmin * (1 - i / grid) and xmax * (1 - j / grid) for i, j < maxshrink * grid,
+// and the first pair with the smallest error is kept; the error is
+// sum |fq - x|^norm, or sum (fq - x)^2 h_c with the Hessian diagonal (hclip).
+// One warp per (row, group); the group's values sit in registers (8 per lane)
+// when it has at most 256 columns, else they are re-read for every candidate.
+// For symmetric quantizers the scale of pair (i, j) is max(a_i, b_j) / half,
+// so only the 2n distinct values are evaluated and the (i, j) walk then picks
+// from them in the reference's order (equal values give equal errors).
+constexpr int CLIP_EPL = 8;
+constexpr int CLIP_MAXN = 64;
+
+struct ClipArgs {
+  int grid;
+  float maxshrink;
+  float norm;
+  const float* hdiag;  // optional, [row blocks][hdiag_ld], column c of the group at c
+  long long hdiag_ld;
+  long long rows_per_block;
+};
+
+__device__ __forceinline__ float clip_err(const float (&xv)[CLIP_EPL], const float (&hv)[CLIP_EPL],
+                                          const float* x, const float* hd, int nc, int lane,
+                                          bool in_regs, float s, float z, float qlo, float qhi,
+                                          float norm) {
+  float e = 0.f;
+  if (in_regs) {
+#pragma unroll
+    for (int k = 0; k < CLIP_EPL; ++k) {
+      const int c = lane + 32 * k;
+      if (c >= nc) break;
+      const float q = fminf(fmaxf(rintf(xv[k] / s) + z, qlo), qhi);
+      const float d = s * (q - z) - xv[k];
+      e += hd ? (d * d) * hv[k] : powf(fabsf(d), norm);
+    }
+  } else {
+    for (int c = lane; c < nc; c += 32) {
+      const float q = fminf(fmaxf(rintf(x[c] / s) + z, qlo), qhi);
+      const float d = s * (q - z) - x[c];
+      e += hd ? (d * d) * hd[c] : powf(fabsf(d), norm);
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) e += __shfl_xor_sync(0xffffffffu, e, o);
+  return e;
+}
+
+__global__ void find_params_clip_kernel(float* scale, float* zero, long long param_ld,
+                                        const float* W, long long rows, long long cols,
+                                        long long ldw, int bits, int sym, int* status,
+                                        long long first_start, int groupsize, long long C,
+                                        ClipArgs ca) {
+  __shared__ float ebuf[8][2 * CLIP_MAXN];
+  const int wib = threadIdx.x >> 5;
+  const long long r = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int gi = blockIdx.y;
+  if (r >= rows) return;  // whole warps leave together
+  long long c0 = 0, ncl = cols;
+  long long pc = 0;
+  if (first_start >= 0) {
+    c0 = first_start + (long long)gi * groupsize;
+    ncl = (C - c0) < groupsize ? (C - c0) : groupsize;
+    pc = c0 / groupsize;
+  }
+  const int nc = (int)ncl;
+  const float* x = W + r * ldw + c0;
+  const float* hd = ca.hdiag ? ca.hdiag + (r / ca.rows_per_block) * ca.hdiag_ld + c0 : nullptr;
+  const bool in_regs = nc <= 32 * CLIP_EPL;
+  float xv[CLIP_EPL], hv[CLIP_EPL];
+  float mn = INFINITY, mx = -INFINITY;
+#pragma unroll
+  for (int k = 0; k < CLIP_EPL; ++k) {
+    const int c = lane + 32 * k;
+    xv[k] = (in_regs && c < nc) ? x[c] : 0.f;
+    hv[k] = (in_regs && hd && c < nc) ? hd[c] : 0.f;
+  }
+  for (int c = lane; c < nc; c += 32) {
+    const float v = x[c];
+    mn = fminf(mn, v);
+    mx = fmaxf(mx, v);
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  }
+  const int maxq = (1 << (bits - 1)) - 1;
+  const int minq = -(maxq + 1);
+  const float bit_range = (float)(maxq - minq);
+  const float qlo = (float)minq, qhi = (float)maxq;
+  const float xmin = fminf(mn, 0.f), xmax = fmaxf(mx, 0.f);
+  float s, z;
+  params_from_range(xmin, xmax, bits, sym, &s, &z);
+  float best = INFINITY;
+  const int n = (int)((double)ca.maxshrink * ca.grid);
+  if (sym && n <= CLIP_MAXN) {
+    float* ea = ebuf[wib];
+    float* eb = ea + CLIP_MAXN;
+    for (int i = 0; i < n; ++i) {
+      const float f = (float)(1.0 - (double)i / ca.grid);
+      const float a = fabsf(f * xmin), b = f * xmax;
+      const float ia = clip_err(xv, hv, x, hd, nc, lane, in_regs, a / (bit_range / 2.f), 0.f,
+                                qlo, qhi, ca.norm);
+      const float ib = clip_err(xv, hv, x, hd, nc, lane, in_regs, b / (bit_range / 2.f), 0.f,
+                                qlo, qhi, ca.norm);
+      if (lane == 0) {
+        ea[i] = ia;
+        eb[i] = ib;
+      }
+    }
+    __syncwarp();
+    for (int i = 0; i < n; ++i) {
+      const float a = fabsf((float)(1.0 - (double)i / ca.grid) * xmin);
+      for (int j = 0; j < n; ++j) {
+        const float b = (float)(1.0 - (double)j / ca.grid) * xmax;
+        const float e = a >= b ? ea[i] : eb[j];
+        if (e < best) {
+          best = e;
+          s = fmaxf(a, b) / (bit_range / 2.f);
+          z = 0.f;
+        }
+      }
+    }
+  } else {
+    for (int i = 0; i < n; ++i) {
+      const float xmin1 = (float)(1.0 - (double)i / ca.grid) * xmin;
+      for (int j = 0; j < n; ++j) {
+        const float xmax1 = (float)(1.0 - (double)j / ca.grid) * xmax;
+        float s1, z1;
+        if (sym) {
+          s1 = fmaxf(fabsf(xmin1), xmax1) / (bit_range / 2.f);
+          z1 = 0.f;
+        } else {
+          s1 = (xmax1 - xmin1) / bit_range;
+          z1 = fminf(fmaxf(rintf((float)minq - xmin1 / s1), qlo), qhi);
+        }
+        const float e = clip_err(xv, hv, x, hd, nc, lane, in_regs, s1, z1, qlo, qhi, ca.norm);
+        if (e < best) {
+          best = e;
+          s = s1;
+          z = z1;
+        }
+      }
+    }
+  }
+  if (lane == 0) {
+    scale[r * param_ld + pc] = s;
+    zero[r * param_ld + pc] = rintf(z);
+    if (!(s > 0.f)) record_error(status, G2Q_ERR_BAD_SCALE);
+  }
+}
+
 static int launch_find_params(float* scale, float* zero, long long param_ld, const float* W,
                               long long rows, long long cols, long long ldw, int bits, int sym,
                               int* status, long long first_start, int ngs, int groupsize,
-                              long long C, cudaStream_t st) {
+                              long long C, const g2q_clip_t* clip, cudaStream_t st) {
   if (rows <= 0) return G2Q_OK;
   const int warps_per_block = 8;
   dim3 grid(cdiv(rows, warps_per_block), first_start >= 0 ? ngs : 1);
-  find_params_kernel<<<grid, 32 * warps_per_block, 0, st>>>(
-      scale, zero, param_ld, W, rows, cols, ldw, bits, sym, status, first_start, groupsize, C);
+  if (grid.y > 65535u) return G2Q_ERR_INVALID_ARG;
+  if (clip) {
+    ClipArgs ca{clip->grid, clip->maxshrink, clip->norm, clip->hdiag, clip->hdiag_ld,
+                clip->rows_per_block > 0 ? clip->rows_per_block : rows};
+    find_params_clip_kernel<<<grid, 32 * warps_per_block, 0, st>>>(
+        scale, zero, param_ld, W, rows, cols, ldw, bits, sym, status, first_start, groupsize, C,
+        ca);
+  } else {
+    find_params_kernel<<<grid, 32 * warps_per_block, 0, st>>>(
+        scale, zero, param_ld, W, rows, cols, ldw, bits, sym, status, first_start, groupsize, C);
+  }
   G2Q_CHECK_LAUNCH();
   return G2Q_OK;
+}
+
+static bool clip_ok(const g2q_clip_t* clip) {
+  return !clip || (clip->grid > 0 && clip->maxshrink >= 0.f && clip->maxshrink < 1.f &&
+                   (!clip->hdiag || (clip->hdiag_ld >= 0 && clip->rows_per_block > 0)));
 }
 
 __global__ void fake_quantize_kernel(float* out, long long ldo, int8_t* codes, long long ldq,
@@ -372,7 +538,17 @@ extern "C" int g2q_find_params(float* scale, float* zero, int64_t param_ld, cons
   if (!scale || !zero || !W || rows < 0 || cols <= 0 || ldw < cols || bits < 1 || bits > 16)
     return G2Q_ERR_INVALID_ARG;
   return launch_find_params(scale, zero, param_ld, W, rows, cols, ldw, bits, sym, status,
-                            -1, 1, 0, cols, (cudaStream_t)stream);
+                            -1, 1, 0, cols, nullptr, (cudaStream_t)stream);
+}
+
+extern "C" int g2q_find_params_clip(float* scale, float* zero, int64_t param_ld, const float* W,
+                                    int64_t rows, int64_t cols, int64_t ldw, int bits, int sym,
+                                    const g2q_clip_t* clip, int* status, void* stream) {
+  if (!scale || !zero || !W || !clip || rows < 0 || cols <= 0 || ldw < cols || bits < 1 ||
+      bits > 16 || !clip_ok(clip))
+    return G2Q_ERR_INVALID_ARG;
+  return launch_find_params(scale, zero, param_ld, W, rows, cols, ldw, bits, sym, status,
+                            -1, 1, 0, cols, clip, (cudaStream_t)stream);
 }
 
 extern "C" int g2q_fake_quantize(float* out, int64_t ldo, int8_t* codes, int64_t ldq,
@@ -443,12 +619,14 @@ extern "C" int g2q_compensate(int method, float* W, int64_t nl, int64_t rows, in
                               const float* U, float* scale, float* zero, int64_t ngroups,
                               const int* colgroup, int dynamic_groups, int groupsize, int bits,
                               int sym, int blocksize, int8_t* codes, const float* z, float* gh,
-                              const float* p, int precision, void* workspace,
-                              size_t workspace_bytes, int* status, void* stream) {
+                              const float* p, const g2q_clip_t* clip, int precision,
+                              void* workspace, size_t workspace_bytes, int* status,
+                              void* stream) {
   if (!W || !U || !scale || !zero || !colgroup || !codes || nl <= 0 || rows <= 0 || C <= 0 ||
       blocksize <= 0 || blocksize > BLK || bits < 1 || bits > 8 || !workspace)
     return G2Q_ERR_INVALID_ARG;
   if (dynamic_groups && groupsize <= 0) return G2Q_ERR_INVALID_ARG;
+  if (!clip_ok(clip)) return G2Q_ERR_INVALID_ARG;
   if (method == G2Q_METHOD_G2PTQ && (!z || !gh)) return G2Q_ERR_INVALID_ARG;
   if (method == G2Q_METHOD_GPTAQ && !p) return G2Q_ERR_INVALID_ARG;
   if (precision != 0 && precision != 1) return G2Q_ERR_INVALID_ARG;
@@ -484,7 +662,7 @@ extern "C" int g2q_compensate(int method, float* W, int64_t nl, int64_t rows, in
       const int cnt = first < i2 ? (int)((i2 - 1 - first) / groupsize + 1) : 0;
       if (cnt > 0)
         G2Q_TRY(launch_find_params(scale, zero, ngroups, W, nl * rows, 0, C, bits, sym, status,
-                                   first, cnt, groupsize, C, st));
+                                   first, cnt, groupsize, C, clip, st));
     }
     BlockParams P{};
     P.W = W + i1; P.ldw = C; P.w_bs = rows * C;

@@ -179,6 +179,26 @@ class ParamSet:
         return (idx // self.groupsize).to(torch.int32).contiguous()
 
 
+def hessian_diag(H, quantizer):
+    """``torch.diagonal(H).clone()`` when the quantizers use ``hclip`` (the
+    reference takes it before the dead-column / damping edits), else None."""
+    if not quantizer.hclip:
+        return None
+    return torch.diagonal(H, dim1=-2, dim2=-1).reshape(-1, H.shape[-1]).clone()
+
+
+def dynamic_clip(quantizer, H_diag, perm, total_rows, columns):
+    """Clip-search configuration for parameters found during the traversal
+    (dynamic groups), with the diagonal in the traversal's column order.
+    Returns ``(config or None, tensor to keep alive)``."""
+    if not quantizer.mse:
+        return None, None
+    hd = H_diag
+    if hd is not None and perm is not None:
+        hd = hd[:, perm].contiguous()
+    return quantizer.clip_config(hd, total_rows, columns), hd
+
+
 def act_order_perm(key):
     """``torch.argsort(key, descending=True)`` (stable) and its inverse."""
     perm = ops.argsort_desc(key.contiguous())

@@ -146,8 +146,6 @@ class G2PTQ(_engine.StagingMixin):
         rps = R // G
         nl = B * G
         q0 = self.quantizer[0]
-        if q0.hclip:
-            raise NotImplementedError("g2ptq_b200: --w_hclip needs the clip search")
         W = torch.stack([l.weight.data for l in self.layers]).float().contiguous()
         W_flat = W.view(B * R, C)
         W_sub = W.view(nl, rps, C)
@@ -155,16 +153,18 @@ class G2PTQ(_engine.StagingMixin):
             grad = self.gradients.to(self.dev, copy=True).view(nl, rps, C).contiguous()
             H = self.H.view(nl, C, C)
             self.H = None
+        H_diag = _engine.hessian_diag(H, q0)
         params = _engine.ParamSet(self.quantizer, B * R, C, groupsize, self.dev)
         dynamic = not (groupsize == -1 or static_groups)
         if not dynamic:
-            params.init_static(W_flat)
+            params.init_static(W_flat, H_diag)
         ops.prepare_hessian(H, W_sub, gzero=grad)
         use_grad = enable_gradient_update and alpha > 0
         Q_sub = None
         if use_grad:
             if dynamic:
                 for i, q in enumerate(self.quantizer):
+                    # g2ptq_utils.py:405-412 passes no Hessian diagonal here
                     q.find_params(W_sub[:, :, i * groupsize:(i + 1) * groupsize]
                                   .reshape(B * R, -1))
             Q_sub = fake_quantize_grouped(self.quantizer, W_sub, groupsize).contiguous()
@@ -176,6 +176,8 @@ class G2PTQ(_engine.StagingMixin):
             grad = ops.permute_cols(grad, perm)
             if Q_sub is not None:
                 Q_sub = ops.permute_cols(Q_sub, perm)
+        clip, clip_hd = _engine.dynamic_clip(q0, H_diag, perm, B * R, C) if dynamic else (None,
+                                                                                          None)
         U, info, damps = _engine.factor_with_retry(H, percdamp)
         colgroup = params.colgroup(perm, static_groups, self.dev)
         W0 = W_sub.contiguous()
@@ -194,7 +196,8 @@ class G2PTQ(_engine.StagingMixin):
             GH = ops.gemm(torch.empty_like(grad), Z, U)
             ops.compensate(_lib.METHOD_G2PTQ, Wp, U, params.scale, params.zero, colgroup,
                            dynamic, groupsize, q0.bits, q0.sym, blocksize, codes, z=Z, gh=GH,
-                           status=params.status, precision=_engine.PRECISION)
+                           status=params.status, precision=_engine.PRECISION, clip=clip)
+            _ = clip_hd  # the diagonal the clip configuration points to stays alive
             Q, cq = Wp, codes
             if actorder:
                 Q = ops.permute_cols(Wp, perm, inverse=True)

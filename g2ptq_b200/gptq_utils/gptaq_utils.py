@@ -119,17 +119,16 @@ class GPTAQ(_engine.StagingMixin):
                    backend="torch", graph=False):
         B, R, C = self.num_layers, self.rows, self.columns
         q0 = self.quantizer[0]
-        if q0.hclip:
-            raise NotImplementedError("g2ptq_b200: --w_hclip needs the clip search")
         with self._maybe_onload_hessian():
             H = self.H
             dX = self.dXXT
             self.H = None
+        H_diag = _engine.hessian_diag(H, q0)
         W = torch.stack([l.weight.data for l in self.layers]).float().contiguous()
         params = _engine.ParamSet(self.quantizer, B * R, C, groupsize, self.dev)
         dynamic = not (groupsize == -1 or static_groups)
         if not dynamic:
-            params.init_static(W.view(B * R, C))
+            params.init_static(W.view(B * R, C), H_diag)
         ops.prepare_hessian(H, W, extra=dX)
         perm = None
         if actorder:
@@ -137,6 +136,8 @@ class GPTAQ(_engine.StagingMixin):
             W = ops.permute_cols(W, perm)
             H = ops.permute_sym(H, perm)
             dX = ops.permute_sym(dX, perm)
+        clip, clip_hd = _engine.dynamic_clip(q0, H_diag, perm, B * R, C) if dynamic else (None,
+                                                                                          None)
         U, info, damps = _engine.factor_with_retry(H, percdamp)
         colgroup = params.colgroup(perm, static_groups, self.dev)
         codes = torch.empty(B, R, C, dtype=torch.int8, device=self.dev)
@@ -146,7 +147,8 @@ class GPTAQ(_engine.StagingMixin):
             P = ops.gemm(torch.empty_like(dX), T, U, beta=float(alpha))
             ops.compensate(_lib.METHOD_GPTAQ, Wp, U, params.scale, params.zero, colgroup,
                            dynamic, groupsize, q0.bits, q0.sym, blocksize, codes, p=P,
-                           status=params.status, precision=_engine.PRECISION)
+                           status=params.status, precision=_engine.PRECISION, clip=clip)
+            _ = clip_hd  # the diagonal the clip configuration points to stays alive
             Q, cq = Wp, codes
             if actorder:
                 Q = ops.permute_cols(Wp, perm, inverse=True)

@@ -82,23 +82,24 @@ class GPTQGuided(GPTQ):
         rps = R // G
         nl = B * G
         q0 = self.quantizer[0]
-        if q0.hclip:
-            raise NotImplementedError("g2ptq_b200: --w_hclip needs the clip search")
         W = torch.stack([l.weight.data for l in self.layers]).float().contiguous()
         with self._maybe_onload_hessian():
             H = self.H.view(nl, C, C)
             self.H = None
+        H_diag = _engine.hessian_diag(H, q0)
         W_sub = W.view(nl, rps, C)
         params = _engine.ParamSet(self.quantizer, B * R, C, groupsize, self.dev)
         dynamic = not (groupsize == -1 or static_groups)
         if not dynamic:
-            params.init_static(W.view(B * R, C))
+            params.init_static(W.view(B * R, C), H_diag)
         ops.prepare_hessian(H, W_sub)
         perm = None
         if actorder:
             perm, _ = _engine.act_order_perm(torch.mean(self.act_square, dim=0))
             W_sub = ops.permute_cols(W_sub, perm)
             H = ops.permute_sym(H, perm)
+        clip, clip_hd = _engine.dynamic_clip(q0, H_diag, perm, B * R, C) if dynamic else (None,
+                                                                                          None)
         U, info, damps = _engine.factor_with_retry(H, percdamp)
         colgroup = params.colgroup(perm, static_groups, self.dev)
         codes = torch.empty(nl, rps, C, dtype=torch.int8, device=self.dev)
@@ -106,7 +107,8 @@ class GPTQGuided(GPTQ):
         def run(Wp):
             ops.compensate(_lib.METHOD_GPTQ, Wp, U, params.scale, params.zero, colgroup,
                            dynamic, groupsize, q0.bits, q0.sym, blocksize, codes,
-                           status=params.status, precision=_engine.PRECISION)
+                           status=params.status, precision=_engine.PRECISION, clip=clip)
+            _ = clip_hd  # the diagonal the clip configuration points to stays alive
             Q, cq = Wp, codes
             if actorder:
                 Q = ops.permute_cols(Wp, perm, inverse=True)

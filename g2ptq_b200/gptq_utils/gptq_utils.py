@@ -105,24 +105,23 @@ class GPTQ(_engine.StagingMixin):
         """Enqueue the whole of fasterquant on the current stream (no host sync)."""
         B, R, C = self.num_layers, self.rows, self.columns
         q0 = self.quantizer[0]
-        hclip = q0.hclip
         with self._maybe_onload_hessian():
             H = self.H
             self.H = None
-        H_diag = torch.diagonal(H, dim1=-2, dim2=-1).clone() if hclip else None
+        H_diag = _engine.hessian_diag(H, q0)
         W = torch.stack([l.weight.data for l in self.layers]).float().contiguous()
         params = _engine.ParamSet(self.quantizer, B * R, C, groupsize, self.dev)
         dynamic = not (groupsize == -1 or static_groups)
         if not dynamic:
             params.init_static(W.view(B * R, C), H_diag)
-        if hclip and dynamic:
-            raise NotImplementedError("g2ptq_b200: --w_hclip needs the clip search")
         ops.prepare_hessian(H, W)
         perm = None
         if actorder:
             perm, _ = _engine.act_order_perm(ops.mean_diag(H))
             W = ops.permute_cols(W, perm)
             H = ops.permute_sym(H, perm)
+        clip, clip_hd = _engine.dynamic_clip(q0, H_diag, perm, B * R, C) if dynamic else (None,
+                                                                                          None)
         U, info, damps = _engine.factor_with_retry(H, percdamp)
         colgroup = params.colgroup(perm, static_groups, self.dev)
         codes = torch.empty(B, R, C, dtype=torch.int8, device=self.dev)
@@ -130,7 +129,8 @@ class GPTQ(_engine.StagingMixin):
         def run(Wp):
             ops.compensate(_lib.METHOD_GPTQ, Wp, U, params.scale, params.zero, colgroup, dynamic,
                            groupsize, q0.bits, q0.sym, blocksize, codes, status=params.status,
-                           precision=_engine.PRECISION)
+                           precision=_engine.PRECISION, clip=clip)
+            _ = clip_hd  # the diagonal the clip configuration points to stays alive
             Q, cq = Wp, codes
             if actorder:
                 Q = ops.permute_cols(Wp, perm, inverse=True)

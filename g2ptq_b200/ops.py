@@ -5,6 +5,8 @@ the current CUDA stream, allocates any workspace through the torch caching
 allocator and calls the library.  No function here computes anything itself.
 """
 
+import ctypes
+
 import torch
 
 from . import _lib
@@ -158,6 +160,33 @@ def find_params(scale, zero, W, bits, sym, status=None, param_col=0):
          W.stride(0), bits, int(bool(sym)), _ptr(status), _stream(W))
 
 
+def clip_config(grid=50, maxshrink=0.5, norm=2.4, hdiag=None, rows_per_block=None):
+    """``g2q_clip_t`` for the clip search; ``hdiag [blocks, C]`` (contiguous
+    rows) switches to the Hessian-weighted error, each block of
+    ``rows_per_block`` weight rows using one row of it."""
+    if hdiag is not None:
+        _cuda(hdiag)
+        if hdiag.dtype != torch.float32 or hdiag.stride(-1) != 1:
+            raise ValueError("hdiag must be fp32 with unit column stride")
+    return _lib.ClipConfig(int(grid), float(maxshrink), float(norm),
+                           None if hdiag is None else hdiag.data_ptr(),
+                           0 if hdiag is None else hdiag.stride(0),
+                           0 if hdiag is None else int(rows_per_block))
+
+
+def find_params_clip(scale, zero, W, bits, sym, clip, status=None, param_col=0):
+    """``find_params`` with the clip search ``clip`` (a ``clip_config``)."""
+    _cuda(scale, zero, W, status)
+    rows, cols = W.shape
+    if W.stride(1) != 1:
+        raise ValueError("find_params expects unit column stride")
+    sp = scale[:, param_col] if scale.dim() == 2 else scale
+    zp = zero[:, param_col] if zero.dim() == 2 else zero
+    pld = scale.stride(0) if scale.dim() == 2 else 1
+    call("g2q_find_params_clip", sp.data_ptr(), zp.data_ptr(), pld, W.data_ptr(), rows, cols,
+         W.stride(0), bits, int(bool(sym)), ctypes.byref(clip), _ptr(status), _stream(W))
+
+
 def fake_quantize(W, scale, zero, maxq, colmap=None, out=None, codes=None):
     """Per-element quantize/dequantize of ``W [rows, cols]`` with parameters
     ``scale[r, colmap[c]]`` (``colmap`` None: column 0 of the parameters)."""
@@ -189,8 +218,9 @@ def compensate_block(method, W, hinv, scale, zero, colmap, maxq, codes=None, err
 
 
 def compensate(method, W, U, scale, zero, colgroup, dynamic_groups, groupsize, bits, sym,
-               blocksize, codes, z=None, gh=None, p=None, status=None, precision=0):
-    """Whole block traversal (``_run_compensation``); ``W [nl, rows, C]`` -> Q in place."""
+               blocksize, codes, z=None, gh=None, p=None, status=None, precision=0, clip=None):
+    """Whole block traversal (``_run_compensation``); ``W [nl, rows, C]`` -> Q in place.
+    ``clip`` (a ``clip_config``) selects the clip search for dynamic groups."""
     _cuda(W, U, scale, zero, colgroup, codes, z, gh, p, status)
     _contig(W, U, scale, zero, colgroup, codes, z, gh, p)
     nl, rows, C = W.shape
@@ -199,7 +229,8 @@ def compensate(method, W, U, scale, zero, colgroup, dynamic_groups, groupsize, b
     call("g2q_compensate", method, W.data_ptr(), nl, rows, C, U.data_ptr(), scale.data_ptr(),
          zero.data_ptr(), scale.shape[1], colgroup.data_ptr(), int(bool(dynamic_groups)),
          int(groupsize), int(bits), int(bool(sym)), int(blocksize), codes.data_ptr(), _ptr(z),
-         _ptr(gh), _ptr(p), precision, ws.data_ptr(), ws_bytes, _ptr(status), _stream(W))
+         _ptr(gh), _ptr(p), None if clip is None else ctypes.byref(clip), precision,
+         ws.data_ptr(), ws_bytes, _ptr(status), _stream(W))
 
 
 # --------------------------------------------------------------------------

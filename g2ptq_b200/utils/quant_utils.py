@@ -67,8 +67,25 @@ class WeightQuantizer(torch.nn.Module):
             self._status = torch.zeros(1, dtype=torch.int32, device=device)
         return self._status
 
+    def clip_config(self, H_diag, rows, cols):
+        """The clip search of ``find_params`` (quant_utils.py:385-425) as a
+        ``g2q_clip_t``, or None without ``mse``.  ``H_diag`` (``[blocks, cols]``,
+        used with ``hclip``) weights the error by the Hessian diagonal of each
+        block of ``rows / blocks`` rows; a constant diagonal falls back to the
+        ``|fq - x|^norm`` error, as in the reference."""
+        if not self.mse:
+            return None
+        hd = None
+        if self.hclip and H_diag is not None:
+            hd = H_diag.to(device="cuda" if not H_diag.is_cuda else H_diag.device,
+                           dtype=torch.float32).reshape(H_diag.shape[0], cols).contiguous()
+            if bool((hd.min() == hd.max()).item()):
+                hd = None
+        return ops.clip_config(self.grid, self.maxshrink, self.norm, hd,
+                               None if hd is None else rows // hd.shape[0])
+
     def find_params(self, x, H_diag=None, out=None) -> None:
-        """quant_utils.py:377-433 (min/max parameters).
+        """quant_utils.py:377-433, with the ``mse`` / ``hclip`` clip search.
 
         ``out`` -- optional ``(scale, zero)`` pair of ``[rows, 1]`` views to
         write into (used by the layer-batched quantizer objects so that all
@@ -76,9 +93,6 @@ class WeightQuantizer(torch.nn.Module):
         """
         if self.bits == 16:
             return
-        if self.mse:
-            raise NotImplementedError(
-                "g2ptq_b200: the --w_clip / --w_hclip grid search is not implemented yet")
         if not x.is_cuda:
             raise RuntimeError("g2ptq_b200 WeightQuantizer requires CUDA tensors")
         x = x.float() if x.dtype != torch.float32 else x
@@ -86,12 +100,20 @@ class WeightQuantizer(torch.nn.Module):
         status = self.status_tensor(x.device)
         if self.weight_groupsize > 0:
             ng = cols // self.weight_groupsize
+            gs = self.weight_groupsize
             scale = torch.empty(rows, ng, dtype=torch.float32, device=x.device)
             zero = torch.empty_like(scale)
             for g in range(ng):
-                ops.find_params(scale, zero,
-                                x[:, g * self.weight_groupsize:(g + 1) * self.weight_groupsize],
-                                self.bits, self.sym, status, param_col=g)
+                xg = x[:, g * gs:(g + 1) * gs]
+                clip = self.clip_config(
+                    None if H_diag is None
+                    else H_diag.reshape(H_diag.shape[0], cols)[:, g * gs:(g + 1) * gs],
+                    rows, gs)
+                if clip is None:
+                    ops.find_params(scale, zero, xg, self.bits, self.sym, status, param_col=g)
+                else:
+                    ops.find_params_clip(scale, zero, xg, self.bits, self.sym, clip, status,
+                                         param_col=g)
         else:
             if not self.perchannel:
                 x = x.reshape(1, -1)
@@ -103,7 +125,11 @@ class WeightQuantizer(torch.nn.Module):
             else:
                 scale = torch.empty(rows, 1, dtype=torch.float32, device=x.device)
                 zero = torch.empty_like(scale)
-            ops.find_params(scale, zero, x, self.bits, self.sym, status)
+            clip = self.clip_config(H_diag, rows, x.shape[1])
+            if clip is None:
+                ops.find_params(scale, zero, x, self.bits, self.sym, status)
+            else:
+                ops.find_params_clip(scale, zero, x, self.bits, self.sym, clip, status)
         self.scale = scale
         self.zero = zero
         self._ready = True

@@ -164,6 +164,29 @@ int g2q_find_params(float* scale, float* zero, int64_t param_ld,
                     const float* W, int64_t rows, int64_t cols, int64_t ldw,
                     int bits, int sym, int* status, void* stream);
 
+/* Clip search of WeightQuantizer.find_params (--w_clip / --w_hclip).  The
+ * range [xmin, xmax] is shrunk on a grid, xmin * (1 - i/grid) and
+ * xmax * (1 - j/grid) for i, j < maxshrink * grid, and the first (i, j) with
+ * the smallest error over the row's columns is kept: sum |fq - x|^norm, or,
+ * with hdiag, sum (fq - x)^2 * hdiag[(r / rows_per_block) * hdiag_ld + c]
+ * (the Hessian diagonal of the row's block).  Defaults of the reference:
+ * grid 50, maxshrink 0.5, norm 2.4. */
+typedef struct {
+  int grid;
+  float maxshrink;
+  float norm;
+  const float* hdiag;      /* NULL: the |fq - x|^norm error */
+  int64_t hdiag_ld;
+  int64_t rows_per_block;  /* rows sharing one hdiag row */
+} g2q_clip_t;
+
+/* g2q_find_params with the clip search above.
+ * Replaces WeightQuantizer.find_params with mse=True (and hclip),
+ * utils/quant_utils.py:373-425 (_mse_step_sym/_asym :106-133). */
+int g2q_find_params_clip(float* scale, float* zero, int64_t param_ld, const float* W,
+                         int64_t rows, int64_t cols, int64_t ldw, int bits, int sym,
+                         const g2q_clip_t* clip, int* status, void* stream);
+
 /* Fake quantization  q = clamp(round(w / s) + z, -(maxq+1), maxq),
  * out = s * (q - z)  with per-element parameters s = scale[r*param_ld + colmap[c]].
  * Writes out (fp32, row stride ldo) and, when codes is non-NULL, int8 codes.
@@ -205,8 +228,10 @@ int g2q_compensate_block(int method, float* W, int64_t ldw, int64_t w_bstride,
  * column of (permuted) column c.  codes: [nl, rows, C] int8 output.
  * G2PTQ: z [nl, rows, C] read, gh [nl, rows, C] updated.  GPTAQ: p [nl, C, C].
  * precision: 0 = fp32 CUDA-core trailing update, 1 = tensor cores
- * (bf16x3 split).  Needs g2q_compensate_workspace_bytes bytes; *status
- * receives G2Q_ERR_BAD_SCALE on a non-positive dynamic scale.
+ * (bf16x3 split).  clip (NULL: plain min/max) selects the clip search for
+ * the dynamic group parameters, its hdiag indexed by the permuted column.
+ * Needs g2q_compensate_workspace_bytes bytes; *status receives
+ * G2Q_ERR_BAD_SCALE on a non-positive dynamic scale.
  * Replaces GPTQ._run_compensation (gptq_utils/gptq_utils.py:165-232),
  * G2PTQ._run_compensation (gptq_utils/g2ptq_utils.py:252-347) and
  * GPTAQ._run_compensation (gptq_utils/gptaq_utils.py:193-261). */
@@ -214,8 +239,9 @@ int g2q_compensate(int method, float* W, int64_t nl, int64_t rows, int64_t C,
                    const float* U, float* scale, float* zero, int64_t ngroups,
                    const int* colgroup, int dynamic_groups, int groupsize, int bits, int sym,
                    int blocksize, int8_t* codes,
-                   const float* z, float* gh, const float* p, int precision,
-                   void* workspace, size_t workspace_bytes, int* status, void* stream);
+                   const float* z, float* gh, const float* p, const g2q_clip_t* clip,
+                   int precision, void* workspace, size_t workspace_bytes, int* status,
+                   void* stream);
 size_t g2q_compensate_workspace_bytes(int method, int64_t nl, int64_t rows, int64_t C,
                                       int precision);
 
