@@ -39,6 +39,15 @@ LINEARS = [  # name, rows, columns, input group
 GROUP_COLS = {"attn": HIDDEN, "o": HEADS * HEAD_DIM, "mlp": HIDDEN, "down": INTER}
 BITS, GROUPSIZE, PERCDAMP, BLOCKSIZE = 4, 128, 0.01, 128
 METRIC = "linear layers quantized/sec"
+# BASELINE configs[1] (GPTQ, the headline) and configs[2] (G2PTQ)
+METHODS = {
+    "gptq": dict(bits=4, sym=True, label="GPTQ W4 sym g128 act-order",
+                 fq=dict(groupsize=GROUPSIZE, actorder=True, static_groups=True)),
+    "g2ptq": dict(bits=3, sym=False, label="G2PTQ W3 asym g128, 4 row groups, trust radius 1.0",
+                  fq=dict(groupsize=GROUPSIZE, actorder=False, static_groups=False,
+                          enable_gradient_update=True, alpha=1.0)),
+}
+G2_GROUPS = 4
 
 
 def parse():
@@ -53,6 +62,8 @@ def parse():
                     help="0: fp32 CUDA-core products, 1: tcgen05 tensor cores")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--method", default="gptq", choices=sorted(METHODS),
+                    help="gptq: BASELINE configs[1] (default); g2ptq: configs[2]")
     return ap.parse_args()
 
 
@@ -144,6 +155,27 @@ def make_inputs(torch, dev, rank, world, seqs, seq_len):
     return acts, n
 
 
+def make_g2ptq_inputs(torch, dev, acts, n_local, seq_len, seed):
+    """Saliency and gradient inputs of G2PTQ from synthetic per-token
+    output gradients N(0, 1e-3) BF16 [tokens, rows] of every linear:
+    s[n, g] = mean over the rows of group g of grad_out[n, r]^2 (the saliency
+    cache, g2ptq_utils.py:611-618) and the weight gradient = mean over sequences of
+    grad_out^T X / tokens (g2ptq_utils.py:704-714).  Made once, outside the timed
+    region (the reference's refresh step that produces them is not on the path)."""
+    g = torch.Generator(device=dev).manual_seed(seed)
+    sal, grad = {}, {}
+    for name, rows, cols, grp in LINEARS:
+        sal[name] = []
+        acc = torch.zeros(rows, cols, device=dev, dtype=torch.float32)
+        for s in range(n_local):
+            go = (torch.randn(seq_len, rows, device=dev, generator=g) * 1e-3).to(torch.bfloat16)
+            gf = go.float()
+            sal[name].append((gf * gf).reshape(seq_len, G2_GROUPS, rows // G2_GROUPS).mean(-1))
+            acc += (go.T @ acts[grp][s]).float() / seq_len
+        grad[name] = acc / n_local
+    return {"sal": sal, "grad": grad}
+
+
 def make_layers(torch, dev):
     g = torch.Generator(device=dev).manual_seed(42)
     layers = {}
@@ -155,15 +187,21 @@ def make_layers(torch, dev):
     return layers
 
 
-def one_step(torch, layers, acts, n_local, world, rank, dist, obj2rank=None, h2d=None):
+def one_step(torch, layers, acts, n_local, world, rank, dist, method="gptq", g2=None):
     """add_batch over the rank's sequences, reduce to owners, fasterquant, broadcast."""
-    from g2ptq_b200.gptq_utils import gptq_utils, common_utils
+    from g2ptq_b200.gptq_utils import gptq_utils, g2ptq_utils, common_utils
     from g2ptq_b200.utils.quant_utils import WeightQuantizer
+    cfg = METHODS[method]
+    mod = g2ptq_utils if method == "g2ptq" else gptq_utils
     objs = {}
     for name, rows, cols, grp in LINEARS:
-        obj = gptq_utils.GPTQ([layers[name]])
+        if method == "g2ptq":
+            obj = g2ptq_utils.G2PTQ([layers[name]], [list(g2["sal"][name])],
+                                    [g2["grad"][name]], num_groups=G2_GROUPS)
+        else:
+            obj = gptq_utils.GPTQ([layers[name]])
         q = WeightQuantizer()
-        q.configure(BITS, perchannel=True, sym=True, mse=False)
+        q.configure(cfg["bits"], perchannel=True, sym=cfg["sym"], mse=False)
         obj.quantizer = common_utils.make_group_quantizers(q, cols, GROUPSIZE)
         objs[name] = obj
     for s in range(n_local):
@@ -174,11 +212,10 @@ def one_step(torch, layers, acts, n_local, world, rank, dist, obj2rank=None, h2d
     if world > 1:
         specs = list(objs.values())
         _, _, obj2rank = common_utils.partition_layers(specs, world)
-        gptq_utils.reduce_to_target_rank(specs, obj2rank)
+        mod.reduce_to_target_rank(specs, obj2rank)
         owners = {k: o for k, o in objs.items() if obj2rank[o] == rank}
     gptq_utils.fasterquant_all(list(owners.values()), blocksize=BLOCKSIZE, percdamp=PERCDAMP,
-                               groupsize=GROUPSIZE, actorder=True, static_groups=True,
-                               export_compressed_tensors=True)
+                               export_compressed_tensors=True, **cfg["fq"])
     if world > 1:
         common_utils.broadcast_quantized_param(list(objs.values()), obj2rank,
                                                export_compressed_tensors=True)
@@ -244,6 +281,8 @@ def native(args):
     lib = _lib.load()
     layers = make_layers(torch, dev)
     acts, n_local = make_inputs(torch, dev, rank, world, args.seqs, args.seq_len)
+    g2 = (make_g2ptq_inputs(torch, dev, acts, n_local, args.seq_len, 44 + rank)
+          if args.method == "g2ptq" else None)
 
     def barrier():
         if world > 1:
@@ -251,7 +290,7 @@ def native(args):
         torch.cuda.synchronize()
 
     for _ in range(args.warmup):
-        one_step(torch, layers, acts, n_local, world, rank, dist)
+        one_step(torch, layers, acts, n_local, world, rank, dist, args.method, g2)
     barrier()
     timer = GramTimer(torch)
     timer.install()
@@ -264,7 +303,7 @@ def native(args):
     t0.record()
     torch.cuda.nvtx.range_push("timed")  # lets a profiler capture exactly the timed steps
     for _ in range(args.steps):
-        one_step(torch, layers, acts, n_local, world, rank, dist)
+        one_step(torch, layers, acts, n_local, world, rank, dist, args.method, g2)
     torch.cuda.nvtx.range_pop()
     t1.record()
     barrier()
@@ -281,7 +320,7 @@ def native(args):
 
     e2e = None
     if not args.no_e2e:
-        e2e = native_e2e(torch, dist, args, layers, world, rank, dev, n_local, acts)
+        e2e = native_e2e(torch, dist, args, layers, world, rank, dev, n_local, acts, g2)
     del acts
     hbm, bf16, peak_kind = load_peaks()
     value = len(LINEARS) / (ms * 1e-3)
@@ -291,7 +330,7 @@ def native(args):
         "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16-in/f32", "data": "synthetic",
         "config": {
-            "workload": "Llama-3-8B decoder layer (7 linears) GPTQ W4 sym g128 act-order, "
+            "workload": f"Llama-3-8B decoder layer (7 linears) {METHODS[args.method]['label']}, "
                         f"{args.seqs}x{args.seq_len} calibration tokens",
             "parallelism": f"tokens dp{world} + linear ownership (LPT)",
             "calibration_seconds_32_layers": round(N_LAYERS * ms * 1e-3, 3),
@@ -313,7 +352,7 @@ def native(args):
     }
     if e2e is not None:
         line["e2e"] = e2e
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.method == "gptq":
         line["cpu_baseline"] = cpu_baseline()
     if rank == 0:
         print(json.dumps(line), flush=True)
@@ -322,7 +361,7 @@ def native(args):
         dist.destroy_process_group()
 
 
-def native_e2e(torch, dist, args, layers, world, rank, dev, n_local, dev_acts):
+def native_e2e(torch, dist, args, layers, world, rank, dev, n_local, dev_acts, g2=None):
     """Same steps through the public API with host-resident inputs: every step
     copies its activations from pinned host memory and reads the quantized
     weights and packed codes back to the host.  The copies stream through a ring
@@ -342,8 +381,7 @@ def native_e2e(torch, dist, args, layers, world, rank, dev, n_local, dev_acts):
     h2d_bytes = sum(h.numel() * h.element_size() for h in host.values())
     outs = {name: torch.empty(rows, cols, dtype=torch.bfloat16, pin_memory=True)
             for name, rows, cols, _ in LINEARS}
-    packed = {name: torch.empty(rows, cols * BITS // 32, dtype=torch.int32, pin_memory=True)
-              for name, rows, cols, _ in LINEARS}
+    packed = {}  # pinned host copies of the packed codes, shaped on first use
     state = {"issued": 0, "consumed": 0}  # sequences copied / handed to add_batch so far
 
     def prefetch_upto(g_end):
@@ -367,7 +405,7 @@ def native_e2e(torch, dist, args, layers, world, rank, dev, n_local, dev_acts):
         return bufs[g % ring]
 
     def step():
-        one_step(torch, layers, feed, n_local, world, rank, dist)
+        one_step(torch, layers, feed, n_local, world, rank, dist, args.method, g2)
         # free the last buffer and keep the copies running into the next step
         free_ev[(state["consumed"] - 1) % ring].record()
         prefetch_upto(state["consumed"] + ring)
@@ -377,8 +415,11 @@ def native_e2e(torch, dist, args, layers, world, rank, dev, n_local, dev_acts):
             qp = layers[name].__dict__.get("_export_qparams")
             d2h += rows * cols * 2
             if qp is not None:
-                packed[name].copy_(qp["weight_packed"], non_blocking=True)
-                d2h += packed[name].numel() * 4
+                src = qp["weight_packed"]
+                if name not in packed:
+                    packed[name] = torch.empty(src.shape, dtype=src.dtype, pin_memory=True)
+                packed[name].copy_(src, non_blocking=True)
+                d2h += packed[name].numel() * packed[name].element_size()
         return d2h
 
     for _ in range(max(1, args.warmup)):

@@ -593,10 +593,12 @@ extern "C" size_t g2q_compensate_workspace_bytes(int method, int64_t nl, int64_t
                                                  int64_t C, int precision) {
   size_t b = (size_t)nl * rows * BLK * sizeof(float) + 256;
   if (precision == 1) {
-    b += 2 * (size_t)nl * rows * BLK * sizeof(__nv_bfloat16) + 256;  // erra hi/lo
-    b += 2 * (size_t)nl * C * C * sizeof(__nv_bfloat16) + 256;       // U hi/lo
-    if (method != G2Q_METHOD_GPTQ)
-      b += 2 * (size_t)nl * rows * C * sizeof(__nv_bfloat16) + 256;  // Z or -Q/P operands
+    b += 2 * (size_t)nl * rows * BLK * sizeof(__nv_bfloat16) + 512;  // erra hi/lo
+    b += 2 * (size_t)nl * C * C * sizeof(__nv_bfloat16) + 512;       // U hi/lo
+    if (method != G2Q_METHOD_GPTQ)  // Z (G2PTQ) or quantized (GPTAQ) block hi/lo
+      b += 2 * (size_t)nl * rows * BLK * sizeof(__nv_bfloat16) + 512;
+    if (method == G2Q_METHOD_GPTAQ)  // P hi/lo
+      b += 2 * (size_t)nl * C * C * sizeof(__nv_bfloat16) + 512;
   }
   return b;
 }
@@ -605,8 +607,11 @@ namespace g2q {
 int tc_trailing_update(float* W, long long C, long long rows, long long batch, long long i1,
                        long long i2, int nc, const __nv_bfloat16* err_hi,
                        const __nv_bfloat16* err_lo, long long err_stride,
-                       const __nv_bfloat16* u_hi, const __nv_bfloat16* u_lo, int* status,
-                       cudaStream_t st);
+                       const __nv_bfloat16* u_hi, const __nv_bfloat16* u_lo, float beta,
+                       int* status, cudaStream_t st);
+int split_block_t(const float* src, long long lds, long long src_bs, long long rows, int nc,
+                  long long batch, __nv_bfloat16* hi, __nv_bfloat16* lo, long long dst_bs,
+                  cudaStream_t st);
 int split_bf16_2d(__nv_bfloat16* hi, __nv_bfloat16* lo, const float* src, long long n,
                   cudaStream_t st);
 }  // namespace g2q
@@ -637,21 +642,33 @@ extern "C" int g2q_compensate(int method, float* W, int64_t nl, int64_t rows, in
   float* erra = (float*)wsp;
   wsp = align_up(wsp + (size_t)nl * rows * BLK * sizeof(float), 256);
   const int maxq = (1 << (bits - 1)) - 1;
-  // Tensor-core trailing update (GPTQ): bf16 hi/lo copies of the error block
-  // (column-major, written by the block kernel) and of U (split once here).
-  const bool use_tc = precision == 1 && method == G2Q_METHOD_GPTQ;
+  // Tensor-core trailing updates: bf16 hi/lo copies of the error block
+  // (column-major, written by the block kernel), of U (and GPTAQ's P, split
+  // once here) and, per block, of G2PTQ's Z block or GPTAQ's quantized block.
+  const bool use_tc = precision == 1;
   __nv_bfloat16 *ea_hi = nullptr, *ea_lo = nullptr, *u_hi = nullptr, *u_lo = nullptr;
+  __nv_bfloat16 *x_hi = nullptr, *x_lo = nullptr, *p_hi = nullptr, *p_lo = nullptr;
   if (use_tc) {
     const size_t ne = (size_t)nl * rows * BLK, nu = (size_t)nl * C * C;
-    ea_hi = (__nv_bfloat16*)wsp;
-    wsp = align_up(wsp + ne * 2, 256);
-    ea_lo = (__nv_bfloat16*)wsp;
-    wsp = align_up(wsp + ne * 2, 256);
-    u_hi = (__nv_bfloat16*)wsp;
-    wsp = align_up(wsp + nu * 2, 256);
-    u_lo = (__nv_bfloat16*)wsp;
-    wsp = align_up(wsp + nu * 2, 256);
+    auto take = [&](size_t n) {
+      __nv_bfloat16* q = (__nv_bfloat16*)wsp;
+      wsp = align_up(wsp + n * 2, 256);
+      return q;
+    };
+    ea_hi = take(ne);
+    ea_lo = take(ne);
+    u_hi = take(nu);
+    u_lo = take(nu);
     G2Q_TRY(split_bf16_2d(u_hi, u_lo, U, (long long)nu, st));
+    if (method != G2Q_METHOD_GPTQ) {
+      x_hi = take(ne);
+      x_lo = take(ne);
+    }
+    if (method == G2Q_METHOD_GPTAQ) {
+      p_hi = take(nu);
+      p_lo = take(nu);
+      G2Q_TRY(split_bf16_2d(p_hi, p_lo, p, (long long)nu, st));
+    }
   }
   for (long long i1 = 0; i1 < C; i1 += blocksize) {
     const long long i2 = (i1 + blocksize < C) ? i1 + blocksize : C;
@@ -686,10 +703,22 @@ extern "C" int g2q_compensate(int method, float* W, int64_t nl, int64_t rows, in
                                                                  (float)blocksize);
       G2Q_CHECK_LAUNCH();
     }
-    // W[:, i2:] -= Erra @ U[i1:i2, i2:]
+    // W[:, i2:] -= Erra @ U[i1:i2, i2:]  (+ G2PTQ: GH[:, i2:] -= Z[:, i1:i2] @ U[i1:i2, i2:];
+    // GPTAQ: W[:, i2:] += Q1 @ P[i1:i2, i2:])
     if (use_tc) {
-      const int s_tc = tc_trailing_update(W, C, rows, nl, i1, i2, nc, ea_hi, ea_lo, BLK, u_hi,
-                                          u_lo, status, st);
+      int s_tc = tc_trailing_update(W, C, rows, nl, i1, i2, nc, ea_hi, ea_lo, BLK, u_hi, u_lo,
+                                    -1.f, status, st);
+      if (s_tc == G2Q_OK && method == G2Q_METHOD_G2PTQ) {
+        G2Q_TRY(split_block_t(z + i1, C, rows * C, rows, nc, nl, x_hi, x_lo, BLK * rows, st));
+        s_tc = tc_trailing_update(gh, C, rows, nl, i1, i2, nc, x_hi, x_lo, BLK, u_hi, u_lo,
+                                  -1.f, status, st);
+        if (s_tc != G2Q_OK) return s_tc == G2Q_ERR_UNSUPPORTED ? G2Q_ERR_CUDA : s_tc;
+      } else if (s_tc == G2Q_OK && method == G2Q_METHOD_GPTAQ) {
+        G2Q_TRY(split_block_t(W + i1, C, rows * C, rows, nc, nl, x_hi, x_lo, BLK * rows, st));
+        s_tc = tc_trailing_update(W, C, rows, nl, i1, i2, nc, x_hi, x_lo, BLK, p_hi, p_lo, 1.f,
+                                  status, st);
+        if (s_tc != G2Q_OK) return s_tc == G2Q_ERR_UNSUPPORTED ? G2Q_ERR_CUDA : s_tc;
+      }
       if (s_tc == G2Q_OK) continue;
       if (s_tc != G2Q_ERR_UNSUPPORTED) return s_tc;
     }

@@ -841,16 +841,17 @@ int tc_gram(float* D, long long ldd, long long M, long long N, const void* A, in
   return tc::dispatch(na, nb, mp, p, 1, st);
 }
 
-// W[b][:, i2 + n] -= sum_k Err[b][k][m] * U[b][i1 + k][i2 + n] on tensor cores.
-// err_hi / err_lo: [batch][err_stride rows][rows] bf16 (column-major error
-// blocks), u_hi / u_lo: [batch][C][C] bf16.  Returns G2Q_ERR_UNSUPPORTED when
-// the shapes do not meet TMA's alignment rules (the caller then uses the
-// CUDA-core path).
+// W[b][:, i2 + n] += beta * sum_k Err[b][k][m] * U[b][i1 + k][i2 + n] on tensor
+// cores.  err_hi / err_lo: [batch][err_stride rows][rows] bf16 (column-major
+// blocks: the compensation error, G2PTQ's Z block or GPTAQ's quantized block),
+// u_hi / u_lo: [batch][C][C] bf16 (U, or GPTAQ's P).  Returns
+// G2Q_ERR_UNSUPPORTED when the shapes do not meet TMA's alignment rules (the
+// caller then uses the CUDA-core path).
 int tc_trailing_update(float* W, long long C, long long rows, long long batch, long long i1,
                        long long i2, int nc, const __nv_bfloat16* err_hi,
                        const __nv_bfloat16* err_lo, long long err_stride,
-                       const __nv_bfloat16* u_hi, const __nv_bfloat16* u_lo, int* status,
-                       cudaStream_t st) {
+                       const __nv_bfloat16* u_hi, const __nv_bfloat16* u_lo, float beta,
+                       int* status, cudaStream_t st) {
   if ((nc % tc::BK) || (i2 % 8) || (rows % 8) || (C % 8) || !tc::encode_fn())
     return G2Q_ERR_UNSUPPORTED;
   tc::Maps mp{};
@@ -866,11 +867,51 @@ int tc_trailing_update(float* W, long long C, long long rows, long long batch, l
   p.ka_batch = err_stride; p.ka0 = 0;
   p.kb_batch = C; p.kb0 = i1;
   p.nb0 = i2;
-  p.alpha = 1.f; p.beta = -1.f;
+  p.alpha = 1.f; p.beta = beta;
   p.symmetric = 0;
   p.status = status;
   p.red = tc::make_map_out(&mp.d, p.D, p.N, p.M, batch, p.ldd, p.d_bs) ? 1 : 0;
   return tc::dispatch(2, 2, mp, p, batch, st);
+}
+
+// dst[b][k][r] = bf16 hi/lo of src[b][r][k] for a rows x nc block (row stride
+// lds, batch stride src_bs): the column-major operand layout of the trailing
+// update for G2PTQ's Z block and GPTAQ's quantized block.
+__global__ void split_block_t_kernel(const float* __restrict__ src, long long lds,
+                                     long long src_bs, long long rows, int nc,
+                                     __nv_bfloat16* hi, __nv_bfloat16* lo, long long dst_bs) {
+  __shared__ float tile[32][33];
+  const int b = blockIdx.z;
+  const long long r0 = (long long)blockIdx.y * 32;
+  const int k0 = blockIdx.x * 32;
+  const float* sb = src + (long long)b * src_bs;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const long long r = r0 + i;
+    const int k = k0 + threadIdx.x;
+    tile[i][threadIdx.x] = (r < rows && k < nc) ? sb[r * lds + k] : 0.f;
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int k = k0 + i;
+    const long long r = r0 + threadIdx.x;
+    if (k >= nc || r >= rows) continue;
+    __nv_bfloat16 h, l;
+    split_bf16(tile[threadIdx.x][i], &h, &l);
+    const long long o = (long long)b * dst_bs + (long long)k * rows + r;
+    hi[o] = h;
+    lo[o] = l;
+  }
+}
+
+int split_block_t(const float* src, long long lds, long long src_bs, long long rows, int nc,
+                  long long batch, __nv_bfloat16* hi, __nv_bfloat16* lo, long long dst_bs,
+                  cudaStream_t st) {
+  if (rows <= 0 || nc <= 0 || batch <= 0) return G2Q_OK;
+  dim3 grid(cdiv(nc, 32), cdiv(rows, 32), (unsigned)batch);
+  if (grid.y > 65535u || grid.z > 65535u) return G2Q_ERR_INVALID_ARG;
+  split_block_t_kernel<<<grid, dim3(32, 8), 0, st>>>(src, lds, src_bs, rows, nc, hi, lo, dst_bs);
+  G2Q_CHECK_LAUNCH();
+  return G2Q_OK;
 }
 
 // Two-term fp16 split of a K x (rows or cols) fp32 block for the fp32-accurate
