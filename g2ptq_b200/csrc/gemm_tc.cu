@@ -712,7 +712,7 @@ static int dispatch(int na, int nb, Maps& m, const Params& p, long long batch,
   }
   if (na == 1 && nb == 1) return launch<1, 1, false, true>(m, p, batch, st);
   if (na == 1 && nb == 2) return launch<1, 2, false>(m, p, batch, st);
-  if (na == 2 && nb == 1) return launch<2, 1, false>(m, p, batch, st);
+  if (na == 2 && nb == 1) return launch<2, 1, false, true>(m, p, batch, st);
   if (na == 2 && nb == 2) return launch<2, 2, false>(m, p, batch, st);
   return G2Q_ERR_UNSUPPORTED;
 }
@@ -797,6 +797,29 @@ int tc_gram(float* D, long long ldd, long long M, long long N, const void* A, in
   long long lda_t = lda, ldb_t = ldb;
   int na = 1, nb = 1;
   const bool same = (A == B) && (a_dtype == b_dtype) && !row_scale;
+  if (symmetric && row_scale && A == B && a_dtype == G2Q_DTYPE_BF16 &&
+      b_dtype == G2Q_DTYPE_BF16) {
+    // X^T diag(s) X of BF16 tokens: the scaled operand (split into a bf16 pair)
+    // goes on the M side and X stays exact on the N side, so the product runs
+    // on the 128 x 256 tiles with two MMAs per K step
+    if (!workspace || workspace_bytes < tc_gram_workspace_bytes(M, N, T))
+      return G2Q_ERR_INVALID_ARG;
+    __nv_bfloat16* hi = take(T * w);
+    __nv_bfloat16* lo = take(T * w);
+    G2Q_TRY(tc::split_rows(A, a_dtype, lda, T, M, row_scale, scale_stride, hi, lo, w, st));
+    tc::Maps mp{};
+    bool ok = tc::make_map(&mp.a[0], hi, M, T, w) && tc::make_map(&mp.a[1], lo, M, T, w) &&
+              tc::make_map(&mp.b[0], B, N, T, ldb);
+    if (!ok) return simt_gemm(sa, true, false, a_dtype, b_dtype, 1, st);
+    tc::Params p{};
+    p.D = D; p.ldd = ldd; p.d_bs = 0;
+    p.M = M; p.N = N;
+    p.num_kb = (int)((T + tc::BK - 1) / tc::BK);
+    p.alpha = alpha; p.beta = beta;
+    p.symmetric = 1;
+    p.raster = 1;
+    return tc::dispatch(2, 1, mp, p, 1, st);
+  }
   if (a_dtype != G2Q_DTYPE_BF16) {
     if (!workspace || workspace_bytes < tc_gram_workspace_bytes(M, N, T))
       return G2Q_ERR_INVALID_ARG;
