@@ -56,6 +56,9 @@ SIGNATURES = {
     "g2q_chol_workspace_bytes": [I64],
     "g2q_find_params": [P, P, I64, P, I64, I64, I64, I32, I32, P, P],
     "g2q_find_params_clip": [P, P, I64, P, I64, I64, I64, I32, I32, P, P, P],
+    "g2q_gemm_tc": [P, I64, I64, P, I64, I64, I32, P, I64, I64, I32, I64, I64, I64, I64, F32, F32,
+                    I32, P, SZ, P],
+    "g2q_gemm_tc_workspace_bytes": [I64, I64, I64, I64, I32, I32],
     "g2q_fake_quantize": [P, I64, P, I64, P, I64, I64, I64, P, P, I64, P, I32, P],
     "g2q_compensate_block": [I32, P, I64, I64, I64, I64, I64, P, I64, I64, P, P, I64, P, I32, P,
                              P, P, P, P, P],
@@ -82,6 +85,7 @@ _RESTYPES = {
     "g2q_gram_workspace_bytes": SZ,
     "g2q_chol_workspace_bytes": SZ,
     "g2q_compensate_workspace_bytes": SZ,
+    "g2q_gemm_tc_workspace_bytes": SZ,
     "g2q_gram_static_scratch_bytes": SZ,
 }
 

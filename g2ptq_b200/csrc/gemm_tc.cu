@@ -65,6 +65,8 @@ struct Params {
   int f16;         // operands are fp16 (else bf16)
   const float* sa;  // optional per-row (M) and per-column (N) output scales, powers of two
   const float* sb;
+  long long sa_bs, sb_bs;  // their batch strides
+  int supper;      // write only m < n (strictly upper part)
   int* status;
 };
 
@@ -230,7 +232,8 @@ struct Cfg {
 #define EPILOGUE_STORE4                                                                        \
   {                                                                                           \
     float* dst = Db + gm * p.ldd + gn;                                                        \
-    if (vec_ok && gn + 3 < p.N && (!p.symmetric || gn >= gm) && (!p.lower || gn + 3 <= gm)) { \
+    if (vec_ok && gn + 3 < p.N && (!p.symmetric || gn >= gm) && (!p.lower || gn + 3 <= gm) && \
+        (!p.supper || gn > gm)) {                                                             \
       float4* d4 = reinterpret_cast<float4*>(dst);                                            \
       if (p.alpha != 0.f) {                                                                   \
         const float4 o = *d4;                                                                 \
@@ -242,7 +245,8 @@ struct Cfg {
       *d4 = make_float4(v[0], v[1], v[2], v[3]);                                              \
     } else {                                                                                  \
       _Pragma("unroll") for (int u = 0; u < 4; ++u) {                                         \
-        if (gn + u >= p.N || (p.symmetric && gn + u < gm) || (p.lower && gn + u > gm))        \
+        if (gn + u >= p.N || (p.symmetric && gn + u < gm) || (p.lower && gn + u > gm) ||      \
+            (p.supper && gn + u <= gm))                                                       \
           continue;                                                                           \
         if (p.alpha != 0.f) v[u] = fmaf(p.alpha, dst[u], v[u]);                               \
         dst[u] = v[u];                                                                        \
@@ -349,6 +353,7 @@ __global__ void __launch_bounds__((Cfg<NA, NB, SMALL, WIDE>::THREADS),
   // tiles holding no element of the upper (symmetric) / lower triangle
   if (p.symmetric && (long long)nt * BN_T + BN_T - 1 < (long long)mt * BM) return;
   if (p.lower && (long long)nt * BN_T > (long long)mt * BM + BM - 1) return;
+  if (p.supper && (long long)mt * BM >= (long long)nt * BN_T + BN_T - 1) return;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -501,8 +506,11 @@ __global__ void __launch_bounds__((Cfg<NA, NB, SMALL, WIDE>::THREADS),
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             v[u] = p.beta * __uint_as_float(r[4 * j4 + u]);
-            if (p.sa) v[u] *= (gm < p.M ? p.sa[gm] : 1.f) * (gn + u < p.N ? p.sb[gn + u] : 1.f);
-            if (p.lower && gn + u > gm) v[u] = 0.f;  // leave the upper triangle as it is
+            if (p.sa)
+              v[u] *= (gm < p.M ? p.sa[bz * p.sa_bs + gm] : 1.f) *
+                      (gn + u < p.N ? p.sb[bz * p.sb_bs + gn + u] : 1.f);
+            // leave the other triangle as it is
+            if ((p.lower && gn + u > gm) || (p.supper && gn + u <= gm)) v[u] = 0.f;
           }
           *reinterpret_cast<float4*>(buf + lane * 32 + ((j4 ^ (lane & 7)) << 2)) =
               make_float4(v[0], v[1], v[2], v[3]);
@@ -537,7 +545,8 @@ __global__ void __launch_bounds__((Cfg<NA, NB, SMALL, WIDE>::THREADS),
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             v[u] = p.beta * __uint_as_float(r[4 * j4 + u]);
-            if (p.sa) v[u] *= p.sa[gm] * (gn + u < p.N ? p.sb[gn + u] : 1.f);
+            if (p.sa)
+              v[u] *= p.sa[bz * p.sa_bs + gm] * (gn + u < p.N ? p.sb[bz * p.sb_bs + gn + u] : 1.f);
           }
           EPILOGUE_STORE4
         }
@@ -586,7 +595,8 @@ __global__ void __launch_bounds__((Cfg<NA, NB, SMALL, WIDE>::THREADS),
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           v[u] = p.beta * acc[4 * j4 + u];
-          if (p.sa) v[u] *= p.sa[gm] * (gn + u < p.N ? p.sb[gn + u] : 1.f);
+          if (p.sa)
+            v[u] *= p.sa[bz * p.sa_bs + gm] * (gn + u < p.N ? p.sb[bz * p.sb_bs + gn + u] : 1.f);
         }
         EPILOGUE_STORE4
       }
@@ -713,7 +723,7 @@ static int dispatch(int na, int nb, Maps& m, const Params& p, long long batch,
   if (na == 1 && nb == 1) return launch<1, 1, false, true>(m, p, batch, st);
   if (na == 1 && nb == 2) return launch<1, 2, false>(m, p, batch, st);
   if (na == 2 && nb == 1) return launch<2, 1, false, true>(m, p, batch, st);
-  if (na == 2 && nb == 2) return launch<2, 2, false>(m, p, batch, st);
+  if (na == 2 && nb == 2) return launch<2, 2, false, true>(m, p, batch, st);
   return G2Q_ERR_UNSUPPORTED;
 }
 
@@ -937,6 +947,190 @@ int split_block_t(const float* src, long long lds, long long src_bs, long long r
   return G2Q_OK;
 }
 
+// ---------------------------------------------------------------------------
+// fp32-accurate batched GEMM on tensor cores (the fp32 products of fasterquant:
+// G2PTQ's Z / GHinv chain and GPTAQ's P).  Each operand is carried as an fp16
+// hi/lo pair, MN-major [batch][Kp][Mp] in the workspace, every output row
+// (column) scaled by the power of two that puts its largest magnitude over K in
+// [2^14, 2^15); the scales are undone exactly in the epilogue.
+// ---------------------------------------------------------------------------
+
+// Largest |x| of every output index of op(X) over K: kmajor != 0 means X is
+// stored [n][K] (one row per output index), else [K][n] (one column each).
+__global__ void op_absmax_kernel(const float* __restrict__ X, long long ldx, long long xbs,
+                                 long long n, long long K, int kmajor, float* fac,
+                                 float* inv, long long obs) {
+  const int b = blockIdx.y;
+  const float* xb = X + (long long)b * xbs;
+  float m = 0.f;
+  long long i;
+  if (kmajor) {
+    // one warp per output index
+    i = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (i < n)
+      for (long long k = lane; k < K; k += 32) m = fmaxf(m, fabsf(xb[i * ldx + k]));
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane != 0) return;
+  } else {
+    i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n)
+      for (long long k = 0; k < K; ++k) m = fmaxf(m, fabsf(xb[k * ldx + i]));
+  }
+  if (i >= n) return;
+  float f = 1.f, v = 1.f;
+  if (m > 0.f && m <= 3.0e38f) {
+    int e;
+    frexpf(m, &e);
+    e = e < -100 ? -100 : e;
+    f = ldexpf(1.f, 15 - e);
+    v = ldexpf(1.f, e - 15);
+  }
+  fac[(long long)b * obs + i] = f;
+  inv[(long long)b * obs + i] = v;
+}
+
+// out[b][k][i] = fp16 hi/lo of op(X)[i][k] * fac[b][i] for k < K, i < n; zero
+// padding up to Kp rows (so that one batch's K tiles never read the next's).
+__global__ void op_split_kernel(const float* __restrict__ X, long long ldx, long long xbs,
+                                long long n, long long K, long long Kp, int kmajor,
+                                const float* fac, long long obs, __half* hi, __half* lo,
+                                long long ldo, long long out_bs) {
+  __shared__ float tile[32][33];
+  const int b = blockIdx.z;
+  const long long i0 = (long long)blockIdx.x * 32, k0 = (long long)blockIdx.y * 32;
+  const float* xb = X + (long long)b * xbs;
+  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+    if (kmajor) {  // rows of X are output indices: read along k, transpose
+      const long long i = i0 + r, k = k0 + threadIdx.x;
+      tile[threadIdx.x][r] = (i < n && k < K) ? xb[i * ldx + k] : 0.f;
+    } else {
+      const long long k = k0 + r, i = i0 + threadIdx.x;
+      tile[r][threadIdx.x] = (i < n && k < K) ? xb[k * ldx + i] : 0.f;
+    }
+  }
+  __syncthreads();
+  const long long i = i0 + threadIdx.x;
+  if (i >= n) return;
+  const float f = fac[(long long)b * obs + i];
+  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+    const long long k = k0 + r;
+    if (k >= Kp) continue;
+    const float v = tile[r][threadIdx.x] * f;
+    const __half h = __float2half_rn(v);
+    const long long o = (long long)b * out_bs + k * ldo + i;
+    hi[o] = h;
+    lo[o] = __float2half_rn(v - __half2float(h));
+  }
+}
+
+// C[b][m][n] = 0 for m >= n (the part a strictly-upper product does not write).
+__global__ void zero_lower_kernel(float* C, long long ldc, long long cbs, long long M,
+                                  long long N) {
+  const int b = blockIdx.y;
+  const long long n_el = M * N;
+  for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < n_el;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const long long m = idx / N, nn = idx - m * N;
+    if (m >= nn) C[(long long)b * cbs + m * ldc + nn] = 0.f;
+  }
+}
+
+namespace tc {
+static long long round64(long long v) { return (v + 63) / 64 * 64; }
+
+struct OpLayout {
+  long long batches, n, Kp, ldo;
+  size_t terms_bytes() const { return (size_t)batches * Kp * ldo * sizeof(__half); }
+};
+
+static OpLayout op_layout(long long n, long long K, long long batches) {
+  return OpLayout{batches, n, round64(K), round8(n)};
+}
+}  // namespace tc
+
+size_t gemm_tc_workspace_bytes(long long M, long long N, long long K, long long batch_a,
+                               long long batch_b) {
+  const tc::OpLayout a = tc::op_layout(M, K, batch_a), b = tc::op_layout(N, K, batch_b);
+  return 2 * a.terms_bytes() + 2 * b.terms_bytes() +
+         (size_t)(2 * batch_a * M + 2 * batch_b * N) * sizeof(float) + 8 * 256;
+}
+
+// C <- alpha C + beta op(A) op(B), batched, fp32 in and out, on tensor cores.
+// mask: G2Q_MASK_FULL, G2Q_MASK_LOWER or G2Q_MASK_STRICT_UPPER (the rest set to
+// zero).  Returns G2Q_ERR_UNSUPPORTED where TMA cannot describe the operands.
+int gemm_tc_f32(float* C, long long ldc, long long sC, const float* A, long long lda,
+                long long sA, bool ta, const float* B, long long ldb, long long sB, bool tb,
+                long long M, long long N, long long K, long long batch, float alpha, float beta,
+                int mask, void* workspace, size_t workspace_bytes, cudaStream_t st) {
+  if (M <= 0 || N <= 0 || batch <= 0) return G2Q_OK;
+  if (K <= 0 || !tc::encode_fn() || (mask != G2Q_MASK_FULL && mask != G2Q_MASK_LOWER &&
+                                     mask != G2Q_MASK_STRICT_UPPER))
+    return G2Q_ERR_UNSUPPORTED;
+  const long long ba = sA ? batch : 1, bb = sB ? batch : 1;
+  if (!workspace || workspace_bytes < gemm_tc_workspace_bytes(M, N, K, ba, bb))
+    return G2Q_ERR_INVALID_ARG;
+  if (batch > 65535 || ((ldc * 4) & 15) || (reinterpret_cast<uintptr_t>(C) & 15))
+    return G2Q_ERR_UNSUPPORTED;
+  const tc::OpLayout la = tc::op_layout(M, K, ba), lb = tc::op_layout(N, K, bb);
+  char* ws = (char*)workspace;
+  auto take = [&](size_t bytes) {
+    char* q = (char*)(((uintptr_t)ws + 255) & ~(uintptr_t)255);
+    ws = q + bytes;
+    return q;
+  };
+  __half* a_hi = (__half*)take(la.terms_bytes());
+  __half* a_lo = (__half*)take(la.terms_bytes());
+  __half* b_hi = (__half*)take(lb.terms_bytes());
+  __half* b_lo = (__half*)take(lb.terms_bytes());
+  float* fa = (float*)take(ba * M * sizeof(float));
+  float* ia = (float*)take(ba * M * sizeof(float));
+  float* fb = (float*)take(bb * N * sizeof(float));
+  float* ib = (float*)take(bb * N * sizeof(float));
+  // op(A)[m][k]: A stored [M][K] (k contiguous) unless ta; op(B)[k][n]: B stored
+  // [K][N] (n contiguous) unless tb.
+  const int a_kmajor = ta ? 0 : 1, b_kmajor = tb ? 1 : 0;
+  op_absmax_kernel<<<dim3(cdiv(M * (a_kmajor ? 32 : 1), 256), (unsigned)ba), 256, 0, st>>>(
+      A, lda, sA, M, K, a_kmajor, fa, ia, M);
+  G2Q_CHECK_LAUNCH();
+  op_absmax_kernel<<<dim3(cdiv(N * (b_kmajor ? 32 : 1), 256), (unsigned)bb), 256, 0, st>>>(
+      B, ldb, sB, N, K, b_kmajor, fb, ib, N);
+  G2Q_CHECK_LAUNCH();
+  op_split_kernel<<<dim3(cdiv(M, 32), cdiv(la.Kp, 32), (unsigned)ba), dim3(32, 8), 0, st>>>(
+      A, lda, sA, M, K, la.Kp, a_kmajor, fa, M, a_hi, a_lo, la.ldo, la.Kp * la.ldo);
+  G2Q_CHECK_LAUNCH();
+  op_split_kernel<<<dim3(cdiv(N, 32), cdiv(lb.Kp, 32), (unsigned)bb), dim3(32, 8), 0, st>>>(
+      B, ldb, sB, N, K, lb.Kp, b_kmajor, fb, N, b_hi, b_lo, lb.ldo, lb.Kp * lb.ldo);
+  G2Q_CHECK_LAUNCH();
+  if (mask == G2Q_MASK_STRICT_UPPER) {
+    long long blocks = (M * N + 255) / 256;
+    if (blocks > 148 * 32) blocks = 148 * 32;
+    zero_lower_kernel<<<dim3((unsigned)blocks, (unsigned)batch), 256, 0, st>>>(C, ldc, sC, M, N);
+    G2Q_CHECK_LAUNCH();
+  }
+  tc::Maps mp{};
+  bool ok = tc::make_map(&mp.a[0], a_hi, M, ba * la.Kp, la.ldo, true) &&
+            tc::make_map(&mp.a[1], a_lo, M, ba * la.Kp, la.ldo, true) &&
+            tc::make_map(&mp.b[0], b_hi, N, bb * lb.Kp, lb.ldo, true) &&
+            tc::make_map(&mp.b[1], b_lo, N, bb * lb.Kp, lb.ldo, true);
+  if (!ok) return G2Q_ERR_UNSUPPORTED;
+  tc::Params p{};
+  p.D = C; p.ldd = ldc; p.d_bs = sC;
+  p.M = M; p.N = N;
+  p.num_kb = (int)(la.Kp / tc::BK);
+  p.ka_batch = ba > 1 ? la.Kp : 0;
+  p.kb_batch = bb > 1 ? lb.Kp : 0;
+  p.alpha = alpha; p.beta = beta;
+  p.lower = mask == G2Q_MASK_LOWER;
+  p.supper = mask == G2Q_MASK_STRICT_UPPER;
+  p.f16 = 1;
+  p.sa = ia; p.sb = ib;
+  p.sa_bs = ba > 1 ? M : 0;
+  p.sb_bs = bb > 1 ? N : 0;
+  p.red = (alpha == 1.f && tc::make_map_out(&mp.d, C, N, M, batch, ldc, sC)) ? 1 : 0;
+  return tc::dispatch(2, 2, mp, p, batch, st);
+}
+
 // Two-term fp16 split of a K x (rows or cols) fp32 block for the fp32-accurate
 // updates of the Cholesky chain.  Each output row (M or N index) is scaled by a
 // power of two that puts its largest magnitude in [2^14, 2^15), so both terms
@@ -1037,3 +1231,33 @@ int tc_update2h(float* D, long long ldd, long long M, long long N, long long K,
 }
 
 }  // namespace g2q
+
+extern "C" size_t g2q_gemm_tc_workspace_bytes(int64_t M, int64_t N, int64_t K, int64_t batch,
+                                              int a_batched, int b_batched) {
+  if (M <= 0 || N <= 0 || K <= 0 || batch <= 0) return 0;
+  return g2q::gemm_tc_workspace_bytes(M, N, K, a_batched ? batch : 1, b_batched ? batch : 1);
+}
+
+extern "C" int g2q_gemm_tc(float* C, int64_t ldc, int64_t strideC, const float* A, int64_t lda,
+                           int64_t strideA, int transA, const float* B, int64_t ldb,
+                           int64_t strideB, int transB, int64_t M, int64_t N, int64_t K,
+                           int64_t batch, float alpha, float beta, int out_mask, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+  if (!C || (!A && K > 0) || (!B && K > 0) || M < 0 || N < 0 || K < 0 || batch < 0)
+    return G2Q_ERR_INVALID_ARG;
+  if (out_mask < 0 || out_mask > 3) return G2Q_ERR_INVALID_ARG;
+  cudaStream_t st = (cudaStream_t)stream;
+  const int s = g2q::gemm_tc_f32(C, ldc, strideC, A, lda, strideA, transA != 0, B, ldb, strideB,
+                                 transB != 0, M, N, K, batch, alpha, beta, out_mask, workspace,
+                                 workspace_bytes, st);
+  if (s != G2Q_ERR_UNSUPPORTED) return s;
+  // shapes TMA cannot describe, or the inclusive upper mask: fp32 CUDA cores
+  g2q::SimtArgs a{};
+  a.A = A; a.B = B; a.C = C;
+  a.lda = lda; a.ldb = ldb; a.ldc = ldc;
+  a.sA = strideA; a.sB = strideB; a.sC = strideC;
+  a.M = M; a.N = N; a.K = K;
+  a.alpha = alpha; a.beta = beta;
+  a.mask = out_mask;
+  return g2q::simt_gemm(a, transA != 0, transB != 0, G2Q_DTYPE_F32, G2Q_DTYPE_F32, batch, st);
+}

@@ -185,15 +185,16 @@ class G2PTQ(_engine.StagingMixin):
 
         def run(Wp):
             # Z = (G U^T) * beta, GHinv = Z U  (g2ptq_utils.py:459-476)
-            T1 = ops.gemm(torch.empty_like(grad), grad, U, transB=True)
+            T1 = ops.gemm(torch.empty_like(grad), grad, U, transB=True,
+                          precision=_engine.PRECISION)
             if use_grad:
-                GH0 = ops.gemm(torch.empty_like(grad), T1, U)
+                GH0 = ops.gemm(torch.empty_like(grad), T1, U, precision=_engine.PRECISION)
                 dinv = ops.diag_of_utu(U)
                 beta = ops.trust_region_beta(grad, GH0, Q_sub, W0, dinv, alpha)
             else:
                 beta = torch.zeros(nl, rps, dtype=torch.float32, device=self.dev)
             Z = ops.scale_rows(T1, beta)
-            GH = ops.gemm(torch.empty_like(grad), Z, U)
+            GH = ops.gemm(torch.empty_like(grad), Z, U, precision=_engine.PRECISION)
             ops.compensate(_lib.METHOD_G2PTQ, Wp, U, params.scale, params.zero, colgroup,
                            dynamic, groupsize, q0.bits, q0.sym, blocksize, codes, z=Z, gh=GH,
                            status=params.status, precision=_engine.PRECISION, clip=clip)

@@ -143,8 +143,9 @@ class GPTAQ(_engine.StagingMixin):
         codes = torch.empty(B, R, C, dtype=torch.int8, device=self.dev)
 
         def run(Wp):
-            T = ops.gemm(torch.empty_like(dX), dX, U, transB=True, mask=_lib.MASK_STRICT_UPPER)
-            P = ops.gemm(torch.empty_like(dX), T, U, beta=float(alpha))
+            T = ops.gemm(torch.empty_like(dX), dX, U, transB=True, mask=_lib.MASK_STRICT_UPPER,
+                         precision=_engine.PRECISION)
+            P = ops.gemm(torch.empty_like(dX), T, U, beta=float(alpha), precision=_engine.PRECISION)
             ops.compensate(_lib.METHOD_GPTAQ, Wp, U, params.scale, params.zero, colgroup,
                            dynamic, groupsize, q0.bits, q0.sym, blocksize, codes, p=P,
                            status=params.status, precision=_engine.PRECISION, clip=clip)

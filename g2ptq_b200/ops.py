@@ -102,8 +102,10 @@ def sq_colsum(acc, X, keep, scale):
 # Dense algebra
 # --------------------------------------------------------------------------
 
-def gemm(C, A, B, transA=False, transB=False, alpha=0.0, beta=1.0, mask=_lib.MASK_FULL):
-    """Batched ``C <- alpha C + beta op(A) op(B)`` on fp32 ``[batch, *, *]`` tensors."""
+def gemm(C, A, B, transA=False, transB=False, alpha=0.0, beta=1.0, mask=_lib.MASK_FULL,
+         precision=0):
+    """Batched ``C <- alpha C + beta op(A) op(B)`` on fp32 ``[batch, *, *]`` tensors
+    (precision 0: fp32 CUDA cores; 1: tensor cores with fp16 hi/lo operands)."""
     _cuda(C, A, B)
     _contig(C, A, B)
     if C.dim() == 2:
@@ -113,6 +115,13 @@ def gemm(C, A, B, transA=False, transB=False, alpha=0.0, beta=1.0, mask=_lib.MAS
     K = A.shape[1] if transA else A.shape[2]
     sA = A.stride(0) if A.shape[0] > 1 else 0
     sB = B.stride(0) if B.shape[0] > 1 else 0
+    if precision == 1:
+        nbytes = query("g2q_gemm_tc_workspace_bytes", M, N, K, batch, int(sA != 0), int(sB != 0))
+        ws = workspace(nbytes, C.device)
+        call("g2q_gemm_tc", C.data_ptr(), C.stride(1), C.stride(0), A.data_ptr(), A.stride(1),
+             sA, int(transA), B.data_ptr(), B.stride(1), sB, int(transB), M, N, K, batch,
+             float(alpha), float(beta), mask, ws.data_ptr(), nbytes, _stream(C))
+        return C
     call("g2q_gemm", C.data_ptr(), C.stride(1), C.stride(0), A.data_ptr(), A.stride(1), sA,
          int(transA), B.data_ptr(), B.stride(1), sB, int(transB), M, N, K, batch, float(alpha),
          float(beta), mask, _stream(C))

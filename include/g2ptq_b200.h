@@ -134,6 +134,21 @@ int g2q_gemm(float* C, int64_t ldc, int64_t strideC,
              int64_t M, int64_t N, int64_t K, int64_t batch,
              float alpha, float beta, int out_mask, void* stream);
 
+/* g2q_gemm on tensor cores with fp32-level accuracy: both operands carried as
+ * fp16 hi/lo pairs (22 significant bits), every output row / column scaled by
+ * a power of two, three products per K step, fp32 accumulation.  out_mask
+ * G2Q_MASK_UPPER falls back to the CUDA-core kernel.  Needs
+ * g2q_gemm_tc_workspace_bytes(M, N, K, batch, strideA != 0, strideB != 0)
+ * bytes of workspace.  Replaces the same fasterquant products as g2q_gemm. */
+int g2q_gemm_tc(float* C, int64_t ldc, int64_t strideC,
+                const float* A, int64_t lda, int64_t strideA, int transA,
+                const float* B, int64_t ldb, int64_t strideB, int transB,
+                int64_t M, int64_t N, int64_t K, int64_t batch,
+                float alpha, float beta, int out_mask,
+                void* workspace, size_t workspace_bytes, void* stream);
+size_t g2q_gemm_tc_workspace_bytes(int64_t M, int64_t N, int64_t K, int64_t batch,
+                                   int a_batched, int b_batched);
+
 /* Damped inverse-Cholesky factor.  For each of `batch` matrices H[b] (C x C,
  * symmetric, row stride ldh, batch stride C*ldh) computes upper-triangular
  * U[b] with U^T U = (H + d I)^-1, d = damp_percent[b] * mean(diag H[b]).

@@ -186,3 +186,38 @@ def test_tc_cholesky_matches_fp32(C):
                                                                 dtype=torch.float64)
     assert float(resid.abs().max()) < 1e-3
     assert float(torch.tril(U1[0], -1).abs().max()) == 0.0
+
+
+@pytest.mark.parametrize("ta,tb", [(False, False), (False, True), (True, False), (True, True)])
+@pytest.mark.parametrize("mask", [_lib.MASK_FULL, _lib.MASK_LOWER, _lib.MASK_STRICT_UPPER])
+def test_tc_gemm_f32_vs_fp64(ta, tb, mask):
+    """g2q_gemm_tc (fp16 hi/lo operands, per-row scales): 1e-6 relative to fp64,
+    the same order as the fp32 CUDA-core GEMM, with the masks' zero / untouched
+    regions exact."""
+    g = torch.Generator(device=DEV).manual_seed(3 + 2 * ta + tb + 5 * mask)
+    Bt, M, N, K = 3, 328, 520, 1000
+    A = torch.randn(Bt, K, M, device=DEV, generator=g) if ta else \
+        torch.randn(Bt, M, K, device=DEV, generator=g)
+    A[0] *= 1e3  # batches of very different scale
+    Bm = torch.randn(1, N, K, device=DEV, generator=g) if tb else \
+        torch.randn(1, K, N, device=DEV, generator=g)  # broadcast B
+    C0 = torch.randn(Bt, M, N, device=DEV, generator=g)
+    C = C0.clone()
+    ops.gemm(C, A, Bm, transA=ta, transB=tb, alpha=0.5, beta=-2.0, mask=mask, precision=1)
+    a64 = (A.transpose(1, 2) if ta else A).double()
+    b64 = (Bm.transpose(1, 2) if tb else Bm).double()
+    full = 0.5 * C0.double() + -2.0 * (a64 @ b64)
+    i = torch.arange(M, device=DEV)[:, None]
+    j = torch.arange(N, device=DEV)[None, :]
+    if mask == _lib.MASK_LOWER:
+        keep = (i >= j)
+        ref = torch.where(keep, full, C0.double())
+    elif mask == _lib.MASK_STRICT_UPPER:
+        keep = (i < j)
+        ref = torch.where(keep, full, torch.zeros_like(full))
+    else:
+        keep = torch.ones(M, N, dtype=torch.bool, device=DEV)
+        ref = full
+    for b in range(Bt):
+        assert rel_fro(C[b][keep], ref[b][keep]) < 1e-6
+        assert torch.equal(C[b][~keep].double(), ref[b][~keep])
