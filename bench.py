@@ -187,8 +187,13 @@ def make_layers(torch, dev):
     return layers
 
 
-def one_step(torch, layers, acts, n_local, world, rank, dist, method="gptq", g2=None):
-    """add_batch over the rank's sequences, reduce to owners, fasterquant, broadcast."""
+def one_step(torch, layers, acts, n_local, world, rank, dist, method="gptq", g2=None,
+             marks=None):
+    """add_batch over the rank's sequences, reduce to owners, fasterquant, broadcast.
+
+    ``marks``: optional list that receives a CUDA event at the end of the
+    calibration phase (every add_batch call and the pending Gram folds, which
+    fasterquant_all would run first anyway) and one at the end of the step."""
     from g2ptq_b200.gptq_utils import gptq_utils, g2ptq_utils, common_utils
     from g2ptq_b200.utils.quant_utils import WeightQuantizer
     cfg = METHODS[method]
@@ -208,6 +213,11 @@ def one_step(torch, layers, acts, n_local, world, rank, dist, method="gptq", g2=
         xs = acts(s) if callable(acts) else {g: acts[g][s:s + 1] for g in acts}
         for name, rows, cols, grp in LINEARS:
             objs[name].add_batch(0, xs[grp], None)
+    if marks is not None:
+        for o in objs.values():
+            o._flush_all()
+        marks.append(torch.cuda.Event(enable_timing=True))
+        marks[-1].record()
     owners = objs
     if world > 1:
         specs = list(objs.values())
@@ -221,6 +231,9 @@ def one_step(torch, layers, acts, n_local, world, rank, dist, method="gptq", g2=
                                                export_compressed_tensors=True)
     for o in objs.values():
         o.free()
+    if marks is not None:
+        marks.append(torch.cuda.Event(enable_timing=True))
+        marks[-1].record()
     return objs
 
 
@@ -301,9 +314,10 @@ def native(args):
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record()
+    marks = [t0]
     torch.cuda.nvtx.range_push("timed")  # lets a profiler capture exactly the timed steps
     for _ in range(args.steps):
-        one_step(torch, layers, acts, n_local, world, rank, dist, args.method, g2)
+        one_step(torch, layers, acts, n_local, world, rank, dist, args.method, g2, marks)
     torch.cuda.nvtx.range_pop()
     t1.record()
     barrier()
@@ -315,6 +329,12 @@ def native(args):
         m = torch.tensor([ms], device=dev, dtype=torch.float64)
         dist.all_reduce(m, op=dist.ReduceOp.MAX)
         ms = float(m.item())
+    # phase split of this rank's steps: calibration (add_batch + Gram folds) and
+    # the rest (reduce, factorization, compensation, export, broadcast)
+    calib_ms = sum(marks[2 * i].elapsed_time(marks[2 * i + 1])
+                   for i in range(args.steps)) / args.steps
+    quant_ms = sum(marks[2 * i + 1].elapsed_time(marks[2 * i + 2])
+                   for i in range(args.steps)) / args.steps
     gram_ms = timer.total_ms() / args.steps
     gram_tflops = timer.flops / args.steps / (gram_ms * 1e-3) / 1e12 if gram_ms > 0 else 0.0
 
@@ -334,6 +354,8 @@ def native(args):
                         f"{args.seqs}x{args.seq_len} calibration tokens",
             "parallelism": f"tokens dp{world} + linear ownership (LPT)",
             "calibration_seconds_32_layers": round(N_LAYERS * ms * 1e-3, 3),
+            "phase_ms_rank0": {"add_batch_and_folds": round(calib_ms, 3),
+                               "reduce_factor_compensate_export": round(quant_ms, 3)},
             "precision": "tcgen05" if _engine.PRECISION == 1 else "fp32-cuda-core",
             "l2": "inputs larger than L2 (GBs of activations per step)",
         },

@@ -33,6 +33,7 @@
 // Every wait on an mbarrier is bounded; on expiry the CTA records
 // G2Q_ERR_TIMEOUT in the caller's status word and winds down.
 #include <cuda.h>
+#include <stdlib.h>
 #include <cudaTypedefs.h>
 
 #include <cuda_fp16.h>
@@ -614,6 +615,270 @@ __global__ void __launch_bounds__((Cfg<NA, NB, SMALL, WIDE>::THREADS),
 }
 
 // ---------------------------------------------------------------------------
+// CTA-pair variant (tcgen05 cta_group::2) for long-K products whose B operand
+// is one bf16 term: the Gram folds of add_batch.  A cluster of two CTAs on
+// neighbouring SMs computes a 256 x 256 output tile.  CTA r of the pair loads
+// rows m0 + 128 r .. + 127 of every A term and columns n0 + 128 r .. + 127 of B
+// into its own shared memory; the leader (rank 0) issues M = 256, N = 256 MMAs
+// that read both CTAs' operands and write each CTA's TMEM (its 128 rows x all
+// 256 columns).  Per SM and 64-token k-block that is 16 KB of A per term plus
+// 16 KB of B for 128 x 256 outputs, where a single-CTA 128 x 256 tile reads
+// 32 KB of B: operand delivery from L2, which bounds the single-CTA kernel,
+// drops by a third for the one-term Gram.
+// Barriers: the leader's full[s] counts both CTAs' TMA bytes (the loads use
+// the .cta_group::2 form, which may signal the peer's barrier; no multicast);
+// one commit with a two-CTA mask frees stage s in both CTAs (empty[s]) and
+// announces a finished accumulator buffer to both epilogues (accf[b]); every
+// epilogue warp of both CTAs arrives on the leader's acce[b] once it drained b.
+// Same accumulator promotion as the single-CTA kernel: PROMOTE_KB k-blocks per
+// TMEM buffer, drained into fp32 registers with rounded adds.
+// ---------------------------------------------------------------------------
+
+template <int NA>
+struct PairCfg {
+  static constexpr int STAGE_BYTES = (NA + 1) * TILE_BYTES;  // per CTA
+  static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+  static constexpr int EPI_WARPS = 8;
+  static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+  static constexpr int ACC_COLS = 512;  // two 256-column buffers
+  static constexpr int PROMOTE_KB = NA == 1 ? 4 : 2;
+};
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// shared::cluster address of the variable at shared::cta address a in CTA rank
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t a, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
+               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                                 uint32_t mbar_cluster) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(mbar_cluster)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_bf16_pair(uint32_t tmem_d, uint64_t a, uint64_t b,
+                                               uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+
+// arrive on the barrier at shared::cta offset mbar in both CTAs of the pair
+// once every MMA issued so far by this thread has completed
+__device__ __forceinline__ void umma_commit_pair(uint32_t mbar) {
+  const uint16_t mask = 0x3;
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(mbar),
+      "h"(mask)
+      : "memory");
+}
+
+// Arrive on a barrier of either CTA of the pair.  The drained-accumulator
+// barrier carries no memory data: the TMEM reads before it are ordered against
+// the MMAs after it by the tcgen05 fences on both sides, so the default
+// (CTA-scope) semantics suffice; a cluster-scope release here costs a memory
+// barrier per epilogue warp and drain.
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t mbar_cluster) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(mbar_cluster) : "memory");
+}
+
+__host__ __device__ constexpr uint32_t idesc_bf16_mn_m256(int n) {
+  return (idesc_bf16_mn(n) & ~(31u << 24)) | ((uint32_t)(256 >> 4) << 24);
+}
+
+template <int NA>
+__global__ void __launch_bounds__(PairCfg<NA>::THREADS, 1)
+    tc_pair_kernel(const __grid_constant__ CUtensorMap ma0, const __grid_constant__ CUtensorMap ma1,
+                   const __grid_constant__ CUtensorMap mb0, Params p) {
+  using K = PairCfg<NA>;
+  constexpr int PT = 256;  // pair tile edge
+  const uint32_t rank = cluster_ctarank();
+  int mt, nt;
+  // both CTAs of a cluster decode the same pair tile, so they leave or stay together
+  if (!decode_tile(blockIdx.x >> 1, p.tiles_m, p.tiles_n, p.symmetric, mt, nt)) return;
+  const long long bz = blockIdx.z;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + K::STAGES * K::STAGE_BYTES);
+  // bars[0..S): full (used in the leader), [S..2S): empty, [2S..2S+2): accumulator
+  // full, [2S+2..2S+4): accumulator drained (used in the leader)
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * K::STAGES + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + K::STAGES);
+  const uint32_t accf0 = smem_u32(bars + 2 * K::STAGES);
+  const uint32_t acce0 = smem_u32(bars + 2 * K::STAGES + 2);
+  const int ngroups = (p.num_kb + p.promote_kb - 1) / p.promote_kb;
+  const int promote_kb = p.promote_kb;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < K::STAGES; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(accf0 + 8 * b, 1);
+      mbar_init(acce0 + 8 * b, 2 * K::EPI_WARPS);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_holder)),
+                 "r"(K::ACC_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  fence_before();
+  __syncthreads();
+  cluster_sync();  // barriers of both CTAs initialised, TMEM allocated in both
+  fence_after();
+  const uint32_t tmem = *tmem_holder;
+  const int m0 = mt * PT, n0 = nt * PT;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint32_t full_lead = mapa_shared(full0, 0);
+      for (int kb = 0; kb < p.num_kb; ++kb) {
+        const int s = kb % K::STAGES;
+        const uint32_t ph = (kb / K::STAGES) & 1;
+        if (!mbar_wait(empty0 + 8 * s, ph ^ 1, abort_flag, p.status)) break;
+        // the leader's full[s] expects the bytes of both CTAs; the peer's loads
+        // may land first (the transaction count goes transiently negative)
+        if (rank == 0) mbar_expect_tx(full0 + 8 * s, 2 * K::STAGE_BYTES);
+        const uint32_t fb = full_lead + 8 * s;
+        const uint32_t st = smem_u32(smem + s * K::STAGE_BYTES);
+        const int ya = (int)(p.ka_batch * bz + p.ka0 + (long long)kb * BK);
+        const int yb = (int)(p.kb_batch * bz + p.kb0 + (long long)kb * BK);
+        const int xa = m0 + 128 * (int)rank;
+        const int xb = (int)(p.nb0 + n0) + 128 * (int)rank;
+#pragma unroll
+        for (int i = 0; i < NA; ++i) {
+          const CUtensorMap* m = i == 0 ? &ma0 : &ma1;
+          tma_load_2d_pair(st + i * TILE_BYTES, m, xa, ya, fb);
+          tma_load_2d_pair(st + i * TILE_BYTES + CHUNK_BYTES, m, xa + 64, ya, fb);
+        }
+        const uint32_t sb = st + NA * TILE_BYTES;
+        tma_load_2d_pair(sb, &mb0, xb, yb, fb);
+        tma_load_2d_pair(sb + CHUNK_BYTES, &mb0, xb + 64, yb, fb);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      const uint32_t idesc = idesc_bf16_mn_m256(PT);
+      int kb = 0;
+      for (int g = 0; g < ngroups; ++g) {
+        const int buf = g & 1;
+        const uint32_t use_ph = (uint32_t)((g >> 1) & 1);
+        if (!mbar_wait(acce0 + 8 * buf, use_ph ^ 1, abort_flag, p.status)) break;
+        fence_after();
+        const uint32_t acc_t = tmem + (uint32_t)(buf * PT);
+        const int kend = (kb + promote_kb < p.num_kb) ? kb + promote_kb : p.num_kb;
+        const int kstart = kb;
+        bool ok = true;
+        for (; kb < kend; ++kb) {
+          const int s = kb % K::STAGES;
+          const uint32_t ph = (kb / K::STAGES) & 1;
+          if (!mbar_wait(full0 + 8 * s, ph, abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          fence_after();
+          const uint32_t sa = smem_u32(smem + s * K::STAGE_BYTES);
+          const uint32_t sb = sa + NA * TILE_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint32_t off = kk * 2048;  // 16 K rows = two 8-row swizzle groups
+            const uint32_t acc0 = (kb > kstart || kk > 0) ? 1u : 0u;
+#pragma unroll
+            for (int i = 0; i < NA; ++i)
+              umma_bf16_pair(acc_t, desc_mn_sw128(sa + i * TILE_BYTES + off),
+                             desc_mn_sw128(sb + off), idesc, i == 0 ? acc0 : 1u);
+          }
+          umma_commit_pair(empty0 + 8 * s);
+        }
+        if (!ok) break;
+        umma_commit_pair(accf0 + 8 * buf);
+      }
+    }
+  } else {
+    // epilogue warps of both CTAs: warp w reads TMEM lanes 32 (w % 4) .. + 31 of
+    // this CTA's 128 rows; the second four warps take the upper 128 columns
+    const int q = warp & 3;
+    const int half = (warp - 2) / 4;
+    const int row = q * 32 + lane;
+    const long long gm = m0 + 128 * (long long)rank + row;
+    const uint32_t acce_lead = mapa_shared(acce0, 0);
+    float acc[BN];
+#pragma unroll
+    for (int j = 0; j < BN; ++j) acc[j] = 0.f;
+    bool ok = true;
+    for (int g = 0; g < ngroups; ++g) {
+      const int buf = g & 1;
+      const uint32_t use_ph = (uint32_t)((g >> 1) & 1);
+      if (ok) ok = mbar_wait(accf0 + 8 * buf, use_ph, abort_flag, p.status);
+      fence_after();
+      const uint32_t base = tmem + (uint32_t)(buf * PT + half * BN) + ((uint32_t)(q * 32) << 16);
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(base + (uint32_t)(c * 32), r);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) acc[c * 32 + j] += __uint_as_float(r[j]);
+      }
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(acce_lead + 8 * buf);
+    }
+    float* Db = p.D + bz * p.d_bs;
+    const bool vec_ok = ((p.ldd & 3) == 0) && ((reinterpret_cast<uintptr_t>(Db) & 15) == 0);
+    if (ok && gm < p.M) {
+#pragma unroll
+      for (int j4 = 0; j4 < BN / 4; ++j4) {
+        const long long gn = n0 + half * BN + 4 * j4;
+        float v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) v[u] = p.beta * acc[4 * j4 + u];
+        EPILOGUE_STORE4
+      }
+    }
+  }
+  fence_before();
+  __syncthreads();
+  // neither CTA leaves while the other may still touch its shared memory or TMEM
+  cluster_sync();
+  if (warp == 1) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(K::ACC_COLS)
+                 : "memory");
+  }
+}
+
+// ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
 
@@ -712,6 +977,59 @@ static int launch(const Maps& m, const Params& p, long long batch, cudaStream_t 
   return G2Q_OK;
 }
 
+template <int NA>
+static int launch_pair(const Maps& m, const Params& p, long long batch, cudaStream_t st) {
+  using K = PairCfg<NA>;
+  static int attr_done[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return G2Q_ERR_CUDA;
+  if (dev >= 64 || !attr_done[dev]) {
+    if (cudaFuncSetAttribute(tc_pair_kernel<NA>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             K::SMEM) != cudaSuccess)
+      return G2Q_ERR_CUDA;
+    if (dev < 64) attr_done[dev] = 1;
+  }
+  Params q = p;
+  q.promote_kb = K::PROMOTE_KB;
+  q.tiles_m = cdiv(p.M, 256);
+  q.tiles_n = cdiv(p.N, 256);
+  q.red = 0;
+  if (q.symmetric && q.tiles_m != q.tiles_n) return G2Q_ERR_INVALID_ARG;
+  const long long tm = q.tiles_m, tn = q.tiles_n;
+  const long long pairs = q.symmetric ? tm * (tm + 1) / 2 : tm * tn;
+  if (2 * pairs > 0x7fffffffLL || batch > 65535) return G2Q_ERR_INVALID_ARG;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(2 * pairs), 1, (unsigned)batch);
+  cfg.blockDim = dim3(K::THREADS, 1, 1);
+  cfg.dynamicSmemBytes = K::SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, tc_pair_kernel<NA>, m.a[0], m.a[1], m.b[0], q);
+  g2q::note_launch();
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    return G2Q_ERR_CUDA;
+  }
+  return G2Q_OK;
+}
+
+// CTA-pair tiles for long-K bf16 products with a one-term B (the Gram folds),
+// unless G2PTQ_B200_PAIR_TILES=0 asks for the single-CTA 128 x 256 tiles.
+static bool pair_tiles_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("G2PTQ_B200_PAIR_TILES");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
 static int dispatch(int na, int nb, Maps& m, const Params& p, long long batch,
                     cudaStream_t st) {
   for (int i = na; i < 3; ++i) m.a[i] = m.a[0];
@@ -719,6 +1037,11 @@ static int dispatch(int na, int nb, Maps& m, const Params& p, long long batch,
   const bool small = p.num_kb <= 4;
   if (small) {
     if (na == 2 && nb == 2) return launch<2, 2, true>(m, p, batch, st);
+  }
+  if (!small && nb == 1 && na <= 2 && !p.f16 && !p.sa && !p.lower && !p.supper &&
+      p.nb0 == 0 && p.M >= 512 && p.N >= 512 && pair_tiles_enabled()) {
+    if (na == 1) return launch_pair<1>(m, p, batch, st);
+    return launch_pair<2>(m, p, batch, st);
   }
   if (na == 1 && nb == 1) return launch<1, 1, false, true>(m, p, batch, st);
   if (na == 1 && nb == 2) return launch<1, 2, false>(m, p, batch, st);

@@ -1,6 +1,7 @@
 """Single-kernel cases of the quantization hot path, for timing and profiling.
 
     python -m g2ptq_b200.kernel_cases gram --tokens 16384 --columns 4096
+    python -m g2ptq_b200.kernel_cases gram_weighted --tokens 16384 --columns 4096
     python -m g2ptq_b200.kernel_cases chol --columns 4096
     python -m g2ptq_b200.kernel_cases compensate --rows 4096 --columns 4096
 
@@ -51,6 +52,27 @@ def gram(args, g):
                 algorithmic_bytes=bytes_, flops=flops)
 
 
+def gram_weighted(args, g):
+    """One G2PTQ fold: H[k] <- a H[k] + b X^T diag(s_k) X for the four row groups
+    (per-token saliency weights s, BF16 tokens)."""
+    T, C = args.tokens, args.columns
+    X = torch.randn(T, C, device="cuda", generator=g)
+    X[:, :4] *= 20
+    X = X.to(torch.bfloat16)
+    S = torch.rand(T, 4, device="cuda", generator=g)
+    H = torch.zeros(4, C, C, device="cuda")
+
+    def run():
+        for k in range(4):
+            ops.gram_update(H[k], X, X, row_scale=S[:, k], alpha=0.5, beta=1.0 / T,
+                            symmetric=True, precision=1)
+
+    ms = _time(run, args.warmup, args.reps)
+    flops = 4 * T * C * (C + 1)
+    return dict(case="gram_weighted", tokens=T, columns=C, ms=ms, tflops=flops / ms / 1e9,
+                flops=flops)
+
+
 def chol(args, g):
     """Damped inverse-Cholesky factor of one C x C Hessian."""
     C = args.columns
@@ -91,7 +113,8 @@ def compensate(args, g):
                 flops=flops)
 
 
-CASES = {"gram": gram, "chol": chol, "compensate": compensate}
+CASES = {"gram": gram, "gram_weighted": gram_weighted, "chol": chol,
+         "compensate": compensate}
 
 
 def main(argv=None):
