@@ -11,7 +11,7 @@ import os
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.environ.get("G2PTQ_B200_LIB", os.path.join(_HERE, "_lib", "libg2ptq_b200.so"))
 
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 G2Q_OK = 0
 G2Q_ERR_INVALID_ARG = -1
@@ -56,6 +56,7 @@ SIGNATURES = {
     "g2q_chol_workspace_bytes": [I64],
     "g2q_find_params": [P, P, I64, P, I64, I64, I64, I32, I32, P, P],
     "g2q_find_params_clip": [P, P, I64, P, I64, I64, I64, I32, I32, P, P, P],
+    "g2q_find_params_groups": [P, P, I64, P, I64, I64, I64, I32, I32, I64, I32, I32, P, P],
     "g2q_gemm_tc": [P, I64, I64, P, I64, I64, I32, P, I64, I64, I32, I64, I64, I64, I64, F32, F32,
                     I32, P, SZ, P],
     "g2q_gemm_tc_workspace_bytes": [I64, I64, I64, I64, I32, I32],

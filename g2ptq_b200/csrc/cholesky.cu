@@ -61,162 +61,349 @@ __global__ void reverse_damp_kernel(const float* H, long long C, long long ldh,
 // Factor the nb x nb diagonal block at (k0, k0) of A in place and write its
 // lower-triangular inverse to Linv (NB x NB, zero padded).
 //
-// The block and its inverse live in registers: thread (ty, tx) of a 16 x 16
-// grid owns rows 8ty..8ty+7 x columns 8tx..8tx+7 of both L and X = L^-1.
-// Blocked right-looking factorization, eight pivots at a time:
-//   1. the thread holding diagonal tile jb runs the unblocked factorization of
-//      that tile (columns scaled by 1/l_jj, as LAPACK's spotf2);
-//   2. the tiles under it apply the same eight pivots to their rows (the strip
-//      L_ij), and the tiles of block row jb of X run the forward substitution
-//      of L X = I for those eight rows;
-//   3. rank-8 updates A_ik -= L_ij L_kj^T of the lower trailing tiles and
-//      X_i: -= L_ij X_j: of X.
-// Every element sees the same operations in the same order as with one pivot
-// at a time, but with two block-wide barriers per eight pivots.
-__global__ void __launch_bounds__(256) panel_kernel(float* A, long long C, long long k0, int nb,
-                                                    float* Linv, int* info) {
-  __shared__ __align__(16) float Ls[8][NB];  // strip L_ij, transposed (column k of the strip)
-  __shared__ __align__(16) float Xb[8][NB];  // finished rows of X in block row jb
-  __shared__ float Ld[8][8];                 // L_jj (scaled columns)
-  __shared__ float Rl[8];                    // 1 / l_jj
-  __shared__ int failed;
-  const int t = threadIdx.x;
-  const int ty = t >> 4, tx = t & 15;
-  const int r0 = ty * 8, c0 = tx * 8;
-  float a[8][8], x[8][8];
+// One CTA of 256 threads; the block A_kk and the inverse accumulator live in
+// shared memory (rows past nb padded with the identity, which factors to
+// itself and does not touch the real rows).  Blocked right-looking
+// factorization in four 32-column sub-panels s:
+//   (a) warp 0 factors the 32 x 32 diagonal sub-block, one row per lane:
+//       every lane takes the pivot's sqrt and reciprocal, scales its element
+//       of the pivot column by 1/l_jj (as LAPACK's spotf2) and applies the
+//       rank-1 update to the rest of its row;
+//   (b) forward substitution with that sub-block, one row (or column) per
+//       lane: the rows under it become L_is, and block row s of the inverse
+//       accumulator Y becomes X_s: = L_ss^-1 Y_s: (L X = I by blocks);
+//   (c) rank-32 updates of the trailing lower part, A_ij -= L_is L_js^T, and
+//       of the inverse rows below, Y_i: -= L_is X_s:, in 4 x 4 thread tiles.
+// Look-ahead: the next diagonal sub-block is updated first, so that warp 0
+// factors it while the other seven warps finish the rest of (c).  The pivot
+// chain (sqrt, reciprocal, one shared-memory round trip and one fma per
+// pivot) is the latency that bounds the kernel.
+constexpr int PSUB = 32;          // sub-panel width
+constexpr int PLD = NB + 4;       // shared row stride of the block and of Y / X
+constexpr int PANEL_THREADS = 256;
+
+__host__ __device__ constexpr int panel_smem_floats() {
+  return 2 * NB * PLD + PSUB * PLD + 2 * PSUB * (PSUB + 1) + PSUB + 4;
+}
+
+// (a): factor the sub-block at (c0, c0) of As in place (warp 0).  Lane i holds
+// row i in registers, shifted four columns after every four pivots, so that
+// the pivot loop is a short runtime loop over groups of four (straight-line
+// code for all 32 pivots runs once per sub-block and stalls on instruction
+// fetch).  The chain from one pivot to the next is a shuffle, sqrt,
+// reciprocal, one multiply and one fma (the diagonal element is kept apart);
+// the column of l_kj reaches the other rows through shared memory off that
+// chain.  Entries of a row at or right of its diagonal are updated too and
+// never read (Lc has zero rows past the block, so the reads stay in bounds).
+// Lc[k][j] receives l_kj, rls[j] = 1 / l_jj.  A non-positive or NaN pivot sets
+// *flag to its 1-based index in A.
+__device__ __forceinline__ void panel_factor_sub(float* As, int c0, float* Lc, float* rls,
+                                                 volatile int* flag, long long k0, int lane) {
+  constexpr int LC = PSUB + 1;
+  float d[PSUB];
+  const float* row = As + (c0 + lane) * PLD + c0;
 #pragma unroll
-  for (int u = 0; u < 8; ++u)
+  for (int m4 = 0; m4 < PSUB; m4 += 4) {
+    const float4 v = *reinterpret_cast<const float4*>(row + m4);
+    d[m4] = v.x; d[m4 + 1] = v.y; d[m4 + 2] = v.z; d[m4 + 3] = v.w;
+  }
+  float diag = row[lane];
+  bool ok = true;
+#pragma unroll 1
+  for (int jb = 0; jb < PSUB && ok; jb += 4) {
 #pragma unroll
-    for (int v = 0; v < 8; ++v) {
-      const int r = r0 + u, c = c0 + v;
-      a[u][v] = (r < nb && c <= r) ? A[(k0 + r) * C + k0 + c] : 0.f;
-      x[u][v] = (r == c && r < nb) ? 1.f : 0.f;
+    for (int jj = 0; jj < 4; ++jj) {
+      const int j = jb + jj;
+      const float piv = __shfl_sync(0xffffffffu, diag, j);
+      if (!(piv > 0.f)) {  // uniform: every lane holds the same pivot
+        if (lane == 0) *flag = (int)(k0 + c0 + j + 1);
+        ok = false;
+        break;
+      }
+      const float l = sqrtf(piv);
+      const float rl = 1.f / l;
+      float lij = 0.f;
+      if (lane == j) {
+        Lc[j * LC + j] = l;
+        rls[j] = rl;
+      } else if (lane > j) {
+        lij = d[jj] * rl;
+        diag = fmaf(-lij, lij, diag);
+        Lc[lane * LC + j] = lij;
+      }
+      __syncwarp();
+      // a_ik -= l_ij l_kj for k > j; d[kk] holds column jb + kk
+      const float* lcol = Lc + j * (LC + 1);  // lcol[q * LC] = Lc[j + q][j]
+#pragma unroll
+      for (int kk = jj + 1; kk < PSUB; ++kk) d[kk] = fmaf(-lij, lcol[(kk - jj) * LC], d[kk]);
     }
-  if (t == 0) failed = 0;
+#pragma unroll
+    for (int kk = 0; kk < PSUB - 4; ++kk) d[kk] = d[kk + 4];
+  }
+  __syncwarp();
+  if (ok) {
+#pragma unroll 4
+    for (int k = 0; k < PSUB; ++k)
+      As[(c0 + k) * PLD + c0 + lane] = (lane <= k) ? Lc[k * LC + lane] : 0.f;
+  }
+  __syncwarp();
+}
+
+// Forward substitution with the factored sub-block, one vector per lane:
+// x <- L_ss^-1 x, where x[m] = v[m * stride] (shared memory, in place).  The
+// vector is held in registers shifted four entries after every four steps
+// (runtime loop, compact code); entries past the block are updated from the
+// zero rows of Lc and never read.
+__device__ __forceinline__ void panel_forward_sub(float* v, int stride, const float* Lc,
+                                                  const float* rls, float* lt_col) {
+  constexpr int LC = PSUB + 1;
+  float x[PSUB];
+#pragma unroll
+  for (int m = 0; m < PSUB; ++m) x[m] = v[m * stride];
+#pragma unroll 1
+  for (int mb = 0; mb < PSUB; mb += 4) {
+#pragma unroll
+    for (int mm = 0; mm < 4; ++mm) {
+      const int m = mb + mm;
+      const float xm = x[mm] * rls[m];
+      v[m * stride] = xm;
+      if (lt_col) lt_col[m * PLD] = xm;
+      const float* lcol = Lc + m * (LC + 1);  // lcol[q * LC] = Lc[m + q][m]
+#pragma unroll
+      for (int kk = mm + 1; kk < PSUB; ++kk) x[kk] = fmaf(-xm, lcol[(kk - mm) * LC], x[kk]);
+    }
+#pragma unroll
+    for (int kk = 0; kk < PSUB - 4; ++kk) x[kk] = x[kk + 4];
+  }
+}
+
+// 4 x 4 tile of D[i0.., j0..] -= sum_m P[m][i0..] Q[m][j0..] over 32 m, where
+// P rows are Lt (the transposed strip) and Q rows are Lt or rows of X.
+__device__ __forceinline__ void panel_tile_update(float* D, int i0, int j0, const float* P,
+                                                  const float* Q, long long ldq, bool lower_only) {
+  float acc[4][4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u)
+#pragma unroll
+    for (int v = 0; v < 4; ++v) acc[u][v] = 0.f;
+#pragma unroll 8
+  for (int m = 0; m < PSUB; ++m) {
+    const float4 p = *reinterpret_cast<const float4*>(P + m * PLD + i0);
+    const float4 q = *reinterpret_cast<const float4*>(Q + m * ldq + j0);
+    const float pv[4] = {p.x, p.y, p.z, p.w};
+    const float qv[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+#pragma unroll
+      for (int v = 0; v < 4; ++v) acc[u][v] = fmaf(pv[u], qv[v], acc[u][v]);
+  }
+#pragma unroll
+  for (int u = 0; u < 4; ++u)
+#pragma unroll
+    for (int v = 0; v < 4; ++v)
+      if (!lower_only || j0 + v <= i0 + u) D[(i0 + u) * PLD + j0 + v] -= acc[u][v];
+}
+
+__global__ void __launch_bounds__(PANEL_THREADS, 1)
+    panel_kernel(float* A, long long C, long long k0, int nb, float* Linv, int* info) {
+  extern __shared__ __align__(16) float psm[];
+  float* As = psm;                  // [NB][PLD] block, lower part
+  float* Ys = As + NB * PLD;        // [NB][PLD] inverse accumulator Y -> X
+  float* Lt = Ys + NB * PLD;        // [PSUB][PLD] strip L_is transposed: Lt[m][i]
+  float* Lc = Lt + PSUB * PLD;      // [2 PSUB][PSUB + 1] factored diagonal sub-block + zero rows
+  float* rls = Lc + 2 * PSUB * (PSUB + 1);
+  volatile int* flag = reinterpret_cast<volatile int*>(rls + PSUB);
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int nsub = (nb + PSUB - 1) / PSUB;
+  const int rend = nsub * PSUB;     // rows / columns past rend are never touched
+
+  {
+    // thread t reads column t % 128 of 64 rows, sixteen loads in flight at a time
+    const int c = t & (NB - 1), rb = (t >> 7) * (NB / 2);
+#pragma unroll 1
+    for (int i0 = 0; i0 < NB / 2; i0 += 16) {
+      float v[16];
+#pragma unroll
+      for (int u = 0; u < 16; ++u) {
+        const int r = rb + i0 + u;
+        v[u] = (r < nb && c <= r) ? A[(k0 + r) * C + k0 + c] : (r == c ? 1.f : 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < 16; ++u) {
+        const int r = rb + i0 + u;
+        As[r * PLD + c] = v[u];
+        Ys[r * PLD + c] = (r == c) ? 1.f : 0.f;
+      }
+    }
+  }
+  for (int idx = t; idx < 2 * PSUB * (PSUB + 1); idx += PANEL_THREADS) Lc[idx] = 0.f;
+  if (t == 0) *flag = 0;
+  __syncthreads();
+  if (warp == 0) panel_factor_sub(As, 0, Lc, rls, flag, k0, lane);
   __syncthreads();
 
-  for (int jb = 0; jb * 8 < nb; ++jb) {
-    const int j0 = jb * 8;
-    const int nbk = (nb - j0) < 8 ? (nb - j0) : 8;
-    // ---- 1. diagonal tile
-    if (ty == jb && tx == jb) {
-      bool ok = true;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        float rl = 0.f;
-        if (j < nbk && ok) {
-          const float d = a[j][j];
-          if (!(d > 0.f)) {  // non-positive or NaN pivot
-            ok = false;
-            failed = 1;
-            if (info) atomicCAS(info, 0, (int)(k0 + j0 + j + 1));
-          } else {
-            const float l = sqrtf(d);
-            rl = 1.f / l;
-            a[j][j] = l;
-#pragma unroll
-            for (int u = j + 1; u < 8; ++u) a[u][j] *= rl;
-#pragma unroll
-            for (int u = j + 1; u < 8; ++u)
-#pragma unroll
-              for (int v = j + 1; v <= u; ++v) a[u][v] = fmaf(-a[u][j], a[v][j], a[u][v]);
-          }
-        }
-        Rl[j] = rl;
-      }
-#pragma unroll
-      for (int u = 0; u < 8; ++u)
-#pragma unroll
-        for (int v = 0; v < 8; ++v) Ld[u][v] = (v < u) ? a[u][v] : 0.f;
+  for (int s = 0; s < nsub; ++s) {
+    if (*flag) break;  // uniform: read after a barrier
+    const int c0 = s * PSUB;
+    // ---- (b) rows under the sub-block: L_is; block row s of Y -> X_s:
+    if (warp < 3) {
+      const int r = c0 + PSUB + warp * 32 + lane;
+      if (r < rend) panel_forward_sub(As + r * PLD + c0, 1, Lc, rls, Lt + r);
+    } else if (warp < 7) {
+      const int j = (warp - 3) * 32 + lane;
+      if (j < c0 + PSUB) panel_forward_sub(Ys + c0 * PLD + j, PLD, Lc, rls, nullptr);
     }
     __syncthreads();
-    if (failed) break;  // uniform after the barrier
-    // ---- 2. the eight pivots on the strip, and on block row jb of X
-    if (tx == jb && ty > jb) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        if (j >= nbk) continue;
-        const float rl = Rl[j];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const float sv = a[u][j] * rl;
-          a[u][j] = sv;
-          Ls[j][r0 + u] = sv;
-#pragma unroll
-          for (int v = j + 1; v < 8; ++v) a[u][v] = fmaf(-sv, Ld[v][j], a[u][v]);
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-        if (j >= nbk) {
-#pragma unroll
-          for (int u = 0; u < 8; ++u) Ls[j][r0 + u] = 0.f;
-        }
+    if (s + 1 >= nsub) break;
+    // ---- (c) look-ahead: the next diagonal sub-block first (36 lower 4 x 4 tiles)
+    const int n0 = c0 + PSUB;
+    if (t < 36) {
+      int ti = 0, tt = t;
+      while (tt > ti) { tt -= ti + 1; ++ti; }
+      panel_tile_update(As, n0 + 4 * ti, n0 + 4 * tt, Lt, Lt, PLD, ti == tt);
     }
-    if (ty == jb && tx <= jb) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float rl = Rl[j];
-#pragma unroll
-        for (int v = 0; v < 8; ++v) {
-          const float xf = (j < nbk) ? x[j][v] * rl : 0.f;
-          x[j][v] = xf;
-          Xb[j][c0 + v] = xf;
-#pragma unroll
-          for (int u = j + 1; u < 8; ++u) x[u][v] = fmaf(-Ld[u][j], xf, x[u][v]);
+    __syncthreads();
+    if (warp == 0) {
+      panel_factor_sub(As, n0, Lc, rls, flag, k0, lane);
+    } else {
+      // rest of the trailing lower part (rows from n0 + 32) and the Y rows below s
+      const int rows_t = (rend - n0 - PSUB) / 4;        // tile rows under the next sub-block
+      const int cols_y = (c0 + PSUB) / 4;               // tile columns of X_s:
+      const int rows_y = (rend - n0) / 4;
+      // trailing tiles: tile row a (rows n0 + 32 + 4a) has columns n0 .. its diagonal
+      const int n_sy = rows_t * 8 + rows_t * (rows_t + 1) / 2;
+      const int n_tot = n_sy + rows_y * cols_y;
+      for (int id = t - 32; id < n_tot; id += PANEL_THREADS - 32) {
+        if (id < n_sy) {
+          // walk tile rows: row a holds 8 + a + 1 tiles
+          int a = 0, rem = id;
+          while (rem >= 9 + a) { rem -= 9 + a; ++a; }
+          const int i0 = n0 + PSUB + 4 * a, j0 = n0 + 4 * rem;
+          panel_tile_update(As, i0, j0, Lt, Lt, PLD, j0 == i0);
+        } else {
+          const int q = id - n_sy;
+          const int i0 = n0 + 4 * (q / cols_y), j0 = 4 * (q % cols_y);
+          panel_tile_update(Ys, i0, j0, Lt, Ys + c0 * PLD, PLD, false);
         }
       }
     }
     __syncthreads();
-    // ---- 3. rank-8 updates of the trailing lower tiles and of X
-    if (ty > jb) {
-      float lr[8][8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const float4 p0 = *reinterpret_cast<const float4*>(&Ls[k][r0]);
-        const float4 p1 = *reinterpret_cast<const float4*>(&Ls[k][r0 + 4]);
-        lr[k][0] = p0.x; lr[k][1] = p0.y; lr[k][2] = p0.z; lr[k][3] = p0.w;
-        lr[k][4] = p1.x; lr[k][5] = p1.y; lr[k][6] = p1.z; lr[k][7] = p1.w;
-      }
-      if (tx > jb && tx <= ty) {
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const float4 q0 = *reinterpret_cast<const float4*>(&Ls[k][c0]);
-          const float4 q1 = *reinterpret_cast<const float4*>(&Ls[k][c0 + 4]);
-          const float lc[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-#pragma unroll
-          for (int u = 0; u < 8; ++u)
-#pragma unroll
-            for (int v = 0; v < 8; ++v) a[u][v] = fmaf(-lr[k][u], lc[v], a[u][v]);
-        }
-      } else if (tx <= jb) {
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const float4 q0 = *reinterpret_cast<const float4*>(&Xb[k][c0]);
-          const float4 q1 = *reinterpret_cast<const float4*>(&Xb[k][c0 + 4]);
-          const float xc[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-#pragma unroll
-          for (int u = 0; u < 8; ++u)
-#pragma unroll
-            for (int v = 0; v < 8; ++v) x[u][v] = fmaf(-lr[k][u], xc[v], x[u][v]);
-        }
-      }
+  }
+  __syncthreads();
+  if (*flag) {
+    if (t == 0 && info) atomicCAS(info, 0, *flag);
+    // mark the inverse as NaN so downstream products are visibly invalid
+    for (int idx = t; idx < NB * NB; idx += PANEL_THREADS) Linv[idx] = __int_as_float(0x7fc00000);
+    return;
+  }
+  for (int idx = t; idx < NB * NB; idx += PANEL_THREADS) {
+    const int r = idx / NB, c = idx % NB;
+    Linv[idx] = (r < nb && c < nb) ? Ys[r * PLD + c] : 0.f;
+    if (r < nb && c <= r) A[(k0 + r) * C + k0 + c] = As[r * PLD + c];
+  }
+}
+
+// Products of a 128-wide strip with the panel's lower-triangular inverse Linv
+// (NB x NB, zero past nb), in place:
+//   RIGHT  S [n x nb] <- S Linv^T   (L_ik = A_ik Linv_kk^T, 64 rows per CTA)
+//   LEFT   S [nb x n] <- Linv S     (X_k: = Linv_kk Y_k:,   64 columns per CTA)
+// Each CTA stages Linv and its part of the strip in shared memory with all
+// loads in flight, then every thread accumulates a 4 x 8 (RIGHT) or 8 x 4
+// (LEFT) output tile over the nonzero part of Linv.  K is only 128, so a
+// k-tiled GEMM spends its time waiting on one small tile after another.
+constexpr int LA_ROWS = 64;   // strip rows (RIGHT) or columns (LEFT) per CTA
+constexpr int LA_LD = NB + 1;
+
+__host__ __device__ constexpr int linv_apply_smem_floats() {
+  return NB * LA_LD + LA_ROWS * LA_LD;
+}
+
+template <bool LEFT>
+__global__ void __launch_bounds__(256) linv_apply_kernel(float* S, long long lds, long long n,
+                                                         const float* __restrict__ Linv, int nb) {
+  extern __shared__ __align__(16) float lsm[];
+  float* Ls = lsm;                 // Linv[r][c] at Ls[r * LA_LD + c]
+  float* Bs = lsm + NB * LA_LD;    // strip part, [i][k]: i = strip row (RIGHT) / column (LEFT)
+  const int t = threadIdx.x;
+  const long long i0 = (long long)blockIdx.x * LA_ROWS;
+  for (int idx = t; idx < NB * NB; idx += 256) Ls[(idx / NB) * LA_LD + idx % NB] = Linv[idx];
+  if (!LEFT) {
+    // rows i0 .. i0+63, columns 0 .. nb-1 (consecutive threads: consecutive columns)
+    for (int idx = t; idx < LA_ROWS * NB; idx += 256) {
+      const int i = idx / NB, k = idx % NB;
+      const long long r = i0 + i;
+      Bs[i * LA_LD + k] = (r < n && k < nb) ? S[r * lds + k] : 0.f;
+    }
+  } else {
+    // rows 0 .. nb-1, columns i0 .. i0+63 (consecutive threads: consecutive columns)
+    for (int idx = t; idx < LA_ROWS * NB; idx += 256) {
+      const int k = idx / LA_ROWS, i = idx % LA_ROWS;
+      const long long c = i0 + i;
+      Bs[i * LA_LD + k] = (c < n && k < nb) ? S[k * lds + c] : 0.f;
     }
   }
   __syncthreads();
-  if (failed) {
-    // mark the inverse as NaN so downstream products are visibly invalid
-    for (int idx = t; idx < NB * NB; idx += blockDim.x) Linv[idx] = __int_as_float(0x7fc00000);
-    return;
+  // output o[i][c] = sum_{k <= c} Bs[i][k] Ls[c][k] for the thread's 4 strip
+  // entries i and 8 Linv rows c (c = Linv row, i.e. output column for RIGHT and
+  // output row for LEFT)
+  const int ti = t & 15, tc = t >> 4;
+  const int ib = ti * 4, cb = tc * 8;
+  float acc[4][8];
+#pragma unroll
+  for (int u = 0; u < 4; ++u)
+#pragma unroll
+    for (int v = 0; v < 8; ++v) acc[u][v] = 0.f;
+  const int kend = cb + 8 < nb ? cb + 8 : nb;
+#pragma unroll 4
+  for (int k = 0; k < kend; ++k) {
+    float a[4], b[8];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) a[u] = Bs[(ib + u) * LA_LD + k];
+#pragma unroll
+    for (int v = 0; v < 8; ++v) b[v] = Ls[(cb + v) * LA_LD + k];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+#pragma unroll
+      for (int v = 0; v < 8; ++v) acc[u][v] = fmaf(a[u], b[v], acc[u][v]);
   }
+  __syncthreads();
 #pragma unroll
-  for (int u = 0; u < 8; ++u)
+  for (int u = 0; u < 4; ++u)
 #pragma unroll
-    for (int v = 0; v < 8; ++v) {
-      const int r = r0 + u, c = c0 + v;
-      Linv[r * NB + c] = (r < nb && c < nb) ? x[u][v] : 0.f;
-      if (r < nb && c <= r) A[(k0 + r) * C + k0 + c] = a[u][v];
+    for (int v = 0; v < 8; ++v) Bs[(ib + u) * LA_LD + cb + v] = acc[u][v];
+  __syncthreads();
+  if (!LEFT) {
+    for (int idx = t; idx < LA_ROWS * NB; idx += 256) {
+      const int i = idx / NB, k = idx % NB;
+      const long long r = i0 + i;
+      if (r < n && k < nb) S[r * lds + k] = Bs[i * LA_LD + k];
     }
+  } else {
+    for (int idx = t; idx < LA_ROWS * NB; idx += 256) {
+      const int k = idx / LA_ROWS, i = idx % LA_ROWS;
+      const long long c = i0 + i;
+      if (c < n && k < nb) S[k * lds + c] = Bs[i * LA_LD + k];
+    }
+  }
+}
+
+template <bool LEFT>
+static int linv_apply(float* S, long long lds, long long n, const float* Linv, int nb,
+                      cudaStream_t st) {
+  if (n <= 0) return G2Q_OK;
+  static int done[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return G2Q_ERR_CUDA;
+  const size_t smem = linv_apply_smem_floats() * sizeof(float);
+  if (dev >= 64 || !done[dev]) {
+    if (cudaFuncSetAttribute(linv_apply_kernel<LEFT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem) != cudaSuccess)
+      return G2Q_ERR_CUDA;
+    if (dev < 64) done[dev] = 1;
+  }
+  linv_apply_kernel<LEFT><<<cdiv(n, LA_ROWS), 256, smem, st>>>(S, lds, n, Linv, nb);
+  G2Q_CHECK_LAUNCH();
+  return G2Q_OK;
 }
 
 // U[i][j] = X[C-1-i][C-1-j] for i <= j, 0 below; NaN -> info = -1.
@@ -317,8 +504,21 @@ static CholWs carve(float* ws, long long C) {
   return w;
 }
 
+static int panel_attr() {
+  static int done[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return G2Q_ERR_CUDA;
+  if (dev < 64 && done[dev]) return G2Q_OK;
+  if (cudaFuncSetAttribute(panel_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)(panel_smem_floats() * sizeof(float))) != cudaSuccess)
+    return G2Q_ERR_CUDA;
+  if (dev < 64) done[dev] = 1;
+  return G2Q_OK;
+}
+
 static int chol_one(float* U, const float* H, long long C, long long ldh, float damp_percent,
                     int* info, float* ws, int precision, cudaStream_t st) {
+  G2Q_TRY(panel_attr());
   CholWs w = carve(ws, C);
   float* A = w.A;
   float* Y = w.Y;
@@ -346,12 +546,12 @@ static int chol_one(float* U, const float* H, long long C, long long ldh, float 
     float* lsc = w.lsc + (kb & 1) * C;
     __half* x2[2] = {w.xk, w.xk + tsz};
     // ---- factorization (caller's stream): panel, TRSM, split, SYRK
-    panel_kernel<<<1, 256, 0, st>>>(A, C, k0, nb, linv, info);
+    panel_kernel<<<1, PANEL_THREADS, panel_smem_floats() * sizeof(float), st>>>(A, C, k0, nb,
+                                                                                linv, info);
     G2Q_CHECK_LAUNCH();
     if (rest > 0) {
       // L_ik = A_ik Linv_kk^T, in place in A
-      G2Q_TRY(simt_gemm_f32(A + (k0 + nb) * C + k0, C, A + (k0 + nb) * C + k0, C, false, linv,
-                            NB, true, rest, nb, nb, 0.f, 1.f, G2Q_MASK_FULL, st));
+      G2Q_TRY(linv_apply<false>(A + (k0 + nb) * C + k0, C, rest, linv, nb, st));
       if (use_tc) {
         // the inverse chain of step kb-2 used this L21^T buffer
         if (kb >= 2 && cudaStreamWaitEvent(st, ev[2 * (kb - 2) + 1], 0) != cudaSuccess)
@@ -368,8 +568,7 @@ static int chol_one(float* U, const float* H, long long C, long long ldh, float 
     if (cudaEventRecord(ev[2 * kb], st) != cudaSuccess) return G2Q_ERR_CUDA;
     // ---- inverse chain (side stream): X_k: = Linv_kk Y_k:, then Y_i: -= L_ik X_k:
     if (cudaStreamWaitEvent(side, ev[2 * kb], 0) != cudaSuccess) return G2Q_ERR_CUDA;
-    G2Q_TRY(simt_gemm_f32(Y + k0 * C, C, linv, NB, false, Y + k0 * C, C, false, nb, k0 + nb, nb,
-                          0.f, 1.f, G2Q_MASK_FULL, side));
+    G2Q_TRY(linv_apply<true>(Y + k0 * C, C, k0 + nb, linv, nb, side));
     if (rest > 0) {
       if (use_tc) {
         G2Q_TRY(split2h(Y + k0 * C, C, k0 + nb, nb, x2[0], x2[1], C, w.xsc, 0, side));

@@ -46,20 +46,49 @@ struct BlockParams {
 // shuffle and one update instead of a whole-row sweep per thread, and each
 // element still receives its updates in column order, as in the reference.
 // Errors are staged in shared memory and written out after the last column.
-constexpr int QT = 8;             // threads per row
-constexpr int SEG = BLK / QT;     // block columns per thread
-constexpr int USEG = SEG + 4;     // padded segment: a row's segments start on distinct banks
-constexpr int LDU = QT * USEG;    // shared-memory row of the U (and P) block
-constexpr int QROWS = 32;         // rows per CTA
-constexpr int LDE = BLK + 1;      // staged error row
+template <int QT_, int QROWS_>
+struct BlockShape {
+  static constexpr int QT = QT_;            // threads per row
+  static constexpr int SEG = BLK / QT;      // block columns per thread
+  static constexpr int USEG = SEG + 4;      // padded segment: a row's segments start on distinct banks
+  static constexpr int LDU = QT * USEG;     // shared-memory row of the U (and P) block
+  static constexpr int QROWS = QROWS_;      // rows per CTA
+  static constexpr int LDE = BLK + 1;       // staged error row
+  static constexpr int THREADS = QT * QROWS;
+  static constexpr int smem_floats(int method) {
+    return BLK * LDU * (method == G2Q_METHOD_GPTAQ ? 2 : 1) +
+           QROWS * LDE * (method == G2Q_METHOD_G2PTQ ? 2 : 1);
+  }
+};
+// Sixteen threads per row (eight columns each), sixteen rows per CTA: twice the
+// warps of an eight-thread split for the same rows, which the latency-bound
+// column loop needs to hide its dependent chains; two CTAs fit on an SM.
+using BlockCfg = BlockShape<16, 16>;
 
-__host__ __device__ constexpr int block_smem_floats(int method) {
-  return BLK * LDU * (method == G2Q_METHOD_GPTAQ ? 2 : 1) +
-         QROWS * LDE * (method == G2Q_METHOD_G2PTQ ? 2 : 1);
+// rint(x / s) of the correctly rounded quotient, from a multiply by rs = 1 / s:
+// x * rs lies within two units in the last place of the rounded quotient, so
+// both round to the same integer unless a half-integer lies within a few
+// units; only then the division itself is evaluated.
+__device__ __forceinline__ float rint_quot(float x, float s, float rs) {
+  const float q0 = x * rs;
+  const float h = floorf(q0) + 0.5f;
+  if (fabsf(q0 - h) <= fabsf(q0) * 0x1p-20f) return rintf(x / s);
+  return rintf(q0);
+}
+
+// num / d rounded to nearest from rd = 1 / d: the product num * rd and one
+// residual correction, r = num - d q (exact in an fma), q + r rd (Markstein's
+// correction step for division with a correctly rounded reciprocal).
+__device__ __forceinline__ float div_rn(float num, float d, float rd) {
+  const float q = num * rd;
+  const float r = fmaf(-q, d, num);
+  return fmaf(r, rd, q);
 }
 
 template <int METHOD>
-__global__ void __launch_bounds__(QT * QROWS, 1) block_kernel(BlockParams P) {
+__global__ void __launch_bounds__(BlockCfg::THREADS, 2) block_kernel(BlockParams P) {
+  constexpr int QT = BlockCfg::QT, SEG = BlockCfg::SEG, USEG = BlockCfg::USEG;
+  constexpr int LDU = BlockCfg::LDU, QROWS = BlockCfg::QROWS, LDE = BlockCfg::LDE;
   extern __shared__ __align__(16) float smem[];
   float* Us = smem;              // [BLK][LDU], segment-padded
   float* Ps = Us + BLK * LDU;    // GPTAQ P block, same layout
@@ -123,33 +152,54 @@ __global__ void __launch_bounds__(QT * QROWS, 1) block_kernel(BlockParams P) {
   }
   __syncthreads();
 
+  // per-column reciprocals (off the column chain): 1 / scale, U's diagonal and
+  // its reciprocal for the columns this thread owns
+  float rsv[SEG], dv[SEG], rdv[SEG];
+#pragma unroll
+  for (int k = 0; k < SEG; ++k) {
+    const int col = t * SEG + k;
+    rsv[k] = 1.f / sv[k];
+    dv[k] = col < nc ? Us[col * LDU + t * USEG + k] : 1.f;
+    rdv[k] = 1.f / dv[k];
+  }
+
   uint32_t cw[SEG / 4];
 #pragma unroll
   for (int k = 0; k < SEG / 4; ++k) cw[k] = 0u;
   const float qlo = -(float)(P.maxq + 1), qhi = (float)P.maxq;
 
+  // The error of column i reaches the other threads one column late: at column
+  // i + 1 every thread first quantizes (the owner), then applies column i's
+  // shuffled error to its own later columns.  The owner carries its next
+  // column's value in `wn` (and `gn`), updated with its own error directly, so
+  // the chain from one column to the next holds no shuffle and no shared
+  // memory load.  Every element still receives its updates in column order.
+  float e_prev = 0.f, aux_prev = 0.f;
 #pragma unroll 1
   for (int tw = 0; tw < QT; ++tw) {
     if (tw * SEG >= nc) break;
-    const bool after = t >= tw;  // updates of columns j > k of segment tw
-    const bool later = t > tw;   // updates of columns j <= k (later segments only)
+    const bool after = t >= tw;  // the owner's columns after the current one
+    const bool later = t > tw;   // every column of the threads after the owner
+    float wn = wv[0], gn = gv[0];
+    int klast = 0;
 #pragma unroll
     for (int k = 0; k < SEG; ++k) {
       const int i = tw * SEG + k;
       if (i >= nc) break;
+      klast = k;
       float e = 0.f, aux = 0.f;
       if (t == tw) {
         const float s = sv[k];
         const float zz = zv[k];
-        const float d = Us[i * LDU + tw * USEG + k];
-        const float wc = wv[k];
-        float q = rintf(wc / s) + zz;
+        const float wc = wn;
+        float q = rint_quot(wc, s, rsv[k]) + zz;
         q = fminf(fmaxf(q, qlo), qhi);
         const float qv = s * (q - zz);
         if (METHOD == G2Q_METHOD_G2PTQ) {
-          e = (wc - qv - gv[k]) / d;
+          e = div_rn(wc - qv - gn, dv[k], rdv[k]);
+          gv[k] = gn;
         } else {
-          e = (wc - qv) / d;
+          e = div_rn(wc - qv, dv[k], rdv[k]);
         }
         aux = (METHOD == G2Q_METHOD_G2PTQ) ? xv[k] : wc;
         wv[k] = qv;
@@ -158,8 +208,57 @@ __global__ void __launch_bounds__(QT * QROWS, 1) block_kernel(BlockParams P) {
         if (METHOD == G2Q_METHOD_G2PTQ)
           EAs[rl * LDE + i] = e - xv[k] * (float)(P.dfact - 1 - i);
       }
-      e = __shfl_sync(0xffffffffu, e, src0 + tw);
-      if (METHOD != G2Q_METHOD_GPTQ) aux = __shfl_sync(0xffffffffu, aux, src0 + tw);
+      const float e_sh = __shfl_sync(0xffffffffu, e, src0 + tw);
+      const float aux_sh =
+          (METHOD != G2Q_METHOD_GPTQ) ? __shfl_sync(0xffffffffu, aux, src0 + tw) : 0.f;
+      // column i - 1's update of this thread's columns after i (the owner's
+      // column i received it through wn)
+      if (k > 0) {
+        const float* urow = Us + (i - 1) * LDU + t * USEG;
+        const float* prow_s = Ps + (i - 1) * LDU + t * USEG;
+#pragma unroll
+        for (int j4 = 0; j4 < SEG; j4 += 4) {
+          const float4 u4 = *reinterpret_cast<const float4*>(urow + j4);
+          const float uu[4] = {u4.x, u4.y, u4.z, u4.w};
+          float pp[4] = {0.f, 0.f, 0.f, 0.f};
+          if (METHOD == G2Q_METHOD_GPTAQ) {
+            const float4 p4 = *reinterpret_cast<const float4*>(prow_s + j4);
+            pp[0] = p4.x; pp[1] = p4.y; pp[2] = p4.z; pp[3] = p4.w;
+          }
+#pragma unroll
+          for (int m = 0; m < 4; ++m) {
+            const int j = j4 + m;
+            if (j > k ? after : later) {
+              if (METHOD == G2Q_METHOD_G2PTQ) {
+                wv[j] = fmaf(-e_prev, uu[m], wv[j] - gv[j]);
+                gv[j] = fmaf(-aux_prev, uu[m], gv[j]);
+              } else if (METHOD == G2Q_METHOD_GPTAQ) {
+                wv[j] = fmaf(pp[m], aux_prev, fmaf(-e_prev, uu[m], wv[j]));
+              } else {
+                wv[j] = fmaf(-e_prev, uu[m], wv[j]);
+              }
+            }
+          }
+        }
+      }
+      // the owner's next column with column i's own update
+      if (k + 1 < SEG) {
+        const float u1 = Us[i * LDU + tw * USEG + k + 1];
+        if (METHOD == G2Q_METHOD_G2PTQ) {
+          wn = fmaf(-e, u1, wv[k + 1] - gv[k + 1]);
+          gn = fmaf(-aux, u1, gv[k + 1]);
+        } else if (METHOD == G2Q_METHOD_GPTAQ) {
+          wn = fmaf(Ps[i * LDU + tw * USEG + k + 1], aux, fmaf(-e, u1, wv[k + 1]));
+        } else {
+          wn = fmaf(-e, u1, wv[k + 1]);
+        }
+      }
+      e_prev = e_sh;
+      aux_prev = aux_sh;
+    }
+    // the segment's last column updates every column of the threads after it
+    if (later) {
+      const int i = tw * SEG + klast;
       const float* urow = Us + i * LDU + t * USEG;
       const float* prow_s = Ps + i * LDU + t * USEG;
 #pragma unroll
@@ -174,15 +273,13 @@ __global__ void __launch_bounds__(QT * QROWS, 1) block_kernel(BlockParams P) {
 #pragma unroll
         for (int m = 0; m < 4; ++m) {
           const int j = j4 + m;
-          if (j > k ? after : later) {
-            if (METHOD == G2Q_METHOD_G2PTQ) {
-              wv[j] = fmaf(-e, uu[m], wv[j] - gv[j]);
-              gv[j] = fmaf(-aux, uu[m], gv[j]);
-            } else if (METHOD == G2Q_METHOD_GPTAQ) {
-              wv[j] = fmaf(pp[m], aux, fmaf(-e, uu[m], wv[j]));
-            } else {
-              wv[j] = fmaf(-e, uu[m], wv[j]);
-            }
+          if (METHOD == G2Q_METHOD_G2PTQ) {
+            wv[j] = fmaf(-e_prev, uu[m], wv[j] - gv[j]);
+            gv[j] = fmaf(-aux_prev, uu[m], gv[j]);
+          } else if (METHOD == G2Q_METHOD_GPTAQ) {
+            wv[j] = fmaf(pp[m], aux_prev, fmaf(-e_prev, uu[m], wv[j]));
+          } else {
+            wv[j] = fmaf(-e_prev, uu[m], wv[j]);
           }
         }
       }
@@ -220,7 +317,9 @@ __global__ void __launch_bounds__(QT * QROWS, 1) block_kernel(BlockParams P) {
   }
 }
 
-static size_t block_smem(int method) { return (size_t)block_smem_floats(method) * sizeof(float); }
+static size_t block_smem(int method) {
+  return (size_t)BlockCfg::smem_floats(method) * sizeof(float);
+}
 
 template <int METHOD>
 static int launch_block_t(const BlockParams& P, long long batch, cudaStream_t st) {
@@ -234,9 +333,9 @@ static int launch_block_t(const BlockParams& P, long long batch, cudaStream_t st
       return G2Q_ERR_CUDA;
     if (dev < 64) attr_done[dev] = 1;
   }
-  dim3 grid(cdiv(P.rows, QROWS), (unsigned)batch);
+  dim3 grid(cdiv(P.rows, BlockCfg::QROWS), (unsigned)batch);
   if (grid.y > 65535u) return G2Q_ERR_INVALID_ARG;
-  block_kernel<METHOD><<<grid, QT * QROWS, smem, st>>>(P);
+  block_kernel<METHOD><<<grid, BlockCfg::THREADS, smem, st>>>(P);
   G2Q_CHECK_LAUNCH();
   return G2Q_OK;
 }
@@ -539,6 +638,20 @@ extern "C" int g2q_find_params(float* scale, float* zero, int64_t param_ld, cons
     return G2Q_ERR_INVALID_ARG;
   return launch_find_params(scale, zero, param_ld, W, rows, cols, ldw, bits, sym, status,
                             -1, 1, 0, cols, nullptr, (cudaStream_t)stream);
+}
+
+extern "C" int g2q_find_params_groups(float* scale, float* zero, int64_t param_ld,
+                                      const float* W, int64_t rows, int64_t C, int64_t ldw,
+                                      int bits, int sym, int64_t first, int count, int groupsize,
+                                      int* status, void* stream) {
+  if (!scale || !zero || !W || rows < 0 || C <= 0 || ldw < C || bits < 1 || bits > 16 ||
+      groupsize <= 0 || count < 0 || first < 0 || first % groupsize != 0 ||
+      (count > 0 && first + (int64_t)(count - 1) * groupsize >= C) ||
+      param_ld < (first / groupsize) + count)
+    return G2Q_ERR_INVALID_ARG;
+  if (count == 0) return G2Q_OK;
+  return launch_find_params(scale, zero, param_ld, W, rows, 0, ldw, bits, sym, status, first,
+                            count, groupsize, C, nullptr, (cudaStream_t)stream);
 }
 
 extern "C" int g2q_find_params_clip(float* scale, float* zero, int64_t param_ld, const float* W,

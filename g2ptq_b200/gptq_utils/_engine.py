@@ -144,8 +144,24 @@ class ParamSet:
         self.columns = columns
 
     def init_static(self, W_flat, H_diag=None):
-        """gptq_utils.py:259-270 for ungrouped / static-group quantizers."""
+        """gptq_utils.py:259-270 for ungrouped / static-group quantizers.
+
+        Fresh per-channel quantizers of one configuration without the clip
+        search (the usual case) get their parameters from a single launch over
+        all groups instead of one ``find_params`` call each."""
         gs = self.groupsize
+        qs = self.quantizers
+        q0 = qs[0]
+        if (gs > 0 and len(qs) == (self.columns + gs - 1) // gs and q0.bits < 16
+                and all(not q.ready() and not q.mse and q.perchannel and q.bits == q0.bits
+                        and q.sym == q0.sym and getattr(q, "weight_groupsize", -1) <= 0
+                        for q in qs)):
+            ops.find_params_groups(self.scale, self.zero, W_flat, q0.bits, q0.sym, gs,
+                                   self.status)
+            for i, q in enumerate(qs):
+                q.scale, q.zero = self.scale[:, i:i + 1], self.zero[:, i:i + 1]
+                q._ready = True
+            return
         for i, q in enumerate(self.quantizers):
             sv = self.scale[:, i:i + 1]
             zv = self.zero[:, i:i + 1]

@@ -74,8 +74,8 @@ class G2PTQ(_engine.StagingMixin):
         self._H = torch.zeros((self.num_layers, num_groups, self.columns, self.columns),
                               dtype=torch.float32, device=H_device)
         self.act_square = torch.zeros((self.num_layers, self.columns), device=self.dev)
-        self.index = torch.tensor([0] * self.num_layers, device=self.dev)
-        self.total_tokens = torch.tensor([0] * self.num_layers, device=self.dev)
+        self.index = torch.zeros(self.num_layers, dtype=torch.long, device=self.dev)
+        self.total_tokens = torch.zeros(self.num_layers, dtype=torch.long, device=self.dev)
         self._k = [0] * self.num_layers
         self._k_folded = [0] * self.num_layers
         self._tok = [0] * self.num_layers

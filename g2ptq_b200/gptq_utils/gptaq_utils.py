@@ -53,7 +53,7 @@ class GPTAQ(_engine.StagingMixin):
         self._H = torch.zeros((self.num_layers, self.columns, self.columns),
                               dtype=torch.float32, device=H_device)
         self._dXXT = torch.zeros_like(self._H)
-        self.nsamples = torch.tensor([0] * self.num_layers, device=self.dev)
+        self.nsamples = torch.zeros(self.num_layers, dtype=torch.long, device=self.dev)
         self.fp_inp = [[] for _ in range(self.num_layers)]
         self._n = [0] * self.num_layers
         self._n_folded = [0] * self.num_layers

@@ -31,7 +31,7 @@ class GPTQGuided(GPTQ):
         self._H = torch.zeros((self.num_layers, num_groups, self.columns, self.columns),
                               dtype=torch.float32, device=H_device)
         self.act_square = torch.zeros((self.num_layers, self.columns), device=self.dev)
-        self.index = torch.tensor([0] * self.num_layers, device=self.dev)
+        self.index = torch.zeros(self.num_layers, dtype=torch.long, device=self.dev)
         self._idx = [0] * self.num_layers
         assert self.rows % self.num_groups == 0, (
             f"Number of rows ({self.rows}) must be divisible by num_groups ({self.num_groups})")

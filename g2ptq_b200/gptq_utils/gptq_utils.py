@@ -52,7 +52,7 @@ class GPTQ(_engine.StagingMixin):
         H_device = "cpu" if offload_hessians else self.dev
         self._H = torch.zeros((self.num_layers, self.columns, self.columns),
                               dtype=torch.float32, device=H_device)
-        self.nsamples = torch.tensor([0] * self.num_layers, device=self.dev)
+        self.nsamples = torch.zeros(self.num_layers, dtype=torch.long, device=self.dev)
         self._n = [0] * self.num_layers          # host copy of nsamples
         self._n_folded = [0] * self.num_layers   # samples already folded into H
         self._init_stages()

@@ -169,6 +169,19 @@ def find_params(scale, zero, W, bits, sym, status=None, param_col=0):
          W.stride(0), bits, int(bool(sym)), _ptr(status), _stream(W))
 
 
+def find_params_groups(scale, zero, W, bits, sym, groupsize, status=None):
+    """``find_params`` of every ``groupsize``-column group of ``W [rows, C]`` in
+    one launch, group ``g`` into column ``g`` of ``scale`` / ``zero``."""
+    _cuda(scale, zero, W, status)
+    rows, C = W.shape
+    if W.stride(1) != 1 or scale.stride(1) != 1 or zero.stride() != scale.stride():
+        raise ValueError("find_params_groups expects unit column strides")
+    count = (C + groupsize - 1) // groupsize
+    call("g2q_find_params_groups", scale.data_ptr(), zero.data_ptr(), scale.stride(0),
+         W.data_ptr(), rows, C, W.stride(0), bits, int(bool(sym)), 0, count, groupsize,
+         _ptr(status), _stream(W))
+
+
 def clip_config(grid=50, maxshrink=0.5, norm=2.4, hdiag=None, rows_per_block=None):
     """``g2q_clip_t`` for the clip search; ``hdiag [blocks, C]`` (contiguous
     rows) switches to the Hessian-weighted error, each block of

@@ -21,10 +21,15 @@ def compress_grouped(layer, group_scale, codes, bits):
     ``[rows, columns]`` int8 code matrix.
     """
     weight = layer.weight
+    # torch.tensor(weight.shape) on the device, filled there: a copy from pageable
+    # host memory would synchronise the stream
+    shape = torch.empty(weight.dim(), dtype=torch.long, device=weight.device)
+    for i, n in enumerate(weight.shape):
+        shape[i] = n
     layer._export_qparams = {
         "weight_packed": ops.pack_int32(codes.contiguous(), bits),
         "weight_scale": group_scale.to(weight.dtype).contiguous(),
-        "weight_shape": torch.tensor(weight.shape).to(weight.device).contiguous(),
+        "weight_shape": shape,
     }
 
 

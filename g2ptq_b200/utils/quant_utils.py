@@ -6,6 +6,8 @@ with every computation done by the sm_100a kernels of ``libg2ptq_b200``.
 Tensors must live on a CUDA device.
 """
 
+import copy
+
 import torch
 
 from .. import ops
@@ -61,6 +63,30 @@ class WeightQuantizer(torch.nn.Module):
         self.minq = -(self.maxq + 1)
         self.bit_range = self.maxq - self.minq
         self._ready = False
+
+    def __deepcopy__(self, memo):
+        """What ``copy.deepcopy`` makes of the quantizer, without the generic
+        ``nn.Module`` traversal: ``make_group_quantizers`` copies one quantizer
+        per weight group (hundreds per decoder layer), and the generic path
+        costs about a tenth of a millisecond each.  Tensors are cloned, the
+        module's bookkeeping dicts copied; the device status word is left for
+        the copy to allocate."""
+        cls = self.__class__
+        new = cls.__new__(cls)
+        memo[id(self)] = new
+        d = new.__dict__
+        for k, v in self.__dict__.items():
+            if k == "_status":
+                v = None
+            elif isinstance(v, torch.Tensor):
+                v = v.clone()
+            elif isinstance(v, dict):
+                v = type(v)((kk, vv.clone() if isinstance(vv, torch.Tensor)
+                             else copy.deepcopy(vv, memo)) for kk, vv in v.items())
+            elif not isinstance(v, (bool, int, float, str, type(None))):
+                v = copy.deepcopy(v, memo)
+            d[k] = v
+        return new
 
     def status_tensor(self, device):
         if self._status is None or self._status.device != device:

@@ -179,6 +179,18 @@ int g2q_find_params(float* scale, float* zero, int64_t param_ld,
                     const float* W, int64_t rows, int64_t cols, int64_t ldw,
                     int bits, int sym, int* status, void* stream);
 
+/* g2q_find_params for `count` consecutive weight groups in one launch: group g
+ * covers columns first + g * groupsize .. (clipped at C) of W [rows, C]
+ * (row stride ldw) and writes column first / groupsize + g of scale / zero
+ * [rows, param_ld]; first is a multiple of groupsize.  Each group's result is
+ * that of g2q_find_params on its columns.
+ * Replaces the per-group WeightQuantizer.find_params loop of fasterquant's
+ * static-group set-up, gptq_utils/gptq_utils.py:259-270. */
+int g2q_find_params_groups(float* scale, float* zero, int64_t param_ld,
+                           const float* W, int64_t rows, int64_t C, int64_t ldw,
+                           int bits, int sym, int64_t first, int count, int groupsize,
+                           int* status, void* stream);
+
 /* Clip search of WeightQuantizer.find_params (--w_clip / --w_hclip).  The
  * range [xmin, xmax] is shrunk on a grid, xmin * (1 - i/grid) and
  * xmax * (1 - j/grid) for i, j < maxshrink * grid, and the first (i, j) with

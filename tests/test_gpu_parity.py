@@ -160,6 +160,23 @@ def test_find_params_and_fake_quantize(golden, bits, sym):
     close(fq, m[tag + "_fq"], rtol=1e-6, atol=1e-9)
 
 
+@pytest.mark.parametrize("bits,sym", [(4, True), (3, False), (2, False)])
+def test_find_params_groups_matches_per_group(bits, sym):
+    """One launch over all groups (static-group set-up) = one call per group,
+    bit for bit, ragged last group included."""
+    g = torch.Generator(device=DEV).manual_seed(bits)
+    rows, C, gs = 300, 1376, 128
+    W = torch.randn(rows, C, device=DEV, generator=g) * 0.02
+    W[:, 7] *= 40
+    ng = (C + gs - 1) // gs
+    s1, z1 = torch.empty(rows, ng, device=DEV), torch.empty(rows, ng, device=DEV)
+    ops.find_params_groups(s1, z1, W, bits, sym, gs)
+    s2, z2 = torch.empty_like(s1), torch.empty_like(z1)
+    for gi in range(ng):
+        ops.find_params(s2, z2, W[:, gi * gs:(gi + 1) * gs], bits, sym, param_col=gi)
+    assert torch.equal(s1, s2) and torch.equal(z1, z2)
+
+
 @pytest.mark.parametrize("bits", [2, 3, 4, 8])
 def test_pack_int32(golden, bits):
     m = golden("misc.npz")
@@ -201,6 +218,58 @@ def test_block_kernels_vs_reference(golden, name):
     close(qi, g[f"{name}__gptaq_int"], rtol=0, atol=0)
     close(W, g[f"{name}__gptaq_q"])
     close(er, g[f"{name}__gptaq_err"])
+
+
+@pytest.mark.parametrize("coupled", [False, True])
+def test_block_kernels_at_rounding_ties(coupled):
+    """Weights whose quotient w / s sits on or within two units in the last
+    place of a half-integer: the block kernels take the quotient from a
+    multiply by 1 / s and must fall back to the division exactly where the
+    rounding could differ.  ``coupled`` adds small off-diagonal U entries, so
+    that the later columns move off the ties through the updates."""
+    rng = np.random.default_rng(11)
+    B, cols, R, maxq = 2, 128, 320, 7
+    scale = rng.uniform(1e-3, 1e-2, (B, cols, R)).astype(np.float32)
+    zero = np.zeros_like(scale)
+    n = rng.integers(-9, 9, (B, cols, R)).astype(np.float32)
+    w = ((n + np.float32(0.5)) * scale).astype(np.float32)
+    steps = rng.integers(-2, 3, w.shape)
+    for _ in range(2):
+        w = np.where(steps > 0, np.nextafter(w, np.float32(np.inf)), w)
+        w = np.where(steps < 0, np.nextafter(w, np.float32(-np.inf)), w)
+        steps = steps - np.sign(steps)
+    hinv = np.zeros((B, cols, cols), np.float32)
+    idx = np.arange(cols)
+    hinv[:, idx, idx] = rng.uniform(0.5, 1.5, (B, cols)).astype(np.float32)
+    if coupled:
+        hinv += np.triu(rng.standard_normal((B, cols, cols)).astype(np.float32) * 1e-3, 1)
+    ratio = w / scale
+    assert np.mean(np.abs(np.abs(ratio - np.floor(ratio)) - 0.5) < 1e-5) > 0.5
+    wt, qi = t(w), torch.empty(B, cols, R, device=DEV)
+    er = torch.empty_like(qi)
+    W = wt.clone()
+    gptq_utils.run_eager(W, t(hinv), t(scale), t(zero), maxq, int_weight=qi, error=er)
+    ow, oq, oe = ocomp.gptq_block(w, hinv, scale, zero, maxq)
+    close(qi, oq, rtol=0, atol=0)
+    close(W, ow)
+    close(er, oe)
+    p = np.triu(rng.standard_normal((B, cols, cols)).astype(np.float32) * 1e-3, 1)
+    W = wt.clone()
+    gptaq_utils.run_eager(W, t(hinv), t(p), t(scale), t(zero), maxq, int_weight=qi, error=er)
+    ow, oq, oe = ocomp.gptaq_block(w, hinv, p, scale, zero, maxq)
+    close(qi, oq, rtol=0, atol=0)
+    close(W, ow)
+    close(er, oe)
+    z = (rng.standard_normal((B, cols, R)) * 1e-4).astype(np.float32)
+    gh0 = (rng.standard_normal((B, cols, R)) * 1e-6).astype(np.float32)
+    W, gh = wt.clone(), t(gh0)
+    g2ptq_utils.run_eager(W, t(hinv), t(scale), t(zero), t(z), gh, maxq, int_weight=qi,
+                          error=er)
+    ow, oq, oe, og = ocomp.g2ptq_block(w, hinv, scale, zero, z, gh0, maxq)
+    close(qi, oq, rtol=0, atol=0)
+    close(W, ow)
+    close(er, oe)
+    close(gh, og)
 
 
 # ---------------------------------------------------------------------------
@@ -305,6 +374,8 @@ def test_gptq_fasterquant_vs_reference(golden, case):
             from oracle.export import pack_to_int32
             ref_packed = pack_to_int32(ref_int[b].astype(np.int8), bits)
             assert float(np.mean(packed == ref_packed)) >= 0.99
+            shape = l._export_qparams["weight_shape"]
+            assert shape.dtype == torch.int64 and shape.cpu().tolist() == [R, C]
 
 
 @pytest.mark.parametrize("case", FQ_CASES, ids=[c[0] for c in FQ_CASES])
