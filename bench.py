@@ -80,10 +80,10 @@ def load_peaks():
 
 
 # DRAM traffic of one Gram fold at the bench's 4096-column fold shape (16384 BF16
-# tokens), dram__bytes_read.sum + dram__bytes_write.sum from one ncu capture
-# (profiles/gram_tc_wide_c4096_t16384.md); the algorithmic bytes of that launch
-# are 268.4 MB (X once, H read and written once).
-GRAM_FOLD_TRAFFIC_BYTES = 310.19e6
+# tokens), dram__bytes_read.sum + dram__bytes_write.sum from one ncu capture of
+# the CTA-pair kernel (profiles/gram_pair_c4096_t16384.md); the algorithmic bytes
+# of that launch are 268.4 MB (X once, H read and written once).
+GRAM_FOLD_TRAFFIC_BYTES = 317.06e6
 # device buffers (one calibration sequence each) of the host-input copy ring
 E2E_RING = 48
 GRAM_FOLD_ALGORITHMIC_BYTES = 268.44e6
