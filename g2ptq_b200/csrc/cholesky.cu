@@ -307,45 +307,51 @@ __global__ void __launch_bounds__(PANEL_THREADS, 1)
 // (NB x NB, zero past nb), in place:
 //   RIGHT  S [n x nb] <- S Linv^T   (L_ik = A_ik Linv_kk^T, 64 rows per CTA)
 //   LEFT   S [nb x n] <- Linv S     (X_k: = Linv_kk Y_k:,   64 columns per CTA)
-// Each CTA stages Linv and its part of the strip in shared memory with all
-// loads in flight, then every thread accumulates a 4 x 8 (RIGHT) or 8 x 4
-// (LEFT) output tile over the nonzero part of Linv.  K is only 128, so a
-// k-tiled GEMM spends its time waiting on one small tile after another.
-constexpr int LA_ROWS = 64;   // strip rows (RIGHT) or columns (LEFT) per CTA
-constexpr int LA_LD = NB + 1;
+// Each CTA stages Linv^T and its part of the strip (k-major) in shared memory
+// with all loads in flight, then every thread accumulates a 4 x 8 output tile
+// over the nonzero part of Linv from three 16-byte shared loads per k.  K is
+// only 128, so a k-tiled GEMM spends its time waiting on one small tile after
+// another.
+constexpr int LA_ROWS = 64;        // strip rows (RIGHT) or columns (LEFT) per CTA
+constexpr int LA_LDT = NB + 4;     // Lt[k][c] = Linv[c][k]
+constexpr int LA_LDB = LA_ROWS + 4;  // Bt[k][i]: strip entry i, index k
+constexpr int LA_LDO = NB + 1;     // Os[i][c]: results
 
 __host__ __device__ constexpr int linv_apply_smem_floats() {
-  return NB * LA_LD + LA_ROWS * LA_LD;
+  return NB * LA_LDT + NB * LA_LDB;
 }
 
 template <bool LEFT>
 __global__ void __launch_bounds__(256) linv_apply_kernel(float* S, long long lds, long long n,
                                                          const float* __restrict__ Linv, int nb) {
   extern __shared__ __align__(16) float lsm[];
-  float* Ls = lsm;                 // Linv[r][c] at Ls[r * LA_LD + c]
-  float* Bs = lsm + NB * LA_LD;    // strip part, [i][k]: i = strip row (RIGHT) / column (LEFT)
+  float* Lt = lsm;                 // [NB][LA_LDT]
+  float* Bt = lsm + NB * LA_LDT;   // [NB][LA_LDB]
+  float* Os = Bt;                  // [LA_ROWS][LA_LDO], reuses Bt after the products
   const int t = threadIdx.x;
   const long long i0 = (long long)blockIdx.x * LA_ROWS;
-  for (int idx = t; idx < NB * NB; idx += 256) Ls[(idx / NB) * LA_LD + idx % NB] = Linv[idx];
+  for (int idx = t; idx < NB * NB; idx += 256) {
+    const int c = idx / NB, k = idx % NB;
+    Lt[k * LA_LDT + c] = Linv[idx];
+  }
   if (!LEFT) {
     // rows i0 .. i0+63, columns 0 .. nb-1 (consecutive threads: consecutive columns)
     for (int idx = t; idx < LA_ROWS * NB; idx += 256) {
       const int i = idx / NB, k = idx % NB;
       const long long r = i0 + i;
-      Bs[i * LA_LD + k] = (r < n && k < nb) ? S[r * lds + k] : 0.f;
+      Bt[k * LA_LDB + i] = (r < n && k < nb) ? S[r * lds + k] : 0.f;
     }
   } else {
     // rows 0 .. nb-1, columns i0 .. i0+63 (consecutive threads: consecutive columns)
     for (int idx = t; idx < LA_ROWS * NB; idx += 256) {
       const int k = idx / LA_ROWS, i = idx % LA_ROWS;
       const long long c = i0 + i;
-      Bs[i * LA_LD + k] = (c < n && k < nb) ? S[k * lds + c] : 0.f;
+      Bt[k * LA_LDB + i] = (c < n && k < nb) ? S[k * lds + c] : 0.f;
     }
   }
   __syncthreads();
-  // output o[i][c] = sum_{k <= c} Bs[i][k] Ls[c][k] for the thread's 4 strip
-  // entries i and 8 Linv rows c (c = Linv row, i.e. output column for RIGHT and
-  // output row for LEFT)
+  // o[i][c] = sum_{k <= c} Bt[k][i] Lt[k][c] for the thread's 4 strip entries i
+  // and 8 Linv rows c (output columns for RIGHT, output rows for LEFT)
   const int ti = t & 15, tc = t >> 4;
   const int ib = ti * 4, cb = tc * 8;
   float acc[4][8];
@@ -356,11 +362,11 @@ __global__ void __launch_bounds__(256) linv_apply_kernel(float* S, long long lds
   const int kend = cb + 8 < nb ? cb + 8 : nb;
 #pragma unroll 4
   for (int k = 0; k < kend; ++k) {
-    float a[4], b[8];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) a[u] = Bs[(ib + u) * LA_LD + k];
-#pragma unroll
-    for (int v = 0; v < 8; ++v) b[v] = Ls[(cb + v) * LA_LD + k];
+    const float4 a4 = *reinterpret_cast<const float4*>(Bt + k * LA_LDB + ib);
+    const float4 b0 = *reinterpret_cast<const float4*>(Lt + k * LA_LDT + cb);
+    const float4 b1 = *reinterpret_cast<const float4*>(Lt + k * LA_LDT + cb + 4);
+    const float a[4] = {a4.x, a4.y, a4.z, a4.w};
+    const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll
     for (int u = 0; u < 4; ++u)
 #pragma unroll
@@ -370,19 +376,19 @@ __global__ void __launch_bounds__(256) linv_apply_kernel(float* S, long long lds
 #pragma unroll
   for (int u = 0; u < 4; ++u)
 #pragma unroll
-    for (int v = 0; v < 8; ++v) Bs[(ib + u) * LA_LD + cb + v] = acc[u][v];
+    for (int v = 0; v < 8; ++v) Os[(ib + u) * LA_LDO + cb + v] = acc[u][v];
   __syncthreads();
   if (!LEFT) {
     for (int idx = t; idx < LA_ROWS * NB; idx += 256) {
       const int i = idx / NB, k = idx % NB;
       const long long r = i0 + i;
-      if (r < n && k < nb) S[r * lds + k] = Bs[i * LA_LD + k];
+      if (r < n && k < nb) S[r * lds + k] = Os[i * LA_LDO + k];
     }
   } else {
     for (int idx = t; idx < LA_ROWS * NB; idx += 256) {
       const int k = idx / LA_ROWS, i = idx % LA_ROWS;
       const long long c = i0 + i;
-      if (c < n && k < nb) S[k * lds + c] = Bs[i * LA_LD + k];
+      if (c < n && k < nb) S[k * lds + c] = Os[i * LA_LDO + k];
     }
   }
 }

@@ -152,6 +152,18 @@ __device__ __forceinline__ uint64_t desc_mn_sw128(uint32_t saddr) {
   return d;
 }
 
+// The same with MN chunks `lbo` bytes apart (chunks of 64 x BKP for a K depth
+// BKP per stage).
+__device__ __forceinline__ uint64_t desc_mn_sw128_lbo(uint32_t saddr, uint32_t lbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFF) >> 4);
+  d |= (uint64_t)(lbo >> 4) << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
 // kind::f16 instruction descriptor: bf16 x bf16 (or f16 x f16) -> f32, both
 // MN-major, M=128, N=n.
 __host__ __device__ constexpr uint32_t idesc_bf16_mn(int n) {
@@ -636,9 +648,11 @@ __global__ void __launch_bounds__((Cfg<NA, NB, SMALL, WIDE>::THREADS),
 // buffer.
 // ---------------------------------------------------------------------------
 
-template <int NA>
+template <int NA, int BKP = BK>
 struct PairCfg {
-  static constexpr int STAGE_BYTES = (NA + 1) * TILE_BYTES;  // per CTA
+  static constexpr int CHUNK = 64 * BKP * 2;                 // one 64 (MN) x BKP (K) box
+  static constexpr int TILE = 2 * CHUNK;                     // one 128 x BKP operand tile
+  static constexpr int STAGE_BYTES = (NA + 1) * TILE;        // per CTA
   static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
   static constexpr int EPI_WARPS = 8;
@@ -646,7 +660,7 @@ struct PairCfg {
   static constexpr int ACC_COLS = 512;  // two 256-column buffers
   // 32 MMAs per accumulator buffer (measured: 16 MMAs per buffer cost 3-5 %
   // of the fold in drains; the accumulation bias stays near 2e-6 relative)
-  static constexpr int PROMOTE_KB = NA == 1 ? 8 : 4;
+  static constexpr int PROMOTE_KB = (NA == 1 ? 8 : 4) * BK / BKP;
 };
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
@@ -716,11 +730,11 @@ __host__ __device__ constexpr uint32_t idesc_bf16_mn_m256(int n) {
   return (idesc_bf16_mn(n) & ~(31u << 24)) | ((uint32_t)(256 >> 4) << 24);
 }
 
-template <int NA>
-__global__ void __launch_bounds__(PairCfg<NA>::THREADS, 1)
+template <int NA, int BKP>
+__global__ void __launch_bounds__(PairCfg<NA, BKP>::THREADS, 1)
     tc_pair_kernel(const __grid_constant__ CUtensorMap ma0, const __grid_constant__ CUtensorMap ma1,
                    const __grid_constant__ CUtensorMap mb0, Params p) {
-  using K = PairCfg<NA>;
+  using K = PairCfg<NA, BKP>;
   constexpr int PT = 256;  // pair tile edge
   const uint32_t rank = cluster_ctarank();
   int mt, nt;
@@ -782,25 +796,25 @@ __global__ void __launch_bounds__(PairCfg<NA>::THREADS, 1)
         if (rank == 0) mbar_expect_tx(full0 + 8 * s, 2 * K::STAGE_BYTES);
         const uint32_t fb = full_lead + 8 * s;
         const uint32_t st = smem_u32(smem + s * K::STAGE_BYTES);
-        const int ya = (int)(p.ka_batch * bz + p.ka0 + (long long)kb * BK);
-        const int yb = (int)(p.kb_batch * bz + p.kb0 + (long long)kb * BK);
+        const int ya = (int)(p.ka_batch * bz + p.ka0 + (long long)kb * BKP);
+        const int yb = (int)(p.kb_batch * bz + p.kb0 + (long long)kb * BKP);
         const int xa = m0 + 128 * (int)rank;
         const int xb = (int)(p.nb0 + n0) + 128 * (int)rank;
 #pragma unroll
         for (int i = 0; i < NA; ++i) {
           const CUtensorMap* m = i == 0 ? &ma0 : &ma1;
-          tma_load_2d_pair(st + i * TILE_BYTES, m, xa, ya, fb);
-          tma_load_2d_pair(st + i * TILE_BYTES + CHUNK_BYTES, m, xa + 64, ya, fb);
+          tma_load_2d_pair(st + i * K::TILE, m, xa, ya, fb);
+          tma_load_2d_pair(st + i * K::TILE + K::CHUNK, m, xa + 64, ya, fb);
         }
-        const uint32_t sb = st + NA * TILE_BYTES;
+        const uint32_t sb = st + NA * K::TILE;
         tma_load_2d_pair(sb, &mb0, xb, yb, fb);
-        tma_load_2d_pair(sb + CHUNK_BYTES, &mb0, xb + 64, yb, fb);
+        tma_load_2d_pair(sb + K::CHUNK, &mb0, xb + 64, yb, fb);
         // warm L2 one ring ahead: the first CTA to reach a token slice otherwise
         // waits for DRAM inside the pipeline
         const int kp = kb + p.prefetch_kb;
         if (p.prefetch_kb > 0 && kp < p.num_kb) {
-          const int yap = (int)(p.ka_batch * bz + p.ka0 + (long long)kp * BK);
-          const int ybp = (int)(p.kb_batch * bz + p.kb0 + (long long)kp * BK);
+          const int yap = (int)(p.ka_batch * bz + p.ka0 + (long long)kp * BKP);
+          const int ybp = (int)(p.kb_batch * bz + p.kb0 + (long long)kp * BKP);
 #pragma unroll
           for (int i = 0; i < NA; ++i) {
             const CUtensorMap* m = i == 0 ? &ma0 : &ma1;
@@ -834,15 +848,15 @@ __global__ void __launch_bounds__(PairCfg<NA>::THREADS, 1)
           }
           fence_after();
           const uint32_t sa = smem_u32(smem + s * K::STAGE_BYTES);
-          const uint32_t sb = sa + NA * TILE_BYTES;
+          const uint32_t sb = sa + NA * K::TILE;
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk) {
+          for (int kk = 0; kk < BKP / 16; ++kk) {
             const uint32_t off = kk * 2048;  // 16 K rows = two 8-row swizzle groups
             const uint32_t acc0 = (kb > kstart || kk > 0) ? 1u : 0u;
 #pragma unroll
             for (int i = 0; i < NA; ++i)
-              umma_bf16_pair(acc_t, desc_mn_sw128(sa + i * TILE_BYTES + off),
-                             desc_mn_sw128(sb + off), idesc, i == 0 ? acc0 : 1u);
+              umma_bf16_pair(acc_t, desc_mn_sw128_lbo(sa + i * K::TILE + off, K::CHUNK),
+                             desc_mn_sw128_lbo(sb + off, K::CHUNK), idesc, i == 0 ? acc0 : 1u);
           }
           umma_commit_pair(empty0 + 8 * s);
         }
@@ -923,14 +937,14 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 // 2-D bf16 tensor [outer, inner] with row stride ld (elements), 64 x 64 boxes.
 static bool make_map(CUtensorMap* m, const void* base, long long inner, long long outer,
-                     long long ld, bool f16 = false) {
+                     long long ld, bool f16 = false, int box_k = BK) {
   auto enc = encode_fn();
   if (!enc) return false;
   if ((reinterpret_cast<uintptr_t>(base) & 15) || ((ld * 2) & 15) || inner <= 0 || outer <= 0)
     return false;
   cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
   cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
-  cuuint32_t box[2] = {64, (cuuint32_t)BK};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_k};
   cuuint32_t estr[2] = {1, 1};
   return enc(m, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
              const_cast<void*>(base), dims, strides, box,
@@ -1014,14 +1028,14 @@ static bool pair_prefetch_enabled() {
   return v == 1;
 }
 
-template <int NA>
+template <int NA, int BKP = BK>
 static int launch_pair(const Maps& m, const Params& p, long long batch, cudaStream_t st) {
-  using K = PairCfg<NA>;
+  using K = PairCfg<NA, BKP>;
   static int attr_done[64] = {0};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return G2Q_ERR_CUDA;
   if (dev >= 64 || !attr_done[dev]) {
-    if (cudaFuncSetAttribute(tc_pair_kernel<NA>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(tc_pair_kernel<NA, BKP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              K::SMEM) != cudaSuccess)
       return G2Q_ERR_CUDA;
     if (dev < 64) attr_done[dev] = 1;
@@ -1048,7 +1062,8 @@ static int launch_pair(const Maps& m, const Params& p, long long batch, cudaStre
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, tc_pair_kernel<NA>, m.a[0], m.a[1], m.b[0], q);
+  const cudaError_t e =
+      cudaLaunchKernelEx(&cfg, tc_pair_kernel<NA, BKP>, m.a[0], m.a[1], m.b[0], q);
   g2q::note_launch();
   if (e != cudaSuccess) {
     (void)cudaGetLastError();
@@ -1066,6 +1081,20 @@ static bool pair_tiles_enabled() {
     v = (e && e[0] == '0') ? 0 : 1;
   }
   return v == 1;
+}
+
+// K depth per pipeline stage of the CTA-pair Gram: 128 tokens (three 64 KB
+// stages per CTA), unless G2PTQ_B200_PAIR_BK=64 asks for 64 (six 32 KB stages).
+// Measured at 16384 tokens: 250 vs 302 us at C=4096, 2.81 vs 3.22 ms at 14336;
+// each k-block then carries 1024 tensor cycles per SM, twice the fixed cost of
+// its full / empty barrier round trip and MMA issue.
+static int pair_bk() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("G2PTQ_B200_PAIR_BK");
+    v = (e && atoi(e) == 64) ? 64 : 128;
+  }
+  return v;
 }
 
 static int dispatch(int na, int nb, Maps& m, const Params& p, long long batch,
@@ -1217,6 +1246,24 @@ int tc_gram(float* D, long long ldd, long long M, long long N, const void* A, in
     b_terms[1] = lo;
     ldb_t = w;
     nb = 2;
+  }
+  if (na == 1 && nb == 1 && M >= 512 && N >= 512 && T > 4 * 128 && tc::pair_tiles_enabled() &&
+      tc::pair_bk() == 128) {
+    // CTA pairs with 128 tokens per pipeline stage (half the barrier round
+    // trips per MMA of the 64-token stages)
+    tc::Maps mp{};
+    if (tc::make_map(&mp.a[0], a_terms[0], M, T, lda_t, false, 128) &&
+        tc::make_map(&mp.b[0], b_terms[0], N, T, ldb_t, false, 128)) {
+      mp.a[1] = mp.a[0];
+      tc::Params p{};
+      p.D = D; p.ldd = ldd; p.d_bs = 0;
+      p.M = M; p.N = N;
+      p.num_kb = (int)((T + 127) / 128);
+      p.alpha = alpha; p.beta = beta;
+      p.symmetric = symmetric ? 1 : 0;
+      p.raster = 1;
+      return tc::launch_pair<1, 128>(mp, p, 1, st);
+    }
   }
   tc::Maps mp{};
   bool ok = tc::make_map(&mp.a[0], a_terms[0], M, T, lda_t) &&

@@ -75,6 +75,37 @@ class TokenStage:
         self.rows = 0
 
 
+def lazy_counter(name):
+    """Class attribute for a per-layer int64 device counter (``nsamples``,
+    ``index``, ``total_tokens``) whose ``add_batch`` increments stay on the
+    host until the attribute is read: one add kernel per layer at a read
+    instead of one per hook call.  Reads see every increment so far, and edits
+    made in place through a read are kept (increments are added, never
+    overwritten)."""
+    store, pend = "_" + name + "_dev", "_" + name + "_pending"
+
+    def get(self):
+        t = self.__dict__.get(store)
+        p = self.__dict__.get(pend)
+        if t is not None and p:
+            for i, d in p.items():
+                t[i] += d
+            p.clear()
+        return t
+
+    def set(self, value):
+        self.__dict__[store] = value
+        self.__dict__[pend] = {}
+
+    return property(get, set)
+
+
+def bump(obj, name, idx, delta):
+    """Record ``obj.<name>[idx] += delta`` for the next read of the counter."""
+    p = obj.__dict__["_" + name + "_pending"]
+    p[idx] = p.get(idx, 0) + delta
+
+
 def stage_dtype(x):
     return torch.bfloat16 if x.dtype == torch.bfloat16 else torch.float32
 

@@ -47,6 +47,9 @@ def run_eager(weight, hinv, scale, zero, z, ghinv, maxq, backend="torch", int_we
 
 
 class G2PTQ(_engine.StagingMixin):
+    index = _engine.lazy_counter("index")
+    total_tokens = _engine.lazy_counter("total_tokens")
+
     def __init__(self, layers, saliencies, gradients, num_groups: int,
                  offload_hessians: bool = False, approx_grad_beta: float = 0.0):
         self.layers = layers
@@ -111,10 +114,10 @@ class G2PTQ(_engine.StagingMixin):
         sal = self.saliencies[idx][0].to(self.dev).float()
         del self.saliencies[idx][0]
         self._k[idx] += 1
-        self.index[idx] += 1
+        _engine.bump(self, "index", idx, 1)
         t_old = self._tok[idx]
         self._tok[idx] += n_tokens
-        self.total_tokens[idx] += n_tokens
+        _engine.bump(self, "total_tokens", idx, n_tokens)
         ops.sq_colsum(self.act_square[idx], x, keep=t_old / self._tok[idx],
                       scale=1.0 / self._tok[idx])
         w = (sal.reshape(n_tokens, self.num_groups) * (1.0 / n_tokens)).contiguous()

@@ -40,6 +40,8 @@ def run_eager(weight, hinv, p, scale, zero, maxq, backend="torch", column_weight
 
 
 class GPTAQ(_engine.StagingMixin):
+    nsamples = _engine.lazy_counter("nsamples")
+
     def __init__(self, layers, offload_hessians: bool = False):
         self.layers = layers
         self.num_layers = len(layers)
@@ -92,7 +94,7 @@ class GPTAQ(_engine.StagingMixin):
         x = _engine.as_rows(inp, self.columns)
         fp = _engine.as_rows(fp, self.columns)
         self._n[idx] += tmp
-        self.nsamples[idx] += tmp
+        _engine.bump(self, "nsamples", idx, tmp)
         self._append(idx, x, sub=fp)
         del self.fp_inp[idx][0]
 

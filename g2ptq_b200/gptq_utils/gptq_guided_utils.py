@@ -16,6 +16,8 @@ from .gptq_utils import GPTQ, _onload
 
 
 class GPTQGuided(GPTQ):
+    index = _engine.lazy_counter("index")
+
     def __init__(self, layers, saliencies, num_groups: int, offload_hessians: bool = False):
         self.layers = layers
         self.num_layers = len(layers)
@@ -53,7 +55,7 @@ class GPTQGuided(GPTQ):
         i0 = self._idx[idx]
         sal = self.saliencies[idx][i0:i0 + bsz].to(self.dev)
         self._idx[idx] += bsz
-        self.index[idx] += bsz
+        _engine.bump(self, "index", idx, bsz)
         x = _engine.as_rows(inp, self.columns)
         sal = sal.reshape(-1, sal.shape[-1]).float().contiguous()
         n_tokens = x.shape[0]

@@ -40,6 +40,8 @@ def run_eager(weight, hinv, scale, zero, maxq, backend="torch", int_weight=None,
 
 
 class GPTQ(_engine.StagingMixin):
+    nsamples = _engine.lazy_counter("nsamples")
+
     def __init__(self, layers, offload_hessians: bool = False):
         self.layers = layers
         self.num_layers = len(layers)
@@ -79,7 +81,7 @@ class GPTQ(_engine.StagingMixin):
             inp = inp.unsqueeze(0)
         tmp = inp.shape[0]
         self._n[idx] += tmp
-        self.nsamples[idx] += tmp
+        _engine.bump(self, "nsamples", idx, tmp)
         self._append(idx, _engine.as_rows(inp, self.columns))
 
     def _fold(self, idx, X, sub, scales):

@@ -469,3 +469,42 @@ def test_gptq_pipeline_vs_oracle(rows, cols, bits, sym, gs, act):
     assert float(np.mean(np.isclose(Q, Qo, rtol=2e-5, atol=2e-5))) >= 0.999
     l_gpu, l_or = proxy_loss(W, Q, Hd.cpu().numpy()), proxy_loss(W, Qo, Hd.cpu().numpy())
     np.testing.assert_allclose(l_gpu, l_or, rtol=1e-3)
+
+
+def test_moe_experts_layer_batched_vs_oracle():
+    """Layer-batched expert quantization (BASELINE configs[3] in miniature):
+    eight same-shape experts in one GPTQ object, each with its own Hessian
+    from a ragged number of routed tokens (add_batch per expert index, 2-D
+    routed-token inputs), W4 group 128, act-order with static groups; every
+    expert against the oracle on its own Hessian."""
+    rng = np.random.default_rng(30)
+    E, R, C, gs = 8, 192, 384, 128
+    W = (rng.standard_normal((E, R, C)) * 0.02).astype(np.float32)
+    layers = [linear(W[e]) for e in range(E)]
+    obj = gptq_utils.GPTQ(layers)
+    obj.quantizer = quantizers(4, True, C, gs)
+    Hs = []
+    for e in range(E):
+        H, n = np.zeros((C, C), np.float32), 0
+        for call in range(3):  # three forward batches, routed-token counts differ
+            T = int(rng.integers(40, 700))
+            x = rng.standard_normal((T, C)).astype(np.float32)
+            x[:, e] *= 15.0
+            obj.add_batch(e, t(x), None)
+            H, n = ohess.gptq_add_batch(H, n, x)
+        Hs.append(H)
+    Hd = obj.H.clone()
+    for e in range(E):
+        assert rel_fro(Hd[e], Hs[e]) < 1e-5
+    obj.fasterquant(blocksize=128, percdamp=0.01, groupsize=gs, actorder=True, static_groups=True,
+                    export_compressed_tensors=True)
+    Q = torch.stack([l.weight.data for l in layers]).cpu().numpy()
+    oq = ocomp.make_group_quantizers(ocomp.Quantizer(4, True), C, gs)
+    Qo, _, _, _ = ofq.gptq_fasterquant(W, Hd.cpu().numpy(), oq, 128, 0.01, gs, True, True,
+                                       route="ul")
+    for e in range(E):
+        assert float(np.mean(np.isclose(Q[e], Qo[e], rtol=2e-5, atol=2e-5))) >= 0.999, e
+        np.testing.assert_allclose(proxy_loss(W[e:e + 1], Q[e:e + 1], Hd[e:e + 1].cpu().numpy()),
+                                   proxy_loss(W[e:e + 1], Qo[e:e + 1], Hd[e:e + 1].cpu().numpy()),
+                                   rtol=1e-3)
+        assert layers[e]._export_qparams["weight_packed"].shape[0] == R

@@ -169,9 +169,10 @@ def test_tc_trailing_update_direct():
     torch.testing.assert_close(outs[1][0], outs[0][0], rtol=0, atol=float(scale.max()) * 1.01)
 
 
-@pytest.mark.parametrize("C", [1152, 4096])
+@pytest.mark.parametrize("C", [600, 1152, 1376, 4096])
 def test_tc_cholesky_matches_fp32(C):
-    """Cholesky trailing updates on tensor cores (three-term split) vs fp32."""
+    """Cholesky trailing updates on tensor cores (three-term split, 512-column
+    outer blocks: one, several, and a ragged last block and panel) vs fp32."""
     g = torch.Generator(device=DEV).manual_seed(C)
     X = torch.randn(2 * C, C, device=DEV, generator=g)
     X[:, :4] *= 20

@@ -147,3 +147,24 @@ def test_reduce_to_target_rank_two_ranks():
     torch.testing.assert_close(Hout1[0], expect)
     assert torch.count_nonzero(Hout1[1]) == 0       # no samples anywhere -> zeros
     assert nout1.tolist() == [total, 0]
+
+
+def test_lazy_counter_applies_increments_on_read():
+    """add_batch counters: increments recorded on the host appear at the next
+    read; edits made in place through a read survive later increments."""
+    from g2ptq_b200.gptq_utils import _engine
+
+    class Obj:
+        nsamples = _engine.lazy_counter("nsamples")
+
+    o = Obj()
+    o.nsamples = torch.zeros(2, dtype=torch.long)
+    for _ in range(5):
+        _engine.bump(o, "nsamples", 1, 3)
+    _engine.bump(o, "nsamples", 0, 1)
+    assert o.nsamples.tolist() == [1, 15]
+    o.nsamples[0] = 7
+    _engine.bump(o, "nsamples", 0, 2)
+    assert o.nsamples.tolist() == [9, 15]
+    o.nsamples = None
+    assert o.nsamples is None
