@@ -330,23 +330,47 @@ __global__ void __launch_bounds__(256) linv_apply_kernel(float* S, long long lds
   float* Os = Bt;                  // [LA_ROWS][LA_LDO], reuses Bt after the products
   const int t = threadIdx.x;
   const long long i0 = (long long)blockIdx.x * LA_ROWS;
-  for (int idx = t; idx < NB * NB; idx += 256) {
-    const int c = idx / NB, k = idx % NB;
-    Lt[k * LA_LDT + c] = Linv[idx];
-  }
-  if (!LEFT) {
-    // rows i0 .. i0+63, columns 0 .. nb-1 (consecutive threads: consecutive columns)
-    for (int idx = t; idx < LA_ROWS * NB; idx += 256) {
-      const int i = idx / NB, k = idx % NB;
-      const long long r = i0 + i;
-      Bt[k * LA_LDB + i] = (r < n && k < nb) ? S[r * lds + k] : 0.f;
+  // all loads of a thread in flight before its shared-memory stores: a loop
+  // that stores each value before the next load waits for L2 sixty-four times
+#pragma unroll 1
+  for (int i0l = 0; i0l < NB * NB; i0l += 16 * 256) {
+    float v[16];
+#pragma unroll
+    for (int u = 0; u < 16; ++u) v[u] = Linv[i0l + u * 256 + t];
+#pragma unroll
+    for (int u = 0; u < 16; ++u) {
+      const int idx = i0l + u * 256 + t, c = idx / NB, k = idx % NB;
+      Lt[k * LA_LDT + c] = v[u];
     }
-  } else {
-    // rows 0 .. nb-1, columns i0 .. i0+63 (consecutive threads: consecutive columns)
-    for (int idx = t; idx < LA_ROWS * NB; idx += 256) {
-      const int k = idx / LA_ROWS, i = idx % LA_ROWS;
-      const long long c = i0 + i;
-      Bt[k * LA_LDB + i] = (c < n && k < nb) ? S[k * lds + c] : 0.f;
+  }
+  {
+    float v[LA_ROWS * NB / 256];
+    if (!LEFT) {
+      // rows i0 .. i0+63, columns 0 .. nb-1 (consecutive threads: consecutive columns)
+#pragma unroll
+      for (int u = 0; u < LA_ROWS * NB / 256; ++u) {
+        const int idx = u * 256 + t, i = idx / NB, k = idx % NB;
+        const long long r = i0 + i;
+        v[u] = (r < n && k < nb) ? S[r * lds + k] : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < LA_ROWS * NB / 256; ++u) {
+        const int idx = u * 256 + t, i = idx / NB, k = idx % NB;
+        Bt[k * LA_LDB + i] = v[u];
+      }
+    } else {
+      // rows 0 .. nb-1, columns i0 .. i0+63 (consecutive threads: consecutive columns)
+#pragma unroll
+      for (int u = 0; u < LA_ROWS * NB / 256; ++u) {
+        const int idx = u * 256 + t, k = idx / LA_ROWS, i = idx % LA_ROWS;
+        const long long c = i0 + i;
+        v[u] = (c < n && k < nb) ? S[k * lds + c] : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < LA_ROWS * NB / 256; ++u) {
+        const int idx = u * 256 + t, k = idx / LA_ROWS, i = idx % LA_ROWS;
+        Bt[k * LA_LDB + i] = v[u];
+      }
     }
   }
   __syncthreads();

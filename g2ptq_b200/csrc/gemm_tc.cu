@@ -1559,15 +1559,44 @@ __global__ void __launch_bounds__(256) split2h_kernel(const float* __restrict__ 
   const int x = threadIdx.x, y = threadIdx.y;
   const long long n0 = (long long)blockIdx.x * 32;
   const long long ni = n0 + x;
+  // sixteen loads of a thread in flight before their shared-memory stores
   if (transpose) {
     // source rows n0..n0+31, K long each: lanes walk k (coalesced), warp y takes
     // rows y, y+8, ...
-    for (int rr = y; rr < 32; rr += 8) {
-      const long long r = n0 + rr;
-      for (int k = x; k < K; k += 32) tile[k][rr] = (r < n) ? src[r * lds + k] : 0.f;
+#pragma unroll 1
+    for (int k0 = 0; k0 < K; k0 += 128) {
+      float v[4][4];
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+          const long long r = n0 + y + 8 * a;
+          const int k = k0 + x + 32 * b;
+          v[a][b] = (r < n && k < K) ? src[r * lds + k] : 0.f;
+        }
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+          const int k = k0 + x + 32 * b;
+          if (k < K) tile[k][y + 8 * a] = v[a][b];
+        }
     }
   } else {
-    for (int k = y; k < K; k += 8) tile[k][x] = (ni < n) ? src[(long long)k * lds + ni] : 0.f;
+#pragma unroll 1
+    for (int k0 = 0; k0 < K; k0 += 128) {
+      float v[16];
+#pragma unroll
+      for (int a = 0; a < 16; ++a) {
+        const int k = k0 + y + 8 * a;
+        v[a] = (ni < n && k < K) ? src[(long long)k * lds + ni] : 0.f;
+      }
+#pragma unroll
+      for (int a = 0; a < 16; ++a) {
+        const int k = k0 + y + 8 * a;
+        if (k < K) tile[k][x] = v[a];
+      }
+    }
   }
   __syncthreads();
   float m = 0.f;

@@ -69,23 +69,28 @@ class WeightQuantizer(torch.nn.Module):
         ``nn.Module`` traversal: ``make_group_quantizers`` copies one quantizer
         per weight group (hundreds per decoder layer), and the generic path
         costs about a tenth of a millisecond each.  Tensors are cloned, the
-        module's bookkeeping dicts copied; the device status word is left for
-        the copy to allocate."""
-        cls = self.__class__
-        new = cls.__new__(cls)
+        module's bookkeeping containers copied (empty ones shallowly), other
+        values deep-copied; the device status word is left for the copy to
+        allocate."""
+        new = object.__new__(self.__class__)
         memo[id(self)] = new
-        d = new.__dict__
+        d = {}
         for k, v in self.__dict__.items():
             if k == "_status":
                 v = None
             elif isinstance(v, torch.Tensor):
                 v = v.clone()
-            elif isinstance(v, dict):
-                v = type(v)((kk, vv.clone() if isinstance(vv, torch.Tensor)
-                             else copy.deepcopy(vv, memo)) for kk, vv in v.items())
+            elif isinstance(v, (dict, set)):
+                if v:
+                    v = (type(v)((kk, vv.clone() if isinstance(vv, torch.Tensor)
+                                  else copy.deepcopy(vv, memo)) for kk, vv in v.items())
+                         if isinstance(v, dict) else copy.deepcopy(v, memo))
+                else:
+                    v = type(v)()
             elif not isinstance(v, (bool, int, float, str, type(None))):
                 v = copy.deepcopy(v, memo)
             d[k] = v
+        new.__dict__.update(d)
         return new
 
     def status_tensor(self, device):

@@ -168,3 +168,26 @@ def test_lazy_counter_applies_increments_on_read():
     assert o.nsamples.tolist() == [9, 15]
     o.nsamples = None
     assert o.nsamples is None
+
+
+def test_weight_quantizer_deepcopy_is_independent():
+    """make_group_quantizers' copies: configuration carried over, buffers and
+    module containers distinct, the status word not shared."""
+    import copy
+    from g2ptq_b200.utils.quant_utils import WeightQuantizer
+    from g2ptq_b200.gptq_utils.common_utils import make_group_quantizers
+
+    q = WeightQuantizer()
+    q.configure(3, perchannel=True, sym=False, mse=True, grid=20, weight_groupsize=-1)
+    q._status = torch.zeros(1, dtype=torch.int32)
+    qs = make_group_quantizers(q, 300, 128)
+    assert len(qs) == 3
+    for c in qs:
+        assert (c.bits, c.sym, c.mse, c.grid, c.maxq, c.minq) == (3, False, True, 20, 3, -4)
+        assert c._status is None and not c.ready()
+        assert c._buffers is not q._buffers and c._modules is not q._modules
+        assert set(c.state_dict()) == {"scale", "zero"}
+    qs[0].scale.fill_(5.0)
+    assert float(q.scale) == 0.0 and float(qs[1].scale) == 0.0
+    c = copy.deepcopy(qs[0])
+    assert float(c.scale) == 5.0 and c.scale is not qs[0].scale
