@@ -248,7 +248,18 @@ class GramTimer:
     def install(self):
         from g2ptq_b200 import ops
         orig = ops.gram_update
+        orig_grouped = ops.gram_update_grouped
         timer = self
+
+        def timed_grouped(D, X, scales, alpha=1.0, beta=1.0, precision=0):
+            s = timer.torch.cuda.Event(enable_timing=True)
+            e = timer.torch.cuda.Event(enable_timing=True)
+            s.record()
+            orig_grouped(D, X, scales, alpha, beta, precision)
+            e.record()
+            G, C, _ = D.shape
+            timer.flops += G * X.shape[0] * C * (C + 1)
+            timer.events.append((s, e))
 
         def timed(D, A, B=None, row_scale=None, alpha=1.0, beta=1.0, symmetric=None,
                   precision=0):
@@ -265,11 +276,14 @@ class GramTimer:
             timer.events.append((s, e))
 
         ops.gram_update = timed
+        ops.gram_update_grouped = timed_grouped
         self._orig = orig
+        self._orig_grouped = orig_grouped
 
     def uninstall(self):
         from g2ptq_b200 import ops
         ops.gram_update = self._orig
+        ops.gram_update_grouped = self._orig_grouped
 
     def total_ms(self):
         return sum(s.elapsed_time(e) for s, e in self.events)

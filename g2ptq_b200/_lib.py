@@ -11,7 +11,7 @@ import os
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.environ.get("G2PTQ_B200_LIB", os.path.join(_HERE, "_lib", "libg2ptq_b200.so"))
 
-ABI_VERSION = 4
+ABI_VERSION = 5
 
 G2Q_OK = 0
 G2Q_ERR_INVALID_ARG = -1
@@ -49,6 +49,9 @@ SIGNATURES = {
     "g2q_gram_update": [P, I64, I64, I64, P, I32, I64, P, I32, I64, P, I64, I64, I32, F32, F32,
                         I32, P, SZ, P],
     "g2q_gram_workspace_bytes": [I64, I64, I64, I32],
+    "g2q_gram_update_grouped": [P, I64, I64, I64, P, I32, I64, P, I64, I32, I64, F32, F32, I32, P,
+                                SZ, P],
+    "g2q_gram_grouped_workspace_bytes": [I64, I64, I32, I32],
     "g2q_sq_colsum": [P, F32, F32, P, I32, I64, I64, I64, P],
     "g2q_gemm": [P, I64, I64, P, I64, I64, I32, P, I64, I64, I32, I64, I64, I64, I64, F32, F32,
                  I32, P],
@@ -84,6 +87,7 @@ _RESTYPES = {
     "g2q_launch_count": ctypes.c_int64,
     "g2q_status_string": ctypes.c_char_p,
     "g2q_gram_workspace_bytes": SZ,
+    "g2q_gram_grouped_workspace_bytes": SZ,
     "g2q_chol_workspace_bytes": SZ,
     "g2q_compensate_workspace_bytes": SZ,
     "g2q_gemm_tc_workspace_bytes": SZ,

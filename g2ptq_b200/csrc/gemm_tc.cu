@@ -1158,6 +1158,37 @@ static int split_rows(const void* X, int dtype, long long ldx, long long T, long
 
 static long long round8(long long v) { return (v + 7) / 8 * 8; }
 
+// hi[g] / lo[g] ([T][ldo] each, group g at offset g * gstride) = bf16 pair of
+// X[t][c] * s[t * sstride + g] for all G row groups in one pass over X, eight
+// columns (16 bytes of bf16 in, 16 bytes per term out) per thread.
+__global__ void __launch_bounds__(256) split_rows_groups_kernel(
+    const __nv_bfloat16* __restrict__ X, long long ldx, long long T, long long C,
+    const float* __restrict__ s, long long sstride, int G, __nv_bfloat16* hi, __nv_bfloat16* lo,
+    long long ldo, long long gstride) {
+  const long long nv = C / 8;
+  for (long long t = blockIdx.y; t < T; t += gridDim.y) {
+    for (long long v = (long long)blockIdx.x * blockDim.x + threadIdx.x; v < nv;
+         v += (long long)gridDim.x * blockDim.x) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(X + t * ldx + v * 8);
+      const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(&raw);
+      float x[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) x[u] = __bfloat162float(xb[u]);
+      for (int g = 0; g < G; ++g) {
+        const float sg = s[t * sstride + g];
+        uint4 h4, l4;
+        __nv_bfloat16* hp = reinterpret_cast<__nv_bfloat16*>(&h4);
+        __nv_bfloat16* lp = reinterpret_cast<__nv_bfloat16*>(&l4);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) split_bf16(x[u] * sg, &hp[u], &lp[u]);
+        const long long o = g * gstride + t * ldo + v * 8;
+        *reinterpret_cast<uint4*>(hi + o) = h4;
+        *reinterpret_cast<uint4*>(lo + o) = l4;
+      }
+    }
+  }
+}
+
 }  // namespace tc
 
 size_t tc_gram_workspace_bytes(long long M, long long N, long long T) {
@@ -1280,6 +1311,63 @@ int tc_gram(float* D, long long ldd, long long M, long long N, const void* A, in
   p.status = nullptr;
   p.raster = 1;
   return tc::dispatch(na, nb, mp, p, 1, st);
+}
+
+size_t tc_gram_grouped_workspace_bytes(long long C, long long T, int G) {
+  const size_t grouped = (size_t)2 * G * T * tc::round8(C) * 2 + 4 * 256;
+  const size_t single = tc_gram_workspace_bytes(C, C, T);
+  return grouped > single ? grouped : single;
+}
+
+// Row-scaled symmetric Gram updates of G row groups (see g2q_gram_update_grouped):
+// BF16 tokens are split for all groups in one pass and the G products run as
+// one batched CTA-pair launch (blockIdx.z = group); other inputs take the
+// per-group path.
+int tc_gram_grouped(float* D, long long ldd, long long d_gstride, long long C, const void* X,
+                    int x_dtype, long long ldx, const float* s, long long sstride, int G,
+                    long long T, float alpha, float beta, void* workspace,
+                    size_t workspace_bytes, cudaStream_t st) {
+  const bool fast = x_dtype == G2Q_DTYPE_BF16 && T > 0 && C >= 512 && (C % 8) == 0 &&
+                    (ldx % 8) == 0 && ((reinterpret_cast<uintptr_t>(X) & 15) == 0) && G <= 65535 &&
+                    tc::encode_fn() && tc::pair_tiles_enabled() &&
+                    workspace_bytes >= tc_gram_grouped_workspace_bytes(C, T, G);
+  if (fast) {
+    const long long w = tc::round8(C);
+    char* ws = (char*)workspace;
+    auto take = [&](long long elems) -> __nv_bfloat16* {
+      uintptr_t q = ((uintptr_t)ws + 255) & ~(uintptr_t)255;
+      ws = (char*)q + elems * 2;
+      return (__nv_bfloat16*)q;
+    };
+    __nv_bfloat16* hi = take((long long)G * T * w);
+    __nv_bfloat16* lo = take((long long)G * T * w);
+    const long long nv = C / 8;
+    dim3 grid((unsigned)cdiv(nv, 256), (unsigned)(T < 65535 ? T : 65535));
+    tc::split_rows_groups_kernel<<<grid, 256, 0, st>>>((const __nv_bfloat16*)X, ldx, T, C, s,
+                                                       sstride, G, hi, lo, w, T * w);
+    G2Q_CHECK_LAUNCH();
+    tc::Maps mp{};
+    // the groups' scaled tokens stacked along K: group g's k-block y sits at
+    // row g * T + y; a last partial k-block reads the next group's first rows,
+    // which meet X's zero-filled rows past T and add nothing
+    if (tc::make_map(&mp.a[0], hi, C, (long long)G * T, w) &&
+        tc::make_map(&mp.a[1], lo, C, (long long)G * T, w) &&
+        tc::make_map(&mp.b[0], X, C, T, ldx)) {
+      tc::Params p{};
+      p.D = D; p.ldd = ldd; p.d_bs = d_gstride;
+      p.M = C; p.N = C;
+      p.num_kb = (int)((T + tc::BK - 1) / tc::BK);
+      p.ka_batch = T; p.kb_batch = 0;
+      p.alpha = alpha; p.beta = beta;
+      p.symmetric = 1;
+      p.raster = 1;
+      return tc::launch_pair<2>(mp, p, G, st);
+    }
+  }
+  for (int g = 0; g < G; ++g)
+    G2Q_TRY(tc_gram(D + g * d_gstride, ldd, C, C, X, x_dtype, ldx, X, x_dtype, ldx, s + g, sstride,
+                    T, 1, alpha, beta, workspace, workspace_bytes, st));
+  return G2Q_OK;
 }
 
 // W[b][:, i2 + n] += beta * sum_k Err[b][k][m] * U[b][i1 + k][i2 + n] on tensor

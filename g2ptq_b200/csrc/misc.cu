@@ -8,6 +8,11 @@
 
 namespace g2q {
 
+int tc_gram_grouped(float* D, long long ldd, long long d_gstride, long long C, const void* X,
+                    int x_dtype, long long ldx, const float* s, long long sstride, int G,
+                    long long T, float alpha, float beta, void* workspace,
+                    size_t workspace_bytes, cudaStream_t st);
+size_t tc_gram_grouped_workspace_bytes(long long C, long long T, int G);
 int tc_gram(float* D, long long ldd, long long M, long long N, const void* A, int a_dtype,
             long long lda, const void* B, int b_dtype, long long ldb, const float* row_scale,
             long long scale_stride, long long T, int symmetric, float alpha, float beta,
@@ -281,7 +286,7 @@ void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 using namespace g2q;
 
-extern "C" int g2q_abi_version(void) { return 4; }
+extern "C" int g2q_abi_version(void) { return 5; }
 
 extern "C" int64_t g2q_launch_count(void) { return g2q::g_launches.load(); }
 
@@ -353,6 +358,31 @@ extern "C" int g2q_stage_tokens(void* dst, int dst_dtype, int64_t dst_ld, int64_
     return G2Q_ERR_INVALID_ARG;
   }
   G2Q_CHECK_LAUNCH();
+  return G2Q_OK;
+}
+
+extern "C" size_t g2q_gram_grouped_workspace_bytes(int64_t C, int64_t T, int G, int precision) {
+  if (precision == 1 && C > 0 && T >= 0 && G > 0) return tc_gram_grouped_workspace_bytes(C, T, G);
+  return 0;
+}
+
+extern "C" int g2q_gram_update_grouped(float* D, int64_t ldd, int64_t d_gstride, int64_t C,
+                                       const void* X, int x_dtype, int64_t ldx, const float* s,
+                                       int64_t sstride, int G, int64_t T, float alpha, float beta,
+                                       int precision, void* workspace, size_t workspace_bytes,
+                                       void* stream) {
+  if (!D || !X || !s || C <= 0 || T < 0 || G <= 0 || ldx < C || ldd < C || sstride < G ||
+      d_gstride < C * ldd)
+    return G2Q_ERR_INVALID_ARG;
+  if (x_dtype != G2Q_DTYPE_BF16 && x_dtype != G2Q_DTYPE_F32) return G2Q_ERR_INVALID_ARG;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (precision == 1)
+    return tc_gram_grouped(D, ldd, d_gstride, C, X, x_dtype, ldx, s, sstride, G, T, alpha, beta,
+                           workspace, workspace_bytes, st);
+  if (precision != 0) return G2Q_ERR_INVALID_ARG;
+  for (int g = 0; g < G; ++g)
+    G2Q_TRY(g2q_gram_update(D + g * d_gstride, ldd, C, C, X, x_dtype, ldx, X, x_dtype, ldx, s + g,
+                            sstride, T, 1, alpha, beta, 0, nullptr, 0, stream));
   return G2Q_OK;
 }
 

@@ -126,10 +126,8 @@ class G2PTQ(_engine.StagingMixin):
     def _fold(self, idx, X, sub, scales):
         k_old, k_new = self._k_folded[idx], self._k[idx]
         self._require_device_stats(self._H)
-        for g in range(self.num_groups):
-            ops.gram_update(self._H[idx, g], X, X, row_scale=scales[:, g],
-                            alpha=k_old / k_new, beta=1.0 / k_new, symmetric=True,
-                            precision=_engine.PRECISION)
+        ops.gram_update_grouped(self._H[idx], X, scales, alpha=k_old / k_new, beta=1.0 / k_new,
+                                precision=_engine.PRECISION)
         self._k_folded[idx] = k_new
 
     def fasterquant(self, blocksize=128, percdamp=0.01, groupsize=-1, actorder=False,

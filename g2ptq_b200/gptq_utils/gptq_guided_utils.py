@@ -64,9 +64,8 @@ class GPTQGuided(GPTQ):
 
     def _fold(self, idx, X, sub, scales):
         self._require_device_stats(self._H)
-        for g in range(self.num_groups):
-            ops.gram_update(self._H[idx, g], X, X, row_scale=scales[:, g], alpha=1.0,
-                            beta=1.0, symmetric=True, precision=_engine.PRECISION)
+        ops.gram_update_grouped(self._H[idx], X, scales, alpha=1.0, beta=1.0,
+                                precision=_engine.PRECISION)
 
     def fasterquant(self, blocksize=128, percdamp=0.01, groupsize=-1, actorder=False,
                     static_groups=False, export_compressed_tensors=False, backend="torch",

@@ -90,6 +90,24 @@ def gram_update(D, A, B=None, row_scale=None, alpha=1.0, beta=1.0, symmetric=Non
          _stream(D))
 
 
+def gram_update_grouped(D, X, scales, alpha=1.0, beta=1.0, precision=0):
+    """``D[g] <- alpha D[g] + beta X^T diag(scales[:, g]) X`` for every row group g:
+    ``D [G, C, C]`` contiguous, ``X [T, C]`` token-major, ``scales [T, G]``."""
+    _cuda(D, X, scales)
+    _contig(D)
+    G, C, _ = D.shape
+    T = X.shape[0]
+    if X.shape[1] != C or X.stride(1) != 1 or scales.shape != (T, G) or scales.stride(1) != 1:
+        raise ValueError("gram_update_grouped: shapes or strides do not match")
+    if scales.dtype != torch.float32:
+        raise TypeError("gram_update_grouped expects fp32 scales")
+    ws_bytes = query("g2q_gram_grouped_workspace_bytes", C, T, G, precision)
+    ws = workspace(ws_bytes, D.device) if ws_bytes else None
+    call("g2q_gram_update_grouped", D.data_ptr(), D.stride(1), D.stride(0), C, X.data_ptr(),
+         dtype_code(X.dtype), X.stride(0), scales.data_ptr(), scales.stride(0), G, T,
+         float(alpha), float(beta), precision, _ptr(ws), ws_bytes, _stream(D))
+
+
 def sq_colsum(acc, X, keep, scale):
     """``acc <- acc * keep + scale * sum_t X[t]^2``."""
     _cuda(acc, X)

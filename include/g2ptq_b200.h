@@ -97,6 +97,24 @@ int g2q_gram_update(float* D, int64_t ldd, int64_t M, int64_t N,
                     void* workspace, size_t workspace_bytes, void* stream);
 size_t g2q_gram_workspace_bytes(int64_t M, int64_t N, int64_t T, int precision);
 
+/* Row-scaled Gram updates of G row groups in one call, for g < G:
+ *   D[g] <- alpha * D[g] + beta * X^T diag(s[:, g]) X
+ * D[g] at D + g * d_gstride (C x C, row stride ldd, left full symmetric),
+ * X [T, C] token-major (row stride ldx, G2Q_DTYPE_BF16 or G2Q_DTYPE_F32),
+ * s[t, g] = s[t * sstride + g].  Each group's result is that of
+ * g2q_gram_update(..., row_scale = s + g, symmetric = 1); at precision 1 BF16
+ * tokens are split for all groups in one pass and the G products run as one
+ * launch (workspace: g2q_gram_grouped_workspace_bytes).
+ * Replaces the per-group saliency-weighted products of G2PTQ.add_batch
+ * (gptq_utils/g2ptq_utils.py:193-200) and GPTQGuided.add_batch
+ * (gptq_utils/gptq_guided_utils.py:78-80). */
+int g2q_gram_update_grouped(float* D, int64_t ldd, int64_t d_gstride, int64_t C,
+                            const void* X, int x_dtype, int64_t ldx,
+                            const float* s, int64_t sstride, int G, int64_t T,
+                            float alpha, float beta, int precision,
+                            void* workspace, size_t workspace_bytes, void* stream);
+size_t g2q_gram_grouped_workspace_bytes(int64_t C, int64_t T, int G, int precision);
+
 /* g2q_gram_update at precision 1 (tensor cores) without caller-provided
  * scratch: the bf16 splits of FP32 or row-scaled operands go to a file-scope
  * device array of G2Q_GRAM_STATIC_SCRATCH_BYTES (40 MiB) owned by the library,

@@ -85,6 +85,33 @@ def test_tc_gram_bf16_weighted_matches_fp32_path():
     assert rel_fro(D1, D0) < 1e-5
 
 
+@pytest.mark.parametrize("dtype,T,C", [(torch.bfloat16, 3000, 1024), (torch.bfloat16, 777, 640),
+                                       (torch.bfloat16, 16384, 512), (torch.float32, 1000, 512),
+                                       (torch.bfloat16, 200, 256)])
+def test_gram_update_grouped_matches_per_group(dtype, T, C):
+    """The four saliency-weighted Grams of a G2PTQ / GuidedQuant fold in one call
+    (one split pass, one batched launch) against one call per group; token
+    counts that are not a multiple of the 64-token k-block make the stacked
+    groups' last k-blocks read across a group boundary."""
+    g = torch.Generator(device=DEV).manual_seed(T + C)
+    X = torch.randn(T, C, device=DEV, generator=g)
+    X[:, :3] *= 20
+    X = X.to(dtype)
+    S = torch.rand(T, 4, device=DEV, generator=g)
+    D0 = torch.randn(4, C, C, device=DEV, generator=g)
+    D0 = D0 + D0.transpose(1, 2)
+    D1, D2 = D0.clone(), D0.clone()
+    ops.gram_update_grouped(D1, X, S, alpha=0.5, beta=1.0 / T, precision=1)
+    for k in range(4):
+        ops.gram_update(D2[k], X, X, row_scale=S[:, k], alpha=0.5, beta=1.0 / T, symmetric=True,
+                        precision=1)
+    assert torch.equal(D1, D2)
+    Xd = X.double()
+    for k in range(4):
+        ref = 0.5 * D0[k].double() + (Xd.T * S[:, k].double()[None, :]) @ Xd / T
+        assert rel_fro(D1[k], ref) < 1e-5
+
+
 def _gptq_layer(W, X, bits, sym, gs, act, precision, monkeypatch, H=None):
     """Calibrate (unless ``H`` is given) and quantize one linear with the chosen path."""
     monkeypatch.setattr(_engine, "PRECISION", precision)
