@@ -422,6 +422,46 @@ extern "C" int g2q_gram_update(float* D, int64_t ldd, int64_t M, int64_t N, cons
   return simt_gemm(a, true, false, a_dtype, b_dtype, 1, st);
 }
 
+// acc[c] += scale * sum_t X[t][c]^2 for BF16 X with 16-byte rows: a CTA of
+// 32 x 8 threads covers 256 columns (eight per thread, one 16-byte load per
+// token) and 128 tokens (eight token lanes), reduces the lanes in shared
+// memory and adds one partial per column.
+constexpr int SQ_TCHUNK = 128;
+__global__ void __launch_bounds__(256) sq_colsum_bf16x8_kernel(float* acc, float scale,
+                                                               const __nv_bfloat16* X,
+                                                               long long ldx, long long T,
+                                                               long long C) {
+  __shared__ float part[8][257];
+  const int tx = threadIdx.x, ty = threadIdx.y;
+  const long long c0 = ((long long)blockIdx.x * 32 + tx) * 8;
+  const long long t0 = (long long)blockIdx.y * SQ_TCHUNK;
+  const long long t1 = (t0 + SQ_TCHUNK < T) ? t0 + SQ_TCHUNK : T;
+  float a[8];
+#pragma unroll
+  for (int u = 0; u < 8; ++u) a[u] = 0.f;
+  if (c0 < C) {
+#pragma unroll 4
+    for (long long t = t0 + ty; t < t1; t += 8) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(X + t * ldx + c0);
+      const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float v = __bfloat162float(xb[u]);
+        a[u] = fmaf(v, v, a[u]);
+      }
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < 8; ++u) part[ty][tx * 8 + u] = a[u];
+  __syncthreads();
+  const int c = ty * 32 + tx;  // 256 columns, one per thread
+  float sum = 0.f;
+#pragma unroll
+  for (int q = 0; q < 8; ++q) sum += part[q][c];
+  const long long gc = (long long)blockIdx.x * 256 + c;
+  if (gc < C) atomicAdd(acc + gc, sum * scale);
+}
+
 extern "C" int g2q_sq_colsum(float* acc, float keep, float scale, const void* X, int x_dtype,
                              int64_t ldx, int64_t T, int64_t C, void* stream) {
   if (!acc || !X || C <= 0 || T < 0 || ldx < C) return G2Q_ERR_INVALID_ARG;
@@ -429,6 +469,14 @@ extern "C" int g2q_sq_colsum(float* acc, float keep, float scale, const void* X,
   scale_vec_kernel<<<cdiv(C, 256), 256, 0, st>>>(acc, C, keep);
   G2Q_CHECK_LAUNCH();
   if (T == 0) return G2Q_OK;
+  if (x_dtype == G2Q_DTYPE_BF16 && (C % 8) == 0 && (ldx % 8) == 0 &&
+      (reinterpret_cast<uintptr_t>(X) & 15) == 0 && cdiv(T, SQ_TCHUNK) <= 65535) {
+    dim3 grid(cdiv(C, 256), cdiv(T, SQ_TCHUNK));
+    sq_colsum_bf16x8_kernel<<<grid, dim3(32, 8), 0, st>>>(acc, scale, (const __nv_bfloat16*)X,
+                                                         ldx, T, C);
+    G2Q_CHECK_LAUNCH();
+    return G2Q_OK;
+  }
   const long long tchunk = 256;
   dim3 grid(cdiv(C, 256), cdiv(T, tchunk));
   if (grid.y > 65535u) return G2Q_ERR_INVALID_ARG;

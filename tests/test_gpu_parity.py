@@ -177,6 +177,20 @@ def test_find_params_groups_matches_per_group(bits, sym):
     assert torch.equal(s1, s2) and torch.equal(z1, z2)
 
 
+@pytest.mark.parametrize("dtype,T,C", [(torch.bfloat16, 2048, 4096), (torch.bfloat16, 300, 1376),
+                                       (torch.bfloat16, 77, 200), (torch.float32, 513, 640)])
+def test_sq_colsum(dtype, T, C):
+    """acc <- acc * keep + scale * sum_t X[t]^2 (the act_square running mean of
+    G2PTQ / GuidedQuant add_batch), vectorized BF16 path and general path."""
+    g = torch.Generator(device=DEV).manual_seed(T)
+    X = (torch.randn(T, C, device=DEV, generator=g) * 3).to(dtype)
+    acc0 = torch.rand(C, device=DEV, generator=g)
+    acc = acc0.clone()
+    ops.sq_colsum(acc, X, keep=0.25, scale=1.0 / 4096)
+    ref = acc0.double() * 0.25 + (X.double() ** 2).sum(0) / 4096
+    torch.testing.assert_close(acc.double(), ref, rtol=2e-6, atol=1e-9)
+
+
 @pytest.mark.parametrize("bits", [2, 3, 4, 8])
 def test_pack_int32(golden, bits):
     m = golden("misc.npz")
