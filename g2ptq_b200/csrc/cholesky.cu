@@ -621,9 +621,58 @@ static int chol_one(float* U, const float* H, long long C, long long ldh, float 
 
 extern "C" size_t g2q_chol_workspace_bytes(int64_t C) {
   const int64_t nblk = (C + g2q::NB - 1) / g2q::NB;
-  return (size_t)(2 * C * C + nblk * g2q::NB * g2q::NB + 64) * sizeof(float) +
-         (size_t)6 * g2q::NB * C * sizeof(__half) + (size_t)3 * C * sizeof(float) + 256;
+  const size_t b = (size_t)(2 * C * C + nblk * g2q::NB * g2q::NB + 64) * sizeof(float) +
+                   (size_t)6 * g2q::NB * C * sizeof(__half) + (size_t)3 * C * sizeof(float) + 256;
+  return (b + 255) / 256 * 256;  // a multiple of 256: concurrent lanes take aligned slices
 }
+
+namespace g2q {
+// Up to CHOL_LANES factorizations of one call run side by side, each on a
+// library-owned stream forked from and joined back to the caller's stream
+// (same priority) with its own slice of the workspace: a chain is a few
+// hundred dependent, mostly latency-bound launches, so concurrent chains fill
+// the GPU that one chain leaves idle.
+constexpr int CHOL_LANES = 4;
+
+struct LaneSet {
+  int dev = -1;
+  cudaStream_t caller = nullptr;
+  cudaStream_t s[CHOL_LANES] = {};
+  cudaEvent_t fork = nullptr;
+  cudaEvent_t join[CHOL_LANES] = {};
+};
+
+static int lane_set(cudaStream_t caller, LaneSet** out) {
+  constexpr int kSets = 32;
+  static LaneSet sets[kSets];
+  static int next = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return G2Q_ERR_CUDA;
+  for (int i = 0; i < kSets; ++i)
+    if (sets[i].fork && sets[i].dev == dev && sets[i].caller == caller) {
+      *out = &sets[i];
+      return G2Q_OK;
+    }
+  LaneSet* ls = &sets[next];
+  next = (next + 1) % kSets;
+  int prio = 0;
+  if (cudaStreamGetPriority(caller, &prio) != cudaSuccess) return G2Q_ERR_CUDA;
+  if (!ls->fork || ls->dev != dev) {  // (a reused slot keeps its streams on the same device)
+    *ls = LaneSet();
+    for (int i = 0; i < CHOL_LANES; ++i) {
+      if (cudaStreamCreateWithPriority(&ls->s[i], cudaStreamNonBlocking, prio) != cudaSuccess ||
+          cudaEventCreateWithFlags(&ls->join[i], cudaEventDisableTiming) != cudaSuccess)
+        return G2Q_ERR_CUDA;
+    }
+    if (cudaEventCreateWithFlags(&ls->fork, cudaEventDisableTiming) != cudaSuccess)
+      return G2Q_ERR_CUDA;
+  }
+  ls->dev = dev;
+  ls->caller = caller;
+  *out = ls;
+  return G2Q_OK;
+}
+}  // namespace g2q
 
 extern "C" int g2q_chol_upper_inverse(float* U, const float* H, int64_t C, int64_t ldh,
                                       int64_t batch, const float* damp_percent_host, int* info,
@@ -631,12 +680,36 @@ extern "C" int g2q_chol_upper_inverse(float* U, const float* H, int64_t C, int64
                                       void* stream) {
   if (!U || !H || C <= 0 || ldh < C || batch < 0 || !damp_percent_host || !workspace)
     return G2Q_ERR_INVALID_ARG;
-  if (workspace_bytes < g2q_chol_workspace_bytes(C)) return G2Q_ERR_INVALID_ARG;
+  const size_t per = g2q_chol_workspace_bytes(C);
+  if (workspace_bytes < per) return G2Q_ERR_INVALID_ARG;
   if (precision != 0 && precision != 1) return G2Q_ERR_INVALID_ARG;
   cudaStream_t st = (cudaStream_t)stream;
-  for (int64_t b = 0; b < batch; ++b) {
-    G2Q_TRY(g2q::chol_one(U + b * C * C, H + b * C * ldh, C, ldh, damp_percent_host[b],
-                          info ? info + b : nullptr, (float*)workspace, precision, st));
+  long long lanes = (long long)(workspace_bytes / per);
+  if (lanes > g2q::CHOL_LANES) lanes = g2q::CHOL_LANES;
+  if (lanes > batch) lanes = batch;
+  if (lanes <= 1) {
+    for (int64_t b = 0; b < batch; ++b)
+      G2Q_TRY(g2q::chol_one(U + b * C * C, H + b * C * ldh, C, ldh, damp_percent_host[b],
+                            info ? info + b : nullptr, (float*)workspace, precision, st));
+    return G2Q_OK;
   }
-  return G2Q_OK;
+  g2q::LaneSet* ls = nullptr;
+  G2Q_TRY(g2q::lane_set(st, &ls));
+  if (cudaEventRecord(ls->fork, st) != cudaSuccess) return G2Q_ERR_CUDA;
+  for (long long l = 0; l < lanes; ++l)
+    if (cudaStreamWaitEvent(ls->s[l], ls->fork, 0) != cudaSuccess) return G2Q_ERR_CUDA;
+  int status = G2Q_OK;
+  for (int64_t b = 0; b < batch && status == G2Q_OK; ++b) {
+    const long long l = b % lanes;
+    float* ws = (float*)((char*)workspace + l * per);
+    status = g2q::chol_one(U + b * C * C, H + b * C * ldh, C, ldh, damp_percent_host[b],
+                           info ? info + b : nullptr, ws, precision, ls->s[l]);
+  }
+  // join every lane, also after an error, so that no lane's work outlives the call's stream
+  for (long long l = 0; l < lanes; ++l) {
+    if (cudaEventRecord(ls->join[l], ls->s[l]) != cudaSuccess ||
+        cudaStreamWaitEvent(st, ls->join[l], 0) != cudaSuccess)
+      return G2Q_ERR_CUDA;
+  }
+  return status;
 }

@@ -162,7 +162,8 @@ def chol_upper_inverse(H, damp_percent, info=None, precision=0):
     U = torch.empty_like(Hb)
     if info is None:
         info = torch.zeros(B, dtype=torch.int32, device=H.device)
-    ws_bytes = query("g2q_chol_workspace_bytes", C)
+    # up to four factorizations of the batch side by side (one workspace each)
+    ws_bytes = query("g2q_chol_workspace_bytes", C) * min(B, 4)
     ws = workspace(ws_bytes, H.device)
     call("g2q_chol_upper_inverse", U.data_ptr(), Hb.data_ptr(), C, C, B, damps, info.data_ptr(),
          int(precision), ws.data_ptr(), ws_bytes, _stream(H))

@@ -175,7 +175,9 @@ size_t g2q_gemm_tc_workspace_bytes(int64_t M, int64_t N, int64_t K, int64_t batc
  * factorization H + dI = V V^T (V upper), U = V^-1 -- potrf + trtri, half the
  * work of potrf + potri + potrf.  precision: 0 = fp32 CUDA cores, 1 = trailing
  * updates on tensor cores with a three-term bf16 split (fp32-level accuracy).
- * Needs g2q_chol_workspace_bytes(C) bytes.
+ * Needs g2q_chol_workspace_bytes(C) bytes; a workspace of k times that (k <= 4)
+ * lets k of the batch's factorizations run side by side on library-owned
+ * streams forked from and joined back to `stream`.
  * Replaces the damped Cholesky chain of gptq_utils/gptq_utils.py:291-311
  * (and its copies g2ptq_utils.py:430-450, gptaq_utils.py:323-343,
  * gptq_guided_utils.py:145-165); the damp auto-increment retry stays with the

@@ -135,6 +135,26 @@ def test_chol_large_identity_check():
     assert float(torch.tril(U[0], -1).abs().max()) == 0.0
 
 
+@pytest.mark.parametrize("precision", [0, 1])
+def test_chol_batch_lanes_match_one_by_one(precision):
+    """A batch of factorizations running side by side on forked streams (up to
+    four workspaces) gives each matrix's result of a call on its own, including
+    a failing one in the middle of the batch."""
+    g = torch.Generator(device=DEV).manual_seed(17)
+    B, C = 6, 640
+    X = torch.randn(B, 2 * C, C, device=DEV, generator=g)
+    H = (X.transpose(1, 2) @ X / (2 * C)).contiguous()
+    H[3] = -torch.eye(C, device=DEV)
+    damps = [0.01, 0.02, 0.01, 0.01, 0.05, 0.01]
+    U, info = ops.chol_upper_inverse(H, damps, precision=precision)
+    for b in range(B):
+        Ub, ib = ops.chol_upper_inverse(H[b:b + 1].contiguous(), [damps[b]], precision=precision)
+        assert int(ib.item()) == int(info[b].item())
+        if b != 3:
+            assert torch.equal(Ub[0], U[b])
+    assert int(info[3].item()) != 0
+
+
 def test_chol_reports_failure():
     H = -torch.eye(64, device=DEV)[None].contiguous()
     U, info = ops.chol_upper_inverse(H, 0.01)
