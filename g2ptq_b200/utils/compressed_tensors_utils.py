@@ -1,17 +1,31 @@
-"""compressed-tensors export staging, mirroring utils/compressed_tensors_utils.py:22-53.
+"""compressed-tensors export, mirroring utils/compressed_tensors_utils.py.
 
 ``compress`` has the reference's signature and checks; the int32 packing runs
 in the ``g2q_pack_int32`` kernel (same bit layout as
 ``compressed_tensors.compressors.pack_to_int32``).  ``compress_grouped`` is the
 direct path used by ``fasterquant``: it takes the per-group scales and int8
 codes the kernels already produce and skips the per-element Scale tensor.
+``register_qparam_buffers``, ``expand_ignore_list`` and
+``save_to_compressed_tensors`` write the quantized model as a "pack-quantized"
+compressed-tensors checkpoint (host code: the compressed-tensors quantization
+config and the transformers checkpoint writer).
 """
+
+import logging
+import os
+import re
 
 import torch
 
 from .. import ops
 
 Q_PARAMS = ("weight_packed", "weight_scale", "weight_shape")
+# fused projections of inference engines: an ignored member ignores the fused module too
+MERGE_PATTERNS = {
+    "qkv_proj": r"(q_proj|k_proj|v_proj)",
+    "in_proj_qkvz": r"(in_proj_qkv|in_proj_z)",
+    "in_proj_ba": r"(in_proj_b|in_proj_a)",
+}
 
 
 def compress_grouped(layer, group_scale, codes, bits):
@@ -52,3 +66,59 @@ def register_qparam_buffers(modules):
             continue
         for name, tensor in qparams.items():
             module.register_buffer(name, tensor)
+
+
+def expand_ignore_list(ignore_list, merge_patterns=None):
+    """compressed_tensors_utils.py:56-80: the ignore list plus, for every entry
+    naming a member of a fused projection, the fused module's name; sorted and
+    without duplicates."""
+    patterns = MERGE_PATTERNS if merge_patterns is None else merge_patterns
+    out = set(ignore_list)
+    for name in ignore_list:
+        for fused, pat in patterns.items():
+            if re.search(pat, name):
+                out.add(re.sub(pat, fused, name))
+    return sorted(out)
+
+
+def save_to_compressed_tensors(source_model, config, model, tokenizer, processor, save_path,
+                               bits=4, group_size=128, sym=True, export_mtp=False):
+    """compressed_tensors_utils.py:83-156: write ``model`` (its quantized linears
+    carrying ``weight_packed`` / ``weight_scale`` / ``weight_shape`` buffers, see
+    ``register_qparam_buffers``) as a pack-quantized compressed-tensors
+    checkpoint with its config, generation config, tokenizer and processor.
+    Linears (and convolutions) without packed weights are listed as ignored;
+    packed ones lose their float ``weight``."""
+    from compressed_tensors.quantization import (QuantizationArgs, QuantizationConfig,
+                                                 QuantizationScheme, QuantizationStrategy,
+                                                 QuantizationType)
+    assert bits in (4, 8) and sym, "pack-quantized export supports symmetric 4 / 8 bits"
+    os.makedirs(save_path, exist_ok=True)
+    ignore = ["re:^mtp.*"]
+    for name, module in model.named_modules():
+        if isinstance(module, (torch.nn.Linear, torch.nn.modules.conv._ConvNd)):
+            if hasattr(module, "weight_packed"):
+                del module.weight
+            else:
+                ignore.append(name)
+    ignore = expand_ignore_list(ignore)
+    weights = QuantizationArgs(
+        num_bits=bits, type=QuantizationType.INT,
+        strategy=QuantizationStrategy.CHANNEL if group_size == -1 else QuantizationStrategy.GROUP,
+        group_size=group_size, symmetric=sym, dynamic=False)
+    scheme = QuantizationScheme(targets=["Linear"], format="pack-quantized", weights=weights)
+    qconfig = QuantizationConfig(config_groups={"group_0": scheme}, ignore=ignore,
+                                 format="pack-quantized", quant_method="compressed-tensors",
+                                 quantization_status="compressed")
+    if hasattr(config, "quantization_config"):
+        delattr(config, "quantization_config")
+    config.quantization_config = qconfig.model_dump()
+    logging.info(f"Saving compressed model to {save_path}...")
+    config.save_pretrained(save_path)
+    model.generation_config.save_pretrained(save_path)
+    tokenizer.save_pretrained(save_path)
+    processor.save_pretrained(save_path)
+    model.save_pretrained(save_path, safe_serialization=True, save_original_format=False)
+    if export_mtp:
+        from compressed_tensors.utils import save_mtp_tensors_to_checkpoint
+        save_mtp_tensors_to_checkpoint(source_model=source_model, dest_dir=save_path)

@@ -402,16 +402,106 @@ def gen_misc(ref):
     save("misc.npz", **out)
 
 
+# ---------------------------------------------------------------------------
+# compressed-tensors export (utils/compressed_tensors_utils.py)
+# ---------------------------------------------------------------------------
+
+EXPORT_IGNORE_CASES = [
+    ["re:^mtp.*", "lm_head"],
+    ["model.layers.0.self_attn.q_proj", "model.layers.3.self_attn.v_proj", "lm_head"],
+    ["model.layers.1.linear_attn.in_proj_qkv", "model.layers.1.linear_attn.in_proj_b",
+     "model.layers.1.linear_attn.in_proj_z", "model.layers.2.mlp.gate"],
+]
+EXPORT_LINEARS = ["self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj", "self_attn.o_proj",
+                  "mlp.gate_proj", "mlp.up_proj", "mlp.down_proj"]
+EXPORT_GS = 32
+
+
+def export_tiny_model():
+    """The tiny Llama the export fixture is written from (seeded, CPU)."""
+    from transformers import LlamaConfig, LlamaForCausalLM
+    torch.manual_seed(1234)
+    cfg = LlamaConfig(hidden_size=64, intermediate_size=96, num_hidden_layers=1,
+                      num_attention_heads=4, num_key_value_heads=2, vocab_size=128,
+                      max_position_embeddings=64)
+    return cfg, LlamaForCausalLM(cfg).to(torch.bfloat16)
+
+
+def export_codes(model):
+    """Seeded int4 codes and group scales for every linear of the decoder layer."""
+    gen = torch.Generator().manual_seed(99)
+    out = {}
+    layer = model.model.layers[0]
+    for name in EXPORT_LINEARS:
+        mod = layer.get_submodule(name)
+        R, C = mod.weight.shape
+        out[name + "__codes"] = torch.randint(-8, 8, (R, C), generator=gen, dtype=torch.int8)
+        out[name + "__scale"] = torch.rand(R, C // EXPORT_GS, generator=gen) * 0.01 + 1e-3
+    return out
+
+
+class _Saver:
+    def save_pretrained(self, path):
+        pass
+
+
+def export_table(path):
+    """{tensor name: [dtype, shape, sha256 of the bytes]} of a saved checkpoint."""
+    import hashlib
+    import glob
+    from safetensors.torch import load_file
+    table = {}
+    for f in sorted(glob.glob(os.path.join(path, "*.safetensors"))):
+        for k, v in load_file(f).items():
+            b = v.contiguous().view(torch.uint8).numpy().tobytes()
+            table[k] = [str(v.dtype), list(v.shape), hashlib.sha256(b).hexdigest()]
+    return table
+
+
+def gen_export(ref_root):
+    import json
+    import tempfile
+    from utils import compressed_tensors_utils as ctu
+    cases = [[c, ctu.expand_ignore_list(c)] for c in EXPORT_IGNORE_CASES]
+    cfg, model = export_tiny_model()
+    codes = export_codes(model)
+    layer = model.model.layers[0]
+    mods = []
+    for name in EXPORT_LINEARS:
+        mod = layer.get_submodule(name)
+        R, C = mod.weight.shape
+        scale = codes[name + "__scale"].repeat_interleave(EXPORT_GS, dim=1)
+        ctu.compress(mod, scale, codes[name + "__codes"].float(), 4, EXPORT_GS)
+        mods.append(mod)
+    ctu.register_qparam_buffers(mods)
+    with tempfile.TemporaryDirectory() as d:
+        ctu.save_to_compressed_tensors("tiny", cfg, model, _Saver(), _Saver(), d, bits=4,
+                                       group_size=EXPORT_GS, sym=True)
+        table = export_table(d)
+        with open(os.path.join(d, "config.json")) as f:
+            qcfg = json.load(f)["quantization_config"]
+    with open(os.path.join(HERE, "export.json"), "w") as f:
+        json.dump({"ignore_cases": cases, "quantization_config": qcfg, "tensors": table}, f,
+                  indent=1, sort_keys=True)
+    save("export.npz", **{k: npy(v) for k, v in codes.items()})
+    print("wrote", os.path.join(HERE, "export.json"), len(table), "tensors")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of the reference checkout")
+    ap.add_argument("--only", default=None, help="one fixture family: export")
     args = ap.parse_args()
     torch.set_num_threads(min(8, os.cpu_count() or 1))
     ref = import_reference(os.path.abspath(args.reference))
+    if args.only == "export":
+        gen_export(os.path.abspath(args.reference))
+        return
     gen_hessians(ref)
     gen_blocks(ref)
     gen_fasterquant(ref)
     gen_misc(ref)
+    gen_export(os.path.abspath(args.reference))
 
 
 if __name__ == "__main__":
