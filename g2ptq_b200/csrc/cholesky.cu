@@ -40,22 +40,36 @@ __global__ void mean_diag_kernel(const float* H, long long C, long long ldh, flo
 }
 
 // A[i][j] = H[C-1-i][C-1-j] (+ damp on the diagonal) for j <= i; Y = I.
+// Row i over the grid's y loop, columns over the x threads (no per-element
+// division).
 __global__ void reverse_damp_kernel(const float* H, long long C, long long ldh,
                                     const float* mean_diag, float damp_percent,
                                     float* A, float* Y) {
   const float damp = damp_percent * (*mean_diag);
-  long long n = C * C;
-  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < n;
-       idx += (long long)gridDim.x * blockDim.x) {
-    long long i = idx / C, j = idx - i * C;
-    float v = 0.f;
-    if (j <= i) {
-      v = H[(C - 1 - i) * ldh + (C - 1 - j)];
-      if (i == j) v += damp;
+  for (long long i = blockIdx.y; i < C; i += gridDim.y) {
+    const float* h = H + (C - 1 - i) * ldh + (C - 1);
+    for (long long j = (long long)blockIdx.x * blockDim.x + threadIdx.x; j < C;
+         j += (long long)gridDim.x * blockDim.x) {
+      float v = 0.f;
+      if (j <= i) {
+        v = h[-j];
+        if (i == j) v += damp;
+      }
+      A[i * C + j] = v;
+      Y[i * C + j] = (i == j) ? 1.f : 0.f;
     }
-    A[idx] = v;
-    Y[idx] = (i == j) ? 1.f : 0.f;
   }
+}
+
+static dim3 grid_rows2(long long rows, long long cols) {
+  long long gx = (cols + 255) / 256;
+  if (gx > 64) gx = 64;
+  if (gx < 1) gx = 1;
+  // one wave of eight 256-thread CTAs per SM; the kernels loop over the rest
+  long long gy = (148 * 8 + gx - 1) / gx;
+  if (gy > rows) gy = rows;
+  if (gy < 1) gy = 1;
+  return dim3((unsigned)gx, (unsigned)gy);
 }
 
 // Factor the nb x nb diagonal block at (k0, k0) of A in place and write its
@@ -438,17 +452,18 @@ static int linv_apply(float* S, long long lds, long long n, const float* Linv, i
 
 // U[i][j] = X[C-1-i][C-1-j] for i <= j, 0 below; NaN -> info = -1.
 __global__ void extract_u_kernel(const float* X, long long C, float* U, int* info) {
-  long long n = C * C;
   bool nan_seen = false;
-  for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < n;
-       idx += (long long)gridDim.x * blockDim.x) {
-    long long i = idx / C, j = idx - i * C;
-    float v = 0.f;
-    if (i <= j) {
-      v = X[(C - 1 - i) * C + (C - 1 - j)];
-      if (v != v) nan_seen = true;
+  for (long long i = blockIdx.y; i < C; i += gridDim.y) {
+    const float* x = X + (C - 1 - i) * C + (C - 1);
+    for (long long j = (long long)blockIdx.x * blockDim.x + threadIdx.x; j < C;
+         j += (long long)gridDim.x * blockDim.x) {
+      float v = 0.f;
+      if (i <= j) {
+        v = x[-j];
+        if (v != v) nan_seen = true;
+      }
+      U[i * C + j] = v;
     }
-    U[idx] = v;
   }
   if (nan_seen && info) atomicCAS(info, 0, -1);
 }
@@ -561,9 +576,7 @@ static int chol_one(float* U, const float* H, long long C, long long ldh, float 
   if (info && cudaMemsetAsync(info, 0, sizeof(int), st) != cudaSuccess) return G2Q_ERR_CUDA;
   mean_diag_kernel<<<1, 1024, 0, st>>>(H, C, ldh, w.mdiag);
   G2Q_CHECK_LAUNCH();
-  int blocks = (int)((C * C + 255) / 256);
-  if (blocks > 148 * 32) blocks = 148 * 32;
-  reverse_damp_kernel<<<blocks, 256, 0, st>>>(H, C, ldh, w.mdiag, damp_percent, A, Y);
+  reverse_damp_kernel<<<grid_rows2(C, C), 256, 0, st>>>(H, C, ldh, w.mdiag, damp_percent, A, Y);
   G2Q_CHECK_LAUNCH();
   const long long tsz = (long long)NB * C;
   for (long long kb = 0; kb < nblk; ++kb) {
@@ -612,7 +625,7 @@ static int chol_one(float* U, const float* H, long long C, long long ldh, float 
     if (cudaEventRecord(ev[2 * kb + 1], side) != cudaSuccess) return G2Q_ERR_CUDA;
   }
   if (cudaStreamWaitEvent(st, ev[2 * (nblk - 1) + 1], 0) != cudaSuccess) return G2Q_ERR_CUDA;
-  extract_u_kernel<<<blocks, 256, 0, st>>>(Y, C, U, info);
+  extract_u_kernel<<<grid_rows2(C, C), 256, 0, st>>>(Y, C, U, info);
   G2Q_CHECK_LAUNCH();
   return G2Q_OK;
 }

@@ -608,15 +608,16 @@ __global__ void fake_quantize_kernel(float* out, long long ldo, int8_t* codes, l
   }
 }
 
-// W[b][:, c] -= f * G[b][:, c] over a column range (G2PTQ gradient term).
+// W[b][:, c] -= f * G[b][:, c] over a column range (G2PTQ gradient term); row r
+// over the grid's y loop, columns over the x threads.
 __global__ void sub_scaled_kernel(float* W, const float* G, long long nl_rows, long long C,
                                   long long c0, float f) {
-  const long long w = C - c0;
-  const long long n = nl_rows * w;
-  for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < n;
-       idx += (long long)gridDim.x * blockDim.x) {
-    const long long r = idx / w, c = c0 + (idx - r * w);
-    W[r * C + c] -= f * G[r * C + c];
+  for (long long r = blockIdx.y; r < nl_rows; r += gridDim.y) {
+    float* w = W + r * C;
+    const float* g = G + r * C;
+    for (long long c = c0 + (long long)blockIdx.x * blockDim.x + threadIdx.x; c < C;
+         c += (long long)gridDim.x * blockDim.x)
+      w[c] -= f * g[c];
   }
 }
 
@@ -812,8 +813,12 @@ extern "C" int g2q_compensate(int method, float* W, int64_t nl, int64_t rows, in
     if (i2 >= C) break;
     const long long N = C - i2;
     if (method == G2Q_METHOD_G2PTQ) {
-      sub_scaled_kernel<<<grid_for(nl * rows * N), 256, 0, st>>>(W, gh, nl * rows, C, i2,
-                                                                 (float)blocksize);
+      long long gx = (N + 255) / 256;
+      if (gx > 64) gx = 64;
+      long long gy = (148 * 8 + gx - 1) / gx;  // one wave of eight CTAs per SM
+      if (gy > nl * rows) gy = nl * rows;
+      const dim3 grid((unsigned)gx, (unsigned)gy);
+      sub_scaled_kernel<<<grid, 256, 0, st>>>(W, gh, nl * rows, C, i2, (float)blocksize);
       G2Q_CHECK_LAUNCH();
     }
     // W[:, i2:] -= Erra @ U[i1:i2, i2:]  (+ G2PTQ: GH[:, i2:] -= Z[:, i1:i2] @ U[i1:i2, i2:];

@@ -1121,18 +1121,19 @@ template <typename S>
 __global__ void split_rows_kernel(const S* X, long long ldx, long long T, long long C,
                                   const float* s, long long sstride, __nv_bfloat16* hi,
                                   __nv_bfloat16* lo, long long ldo) {
-  const long long n = T * C;
-  for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < n;
-       idx += (long long)gridDim.x * blockDim.x) {
-    const long long t = idx / C, c = idx - t * C;
-    float v;
-    if constexpr (sizeof(S) == 2) v = __bfloat162float(X[t * ldx + c]);
-    else v = X[t * ldx + c];
-    if (s) v *= s[t * sstride];
-    __nv_bfloat16 h, l;
-    split_bf16(v, &h, &l);
-    hi[t * ldo + c] = h;
-    if (lo) lo[t * ldo + c] = l;
+  for (long long t = blockIdx.y; t < T; t += gridDim.y) {
+    const float f = s ? s[t * sstride] : 1.f;
+    for (long long c = (long long)blockIdx.x * blockDim.x + threadIdx.x; c < C;
+         c += (long long)gridDim.x * blockDim.x) {
+      float v;
+      if constexpr (sizeof(S) == 2) v = __bfloat162float(X[t * ldx + c]);
+      else v = X[t * ldx + c];
+      if (s) v *= f;
+      __nv_bfloat16 h, l;
+      split_bf16(v, &h, &l);
+      hi[t * ldo + c] = h;
+      if (lo) lo[t * ldo + c] = l;
+    }
   }
 }
 
@@ -1146,12 +1147,17 @@ static int split_rows(const void* X, int dtype, long long ldx, long long T, long
                       const float* s, long long sstride, __nv_bfloat16* hi, __nv_bfloat16* lo,
                       long long ldo, cudaStream_t st) {
   if (T * C == 0) return G2Q_OK;
+  long long gx = (C + 255) / 256;
+  if (gx > 64) gx = 64;
+  long long gy = (148 * 8 + gx - 1) / gx;  // one wave of eight CTAs per SM
+  if (gy > T) gy = T;
+  const dim3 grid((unsigned)gx, (unsigned)gy);
   if (dtype == G2Q_DTYPE_BF16)
-    split_rows_kernel<__nv_bfloat16><<<grid_for(T * C), 256, 0, st>>>(
+    split_rows_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
         (const __nv_bfloat16*)X, ldx, T, C, s, sstride, hi, lo, ldo);
   else
-    split_rows_kernel<float><<<grid_for(T * C), 256, 0, st>>>((const float*)X, ldx, T, C, s,
-                                                              sstride, hi, lo, ldo);
+    split_rows_kernel<float><<<grid, 256, 0, st>>>((const float*)X, ldx, T, C, s, sstride, hi,
+                                                   lo, ldo);
   G2Q_CHECK_LAUNCH();
   return G2Q_OK;
 }
@@ -1342,7 +1348,10 @@ int tc_gram_grouped(float* D, long long ldd, long long d_gstride, long long C, c
     __nv_bfloat16* hi = take((long long)G * T * w);
     __nv_bfloat16* lo = take((long long)G * T * w);
     const long long nv = C / 8;
-    dim3 grid((unsigned)cdiv(nv, 256), (unsigned)(T < 65535 ? T : 65535));
+    const long long gxv = cdiv(nv, 256) < 64 ? cdiv(nv, 256) : 64;
+    long long gyv = (148 * 8 + gxv - 1) / gxv;  // one wave of eight CTAs per SM
+    if (gyv > T) gyv = T;
+    dim3 grid((unsigned)gxv, (unsigned)gyv);
     tc::split_rows_groups_kernel<<<grid, 256, 0, st>>>((const __nv_bfloat16*)X, ldx, T, C, s,
                                                        sstride, G, hi, lo, w, T * w);
     G2Q_CHECK_LAUNCH();

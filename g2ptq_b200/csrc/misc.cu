@@ -163,28 +163,45 @@ __global__ void mean_diag_kernel(float* key, const float* H, long long nl, long 
   key[c] = s / (float)nl;
 }
 
+// Row r of the grid's y loop, columns over the x threads: no 64-bit division
+// per element (the flat-index form of these kernels ran at a sixth of HBM
+// bandwidth on the division alone).
 template <typename T>
 __global__ void permute_cols_kernel(T* dst, const T* src, long long rows, long long C,
                                     const long long* perm, int inverse) {
-  const long long n = rows * C;
-  for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < n;
-       idx += (long long)gridDim.x * blockDim.x) {
-    const long long r = idx / C, c = idx - r * C;
-    if (inverse) dst[r * C + perm[c]] = src[idx];
-    else dst[idx] = src[r * C + perm[c]];
+  for (long long r = blockIdx.y; r < rows; r += gridDim.y) {
+    const T* s = src + r * C;
+    T* d = dst + r * C;
+    for (long long c = (long long)blockIdx.x * blockDim.x + threadIdx.x; c < C;
+         c += (long long)gridDim.x * blockDim.x) {
+      if (inverse) d[perm[c]] = s[c];
+      else d[c] = s[perm[c]];
+    }
   }
 }
 
 __global__ void permute_sym_kernel(float* dst, const float* src, long long nl, long long C,
                                    const long long* perm) {
-  const long long n = nl * C * C;
-  for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < n;
-       idx += (long long)gridDim.x * blockDim.x) {
-    const long long b = idx / (C * C);
-    const long long rem = idx - b * C * C;
-    const long long i = rem / C, j = rem - i * C;
-    dst[idx] = src[b * C * C + perm[i] * C + perm[j]];
+  for (long long row = blockIdx.y; row < nl * C; row += gridDim.y) {
+    const long long b = row / C, i = row - b * C;
+    const float* s = src + b * C * C + perm[i] * C;
+    float* d = dst + row * C;
+    for (long long j = (long long)blockIdx.x * blockDim.x + threadIdx.x; j < C;
+         j += (long long)gridDim.x * blockDim.x)
+      d[j] = s[perm[j]];
   }
+}
+
+// 2-D grid for a rows x cols elementwise kernel with 256 threads along a row
+static dim3 grid_rows(long long rows, long long cols) {
+  long long gx = (cols + 255) / 256;
+  if (gx > 64) gx = 64;
+  if (gx < 1) gx = 1;
+  // one wave of eight 256-thread CTAs per SM; the kernels loop over the rest
+  long long gy = (148 * 8 + gx - 1) / gx;
+  if (gy > rows) gy = rows;
+  if (gy < 1) gy = 1;
+  return dim3((unsigned)gx, (unsigned)gy);
 }
 
 template <typename D>
@@ -527,11 +544,11 @@ extern "C" int g2q_permute_cols(void* dst, const void* src, int elem_bytes, int6
   if (n == 0) return G2Q_OK;
   cudaStream_t st = (cudaStream_t)stream;
   if (elem_bytes == 4)
-    permute_cols_kernel<float><<<grid_for(n), 256, 0, st>>>((float*)dst, (const float*)src,
+    permute_cols_kernel<float><<<grid_rows(nl * rows, C), 256, 0, st>>>((float*)dst, (const float*)src,
                                                             nl * rows, C, (const long long*)perm,
                                                             inverse);
   else if (elem_bytes == 1)
-    permute_cols_kernel<int8_t><<<grid_for(n), 256, 0, st>>>((int8_t*)dst, (const int8_t*)src,
+    permute_cols_kernel<int8_t><<<grid_rows(nl * rows, C), 256, 0, st>>>((int8_t*)dst, (const int8_t*)src,
                                                              nl * rows, C,
                                                              (const long long*)perm, inverse);
   else
@@ -543,7 +560,7 @@ extern "C" int g2q_permute_cols(void* dst, const void* src, int elem_bytes, int6
 extern "C" int g2q_permute_sym(float* dst, const float* src, int64_t nl, int64_t C,
                                const int64_t* perm, void* stream) {
   if (!dst || !src || !perm || nl <= 0 || C <= 0 || dst == src) return G2Q_ERR_INVALID_ARG;
-  permute_sym_kernel<<<grid_for(nl * C * C), 256, 0, (cudaStream_t)stream>>>(
+  permute_sym_kernel<<<grid_rows(nl * C, C), 256, 0, (cudaStream_t)stream>>>(
       dst, src, nl, C, (const long long*)perm);
   G2Q_CHECK_LAUNCH();
   return G2Q_OK;
