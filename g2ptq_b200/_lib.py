@@ -11,7 +11,7 @@ import os
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.environ.get("G2PTQ_B200_LIB", os.path.join(_HERE, "_lib", "libg2ptq_b200.so"))
 
-ABI_VERSION = 5
+ABI_VERSION = 6
 
 G2Q_OK = 0
 G2Q_ERR_INVALID_ARG = -1
@@ -25,6 +25,7 @@ G2Q_ERR_SCRATCH_LIMIT = -7
 DTYPE_BF16, DTYPE_F32, DTYPE_F16 = 0, 1, 2
 METHOD_GPTQ, METHOD_G2PTQ, METHOD_GPTAQ = 0, 1, 2
 MASK_FULL, MASK_LOWER, MASK_UPPER, MASK_STRICT_UPPER = 0, 1, 2, 3
+LOSS_KL, LOSS_NLL, LOSS_MSE = 0, 1, 2
 
 P = ctypes.c_void_p
 I64 = ctypes.c_int64
@@ -82,6 +83,11 @@ SIGNATURES = {
     "g2q_gram_update_noalloc": [P, I64, I64, I64, P, I32, I64, P, I32, I64, P, I64, I64, I32, F32,
                                 F32, P],
     "g2q_gram_static_scratch_bytes": [],
+    "g2q_saliency": [P, P, I32, I64, I64, I64, I32, P],
+    "g2q_scaled_accumulate": [P, P, I64, F32, I32, P],
+    "g2q_running_mean": [P, P, I32, I64, F32, F32, I32, P],
+    "g2q_block_loss_forward": [I32, P, P, P, P, P, I32, I64, I64, I64, I64, P],
+    "g2q_block_loss_backward": [I32, P, I64, P, P, P, P, I32, I64, I64, P, I64, I64, P],
 }
 _RESTYPES = {
     "g2q_launch_count": ctypes.c_int64,

@@ -19,6 +19,8 @@ from . import _engine
 from .common_utils import fake_quantize_grouped
 from .graph_utils import validate_tensors
 from .gptq_utils import _onload
+from .refresh import (SaliencyCache, GradientCache, normalize_loss_weights,  # noqa: F401
+                      compute_kl_grad_hessian, compute_mse_grad_hessian, block_loss)
 
 
 def run_eager(weight, hinv, scale, zero, z, ghinv, maxq, backend="torch", int_weight=None,

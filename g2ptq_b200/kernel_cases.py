@@ -4,6 +4,9 @@
     python -m g2ptq_b200.kernel_cases gram_weighted --tokens 16384 --columns 4096
     python -m g2ptq_b200.kernel_cases chol --columns 4096
     python -m g2ptq_b200.kernel_cases compensate --rows 4096 --columns 4096
+    python -m g2ptq_b200.kernel_cases block_loss --tokens 2048 --vocab 128256 --loss kl
+    python -m g2ptq_b200.kernel_cases saliency --tokens 8192 --rows 14336
+    python -m g2ptq_b200.kernel_cases running_mean --rows 14336 --columns 4096
 
 Each case builds seeded synthetic inputs of one fold / one factorization /
 one compensation pass of a Llama-3-8B linear on ``cuda:0``, runs ``--warmup``
@@ -113,8 +116,53 @@ def compensate(args, g):
                 flops=flops)
 
 
+def block_loss(args, g):
+    """One G2PTQ refresh loss head over ``tokens`` rows of ``vocab`` BF16 logits
+    (KL to a second set of logits, cross entropy against sampled labels, or
+    the squared error to a target): the forward and the backward kernel,
+    timed apart.  Algorithmic bytes: forward reads x (and the target), the
+    backward reads them again and writes the gradient."""
+    N, V = args.tokens, args.vocab
+    kind = {"kl": _lib.LOSS_KL, "nll": _lib.LOSS_NLL, "mse": _lib.LOSS_MSE}[args.loss]
+    x = (torch.randn(N, V, device="cuda", generator=g) * 3).to(torch.bfloat16)
+    t = labels = None
+    if kind == _lib.LOSS_NLL:
+        labels = torch.randint(0, V, (N,), device="cuda", generator=g)
+    else:
+        t = (x.float() + 0.3 * torch.randn(N, V, device="cuda", generator=g)).to(torch.bfloat16)
+    _, stats, x2, t2, lab = ops.block_loss_forward(kind, x, t, labels)
+    fwd = _time(lambda: ops.block_loss_forward(kind, x, t, labels), args.warmup, args.reps)
+    bwd = _time(lambda: ops.block_loss_backward(kind, stats, x2, t2, lab), args.warmup, args.reps)
+    n_in = 1 if kind == _lib.LOSS_NLL else 2
+    fb, bb = n_in * N * V * 2, (n_in + 1) * N * V * 2
+    return dict(case="block_loss", loss=args.loss, tokens=N, vocab=V, fwd_ms=fwd, bwd_ms=bwd,
+                fwd_bytes=fb, bwd_bytes=bb, fwd_gbs=fb / fwd / 1e6, bwd_gbs=bb / bwd / 1e6)
+
+
+def saliency(args, g):
+    """SaliencyCache.grad_hook over a ``tokens`` x ``rows`` BF16 output gradient."""
+    T, R = args.tokens, args.rows
+    grad = (torch.randn(T, R, device="cuda", generator=g) * 1e-3).to(torch.bfloat16)
+    out = torch.empty(T, 4, device="cuda")
+    ms = _time(lambda: ops.saliency(grad, 4, out=out), args.warmup, args.reps)
+    b = T * R * 2 + T * 4 * 4
+    return dict(case="saliency", tokens=T, rows=R, ms=ms, bytes=b, gbs=b / ms / 1e6)
+
+
+def running_mean(args, g):
+    """GradientCache.cache_gradient over a ``rows`` x ``columns`` BF16 weight gradient."""
+    R, C = args.rows, args.columns
+    grad = (torch.randn(R, C, device="cuda", generator=g) * 1e-3).to(torch.bfloat16)
+    cache = torch.zeros(R, C, device="cuda")
+    ms = _time(lambda: ops.running_mean(cache, grad, 0.5, 1.0 / 4096, False), args.warmup,
+               args.reps)
+    b = R * C * (2 + 4 + 4)
+    return dict(case="running_mean", rows=R, columns=C, ms=ms, bytes=b, gbs=b / ms / 1e6)
+
+
 CASES = {"gram": gram, "gram_weighted": gram_weighted, "chol": chol,
-         "compensate": compensate}
+         "compensate": compensate, "block_loss": block_loss, "saliency": saliency,
+         "running_mean": running_mean}
 
 
 def main(argv=None):
@@ -123,6 +171,8 @@ def main(argv=None):
     ap.add_argument("--tokens", type=int, default=16384)
     ap.add_argument("--columns", type=int, default=4096)
     ap.add_argument("--rows", type=int, default=4096)
+    ap.add_argument("--vocab", type=int, default=128256)
+    ap.add_argument("--loss", choices=["kl", "nll", "mse"], default="kl")
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--reps", type=int, default=5)
     args = ap.parse_args(argv)

@@ -373,3 +373,96 @@ def scale_rows(X, s):
     nl, rows, C = X.shape
     call("g2q_scale_rows", X.data_ptr(), s.data_ptr(), nl, rows, C, _stream(X))
     return X
+
+
+# --------------------------------------------------------------------------
+# G2PTQ refresh step: saliency / gradient caches and the block-loss heads
+# --------------------------------------------------------------------------
+
+def _rows2d(t):
+    """``t`` viewed as ``[rows, t.shape[-1]]`` with unit column stride."""
+    t2 = t.reshape(-1, t.shape[-1]) if t.dim() != 2 else t
+    if t2.shape[-1] > 1 and t2.stride(-1) != 1:
+        t2 = t2.contiguous()
+    return t2
+
+
+def saliency(grad, num_groups, out=None):
+    """``[T, G]`` fp32 group means of ``grad**2`` over ``grad``'s last dim."""
+    _cuda(grad, out)
+    g2 = _rows2d(grad)
+    T, R = g2.shape
+    if R % num_groups:
+        raise RuntimeError(f"shape '[{T}, {num_groups}, {R / num_groups}]' is invalid for "
+                           f"input of size {T * R}")
+    if out is None:
+        out = torch.empty(T, num_groups, dtype=torch.float32, device=grad.device)
+    _contig(out)
+    call("g2q_saliency", out.data_ptr(), g2.data_ptr(), dtype_code(g2.dtype),
+         g2.stride(0) if T > 1 else R, T, R, int(num_groups), _stream(g2))
+    return out
+
+
+def scaled_accumulate(out, x, w, first):
+    """``out <- (0 if first else out) + w * x`` (fp32, same shapes)."""
+    _cuda(out, x)
+    _contig(out, x)
+    if out.dtype != torch.float32 or x.dtype != torch.float32 or out.numel() != x.numel():
+        raise ValueError("scaled_accumulate takes two fp32 tensors of the same size")
+    call("g2q_scaled_accumulate", out.data_ptr(), x.data_ptr(), out.numel(), float(w),
+         int(bool(first)), _stream(out))
+    return out
+
+
+def running_mean(cache, grad, keep, inv, first):
+    """``cache <- (0 if first else cache * keep) + grad * inv`` (cache fp32)."""
+    _cuda(cache, grad)
+    _contig(cache, grad)
+    if cache.dtype != torch.float32 or cache.numel() != grad.numel():
+        raise ValueError("running_mean takes an fp32 cache of the gradient's size")
+    call("g2q_running_mean", cache.data_ptr(), grad.data_ptr(), dtype_code(grad.dtype),
+         grad.numel(), float(keep), float(inv), int(bool(first)), _stream(cache))
+    return cache
+
+
+def block_loss_forward(kind, x, target=None, labels=None):
+    """Block-loss head over the rows of ``x`` (last dim = V).  Returns
+    ``(loss, row_stats, x2, t2, labels)``: an fp32 scalar, the per-row
+    statistics the backward needs and the 2-D operands it reads."""
+    _cuda(x, target, labels)
+    x2 = _rows2d(x)
+    rows, V = x2.shape
+    t2 = None
+    if kind == _lib.LOSS_NLL:
+        labels = labels.reshape(-1)
+        if labels.dtype != torch.int64 or labels.numel() != rows:
+            raise ValueError("labels must be int64 with one entry per row")
+        labels = labels.contiguous()
+    else:
+        if target is None or target.shape != x.shape:
+            raise ValueError("target must have the shape of x")
+        if target.dtype != x.dtype:
+            raise TypeError("target and x must have the same dtype")
+        t2 = _rows2d(target)
+    loss = torch.empty((), dtype=torch.float32, device=x.device)
+    stats = torch.empty(max(rows, 1), 3, dtype=torch.float32, device=x.device)
+    call("g2q_block_loss_forward", int(kind), loss.data_ptr(), stats.data_ptr(), x2.data_ptr(),
+         _ptr(t2), _ptr(labels), dtype_code(x2.dtype), x2.stride(0) if rows > 1 else V,
+         (t2.stride(0) if rows > 1 else V) if t2 is not None else V, rows, V, _stream(x2))
+    return loss, stats, x2, t2, labels
+
+
+def block_loss_backward(kind, stats, x2, t2, labels, grad_scale=None):
+    """Gradient of the block loss with respect to the 2-D ``x2`` (same dtype),
+    times the fp32 scalar tensor ``grad_scale`` (None = 1)."""
+    rows, V = x2.shape
+    grad = torch.empty(rows, V, dtype=x2.dtype, device=x2.device)
+    gs = None
+    if grad_scale is not None:
+        gs = grad_scale.reshape(()).to(torch.float32).contiguous()
+    call("g2q_block_loss_backward", int(kind), grad.data_ptr(), V, stats.data_ptr(),
+         x2.data_ptr(), _ptr(t2), _ptr(labels), dtype_code(x2.dtype),
+         x2.stride(0) if rows > 1 else V,
+         (t2.stride(0) if rows > 1 else V) if t2 is not None else V, _ptr(gs), rows, V,
+         _stream(x2))
+    return grad

@@ -48,6 +48,11 @@ extern "C" {
 #define G2Q_METHOD_G2PTQ 1
 #define G2Q_METHOD_GPTAQ 2
 
+/* block-loss heads of the G2PTQ refresh step */
+#define G2Q_LOSS_KL 0  /* sum of KL(softmax(target) || softmax(x)) over rows */
+#define G2Q_LOSS_NLL 1 /* sum of cross entropy of x against int64 labels */
+#define G2Q_LOSS_MSE 2 /* sum over rows of mean((x - target)^2) / 2 */
+
 /* output masks of g2q_gemm */
 #define G2Q_MASK_FULL 0
 #define G2Q_MASK_LOWER 1        /* i >= j */
@@ -348,6 +353,51 @@ int g2q_diag_of_utu(float* dinv, const float* U, int64_t nl, int64_t C, void* st
 /* X[b][r][c] *= s[b*rows + r]  (row scaling, G2PTQ Z = (G U^T) * beta). */
 int g2q_scale_rows(float* X, const float* s, int64_t nl, int64_t rows, int64_t C,
                    void* stream);
+
+/* ---- G2PTQ refresh step (saliency and gradient caches, block losses) ---- */
+
+/* out[t][g] = mean over columns g*R/G .. (g+1)*R/G - 1 of grad[t][:]^2, fp32
+ * ([T, G], contiguous); grad is [T, R] with row stride ld (G2Q_DTYPE_*).
+ * R % G != 0 is invalid.  Replaces SaliencyCache.grad_hook,
+ * gptq_utils/g2ptq_utils.py:605-618. */
+int g2q_saliency(float* out, const void* grad, int dtype, int64_t ld, int64_t T, int64_t R,
+                 int G, void* stream);
+
+/* out[i] = (first ? 0 : out[i]) + w * x[i], product and sum rounded apart.
+ * One term of the weighted sum over loss types of summarize_saliency /
+ * summarize_gradients, gptq_utils/g2ptq_utils.py:620-640 and 704-711. */
+int g2q_scaled_accumulate(float* out, const float* x, int64_t n, float w, int first,
+                          void* stream);
+
+/* cache[i] = (first ? 0 : cache[i] * keep) + grad[i] * inv, each operation
+ * rounded apart; with keep = i / (i + 1) and inv the fp32 reciprocal of
+ * n_tokens * (i + 1) this is GradientCache.cache_gradient,
+ * gptq_utils/g2ptq_utils.py:693-702 (torch divides by a host scalar on the
+ * GPU as a multiply by its fp32 reciprocal). */
+int g2q_running_mean(float* cache, const void* grad, int dtype, int64_t n, float keep,
+                     float inv, int first, void* stream);
+
+/* Block-loss forward over `rows` rows of V values (x row stride ldx; target,
+ * same dtype, stride ldt, for KL and MSE; int64 labels [rows] for NLL, -100 =
+ * ignored row, other out-of-range labels give a NaN row loss).  Writes
+ * row_stats [rows][3] (the base-2 log-sum-exp of x and of target, the row's
+ * loss) and loss[0] = the sum of the row losses in a fixed order.
+ * KL replaces F.kl_div(F.log_softmax(x), F.softmax(target), "none").sum()
+ * (gptq_utils/g2ptq_utils.py:992-997), NLL F.cross_entropy(x, labels, "sum")
+ * (:981-985), MSE F.mse_loss(x, target, "none").mean(-1).sum() / 2
+ * (:1020-1033); computed in fp32 whatever the input dtype. */
+int g2q_block_loss_forward(int kind, float* loss, float* row_stats, const void* x,
+                           const void* target, const int64_t* labels, int dtype, int64_t ldx,
+                           int64_t ldt, int64_t rows, int64_t V, void* stream);
+
+/* The gradient of that loss with respect to x, times *grad_scale (a device
+ * float; NULL = 1), written in x's dtype with row stride ldg: KL
+ * softmax(x) - softmax(target), NLL softmax(x) - onehot(label) (0 for
+ * ignored rows), MSE (x - target) / V.  row_stats from the forward. */
+int g2q_block_loss_backward(int kind, void* grad, int64_t ldg, const float* row_stats,
+                            const void* x, const void* target, const int64_t* labels, int dtype,
+                            int64_t ldx, int64_t ldt, const float* grad_scale, int64_t rows,
+                            int64_t V, void* stream);
 
 #ifdef __cplusplus
 }

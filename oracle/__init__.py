@@ -18,4 +18,4 @@ modules and writes ``tests/golden/*.npz``); ``tests/test_oracle_golden.py``
 holds the comparison.
 """
 
-from . import quant, hessian, linalg, compensation, fasterquant, export, partition  # noqa: F401
+from . import quant, hessian, linalg, compensation, fasterquant, export, partition, refresh  # noqa: F401,E501

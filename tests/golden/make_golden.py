@@ -486,22 +486,133 @@ def gen_export(ref_root):
     save("export.npz", **{k: npy(v) for k, v in codes.items()})
     print("wrote", os.path.join(HERE, "export.json"), len(table), "tensors")
 
+# ---------------------------------------------------------------------------
+# G2PTQ refresh step: saliency / gradient caches and the block-loss heads
+# ---------------------------------------------------------------------------
+
+REFRESH_D, REFRESH_HID, REFRESH_V, REFRESH_G = 16, 32, 40, 4
+# (loss type, head, kl_topk, seed offset, retain_graph) per batch, in call order
+REFRESH_CALLS = [("block", "kl", 0, 100, True), ("topk", "kl", 8, 300, True),
+                 ("patch", "mse", 0, 200, False)]
+REFRESH_WEIGHTS = {"block": 1.0, "topk": 0.25, "patch": 0.5}
+REFRESH_BATCHES = 2
+
+
+def refresh_block(params):
+    """The two-linear block ``b(relu(a(x)))`` and the logit head of the
+    refresh fixtures, built from the arrays in ``params``."""
+    nn = torch.nn
+    a = nn.Linear(REFRESH_D, REFRESH_HID)
+    b = nn.Linear(REFRESH_HID, REFRESH_D)
+    head = nn.Linear(REFRESH_D, REFRESH_V, bias=False)
+    with torch.no_grad():
+        a.weight.copy_(torch.as_tensor(params["Wa"]))
+        a.bias.copy_(torch.as_tensor(params["ba"]))
+        b.weight.copy_(torch.as_tensor(params["Wb"]))
+        b.bias.copy_(torch.as_tensor(params["bb"]))
+        head.weight.copy_(torch.as_tensor(params["Wh"]))
+    head.weight.requires_grad_(False)
+    return a, b, head
+
+
+def gen_refresh(ref):
+    """The reference's SaliencyCache / GradientCache and its two loss
+    functions over a seeded two-linear block (g2ptq_utils.py:586-766 and
+    969-1035), replayed as in its per-layer loop (:1263-1383).  The labels,
+    top-k indices and noise each call drew are re-drawn from the same seed and
+    stored, so the oracle can replay the calls without the generator."""
+    g2 = ref.g2ptq
+    g2.offload_utils.zero_onloaded_grads = lambda: None
+    gen = torch.Generator().manual_seed(11)
+    params = {
+        "Wa": torch.randn(REFRESH_HID, REFRESH_D, generator=gen) * 0.3,
+        "ba": torch.randn(REFRESH_HID, generator=gen) * 0.1,
+        "Wb": torch.randn(REFRESH_D, REFRESH_HID, generator=gen) * 0.3,
+        "bb": torch.randn(REFRESH_D, generator=gen) * 0.1,
+        "Wh": torch.randn(REFRESH_V, REFRESH_D, generator=gen),
+    }
+    a, b, head = refresh_block(params)
+    full = {"a": a, "b": b}
+    sc = g2.SaliencyCache(["a", "b"], REFRESH_G)
+    sc.set_forward_hook(full)
+    gc = g2.GradientCache(["a", "b"], REFRESH_G)
+    gc.set_forward_hook(full)
+    out = {k: npy(v) for k, v in params.items()}
+    for j in range(REFRESH_BATCHES):
+        x = torch.randn(2, 5, REFRESH_D, generator=gen)
+        hfp = torch.randn(2, 5, REFRESH_D, generator=gen)
+        out[f"x{j}"], out[f"hfp{j}"] = npy(x), npy(hfp)
+        with torch.enable_grad():
+            h = b(torch.relu(a(x)))
+            for loss_type, kind, topk, seed, retain in REFRESH_CALLS:
+                args = types.SimpleNamespace(kl_topk=topk)
+                torch.manual_seed(seed + j)
+                if kind == "kl":
+                    logits, logits_fp = head(h), head(hfp)
+                    loss = g2.compute_kl_grad_hessian(logits, logits_fp, sc, gc, full, args,
+                                                      loss_type=loss_type,
+                                                      retain_graph=retain)
+                    lf = logits_fp.detach()
+                    if topk > 0:
+                        lf, idx = lf.topk(topk, dim=-1, sorted=False)
+                        out[f"idx{j}_{loss_type}"] = npy(idx)
+                    torch.manual_seed(seed + j)
+                    out[f"labels{j}_{loss_type}"] = npy(
+                        torch.distributions.Categorical(logits=lf).sample())
+                else:
+                    loss = g2.compute_mse_grad_hessian(h, hfp, sc, gc, full, args,
+                                                       loss_type=loss_type,
+                                                       retain_graph=retain)
+                    torch.manual_seed(seed + j)
+                    out[f"noise{j}_{loss_type}"] = npy(torch.distributions.Normal(
+                        loc=torch.zeros_like(h), scale=float(np.sqrt(REFRESH_D))).sample())
+                out[f"loss{j}_{loss_type}"] = np.float32(float(loss))
+    sc.clear_hook()
+    gc.clear_hook()
+    weights = g2.normalize_loss_weights(dict(REFRESH_WEIGHTS))
+    sc.summarize_saliency(weights)
+    gc.summarize_gradients(weights)
+    for name in ("a", "b"):
+        for j, s in enumerate(sc.saliency_cache[name]):
+            out[f"sal_{name}{j}"] = npy(s)
+        out[f"grad_{name}"] = npy(gc.gradients_cache[name])
+
+    # the two cache hooks on their own, at shapes the block does not reach
+    sc2 = g2.SaliencyCache(["s"], 3)
+    sc2.hooks_enabled = True
+    gs = torch.randn(3, 5, 12, generator=gen)
+    sc2.grad_hook(gs, name="s", loss_type="block")
+    out["sal_in"], out["sal_out"] = npy(gs), npy(sc2.saliency_cache["s"]["block"][0])
+    gc2 = g2.GradientCache(["w"], 4)
+    gc2.hooks_enabled = True
+    for i, n_tok in enumerate((10, 4, 7)):
+        gw = torch.randn(6, 7, generator=gen)
+        gc2.current_batch_tokens["w"] = n_tok
+        gc2.cache_gradient(gw, name="w", loss_type="block")
+        out[f"rm_in{i}"] = npy(gw)
+    out["rm_out"] = npy(gc2.gradients_cache["w"]["block"])
+    save("refresh.npz", **{k: np.asarray(v) for k, v in out.items()})
+
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of the reference checkout")
-    ap.add_argument("--only", default=None, help="one fixture family: export")
+    ap.add_argument("--only", default=None, help="one fixture family: export or refresh")
     args = ap.parse_args()
     torch.set_num_threads(min(8, os.cpu_count() or 1))
     ref = import_reference(os.path.abspath(args.reference))
     if args.only == "export":
         gen_export(os.path.abspath(args.reference))
         return
+    if args.only == "refresh":
+        gen_refresh(ref)
+        return
     gen_hessians(ref)
     gen_blocks(ref)
     gen_fasterquant(ref)
     gen_misc(ref)
     gen_export(os.path.abspath(args.reference))
+    gen_refresh(ref)
 
 
 if __name__ == "__main__":
