@@ -16,10 +16,19 @@ permutation, damped inverse-Cholesky, compensation, un-permutation, cast and
 NaN count).  The host reads back one small status vector per call; the
 damp auto-increment of the reference (gptq_utils.py:291-311) re-runs only
 when a layer's factorization failed.
+
+Shared folds.  Linears fed the same tensor (q/k/v of an attention block,
+gate/up of an MLP) get identical Hessians; the reference computes each one.
+GPTQ objects whose add_batch calls carry the same source tensors, in the same
+order, share one stage and one Gram fold per window (``FoldGroup``); every
+member keeps its own ``H``, refreshed by a copy after each fold, so a member
+that later receives a different input leaves the group with exactly the
+state it would have had alone.
 """
 
 import logging
 import os
+import weakref
 
 import torch
 
@@ -31,6 +40,8 @@ STAGE_TOKENS = int(os.environ.get("G2PTQ_B200_STAGE_TOKENS", "16384"))
 STAGE_BYTES = int(os.environ.get("G2PTQ_B200_STAGE_BYTES", str(512 << 20)))
 # 0 = fp32 CUDA cores, 1 = tcgen05 tensor cores (Gram products and trailing updates)
 PRECISION = int(os.environ.get("G2PTQ_B200_PRECISION", "1"))
+# objects fed the same tensors share their Gram folds (0 disables)
+SHARE_FOLDS = os.environ.get("G2PTQ_B200_SHARE_FOLDS", "1") != "0"
 
 
 class TokenStage:
@@ -276,18 +287,198 @@ def finish(layers, outs, codes, params, bits, groupsize, columns, export, rows):
         layer.weight.data.copy_(outs[b].reshape(layer.weight.shape))
 
 
+def source_key(x, samples):
+    """Identity of an add_batch input: storage address, shape, strides, dtype,
+    version counter (a write through any view bumps it) and the samples the
+    call counts.  A group holds the tensor while its key is in use, so the
+    address cannot be reused by another tensor meanwhile."""
+    return (x.data_ptr(), tuple(x.shape), tuple(x.stride()), x.dtype, x._version, samples)
+
+
+# groups that have not folded yet, by the key of their first call: a fresh
+# object whose first input has that key joins instead of starting its own
+_OPEN_GROUPS = weakref.WeakValueDictionary()
+
+
+class FoldGroup:
+    """Members ``(object, layer)`` whose add_batch calls so far carried the
+    same source tensors in the same order.
+
+    The group stages each call's tokens once (the first member to make the
+    call copies them; the others only compare keys) and folds the window into
+    the first member's statistics with that member's ``_fold``; the other
+    members copy the result and its sample count (``_copy_folded``).  A
+    member's state is its own statistics plus the window's first ``pos``
+    calls.  A window is folded only when every member has made all of its
+    calls; members that lag at that point, or whose next input differs, leave
+    with a private stage holding their part of the window.  The fold's sample
+    count is the one a lone object would use: the folded count, the window's
+    samples and, for a fold that a new call triggers, that call's samples.
+    """
+
+    def __init__(self, obj, idx, dtype, columns, device):
+        self.members = [(obj, idx)]
+        self.pos = [0]
+        self.stage = TokenStage(columns, device)
+        self.stage._ensure(dtype, False)
+        self.keys, self.srcs, self.row_ends = [], [], []
+        self.samples = 0  # samples counted by the window's calls
+        self.folded = False
+        self.first_key = None
+
+    # -- membership -------------------------------------------------------
+    def _index(self, obj, idx):
+        for k, (o, i) in enumerate(self.members):
+            if o is obj and i == idx:
+                return k
+        raise KeyError("not a member")
+
+    def can_join(self, key, dtype):
+        return (not self.folded and self.keys and self.keys[0] == key
+                and self.stage.dtype == dtype)
+
+    def join(self, obj, idx):
+        self.members.append((obj, idx))
+        self.pos.append(0)
+
+    def detach(self, obj, idx):
+        """Remove a member; its private stage receives the tokens of the
+        calls it made in this window."""
+        k = self._index(obj, idx)
+        p = self.pos.pop(k)
+        self.members.pop(k)
+        obj._groups[idx] = None
+        rows = self.row_ends[p - 1] if p else 0
+        if rows:
+            st = obj._stages[idx]
+            st._ensure(self.stage.dtype, False)
+            st.buf[:rows].copy_(self.stage.buf[:rows])
+            st.rows = rows
+        if not self.members:
+            self.close()
+
+    def dissolve(self):
+        for o, i in list(self.members):
+            self.detach(o, i)
+
+    def close(self):
+        self.stage.free()
+        self.keys, self.srcs, self.row_ends = [], [], []
+        self.samples = 0
+        self.folded = True
+
+    # -- calls ------------------------------------------------------------
+    def call(self, obj, idx, x, key, samples):
+        """Handle one add_batch call of a member (``samples`` already added to
+        its count); False when the caller must stage ``x`` itself (the member
+        has left the group)."""
+        k = self._index(obj, idx)
+        p = self.pos[k]
+        if p < len(self.keys):
+            if self.keys[p] == key:
+                self.pos[k] = p + 1
+                return True
+            self.detach(obj, idx)
+            return False
+        t = x.shape[0]
+        if stage_dtype(x) != self.stage.dtype or t > self.stage.cap():
+            self.dissolve()
+            return False
+        if self.stage.rows + t > self.stage.cap():
+            self.fold(trigger_samples=samples)
+            if obj._groups[idx] is not self:  # left while the window closed
+                return False
+        ops.stage_tokens(self.stage.buf, self.stage.rows, x)
+        self.stage.rows += t
+        self.samples += samples
+        self.keys.append(key)
+        self.srcs.append(x)
+        self.row_ends.append(self.stage.rows)
+        self.pos[self._index(obj, idx)] = len(self.keys)
+        return True
+
+    def fold(self, trigger_samples=0):
+        """Fold the window for every member that made all of its calls; the
+        others leave first with their part of it."""
+        n = len(self.keys)
+        for o, i in [m for m, p in zip(self.members, self.pos) if p < n]:
+            self.detach(o, i)
+        if not self.members or self.stage.rows == 0:
+            return
+        o0, i0 = self.members[0]
+        if len({o._n_folded[i] for o, i in self.members}) != 1:
+            self.dissolve()
+            return
+        n_new = o0._n_folded[i0] + self.samples + trigger_samples
+        o0._fold(i0, self.stage.buf[:self.stage.rows], None, None, n_new=n_new)
+        for o, i in self.members[1:]:
+            o._copy_folded(i, o0, i0)
+        self.stage.rows = 0
+        self.samples = 0
+        self.keys, self.srcs, self.row_ends = [], [], []
+        self.pos = [0] * len(self.members)
+        if not self.folded:
+            self.folded = True
+            if self.first_key is not None and _OPEN_GROUPS.get(self.first_key) is self:
+                del _OPEN_GROUPS[self.first_key]
+
+
 class StagingMixin:
     """``add_batch`` plumbing shared by the quantizer objects.
 
     Subclasses provide ``_fold(idx, X, sub, scales)``, which folds staged
     tokens into their statistics using the counts recorded so far.  Because
     every fold rescales by (counts already folded) / (counts now), any split
-    of the pending tokens into folds gives the same statistics.
+    of the pending tokens into folds gives the same statistics.  Subclasses
+    that set ``_share_folds`` and provide ``_copy_folded(idx, src, src_idx)``
+    (copy the folded statistics and counts of another object's layer) share
+    folds with objects fed the same tensors (``FoldGroup``).
     """
+
+    _share_folds = False
 
     def _init_stages(self, groups=0):
         self._stages = [TokenStage(self.columns, self.dev, groups)
                         for _ in range(self.num_layers)]
+        self._groups = [None] * self.num_layers
+        self._calls = [0] * self.num_layers
+
+    def _shared_call(self, idx, x, samples):
+        """Route an add_batch call (``samples`` already counted) through a fold
+        group; False when the tokens must go to the object's own stage."""
+        calls = self._calls[idx]
+        self._calls[idx] = calls + 1
+        if not (SHARE_FOLDS and self._share_folds):
+            return False
+        g = self._groups[idx]
+        key = source_key(x, samples)
+        if g is None:
+            if calls != 0 or self._stages[idx].rows or not self._stats_on_device():
+                return False
+            reg = (key, self.columns, self.dev)
+            g = _OPEN_GROUPS.get(reg)
+            if g is not None and g.can_join(key, stage_dtype(x)):
+                g.join(self, idx)
+            else:
+                g = FoldGroup(self, idx, stage_dtype(x), self.columns, self.dev)
+                g.first_key = reg
+                _OPEN_GROUPS[reg] = g
+            self._groups[idx] = g
+        return g.call(self, idx, x, key, samples)
+
+    def _stats_on_device(self):
+        return True
+
+    def _settle(self, idx):
+        """Called by a flush with nothing pending; subclasses whose folded
+        count can differ from the count at that point (a fold-group member
+        that left right after a fold another member's call triggered, or an
+        add_batch call without tokens) rescale their statistics to it."""
+
+    def _leave_groups(self):
+        for i, g in enumerate(getattr(self, "_groups", None) or []):
+            if g is not None:
+                g.detach(self, i)
 
     def _append(self, idx, x, sub=None, scales=None):
         st = self._stages[idx]
@@ -309,8 +500,12 @@ class StagingMixin:
             st.rows += e - s
 
     def _flush(self, idx):
+        g = self._groups[idx] if getattr(self, "_groups", None) else None
+        if g is not None:
+            g.fold()  # this member, if it lags, leaves with its calls staged privately
         st = self._stages[idx]
         if st.rows == 0:
+            self._settle(idx)
             return
         self._fold(idx, st.buf[:st.rows],
                    None if st.sub_buf is None else st.sub_buf[:st.rows],

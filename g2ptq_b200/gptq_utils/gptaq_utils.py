@@ -98,6 +98,15 @@ class GPTAQ(_engine.StagingMixin):
         self._append(idx, x, sub=fp)
         del self.fp_inp[idx][0]
 
+    def _settle(self, idx):
+        """An add_batch call without tokens still rescales by n / (n + b)."""
+        n, nf = self._n[idx], self._n_folded[idx]
+        if n != nf and n > 0:
+            self._require_device_stats(self._H)
+            self._H[idx] *= nf / n
+            self._dXXT[idx] *= nf / n
+            self._n_folded[idx] = n
+
     def _fold(self, idx, X, diff, scales):
         n_old, n_new = self._n_folded[idx], self._n[idx]
         self._require_device_stats(self._H)

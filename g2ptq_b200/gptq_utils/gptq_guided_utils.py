@@ -17,6 +17,10 @@ from .gptq_utils import GPTQ, _onload
 
 class GPTQGuided(GPTQ):
     index = _engine.lazy_counter("index")
+    # per-linear saliency weights: no two objects share a fold, and H is a
+    # plain sum (nothing to renormalize)
+    _share_folds = False
+    _settle = _engine.StagingMixin._settle
 
     def __init__(self, layers, saliencies, num_groups: int, offload_hessians: bool = False):
         self.layers = layers

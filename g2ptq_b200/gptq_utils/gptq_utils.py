@@ -41,6 +41,7 @@ def run_eager(weight, hinv, scale, zero, maxq, backend="torch", int_weight=None,
 
 class GPTQ(_engine.StagingMixin):
     nsamples = _engine.lazy_counter("nsamples")
+    _share_folds = True  # linears fed the same tensor share their Gram folds
 
     def __init__(self, layers, offload_hessians: bool = False):
         self.layers = layers
@@ -67,7 +68,25 @@ class GPTQ(_engine.StagingMixin):
 
     @H.setter
     def H(self, value):
+        if value is not self._H:
+            self._leave_groups()
         self._H = value
+
+    def _stats_on_device(self):
+        return self._H is not None and self._H.device.type == "cuda"
+
+    def _copy_folded(self, idx, src, src_idx):
+        """Take the folded Hessian and its sample count from ``src``'s layer
+        ``src_idx`` (a fold-group member with the same calls)."""
+        self._H[idx].copy_(src._H[src_idx])
+        self._n_folded[idx] = src._n_folded[src_idx]
+
+    def _settle(self, idx):
+        n, nf = self._n[idx], self._n_folded[idx]
+        if n != nf and n > 0:
+            self._require_device_stats(self._H)
+            self._H[idx] *= nf / n
+            self._n_folded[idx] = n
 
     def _maybe_onload_hessian(self, idx=None):
         """Onload the Hessian for the duration of the context (gptq_utils.py:109-113)."""
@@ -82,10 +101,13 @@ class GPTQ(_engine.StagingMixin):
         tmp = inp.shape[0]
         self._n[idx] += tmp
         _engine.bump(self, "nsamples", idx, tmp)
-        self._append(idx, _engine.as_rows(inp, self.columns))
+        x = _engine.as_rows(inp, self.columns)
+        if not self._shared_call(idx, x, tmp):
+            self._append(idx, x)
 
-    def _fold(self, idx, X, sub, scales):
-        n_old, n_new = self._n_folded[idx], self._n[idx]
+    def _fold(self, idx, X, sub, scales, n_new=None):
+        n_old = self._n_folded[idx]
+        n_new = self._n[idx] if n_new is None else n_new
         self._require_device_stats(self._H)
         ops.gram_update(self._H[idx], X, alpha=n_old / n_new, beta=2.0 / n_new,
                         precision=_engine.PRECISION)
@@ -145,6 +167,7 @@ class GPTQ(_engine.StagingMixin):
                                groupsize, C, R, export_compressed_tensors, dynamic, actorder)
 
     def free(self):
+        self._leave_groups()
         self._H = None
         self.Losses = None
         self.nsamples = None

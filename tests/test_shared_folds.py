@@ -1,0 +1,246 @@
+"""Shared Gram folds of quantizer objects fed the same tensors (FoldGroup).
+
+CPU tests drive the staging mixin with a float64 stand-in object (stage copy
+and fold done by torch on the CPU) and compare every call pattern with the
+same calls made with sharing off: identical Hessians, fewer folds.  The GPU
+test compares real GPTQ objects with and without sharing (bit-identical).
+"""
+
+import pytest
+import torch
+
+from g2ptq_b200 import ops
+from g2ptq_b200.gptq_utils import _engine
+
+
+class FakeObj(_engine.StagingMixin):
+    """One-layer object with the GPTQ fold rule ``H <- H n_old/n_new +
+    (2/n_new) X^T X`` in float64 on the CPU."""
+
+    _share_folds = True
+
+    def __init__(self, C):
+        self.columns, self.dev, self.num_layers = C, torch.device("cpu"), 1
+        self._H = torch.zeros(1, C, C, dtype=torch.float64)
+        self._n, self._n_folded = [0], [0]
+        self._init_stages()
+        self.folds = 0
+
+    def add_batch(self, idx, inp):
+        if inp.dim() == 2:
+            inp = inp.unsqueeze(0)
+        self._n[idx] += inp.shape[0]
+        x = _engine.as_rows(inp, self.columns)
+        if not self._shared_call(idx, x, inp.shape[0]):
+            self._append(idx, x)
+
+    def _fold(self, idx, X, sub, scales, n_new=None):
+        n_old = self._n_folded[idx]
+        n_new = self._n[idx] if n_new is None else n_new
+        X = X.double()
+        self._H[idx] = self._H[idx] * (n_old / n_new) + (2.0 / n_new) * (X.T @ X)
+        self._n_folded[idx] = n_new
+        self.folds += 1
+
+    def _copy_folded(self, idx, src, src_idx):
+        self._H[idx].copy_(src._H[src_idx])
+        self._n_folded[idx] = src._n_folded[src_idx]
+
+    def _settle(self, idx):
+        n, nf = self._n[idx], self._n_folded[idx]
+        if n != nf and n > 0:
+            self._H[idx] *= nf / n
+            self._n_folded[idx] = n
+
+    def H(self):
+        self._flush_all()
+        return self._H[0]
+
+
+@pytest.fixture
+def cpu_staging(monkeypatch):
+    def stage_tokens(buf, row0, x, sub=None):
+        buf[row0:row0 + x.shape[0]].copy_(x)
+    monkeypatch.setattr(ops, "stage_tokens", stage_tokens)
+    monkeypatch.setattr(_engine, "STAGE_TOKENS", 8)   # small windows: many folds
+
+
+def run(pattern, share, monkeypatch, C=6):
+    """``pattern``: list of (object index, tensor) calls; returns the
+    objects' Hessians (after a flush of each) and the total number of folds."""
+    monkeypatch.setattr(_engine, "SHARE_FOLDS", share)
+    n_obj = 1 + max(i for i, _ in pattern)
+    objs = [FakeObj(C) for _ in range(n_obj)]
+    for i, x in pattern:
+        objs[i].add_batch(0, x)
+    Hs = [o.H().clone() for o in objs]
+    return Hs, sum(o.folds for o in objs)
+
+
+def inputs(n, C=6, T=2, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    return [torch.randn(1, T, C, generator=g) for _ in range(n)]
+
+
+def check(pattern, monkeypatch):
+    H1, f1 = run(pattern, True, monkeypatch)
+    H0, f0 = run(pattern, False, monkeypatch)
+    for a, b in zip(H1, H0):
+        assert torch.allclose(a, b, rtol=1e-12, atol=1e-12)
+    return f1, f0
+
+
+def test_lockstep_objects_fold_once(cpu_staging, monkeypatch):
+    xs = inputs(9)
+    pattern = [(o, x) for x in xs for o in range(3)]        # q, k, v per sample
+    f1, f0 = check(pattern, monkeypatch)
+    assert f1 * 3 == f0
+
+
+def test_two_groups_side_by_side(cpu_staging, monkeypatch):
+    a, b = inputs(7, seed=1), inputs(7, seed=2)
+    pattern = []
+    for xa, xb in zip(a, b):
+        pattern += [(0, xa), (1, xa), (2, xb), (3, xb), (4, xa)]
+    f1, f0 = check(pattern, monkeypatch)
+    assert f1 * 5 == f0 * 2
+
+
+def test_member_diverges_mid_window(cpu_staging, monkeypatch):
+    xs, other = inputs(6), inputs(3, seed=5)
+    pattern = [(o, x) for x in xs[:2] for o in range(3)]
+    pattern += [(0, xs[2]), (1, other[0]), (2, xs[2])]
+    pattern += [(o, x) for x in xs[3:] for o in (0, 2)] + [(1, other[1]), (1, other[2])]
+    check(pattern, monkeypatch)
+
+
+def test_member_lags_across_windows(cpu_staging, monkeypatch):
+    xs = inputs(12)
+    pattern = [(0, x) for x in xs[:6]] + [(1, x) for x in xs[:3]] + [(0, x) for x in xs[6:]]
+    pattern += [(1, x) for x in xs[3:]]
+    check(pattern, monkeypatch)
+
+
+def test_flush_of_a_lagging_member(cpu_staging, monkeypatch):
+    monkeypatch.setattr(_engine, "SHARE_FOLDS", True)
+    xs = inputs(5)
+    a, b = FakeObj(6), FakeObj(6)
+    for x in xs[:3]:
+        a.add_batch(0, x)
+        b.add_batch(0, x)
+    a.add_batch(0, xs[3])
+    Hb = b.H().clone()                         # b lags a by one call, then reads H
+    for x in xs[3:]:
+        b.add_batch(0, x)
+    a.add_batch(0, xs[4])
+    monkeypatch.setattr(_engine, "SHARE_FOLDS", False)
+    ref = FakeObj(6)
+    for x in xs[:3]:
+        ref.add_batch(0, x)
+    assert torch.allclose(Hb, ref.H(), rtol=1e-12, atol=1e-12)
+    for x in xs[3:]:
+        ref.add_batch(0, x)
+    assert torch.allclose(a.H(), ref.H(), rtol=1e-12, atol=1e-12)
+    assert torch.allclose(b.H(), ref.H(), rtol=1e-12, atol=1e-12)
+
+
+def test_in_place_write_between_calls_is_not_shared(cpu_staging, monkeypatch):
+    monkeypatch.setattr(_engine, "SHARE_FOLDS", True)
+    x = inputs(1)[0]
+    a, b = FakeObj(6), FakeObj(6)
+    a.add_batch(0, x)
+    x.mul_(2.0)                                 # bumps the version counter
+    b.add_batch(0, x)
+    assert torch.allclose(b.H(), 2.0 * x[0].double().T @ x[0].double())
+    assert not torch.allclose(a.H(), b.H())
+
+
+def test_same_storage_different_sample_count_is_not_folded_together(cpu_staging, monkeypatch):
+    x = inputs(1, T=4)[0]
+    pattern = [(0, x), (1, x.reshape(2, 2, 6)), (0, x), (1, x.reshape(2, 2, 6))]
+    check(pattern, monkeypatch)
+
+
+def test_late_object_does_not_join_a_folded_group(cpu_staging, monkeypatch):
+    xs = inputs(10)
+    pattern = [(0, x) for x in xs] + [(1, x) for x in xs]
+    f1, f0 = check(pattern, monkeypatch)
+    assert f1 == f0
+
+
+@pytest.mark.gpu
+def test_shared_folds_bit_identical_on_gpu(monkeypatch):
+    """q/k/v-style objects fed one tensor: Hessians and quantized weights
+    bit-identical with and without sharing."""
+    from g2ptq_b200.gptq_utils import gptq_utils, common_utils
+    from g2ptq_b200.utils.quant_utils import WeightQuantizer
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(3)
+    C, seqs = 512, 12
+    X = torch.randn(seqs, 2048, C, device=dev, generator=g).to(torch.bfloat16)
+    Ws = [torch.randn(r, C, device=dev, generator=g) * 0.02 for r in (512, 128, 128)]
+
+    def build(share):
+        monkeypatch.setattr(_engine, "SHARE_FOLDS", share)
+        objs = []
+        for W in Ws:
+            lin = torch.nn.Linear(C, W.shape[0], bias=False, device=dev)
+            lin.weight.data = W.clone()
+            o = gptq_utils.GPTQ([lin])
+            q = WeightQuantizer()
+            q.configure(4, perchannel=True, sym=True)
+            o.quantizer = common_utils.make_group_quantizers(q, C, 128)
+            objs.append(o)
+        for s in range(seqs):
+            xs = X[s:s + 1]
+            for o in objs:
+                o.add_batch(0, xs, None)
+        Hs = [o.H.clone() for o in objs]
+        for o in objs:
+            o.fasterquant(blocksize=128, percdamp=0.01, groupsize=128, actorder=True,
+                          static_groups=True)
+        return Hs, [o.layers[0].weight.data.clone() for o in objs]
+
+    H1, Q1 = build(True)
+    H0, Q0 = build(False)
+    for a, b in zip(H1 + Q1, H0 + Q0):
+        assert torch.equal(a, b)
+
+
+def test_member_left_behind_by_a_triggered_fold(cpu_staging, monkeypatch):
+    """a's fifth call folds the full window (its count includes that call);
+    b, one call behind, reads H at once: it leaves with nothing pending and
+    rescales to its own count."""
+    monkeypatch.setattr(_engine, "SHARE_FOLDS", True)
+    xs = inputs(6)
+    a, b = FakeObj(6), FakeObj(6)
+    for x in xs[:4]:
+        a.add_batch(0, x)
+        b.add_batch(0, x)
+    a.add_batch(0, xs[4])
+    Hb = b.H().clone()
+    b.add_batch(0, xs[5])
+    monkeypatch.setattr(_engine, "SHARE_FOLDS", False)
+    r4, r5 = FakeObj(6), FakeObj(6)
+    for x in xs[:4]:
+        r4.add_batch(0, x)
+    for x in xs[:5]:
+        r5.add_batch(0, x)
+    rb = FakeObj(6)
+    for x in xs[:4] + [xs[5]]:
+        rb.add_batch(0, x)
+    assert torch.allclose(Hb, r4.H(), rtol=1e-12, atol=1e-12)
+    assert torch.allclose(a.H(), r5.H(), rtol=1e-12, atol=1e-12)
+    assert torch.allclose(b.H(), rb.H(), rtol=1e-12, atol=1e-12)
+
+
+def test_call_without_tokens_rescales_like_the_reference(cpu_staging, monkeypatch):
+    """gptq_utils.py:119-126 with an empty input: H <- H n/(n+1), nothing added."""
+    monkeypatch.setattr(_engine, "SHARE_FOLDS", False)
+    x = inputs(1)[0]
+    o = FakeObj(6)
+    o.add_batch(0, x)
+    H1 = o.H().clone()
+    o.add_batch(0, torch.zeros(1, 0, 6))
+    assert torch.allclose(o.H(), H1 / 2, rtol=1e-12, atol=1e-12)
