@@ -414,7 +414,8 @@ class FoldGroup:
         for o, i in self.members[1:]:
             o._copy_folded(i, o0, i0)
         self.stage.rows = 0
-        self.samples = 0
+        # the triggering call is staged next, but its samples are in n_new
+        self.samples = -trigger_samples
         self.keys, self.srcs, self.row_ends = [], [], []
         self.pos = [0] * len(self.members)
         if not self.folded:

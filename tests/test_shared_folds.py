@@ -25,6 +25,8 @@ class FakeObj(_engine.StagingMixin):
         self._n, self._n_folded = [0], [0]
         self._init_stages()
         self.folds = 0
+        self.fold_counts = []   # (n_old, n_new) of every fold this object made
+        self.rescales = 0
 
     def add_batch(self, idx, inp):
         if inp.dim() == 2:
@@ -41,6 +43,7 @@ class FakeObj(_engine.StagingMixin):
         self._H[idx] = self._H[idx] * (n_old / n_new) + (2.0 / n_new) * (X.T @ X)
         self._n_folded[idx] = n_new
         self.folds += 1
+        self.fold_counts.append((n_old, n_new))
 
     def _copy_folded(self, idx, src, src_idx):
         self._H[idx].copy_(src._H[src_idx])
@@ -51,6 +54,7 @@ class FakeObj(_engine.StagingMixin):
         if n != nf and n > 0:
             self._H[idx] *= nf / n
             self._n_folded[idx] = n
+            self.rescales += 1
 
     def H(self):
         self._flush_all()
@@ -74,6 +78,7 @@ def run(pattern, share, monkeypatch, C=6):
     for i, x in pattern:
         objs[i].add_batch(0, x)
     Hs = [o.H().clone() for o in objs]
+    run.objs = objs
     return Hs, sum(o.folds for o in objs)
 
 
@@ -91,10 +96,19 @@ def check(pattern, monkeypatch):
 
 
 def test_lockstep_objects_fold_once(cpu_staging, monkeypatch):
+    """Same Hessians with a third of the folds, and the folds use the sample
+    counts a lone object uses (so the GPU results are bit-identical)."""
     xs = inputs(9)
     pattern = [(o, x) for x in xs for o in range(3)]        # q, k, v per sample
-    f1, f0 = check(pattern, monkeypatch)
+    _, f1 = run(pattern, True, monkeypatch)
+    shared = run.objs
+    _, f0 = run(pattern, False, monkeypatch)
+    alone = run.objs
     assert f1 * 3 == f0
+    assert shared[0].fold_counts == alone[0].fold_counts == [(0, 5), (5, 9), (9, 9)][:len(
+        alone[0].fold_counts)]
+    for a, b in zip(shared, alone):
+        assert torch.equal(a._H, b._H) and a.rescales == 0 and a._n_folded == b._n_folded
 
 
 def test_two_groups_side_by_side(cpu_staging, monkeypatch):
