@@ -209,6 +209,8 @@ def reduce_to_target_rank(gptqs, gptq2rank):
     for gptq in gptqs:
         with gptq._maybe_onload_hessian():
             H = gptq.H
+            # the reduced Hessian no longer follows a fold group's
+            gptq._leave_groups()
             pending = []
             target = gptq2rank[gptq]
             global_n = gptq.nsamples.clone()
