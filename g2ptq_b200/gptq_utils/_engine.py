@@ -537,18 +537,24 @@ class Pending:
     """
 
     def __init__(self, layers, nl, H, U, info, damps, params, run, W0, bits, groupsize,
-                 columns, rows, export, dynamic, actorder):
+                 columns, rows, export, dynamic, actorder, borrowed_factor=False):
         self.layers, self.nl, self.H, self.U, self.info = layers, nl, H, U, info
         self.damps, self.params, self.run, self.W0 = damps, params, run, W0
         self.bits, self.groupsize, self.columns, self.rows = bits, groupsize, columns, rows
         self.export, self.dynamic, self.actorder = export, dynamic, actorder
+        # U, info and damps belong to another object's launch (shared factor),
+        # which finishes first and re-factors U in place if it must
+        self.borrowed_factor = borrowed_factor
         self.nan, self.outs, self.codes = run(W0.clone())
 
     def finish(self):
         nl = self.nl
         flags = sync_check(self.info, self.nan, *self.params.statuses())
         if any(i != 0 for i in flags[:nl]):
-            retry_failed(self.H, self.U, flags[:nl], self.damps)
+            if self.borrowed_factor:
+                torch.cuda.synchronize(self.U.device)  # the owner's re-factored U
+            else:
+                retry_failed(self.H, self.U, flags[:nl], self.damps)
             self.params.status.zero_()
             self.nan, self.outs, self.codes = self.run(self.W0.clone())
             flags = sync_check(self.info, self.nan, *self.params.statuses())
@@ -567,6 +573,35 @@ class Pending:
 
 
 _STREAMS = {}
+
+
+def factor_roles(objs):
+    """Which of ``objs`` (in launch order) can share a damped inverse-Cholesky
+    factor: one-layer objects that offer it (``_share_factor``), are still
+    members of the same fold group and whose Hessian was never handed out
+    through the public ``H`` property hold bit-identical Hessians (copies of
+    one fold), hence identical factors.  Returns ``{position: ("factor_out" |
+    "factor_in", slot)}``: the first of each group computes the factor and
+    fills the slot, the others take it from there."""
+    slots, roles = {}, {}
+    for n, o in enumerate(objs):
+        if not (SHARE_FOLDS and getattr(o, "_share_factor", False) and o.num_layers == 1):
+            continue
+        groups = getattr(o, "_groups", None)
+        g = groups[0] if groups else None
+        if g is None or getattr(o, "_h_exposed", False):
+            continue
+        if id(g) in slots:
+            roles[n] = ("factor_in", slots[id(g)])
+        else:
+            slots[id(g)] = {"group": g}
+            roles[n] = ("factor_out", slots[id(g)])
+    # a group with a single eligible member has nothing to share
+    owners = [n for n, (r, sl) in roles.items() if r == "factor_out"
+              and not any(r2 == "factor_in" and sl2 is sl for r2, sl2 in roles.values())]
+    for n in owners:
+        del roles[n]
+    return roles
 
 
 def stream_pool(device, n=4):
@@ -597,6 +632,7 @@ def fasterquant_all(objs, streams=4, **kwargs):
     for o in objs:
         if not getattr(o, "offload_hessians", False):
             o._flush_all()
+    roles = factor_roles([objs[i] for i in order])
     # The longest chain takes the high-priority stream, so that its kernels go
     # first whenever SMs free up; the shorter chains fill the gaps.
     launched = []
@@ -604,8 +640,11 @@ def fasterquant_all(objs, streams=4, **kwargs):
         o = objs[i]
         s = pool[0] if n == 0 else pool[1 + (n - 1) % (len(pool) - 1)]
         s.wait_stream(cur)
+        extra = {}
+        if n in roles:
+            extra = {roles[n][0]: roles[n][1]}
         with torch.cuda.stream(s):
-            launched.append((s, o, o._fq_launch(**kwargs)))
+            launched.append((s, o, o._fq_launch(**kwargs, **extra)))
     for s, o, pending in launched:
         with torch.cuda.stream(s):
             o._last_damps = pending.finish()

@@ -20,6 +20,7 @@ class GPTQGuided(GPTQ):
     # per-linear saliency weights: no two objects share a fold, and H is a
     # plain sum (nothing to renormalize)
     _share_folds = False
+    _share_factor = False
     _settle = _engine.StagingMixin._settle
 
     def __init__(self, layers, saliencies, num_groups: int, offload_hessians: bool = False):

@@ -42,6 +42,8 @@ def run_eager(weight, hinv, scale, zero, maxq, backend="torch", int_weight=None,
 class GPTQ(_engine.StagingMixin):
     nsamples = _engine.lazy_counter("nsamples")
     _share_folds = True  # linears fed the same tensor share their Gram folds
+    _share_factor = True  # ... and, in fasterquant_all, their Cholesky factor
+    _h_exposed = False  # H was handed out through the public property
 
     def __init__(self, layers, offload_hessians: bool = False):
         self.layers = layers
@@ -63,6 +65,11 @@ class GPTQ(_engine.StagingMixin):
     # -- Hessian ----------------------------------------------------------
     @property
     def H(self):
+        self._flush_all()
+        self._h_exposed = True  # the caller may change it: no shared factor
+        return self._H
+
+    def _hessian(self):
         self._flush_all()
         return self._H
 
@@ -125,12 +132,17 @@ class GPTQ(_engine.StagingMixin):
 
     def _fq_launch(self, blocksize=128, percdamp=0.01, groupsize=-1, actorder=False,
                    static_groups=False, export_compressed_tensors=False, backend="torch",
-                   graph=False):
-        """Enqueue the whole of fasterquant on the current stream (no host sync)."""
+                   graph=False, factor_out=None, factor_in=None):
+        """Enqueue the whole of fasterquant on the current stream (no host sync).
+
+        ``factor_out`` / ``factor_in``: a slot through which objects with
+        bit-identical Hessians (``_engine.factor_roles``) share one damped
+        inverse-Cholesky factor; the owner fills it, the others wait for its
+        event and take U, the status word and the damps from it."""
         B, R, C = self.num_layers, self.rows, self.columns
         q0 = self.quantizer[0]
         with self._maybe_onload_hessian():
-            H = self.H
+            H = self._hessian()
             self.H = None
         H_diag = _engine.hessian_diag(H, q0)
         W = torch.stack([l.weight.data for l in self.layers]).float().contiguous()
@@ -146,7 +158,18 @@ class GPTQ(_engine.StagingMixin):
             H = ops.permute_sym(H, perm)
         clip, clip_hd = _engine.dynamic_clip(q0, H_diag, perm, B * R, C) if dynamic else (None,
                                                                                           None)
-        U, info, damps = _engine.factor_with_retry(H, percdamp)
+        if factor_in is not None:
+            stream = torch.cuda.current_stream(self.dev)
+            stream.wait_event(factor_in["event"])
+            U, info, damps = factor_in["U"], factor_in["info"], factor_in["damps"]
+            U.record_stream(stream)
+            info.record_stream(stream)
+        else:
+            U, info, damps = _engine.factor_with_retry(H, percdamp)
+            if factor_out is not None:
+                ev = torch.cuda.Event()
+                ev.record(torch.cuda.current_stream(self.dev))
+                factor_out.update(U=U, info=info, damps=damps, event=ev)
         colgroup = params.colgroup(perm, static_groups, self.dev)
         codes = torch.empty(B, R, C, dtype=torch.int8, device=self.dev)
 
@@ -164,7 +187,8 @@ class GPTQ(_engine.StagingMixin):
             return nan, outs, cq
 
         return _engine.Pending(self.layers, B, H, U, info, damps, params, run, W, q0.bits,
-                               groupsize, C, R, export_compressed_tensors, dynamic, actorder)
+                               groupsize, C, R, export_compressed_tensors, dynamic, actorder,
+                               borrowed_factor=factor_in is not None)
 
     def free(self):
         self._leave_groups()

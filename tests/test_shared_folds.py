@@ -258,3 +258,79 @@ def test_call_without_tokens_rescales_like_the_reference(cpu_staging, monkeypatc
     H1 = o.H().clone()
     o.add_batch(0, torch.zeros(1, 0, 6))
     assert torch.allclose(o.H(), H1 / 2, rtol=1e-12, atol=1e-12)
+
+
+class _RoleObj:
+    _share_factor = True
+
+    def __init__(self, group, exposed=False, layers=1):
+        self._groups = [group] * layers
+        self._h_exposed = exposed
+        self.num_layers = layers
+
+
+def test_factor_roles(monkeypatch):
+    """One owner per fold group; members whose H was handed out, groupless or
+    multi-layer objects, and groups with one eligible member share nothing."""
+    monkeypatch.setattr(_engine, "SHARE_FOLDS", True)
+    g1, g2, g3 = object(), object(), object()
+    objs = [_RoleObj(None), _RoleObj(g1), _RoleObj(g2), _RoleObj(g1), _RoleObj(g1, exposed=True),
+            _RoleObj(g3), _RoleObj(g2, layers=2), _RoleObj(g1)]
+    roles = _engine.factor_roles(objs)
+    assert sorted(roles) == [1, 3, 7]
+    assert roles[1][0] == "factor_out" and roles[3][0] == roles[7][0] == "factor_in"
+    assert roles[1][1] is roles[3][1] is roles[7][1]
+    monkeypatch.setattr(_engine, "SHARE_FOLDS", False)
+    assert _engine.factor_roles(objs) == {}
+
+
+@pytest.mark.gpu
+def test_shared_factor_in_fasterquant_all(monkeypatch):
+    """fasterquant_all over q/k/v-style objects fed one tensor factors their
+    (bit-identical) Hessian once; quantized weights and export buffers are
+    bit-identical to the run without sharing, which factors it three times."""
+    from g2ptq_b200.gptq_utils import gptq_utils, common_utils
+    from g2ptq_b200.utils.quant_utils import WeightQuantizer
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(4)
+    C, seqs = 512, 10
+    X = torch.randn(seqs, 2048, C, device=dev, generator=g).to(torch.bfloat16)
+    Ws = [torch.randn(r, C, device=dev, generator=g) * 0.02 for r in (512, 128, 128, 256)]
+    calls = []
+    chol = ops.chol_upper_inverse
+
+    def counting(*a, **k):
+        calls.append(1)
+        return chol(*a, **k)
+    monkeypatch.setattr(ops, "chol_upper_inverse", counting)
+
+    def build(share):
+        monkeypatch.setattr(_engine, "SHARE_FOLDS", share)
+        objs = []
+        for W in Ws:
+            lin = torch.nn.Linear(C, W.shape[0], bias=False, device=dev)
+            lin.weight.data = W.clone()
+            o = gptq_utils.GPTQ([lin])
+            q = WeightQuantizer()
+            q.configure(4, perchannel=True, sym=True)
+            o.quantizer = common_utils.make_group_quantizers(q, C, 128)
+            objs.append(o)
+        for s in range(seqs):
+            xs = X[s:s + 1]
+            for o in objs[:3]:
+                o.add_batch(0, xs, None)
+            objs[3].add_batch(0, xs.float() * 0.5, None)   # its own input
+        calls.clear()
+        gptq_utils.fasterquant_all(objs, blocksize=128, percdamp=0.01, groupsize=128,
+                                   actorder=True, static_groups=True,
+                                   export_compressed_tensors=True)
+        torch.cuda.synchronize()
+        return len(calls), [(o.layers[0].weight.data.clone(),
+                             o.layers[0]._export_qparams["weight_packed"].clone()) for o in objs]
+
+    n1, out1 = build(True)
+    n0, out0 = build(False)
+    assert (n1, n0) == (2, 4)
+    for (w1, p1), (w0, p0) in zip(out1, out0):
+        assert torch.equal(w1, w0) and torch.equal(p1, p0)
