@@ -61,16 +61,7 @@ __global__ void reverse_damp_kernel(const float* H, long long C, long long ldh,
   }
 }
 
-static dim3 grid_rows2(long long rows, long long cols) {
-  long long gx = (cols + 255) / 256;
-  if (gx > 64) gx = 64;
-  if (gx < 1) gx = 1;
-  // one wave of eight 256-thread CTAs per SM; the kernels loop over the rest
-  long long gy = (148 * 8 + gx - 1) / gx;
-  if (gy > rows) gy = rows;
-  if (gy < 1) gy = 1;
-  return dim3((unsigned)gx, (unsigned)gy);
-}
+static dim3 grid_rows2(long long rows, long long cols) { return wave_grid_2d(rows, cols); }
 
 // Factor the nb x nb diagonal block at (k0, k0) of A in place and write its
 // lower-triangular inverse to Linv (NB x NB, zero padded).

@@ -813,11 +813,7 @@ extern "C" int g2q_compensate(int method, float* W, int64_t nl, int64_t rows, in
     if (i2 >= C) break;
     const long long N = C - i2;
     if (method == G2Q_METHOD_G2PTQ) {
-      long long gx = (N + 255) / 256;
-      if (gx > 64) gx = 64;
-      long long gy = (148 * 8 + gx - 1) / gx;  // one wave of eight CTAs per SM
-      if (gy > nl * rows) gy = nl * rows;
-      const dim3 grid((unsigned)gx, (unsigned)gy);
+      const dim3 grid = wave_grid_2d(nl * rows, N);
       sub_scaled_kernel<<<grid, 256, 0, st>>>(W, gh, nl * rows, C, i2, (float)blocksize);
       G2Q_CHECK_LAUNCH();
     }

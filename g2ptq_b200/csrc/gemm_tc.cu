@@ -1147,11 +1147,7 @@ static int split_rows(const void* X, int dtype, long long ldx, long long T, long
                       const float* s, long long sstride, __nv_bfloat16* hi, __nv_bfloat16* lo,
                       long long ldo, cudaStream_t st) {
   if (T * C == 0) return G2Q_OK;
-  long long gx = (C + 255) / 256;
-  if (gx > 64) gx = 64;
-  long long gy = (148 * 8 + gx - 1) / gx;  // one wave of eight CTAs per SM
-  if (gy > T) gy = T;
-  const dim3 grid((unsigned)gx, (unsigned)gy);
+  const dim3 grid = wave_grid_2d(T, C);
   if (dtype == G2Q_DTYPE_BF16)
     split_rows_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
         (const __nv_bfloat16*)X, ldx, T, C, s, sstride, hi, lo, ldo);
@@ -1348,10 +1344,7 @@ int tc_gram_grouped(float* D, long long ldd, long long d_gstride, long long C, c
     __nv_bfloat16* hi = take((long long)G * T * w);
     __nv_bfloat16* lo = take((long long)G * T * w);
     const long long nv = C / 8;
-    const long long gxv = cdiv(nv, 256) < 64 ? cdiv(nv, 256) : 64;
-    long long gyv = (148 * 8 + gxv - 1) / gxv;  // one wave of eight CTAs per SM
-    if (gyv > T) gyv = T;
-    dim3 grid((unsigned)gxv, (unsigned)gyv);
+    const dim3 grid = wave_grid_2d(T, nv);
     tc::split_rows_groups_kernel<<<grid, 256, 0, st>>>((const __nv_bfloat16*)X, ldx, T, C, s,
                                                        sstride, G, hi, lo, w, T * w);
     G2Q_CHECK_LAUNCH();

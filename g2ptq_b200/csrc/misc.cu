@@ -192,17 +192,7 @@ __global__ void permute_sym_kernel(float* dst, const float* src, long long nl, l
   }
 }
 
-// 2-D grid for a rows x cols elementwise kernel with 256 threads along a row
-static dim3 grid_rows(long long rows, long long cols) {
-  long long gx = (cols + 255) / 256;
-  if (gx > 64) gx = 64;
-  if (gx < 1) gx = 1;
-  // one wave of eight 256-thread CTAs per SM; the kernels loop over the rest
-  long long gy = (148 * 8 + gx - 1) / gx;
-  if (gy > rows) gy = rows;
-  if (gy < 1) gy = 1;
-  return dim3((unsigned)gx, (unsigned)gy);
-}
+static dim3 grid_rows(long long rows, long long cols) { return wave_grid_2d(rows, cols); }
 
 template <typename D>
 __global__ void cast_check_kernel(D* dst, const float* src, long long n, int* nan_count) {
