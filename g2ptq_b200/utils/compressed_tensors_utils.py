@@ -68,6 +68,53 @@ def register_qparam_buffers(modules):
             module.register_buffer(name, tensor)
 
 
+def _expert_stack(experts, n, part, attr, dim0_pair=None):
+    """``[n, ...]`` stack of ``experts[i].<part>.<attr>``; with ``dim0_pair`` the
+    per-expert entry is that part's tensor followed (along dim 0) by the same
+    attribute of the ``dim0_pair`` part."""
+    rows = []
+    for i in range(n):
+        t = getattr(getattr(experts[i], part), attr)
+        if dim0_pair is not None:
+            t = torch.cat([t, getattr(getattr(experts[i], dim0_pair), attr)], dim=0)
+        rows.append(t)
+    return torch.nn.Parameter(torch.stack(rows, dim=0), requires_grad=False)
+
+
+def stack_experts(experts, weight_packed=False):
+    """MoE expert stacking before export (utils/models/mixins.py:93-144,
+    ``MoEMixin.stack_experts``): the per-expert ``gate_proj`` / ``up_proj`` /
+    ``down_proj`` linears of an experts container (``num_experts``, indexable,
+    submodules named ``"0"``, ``"1"``, ...) become 3-D parameters, the layout
+    the exported checkpoint stores for fused experts:
+
+    * ``weight_packed=True``: ``gate_up_proj_packed`` / ``gate_up_proj_scale``
+      ``[E, 2I, .]`` (gate rows, then up rows), ``down_proj_packed`` /
+      ``down_proj_scale`` ``[E, H, .]`` and the int64 shape tensors
+      ``gate_up_proj_shape = (E, 2I, H)``, ``down_proj_shape = (E, H, I)``;
+    * else ``gate_up_proj`` ``[E, 2I, H]`` and ``down_proj`` ``[E, H, I]``.
+
+    The per-expert submodules are removed.  The container is then meant for
+    saving: its forward is left as it was (it indexed the removed submodules).
+    """
+    n = experts.num_experts
+    if weight_packed:
+        experts.gate_up_proj_packed = _expert_stack(experts, n, "gate_proj", "weight_packed",
+                                                    "up_proj")
+        experts.down_proj_packed = _expert_stack(experts, n, "down_proj", "weight_packed")
+        experts.gate_up_proj_scale = _expert_stack(experts, n, "gate_proj", "weight_scale",
+                                                   "up_proj")
+        experts.down_proj_scale = _expert_stack(experts, n, "down_proj", "weight_scale")
+        inter, hidden = (int(v) for v in experts[0].gate_proj.weight_shape[:2])
+        experts.gate_up_proj_shape = torch.tensor((n, 2 * inter, hidden))
+        experts.down_proj_shape = torch.tensor((n, hidden, inter))
+    else:
+        experts.gate_up_proj = _expert_stack(experts, n, "gate_proj", "weight", "up_proj")
+        experts.down_proj = _expert_stack(experts, n, "down_proj", "weight")
+    for i in range(n):
+        del experts._modules[str(i)]
+
+
 def expand_ignore_list(ignore_list, merge_patterns=None):
     """compressed_tensors_utils.py:56-80: the ignore list plus, for every entry
     naming a member of a fused projection, the fused module's name; sorted and

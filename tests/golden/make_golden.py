@@ -594,10 +594,77 @@ def gen_refresh(ref):
     save("refresh.npz", **{k: np.asarray(v) for k, v in out.items()})
 
 
+# ---------------------------------------------------------------------------
+# MoE expert stacking before export
+# ---------------------------------------------------------------------------
+
+STACK_E, STACK_HID, STACK_INTER = 3, 16, 8
+
+
+def stack_container(arrays, packed):
+    """An experts container (``num_experts``, submodules "0".."E-1" with
+    gate/up/down linears) holding the per-expert tensors in ``arrays``:
+    compressed buffers (``weight_packed`` / ``weight_scale`` / ``weight_shape``)
+    when ``packed``, else bf16 weights.  bf16 arrays are stored as int16 bits."""
+    nn = torch.nn
+    experts = nn.ModuleList()
+    experts.num_experts = STACK_E
+    for i in range(STACK_E):
+        e = nn.Module()
+        for part, (rows, cols) in (("gate_proj", (STACK_INTER, STACK_HID)),
+                                   ("up_proj", (STACK_INTER, STACK_HID)),
+                                   ("down_proj", (STACK_HID, STACK_INTER))):
+            lin = nn.Linear(cols, rows, bias=False)
+            if packed:
+                del lin.weight
+                lin.register_buffer("weight_packed",
+                                    torch.as_tensor(arrays[f"{part}{i}_packed"]))
+                lin.register_buffer("weight_scale", torch.as_tensor(
+                    arrays[f"{part}{i}_scale"]).view(torch.bfloat16))
+                lin.register_buffer("weight_shape", torch.tensor([rows, cols]))
+            else:
+                lin.weight = nn.Parameter(torch.as_tensor(
+                    arrays[f"{part}{i}_weight"]).view(torch.bfloat16), requires_grad=False)
+            setattr(e, part, lin)
+        experts.append(e)
+    return experts
+
+
+def gen_stack():
+    """The reference's ``MoEMixin.stack_experts`` (utils/models/mixins.py:93-144)
+    on a seeded container, with and without packed weights."""
+    from utils.models import mixins
+    gen = torch.Generator().manual_seed(21)
+    arrays = {}
+    for i in range(STACK_E):
+        for part, (rows, cols) in (("gate_proj", (STACK_INTER, STACK_HID)),
+                                   ("up_proj", (STACK_INTER, STACK_HID)),
+                                   ("down_proj", (STACK_HID, STACK_INTER))):
+            arrays[f"{part}{i}_packed"] = npy(torch.randint(
+                -2 ** 31, 2 ** 31 - 1, (rows, cols // 8), generator=gen, dtype=torch.int64
+            ).to(torch.int32))
+            arrays[f"{part}{i}_scale"] = npy((torch.rand(rows, cols // 8, generator=gen) + 0.1)
+                                             .to(torch.bfloat16).view(torch.int16))
+            arrays[f"{part}{i}_weight"] = npy(torch.randn(rows, cols, generator=gen)
+                                              .to(torch.bfloat16).view(torch.int16))
+    out = dict(arrays)
+    for packed in (True, False):
+        experts = stack_container(arrays, packed)
+        mixins.MoEMixin.stack_experts(None, experts, weight_packed=packed)
+        names = (["gate_up_proj_packed", "down_proj_packed", "gate_up_proj_scale",
+                  "down_proj_scale", "gate_up_proj_shape", "down_proj_shape"] if packed
+                 else ["gate_up_proj", "down_proj"])
+        for n in names:
+            t = getattr(experts, n).detach()
+            out[f"out_{n}"] = npy(t.view(torch.int16) if t.dtype == torch.bfloat16 else t)
+        out[f"left_{int(packed)}"] = np.asarray(len(experts._modules))
+    save("stack_experts.npz", **out)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of the reference checkout")
-    ap.add_argument("--only", default=None, help="one fixture family: export or refresh")
+    ap.add_argument("--only", default=None, help="one fixture family: export, refresh or stack")
     args = ap.parse_args()
     torch.set_num_threads(min(8, os.cpu_count() or 1))
     ref = import_reference(os.path.abspath(args.reference))
@@ -607,12 +674,16 @@ def main():
     if args.only == "refresh":
         gen_refresh(ref)
         return
+    if args.only == "stack":
+        gen_stack()
+        return
     gen_hessians(ref)
     gen_blocks(ref)
     gen_fasterquant(ref)
     gen_misc(ref)
     gen_export(os.path.abspath(args.reference))
     gen_refresh(ref)
+    gen_stack()
 
 
 if __name__ == "__main__":

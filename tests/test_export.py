@@ -90,3 +90,31 @@ def test_checkpoint_through_compress_on_gpu(fixture):
         mods.append(mod)
     ctu.register_qparam_buffers(mods)
     _save_and_compare(model, cfg, mg, fixture)
+
+
+# ---------------------------------------------------------------------------
+# MoE expert stacking (utils/models/mixins.py:93-144)
+# ---------------------------------------------------------------------------
+
+@pytest.mark.parametrize("packed", [True, False])
+def test_stack_experts_matches_reference(packed):
+    """The 3-D expert parameters equal, bit for bit, those the reference's own
+    ``MoEMixin.stack_experts`` made from the same per-expert tensors
+    (tests/golden/stack_experts.npz), and the per-expert submodules are gone."""
+    mg = _golden_module()
+    z = np.load(os.path.join(HERE, "golden", "stack_experts.npz"))
+    experts = mg.stack_container(z, packed)
+    ctu.stack_experts(experts, weight_packed=packed)
+    names = (["gate_up_proj_packed", "down_proj_packed", "gate_up_proj_scale",
+              "down_proj_scale", "gate_up_proj_shape", "down_proj_shape"] if packed
+             else ["gate_up_proj", "down_proj"])
+    for n in names:
+        t = getattr(experts, n).detach()
+        got = (t.view(torch.int16) if t.dtype == torch.bfloat16 else t).numpy()
+        want = z[f"out_{n}"]
+        assert got.dtype == want.dtype and got.shape == want.shape, n
+        assert np.array_equal(got, want), n
+    assert len(experts._modules) == int(z[f"left_{int(packed)}"]) == 0
+    if packed:
+        assert isinstance(experts.gate_up_proj_packed, torch.nn.Parameter)
+        assert not experts.gate_up_proj_packed.requires_grad
