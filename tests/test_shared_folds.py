@@ -334,3 +334,50 @@ def test_shared_factor_in_fasterquant_all(monkeypatch):
     assert (n1, n0) == (2, 4)
     for (w1, p1), (w0, p0) in zip(out1, out0):
         assert torch.equal(w1, w0) and torch.equal(p1, p0)
+
+
+@pytest.mark.gpu
+def test_shared_factor_damp_retry(monkeypatch):
+    """The shared Hessian is made indefinite (rank-deficient Gram minus a
+    multiple of the identity, written identically into every member), so the
+    first damped factorization fails and the damp auto-increment runs: the
+    owner re-factors, the followers re-run their compensation with its U.
+    Weights and final damps equal those of the unshared run, where each object
+    retries on its own."""
+    from g2ptq_b200.gptq_utils import gptq_utils, common_utils
+    from g2ptq_b200.utils.quant_utils import WeightQuantizer
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(5)
+    C = 512
+    X = torch.randn(2, 32, C, device=dev, generator=g).to(torch.bfloat16)  # rank 64 < C
+    Ws = [torch.randn(r, C, device=dev, generator=g) * 0.02 for r in (256, 128, 128)]
+
+    def build(share):
+        monkeypatch.setattr(_engine, "SHARE_FOLDS", share)
+        objs = []
+        for W in Ws:
+            lin = torch.nn.Linear(C, W.shape[0], bias=False, device=dev)
+            lin.weight.data = W.clone()
+            o = gptq_utils.GPTQ([lin])
+            q = WeightQuantizer()
+            q.configure(4, perchannel=True, sym=True)
+            o.quantizer = common_utils.make_group_quantizers(q, C, 128)
+            objs.append(o)
+        for s in range(2):
+            for o in objs:
+                o.add_batch(0, X[s:s + 1], None)
+        for o in objs:
+            o._flush_all()
+            H = o._H[0]
+            H -= 0.02 * torch.diagonal(H).mean() * torch.eye(C, device=dev)
+        gptq_utils.fasterquant_all(objs, blocksize=128, percdamp=0.01, groupsize=128,
+                                   actorder=False, static_groups=False)
+        torch.cuda.synchronize()
+        return [o.layers[0].weight.data.clone() for o in objs], [o._last_damps for o in objs]
+
+    W1, d1 = build(True)
+    W0, d0 = build(False)
+    assert d1 == d0 and d0[0][0] > 0.02
+    for a, b in zip(W1, W0):
+        assert torch.equal(a, b)
