@@ -19,10 +19,10 @@ class FakeObj(_engine.StagingMixin):
 
     _share_folds = True
 
-    def __init__(self, C):
-        self.columns, self.dev, self.num_layers = C, torch.device("cpu"), 1
-        self._H = torch.zeros(1, C, C, dtype=torch.float64)
-        self._n, self._n_folded = [0], [0]
+    def __init__(self, C, layers=1):
+        self.columns, self.dev, self.num_layers = C, torch.device("cpu"), layers
+        self._H = torch.zeros(layers, C, C, dtype=torch.float64)
+        self._n, self._n_folded = [0] * layers, [0] * layers
         self._init_stages()
         self.folds = 0
         self.fold_counts = []   # (n_old, n_new) of every fold this object made
@@ -267,6 +267,51 @@ class _RoleObj:
         self._groups = [group] * layers
         self._h_exposed = exposed
         self.num_layers = layers
+
+
+def test_layers_of_multi_layer_objects_share(cpu_staging, monkeypatch):
+    """Layer 1 of one object and layer 0 of another, fed the same tensors,
+    share; layer 0 of the first, fed others, stays alone."""
+    def go(share):
+        monkeypatch.setattr(_engine, "SHARE_FOLDS", share)
+        xs, ys = inputs(9, seed=3), inputs(9, seed=4)
+        a, b = FakeObj(6, layers=2), FakeObj(6)
+        for x, y in zip(xs, ys):
+            a.add_batch(0, y)
+            a.add_batch(1, x)
+            b.add_batch(0, x)
+        a._flush_all()
+        b._flush_all()
+        return a._H.clone(), b._H.clone(), a.folds + b.folds
+    Ha1, Hb1, f1 = go(True)
+    Ha0, Hb0, f0 = go(False)
+    assert torch.equal(Ha1, Ha0) and torch.equal(Hb1, Hb0)
+    assert f0 - f1 == 3      # the shared pair folds once per window instead of twice
+
+
+def test_member_leaving_mid_window_keeps_the_others_exact(cpu_staging, monkeypatch):
+    """One member leaves (its statistics handed out and dropped, as fasterquant
+    does) in the middle of a window; the remaining members go on sharing."""
+    monkeypatch.setattr(_engine, "SHARE_FOLDS", True)
+    xs = inputs(7)
+    objs = [FakeObj(6) for _ in range(3)]
+    for x in xs[:3]:
+        for o in objs:
+            o.add_batch(0, x)
+    H_left = objs[0].H().clone()
+    objs[0]._leave_groups()
+    for x in xs[3:]:
+        for o in objs[1:]:
+            o.add_batch(0, x)
+    monkeypatch.setattr(_engine, "SHARE_FOLDS", False)
+    r3, r7 = FakeObj(6), FakeObj(6)
+    for x in xs[:3]:
+        r3.add_batch(0, x)
+    for x in xs:
+        r7.add_batch(0, x)
+    assert torch.allclose(H_left, r3.H(), rtol=1e-12, atol=1e-12)
+    for o in objs[1:]:
+        assert torch.allclose(o.H(), r7.H(), rtol=1e-12, atol=1e-12)
 
 
 def test_factor_roles(monkeypatch):
