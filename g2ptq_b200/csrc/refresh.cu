@@ -515,10 +515,10 @@ using namespace g2q;
 extern "C" int g2q_saliency(float* out, const void* grad, int dtype, int64_t ld, int64_t T,
                             int64_t R, int G, void* stream) {
   const int eb = elem_bytes(dtype);
-  if (!out || eb == 0 || T < 0 || R <= 0 || G <= 0 || (R % G) != 0 || ld < R)
+  if (eb == 0 || T < 0 || R <= 0 || G <= 0 || (R % G) != 0 || ld < R)
     return G2Q_ERR_INVALID_ARG;
-  if (T == 0) return G2Q_OK;
-  if (!grad) return G2Q_ERR_INVALID_ARG;
+  if (T == 0) return G2Q_OK;  // nothing to read or write (empty buffers may be NULL)
+  if (!out || !grad) return G2Q_ERR_INVALID_ARG;
   cudaStream_t st = (cudaStream_t)stream;
   const long long gs = R / G;
   const float inv_gs = 1.f / (float)gs;

@@ -366,3 +366,18 @@ def test_refresh_sequence_on_gpu_matches_oracle():
         got = gc.gradients_cache[name].cpu().numpy()
         ref = want[f"grad_{name}"]
         assert np.abs(got - ref).max() <= 1e-4 * np.abs(ref).max(), name
+
+
+@pytest.mark.gpu
+def test_refresh_kernels_on_empty_inputs():
+    """No tokens: an empty saliency, a zero loss and an empty gradient (the
+    reference's torch ops give the same for empty batches)."""
+    sal = ops.saliency(torch.empty(0, 64, device="cuda", dtype=torch.bfloat16), 4)
+    assert sal.shape == (0, 4)
+    for kind in (_lib.LOSS_KL, _lib.LOSS_NLL, _lib.LOSS_MSE):
+        x = torch.empty(0, 40, device="cuda", requires_grad=True)
+        t = None if kind == _lib.LOSS_NLL else torch.empty(0, 40, device="cuda")
+        lab = torch.empty(0, dtype=torch.int64, device="cuda") if kind == _lib.LOSS_NLL else None
+        loss = G.block_loss(kind, x, target=t, labels=lab)
+        loss.backward()
+        assert float(loss.detach()) == 0.0 and x.grad.shape == (0, 40)
