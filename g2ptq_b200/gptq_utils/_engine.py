@@ -314,10 +314,14 @@ class FoldGroup:
     with a private stage holding their part of the window.  The fold's sample
     count is the one a lone object would use: the folded count, the window's
     samples and, for a fold that a new call triggers, that call's samples.
+
+    Members are held by weak reference (each member holds its group), so the
+    window's tensors go with the last member even if it is dropped without
+    ``free()``.
     """
 
     def __init__(self, obj, idx, dtype, columns, device):
-        self.members = [(obj, idx)]
+        self._members = [(weakref.ref(obj), idx)]
         self.pos = [0]
         self.stage = TokenStage(columns, device)
         self.stage._ensure(dtype, False)
@@ -327,9 +331,23 @@ class FoldGroup:
         self.first_key = None
 
     # -- membership -------------------------------------------------------
+    @property
+    def members(self):
+        """Live members ``(object, layer)``; members whose objects are gone are
+        dropped (with their positions)."""
+        live = [(r(), i) for r, i in self._members]
+        if any(o is None for o, _ in live):
+            keep = [k for k, (o, _) in enumerate(live) if o is not None]
+            self._members = [self._members[k] for k in keep]
+            self.pos = [self.pos[k] for k in keep]
+            live = [live[k] for k in keep]
+            if not live:
+                self.close()
+        return live
+
     def _index(self, obj, idx):
-        for k, (o, i) in enumerate(self.members):
-            if o is obj and i == idx:
+        for k, (r, i) in enumerate(self._members):
+            if r() is obj and i == idx:
                 return k
         raise KeyError("not a member")
 
@@ -338,7 +356,7 @@ class FoldGroup:
                 and self.stage.dtype == dtype)
 
     def join(self, obj, idx):
-        self.members.append((obj, idx))
+        self._members.append((weakref.ref(obj), idx))
         self.pos.append(0)
 
     def detach(self, obj, idx):
@@ -346,7 +364,7 @@ class FoldGroup:
         calls it made in this window."""
         k = self._index(obj, idx)
         p = self.pos.pop(k)
-        self.members.pop(k)
+        self._members.pop(k)
         obj._groups[idx] = None
         rows = self.row_ends[p - 1] if p else 0
         if rows:
@@ -354,11 +372,11 @@ class FoldGroup:
             st._ensure(self.stage.dtype, False)
             st.buf[:rows].copy_(self.stage.buf[:rows])
             st.rows = rows
-        if not self.members:
+        if not self._members:
             self.close()
 
     def dissolve(self):
-        for o, i in list(self.members):
+        for o, i in self.members:
             self.detach(o, i)
 
     def close(self):
@@ -401,23 +419,25 @@ class FoldGroup:
         """Fold the window for every member that made all of its calls; the
         others leave first with their part of it."""
         n = len(self.keys)
-        for o, i in [m for m, p in zip(self.members, self.pos) if p < n]:
+        members = self.members
+        for o, i in [m for m, p in zip(members, self.pos) if p < n]:
             self.detach(o, i)
-        if not self.members or self.stage.rows == 0:
+        members = self.members
+        if not members or self.stage.rows == 0:
             return
-        o0, i0 = self.members[0]
-        if len({o._n_folded[i] for o, i in self.members}) != 1:
+        o0, i0 = members[0]
+        if len({o._n_folded[i] for o, i in members}) != 1:
             self.dissolve()
             return
         n_new = o0._n_folded[i0] + self.samples + trigger_samples
         o0._fold(i0, self.stage.buf[:self.stage.rows], None, None, n_new=n_new)
-        for o, i in self.members[1:]:
+        for o, i in members[1:]:
             o._copy_folded(i, o0, i0)
         self.stage.rows = 0
         # the triggering call is staged next, but its samples are in n_new
         self.samples = -trigger_samples
         self.keys, self.srcs, self.row_ends = [], [], []
-        self.pos = [0] * len(self.members)
+        self.pos = [0] * len(self._members)
         if not self.folded:
             self.folded = True
             if self.first_key is not None and _OPEN_GROUPS.get(self.first_key) is self:

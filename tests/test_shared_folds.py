@@ -426,3 +426,35 @@ def test_shared_factor_damp_retry(monkeypatch):
     assert d1 == d0 and d0[0][0] > 0.02
     for a, b in zip(W1, W0):
         assert torch.equal(a, b)
+
+
+def test_dropped_members_release_the_window(cpu_staging, monkeypatch):
+    """Members dropped without free() leave the group; the others keep their
+    exact statistics, and the window's tensors go with the last member, with
+    no cycle left for the garbage collector."""
+    import gc
+    import weakref
+    monkeypatch.setattr(_engine, "SHARE_FOLDS", True)
+    xs = inputs(7)
+    objs = [FakeObj(6) for _ in range(3)]
+    gc_was = gc.isenabled()
+    gc.disable()
+    try:
+        for x in xs[:3]:
+            for o in objs:
+                o.add_batch(0, x)
+        group = weakref.ref(objs[0]._groups[0])
+        del objs[1:]                                  # dropped mid-window, no free()
+        for x in xs[3:]:
+            objs[0].add_batch(0, x)
+        monkeypatch.setattr(_engine, "SHARE_FOLDS", False)
+        ref = FakeObj(6)
+        for x in xs:
+            ref.add_batch(0, x)
+        assert torch.allclose(objs[0].H(), ref.H(), rtol=1e-12, atol=1e-12)
+        assert len(group().members) == 1
+        del objs
+        assert group() is None    # collected by reference counting alone
+    finally:
+        if gc_was:
+            gc.enable()
