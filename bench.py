@@ -80,9 +80,10 @@ def load_peaks():
 
 
 # DRAM traffic of one Gram fold at the bench's 4096-column fold shape (16384 BF16
-# tokens), dram__bytes_read.sum + dram__bytes_write.sum from one ncu capture of
-# the CTA-pair kernel (profiles/gram_pair_c4096_t16384.md); the algorithmic bytes
-# of that launch are 268.4 MB (X once, H read and written once).
+# tokens): dram__bytes_read.sum + dram__bytes_write.sum of the CTA-pair kernel in
+# one ncu capture of `kernel_cases.py gram --tokens 16384 --columns 4096`.  A
+# static figure (the bench runs without a profiler); the algorithmic bytes of
+# that launch are 268.4 MB (X once, H read and written once).
 GRAM_FOLD_TRAFFIC_BYTES = 317.06e6
 # device buffers (one calibration sequence each) of the host-input copy ring
 E2E_RING = 48
@@ -382,6 +383,7 @@ def native(args):
             "frac": round(gram_tflops / bf16, 4), "traffic": GRAM_FOLD_TRAFFIC_BYTES,
             "traffic_per": "launch, C=4096 x T=16384 fold "
                            f"(algorithmic {GRAM_FOLD_ALGORITHMIC_BYTES:.4g} B)",
+            "traffic_source": "static: one ncu capture of the fold kernel, not this run",
             "peak_kind": f"{peak_kind} bf16 dense sustained",
             "share_of_step": round(gram_ms / ms, 3) if ms else None,
         },

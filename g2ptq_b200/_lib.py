@@ -11,7 +11,7 @@ import os
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.environ.get("G2PTQ_B200_LIB", os.path.join(_HERE, "_lib", "libg2ptq_b200.so"))
 
-ABI_VERSION = 6
+ABI_VERSION = 7
 
 G2Q_OK = 0
 G2Q_ERR_INVALID_ARG = -1
@@ -47,11 +47,12 @@ SIGNATURES = {
     "g2q_launch_count": [],
     "g2q_status_string": [I32],
     "g2q_stage_tokens": [P, I32, I64, I64, P, P, I32, I64, I64, I64, P],
+    "g2q_set_wait_limit": [I64],
     "g2q_gram_update": [P, I64, I64, I64, P, I32, I64, P, I32, I64, P, I64, I64, I32, F32, F32,
-                        I32, P, SZ, P],
+                        I32, P, SZ, P, P],
     "g2q_gram_workspace_bytes": [I64, I64, I64, I32],
     "g2q_gram_update_grouped": [P, I64, I64, I64, P, I32, I64, P, I64, I32, I64, F32, F32, I32, P,
-                                SZ, P],
+                                SZ, P, P],
     "g2q_gram_grouped_workspace_bytes": [I64, I64, I32, I32],
     "g2q_sq_colsum": [P, F32, F32, P, I32, I64, I64, I64, P],
     "g2q_gemm": [P, I64, I64, P, I64, I64, I32, P, I64, I64, I32, I64, I64, I64, I64, F32, F32,
@@ -62,7 +63,7 @@ SIGNATURES = {
     "g2q_find_params_clip": [P, P, I64, P, I64, I64, I64, I32, I32, P, P, P],
     "g2q_find_params_groups": [P, P, I64, P, I64, I64, I64, I32, I32, I64, I32, I32, P, P],
     "g2q_gemm_tc": [P, I64, I64, P, I64, I64, I32, P, I64, I64, I32, I64, I64, I64, I64, F32, F32,
-                    I32, P, SZ, P],
+                    I32, P, SZ, P, P],
     "g2q_gemm_tc_workspace_bytes": [I64, I64, I64, I64, I32, I32],
     "g2q_fake_quantize": [P, I64, P, I64, P, I64, I64, I64, P, P, I64, P, I32, P],
     "g2q_compensate_block": [I32, P, I64, I64, I64, I64, I64, P, I64, I64, P, P, I64, P, I32, P,
@@ -81,7 +82,7 @@ SIGNATURES = {
     "g2q_diag_of_utu": [P, P, I64, I64, P],
     "g2q_scale_rows": [P, P, I64, I64, I64, P],
     "g2q_gram_update_noalloc": [P, I64, I64, I64, P, I32, I64, P, I32, I64, P, I64, I64, I32, F32,
-                                F32, P],
+                                F32, P, P],
     "g2q_gram_static_scratch_bytes": [],
     "g2q_saliency": [P, P, I32, I64, I64, I64, I32, P],
     "g2q_scaled_accumulate": [P, P, I64, F32, I32, P],
@@ -91,6 +92,7 @@ SIGNATURES = {
 }
 _RESTYPES = {
     "g2q_launch_count": ctypes.c_int64,
+    "g2q_set_wait_limit": ctypes.c_int64,
     "g2q_status_string": ctypes.c_char_p,
     "g2q_gram_workspace_bytes": SZ,
     "g2q_gram_grouped_workspace_bytes": SZ,

@@ -466,7 +466,7 @@ int split2h(const float* src, long long lds, long long n, int K, __half* hi, __h
 int tc_update2h(float* D, long long ldd, long long M, long long N, long long K,
                 __half* const* a2, const float* sa, long long lda, __half* const* b2,
                 const float* sb, long long ldb, int lower, float alpha, float beta,
-                cudaStream_t st);
+                int* status, cudaStream_t st);
 
 // Side stream and per-step events of the inverse chain, one set per (device,
 // caller stream) so that factorizations issued on different streams overlap.
@@ -591,8 +591,9 @@ static int chol_one(float* U, const float* H, long long C, long long ldh, float 
         if (kb >= 2 && cudaStreamWaitEvent(st, ev[2 * (kb - 2) + 1], 0) != cudaSuccess)
           return G2Q_ERR_CUDA;
         G2Q_TRY(split2h(A + (k0 + nb) * C + k0, C, rest, nb, l2[0], l2[1], C, lsc, 1, st));
+        // a tensor-core wait that gives up records G2Q_ERR_TIMEOUT in info
         G2Q_TRY(tc_update2h(A + (k0 + nb) * C + (k0 + nb), C, rest, rest, nb, l2, lsc, C, l2,
-                            lsc, C, 1, 1.f, -1.f, st));
+                            lsc, C, 1, 1.f, -1.f, info, st));
       } else {
         G2Q_TRY(simt_gemm_f32(A + (k0 + nb) * C + (k0 + nb), C, A + (k0 + nb) * C + k0, C, false,
                               A + (k0 + nb) * C + k0, C, true, rest, rest, nb, 1.f, -1.f,
@@ -607,7 +608,7 @@ static int chol_one(float* U, const float* H, long long C, long long ldh, float 
       if (use_tc) {
         G2Q_TRY(split2h(Y + k0 * C, C, k0 + nb, nb, x2[0], x2[1], C, w.xsc, 0, side));
         G2Q_TRY(tc_update2h(Y + (k0 + nb) * C, C, rest, k0 + nb, nb, l2, lsc, C, x2, w.xsc, C, 0,
-                            1.f, -1.f, side));
+                            1.f, -1.f, info, side));
       } else {
         G2Q_TRY(simt_gemm_f32(Y + (k0 + nb) * C, C, A + (k0 + nb) * C + k0, C, false, Y + k0 * C,
                               C, false, rest, k0 + nb, nb, 1.f, -1.f, G2Q_MASK_FULL, side));

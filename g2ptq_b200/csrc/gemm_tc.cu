@@ -30,8 +30,11 @@
 // Warp roles (192 threads, 320 for 128 x 256 tiles): warp 0 TMA producer,
 // warp 1 TMEM owner + MMA issuer, the rest epilogue (TMEM lane quadrant =
 // warp % 4).
-// Every wait on an mbarrier is bounded; on expiry the CTA records
-// G2Q_ERR_TIMEOUT in the caller's status word and winds down.
+// Every wait on an mbarrier is bounded (Params::wait_cycles, set from
+// g2q_set_wait_limit); on expiry the CTA records G2Q_ERR_TIMEOUT in the
+// caller's status word and winds down: the producer waits (with its own fixed
+// bound) for the loads it issued to land and the MMA issuer for the MMAs it
+// issued to complete before the TMEM is freed and the CTA exits.
 #include <cuda.h>
 #include <stdlib.h>
 #include <cudaTypedefs.h>
@@ -46,7 +49,8 @@ namespace tc {
 constexpr int BM = 128, BN = 128, BK = 64;
 constexpr int CHUNK_BYTES = 64 * BK * 2;     // one 64 (MN) x 64 (K) bf16 box
 constexpr int TILE_BYTES = 2 * CHUNK_BYTES;  // one 128 x 64 operand tile
-constexpr long long kWaitCycles = 4000000000LL;
+constexpr long long kWaitCycles = 4000000000LL;   // default bound of one pipeline wait
+constexpr long long kDrainCycles = 2000000000LL;  // bound of a wind-down wait after an abort
 
 struct Params {
   float* D;
@@ -69,7 +73,8 @@ struct Params {
   long long sa_bs, sb_bs;  // their batch strides
   int supper;      // write only m < n (strictly upper part)
   int prefetch_kb;  // CTA-pair kernel: L2 prefetch distance in k-blocks (0: none)
-  int* status;
+  int* status;     // receives G2Q_ERR_TIMEOUT when a wait gives up (may be null)
+  long long wait_cycles;  // bound of every pipeline wait (set by the launchers)
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -85,26 +90,43 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t a, uint32_t bytes) {
                : "memory");
 }
 
+__device__ __forceinline__ bool mbar_test(uint32_t a, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(a), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Pipeline wait: gives up when another warp of the CTA has given up
+// (abort_flag) or after `limit` cycles, which sets the flag and records
+// G2Q_ERR_TIMEOUT.
 __device__ __forceinline__ bool mbar_wait(uint32_t a, uint32_t parity, volatile int* abort_flag,
-                                          int* status) {
+                                          int* status, long long limit) {
   const long long t0 = clock64();
   while (true) {
-    uint32_t done;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(done)
-        : "r"(a), "r"(parity)
-        : "memory");
-    if (done) return true;
+    if (mbar_test(a, parity)) return true;
     if (*abort_flag) return false;
-    if (clock64() - t0 > kWaitCycles) {
+    if (clock64() - t0 > limit) {
       *abort_flag = 1;
       record_error(status, G2Q_ERR_TIMEOUT);
       return false;
     }
   }
+}
+
+// Wind-down wait after an abort: the phase completes once asynchronous work
+// this thread already issued (loads, MMAs) has finished; bounded by
+// kDrainCycles, and it ignores the abort flag.
+__device__ __forceinline__ bool mbar_drain(uint32_t a, uint32_t parity) {
+  const long long t0 = clock64();
+  while (!mbar_test(a, parity))
+    if (clock64() - t0 > kDrainCycles) return false;
+  return true;
 }
 
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
@@ -373,14 +395,16 @@ __global__ void __launch_bounds__((Cfg<NA, NB, SMALL, WIDE>::THREADS),
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + K::STAGES * K::STAGE_BYTES);
-  // bars[0..S): full, [S..2S): empty, [2S..2S+2): accumulator full, [2S+2..2S+4): drained
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * K::STAGES + 4);
+  // bars[0..S): full, [S..2S): empty, [2S..2S+2): accumulator full, [2S+2..2S+4): drained,
+  // [2S+4]: MMA completion after an abort
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * K::STAGES + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + K::STAGES);
   const uint32_t accf0 = smem_u32(bars + 2 * K::STAGES);
   const uint32_t acce0 = smem_u32(bars + 2 * K::STAGES + 2);
+  const uint32_t drain0 = smem_u32(bars + 2 * K::STAGES + 4);
   const int ngroups = SMALL ? (p.num_kb > 0 ? 1 : 0)
                             : (p.num_kb + p.promote_kb - 1) / p.promote_kb;
   const int promote_kb = SMALL ? p.num_kb : p.promote_kb;
@@ -394,6 +418,7 @@ __global__ void __launch_bounds__((Cfg<NA, NB, SMALL, WIDE>::THREADS),
       mbar_init(accf0 + 8 * b, 1);
       mbar_init(acce0 + 8 * b, 32 * K::EPI_WARPS);
     }
+    mbar_init(drain0, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -410,12 +435,14 @@ __global__ void __launch_bounds__((Cfg<NA, NB, SMALL, WIDE>::THREADS),
   const uint32_t tmem = *tmem_holder;
   const int m0 = mt * BM, n0 = nt * BN_T;
 
+  int issued = 0;  // k-blocks whose loads the producer issued
   if (warp == 0) {
     if (lane == 0) {
       for (int kb = 0; kb < p.num_kb; ++kb) {
         const int s = kb % K::STAGES;
         const uint32_t ph = (kb / K::STAGES) & 1;
-        if (!mbar_wait(empty0 + 8 * s, ph ^ 1, abort_flag, p.status)) break;
+        if (!mbar_wait(empty0 + 8 * s, ph ^ 1, abort_flag, p.status, p.wait_cycles)) break;
+        issued = kb + 1;
         const uint32_t fb = full0 + 8 * s;
         mbar_expect_tx(fb, K::STAGE_BYTES);
         const uint32_t st = smem_u32(smem + s * K::STAGE_BYTES);
@@ -445,7 +472,7 @@ __global__ void __launch_bounds__((Cfg<NA, NB, SMALL, WIDE>::THREADS),
       for (int g = 0; g < ngroups; ++g) {
         const int buf = g & 1;
         const uint32_t use_ph = (uint32_t)((g >> 1) & 1);
-        if (!mbar_wait(acce0 + 8 * buf, use_ph ^ 1, abort_flag, p.status)) break;
+        if (!mbar_wait(acce0 + 8 * buf, use_ph ^ 1, abort_flag, p.status, p.wait_cycles)) break;
         fence_after();
         const uint32_t acc_t = tmem + (uint32_t)(buf * BN_T);
         const int kend = (kb + promote_kb < p.num_kb) ? kb + promote_kb : p.num_kb;
@@ -454,7 +481,7 @@ __global__ void __launch_bounds__((Cfg<NA, NB, SMALL, WIDE>::THREADS),
         for (; kb < kend; ++kb) {
           const int s = kb % K::STAGES;
           const uint32_t ph = (kb / K::STAGES) & 1;
-          if (!mbar_wait(full0 + 8 * s, ph, abort_flag, p.status)) {
+          if (!mbar_wait(full0 + 8 * s, ph, abort_flag, p.status, p.wait_cycles)) {
             ok = false;
             break;
           }
@@ -490,7 +517,7 @@ __global__ void __launch_bounds__((Cfg<NA, NB, SMALL, WIDE>::THREADS),
     const int row = q * 32 + lane;
     const long long gm = m0 + row;
     bool ok = true;
-    if (ngroups > 0) ok = mbar_wait(accf0, 0, abort_flag, p.status);
+    if (ngroups > 0) ok = mbar_wait(accf0, 0, abort_flag, p.status, p.wait_cycles);
     fence_after();
     float* Db = p.D + bz * p.d_bs;
     if (p.red) {
@@ -585,7 +612,7 @@ __global__ void __launch_bounds__((Cfg<NA, NB, SMALL, WIDE>::THREADS),
     for (int g = 0; g < ngroups; ++g) {
       const int buf = g & 1;
       const uint32_t use_ph = (uint32_t)((g >> 1) & 1);
-      if (ok) ok = mbar_wait(accf0 + 8 * buf, use_ph, abort_flag, p.status);
+      if (ok) ok = mbar_wait(accf0 + 8 * buf, use_ph, abort_flag, p.status, p.wait_cycles);
       fence_after();
       const uint32_t base =
           tmem + (uint32_t)(buf * BN_T + half * BN) + ((uint32_t)(q * 32) << 16);
@@ -618,6 +645,18 @@ __global__ void __launch_bounds__((Cfg<NA, NB, SMALL, WIDE>::THREADS),
   }
   fence_before();
   __syncthreads();
+  if (*abort_flag) {
+    // a wait gave up: let this CTA's loads land and its MMAs finish before the
+    // shared memory and the TMEM are released
+    if (warp == 0 && lane == 0) {
+      for (int kb = issued > K::STAGES ? issued - K::STAGES : 0; kb < issued; ++kb)
+        mbar_drain(full0 + 8 * (kb % K::STAGES), (kb / K::STAGES) & 1);
+    } else if (warp == 1 && lane == 0) {
+      umma_commit(drain0);
+      mbar_drain(drain0, 0);
+    }
+    __syncthreads();
+  }
   if (warp == 1) {
     __syncwarp();
     fence_after();
@@ -747,14 +786,16 @@ __global__ void __launch_bounds__(PairCfg<NA, BKP>::THREADS, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + K::STAGES * K::STAGE_BYTES);
   // bars[0..S): full (used in the leader), [S..2S): empty, [2S..2S+2): accumulator
-  // full, [2S+2..2S+4): accumulator drained (used in the leader)
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * K::STAGES + 4);
+  // full, [2S+2..2S+4): accumulator drained (used in the leader), [2S+4]: MMA completion
+  // after an abort (leader)
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * K::STAGES + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + K::STAGES);
   const uint32_t accf0 = smem_u32(bars + 2 * K::STAGES);
   const uint32_t acce0 = smem_u32(bars + 2 * K::STAGES + 2);
+  const uint32_t drain0 = smem_u32(bars + 2 * K::STAGES + 4);
   const int ngroups = (p.num_kb + p.promote_kb - 1) / p.promote_kb;
   const int promote_kb = p.promote_kb;
 
@@ -767,6 +808,7 @@ __global__ void __launch_bounds__(PairCfg<NA, BKP>::THREADS, 1)
       mbar_init(accf0 + 8 * b, 1);
       mbar_init(acce0 + 8 * b, 2 * K::EPI_WARPS);
     }
+    mbar_init(drain0, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -784,13 +826,15 @@ __global__ void __launch_bounds__(PairCfg<NA, BKP>::THREADS, 1)
   const uint32_t tmem = *tmem_holder;
   const int m0 = mt * PT, n0 = nt * PT;
 
+  int issued = 0;  // k-blocks whose loads this CTA's producer issued
   if (warp == 0) {
     if (lane == 0) {
       const uint32_t full_lead = mapa_shared(full0, 0);
       for (int kb = 0; kb < p.num_kb; ++kb) {
         const int s = kb % K::STAGES;
         const uint32_t ph = (kb / K::STAGES) & 1;
-        if (!mbar_wait(empty0 + 8 * s, ph ^ 1, abort_flag, p.status)) break;
+        if (!mbar_wait(empty0 + 8 * s, ph ^ 1, abort_flag, p.status, p.wait_cycles)) break;
+        issued = kb + 1;
         // the leader's full[s] expects the bytes of both CTAs; the peer's loads
         // may land first (the transaction count goes transiently negative)
         if (rank == 0) mbar_expect_tx(full0 + 8 * s, 2 * K::STAGE_BYTES);
@@ -833,7 +877,7 @@ __global__ void __launch_bounds__(PairCfg<NA, BKP>::THREADS, 1)
       for (int g = 0; g < ngroups; ++g) {
         const int buf = g & 1;
         const uint32_t use_ph = (uint32_t)((g >> 1) & 1);
-        if (!mbar_wait(acce0 + 8 * buf, use_ph ^ 1, abort_flag, p.status)) break;
+        if (!mbar_wait(acce0 + 8 * buf, use_ph ^ 1, abort_flag, p.status, p.wait_cycles)) break;
         fence_after();
         const uint32_t acc_t = tmem + (uint32_t)(buf * PT);
         const int kend = (kb + promote_kb < p.num_kb) ? kb + promote_kb : p.num_kb;
@@ -842,7 +886,7 @@ __global__ void __launch_bounds__(PairCfg<NA, BKP>::THREADS, 1)
         for (; kb < kend; ++kb) {
           const int s = kb % K::STAGES;
           const uint32_t ph = (kb / K::STAGES) & 1;
-          if (!mbar_wait(full0 + 8 * s, ph, abort_flag, p.status)) {
+          if (!mbar_wait(full0 + 8 * s, ph, abort_flag, p.status, p.wait_cycles)) {
             ok = false;
             break;
           }
@@ -879,7 +923,7 @@ __global__ void __launch_bounds__(PairCfg<NA, BKP>::THREADS, 1)
     for (int g = 0; g < ngroups; ++g) {
       const int buf = g & 1;
       const uint32_t use_ph = (uint32_t)((g >> 1) & 1);
-      if (ok) ok = mbar_wait(accf0 + 8 * buf, use_ph, abort_flag, p.status);
+      if (ok) ok = mbar_wait(accf0 + 8 * buf, use_ph, abort_flag, p.status, p.wait_cycles);
       fence_after();
       const uint32_t base = tmem + (uint32_t)(buf * PT + half * BN) + ((uint32_t)(q * 32) << 16);
 #pragma unroll
@@ -908,6 +952,24 @@ __global__ void __launch_bounds__(PairCfg<NA, BKP>::THREADS, 1)
   }
   fence_before();
   __syncthreads();
+  if (*abort_flag) {
+    // a wait gave up: the leader lets the loads of both CTAs into the stages it
+    // armed land (its full barriers count both CTAs' bytes) and its MMAs finish;
+    // the peer's loads into stages the leader never armed complete no barrier
+    // this CTA can wait on, so the peer allows them a fixed settling time
+    if (warp == 0 && lane == 0) {
+      if (rank == 0) {
+        for (int kb = issued > K::STAGES ? issued - K::STAGES : 0; kb < issued; ++kb)
+          mbar_drain(full0 + 8 * (kb % K::STAGES), (kb / K::STAGES) & 1);
+      } else if (issued > 0) {
+        for (int i = 0; i < 200; ++i) __nanosleep(1000);
+      }
+    } else if (warp == 1 && lane == 0 && rank == 0) {
+      umma_commit_pair(drain0);
+      mbar_drain(drain0, 0);
+    }
+    __syncthreads();
+  }
   // neither CTA leaves while the other may still touch its shared memory or TMEM
   cluster_sync();
   if (warp == 1) {
@@ -977,6 +1039,10 @@ static bool make_map_out(CUtensorMap* m, float* D, long long N, long long M, lon
              CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Bound of every pipeline wait of the tensor-core kernels, in SM clock cycles
+// (g2q_set_wait_limit); read at each launch.
+static volatile long long g_wait_cycles = kWaitCycles;
+
 template <int NA, int NB, bool SMALL, bool WIDE = false>
 static int launch(const Maps& m, const Params& p, long long batch, cudaStream_t st) {
   using K = Cfg<NA, NB, SMALL, WIDE>;
@@ -990,6 +1056,7 @@ static int launch(const Maps& m, const Params& p, long long batch, cudaStream_t 
     if (dev < 64) attr_done[dev] = 1;
   }
   Params q = p;
+  q.wait_cycles = g_wait_cycles;
   q.promote_kb = K::PROMOTE_KB;
   q.tiles_m = cdiv(p.M, BM);
   q.tiles_n = cdiv(p.N, K::BN_T);
@@ -1041,6 +1108,7 @@ static int launch_pair(const Maps& m, const Params& p, long long batch, cudaStre
     if (dev < 64) attr_done[dev] = 1;
   }
   Params q = p;
+  q.wait_cycles = g_wait_cycles;
   q.promote_kb = K::PROMOTE_KB;
   q.prefetch_kb = pair_prefetch_enabled() ? K::STAGES : 0;
   q.tiles_m = cdiv(p.M, 256);
@@ -1209,7 +1277,7 @@ int split_bf16_2d(__nv_bfloat16* hi, __nv_bfloat16* lo, const float* src, long l
 int tc_gram(float* D, long long ldd, long long M, long long N, const void* A, int a_dtype,
             long long lda, const void* B, int b_dtype, long long ldb, const float* row_scale,
             long long scale_stride, long long T, int symmetric, float alpha, float beta,
-            void* workspace, size_t workspace_bytes, cudaStream_t st) {
+            void* workspace, size_t workspace_bytes, int* status, cudaStream_t st) {
   SimtArgs sa{};
   sa.A = A; sa.B = B; sa.C = D;
   sa.lda = lda; sa.ldb = ldb; sa.ldc = ldd;
@@ -1245,6 +1313,7 @@ int tc_gram(float* D, long long ldd, long long M, long long N, const void* A, in
               tc::make_map(&mp.b[0], B, N, T, ldb);
     if (!ok) return simt_gemm(sa, true, false, a_dtype, b_dtype, 1, st);
     tc::Params p{};
+    p.status = status;
     p.D = D; p.ldd = ldd; p.d_bs = 0;
     p.M = M; p.N = N;
     p.num_kb = (int)((T + tc::BK - 1) / tc::BK);
@@ -1289,6 +1358,7 @@ int tc_gram(float* D, long long ldd, long long M, long long N, const void* A, in
         tc::make_map(&mp.b[0], b_terms[0], N, T, ldb_t, false, 128)) {
       mp.a[1] = mp.a[0];
       tc::Params p{};
+      p.status = status;
       p.D = D; p.ldd = ldd; p.d_bs = 0;
       p.M = M; p.N = N;
       p.num_kb = (int)((T + 127) / 128);
@@ -1305,12 +1375,12 @@ int tc_gram(float* D, long long ldd, long long M, long long N, const void* A, in
   ok = ok && (nb == 1 || tc::make_map(&mp.b[1], b_terms[1], N, T, ldb_t));
   if (!ok) return simt_gemm(sa, true, false, a_dtype, b_dtype, 1, st);
   tc::Params p{};
+  p.status = status;
   p.D = D; p.ldd = ldd; p.d_bs = 0;
   p.M = M; p.N = N;
   p.num_kb = (int)((T + tc::BK - 1) / tc::BK);
   p.alpha = alpha; p.beta = beta;
   p.symmetric = symmetric ? 1 : 0;
-  p.status = nullptr;
   p.raster = 1;
   return tc::dispatch(na, nb, mp, p, 1, st);
 }
@@ -1328,7 +1398,7 @@ size_t tc_gram_grouped_workspace_bytes(long long C, long long T, int G) {
 int tc_gram_grouped(float* D, long long ldd, long long d_gstride, long long C, const void* X,
                     int x_dtype, long long ldx, const float* s, long long sstride, int G,
                     long long T, float alpha, float beta, void* workspace,
-                    size_t workspace_bytes, cudaStream_t st) {
+                    size_t workspace_bytes, int* status, cudaStream_t st) {
   const bool fast = x_dtype == G2Q_DTYPE_BF16 && T > 0 && C >= 512 && (C % 8) == 0 &&
                     (ldx % 8) == 0 && ((reinterpret_cast<uintptr_t>(X) & 15) == 0) && G <= 65535 &&
                     tc::encode_fn() && tc::pair_tiles_enabled() &&
@@ -1356,6 +1426,7 @@ int tc_gram_grouped(float* D, long long ldd, long long d_gstride, long long C, c
         tc::make_map(&mp.a[1], lo, C, (long long)G * T, w) &&
         tc::make_map(&mp.b[0], X, C, T, ldx)) {
       tc::Params p{};
+      p.status = status;
       p.D = D; p.ldd = ldd; p.d_bs = d_gstride;
       p.M = C; p.N = C;
       p.num_kb = (int)((T + tc::BK - 1) / tc::BK);
@@ -1368,7 +1439,7 @@ int tc_gram_grouped(float* D, long long ldd, long long d_gstride, long long C, c
   }
   for (int g = 0; g < G; ++g)
     G2Q_TRY(tc_gram(D + g * d_gstride, ldd, C, C, X, x_dtype, ldx, X, x_dtype, ldx, s + g, sstride,
-                    T, 1, alpha, beta, workspace, workspace_bytes, st));
+                    T, 1, alpha, beta, workspace, workspace_bytes, status, st));
   return G2Q_OK;
 }
 
@@ -1560,7 +1631,7 @@ size_t gemm_tc_workspace_bytes(long long M, long long N, long long K, long long 
 int gemm_tc_f32(float* C, long long ldc, long long sC, const float* A, long long lda,
                 long long sA, bool ta, const float* B, long long ldb, long long sB, bool tb,
                 long long M, long long N, long long K, long long batch, float alpha, float beta,
-                int mask, void* workspace, size_t workspace_bytes, cudaStream_t st) {
+                int mask, void* workspace, size_t workspace_bytes, int* status, cudaStream_t st) {
   if (M <= 0 || N <= 0 || batch <= 0) return G2Q_OK;
   if (K <= 0 || !tc::encode_fn() || (mask != G2Q_MASK_FULL && mask != G2Q_MASK_LOWER &&
                                      mask != G2Q_MASK_STRICT_UPPER))
@@ -1613,6 +1684,7 @@ int gemm_tc_f32(float* C, long long ldc, long long sC, const float* A, long long
             tc::make_map(&mp.b[1], b_lo, N, bb * lb.Kp, lb.ldo, true);
   if (!ok) return G2Q_ERR_UNSUPPORTED;
   tc::Params p{};
+  p.status = status;
   p.D = C; p.ldd = ldc; p.d_bs = sC;
   p.M = M; p.N = N;
   p.num_kb = (int)(la.Kp / tc::BK);
@@ -1737,7 +1809,7 @@ int split2h(const float* src, long long lds, long long n, int K, __half* hi, __h
 int tc_update2h(float* D, long long ldd, long long M, long long N, long long K,
                 __half* const* a2, const float* sa, long long lda, __half* const* b2,
                 const float* sb, long long ldb, int lower, float alpha, float beta,
-                cudaStream_t st) {
+                int* status, cudaStream_t st) {
   if (M <= 0 || N <= 0 || K <= 0 || !tc::encode_fn()) return G2Q_ERR_UNSUPPORTED;
   tc::Maps mp{};
   bool ok = true;
@@ -1746,6 +1818,7 @@ int tc_update2h(float* D, long long ldd, long long M, long long N, long long K,
          tc::make_map(&mp.b[i], b2[i], N, K, ldb, true);
   if (!ok) return G2Q_ERR_UNSUPPORTED;
   tc::Params p{};
+  p.status = status;
   p.D = D; p.ldd = ldd; p.d_bs = 0;
   p.M = M; p.N = N;
   p.num_kb = (int)((K + tc::BK - 1) / tc::BK);
@@ -1769,14 +1842,14 @@ extern "C" int g2q_gemm_tc(float* C, int64_t ldc, int64_t strideC, const float* 
                            int64_t strideA, int transA, const float* B, int64_t ldb,
                            int64_t strideB, int transB, int64_t M, int64_t N, int64_t K,
                            int64_t batch, float alpha, float beta, int out_mask, void* workspace,
-                           size_t workspace_bytes, void* stream) {
+                           size_t workspace_bytes, int* status, void* stream) {
   if (!C || (!A && K > 0) || (!B && K > 0) || M < 0 || N < 0 || K < 0 || batch < 0)
     return G2Q_ERR_INVALID_ARG;
   if (out_mask < 0 || out_mask > 3) return G2Q_ERR_INVALID_ARG;
   cudaStream_t st = (cudaStream_t)stream;
   const int s = g2q::gemm_tc_f32(C, ldc, strideC, A, lda, strideA, transA != 0, B, ldb, strideB,
                                  transB != 0, M, N, K, batch, alpha, beta, out_mask, workspace,
-                                 workspace_bytes, st);
+                                 workspace_bytes, status, st);
   if (s != G2Q_ERR_UNSUPPORTED) return s;
   // shapes TMA cannot describe, or the inclusive upper mask: fp32 CUDA cores
   g2q::SimtArgs a{};
@@ -1787,4 +1860,10 @@ extern "C" int g2q_gemm_tc(float* C, int64_t ldc, int64_t strideC, const float* 
   a.alpha = alpha; a.beta = beta;
   a.mask = out_mask;
   return g2q::simt_gemm(a, transA != 0, transB != 0, G2Q_DTYPE_F32, G2Q_DTYPE_F32, batch, st);
+}
+
+extern "C" int64_t g2q_set_wait_limit(int64_t cycles) {
+  const long long prev = g2q::tc::g_wait_cycles;
+  g2q::tc::g_wait_cycles = cycles > 0 ? cycles : g2q::tc::kWaitCycles;
+  return prev;
 }

@@ -25,7 +25,7 @@ namespace g2q {
 int tc_gram(float* D, long long ldd, long long M, long long N, const void* A, int a_dtype,
             long long lda, const void* B, int b_dtype, long long ldb, const float* row_scale,
             long long scale_stride, long long T, int symmetric, float alpha, float beta,
-            void* workspace, size_t workspace_bytes, cudaStream_t st);
+            void* workspace, size_t workspace_bytes, int* status, cudaStream_t st);
 size_t tc_gram_workspace_bytes(long long M, long long N, long long T);
 
 static __device__ __align__(256) unsigned char gram_scratch[G2Q_GRAM_STATIC_SCRATCH_BYTES];
@@ -34,12 +34,16 @@ constexpr int kMaxDevices = 64;
 static std::mutex scratch_mu;
 static void* scratch_ptr[kMaxDevices];
 
-// Device address of gram_scratch on the current device, looked up once per
-// device.  The first call on a device does this set-up (it loads the module
-// there); make it before any stream capture.
-static int scratch_for_current_device(void** out) {
-  int dev = -1;
+// Device address of gram_scratch on the stream's device, looked up once per
+// device.  That device must be the current one (the symbol is resolved and
+// the kernels launched there); a stream of another device is rejected.  The
+// first call on a device does this set-up (it loads the module there); make
+// it before any stream capture.
+static int scratch_for_stream(cudaStream_t st, void** out) {
+  int dev = -1, sdev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return G2Q_ERR_CUDA;
+  if (cudaStreamGetDevice(st, &sdev) != cudaSuccess) return G2Q_ERR_INVALID_ARG;
+  if (sdev != dev) return G2Q_ERR_INVALID_ARG;
   std::lock_guard<std::mutex> lock(scratch_mu);
   if (!scratch_ptr[dev]) {
     void* p = nullptr;
@@ -58,7 +62,7 @@ extern "C" int g2q_gram_update_noalloc(float* D, int64_t ldd, int64_t M, int64_t
                                        const void* A, int a_dtype, int64_t lda, const void* B,
                                        int b_dtype, int64_t ldb, const float* row_scale,
                                        int64_t scale_stride, int64_t T, int symmetric,
-                                       float alpha, float beta, void* stream) {
+                                       float alpha, float beta, int* status, void* stream) {
   if (!D || !A || !B || M <= 0 || N <= 0 || T < 0 || lda < M || ldb < N || ldd < N)
     return G2Q_ERR_INVALID_ARG;
   if ((a_dtype != G2Q_DTYPE_BF16 && a_dtype != G2Q_DTYPE_F32) ||
@@ -73,8 +77,8 @@ extern "C" int g2q_gram_update_noalloc(float* D, int64_t ldd, int64_t M, int64_t
   if (split && g2q::tc_gram_workspace_bytes(M, N, T) > (size_t)G2Q_GRAM_STATIC_SCRATCH_BYTES)
     return G2Q_ERR_SCRATCH_LIMIT;
   void* scratch = nullptr;
-  G2Q_TRY(g2q::scratch_for_current_device(&scratch));
+  G2Q_TRY(g2q::scratch_for_stream((cudaStream_t)stream, &scratch));
   return g2q::tc_gram(D, ldd, M, N, A, a_dtype, lda, B, b_dtype, ldb, row_scale, scale_stride,
                       T, symmetric, alpha, beta, scratch,
-                      (size_t)G2Q_GRAM_STATIC_SCRATCH_BYTES, (cudaStream_t)stream);
+                      (size_t)G2Q_GRAM_STATIC_SCRATCH_BYTES, status, (cudaStream_t)stream);
 }

@@ -11,12 +11,12 @@ namespace g2q {
 int tc_gram_grouped(float* D, long long ldd, long long d_gstride, long long C, const void* X,
                     int x_dtype, long long ldx, const float* s, long long sstride, int G,
                     long long T, float alpha, float beta, void* workspace,
-                    size_t workspace_bytes, cudaStream_t st);
+                    size_t workspace_bytes, int* status, cudaStream_t st);
 size_t tc_gram_grouped_workspace_bytes(long long C, long long T, int G);
 int tc_gram(float* D, long long ldd, long long M, long long N, const void* A, int a_dtype,
             long long lda, const void* B, int b_dtype, long long ldb, const float* row_scale,
             long long scale_stride, long long T, int symmetric, float alpha, float beta,
-            void* workspace, size_t workspace_bytes, cudaStream_t st);
+            void* workspace, size_t workspace_bytes, int* status, cudaStream_t st);
 size_t tc_gram_workspace_bytes(long long M, long long N, long long T);
 
 static int grid_for(long long n, int threads = 256) {
@@ -293,7 +293,7 @@ void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 using namespace g2q;
 
-extern "C" int g2q_abi_version(void) { return 6; }
+extern "C" int g2q_abi_version(void) { return 7; }
 
 extern "C" int64_t g2q_launch_count(void) { return g2q::g_launches.load(); }
 
@@ -377,7 +377,7 @@ extern "C" int g2q_gram_update_grouped(float* D, int64_t ldd, int64_t d_gstride,
                                        const void* X, int x_dtype, int64_t ldx, const float* s,
                                        int64_t sstride, int G, int64_t T, float alpha, float beta,
                                        int precision, void* workspace, size_t workspace_bytes,
-                                       void* stream) {
+                                       int* status, void* stream) {
   if (!D || !X || !s || C <= 0 || T < 0 || G <= 0 || ldx < C || ldd < C || sstride < G ||
       d_gstride < C * ldd)
     return G2Q_ERR_INVALID_ARG;
@@ -385,11 +385,11 @@ extern "C" int g2q_gram_update_grouped(float* D, int64_t ldd, int64_t d_gstride,
   cudaStream_t st = (cudaStream_t)stream;
   if (precision == 1)
     return tc_gram_grouped(D, ldd, d_gstride, C, X, x_dtype, ldx, s, sstride, G, T, alpha, beta,
-                           workspace, workspace_bytes, st);
+                           workspace, workspace_bytes, status, st);
   if (precision != 0) return G2Q_ERR_INVALID_ARG;
   for (int g = 0; g < G; ++g)
     G2Q_TRY(g2q_gram_update(D + g * d_gstride, ldd, C, C, X, x_dtype, ldx, X, x_dtype, ldx, s + g,
-                            sstride, T, 1, alpha, beta, 0, nullptr, 0, stream));
+                            sstride, T, 1, alpha, beta, 0, nullptr, 0, status, stream));
   return G2Q_OK;
 }
 
@@ -402,7 +402,8 @@ extern "C" int g2q_gram_update(float* D, int64_t ldd, int64_t M, int64_t N, cons
                                int a_dtype, int64_t lda, const void* B, int b_dtype,
                                int64_t ldb, const float* row_scale, int64_t scale_stride,
                                int64_t T, int symmetric, float alpha, float beta, int precision,
-                               void* workspace, size_t workspace_bytes, void* stream) {
+                               void* workspace, size_t workspace_bytes, int* status,
+                               void* stream) {
   if (!D || !A || !B || M <= 0 || N <= 0 || T < 0 || lda < M || ldb < N || ldd < N)
     return G2Q_ERR_INVALID_ARG;
   if ((a_dtype != G2Q_DTYPE_BF16 && a_dtype != G2Q_DTYPE_F32) ||
@@ -412,7 +413,7 @@ extern "C" int g2q_gram_update(float* D, int64_t ldd, int64_t M, int64_t N, cons
   cudaStream_t st = (cudaStream_t)stream;
   if (precision == 1)
     return tc_gram(D, ldd, M, N, A, a_dtype, lda, B, b_dtype, ldb, row_scale, scale_stride, T,
-                   symmetric, alpha, beta, workspace, workspace_bytes, st);
+                   symmetric, alpha, beta, workspace, workspace_bytes, status, st);
   if (precision != 0) return G2Q_ERR_INVALID_ARG;
   SimtArgs a{};
   a.A = A; a.B = B; a.C = D;

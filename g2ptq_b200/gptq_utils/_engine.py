@@ -149,6 +149,17 @@ def factor_with_retry(H, percdamp, info=None):
     return U, info, damps
 
 
+def raise_device_errors(info, statuses):
+    """Raise for device conditions other than a failed pivot: a tensor-core
+    wait that gave up (in a Cholesky ``info`` or a status word) and a
+    non-positive quantization scale (``find_params``)."""
+    if any(s == _lib.G2Q_ERR_TIMEOUT for s in list(info) + list(statuses)):
+        raise RuntimeError("g2ptq_b200: a tensor-core pipeline wait timed out "
+                           f"({_lib.status_string(_lib.G2Q_ERR_TIMEOUT)})")
+    if any(s != 0 for s in statuses):
+        raise RuntimeError("WeightQuantizer.find_params: non-positive scale")
+
+
 def retry_failed(H, U, info_list, damps):
     """Re-factor failing layers with the damp auto-increment."""
     for b, inf in enumerate(info_list):
@@ -163,7 +174,9 @@ def retry_failed(H, U, info_list, damps):
                 raise ValueError(
                     f"Quantization: `damp_percent` must between 0 and 1. current is {d}")
             Ub, ib = ops.chol_upper_inverse(H[b:b + 1].contiguous(), [d], precision=PRECISION)
-            if int(ib.item()) == 0:
+            code = int(ib.item())
+            raise_device_errors([code], [])
+            if code == 0:
                 U[b].copy_(Ub[0])
                 break
         damps[b] = d
@@ -567,9 +580,16 @@ class Pending:
         self.borrowed_factor = borrowed_factor
         self.nan, self.outs, self.codes = run(W0.clone())
 
+    def _flags(self):
+        """One device-to-host read: per-layer Cholesky info, the NaN count and
+        the status words (the device's tensor-core word, then the parameters')."""
+        return sync_check(self.info, self.nan, ops.device_status(self.U.device),
+                          *self.params.statuses())
+
     def finish(self):
         nl = self.nl
-        flags = sync_check(self.info, self.nan, *self.params.statuses())
+        flags = self._flags()
+        raise_device_errors(flags[:nl], flags[nl + 1:])
         if any(i != 0 for i in flags[:nl]):
             if self.borrowed_factor:
                 torch.cuda.synchronize(self.U.device)  # the owner's re-factored U
@@ -577,10 +597,9 @@ class Pending:
                 retry_failed(self.H, self.U, flags[:nl], self.damps)
             self.params.status.zero_()
             self.nan, self.outs, self.codes = self.run(self.W0.clone())
-            flags = sync_check(self.info, self.nan, *self.params.statuses())
+            flags = self._flags()
             flags[:nl] = [0] * nl
-        if any(f != 0 for f in flags[nl + 1:]):
-            raise RuntimeError("WeightQuantizer.find_params: non-positive scale")
+            raise_device_errors(flags[:nl], flags[nl + 1:])
         if flags[nl] != 0:
             raise ValueError("NaN in weights")
         if self.dynamic:

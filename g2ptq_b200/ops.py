@@ -55,6 +55,25 @@ def workspace(nbytes, device):
     return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device)
 
 
+_DEVICE_STATUS = {}
+
+
+def device_status(device):
+    """The status word (device int32 [1]) that tensor-core launches without a
+    caller-given one report to: G2Q_ERR_TIMEOUT when a pipeline wait gave up.
+    ``fasterquant`` reads it with its other status words and raises."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    t = _DEVICE_STATUS.get(idx)
+    if t is None:
+        t = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        _DEVICE_STATUS[idx] = t
+    return t
+
+
+def _status(status, device):
+    return (device_status(device) if status is None else status).data_ptr()
+
+
 # --------------------------------------------------------------------------
 # Hessian accumulation
 # --------------------------------------------------------------------------
@@ -70,8 +89,10 @@ def stage_tokens(dst, row0, src, sub=None):
 
 
 def gram_update(D, A, B=None, row_scale=None, alpha=1.0, beta=1.0, symmetric=None,
-                precision=0):
-    """``D <- alpha D + beta A^T diag(s) B`` for token-major ``A [T, M]``, ``B [T, N]``."""
+                precision=0, status=None):
+    """``D <- alpha D + beta A^T diag(s) B`` for token-major ``A [T, M]``, ``B [T, N]``.
+    ``status``: device int32 word for a tensor-core timeout (default: the
+    device's, ``device_status``)."""
     if B is None:
         B = A
     _cuda(D, A, B, row_scale)
@@ -87,10 +108,10 @@ def gram_update(D, A, B=None, row_scale=None, alpha=1.0, beta=1.0, symmetric=Non
     call("g2q_gram_update", D.data_ptr(), D.stride(0), M, N, A.data_ptr(), dtype_code(A.dtype),
          A.stride(0), B.data_ptr(), dtype_code(B.dtype), B.stride(0), _ptr(row_scale), sstride,
          T, int(bool(symmetric)), float(alpha), float(beta), precision, _ptr(ws), ws_bytes,
-         _stream(D))
+         _status(status, D.device), _stream(D))
 
 
-def gram_update_grouped(D, X, scales, alpha=1.0, beta=1.0, precision=0):
+def gram_update_grouped(D, X, scales, alpha=1.0, beta=1.0, precision=0, status=None):
     """``D[g] <- alpha D[g] + beta X^T diag(scales[:, g]) X`` for every row group g:
     ``D [G, C, C]`` contiguous, ``X [T, C]`` token-major, ``scales [T, G]``."""
     _cuda(D, X, scales)
@@ -105,7 +126,8 @@ def gram_update_grouped(D, X, scales, alpha=1.0, beta=1.0, precision=0):
     ws = workspace(ws_bytes, D.device) if ws_bytes else None
     call("g2q_gram_update_grouped", D.data_ptr(), D.stride(1), D.stride(0), C, X.data_ptr(),
          dtype_code(X.dtype), X.stride(0), scales.data_ptr(), scales.stride(0), G, T,
-         float(alpha), float(beta), precision, _ptr(ws), ws_bytes, _stream(D))
+         float(alpha), float(beta), precision, _ptr(ws), ws_bytes, _status(status, D.device),
+         _stream(D))
 
 
 def sq_colsum(acc, X, keep, scale):
@@ -121,7 +143,7 @@ def sq_colsum(acc, X, keep, scale):
 # --------------------------------------------------------------------------
 
 def gemm(C, A, B, transA=False, transB=False, alpha=0.0, beta=1.0, mask=_lib.MASK_FULL,
-         precision=0):
+         precision=0, status=None):
     """Batched ``C <- alpha C + beta op(A) op(B)`` on fp32 ``[batch, *, *]`` tensors
     (precision 0: fp32 CUDA cores; 1: tensor cores with fp16 hi/lo operands)."""
     _cuda(C, A, B)
@@ -138,7 +160,8 @@ def gemm(C, A, B, transA=False, transB=False, alpha=0.0, beta=1.0, mask=_lib.MAS
         ws = workspace(nbytes, C.device)
         call("g2q_gemm_tc", C.data_ptr(), C.stride(1), C.stride(0), A.data_ptr(), A.stride(1),
              sA, int(transA), B.data_ptr(), B.stride(1), sB, int(transB), M, N, K, batch,
-             float(alpha), float(beta), mask, ws.data_ptr(), nbytes, _stream(C))
+             float(alpha), float(beta), mask, ws.data_ptr(), nbytes, _status(status, C.device),
+             _stream(C))
         return C
     call("g2q_gemm", C.data_ptr(), C.stride(1), C.stride(0), A.data_ptr(), A.stride(1), sA,
          int(transA), B.data_ptr(), B.stride(1), sB, int(transB), M, N, K, batch, float(alpha),
@@ -150,7 +173,8 @@ def chol_upper_inverse(H, damp_percent, info=None, precision=0):
     """``U`` with ``U^T U = (H + d I)^-1`` per batch entry; returns ``(U, info)``.
 
     ``damp_percent`` is a float or a sequence (one per batch entry);
-    ``info`` (device int32 [B]) receives 0 / failing pivot / -1 for NaN.
+    ``info`` (device int32 [B]) receives 0 / failing pivot / -1 for NaN /
+    ``G2Q_ERR_TIMEOUT`` when a tensor-core wait gave up.
     """
     _cuda(H)
     _contig(H)

@@ -8,7 +8,10 @@
  * memory and never synchronise the device: callers pass the scratch space a
  * call needs (the *_workspace_bytes queries give its size).  Conditions that
  * are only known on the device (a non-positive Cholesky pivot, a NaN, a zero
- * quantization scale) are written to caller-provided device int words.
+ * quantization scale, a tensor-core pipeline wait that gave up) are written
+ * to caller-provided device int words (`status`, `info`); a status word is
+ * only ever changed from 0 to the first code recorded, so one word can collect
+ * the outcome of many calls, and a NULL status discards it.
  *
  * Matrices are row-major fp32 unless stated.  "Token-major" activations are
  * [T, C] with the channel index contiguous, exactly as a linear layer's input
@@ -62,6 +65,14 @@ extern "C" {
 /* ABI version; bumped on any signature change. */
 int g2q_abi_version(void);
 
+/* Bound, in SM clock cycles, of every pipeline wait of the tensor-core
+ * kernels launched after this call (cycles <= 0 restores the default of
+ * 4e9, about two seconds); returns the previous bound.  A wait that runs out
+ * records G2Q_ERR_TIMEOUT in the call's status word and the kernel winds down
+ * without trapping, so the CUDA context stays usable.  No counterpart in the
+ * reference, whose products run in cuBLAS. */
+int64_t g2q_set_wait_limit(int64_t cycles);
+
 /* Number of kernels this library has launched in the process so far
  * (host-side count of successful launch calls). */
 int64_t g2q_launch_count(void);
@@ -90,6 +101,8 @@ int g2q_stage_tokens(void* dst, int dst_dtype, int64_t dst_ld, int64_t row0,
  * a full symmetric D.  precision: 0 = fp32 CUDA cores, 1 = tensor cores
  * (bf16 operands exact for BF16 input; FP32 input split into bf16 hi/lo
  * pairs), which needs `workspace` of g2q_gram_workspace_bytes bytes.
+ * `status` (device int, may be NULL) receives G2Q_ERR_TIMEOUT when a
+ * tensor-core pipeline wait gives up (D is then incomplete).
  * Replaces the Hessian products of GPTQ.add_batch (gptq_utils/gptq_utils.py:123-126),
  * G2PTQ.add_batch (gptq_utils/g2ptq_utils.py:193-200), GPTAQ.add_batch
  * (gptq_utils/gptaq_utils.py:139-146) and GPTQGuided.add_batch
@@ -99,7 +112,7 @@ int g2q_gram_update(float* D, int64_t ldd, int64_t M, int64_t N,
                     const void* B, int b_dtype, int64_t ldb,
                     const float* row_scale, int64_t scale_stride,
                     int64_t T, int symmetric, float alpha, float beta, int precision,
-                    void* workspace, size_t workspace_bytes, void* stream);
+                    void* workspace, size_t workspace_bytes, int* status, void* stream);
 size_t g2q_gram_workspace_bytes(int64_t M, int64_t N, int64_t T, int precision);
 
 /* Row-scaled Gram updates of G row groups in one call, for g < G:
@@ -109,7 +122,8 @@ size_t g2q_gram_workspace_bytes(int64_t M, int64_t N, int64_t T, int precision);
  * s[t, g] = s[t * sstride + g].  Each group's result is that of
  * g2q_gram_update(..., row_scale = s + g, symmetric = 1); at precision 1 BF16
  * tokens are split for all groups in one pass and the G products run as one
- * launch (workspace: g2q_gram_grouped_workspace_bytes).
+ * launch (workspace: g2q_gram_grouped_workspace_bytes).  `status` as for
+ * g2q_gram_update.
  * Replaces the per-group saliency-weighted products of G2PTQ.add_batch
  * (gptq_utils/g2ptq_utils.py:193-200) and GPTQGuided.add_batch
  * (gptq_utils/gptq_guided_utils.py:78-80). */
@@ -117,7 +131,8 @@ int g2q_gram_update_grouped(float* D, int64_t ldd, int64_t d_gstride, int64_t C,
                             const void* X, int x_dtype, int64_t ldx,
                             const float* s, int64_t sstride, int G, int64_t T,
                             float alpha, float beta, int precision,
-                            void* workspace, size_t workspace_bytes, void* stream);
+                            void* workspace, size_t workspace_bytes, int* status,
+                            void* stream);
 size_t g2q_gram_grouped_workspace_bytes(int64_t C, int64_t T, int G, int precision);
 
 /* g2q_gram_update at precision 1 (tensor cores) without caller-provided
@@ -127,17 +142,21 @@ size_t g2q_gram_grouped_workspace_bytes(int64_t C, int64_t T, int G, int precisi
  * g2q_gram_workspace_bytes(M, N, T, 1) above that size return
  * G2Q_ERR_SCRATCH_LIMIT (e.g. T = 1024 tokens at C = 4096 fits; split longer
  * token runs into several calls with alpha = 1 after the first).  BF16 inputs
- * without row scale use no scratch.  The first call on a device looks the
- * array up (set-up; make it before any stream capture).  One array per
- * device: calls that overlap in time (several streams or host threads) race
- * on it; calls on one stream are safe.  No counterpart in the reference,
- * whose add_batch products allocate through torch. */
+ * without row scale use no scratch.  The array used is the one of `stream`'s
+ * device, which must be the current device (a stream of another device
+ * returns G2Q_ERR_INVALID_ARG).  The first call on a device looks the array
+ * up (set-up; make it before any stream capture).  One array per device:
+ * calls that overlap in time (several streams or host threads) race on it;
+ * calls on one stream are safe.  `status` as for g2q_gram_update.  No
+ * counterpart in the reference, whose add_batch products allocate through
+ * torch. */
 #define G2Q_GRAM_STATIC_SCRATCH_BYTES (40u << 20)
 int g2q_gram_update_noalloc(float* D, int64_t ldd, int64_t M, int64_t N,
                             const void* A, int a_dtype, int64_t lda,
                             const void* B, int b_dtype, int64_t ldb,
                             const float* row_scale, int64_t scale_stride,
-                            int64_t T, int symmetric, float alpha, float beta, void* stream);
+                            int64_t T, int symmetric, float alpha, float beta, int* status,
+                            void* stream);
 size_t g2q_gram_static_scratch_bytes(void);
 
 /* Adds sum_t x[t, c]^2 * scale to acc[c] after acc *= keep: the running mean
@@ -162,13 +181,14 @@ int g2q_gemm(float* C, int64_t ldc, int64_t strideC,
  * a power of two, three products per K step, fp32 accumulation.  out_mask
  * G2Q_MASK_UPPER falls back to the CUDA-core kernel.  Needs
  * g2q_gemm_tc_workspace_bytes(M, N, K, batch, strideA != 0, strideB != 0)
- * bytes of workspace.  Replaces the same fasterquant products as g2q_gemm. */
+ * bytes of workspace.  `status` as for g2q_gram_update.  Replaces the same
+ * fasterquant products as g2q_gemm. */
 int g2q_gemm_tc(float* C, int64_t ldc, int64_t strideC,
                 const float* A, int64_t lda, int64_t strideA, int transA,
                 const float* B, int64_t ldb, int64_t strideB, int transB,
                 int64_t M, int64_t N, int64_t K, int64_t batch,
                 float alpha, float beta, int out_mask,
-                void* workspace, size_t workspace_bytes, void* stream);
+                void* workspace, size_t workspace_bytes, int* status, void* stream);
 size_t g2q_gemm_tc_workspace_bytes(int64_t M, int64_t N, int64_t K, int64_t batch,
                                    int a_batched, int b_batched);
 
@@ -176,7 +196,8 @@ size_t g2q_gemm_tc_workspace_bytes(int64_t M, int64_t N, int64_t K, int64_t batc
  * symmetric, row stride ldh, batch stride C*ldh) computes upper-triangular
  * U[b] with U^T U = (H + d I)^-1, d = damp_percent[b] * mean(diag H[b]).
  * info[b] (device int) receives 0, the 1-based index of the first
- * non-positive pivot, or -1 when the factor holds a NaN.  Route: UL
+ * non-positive pivot, -1 when the factor holds a NaN, or G2Q_ERR_TIMEOUT when
+ * a tensor-core pipeline wait of the chain gave up.  Route: UL
  * factorization H + dI = V V^T (V upper), U = V^-1 -- potrf + trtri, half the
  * work of potrf + potri + potrf.  precision: 0 = fp32 CUDA cores, 1 = trailing
  * updates on tensor cores with a three-term bf16 split (fp32-level accuracy).

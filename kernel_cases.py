@@ -1,12 +1,12 @@
 """Single-kernel cases of the quantization hot path, for timing and profiling.
 
-    python -m g2ptq_b200.kernel_cases gram --tokens 16384 --columns 4096
-    python -m g2ptq_b200.kernel_cases gram_weighted --tokens 16384 --columns 4096
-    python -m g2ptq_b200.kernel_cases chol --columns 4096
-    python -m g2ptq_b200.kernel_cases compensate --rows 4096 --columns 4096
-    python -m g2ptq_b200.kernel_cases block_loss --tokens 2048 --vocab 128256 --loss kl
-    python -m g2ptq_b200.kernel_cases saliency --tokens 8192 --rows 14336
-    python -m g2ptq_b200.kernel_cases running_mean --rows 14336 --columns 4096
+    python kernel_cases.py gram --tokens 16384 --columns 4096
+    python kernel_cases.py gram_weighted --tokens 16384 --columns 4096
+    python kernel_cases.py chol --columns 4096
+    python kernel_cases.py compensate --rows 4096 --columns 4096
+    python kernel_cases.py block_loss --tokens 2048 --vocab 128256 --loss kl
+    python kernel_cases.py saliency --tokens 8192 --rows 14336
+    python kernel_cases.py running_mean --rows 14336 --columns 4096
 
 Each case builds seeded synthetic inputs of one fold / one factorization /
 one compensation pass of a Llama-3-8B linear on ``cuda:0``, runs ``--warmup``
@@ -21,7 +21,7 @@ import json
 
 import torch
 
-from . import ops, _lib
+from g2ptq_b200 import ops, _lib
 
 
 def _time(fn, warmup, reps):

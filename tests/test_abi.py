@@ -74,3 +74,16 @@ def test_workspace_queries(lib):
     from g2ptq_b200 import _lib
     assert _lib.query("g2q_chol_workspace_bytes", 4096) >= 2 * 4096 * 4096 * 4
     assert _lib.query("g2q_compensate_workspace_bytes", 0, 1, 4096, 4096, 0) >= 4096 * 128 * 4
+
+
+def test_wait_limit_is_settable_on_the_host(lib):
+    # host-side setting read by every tensor-core launch; no GPU call here
+    default = 4_000_000_000
+    prev = lib.g2q_set_wait_limit(1000)
+    try:
+        assert prev == default
+        assert lib.g2q_set_wait_limit(0) == 1000  # 0 restores the default
+        assert lib.g2q_set_wait_limit(-5) == default
+    finally:
+        lib.g2q_set_wait_limit(0)
+    assert lib.g2q_set_wait_limit(0) == default

@@ -38,23 +38,23 @@ def ptr(t):
     return ctypes.c_void_p(0 if t is None else t.data_ptr())
 
 
-def existing(lib, D, A, B, s, sym, alpha, beta):
+def existing(lib, D, A, B, s, sym, alpha, beta, status=None):
     T, M = A.shape
     N = B.shape[1]
     nbytes = lib.g2q_gram_workspace_bytes(M, N, T, 1)
     ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=DEV)
     return lib.g2q_gram_update(ptr(D), D.stride(0), M, N, ptr(A), code(A), A.stride(0), ptr(B),
                                code(B), B.stride(0), ptr(s), 0 if s is None else s.stride(0), T,
-                               int(sym), alpha, beta, 1, ptr(ws), nbytes, stream())
+                               int(sym), alpha, beta, 1, ptr(ws), nbytes, ptr(status), stream())
 
 
-def noalloc(lib, D, A, B, s, sym, alpha, beta):
+def noalloc(lib, D, A, B, s, sym, alpha, beta, status=None):
     T, M = A.shape
     N = B.shape[1]
     return lib.g2q_gram_update_noalloc(ptr(D), D.stride(0), M, N, ptr(A), code(A), A.stride(0),
                                        ptr(B), code(B), B.stride(0), ptr(s),
                                        0 if s is None else s.stride(0), T, int(sym), alpha, beta,
-                                       stream())
+                                       ptr(status), stream())
 
 
 @pytest.mark.parametrize("case", ["f32_sym", "bf16_scaled", "f32_cross", "bf16_plain"])
@@ -66,6 +66,7 @@ def test_noalloc_matches_existing_two_calls(case):
     D0 = D0 + D0.T
     D_ref, D_new = D0.clone(), D0.clone()
     expect = D0.double()
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
     for step, alpha in enumerate((0.5, 1.0)):
         X = torch.randn(T, C, device=DEV, generator=g)
         X[:, 3] *= 20
@@ -84,10 +85,11 @@ def test_noalloc_matches_existing_two_calls(case):
             Y = X
         beta = 2.0 / (step + 3)
         assert existing(lib, D_ref, Y, X, s, sym, alpha, beta) == 0
-        assert noalloc(lib, D_new, Y, X, s, sym, alpha, beta) == 0
+        assert noalloc(lib, D_new, Y, X, s, sym, alpha, beta, status) == 0
         w = torch.ones(T, device=DEV, dtype=torch.float64) if s is None else s.double()
         expect = alpha * expect + beta * (Y.double().T @ (X.double() * w[:, None]))
     torch.cuda.synchronize()
+    assert int(status.item()) == 0  # no tensor-core wait gave up
     assert rel_fro(D_new, D_ref) < TOL
     assert rel_fro(D_new, expect) < TOL
     assert torch.isfinite(D_new).all()
