@@ -484,49 +484,73 @@ def native_e2e(torch, dist, args, layers, world, rank, dev, n_local, dev_acts, g
 
 
 # ---------------------------------------------------------------------------
-# CPU baseline / reference arm: the numpy oracle of the reference's torch path
+# CPU baseline / reference arm: the reference's torch path on the host cores
 # ---------------------------------------------------------------------------
 
-SAMPLE_TOKENS = 8192
-SAMPLE_LINEAR = (1024, 4096)  # k_proj-shaped sample: rows x columns
+SAMPLE_ROWS = 4096
 
 
-def cpu_sample(threads=None):
-    """Time the oracle pipeline on one k_proj-shaped linear with 4 sequences of
-    2048 tokens, then scale each stage to the full step (Hessian by T*C^2,
-    factorization by C^3, compensation by R*C^2) -> seconds per step."""
-    from oracle import compensation as comp, fasterquant as fq, hessian
-    rows, cols = SAMPLE_LINEAR
-    rng = np.random.default_rng(0)
-    W = (rng.standard_normal((1, rows, cols)) * 0.02).astype(np.float32)
-    X = rng.standard_normal((SAMPLE_TOKENS, cols)).astype(np.float32)
-    X[:, :4] *= 20
-    t0 = time.perf_counter()
-    H = np.zeros((cols, cols), np.float32)
-    n = 0
-    for s in range(0, SAMPLE_TOKENS, 2048):
-        H, n = hessian.gptq_add_batch(H, n, X[None, s:s + 2048])
-    t_hess = time.perf_counter() - t0
-    t0 = time.perf_counter()
-    qz = comp.make_group_quantizers(comp.Quantizer(BITS, True), cols, GROUPSIZE)
-    fq.gptq_fasterquant(W, H[None], qz, BLOCKSIZE, PERCDAMP, GROUPSIZE, True, True)
-    t_fq = time.perf_counter() - t0
-    total_tokens = 128 * 2048
-    hess_units = sum(total_tokens * c * c for _, r, c, _ in LINEARS)
-    comp_units = sum(r * c * c for _, r, c, _ in LINEARS)
-    step_s = (t_hess * hess_units / (SAMPLE_TOKENS * cols * cols) +
-              t_fq * comp_units / (rows * cols * cols))
-    return step_s, t_hess + t_fq
+def cpu_threads():
+    """All host threads this process may use, set explicitly (torchrun exports
+    OMP_NUM_THREADS=1 to its workers)."""
+    import torch
+    n = len(os.sched_getaffinity(0))
+    torch.set_num_threads(n)
+    return torch.get_num_threads()
+
+
+def cpu_sample():
+    """Time the reference's torch operations (``oracle/torch_port.py``) on the
+    host cores at the step's two column counts: one 2048-token ``add_batch``
+    call at C = 4096 and at C = 14336, and ``fasterquant`` (W4 sym g128,
+    act-order, static groups) of a 4096-row linear on each resulting Hessian.
+    The step is assembled from the stages: 768 add_batch calls at C = 4096
+    (q/k/v/o/gate/up x 128 sequences) and 128 at C = 14336 (down), one
+    factorization per linear, the compensation scaled by rows (38912 rows at
+    C = 4096, 4096 at C = 14336), the rest of fasterquant (parameters, dead
+    columns, permutations) once per linear.  -> (seconds per step, parts)."""
+    import torch
+    from oracle import torch_port as tp
+    threads = cpu_threads()
+    g = torch.Generator().manual_seed(0)
+    parts, wall0 = {}, time.perf_counter()
+    for C in (HIDDEN, INTER):
+        X = torch.randn(1, 2048, C, generator=g)
+        X[..., :4] *= 20.0
+        X = X.to(torch.bfloat16)
+        t0 = time.perf_counter()
+        H, _ = tp.add_batch(torch.zeros(C, C), 0, X)
+        parts[f"add_batch_c{C}"] = time.perf_counter() - t0
+        W = (torch.randn(1, SAMPLE_ROWS, C, generator=g) * 0.02).to(torch.bfloat16)
+        tim = {}
+        t0 = time.perf_counter()
+        tp.fasterquant(W, H[None], BITS, True, GROUPSIZE, True, True, PERCDAMP, BLOCKSIZE,
+                       timings=tim)
+        total = time.perf_counter() - t0
+        parts[f"factor_c{C}"] = tim["factor"]
+        parts[f"compensate_r{SAMPLE_ROWS}_c{C}"] = tim["compensate"]
+        parts[f"other_c{C}"] = total - tim["factor"] - tim["compensate"]
+    step = 0.0
+    seqs = 128
+    for name, rows, cols, _ in LINEARS:
+        step += seqs * parts[f"add_batch_c{cols}"]
+        step += parts[f"factor_c{cols}"] + parts[f"other_c{cols}"]
+        step += parts[f"compensate_r{SAMPLE_ROWS}_c{cols}"] * rows / SAMPLE_ROWS
+    return step, parts, time.perf_counter() - wall0, threads
+
+
+def _sample_text(parts, wall):
+    p = ", ".join(f"{k} {v:.3f} s" for k, v in parts.items())
+    return (f"reference torch ops on the host (oracle/torch_port.py): one 2048-token add_batch "
+            f"call and fasterquant of a 4096-row linear at C=4096 and C=14336 ({wall:.1f} s: "
+            f"{p}); step = 128 add_batch calls per linear + one fasterquant per linear, "
+            f"compensation scaled by rows")
 
 
 def cpu_baseline():
-    step_s, wall = cpu_sample()
+    step_s, parts, wall, threads = cpu_sample()
     return {"value": round(len(LINEARS) / step_s, 6), "unit": "linears/s",
-            "cores": os.cpu_count(), "kind": "port",
-            "sample": f"numpy oracle of the reference torch path: one {SAMPLE_LINEAR[0]}x"
-                      f"{SAMPLE_LINEAR[1]} linear, {SAMPLE_TOKENS} tokens, add_batch + "
-                      f"fasterquant ({wall:.1f} s), scaled per stage to the 7-linear, "
-                      f"262144-token step"}
+            "cores": threads, "kind": "port", "sample": _sample_text(parts, wall)}
 
 
 def reference(args):
@@ -536,12 +560,10 @@ def reference(args):
         return
     for _ in range(args.warmup):
         cpu_sample()
-    vals = []
-    walls = []
+    vals, parts, wall, threads = [], None, 0.0, 1
     for _ in range(args.steps):
-        s, w = cpu_sample()
+        s, parts, wall, threads = cpu_sample()
         vals.append(s)
-        walls.append(w)
     step_s = float(np.mean(vals))
     value = len(LINEARS) / step_s
     line = {"impl": "reference", "metric": METRIC, "value": round(value, 6),
@@ -550,10 +572,8 @@ def reference(args):
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": "Llama-3-8B decoder layer (7 linears) GPTQ W4 sym g128 "
                                    "act-order, 128x2048 calibration tokens"},
-            "cpu_baseline": {"value": round(value, 6), "unit": "linears/s",
-                             "cores": os.cpu_count(), "kind": "port",
-                             "sample": "one 1024x4096 linear, 8192 tokens per step, scaled "
-                                       "per stage to the full step"},
+            "cpu_baseline": {"value": round(value, 6), "unit": "linears/s", "cores": threads,
+                             "kind": "port", "sample": _sample_text(parts, wall)},
             "e2e": {"value": round(value, 6), "unit": "linears/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)

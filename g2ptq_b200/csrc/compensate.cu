@@ -30,8 +30,6 @@ struct BlockParams {
   long long lde, e_bs;
   float* erra;  // optional trailing-update operand, column-major (ldea, ea_bs)
   long long ldea, ea_bs;
-  __nv_bfloat16* erra_hi;  // optional split copy of erra (same layout)
-  __nv_bfloat16* erra_lo;
   const float* z;  // G2PTQ, row-major (ldz, z_bs)
   float* gh;
   long long ldz, z_bs;
@@ -308,12 +306,6 @@ __global__ void __launch_bounds__(BlockCfg::THREADS, 2) block_kernel(BlockParams
     if (P.err) P.err[(long long)b * P.e_bs + (long long)i * P.lde + rq] = e;
     const long long ao = (long long)b * P.ea_bs + (long long)i * P.ldea + rq;
     if (P.erra) P.erra[ao] = ea;
-    if (P.erra_hi) {
-      __nv_bfloat16 h, l;
-      split_bf16(ea, &h, &l);
-      P.erra_hi[ao] = h;
-      P.erra_lo[ao] = l;
-    }
   }
 }
 
@@ -703,32 +695,23 @@ extern "C" int g2q_compensate_block(int method, float* W, int64_t ldw, int64_t w
 }
 
 
+namespace g2q {
+size_t gemm_tc_workspace_bytes(long long M, long long N, long long K, long long batch_a,
+                               long long batch_b);
+int gemm_tc_f32(float* C, long long ldc, long long sC, const float* A, long long lda,
+                long long sA, bool ta, const float* B, long long ldb, long long sB, bool tb,
+                long long M, long long N, long long K, long long batch, float alpha, float beta,
+                int mask, void* workspace, size_t workspace_bytes, int* status, cudaStream_t st);
+}  // namespace g2q
+
 extern "C" size_t g2q_compensate_workspace_bytes(int method, int64_t nl, int64_t rows,
                                                  int64_t C, int precision) {
-  size_t b = (size_t)nl * rows * BLK * sizeof(float) + 256;
-  if (precision == 1) {
-    b += 2 * (size_t)nl * rows * BLK * sizeof(__nv_bfloat16) + 512;  // erra hi/lo
-    b += 2 * (size_t)nl * C * C * sizeof(__nv_bfloat16) + 512;       // U hi/lo
-    if (method != G2Q_METHOD_GPTQ)  // Z (G2PTQ) or quantized (GPTAQ) block hi/lo
-      b += 2 * (size_t)nl * rows * BLK * sizeof(__nv_bfloat16) + 512;
-    if (method == G2Q_METHOD_GPTAQ)  // P hi/lo
-      b += 2 * (size_t)nl * C * C * sizeof(__nv_bfloat16) + 512;
-  }
+  size_t b = (size_t)nl * rows * BLK * sizeof(float) + 256;  // the block's errors
+  // tensor-core trailing updates: fp16 hi/lo splits of one error block and one
+  // 128-row strip of U (or P), with their row / column scales
+  if (precision == 1) b += g2q::gemm_tc_workspace_bytes(rows, C, BLK, nl, nl) + 256;
   return b;
 }
-
-namespace g2q {
-int tc_trailing_update(float* W, long long C, long long rows, long long batch, long long i1,
-                       long long i2, int nc, const __nv_bfloat16* err_hi,
-                       const __nv_bfloat16* err_lo, long long err_stride,
-                       const __nv_bfloat16* u_hi, const __nv_bfloat16* u_lo, float beta,
-                       int* status, cudaStream_t st);
-int split_block_t(const float* src, long long lds, long long src_bs, long long rows, int nc,
-                  long long batch, __nv_bfloat16* hi, __nv_bfloat16* lo, long long dst_bs,
-                  cudaStream_t st);
-int split_bf16_2d(__nv_bfloat16* hi, __nv_bfloat16* lo, const float* src, long long n,
-                  cudaStream_t st);
-}  // namespace g2q
 
 static char* align_up(char* p, size_t a) {
   return (char*)(((uintptr_t)p + a - 1) / a * a);
@@ -756,34 +739,13 @@ extern "C" int g2q_compensate(int method, float* W, int64_t nl, int64_t rows, in
   float* erra = (float*)wsp;
   wsp = align_up(wsp + (size_t)nl * rows * BLK * sizeof(float), 256);
   const int maxq = (1 << (bits - 1)) - 1;
-  // Tensor-core trailing updates: bf16 hi/lo copies of the error block
-  // (column-major, written by the block kernel), of U (and GPTAQ's P, split
-  // once here) and, per block, of G2PTQ's Z block or GPTAQ's quantized block.
+  // Tensor-core trailing updates run through the fp32-accurate GEMM: each
+  // operand becomes an fp16 hi/lo pair after a power-of-two scale per output
+  // row (the error block) or column (U's strip), 22 significant bits, three
+  // products per K step (a bf16 hi/lo pair keeps 16 bits, and over the 112
+  // blocks of a 14336-column layer that drift flipped 0.14 % of the codes).
   const bool use_tc = precision == 1;
-  __nv_bfloat16 *ea_hi = nullptr, *ea_lo = nullptr, *u_hi = nullptr, *u_lo = nullptr;
-  __nv_bfloat16 *x_hi = nullptr, *x_lo = nullptr, *p_hi = nullptr, *p_lo = nullptr;
-  if (use_tc) {
-    const size_t ne = (size_t)nl * rows * BLK, nu = (size_t)nl * C * C;
-    auto take = [&](size_t n) {
-      __nv_bfloat16* q = (__nv_bfloat16*)wsp;
-      wsp = align_up(wsp + n * 2, 256);
-      return q;
-    };
-    ea_hi = take(ne);
-    ea_lo = take(ne);
-    u_hi = take(nu);
-    u_lo = take(nu);
-    G2Q_TRY(split_bf16_2d(u_hi, u_lo, U, (long long)nu, st));
-    if (method != G2Q_METHOD_GPTQ) {
-      x_hi = take(ne);
-      x_lo = take(ne);
-    }
-    if (method == G2Q_METHOD_GPTAQ) {
-      p_hi = take(nu);
-      p_lo = take(nu);
-      G2Q_TRY(split_bf16_2d(p_hi, p_lo, p, (long long)nu, st));
-    }
-  }
+  const size_t gws = use_tc ? gemm_tc_workspace_bytes(rows, C, BLK, nl, nl) : 0;
   for (long long i1 = 0; i1 < C; i1 += blocksize) {
     const long long i2 = (i1 + blocksize < C) ? i1 + blocksize : C;
     const int nc = (int)(i2 - i1);
@@ -803,7 +765,6 @@ extern "C" int g2q_compensate(int method, float* W, int64_t nl, int64_t rows, in
     P.maxq = maxq;
     P.codes = codes + i1; P.ldq = C; P.q_bs = rows * C;
     P.erra = erra; P.ldea = rows; P.ea_bs = rows * BLK;
-    P.erra_hi = ea_hi; P.erra_lo = ea_lo;
     if (method == G2Q_METHOD_G2PTQ) {
       P.z = z + i1; P.gh = gh + i1; P.ldz = C; P.z_bs = rows * C;
     }
@@ -820,17 +781,18 @@ extern "C" int g2q_compensate(int method, float* W, int64_t nl, int64_t rows, in
     // W[:, i2:] -= Erra @ U[i1:i2, i2:]  (+ G2PTQ: GH[:, i2:] -= Z[:, i1:i2] @ U[i1:i2, i2:];
     // GPTAQ: W[:, i2:] += Q1 @ P[i1:i2, i2:])
     if (use_tc) {
-      int s_tc = tc_trailing_update(W, C, rows, nl, i1, i2, nc, ea_hi, ea_lo, BLK, u_hi, u_lo,
-                                    -1.f, status, st);
+      int s_tc = gemm_tc_f32(W + i2, C, rows * C, erra, rows, rows * BLK, true, U + i1 * C + i2, C,
+                             C * C, false, rows, N, nc, nl, 1.f, -1.f, G2Q_MASK_FULL, wsp, gws,
+                             status, st);
       if (s_tc == G2Q_OK && method == G2Q_METHOD_G2PTQ) {
-        G2Q_TRY(split_block_t(z + i1, C, rows * C, rows, nc, nl, x_hi, x_lo, BLK * rows, st));
-        s_tc = tc_trailing_update(gh, C, rows, nl, i1, i2, nc, x_hi, x_lo, BLK, u_hi, u_lo,
-                                  -1.f, status, st);
+        s_tc = gemm_tc_f32(gh + i2, C, rows * C, z + i1, C, rows * C, false, U + i1 * C + i2, C,
+                           C * C, false, rows, N, nc, nl, 1.f, -1.f, G2Q_MASK_FULL, wsp, gws,
+                           status, st);
         if (s_tc != G2Q_OK) return s_tc == G2Q_ERR_UNSUPPORTED ? G2Q_ERR_CUDA : s_tc;
       } else if (s_tc == G2Q_OK && method == G2Q_METHOD_GPTAQ) {
-        G2Q_TRY(split_block_t(W + i1, C, rows * C, rows, nc, nl, x_hi, x_lo, BLK * rows, st));
-        s_tc = tc_trailing_update(W, C, rows, nl, i1, i2, nc, x_hi, x_lo, BLK, p_hi, p_lo, 1.f,
-                                  status, st);
+        s_tc = gemm_tc_f32(W + i2, C, rows * C, W + i1, C, rows * C, false, p + i1 * C + i2, C,
+                           C * C, false, rows, N, nc, nl, 1.f, 1.f, G2Q_MASK_FULL, wsp, gws,
+                           status, st);
         if (s_tc != G2Q_OK) return s_tc == G2Q_ERR_UNSUPPORTED ? G2Q_ERR_CUDA : s_tc;
       }
       if (s_tc == G2Q_OK) continue;

@@ -1205,12 +1205,6 @@ __global__ void split_rows_kernel(const S* X, long long ldx, long long T, long l
   }
 }
 
-static int grid_for(long long n) {
-  long long b = (n + 255) / 256;
-  if (b > 148 * 64) b = 148 * 64;
-  return (int)(b < 1 ? 1 : b);
-}
-
 static int split_rows(const void* X, int dtype, long long ldx, long long T, long long C,
                       const float* s, long long sstride, __nv_bfloat16* hi, __nv_bfloat16* lo,
                       long long ldo, cudaStream_t st) {
@@ -1266,10 +1260,6 @@ size_t tc_gram_workspace_bytes(long long M, long long N, long long T) {
   return (size_t)(4 * T * w * 2 + 4 * 256);
 }
 
-int split_bf16_2d(__nv_bfloat16* hi, __nv_bfloat16* lo, const float* src, long long n,
-                  cudaStream_t st) {
-  return tc::split_rows(src, G2Q_DTYPE_F32, n, 1, n, nullptr, 0, hi, lo, n, st);
-}
 
 // Gram update on tensor cores (see g2q_gram_update).  Falls back to the fp32
 // CUDA-core kernel where TMA cannot describe the operands (row strides that
@@ -1443,78 +1433,6 @@ int tc_gram_grouped(float* D, long long ldd, long long d_gstride, long long C, c
   return G2Q_OK;
 }
 
-// W[b][:, i2 + n] += beta * sum_k Err[b][k][m] * U[b][i1 + k][i2 + n] on tensor
-// cores.  err_hi / err_lo: [batch][err_stride rows][rows] bf16 (column-major
-// blocks: the compensation error, G2PTQ's Z block or GPTAQ's quantized block),
-// u_hi / u_lo: [batch][C][C] bf16 (U, or GPTAQ's P).  Returns
-// G2Q_ERR_UNSUPPORTED when the shapes do not meet TMA's alignment rules (the
-// caller then uses the CUDA-core path).
-int tc_trailing_update(float* W, long long C, long long rows, long long batch, long long i1,
-                       long long i2, int nc, const __nv_bfloat16* err_hi,
-                       const __nv_bfloat16* err_lo, long long err_stride,
-                       const __nv_bfloat16* u_hi, const __nv_bfloat16* u_lo, float beta,
-                       int* status, cudaStream_t st) {
-  if ((nc % tc::BK) || (i2 % 8) || (rows % 8) || (C % 8) || !tc::encode_fn())
-    return G2Q_ERR_UNSUPPORTED;
-  tc::Maps mp{};
-  bool ok = tc::make_map(&mp.a[0], err_hi, rows, batch * err_stride, rows) &&
-            tc::make_map(&mp.a[1], err_lo, rows, batch * err_stride, rows) &&
-            tc::make_map(&mp.b[0], u_hi, C, batch * C, C) &&
-            tc::make_map(&mp.b[1], u_lo, C, batch * C, C);
-  if (!ok) return G2Q_ERR_UNSUPPORTED;
-  tc::Params p{};
-  p.D = W + i2; p.ldd = C; p.d_bs = rows * C;
-  p.M = rows; p.N = C - i2;
-  p.num_kb = nc / tc::BK;
-  p.ka_batch = err_stride; p.ka0 = 0;
-  p.kb_batch = C; p.kb0 = i1;
-  p.nb0 = i2;
-  p.alpha = 1.f; p.beta = beta;
-  p.symmetric = 0;
-  p.status = status;
-  p.red = tc::make_map_out(&mp.d, p.D, p.N, p.M, batch, p.ldd, p.d_bs) ? 1 : 0;
-  return tc::dispatch(2, 2, mp, p, batch, st);
-}
-
-// dst[b][k][r] = bf16 hi/lo of src[b][r][k] for a rows x nc block (row stride
-// lds, batch stride src_bs): the column-major operand layout of the trailing
-// update for G2PTQ's Z block and GPTAQ's quantized block.
-__global__ void split_block_t_kernel(const float* __restrict__ src, long long lds,
-                                     long long src_bs, long long rows, int nc,
-                                     __nv_bfloat16* hi, __nv_bfloat16* lo, long long dst_bs) {
-  __shared__ float tile[32][33];
-  const int b = blockIdx.z;
-  const long long r0 = (long long)blockIdx.y * 32;
-  const int k0 = blockIdx.x * 32;
-  const float* sb = src + (long long)b * src_bs;
-  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-    const long long r = r0 + i;
-    const int k = k0 + threadIdx.x;
-    tile[i][threadIdx.x] = (r < rows && k < nc) ? sb[r * lds + k] : 0.f;
-  }
-  __syncthreads();
-  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-    const int k = k0 + i;
-    const long long r = r0 + threadIdx.x;
-    if (k >= nc || r >= rows) continue;
-    __nv_bfloat16 h, l;
-    split_bf16(tile[threadIdx.x][i], &h, &l);
-    const long long o = (long long)b * dst_bs + (long long)k * rows + r;
-    hi[o] = h;
-    lo[o] = l;
-  }
-}
-
-int split_block_t(const float* src, long long lds, long long src_bs, long long rows, int nc,
-                  long long batch, __nv_bfloat16* hi, __nv_bfloat16* lo, long long dst_bs,
-                  cudaStream_t st) {
-  if (rows <= 0 || nc <= 0 || batch <= 0) return G2Q_OK;
-  dim3 grid(cdiv(nc, 32), cdiv(rows, 32), (unsigned)batch);
-  if (grid.y > 65535u || grid.z > 65535u) return G2Q_ERR_INVALID_ARG;
-  split_block_t_kernel<<<grid, dim3(32, 8), 0, st>>>(src, lds, src_bs, rows, nc, hi, lo, dst_bs);
-  G2Q_CHECK_LAUNCH();
-  return G2Q_OK;
-}
 
 // ---------------------------------------------------------------------------
 // fp32-accurate batched GEMM on tensor cores (the fp32 products of fasterquant:

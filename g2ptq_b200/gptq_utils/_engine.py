@@ -149,14 +149,14 @@ def factor_with_retry(H, percdamp, info=None):
     return U, info, damps
 
 
-def raise_device_errors(info, statuses):
+def raise_device_errors(info, statuses, timeouts_only=False):
     """Raise for device conditions other than a failed pivot: a tensor-core
-    wait that gave up (in a Cholesky ``info`` or a status word) and a
-    non-positive quantization scale (``find_params``)."""
+    wait that gave up (in a Cholesky ``info`` or a status word) and, unless
+    ``timeouts_only``, a non-positive quantization scale (``find_params``)."""
     if any(s == _lib.G2Q_ERR_TIMEOUT for s in list(info) + list(statuses)):
         raise RuntimeError("g2ptq_b200: a tensor-core pipeline wait timed out "
                            f"({_lib.status_string(_lib.G2Q_ERR_TIMEOUT)})")
-    if any(s != 0 for s in statuses):
+    if not timeouts_only and any(s != 0 for s in statuses):
         raise RuntimeError("WeightQuantizer.find_params: non-positive scale")
 
 
@@ -589,7 +589,9 @@ class Pending:
     def finish(self):
         nl = self.nl
         flags = self._flags()
-        raise_device_errors(flags[:nl], flags[nl + 1:])
+        # a timeout is fatal; a non-positive scale is judged after any re-run
+        # (a failed factorization can leave NaN weights behind it)
+        raise_device_errors(flags[:nl], flags[nl + 1:], timeouts_only=True)
         if any(i != 0 for i in flags[:nl]):
             if self.borrowed_factor:
                 torch.cuda.synchronize(self.U.device)  # the owner's re-factored U
@@ -599,7 +601,7 @@ class Pending:
             self.nan, self.outs, self.codes = self.run(self.W0.clone())
             flags = self._flags()
             flags[:nl] = [0] * nl
-            raise_device_errors(flags[:nl], flags[nl + 1:])
+        raise_device_errors(flags[:nl], flags[nl + 1:])
         if flags[nl] != 0:
             raise ValueError("NaN in weights")
         if self.dynamic:

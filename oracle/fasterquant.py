@@ -58,9 +58,20 @@ def _factor_all(H, percdamp, route):
     return U, Hinv, damps
 
 
+def _given_factor(U):
+    """A factor supplied by the caller (a test comparing the compensation on
+    one shared U): ``(U, U^T U, damps unknown)``."""
+    U = np.asarray(U, f32)
+    return U, (U.transpose(0, 2, 1) @ U).astype(f32), None
+
+
 def gptq_fasterquant(W, H, quantizers, blocksize=128, percdamp=0.01, groupsize=-1,
-                     actorder=False, static_groups=False, route="reference"):
-    """gptq_utils.py:234-353 -> ``(Q, W_int, Scale, info)``."""
+                     actorder=False, static_groups=False, route="reference", U=None):
+    """gptq_utils.py:234-353 -> ``(Q, W_int, Scale, info)``.
+
+    ``U`` (optional, ``[B, C, C]``, in the act-order column order) replaces the
+    damped Cholesky chain, so that the rest of the pipeline can be compared
+    on a factor computed elsewhere."""
     W = np.asarray(W, f32).copy()
     H = np.asarray(H, f32).copy()
     B, R, C = W.shape
@@ -75,7 +86,7 @@ def gptq_fasterquant(W, H, quantizers, blocksize=128, percdamp=0.01, groupsize=-
         invperm = np.argsort(perm)
         W = W[:, :, perm].copy()
         H = H[:, perm][:, :, perm].copy()
-    U, _, damps = _factor_all(H, percdamp, route)
+    U, _, damps = _factor_all(H, percdamp, route) if U is None else _given_factor(U)
     if H_diag is not None and actorder:
         H_diag = H_diag[:, perm].copy()
     Q, W_int, Scale = run_compensation_gptq(
@@ -148,10 +159,12 @@ def trust_region(grad, Hinv_init, Q_sub, W_sub, alpha):
 
 def g2ptq_fasterquant(W, H, act_square, gradients, quantizers, num_groups, blocksize=128,
                       percdamp=0.01, groupsize=-1, actorder=False, static_groups=False,
-                      enable_gradient_update=True, alpha=0.0, route="reference"):
+                      enable_gradient_update=True, alpha=0.0, route="reference", U=None):
     """g2ptq_utils.py:349-519 (approx_grad_beta = 0) -> ``(Q, W_int, Scale, info)``.
 
-    ``H`` is ``[B, G, C, C]``, ``gradients`` ``[B, R, C]``, ``act_square`` ``[B, C]``.
+    ``H`` is ``[B, G, C, C]``, ``gradients`` ``[B, R, C]``, ``act_square`` ``[B, C]``;
+    ``U`` (optional, ``[B*G, C, C]`` in the act-order column order) replaces the
+    damped Cholesky chain (see ``gptq_fasterquant``).
     """
     W = np.asarray(W, f32).copy()
     B, R, C = W.shape
@@ -185,7 +198,8 @@ def g2ptq_fasterquant(W, H, act_square, gradients, quantizers, num_groups, block
         W_sub = W_sub[:, :, perm].copy()
         H_sub = H_sub[:, perm][:, :, perm].copy()
         grad = grad[:, :, perm].copy()
-    U, Hinv_init, damps = _factor_all(H_sub, percdamp, route)
+    U, Hinv_init, damps = (_factor_all(H_sub, percdamp, route) if U is None
+                           else _given_factor(U))
     if Q_sub is not None and actorder:
         Q_sub = Q_sub[:, :, perm]
     if H_diag is not None and actorder:
