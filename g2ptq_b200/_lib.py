@@ -77,6 +77,8 @@ SIGNATURES = {
     "g2q_permute_cols": [P, P, I32, I64, I64, I64, P, I32, P],
     "g2q_permute_sym": [P, P, I64, I64, P, P],
     "g2q_cast_check": [P, I32, P, I64, P, P],
+    "g2q_pack_upper": [P, P, I64, I64, I64, I64, F32, P],
+    "g2q_unpack_upper": [P, P, I64, I64, I64, I64, I32, P],
     "g2q_pack_int32": [P, P, I64, I64, I32, P],
     "g2q_trust_region_beta": [P, P, P, P, P, P, I64, I64, I64, F32, P],
     "g2q_diag_of_utu": [P, P, I64, I64, P],

@@ -194,6 +194,58 @@ __global__ void permute_sym_kernel(float* dst, const float* src, long long nl, l
 
 static dim3 grid_rows(long long rows, long long cols) { return wave_grid_2d(rows, cols); }
 
+// Upper triangle of symmetric matrices, packed row by row: element (i, j),
+// i <= j, of matrix b sits at b * C(C+1)/2 + i C - i(i-1)/2 + (j - i).  Rows are
+// walked by grid y, columns by thread: reads and writes are both contiguous.
+__global__ void pack_upper_kernel(float* dst, const float* H, long long nl, long long C,
+                                  long long ldh, long long h_bs, float s) {
+  const long long tri = C * (C + 1) / 2;
+  for (long long row = blockIdx.y; row < nl * C; row += gridDim.y) {
+    const long long b = row / C, i = row - b * C;
+    const float* h = H + b * h_bs + i * ldh;
+    float* d = dst + b * tri + i * C - i * (i - 1) / 2 - i;
+    for (long long j = i + (long long)blockIdx.x * blockDim.x + threadIdx.x; j < C;
+         j += (long long)gridDim.x * blockDim.x)
+      d[j] = s * h[j];
+  }
+}
+
+// The inverse of pack_upper_kernel, writing both triangles (the lower one
+// mirrored, or zero for a triangular matrix).  One CTA per pair of 32 x 32
+// tiles (ti <= tj): the upper tile is read from the packed rows into shared
+// memory, then written to (ti, tj) row by row and, transposed, to (tj, ti):
+// every global write is a contiguous 32-float run.
+__global__ void unpack_upper_kernel(float* H, const float* src, long long C, long long ldh,
+                                    long long h_bs, int mirror) {
+  const long long ti = blockIdx.y, tj = blockIdx.x;
+  if (ti > tj) return;
+  __shared__ float tile[32][33];
+  const long long b = blockIdx.z;
+  const long long tri = C * (C + 1) / 2;
+  const float* sb = src + b * tri;
+  float* hb = H + b * h_bs;
+  const int x = threadIdx.x;
+  const long long j = tj * 32 + x;
+  for (int y = threadIdx.y; y < 32; y += blockDim.y) {
+    const long long i = ti * 32 + y;
+    float v = 0.f;
+    if (i < C && j < C && j >= i) v = sb[i * C - i * (i - 1) / 2 + (j - i)];
+    tile[y][x] = v;
+  }
+  __syncthreads();
+  for (int y = threadIdx.y; y < 32; y += blockDim.y) {
+    const long long i = ti * 32 + y;
+    if (i < C && j < C && j >= i) hb[i * ldh + j] = tile[y][x];
+  }
+  // lower triangle: H[jj][ii] = upper (ii, jj) for ii < jj (rows jj of tile
+  // tj), or zero for a triangular factor
+  const long long ii = ti * 32 + x;
+  for (int y = threadIdx.y; y < 32; y += blockDim.y) {
+    const long long jj = tj * 32 + y;
+    if (ii < C && jj < C && ii < jj) hb[jj * ldh + ii] = mirror ? tile[x][y] : 0.f;
+  }
+}
+
 template <typename D>
 __global__ void cast_check_kernel(D* dst, const float* src, long long n, int* nan_count) {
   int local = 0;
@@ -553,6 +605,30 @@ extern "C" int g2q_permute_sym(float* dst, const float* src, int64_t nl, int64_t
   if (!dst || !src || !perm || nl <= 0 || C <= 0 || dst == src) return G2Q_ERR_INVALID_ARG;
   permute_sym_kernel<<<grid_rows(nl * C, C), 256, 0, (cudaStream_t)stream>>>(
       dst, src, nl, C, (const long long*)perm);
+  G2Q_CHECK_LAUNCH();
+  return G2Q_OK;
+}
+
+extern "C" int g2q_pack_upper(float* dst, const float* H, int64_t C, int64_t ldh,
+                              int64_t h_bstride, int64_t batch, float scale, void* stream) {
+  if (!dst || !H || C <= 0 || ldh < C || batch < 0 || (batch > 1 && h_bstride < C * ldh))
+    return G2Q_ERR_INVALID_ARG;
+  if (batch == 0) return G2Q_OK;
+  pack_upper_kernel<<<grid_rows(batch * C, C), 256, 0, (cudaStream_t)stream>>>(
+      dst, H, batch, C, ldh, h_bstride, scale);
+  G2Q_CHECK_LAUNCH();
+  return G2Q_OK;
+}
+
+extern "C" int g2q_unpack_upper(float* H, const float* src, int64_t C, int64_t ldh,
+                                int64_t h_bstride, int64_t batch, int mirror, void* stream) {
+  if (!H || !src || C <= 0 || ldh < C || batch < 0 || (batch > 1 && h_bstride < C * ldh) ||
+      batch > 65535)
+    return G2Q_ERR_INVALID_ARG;
+  if (batch == 0) return G2Q_OK;
+  const unsigned t = (unsigned)((C + 31) / 32);
+  unpack_upper_kernel<<<dim3(t, t, (unsigned)batch), dim3(32, 8), 0, (cudaStream_t)stream>>>(
+      H, src, C, ldh, h_bstride, mirror);
   G2Q_CHECK_LAUNCH();
   return G2Q_OK;
 }

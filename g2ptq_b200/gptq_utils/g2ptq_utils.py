@@ -12,10 +12,9 @@ token carries the weight ``s[n,g] / t_call`` and a fold rescales by
 import contextlib
 
 import torch
-import torch.distributed as dist
 
 from .. import ops, _lib
-from . import _engine
+from . import _engine, collectives
 from .common_utils import fake_quantize_grouped
 from .graph_utils import validate_tensors
 from .gptq_utils import _onload
@@ -224,39 +223,38 @@ class G2PTQ(_engine.StagingMixin):
 
 
 def reduce_to_target_rank(g2ptqs, g2ptq2rank):
-    """g2ptq_utils.py:530-575."""
-    rank = dist.get_rank()
-    dist.barrier()
-    for g in g2ptqs:
-        with g._maybe_onload_hessian_grad(gradients=True):
-            H = g.H
-            pending = []
-            target = g2ptq2rank[g]
-            gi = g.index.clone()
-            gt = g.total_tokens.clone()
-            dist.all_reduce(gi, op=dist.ReduceOp.SUM)
-            dist.all_reduce(gt, op=dist.ReduceOp.SUM)
-            gil, gtl = gi.cpu().tolist(), gt.cpu().tolist()
-            for b in range(g.num_layers):
-                if gil[b] == 0:
-                    H[b].zero_()
-                    g.gradients[b].zero_()
-                    g.act_square[b].zero_()
-                else:
-                    H[b] *= g._k[b] / gil[b]
-                    g.gradients[b] *= g._k[b] / gil[b]
-                    g.act_square[b] *= g._tok[b] / gtl[b]
-                    pending.extend([
-                        dist.reduce(H[b], op=dist.ReduceOp.SUM, dst=target, async_op=True),
-                        dist.reduce(g.act_square[b], op=dist.ReduceOp.SUM, dst=target,
-                                    async_op=True),
-                        dist.reduce(g.gradients[b], op=dist.ReduceOp.SUM, dst=target,
-                                    async_op=True),
-                    ])
-            if rank == target:
-                g.index.copy_(gi)
-                g.total_tokens.copy_(gt)
-                g._k, g._k_folded, g._tok = list(gil), list(gil), list(gtl)
-            for w in pending:
-                w.wait()
-    dist.barrier()
+    """g2ptq_utils.py:530-575: the block-wise Hessians and the gradients
+    rescaled by each rank's share of the calls, the squared-activation means by
+    its share of the tokens, summed onto the owner, whose ``index`` /
+    ``total_tokens`` become the global counts (one count all_reduce, one
+    packed reduce per owner rank)."""
+
+    def counts(g):
+        g._flush_all()
+        return list(g._k) + list(g._tok)
+
+    def entries(g, local, glob, owner):
+        B = g.num_layers
+        out = []
+        for b in range(B):
+            k_loc, k_glob = local[b], glob[b]
+            t_loc, t_glob = local[B + b], glob[B + b]
+            if k_glob == 0:
+                g._H[b].zero_()
+                g.gradients[b].zero_()
+                g.act_square[b].zero_()
+                continue
+            w = k_loc / k_glob
+            out += [collectives.Entry(owner, g._H[b], symmetric=True, weight=w),
+                    collectives.Entry(owner, g.act_square[b], weight=t_loc / t_glob),
+                    collectives.Entry(owner, g.gradients[b], weight=w)]
+        return out
+
+    def commit(g, glob):
+        B = g.num_layers
+        g.index = torch.tensor(glob[:B], dtype=torch.long, device=g.dev)
+        g.total_tokens = torch.tensor(glob[B:], dtype=torch.long, device=g.dev)
+        g._k, g._k_folded, g._tok = list(glob[:B]), list(glob[:B]), list(glob[B:])
+
+    collectives.reduce_objects(g2ptqs, g2ptq2rank, counts, entries, commit,
+                               lambda g: g._maybe_onload_hessian_grad(gradients=True))

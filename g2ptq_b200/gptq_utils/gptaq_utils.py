@@ -11,10 +11,9 @@ Compensation adds ``+ w_c * P[c, c+1:]`` with
 import contextlib
 
 import torch
-import torch.distributed as dist
 
 from .. import ops, _lib
-from . import _engine
+from . import _engine, collectives
 from .graph_utils import validate_tensors
 from .gptq_utils import _onload
 
@@ -182,32 +181,29 @@ class GPTAQ(_engine.StagingMixin):
 
 
 def reduce_to_target_rank(gptqs, gptq2rank):
-    """gptaq_utils.py:402-439."""
-    rank = dist.get_rank()
-    dist.barrier()
-    for g in gptqs:
-        with g._maybe_onload_hessian():
-            H, dX = g.H, g.dXXT
-            pending = []
-            target = gptq2rank[g]
-            gn = g.nsamples.clone()
-            dist.all_reduce(gn, op=dist.ReduceOp.SUM)
-            gnl = gn.cpu().tolist()
-            for b in range(g.num_layers):
-                if gnl[b] == 0:
-                    H[b].zero_()
-                    dX[b].zero_()
-                    g.nsamples[b].zero_()
-                else:
-                    H[b] *= g._n[b] / gnl[b]
-                    dX[b] *= g._n[b] / gnl[b]
-                    pending.extend([
-                        dist.reduce(H[b], op=dist.ReduceOp.SUM, dst=target, async_op=True),
-                        dist.reduce(dX[b], op=dist.ReduceOp.SUM, dst=target, async_op=True),
-                    ])
-            if rank == target:
-                g.nsamples.copy_(gn)
-                g._n, g._n_folded = list(gnl), list(gnl)
-            for w in pending:
-                w.wait()
-    dist.barrier()
+    """gptaq_utils.py:402-439: H and dXX^T rescaled by each rank's share of the
+    samples and summed onto the owner (one count all_reduce, one packed
+    reduce per owner rank; dXX^T is not symmetric and travels whole)."""
+
+    def counts(g):
+        g._flush_all()
+        return list(g._n)
+
+    def entries(g, local, glob, owner):
+        out = []
+        for b in range(g.num_layers):
+            if glob[b] == 0:
+                g._H[b].zero_()
+                g._dXXT[b].zero_()
+                continue
+            w = local[b] / glob[b]
+            out += [collectives.Entry(owner, g._H[b], symmetric=True, weight=w),
+                    collectives.Entry(owner, g._dXXT[b], weight=w)]
+        return out
+
+    def commit(g, glob):
+        g.nsamples = torch.tensor(glob, dtype=torch.long, device=g.dev)
+        g._n, g._n_folded = list(glob), list(glob)
+
+    collectives.reduce_objects(gptqs, gptq2rank, counts, entries, commit,
+                               lambda g: g._maybe_onload_hessian())

@@ -8,10 +8,9 @@ GPTQ's compensation over ``num_layers * num_groups`` row blocks.
 import contextlib
 
 import torch
-import torch.distributed as dist
 
 from .. import ops, _lib
-from . import _engine
+from . import _engine, collectives
 from .gptq_utils import GPTQ, _onload
 
 
@@ -137,17 +136,21 @@ class GPTQGuided(GPTQ):
 
 
 def reduce_to_target_rank(gptqs, gptq2rank):
-    """gptq_guided_utils.py:222-249 (un-normalized sums: plain SUM to the owner)."""
-    dist.barrier()
-    for g in gptqs:
-        with g._maybe_onload_hessian():
-            H = g.H
-            pending = [
-                dist.reduce(H, op=dist.ReduceOp.SUM, dst=gptq2rank[g], async_op=True),
-                dist.reduce(g.act_square, op=dist.ReduceOp.SUM, dst=gptq2rank[g],
-                            async_op=True),
-                dist.reduce(g.index, op=dist.ReduceOp.SUM, dst=gptq2rank[g], async_op=True),
-            ]
-            for w in pending:
-                w.wait()
-    dist.barrier()
+    """gptq_guided_utils.py:222-249: the un-normalized block-wise Hessians,
+    squared-activation sums and call counts summed onto the owner (one count
+    all_reduce, one packed reduce per owner rank)."""
+
+    def counts(g):
+        g._flush_all()
+        return list(g._idx)
+
+    def entries(g, local, glob, owner):
+        return [collectives.Entry(owner, g._H[b], symmetric=True)
+                for b in range(g.num_layers)] + [collectives.Entry(owner, g.act_square)]
+
+    def commit(g, glob):
+        g.index = torch.tensor(glob, dtype=torch.long, device=g.dev)
+        g._idx = list(glob)
+
+    collectives.reduce_objects(gptqs, gptq2rank, counts, entries, commit,
+                               lambda g: g._maybe_onload_hessian())

@@ -11,10 +11,9 @@ All arithmetic runs in libg2ptq_b200's sm_100a kernels.
 import contextlib
 
 import torch
-import torch.distributed as dist
 
 from .. import ops, _lib
-from . import _engine
+from . import _engine, collectives
 from .common_utils import make_group_quantizers, merge_group_quantizers  # noqa: F401
 from .graph_utils import validate_tensors
 
@@ -226,32 +225,31 @@ def fasterquant_all(gptqs, **kwargs):
 
 
 def reduce_to_target_rank(gptqs, gptq2rank):
-    """gptq_utils.py:362-391: sum the rank-local Hessians, rescaled by their
-    sample share, onto each object's owner rank."""
-    rank = dist.get_rank()
-    dist.barrier()
-    for gptq in gptqs:
-        with gptq._maybe_onload_hessian():
-            H = gptq.H
-            # the reduced Hessian no longer follows a fold group's
-            gptq._leave_groups()
-            pending = []
-            target = gptq2rank[gptq]
-            global_n = gptq.nsamples.clone()
-            dist.all_reduce(global_n, op=dist.ReduceOp.SUM)
-            gn = global_n.cpu().tolist()
-            for b in range(gptq.num_layers):
-                if gn[b] == 0:
-                    H[b].zero_()
-                    gptq.nsamples[b].zero_()
-                else:
-                    H[b] *= gptq._n[b] / gn[b]
-                    pending.append(dist.reduce(H[b], op=dist.ReduceOp.SUM, dst=target,
-                                               async_op=True))
-            if rank == target:
-                gptq.nsamples.copy_(global_n)
-                gptq._n = list(gn)
-                gptq._n_folded = list(gn)
-            for w in pending:
-                w.wait()
-    dist.barrier()
+    """gptq_utils.py:362-391: sum the rank-local Hessians, each rescaled by its
+    rank's share of the samples, onto the object's owner rank; the owner's
+    ``nsamples`` becomes the global count.  One count all_reduce for all
+    objects and one packed-upper-triangle reduce per owner rank
+    (``collectives.reduce_objects``)."""
+
+    def counts(g):
+        g._hessian()        # pending folds first
+        g._leave_groups()   # the reduced Hessian no longer follows a fold group
+        return list(g._n)
+
+    def entries(g, local, glob, owner):
+        out = []
+        for b in range(g.num_layers):
+            if glob[b] == 0:
+                g._H[b].zero_()
+            else:
+                out.append(collectives.Entry(owner, g._H[b], symmetric=True,
+                                             weight=local[b] / glob[b]))
+        return out
+
+    def commit(g, glob):
+        g.nsamples = torch.tensor(glob, dtype=torch.long, device=g.dev)
+        g._n = list(glob)
+        g._n_folded = list(glob)
+
+    collectives.reduce_objects(gptqs, gptq2rank, counts, entries, commit,
+                               lambda g: g._maybe_onload_hessian())

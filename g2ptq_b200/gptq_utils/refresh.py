@@ -75,163 +75,170 @@ def _weighted_sum(tensors_and_weights):
     return acc
 
 
-class SaliencyCache:
-    """Output-gradient saliencies per linear (g2ptq_utils.py:586-679)."""
+def _present(per_loss, loss_weights):
+    """``(loss_type, weight)`` pairs of ``loss_weights`` that have cached data."""
+    return [(lt, w) for lt, w in loss_weights.items() if lt in per_loss]
+
+
+class _LinearHooks:
+    """Hook bookkeeping shared by the two caches: the block's linears are
+    looked up by name (or ``name + ".module"`` for wrapped ones), forward
+    hooks are kept in ``handles`` until ``clear_hook``, and ``hooks_enabled``
+    gates the gradient-side hooks to the backward passes the caller asks for."""
 
     def __init__(self, names, num_groups):
-        self.num_groups = num_groups
-        self.saliency_cache = {}
-        self.outs = {}
         self.names = names
-        for name in self.names:
-            self.saliency_cache[name] = {}   # loss -> list of per-batch [tokens, G] tensors
-            self.outs[name] = 0
+        self.num_groups = num_groups
         self.handles = []
         self.hooks_enabled = False
+
+    @staticmethod
+    def _linear(full, name):
+        module = full.get(name)
+        return module if module is not None else full.get(name + ".module")
+
+    def _on_forward(self, name):
+        raise NotImplementedError
+
+    def set_forward_hook(self, full):
+        for name in self.names:
+            self.handles.append(self._linear(full, name).register_forward_hook(
+                self._on_forward(name)))
+
+    @contextlib.contextmanager
+    def _gradients_on(self):
+        self.hooks_enabled = True
+        try:
+            yield
+        finally:
+            self.hooks_enabled = False
+
+    def clear_hook(self):
+        while self.handles:
+            self.handles.pop().remove()
+        self.hooks_enabled = False
+
+
+class SaliencyCache(_LinearHooks):
+    """Per linear and loss type, the per-batch ``[tokens, G]`` saliencies of
+    its output gradient (g2ptq_utils.py:586-679): ``saliency_cache[name]`` maps
+    a loss type to the list of batches until ``summarize_saliency`` collapses
+    it to one list weighted over loss types."""
+
+    def __init__(self, names, num_groups):
+        super().__init__(names, num_groups)
+        self.outs = {name: 0 for name in names}
+        self.saliency_cache = {name: {} for name in names}
 
     def cache_saliency(self, module, inp, out, name):
         self.outs[name] = out
 
+    def _on_forward(self, name):
+        return functools.partial(self.cache_saliency, name=name)
+
     def grad_hook(self, grad, name, loss_type):
-        """g2ptq_utils.py:605-618: ``[tokens, G]`` means of ``grad**2`` over
-        each of the G channel groups."""
-        if not self.hooks_enabled:
-            return
-        grad = grad.reshape(-1, grad.shape[-1])
-        sal = ops.saliency(grad, self.num_groups)
-        self.saliency_cache[name].setdefault(loss_type, []).append(sal)
-
-    def summarize_saliency(self, loss_weights):
-        """g2ptq_utils.py:620-640: per batch, the weighted sum over loss types."""
-        for name in self.names:
-            per_loss = self.saliency_cache[name]
-            present = [(l, w) for l, w in loss_weights.items() if l in per_loss]
-            if not present:
-                self.saliency_cache[name] = []
-                continue
-            lengths = [len(per_loss[l]) for l, _ in present]
-            assert len(set(lengths)) == 1, (
-                f"Saliency for '{name}' has mismatched per-loss batch counts: "
-                f"{ {l: len(per_loss[l]) for l, _ in present} }"
-            )
-            self.saliency_cache[name] = [
-                _weighted_sum([(per_loss[l][i], w) for l, w in present])
-                for i in range(lengths[0])
-            ]
-
-    def set_forward_hook(self, full):
-        for name in self.names:
-            module = full.get(name, full.get(name + ".module", None))
-            self.handles.append(
-                module.register_forward_hook(functools.partial(self.cache_saliency, name=name)))
+        """Group means of ``grad**2`` over the G channel groups of the output
+        (g2ptq_utils.py:605-618), one kernel pass over the gradient."""
+        if self.hooks_enabled:
+            sal = ops.saliency(grad.reshape(-1, grad.shape[-1]), self.num_groups)
+            self.saliency_cache[name].setdefault(loss_type, []).append(sal)
 
     def backward(self, loss_tensor, loss_type="block", retain_graph=True):
-        """g2ptq_utils.py:652-669: gradients of the loss at every cached output."""
-        names = [name for name in self.names if isinstance(self.outs[name], torch.Tensor)]
-        if not names:
+        """The loss's gradient at every output captured since the last clear
+        (g2ptq_utils.py:652-669), turned into saliencies."""
+        live = [(n, out) for n, out in self.outs.items() if isinstance(out, torch.Tensor)]
+        if not live:
             return
-        self.hooks_enabled = True
-        try:
-            grads = torch.autograd.grad(loss_tensor, [self.outs[name] for name in names],
+        with self._gradients_on():
+            grads = torch.autograd.grad(loss_tensor, [out for _, out in live],
                                         retain_graph=retain_graph, allow_unused=True)
-            for name, grad in zip(names, grads):
+            for (name, _), grad in zip(live, grads):
                 if grad is not None:
                     self.grad_hook(grad, name=name, loss_type=loss_type)
-        finally:
-            self.hooks_enabled = False
 
-    def clear_hook(self):
-        for h in self.handles:
-            h.remove()
-        self.handles = []
-        self.hooks_enabled = False
+    def summarize_saliency(self, loss_weights):
+        """Batch by batch, the ``loss_weights``-weighted sum over loss types
+        (g2ptq_utils.py:620-640); every loss type must hold the same number of
+        batches."""
+        for name in self.names:
+            per_loss = self.saliency_cache[name]
+            terms = _present(per_loss, loss_weights)
+            counts = {lt: len(per_loss[lt]) for lt, _ in terms}
+            if len(set(counts.values())) > 1:
+                raise AssertionError(f"saliency batches of {name!r} differ between loss types: "
+                                     f"{counts}")
+            batches = next(iter(counts.values()), 0)
+            self.saliency_cache[name] = [
+                _weighted_sum([(per_loss[lt][i], w) for lt, w in terms]) for i in range(batches)]
 
     def clear_cache(self):
-        for name in self.names:
-            self.saliency_cache[name] = {}
-            self.outs[name] = 0
+        self.outs = {name: 0 for name in self.names}
+        self.saliency_cache = {name: {} for name in self.names}
         _cleanup_memory()
 
 
-class GradientCache:
-    """Running-mean weight gradients per linear (g2ptq_utils.py:682-763)."""
+class GradientCache(_LinearHooks):
+    """Per linear and loss type, the running mean over backward passes of the
+    weight gradient divided by the batch's token count (g2ptq_utils.py:682-763):
+    ``gradients_cache[name][loss_type]`` and its count ``index[name][loss_type]``
+    until ``summarize_gradients`` collapses the loss types."""
 
     def __init__(self, names, num_groups):
-        self.num_groups = num_groups
-        self.gradients_cache = {}
-        self.index = {}
+        super().__init__(names, num_groups)
         self.current_batch_tokens = {}
-        self.names = names
-        for name in self.names:
-            self.gradients_cache[name] = {}   # loss -> running-mean gradient tensor
-            self.index[name] = {}             # loss -> accumulation count
-        self.handles = []
-        self.hooks_enabled = False
+        self.gradients_cache = {name: {} for name in names}
+        self.index = {name: {} for name in names}
 
     def forward_hook(self, module, inp, out, name):
-        x = inp[0]
+        x = inp[0]  # [batch, seq, hidden] or, for routed experts, [tokens, hidden]
         self.current_batch_tokens[name] = x.numel() // x.shape[-1]
 
+    def _on_forward(self, name):
+        return functools.partial(self.forward_hook, name=name)
+
     def cache_gradient(self, grad, name, loss_type):
-        """g2ptq_utils.py:693-702: ``cache <- cache i/(i+1) + grad / (n_tok (i+1))``
-        in one pass, in place."""
+        """``cache <- cache i/(i+1) + grad / (n_tok (i+1))`` (g2ptq_utils.py:693-702),
+        in place in one kernel pass."""
         if not self.hooks_enabled:
             return
-        n_tokens = self.current_batch_tokens[name]
-        index = self.index[name].get(loss_type, 0)
-        cache = self.gradients_cache[name].get(loss_type, 0)
-        keep = index / (index + 1)
-        index += 1
-        # torch divides a CUDA tensor by a host scalar as a multiply by the
-        # scalar's fp32 reciprocal
-        inv = float(np.float32(1.0) / np.float32(n_tokens * index))
-        grad = grad.contiguous()
-        first = not torch.is_tensor(cache)
+        i = self.index[name].get(loss_type, 0)
+        cache = self.gradients_cache[name].get(loss_type)
+        first = cache is None
         if first:
             cache = torch.empty(grad.shape, dtype=torch.float32, device=grad.device)
-        ops.running_mean(cache, grad, keep, inv, first)
+        # the reference divides a CUDA tensor by a host scalar, which torch
+        # evaluates as a multiply by the scalar's fp32 reciprocal
+        inv = float(np.float32(1.0) / np.float32(self.current_batch_tokens[name] * (i + 1)))
+        ops.running_mean(cache, grad.contiguous(), i / (i + 1), inv, first)
         self.gradients_cache[name][loss_type] = cache
-        self.index[name][loss_type] = index
-
-    def summarize_gradients(self, loss_weights):
-        """g2ptq_utils.py:704-711: the weighted sum over loss types (0 if none)."""
-        for name in self.names:
-            per_loss = self.gradients_cache[name]
-            present = [(l, w) for l, w in loss_weights.items() if l in per_loss]
-            self.gradients_cache[name] = (_weighted_sum([(per_loss[l], w) for l, w in present])
-                                          if present else 0)
-
-    def set_forward_hook(self, full):
-        for name in self.names:
-            module = full.get(name, full.get(name + ".module", None))
-            self.handles.append(
-                module.register_forward_hook(functools.partial(self.forward_hook, name=name)))
+        self.index[name][loss_type] = i + 1
 
     @contextlib.contextmanager
     def set_backward_hook(self, full, loss_type="block"):
-        self.hooks_enabled = True
-        handles = []
-        for name in self.names:
-            module = full.get(name, full.get(name + ".module", None))
-            handles.append(module.weight.register_hook(
-                functools.partial(self.cache_gradient, name=name, loss_type=loss_type)))
-        try:
-            yield
-        finally:
-            for h in handles:
-                h.remove()
-            self.hooks_enabled = False
+        """Gradient hooks on the linears' weights for the backward passes run
+        inside the context."""
+        hooks = [self._linear(full, name).weight.register_hook(
+                     functools.partial(self.cache_gradient, name=name, loss_type=loss_type))
+                 for name in self.names]
+        with self._gradients_on():
+            try:
+                yield
+            finally:
+                for h in hooks:
+                    h.remove()
 
-    def clear_hook(self):
-        for h in self.handles:
-            h.remove()
-        self.handles = []
-        self.hooks_enabled = False
+    def summarize_gradients(self, loss_weights):
+        """The ``loss_weights``-weighted sum over loss types, or 0 where
+        nothing was cached (g2ptq_utils.py:704-711)."""
+        for name in self.names:
+            per_loss = self.gradients_cache[name]
+            terms = _present(per_loss, loss_weights)
+            self.gradients_cache[name] = (_weighted_sum([(per_loss[lt], w) for lt, w in terms])
+                                          if terms else 0)
 
     def clear_cache(self):
-        for name in self.names:
-            self.gradients_cache[name] = {}
-            self.index[name] = {}
+        self.gradients_cache = {name: {} for name in self.names}
+        self.index = {name: {} for name in self.names}
         _cleanup_memory()
 
 

@@ -361,6 +361,38 @@ def cast_check(src, dtype, nan_count, out=None):
     return out
 
 
+def pack_upper(H, scale=1.0, out=None):
+    """Upper triangles of ``H [B, C, C]`` (or ``[C, C]``) packed row by row,
+    times ``scale`` -> fp32 ``[B * C(C+1)/2]`` (``out`` may be a view of a
+    larger buffer)."""
+    _cuda(H, out)
+    Hb = H if H.dim() == 3 else H[None]
+    B, C, _ = Hb.shape
+    if Hb.stride(2) != 1 or (B > 1 and Hb.stride(0) < C * Hb.stride(1)):
+        raise ValueError("pack_upper expects unit column stride")
+    n = B * C * (C + 1) // 2
+    if out is None:
+        out = torch.empty(n, dtype=torch.float32, device=H.device)
+    if out.numel() != n or not out.is_contiguous():
+        raise ValueError("pack_upper: out must be contiguous with B * C(C+1)/2 elements")
+    call("g2q_pack_upper", out.data_ptr(), Hb.data_ptr(), C, Hb.stride(1), Hb.stride(0), B,
+         float(scale), _stream(H))
+    return out
+
+
+def unpack_upper(H, packed, mirror=True):
+    """Fill ``H [B, C, C]`` (or ``[C, C]``) from ``pack_upper``'s layout: the
+    lower triangle mirrored, or zero (``mirror=False``, a triangular factor)."""
+    _cuda(H, packed)
+    Hb = H if H.dim() == 3 else H[None]
+    B, C, _ = Hb.shape
+    if packed.numel() != B * C * (C + 1) // 2 or not packed.is_contiguous():
+        raise ValueError("unpack_upper: packed has the wrong size")
+    call("g2q_unpack_upper", Hb.data_ptr(), packed.data_ptr(), C, Hb.stride(1), Hb.stride(0), B,
+         int(bool(mirror)), _stream(H))
+    return H
+
+
 def pack_int32(codes, bits):
     _cuda(codes)
     _contig(codes)

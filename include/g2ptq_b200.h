@@ -213,6 +213,21 @@ int g2q_chol_upper_inverse(float* U, const float* H, int64_t C, int64_t ldh, int
                            void* workspace, size_t workspace_bytes, void* stream);
 size_t g2q_chol_workspace_bytes(int64_t C);
 
+/* Upper triangle (i <= j) of `batch` C x C matrices H[b] (row stride ldh,
+ * batch stride h_bstride), packed row by row and multiplied by `scale`:
+ * element (i, j) of matrix b goes to dst[b * C(C+1)/2 + i C - i(i-1)/2 + j - i].
+ * g2q_unpack_upper writes H back from that layout: the lower triangle
+ * mirrored (mirror != 0) or set to zero (an upper-triangular factor).  The
+ * symmetric Hessians and the triangular factors cross NCCL in this form
+ * (half the bytes), with the sample-share rescale folded into the pack.
+ * Replaces the full-matrix dist.reduce / dist.broadcast of
+ * gptq_utils/gptq_utils.py:369-387 and the per-method copies
+ * (g2ptq_utils.py:530-575, gptaq_utils.py:393-439, gptq_guided_utils.py:213-249). */
+int g2q_pack_upper(float* dst, const float* H, int64_t C, int64_t ldh, int64_t h_bstride,
+                   int64_t batch, float scale, void* stream);
+int g2q_unpack_upper(float* H, const float* src, int64_t C, int64_t ldh, int64_t h_bstride,
+                     int64_t batch, int mirror, void* stream);
+
 /* Per-row quantization parameters over `cols` columns of W (row stride ldw):
  * xmin = min(min(x), 0), xmax = max(max(x), 0); symmetric:
  * scale = max(|xmin|, xmax) / ((2^bits - 1) / 2), zero = 0; asymmetric:

@@ -88,12 +88,38 @@ def test_g2ptq_token_weights_match_per_call_update():
 # two CPU ranks: reduce_to_target_rank semantics
 # ---------------------------------------------------------------------------
 
+def cpu_pack_upper(H, scale=1.0, out=None):
+    """CPU stand-in of ops.pack_upper (row-major upper triangle)."""
+    Hb = H if H.dim() == 3 else H[None]
+    C = Hb.shape[-1]
+    iu = torch.triu_indices(C, C)
+    vals = (Hb[:, iu[0], iu[1]] * scale).reshape(-1)
+    if out is None:
+        return vals
+    out.copy_(vals)
+    return out
+
+
+def cpu_unpack_upper(H, packed, mirror=True):
+    """CPU stand-in of ops.unpack_upper."""
+    Hb = H if H.dim() == 3 else H[None]
+    C = Hb.shape[-1]
+    iu = torch.triu_indices(C, C)
+    vals = packed.view(Hb.shape[0], -1)
+    Hb[:, iu[0], iu[1]] = vals
+    Hb[:, iu[1], iu[0]] = vals if mirror else 0.0
+    Hb[:, iu[0], iu[1]] = vals
+    return H
+
+
 class HostGPTQ:
     """CPU stand-in carrying the attributes reduce_to_target_rank touches."""
 
     def __init__(self, H, n):
         import contextlib
         self.num_layers = H.shape[0]
+        self.dev = torch.device("cpu")
+        self.offload_hessians = False
         self._H = H
         self.nsamples = torch.tensor(n)
         self._n = list(n)
@@ -104,8 +130,29 @@ class HostGPTQ:
     def H(self):
         return self._H
 
+    def _hessian(self):
+        return self._H
+
     def _leave_groups(self):
         pass
+
+
+class HostLayer:
+    def __init__(self, rows, cols, fill):
+        self.weight = torch.nn.Parameter(torch.full((rows, cols), float(fill),
+                                                    dtype=torch.bfloat16),
+                                         requires_grad=False)
+
+
+class HostQuantized:
+    """Stand-in of a quantized object for broadcast_quantized_param: layers,
+    the group quantizers' bit width and count."""
+
+    def __init__(self, layers, bits, groups):
+        from types import SimpleNamespace
+        self.layers = layers
+        self.num_layers = len(layers)
+        self.quantizer = [SimpleNamespace(bits=bits) for _ in range(groups)]
 
 
 def _free_port():
@@ -116,40 +163,142 @@ def _free_port():
     return p
 
 
-def _rank_main(rank, world, port, q):
+def _init(rank, world, port):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
+    from g2ptq_b200.gptq_utils import collectives
+    collectives.pack_upper = cpu_pack_upper
+    collectives.unpack_upper = cpu_unpack_upper
+
+
+def _run_ranks(target, world=2):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=target, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(world):
+        r, payload = q.get(timeout=120)
+        res[r] = payload
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    return res
+
+
+def _rank_reduce(rank, world, port, q):
+    _init(rank, world, port)
     from g2ptq_b200.gptq_utils.gptq_utils import reduce_to_target_rank
     torch.manual_seed(rank)
     H = torch.rand(2, 8, 8)
+    H = H + H.transpose(1, 2)  # symmetric, as every Hessian is
+    H2 = torch.rand(1, 6, 6)
+    H2 = H2 + H2.transpose(1, 2)
     n = [3 + rank, 0]  # second layer never saw data on any rank
     obj = HostGPTQ(H.clone(), n)
-    reduce_to_target_rank([obj], {obj: 1})
-    q.put((rank, H, n, obj.H.clone(), obj.nsamples.clone()))
+    obj2 = HostGPTQ(H2.clone(), [5])
+    reduce_to_target_rank([obj, obj2], {obj: 1, obj2: 0})
+    q.put((rank, (H, n, obj.H.clone(), obj.nsamples.clone(), H2, obj2.H.clone(),
+                  obj2.nsamples.clone())))
     dist.barrier()
     dist.destroy_process_group()
 
 
 def test_reduce_to_target_rank_two_ranks():
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, q)) for r in range(2)]
-    for p in procs:
-        p.start()
-    res = {}
-    for _ in range(2):
-        r, H, n, Hout, nout = q.get(timeout=120)
-        res[r] = (H, n, Hout, nout)
-    for p in procs:
-        p.join(timeout=60)
-        assert p.exitcode == 0
-    (H0, n0, _, _), (H1, n1, Hout1, nout1) = res[0], res[1]
+    """Two objects owned by different ranks in one coalesced exchange: each
+    owner gets the sample-share weighted sum and the global counts."""
+    res = _run_ranks(_rank_reduce)
+    (H0, n0, _, _, H20, _, _), (H1, n1, Hout1, nout1, H21, _, _) = res[0], res[1]
     total = n0[0] + n1[0]
     expect = H0[0] * n0[0] / total + H1[0] * n1[0] / total
     torch.testing.assert_close(Hout1[0], expect)
     assert torch.count_nonzero(Hout1[1]) == 0       # no samples anywhere -> zeros
     assert nout1.tolist() == [total, 0]
+    # the second object is owned by rank 0: equal shares of 5 samples each
+    torch.testing.assert_close(res[0][5][0], (H20[0] + H21[0]) / 2)
+    assert res[0][6].tolist() == [10]
+
+
+def _rank_broadcast(rank, world, port, q):
+    _init(rank, world, port)
+    from g2ptq_b200.gptq_utils.common_utils import broadcast_quantized_param
+    objs = [HostQuantized([HostLayer(8, 40, 10 * rank + k) for k in range(2)], 4, 2),
+            HostQuantized([HostLayer(16, 24, 100 + rank)], 3, 1)]
+    owner = {objs[0]: 1, objs[1]: 0}
+    for o in objs:
+        if owner[o] != rank:
+            continue
+        for k, layer in enumerate(o.layers):
+            rows, cols = layer.weight.shape
+            bits = o.quantizer[0].bits
+            layer._export_qparams = {
+                "weight_packed": torch.full((rows, -(-cols // (32 // bits))), 7 + k,
+                                            dtype=torch.int32),
+                "weight_scale": torch.full((rows, len(o.quantizer)), 0.5 + k,
+                                           dtype=torch.bfloat16),
+                "weight_shape": torch.tensor([rows, cols])}
+    staged = broadcast_quantized_param(objs, owner, export_compressed_tensors=True)
+    out = [[(l.weight.data.float().clone(), {k: v.clone() for k, v in l._export_qparams.items()})
+            for l in o.layers] for o in objs]
+    q.put((rank, (out, len(staged))))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_broadcast_quantized_param_two_ranks():
+    """Every rank ends with the owner's weights and export buffers, without
+    any metadata exchange: non-owners derive the buffer shapes."""
+    res = _run_ranks(_rank_broadcast)
+    for r in (0, 1):
+        out, n_staged = res[r]
+        assert n_staged == 3
+        for k in range(2):  # object 0 owned by rank 1
+            w, qp = out[0][k]
+            assert torch.all(w == 10 + k)
+            assert qp["weight_packed"].shape == (8, 5)
+            assert torch.all(qp["weight_packed"] == 7 + k)
+            assert torch.all(qp["weight_scale"].float() == 0.5 + k)
+            assert qp["weight_shape"].tolist() == [8, 40]
+        w, qp = out[1][0]  # object 1 owned by rank 0, 3-bit: 10 codes per word
+        assert torch.all(w == 100)
+        assert qp["weight_packed"].shape == (16, 3) and qp["weight_scale"].shape == (16, 1)
+
+
+def _rank_gather(rank, world, port, q):
+    _init(rank, world, port)
+    from g2ptq_b200.gptq_utils import collectives
+    full_a = torch.zeros(10, 3)
+    full_b = torch.zeros(7, dtype=torch.int32)
+    a_rows = [(0, 6), (6, 10)][rank]   # ragged slices
+    b_rows = [(0, 2), (2, 7)][rank]
+    part_a = (torch.arange(30, dtype=torch.float32).view(10, 3) + 0.5)[a_rows[0]:a_rows[1]]
+    part_b = torch.arange(7, dtype=torch.int32)[b_rows[0]:b_rows[1]] * 3
+    collectives.all_gather_rows([(part_a.contiguous(), full_a), (part_b.contiguous(), full_b)],
+                                torch.device("cpu"))
+    q.put((rank, (full_a, full_b)))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_all_gather_rows_two_ranks():
+    res = _run_ranks(_rank_gather)
+    for r in (0, 1):
+        a, b = res[r]
+        torch.testing.assert_close(a, torch.arange(30, dtype=torch.float32).view(10, 3) + 0.5)
+        assert b.tolist() == [3 * i for i in range(7)]
+
+
+def test_cpu_pack_stand_in_layout():
+    """The CPU stand-in packs in the kernel's documented layout: element
+    (i, j), i <= j, at i C - i(i-1)/2 + j - i."""
+    C = 5
+    H = torch.arange(C * C, dtype=torch.float32).view(C, C)
+    p = cpu_pack_upper(H)
+    for i in range(C):
+        for j in range(i, C):
+            assert p[i * C - i * (i - 1) // 2 + j - i] == H[i, j]
 
 
 def test_lazy_counter_applies_increments_on_read():

@@ -113,7 +113,7 @@ def test_summarize_saliency_rejects_mismatched_counts():
     sc = G.SaliencyCache(["a"], 4)
     t = torch.zeros(3, 4)
     sc.saliency_cache["a"] = {"block": [t, t], "patch": [t]}
-    with pytest.raises(AssertionError, match="mismatched per-loss batch counts"):
+    with pytest.raises(AssertionError, match="differ between loss types"):
         sc.summarize_saliency({"block": 0.5, "patch": 0.5})
 
 
