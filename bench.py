@@ -64,6 +64,10 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--method", default="gptq", choices=sorted(METHODS),
                     help="gptq: BASELINE configs[1] (default); g2ptq: configs[2]")
+    ap.add_argument("--multi", default="rows", choices=["rows", "owner"],
+                    help="N>1: rows = factor owners + row-sharded compensation + one gather; "
+                         "owner = the reference's flow (reduce to owner, owner quantizes, "
+                         "broadcast)")
     return ap.parse_args()
 
 
@@ -189,7 +193,7 @@ def make_layers(torch, dev):
 
 
 def one_step(torch, layers, acts, n_local, world, rank, dist, method="gptq", g2=None,
-             marks=None):
+             marks=None, multi="rows", phases=None):
     """add_batch over the rank's sequences, reduce to owners, fasterquant, broadcast.
 
     ``marks``: optional list that receives a CUDA event at the end of the
@@ -219,17 +223,23 @@ def one_step(torch, layers, acts, n_local, world, rank, dist, method="gptq", g2=
             o._flush_all()
         marks.append(torch.cuda.Event(enable_timing=True))
         marks[-1].record()
-    owners = objs
-    if world > 1:
-        specs = list(objs.values())
-        _, _, obj2rank = common_utils.partition_layers(specs, world)
-        mod.reduce_to_target_rank(specs, obj2rank)
-        owners = {k: o for k, o in objs.items() if obj2rank[o] == rank}
-    gptq_utils.fasterquant_all(list(owners.values()), blocksize=BLOCKSIZE, percdamp=PERCDAMP,
-                               export_compressed_tensors=True, **cfg["fq"])
-    if world > 1:
-        common_utils.broadcast_quantized_param(list(objs.values()), obj2rank,
-                                               export_compressed_tensors=True)
+    if world > 1 and multi == "rows" and method == "gptq":
+        from g2ptq_b200.gptq_utils import sharded
+        sharded.fasterquant_rows(list(objs.values()), blocksize=BLOCKSIZE, percdamp=PERCDAMP,
+                                 export_compressed_tensors=True, marks=phases, **cfg["fq"])
+    else:
+        owners = objs
+        if world > 1:
+            specs = list(objs.values())
+            _, _, obj2rank = common_utils.partition_layers(specs, world)
+            mod.reduce_to_target_rank(specs, obj2rank)
+            owners = {k: o for k, o in objs.items() if obj2rank[o] == rank}
+        gptq_utils.fasterquant_all(list(owners.values()), blocksize=BLOCKSIZE,
+                                   percdamp=PERCDAMP, export_compressed_tensors=True,
+                                   **cfg["fq"])
+        if world > 1:
+            common_utils.broadcast_quantized_param(list(objs.values()), obj2rank,
+                                                   export_compressed_tensors=True)
     for o in objs.values():
         o.free()
     if marks is not None:
@@ -318,7 +328,8 @@ def native(args):
         torch.cuda.synchronize()
 
     for _ in range(args.warmup):
-        one_step(torch, layers, acts, n_local, world, rank, dist, args.method, g2)
+        one_step(torch, layers, acts, n_local, world, rank, dist, args.method, g2,
+                 multi=args.multi)
     barrier()
     timer = GramTimer(torch)
     timer.install()
@@ -330,9 +341,13 @@ def native(args):
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record()
     marks = [t0]
+    phases = []  # per step: the row-sharded path's phase boundaries
     torch.cuda.nvtx.range_push("timed")  # lets a profiler capture exactly the timed steps
     for _ in range(args.steps):
-        one_step(torch, layers, acts, n_local, world, rank, dist, args.method, g2, marks)
+        step_phases = []
+        one_step(torch, layers, acts, n_local, world, rank, dist, args.method, g2, marks,
+                 multi=args.multi, phases=step_phases)
+        phases.append(step_phases)
     torch.cuda.nvtx.range_pop()
     t1.record()
     barrier()
@@ -350,6 +365,26 @@ def native(args):
                    for i in range(args.steps)) / args.steps
     quant_ms = sum(marks[2 * i + 1].elapsed_time(marks[2 * i + 2])
                    for i in range(args.steps)) / args.steps
+    # the quantization phase split at the row-sharded path's events, every rank
+    split = {}
+    if phases and phases[0]:
+        for i, step_marks in enumerate(phases):
+            prev = marks[2 * i + 1]
+            for name, ev in step_marks:
+                split[name] = split.get(name, 0.0) + prev.elapsed_time(ev) / args.steps
+                prev = ev
+            split["export_and_free"] = (split.get("export_and_free", 0.0) +
+                                        prev.elapsed_time(marks[2 * i + 2]) / args.steps)
+        split = {k: round(v, 3) for k, v in split.items()}
+    per_rank = None
+    if world > 1:
+        keys = ["add_batch_and_folds"] + (list(split) if split else ["quantize"])
+        mine = [calib_ms] + ([split[k] for k in keys[1:]] if split else [quant_ms])
+        t = torch.tensor(mine, device=dev, dtype=torch.float64)
+        table = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(table, t)
+        per_rank = [{k: round(float(v), 3) for k, v in zip(keys, row.tolist())}
+                    for row in table]
     gram_ms = timer.total_ms() / args.steps
     gram_tflops = timer.flops / args.steps / (gram_ms * 1e-3) / 1e12 if gram_ms > 0 else 0.0
 
@@ -367,10 +402,15 @@ def native(args):
         "config": {
             "workload": f"Llama-3-8B decoder layer (7 linears) {METHODS[args.method]['label']}, "
                         f"{args.seqs}x{args.seq_len} calibration tokens",
-            "parallelism": f"tokens dp{world} + linear ownership (LPT)",
+            "parallelism": (f"tokens dp{world} + factor ownership (LPT) + row-sharded "
+                            "compensation + one all_gather"
+                            if world > 1 and args.multi == "rows" and args.method == "gptq"
+                            else f"tokens dp{world} + linear ownership (LPT)"),
             "calibration_seconds_32_layers": round(N_LAYERS * ms * 1e-3, 3),
             "phase_ms_rank0": {"add_batch_and_folds": round(calib_ms, 3),
-                               "reduce_factor_compensate_export": round(quant_ms, 3)},
+                               "reduce_factor_compensate_export": round(quant_ms, 3),
+                               **({"split": split} if split else {})},
+            **({"phase_ms_per_rank": per_rank} if per_rank else {}),
             "precision": "tcgen05" if _engine.PRECISION == 1 else "fp32-cuda-core",
             "l2": "inputs larger than L2 (GBs of activations per step)",
         },
@@ -443,7 +483,8 @@ def native_e2e(torch, dist, args, layers, world, rank, dev, n_local, dev_acts, g
         return bufs[g % ring]
 
     def step():
-        one_step(torch, layers, feed, n_local, world, rank, dist, args.method, g2)
+        one_step(torch, layers, feed, n_local, world, rank, dist, args.method, g2,
+                 multi=args.multi)
         # free the last buffer and keep the copies running into the next step
         free_ev[(state["consumed"] - 1) % ring].record()
         prefetch_upto(state["consumed"] + ring)
