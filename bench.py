@@ -228,18 +228,26 @@ def one_step(torch, layers, acts, n_local, world, rank, dist, method="gptq", g2=
         sharded.fasterquant_rows(list(objs.values()), blocksize=BLOCKSIZE, percdamp=PERCDAMP,
                                  export_compressed_tensors=True, marks=phases, **cfg["fq"])
     else:
+        def mark(name):
+            if phases is not None and world > 1:
+                ev = torch.cuda.Event(enable_timing=True)
+                ev.record()
+                phases.append((name, ev))
         owners = objs
         if world > 1:
             specs = list(objs.values())
             _, _, obj2rank = common_utils.partition_layers(specs, world)
             mod.reduce_to_target_rank(specs, obj2rank)
             owners = {k: o for k, o in objs.items() if obj2rank[o] == rank}
+            mark("reduce")
         gptq_utils.fasterquant_all(list(owners.values()), blocksize=BLOCKSIZE,
                                    percdamp=PERCDAMP, export_compressed_tensors=True,
                                    **cfg["fq"])
+        mark("owner_fasterquant")
         if world > 1:
             common_utils.broadcast_quantized_param(list(objs.values()), obj2rank,
                                                    export_compressed_tensors=True)
+            mark("broadcast")
     for o in objs.values():
         o.free()
     if marks is not None:

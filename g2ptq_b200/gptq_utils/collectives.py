@@ -114,6 +114,13 @@ def _bytes(t):
     return t.contiguous().view(-1).view(torch.uint8)
 
 
+def _dest_bytes(t):
+    """A contiguous destination tensor as a flat byte view of its storage."""
+    if not t.is_contiguous():
+        raise ValueError("collectives: destination tensors must be contiguous")
+    return t.view(-1).view(torch.uint8)
+
+
 def broadcast_from_owners(entries, device):
     """Copy every entry's tensor from its ``rank`` into the same tensor on all
     other ranks: one byte buffer and one ``broadcast`` per source rank.
@@ -133,7 +140,9 @@ def broadcast_from_owners(entries, device):
             continue
         off = 0
         for e, n in zip(es, sizes):
-            e.t.copy_(buf[off:off + n].view(e.t.dtype).view(e.t.shape))
+            # bytes into the destination seen as bytes: a slice of the buffer
+            # need not be aligned for the destination's element type
+            _dest_bytes(e.t).copy_(buf[off:off + n])
             off += n
 
 
@@ -162,7 +171,7 @@ def all_gather_rows(pieces, device):
     recv = torch.empty(world * width, dtype=torch.uint8, device=device)
     dist.all_gather_into_tensor(recv, send)
     for k, (_, full) in enumerate(pieces):
-        dst = full.view(-1).view(torch.uint8)
+        dst = _dest_bytes(full)
         pos = 0
         for r in range(world):
             off = sum(table[r][1:1 + k])

@@ -224,8 +224,10 @@ def test_reduce_to_target_rank_two_ranks():
 def _rank_broadcast(rank, world, port, q):
     _init(rank, world, port)
     from g2ptq_b200.gptq_utils.common_utils import broadcast_quantized_param
+    # 3-bit layer first: its 2-byte scales leave the next int64 weight_shape
+    # at a byte offset that is not a multiple of 8 inside the buffer
     objs = [HostQuantized([HostLayer(8, 40, 10 * rank + k) for k in range(2)], 4, 2),
-            HostQuantized([HostLayer(16, 24, 100 + rank)], 3, 1)]
+            HostQuantized([HostLayer(17, 24, 100 + rank)], 3, 1)]
     owner = {objs[0]: 1, objs[1]: 0}
     for o in objs:
         if owner[o] != rank:
@@ -263,7 +265,8 @@ def test_broadcast_quantized_param_two_ranks():
             assert qp["weight_shape"].tolist() == [8, 40]
         w, qp = out[1][0]  # object 1 owned by rank 0, 3-bit: 10 codes per word
         assert torch.all(w == 100)
-        assert qp["weight_packed"].shape == (16, 3) and qp["weight_scale"].shape == (16, 1)
+        assert qp["weight_packed"].shape == (17, 3) and qp["weight_scale"].shape == (17, 1)
+        assert qp["weight_shape"].tolist() == [17, 24]
 
 
 def _rank_gather(rank, world, port, q):
