@@ -11,7 +11,7 @@ import os
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.environ.get("G2PTQ_B200_LIB", os.path.join(_HERE, "_lib", "libg2ptq_b200.so"))
 
-ABI_VERSION = 7
+ABI_VERSION = 8
 
 G2Q_OK = 0
 G2Q_ERR_INVALID_ARG = -1
@@ -67,9 +67,9 @@ SIGNATURES = {
     "g2q_gemm_tc_workspace_bytes": [I64, I64, I64, I64, I32, I32],
     "g2q_fake_quantize": [P, I64, P, I64, P, I64, I64, I64, P, P, I64, P, I32, P],
     "g2q_compensate_block": [I32, P, I64, I64, I64, I64, I64, P, I64, I64, P, P, I64, P, I32, P,
-                             P, P, P, P, P],
+                             P, P, P, P, P, F32, P],
     "g2q_compensate": [I32, P, I64, I64, I64, P, P, P, I64, P, I32, I32, I32, I32, I32, P, P, P,
-                       P, P, I32, P, SZ, P, P],
+                       P, P, F32, P, I32, P, SZ, P, P],
     "g2q_compensate_workspace_bytes": [I32, I64, I64, I64, I32],
     "g2q_prepare_hessian": [P, I64, I64, P, I64, P, I64, P, P],
     "g2q_argsort_desc": [P, P, I64, P],

@@ -35,6 +35,10 @@ struct BlockParams {
   long long ldz, z_bs;
   const float* p;  // GPTAQ, layout (ldh, h_bs)
   int dfact;       // G2PTQ distance factor (the traversal's blocksize)
+  // G2PTQ --approx_grad: the traversal's input weights (layout of W) and the
+  // shrink factor; wraw == nullptr leaves the standard path
+  const float* wraw;
+  float beta;
 };
 
 // Eight threads share a row and each keeps 16 of the block's columns in
@@ -130,10 +134,13 @@ __global__ void __launch_bounds__(BlockCfg::THREADS, 2) block_kernel(BlockParams
   }
 
   // this thread's 32 columns of W (and of gh / z for G2PTQ) and their parameters
-  float wv[SEG], gv[SEG], xv[SEG], sv[SEG], zv[SEG];
+  float wv[SEG], gv[SEG], xv[SEG], sv[SEG], zv[SEG], rv[SEG];
   float* wrow = P.W + (long long)b * P.w_bs + rr * P.ldw + t * SEG;
   float* grow = (METHOD == G2Q_METHOD_G2PTQ)
                     ? P.gh + (long long)b * P.z_bs + rr * P.ldz + t * SEG : nullptr;
+  // --approx_grad (G2PTQ): raw weights of this thread's columns
+  const bool approx = (METHOD == G2Q_METHOD_G2PTQ) && P.wraw != nullptr;
+  const float* rawrow = approx ? P.wraw + (long long)b * P.w_bs + rr * P.ldw + t * SEG : nullptr;
   const float* zrow = (METHOD == G2Q_METHOD_G2PTQ)
                           ? P.z + (long long)b * P.z_bs + rr * P.ldz + t * SEG : nullptr;
   const long long prow = ((long long)b * P.rows + rr) * P.param_ld;
@@ -147,6 +154,7 @@ __global__ void __launch_bounds__(BlockCfg::THREADS, 2) block_kernel(BlockParams
     zv[k] = in ? P.zero[prow + pc] : 0.f;
     gv[k] = (METHOD == G2Q_METHOD_G2PTQ && in) ? grow[k] : 0.f;
     xv[k] = (METHOD == G2Q_METHOD_G2PTQ && in) ? zrow[k] : 0.f;
+    rv[k] = (approx && in) ? rawrow[k] : 0.f;
   }
   __syncthreads();
 
@@ -179,6 +187,10 @@ __global__ void __launch_bounds__(BlockCfg::THREADS, 2) block_kernel(BlockParams
     const bool after = t >= tw;  // the owner's columns after the current one
     const bool later = t > tw;   // every column of the threads after the owner
     float wn = wv[0], gn = gv[0];
+    // --approx_grad: the previous segment's last column of this block pulls
+    // this segment's first column toward its raw value after its update
+    // (the products rounded apart, as the reference's tensor expression)
+    if (approx && tw > 0) wn = __fsub_rn(wn, __fmul_rn(__fsub_rn(wn, rv[0]), P.beta));
     int klast = 0;
 #pragma unroll
     for (int k = 0; k < SEG; ++k) {
@@ -194,7 +206,10 @@ __global__ void __launch_bounds__(BlockCfg::THREADS, 2) block_kernel(BlockParams
         q = fminf(fmaxf(q, qlo), qhi);
         const float qv = s * (q - zz);
         if (METHOD == G2Q_METHOD_G2PTQ) {
-          e = div_rn(wc - qv - gn, dv[k], rdv[k]);
+          float num = wc - qv - gn;
+          // --approx_grad: the error also shrinks toward the raw weight
+          if (approx) num = __fsub_rn(num, __fmul_rn(__fsub_rn(wc, rv[k]), P.beta));
+          e = div_rn(num, dv[k], rdv[k]);
           gv[k] = gn;
         } else {
           e = div_rn(wc - qv, dv[k], rdv[k]);
@@ -244,6 +259,7 @@ __global__ void __launch_bounds__(BlockCfg::THREADS, 2) block_kernel(BlockParams
         const float u1 = Us[i * LDU + tw * USEG + k + 1];
         if (METHOD == G2Q_METHOD_G2PTQ) {
           wn = fmaf(-e, u1, wv[k + 1] - gv[k + 1]);
+          if (approx) wn = __fsub_rn(wn, __fmul_rn(__fsub_rn(wn, rv[k + 1]), P.beta));
           gn = fmaf(-aux, u1, gv[k + 1]);
         } else if (METHOD == G2Q_METHOD_GPTAQ) {
           wn = fmaf(Ps[i * LDU + tw * USEG + k + 1], aux, fmaf(-e, u1, wv[k + 1]));
@@ -675,9 +691,11 @@ extern "C" int g2q_compensate_block(int method, float* W, int64_t ldw, int64_t w
                                     const float* scale, const float* zero, int64_t param_ld,
                                     const int* colmap, int maxq, int8_t* codes, float* err,
                                     const float* z, float* ghinv, const float* p,
-                                    void* stream) {
+                                    const float* wraw, float approx_beta, void* stream) {
   if (!W || !hinv || !scale || !zero || !colmap || ncols <= 0 || ncols > BLK || rows < 0 ||
       batch < 0 || maxq < 0)
+    return G2Q_ERR_INVALID_ARG;
+  if ((wraw != nullptr) != (approx_beta != 0.f) || (wraw && method != G2Q_METHOD_G2PTQ))
     return G2Q_ERR_INVALID_ARG;
   if (method == G2Q_METHOD_G2PTQ && (!z || !ghinv)) return G2Q_ERR_INVALID_ARG;
   if (method == G2Q_METHOD_GPTAQ && !p) return G2Q_ERR_INVALID_ARG;
@@ -691,6 +709,8 @@ extern "C" int g2q_compensate_block(int method, float* W, int64_t ldw, int64_t w
   P.z = z; P.gh = ghinv; P.ldz = ldw; P.z_bs = w_bstride;
   P.p = p;
   P.dfact = (int)ncols;
+  P.wraw = wraw;
+  P.beta = approx_beta;
   return launch_block(method, P, batch, (cudaStream_t)stream);
 }
 
@@ -721,7 +741,8 @@ extern "C" int g2q_compensate(int method, float* W, int64_t nl, int64_t rows, in
                               const float* U, float* scale, float* zero, int64_t ngroups,
                               const int* colgroup, int dynamic_groups, int groupsize, int bits,
                               int sym, int blocksize, int8_t* codes, const float* z, float* gh,
-                              const float* p, const g2q_clip_t* clip, int precision,
+                              const float* p, const float* wraw, float approx_beta,
+                              const g2q_clip_t* clip, int precision,
                               void* workspace, size_t workspace_bytes, int* status,
                               void* stream) {
   if (!W || !U || !scale || !zero || !colgroup || !codes || nl <= 0 || rows <= 0 || C <= 0 ||
@@ -731,6 +752,8 @@ extern "C" int g2q_compensate(int method, float* W, int64_t nl, int64_t rows, in
   if (!clip_ok(clip)) return G2Q_ERR_INVALID_ARG;
   if (method == G2Q_METHOD_G2PTQ && (!z || !gh)) return G2Q_ERR_INVALID_ARG;
   if (method == G2Q_METHOD_GPTAQ && !p) return G2Q_ERR_INVALID_ARG;
+  if ((wraw != nullptr) != (approx_beta != 0.f) || (wraw && method != G2Q_METHOD_G2PTQ))
+    return G2Q_ERR_INVALID_ARG;
   if (precision != 0 && precision != 1) return G2Q_ERR_INVALID_ARG;
   if (workspace_bytes < g2q_compensate_workspace_bytes(method, nl, rows, C, precision))
     return G2Q_ERR_INVALID_ARG;
@@ -770,6 +793,10 @@ extern "C" int g2q_compensate(int method, float* W, int64_t nl, int64_t rows, in
     }
     if (method == G2Q_METHOD_GPTAQ) P.p = p + i1 * C + i1;
     P.dfact = blocksize;
+    if (wraw) {
+      P.wraw = wraw + i1;
+      P.beta = approx_beta;
+    }
     G2Q_TRY(launch_block(method, P, nl, st));
     if (i2 >= C) break;
     const long long N = C - i2;

@@ -345,7 +345,7 @@ void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 using namespace g2q;
 
-extern "C" int g2q_abi_version(void) { return 7; }
+extern "C" int g2q_abi_version(void) { return 8; }
 
 extern "C" int64_t g2q_launch_count(void) { return g2q::g_launches.load(); }
 

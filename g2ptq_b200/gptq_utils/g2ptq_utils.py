@@ -25,10 +25,13 @@ from .refresh import (SaliencyCache, GradientCache, normalize_loss_weights,  # n
 def run_eager(weight, hinv, scale, zero, z, ghinv, maxq, backend="torch", int_weight=None,
               error=None, weight_raw=None, approx_beta=0.0):
     """One G2PTQ compensation block, reference layout ``[B, blk, R]``
-    (g2ptq_utils.py:97-126); updates ``weight`` and ``ghinv`` in place."""
-    if approx_beta:
-        raise NotImplementedError("g2ptq_b200: --approx_grad is not implemented")
-    validate_tensors("G2PTQ", weight, hinv, scale, zero, z, ghinv, int_weight, error)
+    (g2ptq_utils.py:97-126); updates ``weight`` and ``ghinv`` in place.
+    ``weight_raw`` with ``approx_beta`` != 0 runs the --approx_grad ablation
+    (lines 48-51, 71-73)."""
+    tensors = [weight, hinv, scale, zero, z, ghinv, int_weight, error]
+    if weight_raw is not None:
+        tensors.append(weight_raw)
+    validate_tensors("G2PTQ", *tensors)
     B, blk, R = weight.shape
     W = weight.transpose(1, 2).contiguous()
     S = scale.transpose(1, 2).contiguous().reshape(B * R, blk)
@@ -38,8 +41,11 @@ def run_eager(weight, hinv, scale, zero, z, ghinv, maxq, backend="torch", int_we
     colmap = torch.arange(blk, dtype=torch.int32, device=weight.device)
     codes = torch.empty(B, R, blk, dtype=torch.int8, device=weight.device)
     err = torch.empty(B, blk, R, dtype=torch.float32, device=weight.device)
+    raw = (weight_raw.transpose(1, 2).contiguous()
+           if (approx_beta and weight_raw is not None) else None)
     ops.compensate_block(_lib.METHOD_G2PTQ, W, hinv.contiguous(), S, Zp, colmap, maxq,
-                         codes=codes, err=err, z=zz, ghinv=gh)
+                         codes=codes, err=err, z=zz, ghinv=gh, wraw=raw,
+                         approx_beta=approx_beta if raw is not None else 0.0)
     weight.copy_(W.transpose(1, 2))
     ghinv.copy_(gh.transpose(1, 2))
     int_weight.copy_(codes.transpose(1, 2))
@@ -57,8 +63,6 @@ class G2PTQ(_engine.StagingMixin):
         self.num_layers = len(layers)
         self.offload_hessians = offload_hessians
         self.approx_grad_beta = approx_grad_beta
-        if approx_grad_beta:
-            raise NotImplementedError("g2ptq_b200: --approx_grad is not implemented")
         weight = layers[0].weight
         self.dev = weight.device
         if self.dev.type != "cuda":
@@ -197,9 +201,13 @@ class G2PTQ(_engine.StagingMixin):
                 beta = torch.zeros(nl, rps, dtype=torch.float32, device=self.dev)
             Z = ops.scale_rows(T1, beta)
             GH = ops.gemm(torch.empty_like(grad), Z, U, precision=_engine.PRECISION)
+            # --approx_grad: W0 is the reference's W_raw snapshot (the traversal's
+            # input after act-order and dead columns, g2ptq_utils.py:270-273)
+            approx = float(self.approx_grad_beta or 0.0)
             ops.compensate(_lib.METHOD_G2PTQ, Wp, U, params.scale, params.zero, colgroup,
                            dynamic, groupsize, q0.bits, q0.sym, blocksize, codes, z=Z, gh=GH,
-                           status=params.status, precision=_engine.PRECISION, clip=clip)
+                           status=params.status, precision=_engine.PRECISION, clip=clip,
+                           wraw=W0 if approx else None, approx_beta=approx)
             _ = clip_hd  # the diagonal the clip configuration points to stays alive
             Q, cq = Wp, codes
             if actorder:

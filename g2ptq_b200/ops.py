@@ -267,34 +267,38 @@ def fake_quantize(W, scale, zero, maxq, colmap=None, out=None, codes=None):
 
 
 def compensate_block(method, W, hinv, scale, zero, colmap, maxq, codes=None, err=None, z=None,
-                     ghinv=None, p=None):
+                     ghinv=None, p=None, wraw=None, approx_beta=0.0):
     """One compensation block on ``W [B, rows, ncols]`` (in place -> Q).
 
     ``err`` (optional) is written column-major ``[B, ncols, rows]`` (the
     reference's kernel layout); ``codes`` is ``[B, rows, ncols]`` int8.
     """
-    _cuda(W, hinv, scale, zero, colmap, codes, err, z, ghinv, p)
-    _contig(W, hinv, scale, zero, colmap, codes, err, z, ghinv, p)
+    _cuda(W, hinv, scale, zero, colmap, codes, err, z, ghinv, p, wraw)
+    _contig(W, hinv, scale, zero, colmap, codes, err, z, ghinv, p, wraw)
     B, rows, ncols = W.shape
     call("g2q_compensate_block", method, W.data_ptr(), ncols, rows * ncols, B, rows, ncols,
          hinv.data_ptr(), ncols, ncols * ncols, scale.data_ptr(), zero.data_ptr(),
          scale.stride(0) if scale.dim() == 2 else 1, colmap.data_ptr(), int(maxq), _ptr(codes),
-         _ptr(err), _ptr(z), _ptr(ghinv), _ptr(p), _stream(W))
+         _ptr(err), _ptr(z), _ptr(ghinv), _ptr(p), _ptr(wraw),
+         float(approx_beta) if wraw is not None else 0.0, _stream(W))
 
 
 def compensate(method, W, U, scale, zero, colgroup, dynamic_groups, groupsize, bits, sym,
-               blocksize, codes, z=None, gh=None, p=None, status=None, precision=0, clip=None):
+               blocksize, codes, z=None, gh=None, p=None, status=None, precision=0, clip=None,
+               wraw=None, approx_beta=0.0):
     """Whole block traversal (``_run_compensation``); ``W [nl, rows, C]`` -> Q in place.
-    ``clip`` (a ``clip_config``) selects the clip search for dynamic groups."""
-    _cuda(W, U, scale, zero, colgroup, codes, z, gh, p, status)
-    _contig(W, U, scale, zero, colgroup, codes, z, gh, p)
+    ``clip`` (a ``clip_config``) selects the clip search for dynamic groups;
+    ``wraw`` / ``approx_beta``: G2PTQ's --approx_grad ablation."""
+    _cuda(W, U, scale, zero, colgroup, codes, z, gh, p, status, wraw)
+    _contig(W, U, scale, zero, colgroup, codes, z, gh, p, wraw)
     nl, rows, C = W.shape
     ws_bytes = query("g2q_compensate_workspace_bytes", method, nl, rows, C, precision)
     ws = workspace(ws_bytes, W.device)
     call("g2q_compensate", method, W.data_ptr(), nl, rows, C, U.data_ptr(), scale.data_ptr(),
          zero.data_ptr(), scale.shape[1], colgroup.data_ptr(), int(bool(dynamic_groups)),
          int(groupsize), int(bits), int(bool(sym)), int(blocksize), codes.data_ptr(), _ptr(z),
-         _ptr(gh), _ptr(p), None if clip is None else ctypes.byref(clip), precision,
+         _ptr(gh), _ptr(p), _ptr(wraw), float(approx_beta) if wraw is not None else 0.0,
+         None if clip is None else ctypes.byref(clip), precision,
          ws.data_ptr(), ws_bytes, _ptr(status), _stream(W))
 
 

@@ -292,7 +292,11 @@ int g2q_fake_quantize(float* out, int64_t ldo, int8_t* codes, int64_t ldq,
  * scale[(b*rows + r) * param_ld + colmap[c]] (same for zero).
  * In place: W <- dequantized Q; codes (int8, optional), err (fp32, optional,
  * same layout as W).  G2PTQ also reads z and updates ghinv (same layout as W);
- * GPTAQ reads p (same layout as hinv).  ncols <= 128.
+ * GPTAQ reads p (same layout as hinv).  ncols <= 128.  G2PTQ's --approx_grad
+ * ablation: wraw (same layout as W, the raw weights) and approx_beta != 0
+ * subtract (w - wraw) * approx_beta from each column's error and pull the
+ * next column toward its raw value by the same factor (g2ptq_utils.py:48-51,
+ * 71-73); NULL / 0 otherwise (and for the other methods).
  * Replaces run_eager / _run_torch_compensation / _run_triton_compensation of
  * gptq_utils/gptq_utils.py:28-90, gptq_utils/g2ptq_utils.py:34-126 and
  * gptq_utils/gptaq_utils.py:28-100 (reference layout [B, blk, R] is the
@@ -304,7 +308,7 @@ int g2q_compensate_block(int method, float* W, int64_t ldw, int64_t w_bstride,
                          const int* colmap, int maxq,
                          int8_t* codes, float* err,
                          const float* z, float* ghinv, const float* p,
-                         void* stream);
+                         const float* wraw, float approx_beta, void* stream);
 
 /* Whole block traversal of fasterquant: for each block of `blocksize`
  * columns (dynamic groups: find parameters at each group start from the
@@ -314,9 +318,12 @@ int g2q_compensate_block(int method, float* W, int64_t ldw, int64_t w_bstride,
  * U: [nl, C, C] upper factors.  scale/zero: [nl*rows, ngroups] (static
  * parameters are read, dynamic ones are written).  colgroup[c]: parameter
  * column of (permuted) column c.  codes: [nl, rows, C] int8 output.
- * G2PTQ: z [nl, rows, C] read, gh [nl, rows, C] updated.  GPTAQ: p [nl, C, C].
+ * G2PTQ: z [nl, rows, C] read, gh [nl, rows, C] updated; with --approx_grad
+ * wraw [nl, rows, C] holds the traversal's input weights (the reference's
+ * W_raw snapshot, g2ptq_utils.py:270-273) and approx_beta the shrink factor
+ * (NULL / 0 otherwise).  GPTAQ: p [nl, C, C].
  * precision: 0 = fp32 CUDA-core trailing update, 1 = tensor cores
- * (bf16x3 split).  clip (NULL: plain min/max) selects the clip search for
+ * (fp16 hi/lo operands with power-of-two row / column scales).  clip (NULL: plain min/max) selects the clip search for
  * the dynamic group parameters, its hdiag indexed by the permuted column.
  * Needs g2q_compensate_workspace_bytes bytes; *status receives
  * G2Q_ERR_BAD_SCALE on a non-positive dynamic scale.
@@ -327,7 +334,8 @@ int g2q_compensate(int method, float* W, int64_t nl, int64_t rows, int64_t C,
                    const float* U, float* scale, float* zero, int64_t ngroups,
                    const int* colgroup, int dynamic_groups, int groupsize, int bits, int sym,
                    int blocksize, int8_t* codes,
-                   const float* z, float* gh, const float* p, const g2q_clip_t* clip,
+                   const float* z, float* gh, const float* p, const float* wraw,
+                   float approx_beta, const g2q_clip_t* clip,
                    int precision, void* workspace, size_t workspace_bytes, int* status,
                    void* stream);
 size_t g2q_compensate_workspace_bytes(int method, int64_t nl, int64_t rows, int64_t C,

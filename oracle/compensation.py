@@ -76,17 +76,26 @@ def gptq_block(weight, hinv, scale, zero, maxq):
     return weight, int_weight, error
 
 
-def g2ptq_block(weight, hinv, scale, zero, z, ghinv, maxq):
-    """g2ptq_utils.py:34-74 (approx_beta = 0) -> ``(weight, int_weight, error, ghinv)``."""
+def g2ptq_block(weight, hinv, scale, zero, z, ghinv, maxq, weight_raw=None, approx_beta=0.0):
+    """g2ptq_utils.py:34-74 -> ``(weight, int_weight, error, ghinv)``.
+
+    ``approx_beta`` != 0 (the ``--approx_grad`` ablation, lines 48-51 and
+    71-73): the column error also subtracts ``(w - weight_raw) * beta``, and
+    after each column's update the next column is pulled toward its raw
+    value by ``(w_next - raw_next) * beta``."""
     weight = weight.astype(f32).copy()
     ghinv = ghinv.astype(f32).copy()
+    beta = f32(approx_beta)
     B, cols, R = weight.shape
     int_weight = np.empty_like(weight)
     error = np.empty_like(weight)
     for c in range(cols):
         w = weight[:, c].copy()
         q, qi = _quant_column(w, scale[:, c], zero[:, c], maxq)
-        err = ((w - q - ghinv[:, c]) / hinv[:, c, c][:, None]).astype(f32)
+        num = (w - q - ghinv[:, c]).astype(f32)
+        if approx_beta:
+            num = (num - ((w - weight_raw[:, c]).astype(f32) * beta).astype(f32)).astype(f32)
+        err = (num / hinv[:, c, c][:, None]).astype(f32)
         weight[:, c] = q
         int_weight[:, c] = qi
         error[:, c] = err
@@ -95,6 +104,9 @@ def g2ptq_block(weight, hinv, scale, zero, z, ghinv, maxq):
             weight[:, c + 1:] -= ghinv[:, c + 1:]
             weight[:, c + 1:] -= row * err[:, None, :]
             ghinv[:, c + 1:] -= row * z[:, c][:, None, :]
+            if approx_beta:
+                drift = ((weight[:, c + 1] - weight_raw[:, c + 1]).astype(f32) * beta)
+                weight[:, c + 1] -= drift.astype(f32)
     return weight, int_weight, error, ghinv
 
 
@@ -170,9 +182,12 @@ def run_compensation_gptq(W, Hinv, quantizers, blocksize, groupsize, static_grou
 
 
 def run_compensation_g2ptq(W, Hinv, Z, GHinv, quantizers, blocksize, groupsize,
-                           static_groups, qparam_perm=None, H_diag=None):
-    """g2ptq_utils.py:252-347; mutates ``W`` and ``GHinv`` -> ``(Q, W_int, Scale)``."""
+                           static_groups, qparam_perm=None, H_diag=None, approx_beta=0.0):
+    """g2ptq_utils.py:252-347; mutates ``W`` and ``GHinv`` -> ``(Q, W_int, Scale)``.
+    With ``approx_beta`` the raw weights are the traversal's input ``W``
+    (snapshot taken before the first block, line 273)."""
     B, R, C = W.shape
+    W_raw = W.copy() if approx_beta else None
     Q = np.zeros_like(W)
     W_int = np.zeros_like(W)
     Scale = np.zeros_like(W)
@@ -188,7 +203,9 @@ def run_compensation_g2ptq(W, Hinv, Z, GHinv, quantizers, blocksize, groupsize,
         S1, Zr1 = _stack_params(cq, W1.shape)
         q, qi, err, _ = g2ptq_block(W1.transpose(0, 2, 1), Hinv[:, i1:i2, i1:i2],
                                     S1.transpose(0, 2, 1), Zr1.transpose(0, 2, 1),
-                                    Z1.transpose(0, 2, 1), GH1.transpose(0, 2, 1), maxq)
+                                    Z1.transpose(0, 2, 1), GH1.transpose(0, 2, 1), maxq,
+                                    None if W_raw is None
+                                    else W_raw[:, :, i1:i2].transpose(0, 2, 1), approx_beta)
         Q[:, :, i1:i2] = q.transpose(0, 2, 1)
         W_int[:, :, i1:i2] = qi.transpose(0, 2, 1)
         Scale[:, :, i1:i2] = S1

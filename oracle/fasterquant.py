@@ -159,8 +159,10 @@ def trust_region(grad, Hinv_init, Q_sub, W_sub, alpha):
 
 def g2ptq_fasterquant(W, H, act_square, gradients, quantizers, num_groups, blocksize=128,
                       percdamp=0.01, groupsize=-1, actorder=False, static_groups=False,
-                      enable_gradient_update=True, alpha=0.0, route="reference", U=None):
-    """g2ptq_utils.py:349-519 (approx_grad_beta = 0) -> ``(Q, W_int, Scale, info)``.
+                      enable_gradient_update=True, alpha=0.0, route="reference", U=None,
+                      approx_beta=0.0):
+    """g2ptq_utils.py:349-519 -> ``(Q, W_int, Scale, info)``; ``approx_beta`` is
+    the object's ``approx_grad_beta`` (the ``--approx_grad`` ablation).
 
     ``H`` is ``[B, G, C, C]``, ``gradients`` ``[B, R, C]``, ``act_square`` ``[B, C]``;
     ``U`` (optional, ``[B*G, C, C]`` in the act-order column order) replaces the
@@ -213,7 +215,7 @@ def g2ptq_fasterquant(W, H, act_square, gradients, quantizers, num_groups, block
     Wc = W_sub.copy()
     Q, W_int, Scale = run_compensation_g2ptq(
         Wc, U, Z, GHinv, quantizers, blocksize, groupsize, static_groups,
-        perm if (static_groups and actorder) else None, H_diag)
+        perm if (static_groups and actorder) else None, H_diag, approx_beta)
     if actorder:
         Q, W_int, Scale = Q[:, :, invperm], W_int[:, :, invperm], Scale[:, :, invperm]
     return (Q.reshape(B, R, C), W_int.reshape(B, R, C), Scale.reshape(B, R, C),

@@ -221,6 +221,50 @@ def gen_blocks(ref):
     save("blocks.npz", **out)
 
 
+APPROX_BETA = 0.3
+
+
+def gen_approx(ref):
+    """G2PTQ's ``--approx_grad`` ablation (``approx_beta`` != 0): the block
+    cases through the reference's torch compensation with a raw-weight
+    snapshot, and whole ``fasterquant`` runs with ``approx_grad_beta``."""
+    out = {"beta": np.array(APPROX_BETA, np.float32)}
+    for name, batch, columns, rows, maxq, asym, seed in BLOCK_CASES:
+        weight, hinv, scale, zero, z, ghinv, p = block_inputs(batch, columns, rows, maxq,
+                                                              asym, seed)
+        gen = torch.Generator().manual_seed(seed + 7)
+        raw = weight + torch.randn(weight.shape, generator=gen) * scale * 0.3
+        w, gh = weight.clone(), ghinv.clone()
+        qi, err = torch.empty_like(weight), torch.empty_like(weight)
+        ref.g2ptq._run_torch_compensation(w, hinv.clone(), scale, zero, z.clone(), gh, qi, err,
+                                          maxq, weight_raw=raw.clone(), approx_beta=APPROX_BETA)
+        out[f"{name}__raw"] = npy(raw)
+        out[f"{name}__q"], out[f"{name}__int"] = npy(w), npy(qi)
+        out[f"{name}__err"], out[f"{name}__ghinv"] = npy(err), npy(gh)
+    gen = torch.Generator().manual_seed(46)
+    for name, bits, sym, gs, act, B, R, C, blk in FQ_CASES[1:3]:
+        layers = [torch.nn.Linear(C, R, bias=False) for _ in range(B)]
+        for l in layers:
+            l.weight.data = torch.randn(R, C, generator=gen) * 0.02
+        W0 = torch.stack([l.weight.data.clone() for l in layers])
+        G = 4
+        sal = [[torch.rand(300, G, generator=gen)] for _ in range(B)]
+        grads = [torch.randn(R, C, generator=gen) * 1e-3 for _ in range(B)]
+        g2 = ref.g2ptq.G2PTQ(layers, [list(s) for s in sal], grads, num_groups=G,
+                             approx_grad_beta=APPROX_BETA)
+        g2.quantizer = make_quantizers(ref, bits, sym, C, gs)
+        for b in range(B):
+            g2.add_batch(b, hessian_from(gen, C, 300), None)
+        out[f"{name}__W"] = npy(W0)
+        out[f"{name}__grad"] = npy(torch.stack(grads))
+        out[f"{name}__H"] = npy(g2.H)
+        out[f"{name}__act_square"] = npy(g2.act_square)
+        g2.fasterquant(blocksize=blk, percdamp=0.01, groupsize=gs, actorder=act,
+                       static_groups=act, enable_gradient_update=True, alpha=1.0)
+        out[f"{name}__Q"] = npy(torch.stack([l.weight.data for l in layers]))
+    save("approx.npz", **out)
+
+
 # ---------------------------------------------------------------------------
 # Whole fasterquant pipelines
 # ---------------------------------------------------------------------------
@@ -664,7 +708,8 @@ def gen_stack():
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of the reference checkout")
-    ap.add_argument("--only", default=None, help="one fixture family: export, refresh or stack")
+    ap.add_argument("--only", default=None,
+                    help="one fixture family: export, refresh, stack or approx")
     args = ap.parse_args()
     torch.set_num_threads(min(8, os.cpu_count() or 1))
     ref = import_reference(os.path.abspath(args.reference))
@@ -677,6 +722,9 @@ def main():
     if args.only == "stack":
         gen_stack()
         return
+    if args.only == "approx":
+        gen_approx(ref)
+        return
     gen_hessians(ref)
     gen_blocks(ref)
     gen_fasterquant(ref)
@@ -684,6 +732,7 @@ def main():
     gen_export(os.path.abspath(args.reference))
     gen_refresh(ref)
     gen_stack()
+    gen_approx(ref)
 
 
 if __name__ == "__main__":

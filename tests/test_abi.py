@@ -59,7 +59,7 @@ def test_invalid_arguments_rejected_without_gpu(lib):
     assert lib.g2q_gemm(None, 0, 0, None, 0, 0, 0, None, 0, 0, 0, 1, 1, 1, 1,
                         ctypes.c_float(0), ctypes.c_float(1), 0, None) == -1
     assert lib.g2q_compensate_block(0, None, 0, 0, 0, 0, 0, None, 0, 0, None, None, 0, None,
-                                    7, None, None, None, None, None, None) == -1
+                                    7, None, None, None, None, None, None, 0.0, None) == -1
     assert lib.g2q_pack_int32(None, None, 1, 1, 4, None) == -1
 
 
