@@ -15,13 +15,14 @@ and quantization parameters.  So here, after the token-parallel calibration:
    ``layers * C^3``; objects whose Hessians are bit-identical copies of one
    shared fold (q/k/v, gate/up) reduce and factor once;
 2. the owner applies the RTN fallback / dead columns, the act-order
-   permutation and the damped inverse-Cholesky chain with its damp retry,
-   and broadcasts U (packed), the permutation, the raw Hessian diagonal and
-   the damps -- one byte buffer per owner rank;
-3. every rank quantizes its slice of rows of every layer (static group
-   parameters, dead columns, compensation, un-permutation, cast, code
-   packing) with exactly the kernels of the single-GPU path, so that every
-   row comes out bit-identical to it;
+   permutation and the damped inverse-Cholesky chain, and broadcasts U
+   (packed), the permutation, the raw Hessian diagonal, the damps and the
+   status words in one buffer per distinct Hessian, cheapest first;
+3. as each factor arrives, every rank quantizes its slice of rows of the
+   layers that use it (static group parameters, dead columns, compensation,
+   un-permutation, cast, code packing) with exactly the kernels of the
+   single-GPU path, so that every row comes out bit-identical to it; a
+   failed factorization is redone with the damp auto-increment afterwards;
 4. one ``all_gather`` hands all slices of all layers (weights, packed codes,
    export scales, quantizer parameters) to every rank.
 
@@ -147,6 +148,51 @@ def _mark(marks, name, dev):
         marks.append((name, ev))
 
 
+class _FactorBundle:
+    """What a factor owner sends for one distinct Hessian, laid out in one
+    byte buffer (every part 16-byte aligned) so that it crosses NCCL in one
+    broadcast and every rank reads it in place: the packed factor U, the raw
+    Hessian diagonal, the act-order permutation, the damps and the
+    factorization status words."""
+
+    def __init__(self, B, C, actorder, dev):
+        parts = [("U", B * C * (C + 1) // 2, torch.float32), ("diag", B * C, torch.float32),
+                 ("damps", B, torch.float32), ("info", B, torch.int32)]
+        if actorder:
+            parts.append(("perm", C, torch.int64))
+        offs, off = {}, 0
+        for name, n, dt in parts:
+            nbytes = n * torch.tensor([], dtype=dt).element_size()
+            offs[name] = (off, n, dt)
+            off += -(-nbytes // 16) * 16
+        self.buf = torch.zeros(off, dtype=torch.uint8, device=dev)
+        self.t = {name: self.buf[o:o + n * torch.tensor([], dtype=dt).element_size()].view(dt)
+                  for name, (o, n, dt) in offs.items()}
+        self.t["diag"] = self.t["diag"].view(B, C)
+        self.B, self.C = B, C
+        self.U = None  # the unpacked factor, once known on this rank
+
+
+def _factor_on_owner(o, bundle, percdamp, actorder):
+    """The owner's part for one distinct Hessian, enqueued on the current
+    stream: RTN fallback / dead columns, act-order permutation, the damped
+    inverse-Cholesky chain; results written into the bundle.  Returns what a
+    damp retry needs."""
+    t, H = bundle.t, o._H
+    t["diag"].copy_(torch.diagonal(H, dim1=-2, dim2=-1))
+    ops.prepare_hessian(H)
+    if actorder:
+        perm, _ = _engine.act_order_perm(ops.mean_diag(H))
+        t["perm"].copy_(perm)
+        H = ops.permute_sym(H, perm)
+    U, info, damps = _engine.factor_with_retry(H, percdamp)
+    ops.pack_upper(U, 1.0, out=t["U"])
+    t["info"].copy_(info)
+    t["damps"].fill_(float(percdamp))
+    bundle.U = U
+    return H, U, damps
+
+
 def fasterquant_rows(objs, blocksize=128, percdamp=0.01, groupsize=-1, actorder=False,
                      static_groups=False, export_compressed_tensors=False, backend="torch",
                      graph=False, streams=4, marks=None):
@@ -156,8 +202,16 @@ def fasterquant_rows(objs, blocksize=128, percdamp=0.01, groupsize=-1, actorder=
     every rank holds every layer's quantized weights, export buffers and
     quantizer parameters, as after ``fasterquant`` on a single GPU with the
     summed statistics.  ``backend`` and ``graph`` are accepted and ignored.
+
+    The factors are broadcast one distinct Hessian at a time, cheapest
+    first, and each object's rows start on a side stream as soon as its
+    factor has arrived, so the compensation of the small layers overlaps the
+    factorization of the largest.  A failed factorization (non-positive
+    pivot) is re-done with the damp auto-increment on its owner after the
+    row work, and the rows of the objects that use it are re-run.
+
     ``marks`` (optional list) receives ``(phase, CUDA event)`` pairs at the end
-    of the reduce, the factorization + broadcast, the row work and the gather."""
+    of the reduce, the factorization + row work, and the gather."""
     if not objs:
         return
     if export_compressed_tensors and actorder and not (groupsize == -1 or static_groups):
@@ -165,6 +219,8 @@ def fasterquant_rows(objs, blocksize=128, percdamp=0.01, groupsize=-1, actorder=
     world, rank = dist.get_world_size(), dist.get_rank()
     dev = objs[0].dev
     cur = torch.cuda.current_stream(dev)
+    rows_of = {o: row_ranges(o.rows, world)[rank] for o in objs}
+    args = (blocksize, groupsize, actorder, static_groups, export_compressed_tensors)
     with contextlib.ExitStack() as onloaded:
         for o in objs:
             onloaded.enter_context(o._maybe_onload_hessian())
@@ -191,70 +247,67 @@ def fasterquant_rows(objs, blocksize=128, percdamp=0.01, groupsize=-1, actorder=
         collectives.reduce_to_owners(entries, dev)
         _mark(marks, "reduce", dev)
 
-        # 2. factors on their owners (launched together, one status read),
-        # then one broadcast per owner rank
-        shared = {}
-        for o in distinct:
-            B, C = o.num_layers, o.columns
-            t = {"U": torch.empty(B * C * (C + 1) // 2, dtype=torch.float32, device=dev),
-                 "diag": torch.empty(B, C, dtype=torch.float32, device=dev),
-                 "damps": torch.empty(B, dtype=torch.float32, device=dev)}
-            if actorder:
-                t["perm"] = torch.empty(C, dtype=torch.int64, device=dev)
-            shared[o] = t
-        factored = []
-        for o in distinct:
+        # 2. factors, cheapest first; each broadcast as soon as its owner has
+        # enqueued it, and the rows that use it launched behind it
+        # The factorizations (the critical path) and the broadcasts run on the
+        # pool's high-priority stream; the row work on the others waits for
+        # each factor's broadcast on its own stream, never on the host.
+        users = {o: [u for u in objs if rep[u] is o] for o in distinct}
+        order = sorted(distinct, key=lambda o: o.num_layers * o.columns ** 3)
+        pool = _engine.stream_pool(dev, max(2, streams))
+        fs, row_streams = pool[0], pool[1:]
+        fs.wait_stream(cur)
+        bundles, retry_state, work = {}, {}, {}
+        n_launched = 0
+        for o in order:
+            bundle = _FactorBundle(o.num_layers, o.columns, actorder, dev)
+            bundles[o] = bundle
+            with torch.cuda.stream(fs):
+                if owner[o] == rank:
+                    retry_state[o] = _factor_on_owner(o, bundle, percdamp, actorder)
+                done = dist.broadcast(bundle.buf, src=owner[o], async_op=True)
+            for u in sorted(users[o], key=lambda u: -u.rows):
+                s = row_streams[n_launched % len(row_streams)]
+                n_launched += 1
+                s.wait_stream(cur)
+                with torch.cuda.stream(s):
+                    done.wait()  # this stream waits for the broadcast, not the host
+                    if bundle.U is None:
+                        B, C = bundle.B, bundle.C
+                        bundle.U = ops.unpack_upper(
+                            torch.empty(B, C, C, dtype=torch.float32, device=dev),
+                            bundle.t["U"], mirror=False)
+                    work[u] = _Rows(u, bundle.U, bundle.t, *rows_of[u], *args)
+        for s in pool:
+            cur.wait_stream(s)
+
+        # a failed factorization: its owner retries with the damp increment,
+        # everybody re-runs the rows that used it (collective, in order)
+        infos = _engine.sync_check(*[bundles[o].t["info"] for o in order])
+        k, failed = 0, []
+        for o in order:
+            codes = infos[k:k + o.num_layers]
+            k += o.num_layers
+            _engine.raise_device_errors(codes, [], timeouts_only=True)
+            if any(codes):
+                failed.append((o, codes))
+        for o, codes in failed:
+            bundle = bundles[o]
+            if owner[o] == rank:
+                H, U, damps = retry_state[o]
+                _engine.retry_failed(H, U, codes, damps)
+                ops.pack_upper(U, 1.0, out=bundle.t["U"])
+                bundle.t["damps"].copy_(torch.tensor(damps, dtype=torch.float32))
+                bundle.t["info"].zero_()
+            dist.broadcast(bundle.buf, src=owner[o])
             if owner[o] != rank:
-                continue
-            t, H = shared[o], o._H
-            t["diag"].copy_(torch.diagonal(H, dim1=-2, dim2=-1))
-            ops.prepare_hessian(H)
-            if actorder:
-                perm, _ = _engine.act_order_perm(ops.mean_diag(H))
-                t["perm"].copy_(perm)
-                H = ops.permute_sym(H, perm)
-            U, info, damps = _engine.factor_with_retry(H, percdamp)
-            factored.append((o, H, U, info, damps))
-        if factored:
-            infos = _engine.sync_check(*[f[3] for f in factored])
-            k = 0
-            for o, H, U, info, damps in factored:
-                codes = infos[k:k + o.num_layers]
-                k += o.num_layers
-                _engine.raise_device_errors(codes, [], timeouts_only=True)
-                if any(codes):
-                    _engine.retry_failed(H, U, codes, damps)
-                t = shared[o]
-                ops.pack_upper(U, 1.0, out=t["U"])
-                t["damps"].copy_(torch.tensor(damps, dtype=torch.float32))
-                t["_U"] = U
-        collectives.broadcast_from_owners(
-            [collectives.Entry(owner[o], shared[o][k]) for o in distinct
-             for k in ("U", "diag", "damps", "perm") if k in shared[o]], dev)
-        for o in distinct:
-            t = shared[o]
-            if "_U" not in t:
-                B, C = o.num_layers, o.columns
-                t["_U"] = ops.unpack_upper(torch.empty(B, C, C, dtype=torch.float32, device=dev),
-                                           t["U"], mirror=False)
+                ops.unpack_upper(bundle.U, bundle.t["U"], mirror=False)
+            for u in users[o]:
+                work[u] = _Rows(u, bundle.U, bundle.t, *rows_of[u], *args)
         for o in objs:
             o._H = None
-    _mark(marks, "factor", dev)
-
-    # 3. this rank's rows of every object, longest first on a small stream pool
-    pool = _engine.stream_pool(dev, streams)
-    order = sorted(objs, key=lambda o: -o.num_layers * o.rows * o.columns ** 2)
-    work = {}
-    for n, o in enumerate(order):
-        s = pool[0] if n == 0 else pool[1 + (n - 1) % (len(pool) - 1)]
-        s.wait_stream(cur)
-        r0, r1 = row_ranges(o.rows, world)[rank]
-        with torch.cuda.stream(s):
-            work[o] = _Rows(o, shared[rep[o]]["_U"], shared[rep[o]], r0, r1, blocksize,
-                            groupsize, actorder, static_groups, export_compressed_tensors)
-    for s in pool:
-        cur.wait_stream(s)
-    _mark(marks, "compensate", dev)
+        retry_state.clear()
+    _mark(marks, "factor_and_compensate", dev)
 
     # errors on any rank stop every rank before the gather
     flat = _engine.sync_check(ops.device_status(dev),
@@ -316,5 +369,5 @@ def fasterquant_rows(objs, blocksize=128, percdamp=0.01, groupsize=-1, actorder=
         for b, layer in enumerate(o.layers):
             if export_compressed_tensors:
                 layer._export_qparams = staged[(o, b)]
-        o._last_damps = shared[rep[o]]["damps"].tolist()
+        o._last_damps = bundles[rep[o]].t["damps"].tolist()
         o._stages = None
