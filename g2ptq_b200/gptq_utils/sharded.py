@@ -11,18 +11,20 @@ walks the same columns with the same ``U`` and only its own weights, errors
 and quantization parameters.  So here, after the token-parallel calibration:
 
 1. each distinct Hessian is reduced once (packed upper triangle, weighted
-   by the ranks' sample shares) to a factor owner chosen by LPT over
-   ``layers * C^3``; objects whose Hessians are bit-identical copies of one
-   shared fold (q/k/v, gate/up) reduce and factor once;
-2. the owner applies the RTN fallback / dead columns, the act-order
-   permutation and the damped inverse-Cholesky chain, and broadcasts U
-   (packed), the permutation, the raw Hessian diagonal, the damps and the
-   status words in one buffer per distinct Hessian, cheapest first;
-3. as each factor arrives, every rank quantizes its slice of rows of the
-   layers that use it (static group parameters, dead columns, compensation,
-   un-permutation, cast, code packing) with exactly the kernels of the
-   single-GPU path, so that every row comes out bit-identical to it; a
-   failed factorization is redone with the damp auto-increment afterwards;
+   by the ranks' sample shares) to its factor owner; objects whose Hessians
+   are bit-identical copies of one shared fold (q/k/v, gate/up) reduce and
+   factor once;
+2. the distinct Hessian with the largest factorization (the critical path:
+   down_proj's C = 14336 in a Llama layer) is factored on rank 0, which
+   broadcasts U (packed), the permutation, the raw Hessian diagonal, the
+   damps and the status words in one buffer; meanwhile the other ranks
+   quantize the other layers whole (LPT over their work);
+3. when the large factor arrives, every rank quantizes its slice of rows of
+   the layers that use it (static group parameters, dead columns,
+   compensation, un-permutation, cast, code packing) with exactly the
+   kernels of the single-GPU path, so that every row comes out
+   bit-identical to it; a failed factorization is re-done with the damp
+   auto-increment afterwards;
 4. one ``all_gather`` hands all slices of all layers (weights, packed codes,
    export scales, quantizer parameters) to every rank.
 
@@ -198,20 +200,21 @@ def fasterquant_rows(objs, blocksize=128, percdamp=0.01, groupsize=-1, actorder=
                      graph=False, streams=4, marks=None):
     """``fasterquant`` of every GPTQ object in ``objs`` (the same list on every
     rank, calibrated on each rank's token shard) with the work split over
-    all ranks: factorizations by object, compensation by rows.  On return
-    every rank holds every layer's quantized weights, export buffers and
-    quantizer parameters, as after ``fasterquant`` on a single GPU with the
-    summed statistics.  ``backend`` and ``graph`` are accepted and ignored.
+    all ranks.  On return every rank holds every layer's quantized weights,
+    export buffers and quantizer parameters, as after ``fasterquant`` on a
+    single GPU with the summed statistics.  ``backend`` and ``graph`` are
+    accepted and ignored.
 
-    The factors are broadcast one distinct Hessian at a time, cheapest
-    first, and each object's rows start on a side stream as soon as its
-    factor has arrived, so the compensation of the small layers overlaps the
-    factorization of the largest.  A failed factorization (non-positive
-    pivot) is re-done with the damp auto-increment on its owner after the
-    row work, and the rows of the objects that use it are re-run.
+    The distinct Hessian with the largest factorization is factored on rank 0
+    and broadcast; the rows of the layers that use it are split over all
+    ranks.  Every other distinct Hessian goes whole to one of the other ranks
+    (LPT over its factorization and compensation work), so that their work
+    overlaps the large factorization.  A failed factorization is re-done
+    with the damp auto-increment after the row work (collectively for the
+    shared one).
 
     ``marks`` (optional list) receives ``(phase, CUDA event)`` pairs at the end
-    of the reduce, the factorization + row work, and the gather."""
+    of the reduce, the factorizations + row work, and the gather."""
     if not objs:
         return
     if export_compressed_tensors and actorder and not (groupsize == -1 or static_groups):
@@ -231,11 +234,36 @@ def fasterquant_rows(objs, blocksize=128, percdamp=0.01, groupsize=-1, actorder=
         for o in objs:
             o._leave_groups()
 
+        # 0. the plan: the distinct Hessian with the largest factorization is
+        # factored on rank 0 and its rows are sharded over all ranks; every
+        # other one goes whole (factor and rows) to one of the other ranks by
+        # LPT over its factorization and compensation work
+        users = {o: [u for u in objs if rep[u] is o] for o in distinct}
+        fcost = {o: o.num_layers * o.columns ** 3 for o in distinct}
+        ccost = {o: sum(u.num_layers * u.rows * u.columns ** 2 for u in users[o])
+                 for o in distinct}
+        big = max(distinct, key=lambda o: fcost[o]) if world > 1 else None
+        rest = [o for o in distinct if o is not big]
+        owner = {}
+        if big is not None:
+            owner[big] = 0
+        if rest:
+            others = world - 1 if world > 1 else 1
+            _, _, placed = greedy_bin_packing(rest, others, lambda o: fcost[o] + ccost[o])
+            for o in rest:
+                owner[o] = placed[o] + (1 if world > 1 else 0)
+        rows_of = {}
+        for o in distinct:
+            for u in users[o]:
+                if o is big:
+                    rows_of[u] = row_ranges(u.rows, world)[rank]
+                else:  # whole on its owner; slices in rank order for the gather
+                    rows_of[u] = ((0, u.rows) if rank == owner[o] else
+                                  (0, 0) if rank < owner[o] else (u.rows, u.rows))
+
         # 1. statistics of the distinct Hessians to their factor owners
         local = [list(o._n) for o in distinct]
         glob = collectives.sum_counts(local, dev)
-        _, _, owner = greedy_bin_packing(distinct, world,
-                                         lambda o: o.num_layers * o.columns ** 3)
         entries = []
         for o, loc, gl in zip(distinct, local, glob):
             for b in range(o.num_layers):
@@ -247,29 +275,40 @@ def fasterquant_rows(objs, blocksize=128, percdamp=0.01, groupsize=-1, actorder=
         collectives.reduce_to_owners(entries, dev)
         _mark(marks, "reduce", dev)
 
-        # 2. factors, cheapest first; each broadcast as soon as its owner has
-        # enqueued it, and the rows that use it launched behind it
-        # The factorizations (the critical path) and the broadcasts run on the
-        # pool's high-priority stream; the row work on the others waits for
-        # each factor's broadcast on its own stream, never on the host.
-        users = {o: [u for u in objs if rep[u] is o] for o in distinct}
-        order = sorted(distinct, key=lambda o: o.num_layers * o.columns ** 3)
+        # 2. The large factorization (the critical path) and its broadcast run
+        # on the pool's high-priority stream; whole objects run factor-then-rows
+        # on the other streams of their owner; the shared rows of the large one
+        # wait for its broadcast on their own stream, never on the host.
         pool = _engine.stream_pool(dev, max(2, streams))
         fs, row_streams = pool[0], pool[1:]
-        fs.wait_stream(cur)
+        for s in pool:
+            s.wait_stream(cur)
         bundles, retry_state, work = {}, {}, {}
         n_launched = 0
-        for o in order:
-            bundle = _FactorBundle(o.num_layers, o.columns, actorder, dev)
-            bundles[o] = bundle
+        for o in distinct:
+            bundles[o] = _FactorBundle(o.num_layers, o.columns, actorder, dev)
+        if big is not None:
+            bundle = bundles[big]
             with torch.cuda.stream(fs):
-                if owner[o] == rank:
-                    retry_state[o] = _factor_on_owner(o, bundle, percdamp, actorder)
-                done = dist.broadcast(bundle.buf, src=owner[o], async_op=True)
-            for u in sorted(users[o], key=lambda u: -u.rows):
+                if rank == owner[big]:
+                    retry_state[big] = _factor_on_owner(big, bundle, percdamp, actorder)
+                done = dist.broadcast(bundle.buf, src=owner[big], async_op=True)
+        for o in sorted(rest, key=lambda o: -(fcost[o] + ccost[o])):
+            if owner[o] != rank:
+                for u in users[o]:
+                    work[u] = _Rows(u, None, bundles[o].t, *rows_of[u], *args)
+                continue
+            s = row_streams[n_launched % len(row_streams)]
+            n_launched += 1
+            with torch.cuda.stream(s):
+                retry_state[o] = _factor_on_owner(o, bundles[o], percdamp, actorder)
+                for u in users[o]:
+                    work[u] = _Rows(u, bundles[o].U, bundles[o].t, *rows_of[u], *args)
+        if big is not None:
+            bundle = bundles[big]
+            for u in sorted(users[big], key=lambda u: -u.rows):
                 s = row_streams[n_launched % len(row_streams)]
                 n_launched += 1
-                s.wait_stream(cur)
                 with torch.cuda.stream(s):
                     done.wait()  # this stream waits for the broadcast, not the host
                     if bundle.U is None:
@@ -281,11 +320,13 @@ def fasterquant_rows(objs, blocksize=128, percdamp=0.01, groupsize=-1, actorder=
         for s in pool:
             cur.wait_stream(s)
 
-        # a failed factorization: its owner retries with the damp increment,
-        # everybody re-runs the rows that used it (collective, in order)
-        infos = _engine.sync_check(*[bundles[o].t["info"] for o in order])
+        # a failed factorization: its owner retries with the damp increment and
+        # re-runs the rows that used it; for the shared factor the retry is
+        # collective (its status words reached every rank with the broadcast)
+        mine = [o for o in distinct if o is big or owner[o] == rank]
+        infos = _engine.sync_check(*[bundles[o].t["info"] for o in mine])
         k, failed = 0, []
-        for o in order:
+        for o in mine:
             codes = infos[k:k + o.num_layers]
             k += o.num_layers
             _engine.raise_device_errors(codes, [], timeouts_only=True)
@@ -299,9 +340,10 @@ def fasterquant_rows(objs, blocksize=128, percdamp=0.01, groupsize=-1, actorder=
                 ops.pack_upper(U, 1.0, out=bundle.t["U"])
                 bundle.t["damps"].copy_(torch.tensor(damps, dtype=torch.float32))
                 bundle.t["info"].zero_()
-            dist.broadcast(bundle.buf, src=owner[o])
-            if owner[o] != rank:
-                ops.unpack_upper(bundle.U, bundle.t["U"], mirror=False)
+            if o is big:
+                dist.broadcast(bundle.buf, src=owner[o])
+                if owner[o] != rank:
+                    ops.unpack_upper(bundle.U, bundle.t["U"], mirror=False)
             for u in users[o]:
                 work[u] = _Rows(u, bundle.U, bundle.t, *rows_of[u], *args)
         for o in objs:
@@ -359,6 +401,11 @@ def fasterquant_rows(objs, blocksize=128, percdamp=0.01, groupsize=-1, actorder=
                 pieces.append((w.gscale[b] if w.n else qp["weight_scale"][:0],
                                qp["weight_scale"]))
                 staged[(o, b)] = qp
+    # the damps of every factorization, from its owner (one small exchange)
+    collectives.broadcast_from_owners(
+        [collectives.Entry(owner[o], bundles[o].t["damps"]) for o in distinct if o is not big],
+        dev)
+    damps_of = {o: bundles[o].t["damps"].tolist() for o in distinct}
     collectives.all_gather_rows(pieces, dev)
     _mark(marks, "gather", dev)
     for o in objs:
@@ -369,5 +416,5 @@ def fasterquant_rows(objs, blocksize=128, percdamp=0.01, groupsize=-1, actorder=
         for b, layer in enumerate(o.layers):
             if export_compressed_tensors:
                 layer._export_qparams = staged[(o, b)]
-        o._last_damps = bundles[rep[o]].t["damps"].tolist()
+        o._last_damps = damps_of[rep[o]]
         o._stages = None
