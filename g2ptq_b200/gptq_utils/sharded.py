@@ -292,6 +292,7 @@ def fasterquant_rows(objs, blocksize=128, percdamp=0.01, groupsize=-1, actorder=
             with torch.cuda.stream(fs):
                 if rank == owner[big]:
                     retry_state[big] = _factor_on_owner(big, bundle, percdamp, actorder)
+                _mark(marks, "big_factor", dev)
                 done = dist.broadcast(bundle.buf, src=owner[big], async_op=True)
         for o in sorted(rest, key=lambda o: -(fcost[o] + ccost[o])):
             if owner[o] != rank:
@@ -304,6 +305,7 @@ def fasterquant_rows(objs, blocksize=128, percdamp=0.01, groupsize=-1, actorder=
                 retry_state[o] = _factor_on_owner(o, bundles[o], percdamp, actorder)
                 for u in users[o]:
                     work[u] = _Rows(u, bundles[o].U, bundles[o].t, *rows_of[u], *args)
+        n_first_big = n_launched
         if big is not None:
             bundle = bundles[big]
             for u in sorted(users[big], key=lambda u: -u.rows):
@@ -311,6 +313,8 @@ def fasterquant_rows(objs, blocksize=128, percdamp=0.01, groupsize=-1, actorder=
                 n_launched += 1
                 with torch.cuda.stream(s):
                     done.wait()  # this stream waits for the broadcast, not the host
+                    if n_launched == n_first_big + 1:
+                        _mark(marks, "big_received", dev)
                     if bundle.U is None:
                         B, C = bundle.B, bundle.C
                         bundle.U = ops.unpack_upper(
