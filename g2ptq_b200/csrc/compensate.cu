@@ -6,6 +6,8 @@
 // columns through the shared row U[c, c+1:].  The block of U (and of P for
 // GPTAQ) sits in shared memory; the trailing update of the columns after the
 // block is a GEMM (gemm_simt.cu or gemm_tc.cu).
+#include <cuda_fp16.h>
+
 #include "gemm_simt.cuh"
 
 namespace g2q {
@@ -30,6 +32,14 @@ struct BlockParams {
   long long lde, e_bs;
   float* erra;  // optional trailing-update operand, column-major (ldea, ea_bs)
   long long ldea, ea_bs;
+  // optional fp16 hi/lo copy of the trailing-update operand for the tensor
+  // cores: column-major (ldea, eh_bs), each row scaled by a power of two that
+  // puts its largest magnitude in [2^14, 2^15); the inverse scale of row r goes
+  // to eh_scale[b * rows + r]
+  __half* eh_hi;
+  __half* eh_lo;
+  float* eh_scale;
+  long long eh_bs;
   const float* z;  // G2PTQ, row-major (ldz, z_bs)
   float* gh;
   long long ldz, z_bs;
@@ -313,6 +323,29 @@ __global__ void __launch_bounds__(BlockCfg::THREADS, 2) block_kernel(BlockParams
   // errors, column-major: consecutive threads take consecutive rows of a column
   __syncthreads();
   const long long row0 = (long long)blockIdx.x * QROWS;
+  // fp16 split of the trailing-update operand: the QT threads of a row find
+  // its largest magnitude over the block's columns
+  __shared__ float rowf[QROWS];
+  if (P.eh_hi) {
+    const float* src = (METHOD == G2Q_METHOD_G2PTQ) ? EAs : Es;
+    float m = 0.f;
+    for (int i = t; i < nc; i += QT) m = fmaxf(m, fabsf(src[rl * LDE + i]));
+#pragma unroll
+    for (int o = QT / 2; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (t == 0) {
+      float f = 1.f, v = 1.f;
+      if (m > 0.f && m <= 3.0e38f) {
+        int e;
+        frexpf(m, &e);
+        e = e < -100 ? -100 : e;
+        f = ldexpf(1.f, 15 - e);
+        v = ldexpf(1.f, e - 15);
+      }
+      rowf[rl] = f;
+      if (active) P.eh_scale[(long long)b * P.rows + r] = v;
+    }
+    __syncthreads();
+  }
   for (int idx = tid; idx < QROWS * nc; idx += QT * QROWS) {
     const int i = idx / QROWS, q = idx % QROWS;
     const long long rq = row0 + q;
@@ -322,6 +355,13 @@ __global__ void __launch_bounds__(BlockCfg::THREADS, 2) block_kernel(BlockParams
     if (P.err) P.err[(long long)b * P.e_bs + (long long)i * P.lde + rq] = e;
     const long long ao = (long long)b * P.ea_bs + (long long)i * P.ldea + rq;
     if (P.erra) P.erra[ao] = ea;
+    if (P.eh_hi) {
+      const float v = ea * rowf[q];
+      const __half h = __float2half_rn(v);
+      const long long ho = (long long)b * P.eh_bs + (long long)i * P.ldea + rq;
+      P.eh_hi[ho] = h;
+      P.eh_lo[ho] = __float2half_rn(v - __half2float(h));
+    }
   }
 }
 
@@ -724,12 +764,50 @@ int gemm_tc_f32(float* C, long long ldc, long long sC, const float* A, long long
                 int mask, void* workspace, size_t workspace_bytes, int* status, cudaStream_t st);
 }  // namespace g2q
 
+// Deferred trailing update of GPTQ: blocks are grouped SUPER at a time; after
+// each block only the rest of its group is updated (K = one block), the
+// columns after the group once per group (K = SUPER blocks), so the HBM passes
+// over W's far columns drop SUPER-fold.
+constexpr int SUPER = 4;
+
+namespace g2q {
+int split2h_strips(const float* src, long long lds, long long n, int K, __half* hi, __half* lo,
+                   long long ldd, float* scale, int transpose, int ny, long long src_by,
+                   long long dst_by, long long sc_by, int nz, long long src_bz,
+                   long long dst_bz, long long sc_bz, cudaStream_t st);
+int tc_update_f16(float* D, long long ldd, long long d_bs, long long M, long long N, int K,
+                  long long batch, __half* const* a2, long long lda, long long a_outer,
+                  long long ka_batch, long long ka0, const float* sa, long long sa_bs,
+                  __half* const* b2, long long ldb, long long b_inner, long long b_outer,
+                  long long kb_batch, long long kb0, long long nb0, const float* sb,
+                  long long sb_bs, float beta, int* status, cudaStream_t st);
+}  // namespace g2q
+
+// Layout of the workspace (each part 256-byte aligned): the errors of up to
+// SUPER blocks (fp32, column-major per block), the fp32-accurate GEMM's own
+// operand splits (far updates, and every update where the fused path does not
+// apply), and for GPTQ / G2PTQ at precision 1 the fused path's operands: the
+// error block's fp16 hi/lo pair and row scales, U cut into 128-row (at most)
+// strips as fp16 hi/lo pairs with a scale per strip and column, and for G2PTQ
+// Z's block columns transposed the same way with a scale per block and row.
 extern "C" size_t g2q_compensate_workspace_bytes(int method, int64_t nl, int64_t rows,
                                                  int64_t C, int precision) {
-  size_t b = (size_t)nl * rows * BLK * sizeof(float) + 256;  // the block's errors
-  // tensor-core trailing updates: fp16 hi/lo splits of one error block and one
-  // 128-row strip of U (or P), with their row / column scales
-  if (precision == 1) b += g2q::gemm_tc_workspace_bytes(rows, C, BLK, nl, nl) + 256;
+  const size_t S = (method == G2Q_METHOD_GPTQ && precision == 1) ? SUPER : 1;
+  size_t b = (size_t)nl * rows * BLK * S * sizeof(float) + 256;
+  if (precision == 1) {
+    b += g2q::gemm_tc_workspace_bytes(rows, C, (long long)S * BLK, nl, nl) + 256;
+    if (method != G2Q_METHOD_GPTAQ) {
+      const size_t strips = (size_t)(C / 64 + 1);  // blocks of >= 64 columns
+      b += 2 * ((size_t)nl * BLK * rows * sizeof(__half) + 256);
+      b += (size_t)nl * rows * sizeof(float) + 256;
+      b += 2 * ((size_t)nl * (C + BLK) * C * sizeof(__half) + 256);
+      b += (size_t)nl * strips * C * sizeof(float) + 256;
+      if (method == G2Q_METHOD_G2PTQ) {
+        b += 2 * ((size_t)nl * (C + BLK) * rows * sizeof(__half) + 256);
+        b += (size_t)nl * strips * rows * sizeof(float) + 256;
+      }
+    }
+  }
   return b;
 }
 
@@ -758,20 +836,80 @@ extern "C" int g2q_compensate(int method, float* W, int64_t nl, int64_t rows, in
   if (workspace_bytes < g2q_compensate_workspace_bytes(method, nl, rows, C, precision))
     return G2Q_ERR_INVALID_ARG;
   cudaStream_t st = (cudaStream_t)stream;
-  char* wsp = align_up((char*)workspace, 256);
-  float* erra = (float*)wsp;
-  wsp = align_up(wsp + (size_t)nl * rows * BLK * sizeof(float), 256);
   const int maxq = (1 << (bits - 1)) - 1;
-  // Tensor-core trailing updates run through the fp32-accurate GEMM: each
-  // operand becomes an fp16 hi/lo pair after a power-of-two scale per output
-  // row (the error block) or column (U's strip), 22 significant bits, three
-  // products per K step (a bf16 hi/lo pair keeps 16 bits, and over the 112
-  // blocks of a 14336-column layer that drift flipped 0.14 % of the codes).
   const bool use_tc = precision == 1;
-  const size_t gws = use_tc ? gemm_tc_workspace_bytes(rows, C, BLK, nl, nl) : 0;
+  // fused tensor-core updates: operands pre-split once (U, Z) or by the block
+  // kernel itself (the error block), one GEMM launch per update
+  const bool fused = use_tc && method != G2Q_METHOD_GPTAQ && blocksize % 64 == 0 &&
+                     rows % 8 == 0 && C % 8 == 0;
+  // GPTQ defers far updates when no group's parameters read columns beyond
+  // the block they start in (static groups: found before the traversal)
+  const bool defer = fused && method == G2Q_METHOD_GPTQ &&
+                     (!dynamic_groups || blocksize % groupsize == 0);
+  const int S = defer ? SUPER : 1;
+  const int S_ws = (method == G2Q_METHOD_GPTQ && use_tc) ? SUPER : 1;
+  char* wsp = align_up((char*)workspace, 256);
+  auto take = [&](size_t bytes) {
+    char* q = wsp;
+    wsp = align_up(wsp + bytes, 256);
+    return q;
+  };
+  float* erra = (float*)take((size_t)nl * rows * BLK * S_ws * sizeof(float));
+  const size_t gws = use_tc ? gemm_tc_workspace_bytes(rows, C, (long long)S_ws * BLK, nl, nl)
+                            : 0;
+  void* gwsp = use_tc ? (void*)take(gws) : nullptr;
+  const long long nblk = (C + blocksize - 1) / blocksize;
+  const long long nupd = nblk - 1;  // blocks followed by a trailing update (all full)
+  __half *eh[2] = {nullptr, nullptr}, *uh[2] = {nullptr, nullptr}, *zh[2] = {nullptr, nullptr};
+  float *eh_sc = nullptr, *u_sc = nullptr, *z_sc = nullptr;
+  if (fused) {
+    eh[0] = (__half*)take((size_t)nl * BLK * rows * sizeof(__half));
+    eh[1] = (__half*)take((size_t)nl * BLK * rows * sizeof(__half));
+    eh_sc = (float*)take((size_t)nl * rows * sizeof(float));
+    uh[0] = (__half*)take((size_t)nl * (C + BLK) * C * sizeof(__half));
+    uh[1] = (__half*)take((size_t)nl * (C + BLK) * C * sizeof(__half));
+    u_sc = (float*)take((size_t)nl * (C / 64 + 1) * C * sizeof(float));
+    if (method == G2Q_METHOD_G2PTQ) {
+      zh[0] = (__half*)take((size_t)nl * (C + BLK) * rows * sizeof(__half));
+      zh[1] = (__half*)take((size_t)nl * (C + BLK) * rows * sizeof(__half));
+      z_sc = (float*)take((size_t)nl * (C / 64 + 1) * rows * sizeof(float));
+    }
+    if (nupd > 0) {
+      // U's strips: strip k = rows [k bs, (k+1) bs), one scale per strip and column
+      G2Q_TRY(split2h_strips(U, C, C, blocksize, uh[0], uh[1], C, u_sc, 0, (int)nupd,
+                             (long long)blocksize * C, (long long)blocksize * C, C, (int)nl,
+                             C * C, nupd * blocksize * C, nupd * C, st));
+      // Z's block columns, transposed: [k][row], one scale per block and row
+      if (method == G2Q_METHOD_G2PTQ)
+        G2Q_TRY(split2h_strips(z, C, rows, blocksize, zh[0], zh[1], rows, z_sc, 1, (int)nupd,
+                               blocksize, (long long)blocksize * rows, rows, (int)nl,
+                               rows * C, nupd * blocksize * rows, nupd * rows, st));
+    }
+  }
+  // D[:, :, c0:c1] += beta * A @ P[k-rows of the block, c0:c1] on fp32 operands:
+  // tensor cores, or CUDA cores where TMA cannot describe them.  A is stored
+  // k-major (column-major error) when a_kmajor, else row-major.
+  auto update_f32 = [&](float* D, long long c0, long long c1, const float* A, long long lda,
+                        long long a_bs, bool a_kmajor, const float* Pm, long long k0, int K,
+                        float beta) -> int {
+    const long long N = c1 - c0;
+    if (N <= 0) return G2Q_OK;
+    if (use_tc) {
+      const int s = gemm_tc_f32(D + c0, C, rows * C, A, lda, a_bs, a_kmajor, Pm + k0 * C + c0, C,
+                                C * C, false, rows, N, K, nl, 1.f, beta, G2Q_MASK_FULL, gwsp, gws,
+                                status, st);
+      if (s != G2Q_ERR_UNSUPPORTED) return s;
+    }
+    return simt_gemm_f32(D + c0, C, A, lda, a_kmajor, Pm + k0 * C + c0, C, false, rows, N, K,
+                         1.f, beta, G2Q_MASK_FULL, st, nl, a_bs, C * C, rows * C);
+  };
   for (long long i1 = 0; i1 < C; i1 += blocksize) {
     const long long i2 = (i1 + blocksize < C) ? i1 + blocksize : C;
     const int nc = (int)(i2 - i1);
+    const long long kb = i1 / blocksize;
+    const int j = (int)(kb % S);                       // place in its group of S blocks
+    const long long s1 = (kb - j) * blocksize;          // the group's first column
+    const long long s2 = (s1 + (long long)S * blocksize < C) ? s1 + (long long)S * blocksize : C;
     if (dynamic_groups) {
       // group starts c0 with i1 <= c0 < i2 and c0 % groupsize == 0
       const long long first = (i1 + groupsize - 1) / groupsize * groupsize;
@@ -787,7 +925,13 @@ extern "C" int g2q_compensate(int method, float* W, int64_t nl, int64_t rows, in
     P.scale = scale; P.zero = zero; P.param_ld = ngroups; P.colmap = colgroup + i1;
     P.maxq = maxq;
     P.codes = codes + i1; P.ldq = C; P.q_bs = rows * C;
-    P.erra = erra; P.ldea = rows; P.ea_bs = rows * BLK;
+    // block j of its group keeps its errors at k = j * blocksize, so that the
+    // group's errors form one contiguous K range for the far update
+    P.erra = erra + (size_t)j * blocksize * rows; P.ldea = rows;
+    P.ea_bs = (long long)S * BLK * rows;
+    if (fused && i2 < C) {
+      P.eh_hi = eh[0]; P.eh_lo = eh[1]; P.eh_scale = eh_sc; P.eh_bs = BLK * rows;
+    }
     if (method == G2Q_METHOD_G2PTQ) {
       P.z = z + i1; P.gh = gh + i1; P.ldz = C; P.z_bs = rows * C;
     }
@@ -806,37 +950,46 @@ extern "C" int g2q_compensate(int method, float* W, int64_t nl, int64_t rows, in
       G2Q_CHECK_LAUNCH();
     }
     // W[:, i2:] -= Erra @ U[i1:i2, i2:]  (+ G2PTQ: GH[:, i2:] -= Z[:, i1:i2] @ U[i1:i2, i2:];
-    // GPTAQ: W[:, i2:] += Q1 @ P[i1:i2, i2:])
-    if (use_tc) {
-      int s_tc = gemm_tc_f32(W + i2, C, rows * C, erra, rows, rows * BLK, true, U + i1 * C + i2, C,
-                             C * C, false, rows, N, nc, nl, 1.f, -1.f, G2Q_MASK_FULL, wsp, gws,
-                             status, st);
-      if (s_tc == G2Q_OK && method == G2Q_METHOD_G2PTQ) {
-        s_tc = gemm_tc_f32(gh + i2, C, rows * C, z + i1, C, rows * C, false, U + i1 * C + i2, C,
-                           C * C, false, rows, N, nc, nl, 1.f, -1.f, G2Q_MASK_FULL, wsp, gws,
-                           status, st);
-        if (s_tc != G2Q_OK) return s_tc == G2Q_ERR_UNSUPPORTED ? G2Q_ERR_CUDA : s_tc;
-      } else if (s_tc == G2Q_OK && method == G2Q_METHOD_GPTAQ) {
-        s_tc = gemm_tc_f32(W + i2, C, rows * C, W + i1, C, rows * C, false, p + i1 * C + i2, C,
-                           C * C, false, rows, N, nc, nl, 1.f, 1.f, G2Q_MASK_FULL, wsp, gws,
-                           status, st);
-        if (s_tc != G2Q_OK) return s_tc == G2Q_ERR_UNSUPPORTED ? G2Q_ERR_CUDA : s_tc;
+    // GPTAQ: W[:, i2:] += Q1 @ P[i1:i2, i2:]).  With deferral the block updates
+    // only [i2, s2) and the last block of the group the columns after it.
+    if (fused) {
+      __half* const ub[2] = {uh[0], uh[1]};
+      // one fused update of D[:, :, i2:c1] from the block's pre-split error
+      auto fused_update = [&](float* D, long long c1, __half* const* a2, long long a_outer,
+                              long long ka_batch, long long ka0, const float* sa,
+                              long long sa_bs) -> int {
+        return tc_update_f16(D + i2, C, rows * C, rows, c1 - i2, nc, nl, a2, rows, a_outer,
+                             ka_batch, ka0, sa, sa_bs, ub, C, C, nl * nupd * blocksize,
+                             nupd * blocksize, kb * blocksize, i2, u_sc + kb * C + i2, nupd * C,
+                             -1.f, status, st);
+      };
+      if (S == 1 || i2 < s2) {
+        // near update: the rest of the group (or, undeferred, every later column)
+        const long long c1 = (S == 1) ? C : s2;
+        int s_w = fused_update(W, c1, eh, nl * BLK, BLK, 0, eh_sc, rows);
+        if (s_w == G2Q_ERR_UNSUPPORTED)
+          s_w = update_f32(W, i2, c1, P.erra, rows, (long long)S * BLK * rows, true, U, i1, nc,
+                           -1.f);
+        G2Q_TRY(s_w);
+      } else if (s2 < C) {
+        // the group's far update, K = S blocks, from the fp32 errors
+        G2Q_TRY(update_f32(W, s2, C, erra, rows, (long long)S * BLK * rows, true, U, s1,
+                           (int)(s2 - s1), -1.f));
       }
-      if (s_tc == G2Q_OK) continue;
-      if (s_tc != G2Q_ERR_UNSUPPORTED) return s_tc;
+      if (method == G2Q_METHOD_G2PTQ) {
+        int s_g = fused_update(gh, C, zh, nl * nupd * blocksize, nupd * blocksize,
+                               kb * blocksize, z_sc + kb * rows, nupd * rows);
+        if (s_g == G2Q_ERR_UNSUPPORTED)
+          s_g = update_f32(gh, i2, C, z + i1, C, rows * C, false, U, i1, nc, -1.f);
+        G2Q_TRY(s_g);
+      }
+      continue;
     }
-    G2Q_TRY(simt_gemm_f32(W + i2, C, erra, rows, true, U + i1 * C + i2, C, false, rows, N, nc,
-                          1.f, -1.f, G2Q_MASK_FULL, st, nl, rows * BLK, C * C, rows * C));
-    if (method == G2Q_METHOD_G2PTQ) {
-      // GH[:, i2:] -= Z[:, i1:i2] @ U[i1:i2, i2:]
-      G2Q_TRY(simt_gemm_f32(gh + i2, C, z + i1, C, false, U + i1 * C + i2, C, false, rows, N,
-                            nc, 1.f, -1.f, G2Q_MASK_FULL, st, nl, rows * C, C * C, rows * C));
-    }
-    if (method == G2Q_METHOD_GPTAQ) {
-      // W[:, i2:] += Q1 @ P[i1:i2, i2:]
-      G2Q_TRY(simt_gemm_f32(W + i2, C, W + i1, C, false, p + i1 * C + i2, C, false, rows, N, nc,
-                            1.f, 1.f, G2Q_MASK_FULL, st, nl, rows * C, C * C, rows * C));
-    }
+    G2Q_TRY(update_f32(W, i2, C, P.erra, rows, (long long)S * BLK * rows, true, U, i1, nc, -1.f));
+    if (method == G2Q_METHOD_G2PTQ)
+      G2Q_TRY(update_f32(gh, i2, C, z + i1, C, rows * C, false, U, i1, nc, -1.f));
+    if (method == G2Q_METHOD_GPTAQ)
+      G2Q_TRY(update_f32(W, i2, C, W + i1, C, rows * C, false, p, i1, nc, 1.f));
   }
   return G2Q_OK;
 }

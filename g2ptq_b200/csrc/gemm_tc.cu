@@ -1629,10 +1629,19 @@ int gemm_tc_f32(float* C, long long ldc, long long sC, const float* A, long long
 //   transpose == 0: src is [K][cols] (row stride lds), dst [K][cols], one scale
 //                   per column (the operand X_k of the Y update).
 // One block handles 32 rows (or columns) and all K <= 128 of them.
+// Batched over grid y and z: block (y, z) reads src + y * src_by + z * src_bz and
+// writes hi / lo + y * dst_by + z * dst_bz and scale + y * sc_by + z * sc_bz.
 __global__ void __launch_bounds__(256) split2h_kernel(const float* __restrict__ src,
                                                       long long lds, long long n, int K,
                                                       __half* hi, __half* lo, long long ldd,
-                                                      float* scale, int transpose) {
+                                                      float* scale, int transpose,
+                                                      long long src_by, long long dst_by,
+                                                      long long sc_by, long long src_bz,
+                                                      long long dst_bz, long long sc_bz) {
+  src += blockIdx.y * src_by + blockIdx.z * src_bz;
+  hi += blockIdx.y * dst_by + blockIdx.z * dst_bz;
+  lo += blockIdx.y * dst_by + blockIdx.z * dst_bz;
+  scale += blockIdx.y * sc_by + blockIdx.z * sc_bz;
   __shared__ float tile[128][33];
   __shared__ float smax[8][32];
   __shared__ float sfac[32];
@@ -1714,9 +1723,57 @@ int split2h(const float* src, long long lds, long long n, int K, __half* hi, __h
   if (n <= 0 || K <= 0) return G2Q_OK;
   if (K > 128) return G2Q_ERR_INVALID_ARG;
   split2h_kernel<<<cdiv(n, 32), dim3(32, 8), 0, st>>>(src, lds, n, K, hi, lo, ldd, scale,
-                                                      transpose);
+                                                      transpose, 0, 0, 0, 0, 0, 0);
   G2Q_CHECK_LAUNCH();
   return G2Q_OK;
+}
+
+// split2h over ny x nz strips in one launch (strip (y, z) at the given strides).
+int split2h_strips(const float* src, long long lds, long long n, int K, __half* hi, __half* lo,
+                   long long ldd, float* scale, int transpose, int ny, long long src_by,
+                   long long dst_by, long long sc_by, int nz, long long src_bz,
+                   long long dst_bz, long long sc_bz, cudaStream_t st) {
+  if (n <= 0 || K <= 0 || ny <= 0 || nz <= 0) return G2Q_OK;
+  if (K > 128 || ny > 65535 || nz > 65535) return G2Q_ERR_INVALID_ARG;
+  split2h_kernel<<<dim3(cdiv(n, 32), ny, nz), dim3(32, 8), 0, st>>>(
+      src, lds, n, K, hi, lo, ldd, scale, transpose, src_by, dst_by, sc_by, src_bz, dst_bz,
+      sc_bz);
+  G2Q_CHECK_LAUNCH();
+  return G2Q_OK;
+}
+
+// D[b][m][n] += beta sa[b][m] sb[b][n] sum_k A[b][k][m] B[b][k][n] over fp16 hi/lo pairs
+// (three products), batched: A's k-rows of batch b start at ka_batch b + ka0 in a
+// [a_outer][lda] tensor (M contiguous), B's at kb_batch b + kb0 in [b_outer][ldb]
+// (columns from nb0, b_inner wide).  The short-K tensor-core update of the lazy
+// compensation on pre-split operands.  Returns G2Q_ERR_UNSUPPORTED where TMA
+// cannot describe the operands.
+int tc_update_f16(float* D, long long ldd, long long d_bs, long long M, long long N, int K,
+                  long long batch, __half* const* a2, long long lda, long long a_outer,
+                  long long ka_batch, long long ka0, const float* sa, long long sa_bs,
+                  __half* const* b2, long long ldb, long long b_inner, long long b_outer,
+                  long long kb_batch, long long kb0, long long nb0, const float* sb,
+                  long long sb_bs, float beta, int* status, cudaStream_t st) {
+  if (M <= 0 || N <= 0 || K <= 0 || batch <= 0) return G2Q_OK;
+  if ((K % tc::BK) || !tc::encode_fn()) return G2Q_ERR_UNSUPPORTED;
+  tc::Maps mp{};
+  bool ok = true;
+  for (int i = 0; i < 2 && ok; ++i)
+    ok = tc::make_map(&mp.a[i], a2[i], M, a_outer, lda, true) &&
+         tc::make_map(&mp.b[i], b2[i], b_inner, b_outer, ldb, true);
+  if (!ok) return G2Q_ERR_UNSUPPORTED;
+  tc::Params p{};
+  p.status = status;
+  p.D = D; p.ldd = ldd; p.d_bs = d_bs;
+  p.M = M; p.N = N;
+  p.num_kb = K / tc::BK;
+  p.ka_batch = ka_batch; p.ka0 = ka0;
+  p.kb_batch = kb_batch; p.kb0 = kb0; p.nb0 = nb0;
+  p.alpha = 1.f; p.beta = beta;
+  p.f16 = 1;
+  p.sa = sa; p.sb = sb; p.sa_bs = sa_bs; p.sb_bs = sb_bs;
+  p.red = tc::make_map_out(&mp.d, D, N, M, batch, ldd, d_bs) ? 1 : 0;
+  return tc::dispatch(2, 2, mp, p, batch, st);
 }
 
 // fp32-accurate tensor-core update  D <- alpha D + beta * diag(sa) A^T B diag(sb)
