@@ -7,6 +7,7 @@
 // GPTAQ) sits in shared memory; the trailing update of the columns after the
 // block is a GEMM (gemm_simt.cu or gemm_tc.cu).
 #include <cuda_fp16.h>
+#include <stdlib.h>
 
 #include "gemm_simt.cuh"
 
@@ -767,8 +768,22 @@ int gemm_tc_f32(float* C, long long ldc, long long sC, const float* A, long long
 // Deferred trailing update of GPTQ: blocks are grouped SUPER at a time; after
 // each block only the rest of its group is updated (K = one block), the
 // columns after the group once per group (K = SUPER blocks), so the HBM passes
-// over W's far columns drop SUPER-fold.
+// over W's far columns drop SUPER-fold.  The workspace always has room for
+// SUPER blocks; the group size used is G2PTQ_B200_DEFER_BLOCKS (1 to SUPER,
+// default 1: measured, the K = 512 updates on the long-K kernel cost more than
+// the passes they save).
 constexpr int SUPER = 4;
+
+static int defer_blocks() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("G2PTQ_B200_DEFER_BLOCKS");
+    v = e ? atoi(e) : 1;
+    if (v < 1) v = 1;
+    if (v > SUPER) v = SUPER;
+  }
+  return v;
+}
 
 namespace g2q {
 int split2h_strips(const float* src, long long lds, long long n, int K, __half* hi, __half* lo,
@@ -846,7 +861,7 @@ extern "C" int g2q_compensate(int method, float* W, int64_t nl, int64_t rows, in
   // the block they start in (static groups: found before the traversal)
   const bool defer = fused && method == G2Q_METHOD_GPTQ &&
                      (!dynamic_groups || blocksize % groupsize == 0);
-  const int S = defer ? SUPER : 1;
+  const int S = defer ? defer_blocks() : 1;
   const int S_ws = (method == G2Q_METHOD_GPTQ && use_tc) ? SUPER : 1;
   char* wsp = align_up((char*)workspace, 256);
   auto take = [&](size_t bytes) {

@@ -1443,7 +1443,9 @@ int tc_gram_grouped(float* D, long long ldd, long long d_gstride, long long C, c
 // ---------------------------------------------------------------------------
 
 // Largest |x| of every output index of op(X) over K: kmajor != 0 means X is
-// stored [n][K] (one row per output index), else [K][n] (one column each).
+// stored [n][K] (one row per output index, one warp each), else [K][n] (one
+// column each: a CTA takes 32 columns, its eight warps eight interleaved
+// slices of K, combined in shared memory).
 __global__ void op_absmax_kernel(const float* __restrict__ X, long long ldx, long long xbs,
                                  long long n, long long K, int kmajor, float* fac,
                                  float* inv, long long obs) {
@@ -1452,7 +1454,6 @@ __global__ void op_absmax_kernel(const float* __restrict__ X, long long ldx, lon
   float m = 0.f;
   long long i;
   if (kmajor) {
-    // one warp per output index
     i = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (i < n)
@@ -1460,9 +1461,16 @@ __global__ void op_absmax_kernel(const float* __restrict__ X, long long ldx, lon
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     if (lane != 0) return;
   } else {
-    i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    __shared__ float part[8][32];
+    const int lane = threadIdx.x & 31, ws = threadIdx.x >> 5;
+    i = (long long)blockIdx.x * 32 + lane;
     if (i < n)
-      for (long long k = 0; k < K; ++k) m = fmaxf(m, fabsf(xb[k * ldx + i]));
+      for (long long k = ws; k < K; k += 8) m = fmaxf(m, fabsf(xb[k * ldx + i]));
+    part[ws][lane] = m;
+    __syncthreads();
+    if (ws != 0) return;
+#pragma unroll
+    for (int q = 1; q < 8; ++q) m = fmaxf(m, part[q][lane]);
   }
   if (i >= n) return;
   float f = 1.f, v = 1.f;
@@ -1577,11 +1585,11 @@ int gemm_tc_f32(float* C, long long ldc, long long sC, const float* A, long long
   // op(A)[m][k]: A stored [M][K] (k contiguous) unless ta; op(B)[k][n]: B stored
   // [K][N] (n contiguous) unless tb.
   const int a_kmajor = ta ? 0 : 1, b_kmajor = tb ? 1 : 0;
-  op_absmax_kernel<<<dim3(cdiv(M * (a_kmajor ? 32 : 1), 256), (unsigned)ba), 256, 0, st>>>(
-      A, lda, sA, M, K, a_kmajor, fa, ia, M);
+  op_absmax_kernel<<<dim3(a_kmajor ? cdiv(M * 32, 256) : cdiv(M, 32), (unsigned)ba), 256, 0,
+                     st>>>(A, lda, sA, M, K, a_kmajor, fa, ia, M);
   G2Q_CHECK_LAUNCH();
-  op_absmax_kernel<<<dim3(cdiv(N * (b_kmajor ? 32 : 1), 256), (unsigned)bb), 256, 0, st>>>(
-      B, ldb, sB, N, K, b_kmajor, fb, ib, N);
+  op_absmax_kernel<<<dim3(b_kmajor ? cdiv(N * 32, 256) : cdiv(N, 32), (unsigned)bb), 256, 0,
+                     st>>>(B, ldb, sB, N, K, b_kmajor, fb, ib, N);
   G2Q_CHECK_LAUNCH();
   op_split_kernel<<<dim3(cdiv(M, 32), cdiv(la.Kp, 32), (unsigned)ba), dim3(32, 8), 0, st>>>(
       A, lda, sA, M, K, la.Kp, a_kmajor, fa, M, a_hi, a_lo, la.ldo, la.Kp * la.ldo);
