@@ -64,6 +64,13 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--method", default="gptq", choices=sorted(METHODS),
                     help="gptq: BASELINE configs[1] (default); g2ptq: configs[2]")
+    ap.add_argument("--model", default="llama3-8b", choices=["llama3-8b", "qwen3-moe"],
+                    help="llama3-8b: one decoder layer's 7 linears (configs[1] / [2]); "
+                         "qwen3-moe: one Qwen3-30B-A3B MoE layer's 128 experts x 3 projections "
+                         "(configs[3])")
+    ap.add_argument("--moe-bsz", type=int, default=32,
+                    help="sequences per forward batch of the MoE workload (one add_batch call "
+                         "per hit expert and batch)")
     ap.add_argument("--multi", default="owner", choices=["rows", "owner"],
                     help="N>1: owner = the reference's flow over the coalesced collectives "
                          "(reduce to owners, each owner quantizes its layers, one broadcast "
@@ -535,6 +542,178 @@ def native_e2e(torch, dist, args, layers, world, rank, dev, n_local, dev_acts, g
 
 
 # ---------------------------------------------------------------------------
+# MoE workload: one Qwen3-30B-A3B MoE layer's experts
+# ---------------------------------------------------------------------------
+
+MOE_HIDDEN, MOE_INTER, MOE_EXPERTS, MOE_TOPK, MOE_LAYER_BSZ = 2048, 768, 128, 8, 64
+
+
+def make_moe(torch, dev, rank, world, args):
+    """Random-init experts (N(0, 0.02) BF16), a router N(0, 0.02), and this
+    rank's share of the calibration tokens routed top-8: per forward batch of
+    ``moe_bsz`` sequences the hidden states (BF16 N(0, 1), 4 outlier channels
+    x20) gathered into expert order, one contiguous row range per expert, and
+    the down projections' inputs (BF16 N(0, 1), the stand-in for
+    act(gate) * up).  Made outside the timed region, like the Llama
+    workload's activations."""
+    g = torch.Generator(device=dev).manual_seed(42)
+    experts = {}
+    for proj, (rows, cols) in (("gate_proj", (MOE_INTER, MOE_HIDDEN)),
+                               ("up_proj", (MOE_INTER, MOE_HIDDEN)),
+                               ("down_proj", (MOE_HIDDEN, MOE_INTER))):
+        for e in range(MOE_EXPERTS):
+            lin = torch.nn.Linear(cols, rows, bias=False, device=dev, dtype=torch.bfloat16)
+            lin.weight.data = (torch.randn(rows, cols, device=dev, generator=g) * 0.02).to(
+                torch.bfloat16)
+            experts[(proj, e)] = lin
+    router = torch.randn(MOE_EXPERTS, MOE_HIDDEN, device=dev, generator=g) * 0.02
+    lo, hi = args.seqs * rank // world, args.seqs * (rank + 1) // world
+    gx = torch.Generator(device=dev).manual_seed(43 + rank)
+    idx_out = torch.randperm(MOE_HIDDEN, device=dev, generator=gx)[:4]
+    batches = []
+    for s in range(lo, hi, args.moe_bsz):
+        n = min(args.moe_bsz, hi - s)
+        x = torch.randn(n * args.seq_len, MOE_HIDDEN, device=dev, generator=gx)
+        x[:, idx_out] *= 20.0
+        x = x.to(torch.bfloat16)
+        top = torch.topk(x.float() @ router.T, MOE_TOPK, dim=-1).indices.reshape(-1)
+        order = torch.argsort(top, stable=True)
+        counts = torch.bincount(top, minlength=MOE_EXPERTS).tolist()
+        routed = x[order // MOE_TOPK].contiguous()
+        down_in = torch.randn(routed.shape[0], MOE_INTER, device=dev, generator=gx).to(
+            torch.bfloat16)
+        bounds, c0 = [], 0
+        for c in counts:
+            bounds.append((c0, c0 + c))
+            c0 += c
+        batches.append((routed, down_in, bounds))
+    return experts, batches
+
+
+def moe_step(torch, experts, batches, world, rank, dist, marks=None):
+    """add_batch of every hit expert per forward batch (gate and up share each
+    call's routed tokens), the objects of ``layer_bsz`` = 64 same-shape experts
+    (common_utils.build_chunk_specs order), then fasterquant of all of them;
+    with several ranks the reference's owner flow."""
+    from g2ptq_b200.gptq_utils import gptq_utils, common_utils
+    from g2ptq_b200.utils.quant_utils import WeightQuantizer
+    objs, where = [], {}
+    for proj in ("up_proj", "gate_proj", "down_proj"):
+        for c0 in range(0, MOE_EXPERTS, MOE_LAYER_BSZ):
+            ids = list(range(c0, min(c0 + MOE_LAYER_BSZ, MOE_EXPERTS)))
+            obj = gptq_utils.GPTQ([experts[(proj, e)] for e in ids])
+            q = WeightQuantizer()
+            q.configure(BITS, perchannel=True, sym=True, mse=False)
+            obj.quantizer = common_utils.make_group_quantizers(
+                q, experts[(proj, ids[0])].weight.shape[1], GROUPSIZE)
+            objs.append(obj)
+            for k, e in enumerate(ids):
+                where[(proj, e)] = (obj, k)
+    for routed, down_in, bounds in batches:
+        for e, (a, b) in enumerate(bounds):
+            if b == a:
+                continue  # the reference calls only the hit experts
+            x = routed[a:b]
+            for proj in ("up_proj", "gate_proj"):
+                o, k = where[(proj, e)]
+                o.add_batch(k, x, None)
+            o, k = where[("down_proj", e)]
+            o.add_batch(k, down_in[a:b], None)
+    if marks is not None:
+        for o in objs:
+            o._flush_all()
+        marks.append(torch.cuda.Event(enable_timing=True))
+        marks[-1].record()
+    kw = dict(blocksize=BLOCKSIZE, percdamp=PERCDAMP, groupsize=GROUPSIZE, actorder=True,
+              static_groups=True, export_compressed_tensors=True)
+    if world > 1:
+        _, _, owner = common_utils.partition_layers(objs, world)
+        gptq_utils.reduce_to_target_rank(objs, owner)
+        gptq_utils.fasterquant_all([o for o in objs if owner[o] == rank], **kw)
+        common_utils.broadcast_quantized_param(objs, owner, export_compressed_tensors=True)
+    else:
+        gptq_utils.fasterquant_all(objs, **kw)
+    for o in objs:
+        o.free()
+    if marks is not None:
+        marks.append(torch.cuda.Event(enable_timing=True))
+        marks[-1].record()
+
+
+def native_moe(args):
+    import torch
+    import torch.distributed as dist
+    from g2ptq_b200 import _lib
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=dev)
+    lib = _lib.load()
+    experts, batches = make_moe(torch, dev, rank, world, args)
+    routed_rows = sum(r.shape[0] for r, _, _ in batches)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        moe_step(torch, experts, batches, world, rank, dist)
+    barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    launches0 = lib.g2q_launch_count()
+    barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    marks = [t0]
+    for _ in range(args.steps):
+        moe_step(torch, experts, batches, world, rank, dist, marks)
+    t1.record()
+    barrier()
+    clk = clocks.stop()
+    launches = lib.g2q_launch_count() - launches0
+    ms = t0.elapsed_time(t1) / args.steps
+    calib = sum(marks[2 * i].elapsed_time(marks[2 * i + 1]) for i in range(args.steps))
+    quant = sum(marks[2 * i + 1].elapsed_time(marks[2 * i + 2]) for i in range(args.steps))
+    if world > 1:
+        m = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(m, op=dist.ReduceOp.MAX)
+        ms = float(m.item())
+    n_lin = 3 * MOE_EXPERTS
+    line = {
+        "metric": "expert linear layers quantized/sec", "value": round(n_lin / (ms * 1e-3), 3),
+        "unit": "linears/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16-in/f32", "data": "synthetic",
+        "config": {
+            "workload": "Qwen3-30B-A3B MoE layer: 128 experts x (gate 768x2048, up 768x2048, "
+                        "down 2048x768), top-8 routing, GPTQ W4 sym g128 act-order, "
+                        f"{args.seqs}x{args.seq_len} tokens, layer_bsz 64",
+            "routed_rows_rank0": routed_rows, "forward_batch": args.moe_bsz,
+            "add_batch_calls_rank0_per_step": sum(
+                3 * sum(1 for a, b in bd if b > a) for _, _, bd in batches),
+            "seconds_48_layers": round(48 * ms * 1e-3, 3),
+            "phase_ms_rank0": {"add_batch_and_folds": round(calib / args.steps, 3),
+                               "reduce_factor_compensate_export": round(quant / args.steps, 3)},
+            "parallelism": f"tokens dp{world} + expert-chunk ownership (LPT)",
+        },
+        "gpu_launches": int(launches), "clocks": clk,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
 # CPU baseline / reference arm: the reference's torch path on the host cores
 # ---------------------------------------------------------------------------
 
@@ -634,5 +813,7 @@ if __name__ == "__main__":
     a = parse()
     if a.impl == "reference":
         reference(a)
+    elif a.model == "qwen3-moe":
+        native_moe(a)
     else:
         native(a)

@@ -5,7 +5,9 @@
 * The packed upper-triangle exchange format (pack / unpack kernels).
 * With two or more GPUs: ``fasterquant_rows`` and the reference's owner flow
   (``reduce_to_target_rank`` + owner ``fasterquant`` + ``broadcast_quantized_param``)
-  over NCCL against the single-GPU result.  Every rank feeds the same tokens,
+  over NCCL against the single-GPU result, for GPTQ and (owner flow, with
+  G2PTQ's reduction of block-wise Hessians, gradients and squared
+  activations) for G2PTQ.  Every rank feeds the same tokens,
   so the reduced statistics equal each rank's own exactly (x/2 + x/2 = x in
   fp32) and the results must match bit for bit.
 """
@@ -149,6 +151,32 @@ def _build(dev):
 
 FQ = dict(blocksize=128, percdamp=0.01, groupsize=128, actorder=True, static_groups=True,
           export_compressed_tensors=True)
+FQ_G2 = dict(blocksize=128, percdamp=0.01, groupsize=128, actorder=False, static_groups=False,
+             enable_gradient_update=True, alpha=1.0, export_compressed_tensors=True)
+
+
+def _build_g2ptq(dev):
+    """Two G2PTQ linears (W3 asym, four row groups) with saliencies and
+    gradients from seeded synthetic output gradients."""
+    from g2ptq_b200.gptq_utils import g2ptq_utils
+    layers = {"a": _layer(512, 1024, 31, dev), "b": _layer(256, 768, 32, dev)}
+    objs = {}
+    for n, lin in layers.items():
+        rows, cols = lin.weight.shape
+        xs = _tokens(cols, 3, 33 + cols, dev)
+        g = torch.Generator(device=dev).manual_seed(34 + rows)
+        sal, grad = [], torch.zeros(rows, cols, device=dev)
+        for x in xs:
+            go = (torch.randn(x.shape[1], rows, device=dev, generator=g) * 1e-3).to(
+                torch.bfloat16)
+            sal.append((go.float() ** 2).reshape(-1, 4, rows // 4).mean(-1))
+            grad += (go.T @ x[0]).float() / x.shape[1]
+        o = g2ptq_utils.G2PTQ([lin], [sal], [grad / len(xs)], num_groups=4)
+        o.quantizer = _quantizers(3, False, cols, 128)
+        for x in xs:
+            o.add_batch(0, x, None)
+        objs[n] = o
+    return layers, objs
 
 
 def _rank_main(rank, world, port, q):
@@ -183,6 +211,20 @@ def _rank_main(rank, world, port, q):
         ok_owner = all(torch.equal(layers[n].weight.data, ref[n][0]) and
                        torch.equal(layers[n]._export_qparams["weight_packed"], ref[n][1])
                        for n in ref)
+        # G2PTQ through its own coalesced reduction and the owner flow
+        from g2ptq_b200.gptq_utils import g2ptq_utils
+        g2_ref = _build_g2ptq(dev)
+        gptq_utils.fasterquant_all(list(g2_ref[1].values()), **FQ_G2)
+        g2_lay, g2_objs = _build_g2ptq(dev)
+        specs = list(g2_objs.values())
+        _, _, owner = common_utils.partition_layers(specs, world)
+        g2ptq_utils.reduce_to_target_rank(specs, owner)
+        gptq_utils.fasterquant_all([o for o in specs if owner[o] == rank], **FQ_G2)
+        common_utils.broadcast_quantized_param(specs, owner, export_compressed_tensors=True)
+        ok_owner = ok_owner and all(
+            torch.equal(g2_lay[n].weight.data, g2_ref[0][n].weight.data) and
+            torch.equal(g2_lay[n]._export_qparams["weight_packed"],
+                        g2_ref[0][n]._export_qparams["weight_packed"]) for n in g2_lay)
         torch.cuda.synchronize()
         q.put((rank, ok_rows, ok_owner, None))
     except Exception as e:  # reported to the parent; the group is torn down below
