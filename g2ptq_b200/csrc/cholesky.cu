@@ -24,9 +24,12 @@ namespace g2q {
 
 constexpr int NB = 128;
 
-// mean(diag(H)) -> *out (one block).
-__global__ void mean_diag_kernel(const float* H, long long C, long long ldh, float* out) {
+// mean(diag(H)) -> *out, one block per batch entry (H + b h_bs -> out[b]).
+__global__ void mean_diag_kernel(const float* H, long long C, long long ldh, float* out,
+                                 long long h_bs) {
   __shared__ float red[32];
+  H += blockIdx.x * h_bs;
+  out += blockIdx.x;
   float s = 0.f;
   for (long long i = threadIdx.x; i < C; i += blockDim.x) s += H[i * ldh + i];
   for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
@@ -39,13 +42,24 @@ __global__ void mean_diag_kernel(const float* H, long long C, long long ldh, flo
   }
 }
 
+// Damp percentages of up to kDampSlots batch entries, passed by value.
+constexpr int kDampSlots = 64;
+struct DampSet {
+  float pct[kDampSlots];
+};
+
 // A[i][j] = H[C-1-i][C-1-j] (+ damp on the diagonal) for j <= i; Y = I.
 // Row i over the grid's y loop, columns over the x threads (no per-element
-// division).
+// division); batch entry z = blockIdx.z at H + z h_bs, A / Y + z a_bs, with
+// damp percentage d.pct[z] of mean_diag[z].
 __global__ void reverse_damp_kernel(const float* H, long long C, long long ldh,
-                                    const float* mean_diag, float damp_percent,
-                                    float* A, float* Y) {
-  const float damp = damp_percent * (*mean_diag);
+                                    const float* mean_diag, DampSet d, float* A, float* Y,
+                                    long long h_bs, long long a_bs) {
+  const int z = blockIdx.z;
+  H += z * h_bs;
+  A += z * a_bs;
+  Y += z * a_bs;
+  const float damp = d.pct[z] * mean_diag[z];
   for (long long i = blockIdx.y; i < C; i += gridDim.y) {
     const float* h = H + (C - 1 - i) * ldh + (C - 1);
     for (long long j = (long long)blockIdx.x * blockDim.x + threadIdx.x; j < C;
@@ -210,8 +224,13 @@ __device__ __forceinline__ void panel_tile_update(float* D, int i0, int j0, cons
 }
 
 __global__ void __launch_bounds__(PANEL_THREADS, 1)
-    panel_kernel(float* A, long long C, long long k0, int nb, float* Linv, int* info) {
+    panel_kernel(float* A, long long C, long long k0, int nb, float* Linv, int* info,
+                 long long a_bs, long long linv_bs) {
   extern __shared__ __align__(16) float psm[];
+  // batch entry blockIdx.x: its matrix, its diagonal inverses and its info word
+  A += blockIdx.x * a_bs;
+  Linv += blockIdx.x * linv_bs;
+  if (info) info += blockIdx.x;
   float* As = psm;                  // [NB][PLD] block, lower part
   float* Ys = As + NB * PLD;        // [NB][PLD] inverse accumulator Y -> X
   float* Lt = Ys + NB * PLD;        // [PSUB][PLD] strip L_is transposed: Lt[m][i]
@@ -328,8 +347,11 @@ __host__ __device__ constexpr int linv_apply_smem_floats() {
 
 template <bool LEFT>
 __global__ void __launch_bounds__(256) linv_apply_kernel(float* S, long long lds, long long n,
-                                                         const float* __restrict__ Linv, int nb) {
+                                                         const float* __restrict__ Linv, int nb,
+                                                         long long s_bs, long long linv_bs) {
   extern __shared__ __align__(16) float lsm[];
+  S += blockIdx.z * s_bs;
+  Linv += blockIdx.z * linv_bs;
   float* Lt = lsm;                 // [NB][LA_LDT]
   float* Bt = lsm + NB * LA_LDT;   // [NB][LA_LDB]
   float* Os = Bt;                  // [LA_ROWS][LA_LDO], reuses Bt after the products
@@ -424,8 +446,9 @@ __global__ void __launch_bounds__(256) linv_apply_kernel(float* S, long long lds
 
 template <bool LEFT>
 static int linv_apply(float* S, long long lds, long long n, const float* Linv, int nb,
-                      cudaStream_t st) {
-  if (n <= 0) return G2Q_OK;
+                      cudaStream_t st, long long batch = 1, long long s_bs = 0,
+                      long long linv_bs = 0) {
+  if (n <= 0 || batch <= 0) return G2Q_OK;
   static int done[64] = {0};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return G2Q_ERR_CUDA;
@@ -436,13 +459,19 @@ static int linv_apply(float* S, long long lds, long long n, const float* Linv, i
       return G2Q_ERR_CUDA;
     if (dev < 64) done[dev] = 1;
   }
-  linv_apply_kernel<LEFT><<<cdiv(n, LA_ROWS), 256, smem, st>>>(S, lds, n, Linv, nb);
+  linv_apply_kernel<LEFT><<<dim3((unsigned)cdiv(n, LA_ROWS), 1, (unsigned)batch), 256, smem,
+                            st>>>(S, lds, n, Linv, nb, s_bs, linv_bs);
   G2Q_CHECK_LAUNCH();
   return G2Q_OK;
 }
 
-// U[i][j] = X[C-1-i][C-1-j] for i <= j, 0 below; NaN -> info = -1.
-__global__ void extract_u_kernel(const float* X, long long C, float* U, int* info) {
+// U[i][j] = X[C-1-i][C-1-j] for i <= j, 0 below; NaN -> info = -1.  Batch
+// entry z = blockIdx.z at X + z x_bs, U + z u_bs, info + z.
+__global__ void extract_u_kernel(const float* X, long long C, float* U, int* info,
+                                 long long x_bs, long long u_bs) {
+  X += blockIdx.z * x_bs;
+  U += blockIdx.z * u_bs;
+  if (info) info += blockIdx.z;
   bool nan_seen = false;
   for (long long i = blockIdx.y; i < C; i += gridDim.y) {
     const float* x = X + (C - 1 - i) * C + (C - 1);
@@ -466,7 +495,12 @@ int split2h(const float* src, long long lds, long long n, int K, __half* hi, __h
 int tc_update2h(float* D, long long ldd, long long M, long long N, long long K,
                 __half* const* a2, const float* sa, long long lda, __half* const* b2,
                 const float* sb, long long ldb, int lower, float alpha, float beta,
-                int* status, cudaStream_t st);
+                int* status, cudaStream_t st, long long batch = 1, long long k_bs = 0,
+                long long d_bs = 0, long long sa_bs = 0, long long sb_bs = 0);
+int split2h_strips(const float* src, long long lds, long long n, int K, __half* hi, __half* lo,
+                   long long ldd, float* scale, int transpose, int ny, long long src_by,
+                   long long dst_by, long long sc_by, int nz, long long src_bz,
+                   long long dst_bz, long long sc_bz, cudaStream_t st);
 
 // Side stream and per-step events of the inverse chain, one set per (device,
 // caller stream) so that factorizations issued on different streams overlap.
@@ -565,9 +599,11 @@ static int chol_one(float* U, const float* H, long long C, long long ldh, float 
   cudaStream_t side = ss->side;
   cudaEvent_t* ev = ss->ev;  // ev[2k]: factor step k done, ev[2k+1]: inverse step k done
   if (info && cudaMemsetAsync(info, 0, sizeof(int), st) != cudaSuccess) return G2Q_ERR_CUDA;
-  mean_diag_kernel<<<1, 1024, 0, st>>>(H, C, ldh, w.mdiag);
+  mean_diag_kernel<<<1, 1024, 0, st>>>(H, C, ldh, w.mdiag, 0);
   G2Q_CHECK_LAUNCH();
-  reverse_damp_kernel<<<grid_rows2(C, C), 256, 0, st>>>(H, C, ldh, w.mdiag, damp_percent, A, Y);
+  DampSet ds{};
+  ds.pct[0] = damp_percent;
+  reverse_damp_kernel<<<grid_rows2(C, C), 256, 0, st>>>(H, C, ldh, w.mdiag, ds, A, Y, 0, 0);
   G2Q_CHECK_LAUNCH();
   const long long tsz = (long long)NB * C;
   for (long long kb = 0; kb < nblk; ++kb) {
@@ -581,7 +617,7 @@ static int chol_one(float* U, const float* H, long long C, long long ldh, float 
     __half* x2[2] = {w.xk, w.xk + tsz};
     // ---- factorization (caller's stream): panel, TRSM, split, SYRK
     panel_kernel<<<1, PANEL_THREADS, panel_smem_floats() * sizeof(float), st>>>(A, C, k0, nb,
-                                                                                linv, info);
+                                                                                linv, info, 0, 0);
     G2Q_CHECK_LAUNCH();
     if (rest > 0) {
       // L_ik = A_ik Linv_kk^T, in place in A
@@ -617,7 +653,116 @@ static int chol_one(float* U, const float* H, long long C, long long ldh, float 
     if (cudaEventRecord(ev[2 * kb + 1], side) != cudaSuccess) return G2Q_ERR_CUDA;
   }
   if (cudaStreamWaitEvent(st, ev[2 * (nblk - 1) + 1], 0) != cudaSuccess) return G2Q_ERR_CUDA;
-  extract_u_kernel<<<grid_rows2(C, C), 256, 0, st>>>(Y, C, U, info);
+  extract_u_kernel<<<grid_rows2(C, C), 256, 0, st>>>(Y, C, U, info, 0, 0);
+  G2Q_CHECK_LAUNCH();
+  return G2Q_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Batched chain: n factorizations of one size advance panel by panel together,
+// every launch of a step covering all n (grid z, or one panel CTA each), so a
+// layer-batched object (n same-shape linears or experts) costs one chain of
+// launches instead of n.  Workspace as arrays over the batch, each 256-byte
+// aligned: A [n][C][C], Y [n][C][C], diagonal inverses [n][nblk][NB][NB], mean
+// diagonals [n], then fp16: L21^T splits [2 buffers][2][n][NB][C], X_k splits
+// [2][n][NB][C], then the splits' scales: L21 [2 buffers][n][C], X_k [n][C].
+struct CholWsB {
+  float *A, *Y, *linv, *mdiag;
+  __half *lt, *xk;
+  float *lsc, *xsc;
+  size_t bytes;
+};
+
+static CholWsB carve_batched(void* base, long long C, long long n) {
+  const long long nblk = (C + NB - 1) / NB;
+  CholWsB w{};
+  char* p = static_cast<char*>(base);
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    char* q = p ? p + off : nullptr;
+    off += (bytes + 255) / 256 * 256;
+    return q;
+  };
+  w.A = reinterpret_cast<float*>(take((size_t)n * C * C * sizeof(float)));
+  w.Y = reinterpret_cast<float*>(take((size_t)n * C * C * sizeof(float)));
+  w.linv = reinterpret_cast<float*>(take((size_t)n * nblk * NB * NB * sizeof(float)));
+  w.mdiag = reinterpret_cast<float*>(take((size_t)n * sizeof(float)));
+  w.lt = reinterpret_cast<__half*>(take((size_t)4 * n * NB * C * sizeof(__half)));
+  w.xk = reinterpret_cast<__half*>(take((size_t)2 * n * NB * C * sizeof(__half)));
+  w.lsc = reinterpret_cast<float*>(take((size_t)2 * n * C * sizeof(float)));
+  w.xsc = reinterpret_cast<float*>(take((size_t)n * C * sizeof(float)));
+  w.bytes = off;
+  return w;
+}
+
+// the elementwise grid of one C x C matrix, its y extent shared out over n
+static dim3 batch_grid(long long C, long long n) {
+  dim3 g = grid_rows2(C, C);
+  long long gy = (long long)g.y / n;
+  g.y = (unsigned)(gy < 1 ? 1 : gy);
+  g.z = (unsigned)n;
+  return g;
+}
+
+static int chol_batched(float* U, const float* H, long long C, long long ldh, long long n,
+                        const float* damp_percent, int* info, void* ws, cudaStream_t st) {
+  G2Q_TRY(panel_attr());
+  const CholWsB w = carve_batched(ws, C, n);
+  const long long nblk = (C + NB - 1) / NB;
+  const long long CC = C * C, lbs = nblk * NB * NB;  // batch strides of A / Y / U, Linv
+  const long long tsz = n * NB * C;                   // one fp16 term of a strip set
+  SideState* ss = nullptr;
+  G2Q_TRY(side_state(st, (int)nblk, &ss));
+  cudaStream_t side = ss->side;
+  cudaEvent_t* ev = ss->ev;
+  if (info && cudaMemsetAsync(info, 0, n * sizeof(int), st) != cudaSuccess) return G2Q_ERR_CUDA;
+  mean_diag_kernel<<<(unsigned)n, 1024, 0, st>>>(H, C, ldh, w.mdiag, C * ldh);
+  G2Q_CHECK_LAUNCH();
+  for (long long z0 = 0; z0 < n; z0 += kDampSlots) {
+    const long long m = n - z0 < kDampSlots ? n - z0 : kDampSlots;
+    DampSet ds{};
+    for (long long z = 0; z < m; ++z) ds.pct[z] = damp_percent[z0 + z];
+    reverse_damp_kernel<<<batch_grid(C, m), 256, 0, st>>>(H + z0 * C * ldh, C, ldh,
+                                                          w.mdiag + z0, ds, w.A + z0 * CC,
+                                                          w.Y + z0 * CC, C * ldh, CC);
+    G2Q_CHECK_LAUNCH();
+  }
+  for (long long kb = 0; kb < nblk; ++kb) {
+    const long long k0 = kb * NB;
+    const int nb = (int)((C - k0) < NB ? (C - k0) : NB);
+    const long long rest = C - k0 - nb;  // > 0 only for full panels (nb == NB)
+    float* linv = w.linv + kb * NB * NB;
+    __half* lt = w.lt + (kb & 1) * 2 * tsz;
+    __half* l2[2] = {lt, lt + tsz};
+    float* lsc = w.lsc + (kb & 1) * n * C;
+    __half* x2[2] = {w.xk, w.xk + tsz};
+    // ---- factorization: panel, TRSM, split, SYRK for all n
+    panel_kernel<<<(unsigned)n, PANEL_THREADS, panel_smem_floats() * sizeof(float), st>>>(
+        w.A, C, k0, nb, linv, info, CC, lbs);
+    G2Q_CHECK_LAUNCH();
+    if (rest > 0) {
+      G2Q_TRY(linv_apply<false>(w.A + (k0 + nb) * C + k0, C, rest, linv, nb, st, n, CC, lbs));
+      if (kb >= 2 && cudaStreamWaitEvent(st, ev[2 * (kb - 2) + 1], 0) != cudaSuccess)
+        return G2Q_ERR_CUDA;
+      G2Q_TRY(split2h_strips(w.A + (k0 + nb) * C + k0, C, rest, nb, l2[0], l2[1], C, lsc, 1, 1,
+                             0, 0, 0, (int)n, CC, (long long)NB * C, C, st));
+      G2Q_TRY(tc_update2h(w.A + (k0 + nb) * C + (k0 + nb), C, rest, rest, nb, l2, lsc, C, l2,
+                          lsc, C, 1, 1.f, -1.f, info, st, n, NB, CC, C, C));
+    }
+    if (cudaEventRecord(ev[2 * kb], st) != cudaSuccess) return G2Q_ERR_CUDA;
+    // ---- inverse chain (side stream)
+    if (cudaStreamWaitEvent(side, ev[2 * kb], 0) != cudaSuccess) return G2Q_ERR_CUDA;
+    G2Q_TRY(linv_apply<true>(w.Y + k0 * C, C, k0 + nb, linv, nb, side, n, CC, lbs));
+    if (rest > 0) {
+      G2Q_TRY(split2h_strips(w.Y + k0 * C, C, k0 + nb, nb, x2[0], x2[1], C, w.xsc, 0, 1, 0, 0, 0,
+                             (int)n, CC, (long long)NB * C, C, side));
+      G2Q_TRY(tc_update2h(w.Y + (k0 + nb) * C, C, rest, k0 + nb, nb, l2, lsc, C, x2, w.xsc, C, 0,
+                          1.f, -1.f, info, side, n, NB, CC, C, C));
+    }
+    if (cudaEventRecord(ev[2 * kb + 1], side) != cudaSuccess) return G2Q_ERR_CUDA;
+  }
+  if (cudaStreamWaitEvent(st, ev[2 * (nblk - 1) + 1], 0) != cudaSuccess) return G2Q_ERR_CUDA;
+  extract_u_kernel<<<batch_grid(C, n), 256, 0, st>>>(w.Y, C, U, info, CC, CC);
   G2Q_CHECK_LAUNCH();
   return G2Q_OK;
 }
@@ -689,6 +834,25 @@ extern "C" int g2q_chol_upper_inverse(float* U, const float* H, int64_t C, int64
   if (workspace_bytes < per) return G2Q_ERR_INVALID_ARG;
   if (precision != 0 && precision != 1) return G2Q_ERR_INVALID_ARG;
   cudaStream_t st = (cudaStream_t)stream;
+  if (precision == 1 && g2q::tc_ok(C) && batch >= 2 && batch <= 65535) {
+    // batched chains of as many factorizations as the workspace holds
+    long long n = (long long)(workspace_bytes / per);
+    if (n > batch) n = batch;
+    while (n >= 2 && g2q::carve_batched(nullptr, C, n).bytes > workspace_bytes) --n;
+    if (n >= 2) {
+      for (int64_t b = 0; b < batch; b += n) {
+        const long long m = batch - b < n ? batch - b : n;
+        if (m == 1)
+          G2Q_TRY(g2q::chol_one(U + b * C * C, H + b * C * ldh, C, ldh, damp_percent_host[b],
+                                info ? info + b : nullptr, (float*)workspace, precision, st));
+        else
+          G2Q_TRY(g2q::chol_batched(U + b * C * C, H + b * C * ldh, C, ldh, m,
+                                    damp_percent_host + b, info ? info + b : nullptr, workspace,
+                                    st));
+      }
+      return G2Q_OK;
+    }
+  }
   long long lanes = (long long)(workspace_bytes / per);
   if (lanes > g2q::CHOL_LANES) lanes = g2q::CHOL_LANES;
   if (lanes > batch) lanes = batch;

@@ -1787,30 +1787,40 @@ int tc_update_f16(float* D, long long ldd, long long d_bs, long long M, long lon
 // fp32-accurate tensor-core update  D <- alpha D + beta * diag(sa) A^T B diag(sb)
 // for MN-major two-term fp16 operands A[k][m] (terms a2, row stride lda) and
 // B[k][n] (b2, ldb) over K rows (three products: hi*hi, hi*lo, lo*hi); lower != 0
-// writes only m >= n.  Returns G2Q_ERR_UNSUPPORTED when TMA cannot describe the
-// operands.
+// writes only m >= n.  Batched (batch > 1): entry b's K rows of A and B start at
+// row b k_bs of a2 / b2 (k_bs >= K, K a multiple of the K tile), its output at
+// D + b d_bs, its scales at sa + b sa_bs and sb + b sb_bs.  Returns
+// G2Q_ERR_UNSUPPORTED when TMA cannot describe the operands.
 int tc_update2h(float* D, long long ldd, long long M, long long N, long long K,
                 __half* const* a2, const float* sa, long long lda, __half* const* b2,
                 const float* sb, long long ldb, int lower, float alpha, float beta,
-                int* status, cudaStream_t st) {
-  if (M <= 0 || N <= 0 || K <= 0 || !tc::encode_fn()) return G2Q_ERR_UNSUPPORTED;
+                int* status, cudaStream_t st, long long batch, long long k_bs, long long d_bs,
+                long long sa_bs, long long sb_bs) {
+  if (M <= 0 || N <= 0 || K <= 0 || batch <= 0 || !tc::encode_fn()) return G2Q_ERR_UNSUPPORTED;
+  if (batch > 1 && ((K % tc::BK) || k_bs < K || d_bs < M * ldd)) return G2Q_ERR_INVALID_ARG;
+  // rows of the operand maps: every batch entry's K rows
+  const long long rows = batch > 1 ? (batch - 1) * k_bs + K : K;
   tc::Maps mp{};
   bool ok = true;
   for (int i = 0; i < 2 && ok; ++i)
-    ok = tc::make_map(&mp.a[i], a2[i], M, K, lda, true) &&
-         tc::make_map(&mp.b[i], b2[i], N, K, ldb, true);
+    ok = tc::make_map(&mp.a[i], a2[i], M, rows, lda, true) &&
+         tc::make_map(&mp.b[i], b2[i], N, rows, ldb, true);
   if (!ok) return G2Q_ERR_UNSUPPORTED;
   tc::Params p{};
   p.status = status;
-  p.D = D; p.ldd = ldd; p.d_bs = 0;
+  p.D = D; p.ldd = ldd; p.d_bs = batch > 1 ? d_bs : 0;
   p.M = M; p.N = N;
   p.num_kb = (int)((K + tc::BK - 1) / tc::BK);
+  p.ka_batch = batch > 1 ? k_bs : 0;
+  p.kb_batch = batch > 1 ? k_bs : 0;
   p.alpha = alpha; p.beta = beta;
   p.lower = lower;
   p.f16 = 1;
   p.sa = sa; p.sb = sb;
-  p.red = (alpha == 1.f && tc::make_map_out(&mp.d, D, N, M, 1, ldd, 0)) ? 1 : 0;
-  return tc::dispatch(2, 2, mp, p, 1, st);
+  p.sa_bs = batch > 1 ? sa_bs : 0;
+  p.sb_bs = batch > 1 ? sb_bs : 0;
+  p.red = (alpha == 1.f && tc::make_map_out(&mp.d, D, N, M, batch, ldd, p.d_bs)) ? 1 : 0;
+  return tc::dispatch(2, 2, mp, p, batch, st);
 }
 
 }  // namespace g2q

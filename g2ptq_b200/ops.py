@@ -6,6 +6,7 @@ allocator and calls the library.  No function here computes anything itself.
 """
 
 import ctypes
+import os
 
 import torch
 
@@ -169,6 +170,10 @@ def gemm(C, A, B, transA=False, transB=False, alpha=0.0, beta=1.0, mask=_lib.MAS
     return C
 
 
+# workspace budget of one batched factorization call (bytes)
+CHOL_BATCH_BYTES = int(os.environ.get("G2PTQ_B200_CHOL_BATCH_MB", "4096")) << 20
+
+
 def chol_upper_inverse(H, damp_percent, info=None, precision=0):
     """``U`` with ``U^T U = (H + d I)^-1`` per batch entry; returns ``(U, info)``.
 
@@ -186,8 +191,12 @@ def chol_upper_inverse(H, damp_percent, info=None, precision=0):
     U = torch.empty_like(Hb)
     if info is None:
         info = torch.zeros(B, dtype=torch.int32, device=H.device)
-    # up to four factorizations of the batch side by side (one workspace each)
-    ws_bytes = query("g2q_chol_workspace_bytes", C) * min(B, 4)
+    # precision 1: chains of the batch's factorizations advancing together, as
+    # many per chain as CHOL_BATCH_BYTES of workspace holds (at least four);
+    # precision 0: up to four side by side on forked streams
+    per = query("g2q_chol_workspace_bytes", C)
+    chain = min(B, max(4, CHOL_BATCH_BYTES // per)) if precision == 1 else min(B, 4)
+    ws_bytes = per * chain + 4096
     ws = workspace(ws_bytes, H.device)
     call("g2q_chol_upper_inverse", U.data_ptr(), Hb.data_ptr(), C, C, B, damps, info.data_ptr(),
          int(precision), ws.data_ptr(), ws_bytes, _stream(H))

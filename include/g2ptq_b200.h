@@ -200,10 +200,17 @@ size_t g2q_gemm_tc_workspace_bytes(int64_t M, int64_t N, int64_t K, int64_t batc
  * a tensor-core pipeline wait of the chain gave up.  Route: UL
  * factorization H + dI = V V^T (V upper), U = V^-1 -- potrf + trtri, half the
  * work of potrf + potri + potrf.  precision: 0 = fp32 CUDA cores, 1 = trailing
- * updates on tensor cores with a three-term bf16 split (fp32-level accuracy).
- * Needs g2q_chol_workspace_bytes(C) bytes; a workspace of k times that (k <= 4)
- * lets k of the batch's factorizations run side by side on library-owned
- * streams forked from and joined back to `stream`.
+ * updates on tensor cores over scaled fp16 hi/lo operand pairs (three
+ * products, fp32-level accuracy).
+ * Needs g2q_chol_workspace_bytes(C) bytes.  With precision 1 and batch >= 2, a
+ * workspace of k times that (plus 4 KiB) factors the batch in chains of
+ * min(k, batch) matrices that advance panel by panel together, every launch
+ * of a step covering the whole chain (the layer-batched objects' one launch
+ * sequence; results equal those of one-by-one calls bit for bit).  With
+ * precision 0, up to four of the batch's factorizations run side by side on
+ * library-owned streams forked from and joined back to `stream`.  A timeout
+ * in a batched chain is reported in the info word of the chain's first
+ * matrix.
  * Replaces the damped Cholesky chain of gptq_utils/gptq_utils.py:291-311
  * (and its copies g2ptq_utils.py:430-450, gptaq_utils.py:323-343,
  * gptq_guided_utils.py:145-165); the damp auto-increment retry stays with the

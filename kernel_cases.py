@@ -2,8 +2,9 @@
 
     python kernel_cases.py gram --tokens 16384 --columns 4096
     python kernel_cases.py gram_weighted --tokens 16384 --columns 4096
-    python kernel_cases.py chol --columns 4096
-    python kernel_cases.py compensate --rows 4096 --columns 4096
+    python kernel_cases.py chol --columns 4096 [--batch 64]
+    python kernel_cases.py compensate --rows 4096 --columns 4096 [--bits 4 --groupsize 128]
+    python kernel_cases.py sweep [--tokens 262144]
     python kernel_cases.py block_loss --tokens 2048 --vocab 128256 --loss kl
     python kernel_cases.py saliency --tokens 8192 --rows 14336
     python kernel_cases.py running_mean --rows 14336 --columns 4096
@@ -76,44 +77,131 @@ def gram_weighted(args, g):
                 flops=flops)
 
 
+def _hessian(C, g, batch=1):
+    H = torch.zeros(batch, C, C, device="cuda")
+    for b in range(batch):
+        X = torch.randn(2 * C, C, device="cuda", generator=g).to(torch.bfloat16)
+        ops.gram_update(H[b], X, alpha=0.0, beta=1.0 / (2 * C), precision=1)
+    return H
+
+
 def chol(args, g):
-    """Damped inverse-Cholesky factor of one C x C Hessian."""
-    C = args.columns
-    X = torch.randn(2 * C, C, device="cuda", generator=g).to(torch.bfloat16)
-    H = torch.zeros(C, C, device="cuda")
-    ops.gram_update(H, X, alpha=0.0, beta=1.0 / (2 * C), precision=1)
-    H = H[None].contiguous()
+    """Damped inverse-Cholesky factors of ``batch`` C x C Hessians in one call
+    (a layer-batched object's factorization)."""
+    C, B = args.columns, args.batch
+    H = _hessian(C, g, B)
     ms = _time(lambda: ops.chol_upper_inverse(H, 0.01, precision=1), args.warmup, args.reps)
-    flops = 2 * C ** 3 / 3
-    return dict(case="chol", columns=C, ms=ms, tflops=flops / ms / 1e9, flops=flops)
+    flops = B * 2 * C ** 3 / 3
+    return dict(case="chol", columns=C, batch=B, ms=ms, tflops=flops / ms / 1e9, flops=flops)
 
 
-def compensate(args, g):
-    """One GPTQ compensation pass (W4 sym, group 128, static groups) over R x C."""
-    R, C = args.rows, args.columns
-    X = torch.randn(2 * C, C, device="cuda", generator=g).to(torch.bfloat16)
-    H = torch.zeros(C, C, device="cuda")
-    ops.gram_update(H, X, alpha=0.0, beta=1.0 / (2 * C), precision=1)
-    U, _ = ops.chol_upper_inverse(H[None].contiguous(), 0.01, precision=1)
+def _compensate_pass(R, C, bits, gs, U, g, warmup, reps):
+    """One GPTQ compensation pass (symmetric, static groups of ``gs``) of an
+    R x C weight with the factor U: average ms over ``reps``."""
     W = torch.randn(1, R, C, device="cuda", generator=g) * 0.02
-    ng = C // 128
+    ng = C // gs
     scale = torch.empty(R, ng, device="cuda")
     zero = torch.empty_like(scale)
     for gi in range(ng):
-        ops.find_params(scale, zero, W[0][:, gi * 128:(gi + 1) * 128], 4, True, param_col=gi)
-    colgroup = (torch.arange(C, device="cuda") // 128).to(torch.int32)
+        ops.find_params(scale, zero, W[0][:, gi * gs:(gi + 1) * gs], bits, True, param_col=gi)
+    colgroup = (torch.arange(C, device="cuda") // gs).to(torch.int32)
     codes = torch.empty(1, R, C, dtype=torch.int8, device="cuda")
     Wp = W.clone()
 
     def run():
         Wp.copy_(W)
-        ops.compensate(_lib.METHOD_GPTQ, Wp, U, scale, zero, colgroup, False, 128, 4, True, 128,
-                       codes, precision=1)
+        ops.compensate(_lib.METHOD_GPTQ, Wp, U, scale, zero, colgroup, False, 128, bits, True,
+                       gs, codes, precision=1)
 
-    ms = _time(run, args.warmup, args.reps)
-    flops = R * C * C  # trailing updates: sum over blocks of 2 R * blk * (C - i2)
-    return dict(case="compensate", rows=R, columns=C, ms=ms, tflops=flops / ms / 1e9,
-                flops=flops)
+    return _time(run, warmup, reps)
+
+
+def _compensate_units(R, C):
+    # 11 B per weight (read W fp32, write Q bf16, code int8, error fp32) and the
+    # trailing updates: sum over blocks of 2 R * 128 * (C - i2) = R C (C - 128) flop
+    return 11 * R * C, R * C * (C - 128)
+
+
+def compensate(args, g):
+    """One GPTQ compensation pass (sym, static groups) over R x C."""
+    R, C = args.rows, args.columns
+    U, _ = ops.chol_upper_inverse(_hessian(C, g), 0.01, precision=1)
+    ms = _compensate_pass(R, C, args.bits, args.groupsize, U, g, args.warmup, args.reps)
+    b, flops = _compensate_units(R, C)
+    return dict(case="compensate", rows=R, columns=C, bits=args.bits, groupsize=args.groupsize,
+                ms=ms, gbs=b / ms / 1e6, tflops=flops / ms / 1e9, flops=flops)
+
+
+SWEEP_SHAPES = [(4096, 4096), (4096, 14336), (8192, 8192), (8192, 28672), (14336, 4096),
+                (28672, 8192)]  # (columns, rows)
+
+
+def _heavy_tailed_tokens(T, C, g, heavy):
+    """T tokens ~N(0, 1) in fp32 whose ``heavy`` channels are Student-t (nu = 3)."""
+    X = torch.randn(T, C, device="cuda", generator=g)
+    z = torch.randn(T, heavy.numel(), device="cuda", generator=g)
+    chi2 = (torch.randn(3, T, heavy.numel(), device="cuda", generator=g) ** 2).sum(0)
+    X[:, heavy] = z / torch.sqrt(chi2 / 3.0)
+    return X
+
+
+def sweep(args, g):
+    """The operator sweep: per column count, the Hessian of ``tokens`` fp32
+    tokens (~N(0, 1), 1% Student-t channels) folded chunk by chunk (Gram
+    TFLOP/s), its damped inverse-Cholesky factor (ms), and GPTQ compensation
+    passes at bits 2/3/4 x group 64/128 for each row count of the column count
+    (GB/s of the 11 B per weight, and the trailing updates' TFLOP/s).  One
+    JSON line per measurement."""
+    T, chunk = args.tokens, 16384
+    out = []
+    for C in sorted({c for c, _ in SWEEP_SHAPES}):
+        heavy = torch.randperm(C, device="cuda", generator=g)[:max(1, C // 100)]
+        H = torch.zeros(C, C, device="cuda")
+        X = _heavy_tailed_tokens(chunk, C, g, heavy)
+        n = 0
+        fold_ms = 0.0
+        for t0 in range(0, T, chunk):
+            if t0:
+                X = _heavy_tailed_tokens(chunk, C, g, heavy)
+            torch.cuda.synchronize()
+            s = torch.cuda.Event(enable_timing=True)
+            e = torch.cuda.Event(enable_timing=True)
+            s.record()
+            ops.gram_update(H, X, alpha=n / (n + chunk), beta=2.0 / (n + chunk), precision=1)
+            e.record()
+            torch.cuda.synchronize()
+            fold_ms += s.elapsed_time(e)
+            n += chunk
+        del X
+        gflops = T * C * (C + 1)
+        line = dict(case="sweep_gram", columns=C, tokens=T, dtype="f32", ms=fold_ms,
+                    tflops=gflops / fold_ms / 1e9)
+        print(json.dumps(line), flush=True)
+        out.append(line)
+        H = H[None].contiguous()
+        ms = _time(lambda: ops.chol_upper_inverse(H, 0.01, precision=1), 1, 2)
+        U, info = ops.chol_upper_inverse(H, 0.01, precision=1)
+        cf = 2 * C ** 3 / 3
+        line = dict(case="sweep_chol", columns=C, ms=ms, tflops=cf / ms / 1e9,
+                    info=int(info[0].item()))
+        print(json.dumps(line), flush=True)
+        out.append(line)
+        del H
+        for c2, R in SWEEP_SHAPES:
+            if c2 != C:
+                continue
+            for bits in (2, 3, 4):
+                for gs in (64, 128):
+                    ms = _compensate_pass(R, C, bits, gs, U, g, 1, 3)
+                    b, flops = _compensate_units(R, C)
+                    line = dict(case="sweep_compensate", columns=C, rows=R, bits=bits,
+                                groupsize=gs, ms=ms, gbs=b / ms / 1e6,
+                                tflops=flops / ms / 1e9)
+                    print(json.dumps(line), flush=True)
+                    out.append(line)
+        del U
+        torch.cuda.empty_cache()
+    return dict(case="sweep", lines=len(out))
 
 
 def block_loss(args, g):
@@ -162,7 +250,7 @@ def running_mean(args, g):
 
 CASES = {"gram": gram, "gram_weighted": gram_weighted, "chol": chol,
          "compensate": compensate, "block_loss": block_loss, "saliency": saliency,
-         "running_mean": running_mean}
+         "running_mean": running_mean, "sweep": sweep}
 
 
 def main(argv=None):
@@ -173,6 +261,9 @@ def main(argv=None):
     ap.add_argument("--rows", type=int, default=4096)
     ap.add_argument("--vocab", type=int, default=128256)
     ap.add_argument("--loss", choices=["kl", "nll", "mse"], default="kl")
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--bits", type=int, default=4)
+    ap.add_argument("--groupsize", type=int, default=128)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--reps", type=int, default=5)
     args = ap.parse_args(argv)

@@ -135,17 +135,22 @@ def test_chol_large_identity_check():
     assert float(torch.tril(U[0], -1).abs().max()) == 0.0
 
 
-@pytest.mark.parametrize("precision", [0, 1])
-def test_chol_batch_lanes_match_one_by_one(precision):
-    """A batch of factorizations running side by side on forked streams (up to
-    four workspaces) gives each matrix's result of a call on its own, including
-    a failing one in the middle of the batch."""
+@pytest.mark.parametrize("precision,C,B,budget", [(0, 640, 6, None), (1, 640, 6, None),
+                                                 (1, 600, 5, 1), (1, 256, 70, None)])
+def test_chol_batch_lanes_match_one_by_one(precision, C, B, budget, monkeypatch):
+    """A batch of factorizations in one call gives each matrix's result of a
+    call on its own, bit for bit, including a failing one in the middle of the
+    batch: precision 0 runs up to four side by side on forked streams,
+    precision 1 advances chains of the batch panel by panel together (one
+    chain of four and a single one when the workspace holds four; a partial
+    last panel at C = 600; more than the 64 damps one launch carries)."""
+    if budget is not None:
+        monkeypatch.setattr(ops, "CHOL_BATCH_BYTES", budget)
     g = torch.Generator(device=DEV).manual_seed(17)
-    B, C = 6, 640
     X = torch.randn(B, 2 * C, C, device=DEV, generator=g)
     H = (X.transpose(1, 2) @ X / (2 * C)).contiguous()
     H[3] = -torch.eye(C, device=DEV)
-    damps = [0.01, 0.02, 0.01, 0.01, 0.05, 0.01]
+    damps = [(0.01, 0.02, 0.05)[b % 3] for b in range(B)]
     U, info = ops.chol_upper_inverse(H, damps, precision=precision)
     for b in range(B):
         Ub, ib = ops.chol_upper_inverse(H[b:b + 1].contiguous(), [damps[b]], precision=precision)
