@@ -570,7 +570,8 @@ class Pending:
     """
 
     def __init__(self, layers, nl, H, U, info, damps, params, run, W0, bits, groupsize,
-                 columns, rows, export, dynamic, actorder, borrowed_factor=False):
+                 columns, rows, export, dynamic, actorder, borrowed_factor=False,
+                 lent_factor=False):
         self.layers, self.nl, self.H, self.U, self.info = layers, nl, H, U, info
         self.damps, self.params, self.run, self.W0 = damps, params, run, W0
         self.bits, self.groupsize, self.columns, self.rows = bits, groupsize, columns, rows
@@ -578,6 +579,8 @@ class Pending:
         # U, info and damps belong to another object's launch (shared factor),
         # which finishes first and re-factors U in place if it must
         self.borrowed_factor = borrowed_factor
+        # other objects' compensations, on other streams, read this launch's U
+        self.lent_factor = lent_factor
         self.nan, self.outs, self.codes = run(W0.clone())
 
     def _flags(self):
@@ -596,6 +599,11 @@ class Pending:
             if self.borrowed_factor:
                 torch.cuda.synchronize(self.U.device)  # the owner's re-factored U
             else:
+                if self.lent_factor:
+                    # the borrowers' first compensations still read U on their
+                    # own streams: let them end before U is re-factored in place
+                    # (their results are discarded and re-run with the new U)
+                    torch.cuda.synchronize(self.U.device)
                 retry_failed(self.H, self.U, flags[:nl], self.damps)
             self.params.status.zero_()
             self.nan, self.outs, self.codes = self.run(self.W0.clone())

@@ -187,7 +187,8 @@ class GPTQ(_engine.StagingMixin):
 
         return _engine.Pending(self.layers, B, H, U, info, damps, params, run, W, q0.bits,
                                groupsize, C, R, export_compressed_tensors, dynamic, actorder,
-                               borrowed_factor=factor_in is not None)
+                               borrowed_factor=factor_in is not None,
+                               lent_factor=factor_out is not None)
 
     def free(self):
         self._leave_groups()

@@ -310,8 +310,11 @@ def compute_mse_grad_hessian(hidden_states, hidden_states_fp, saliency_cache, gr
     zero_onloaded_grads(full)
     saliency_cache.backward(mse_loss, loss_type=loss_type, retain_graph=True)
 
-    mse_loss = block_loss(_lib.LOSS_MSE, hidden_states,
-                          target=hidden_states_fp.detach().to(hidden_states.dtype))
+    # F.mse_loss promotes mixed operand dtypes: a bf16 block output against an
+    # fp32 target is compared in fp32, the target never rounded to bf16
+    dt = torch.promote_types(hidden_states.dtype, hidden_states_fp.dtype)
+    mse_loss = block_loss(_lib.LOSS_MSE, hidden_states.to(dt),
+                          target=hidden_states_fp.detach().to(dt))
     if compute_gradient:
         zero_onloaded_grads(full)
         with gradients_cache.set_backward_hook(full, loss_type=loss_type):

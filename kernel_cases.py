@@ -43,7 +43,7 @@ def _time(fn, warmup, reps):
 
 def gram(args, g):
     """One add_batch fold: H <- a H + b X^T X over T staged BF16 tokens."""
-    T, C = args.tokens, args.columns
+    T, C = args.tokens or 16384, args.columns
     X = torch.randn(T, C, device="cuda", generator=g)
     X[:, :4] *= 20
     X = X.to(torch.bfloat16)
@@ -59,7 +59,7 @@ def gram(args, g):
 def gram_weighted(args, g):
     """One G2PTQ fold: H[k] <- a H[k] + b X^T diag(s_k) X for the four row groups
     (per-token saliency weights s, BF16 tokens)."""
-    T, C = args.tokens, args.columns
+    T, C = args.tokens or 16384, args.columns
     X = torch.randn(T, C, device="cuda", generator=g)
     X[:, :4] *= 20
     X = X.to(torch.bfloat16)
@@ -152,12 +152,13 @@ def sweep(args, g):
     passes at bits 2/3/4 x group 64/128 for each row count of the column count
     (GB/s of the 11 B per weight, and the trailing updates' TFLOP/s).  One
     JSON line per measurement."""
-    T, chunk = args.tokens, 16384
+    T, chunk = args.tokens or 262144, 16384
     out = []
     for C in sorted({c for c, _ in SWEEP_SHAPES}):
         heavy = torch.randperm(C, device="cuda", generator=g)[:max(1, C // 100)]
         H = torch.zeros(C, C, device="cuda")
         X = _heavy_tailed_tokens(chunk, C, g, heavy)
+        ops.gram_update(H, X, alpha=0.0, beta=1.0, precision=1)  # untimed first fold
         n = 0
         fold_ms = 0.0
         for t0 in range(0, T, chunk):
@@ -210,7 +211,7 @@ def block_loss(args, g):
     the squared error to a target): the forward and the backward kernel,
     timed apart.  Algorithmic bytes: forward reads x (and the target), the
     backward reads them again and writes the gradient."""
-    N, V = args.tokens, args.vocab
+    N, V = args.tokens or 16384, args.vocab
     kind = {"kl": _lib.LOSS_KL, "nll": _lib.LOSS_NLL, "mse": _lib.LOSS_MSE}[args.loss]
     x = (torch.randn(N, V, device="cuda", generator=g) * 3).to(torch.bfloat16)
     t = labels = None
@@ -229,7 +230,7 @@ def block_loss(args, g):
 
 def saliency(args, g):
     """SaliencyCache.grad_hook over a ``tokens`` x ``rows`` BF16 output gradient."""
-    T, R = args.tokens, args.rows
+    T, R = args.tokens or 16384, args.rows
     grad = (torch.randn(T, R, device="cuda", generator=g) * 1e-3).to(torch.bfloat16)
     out = torch.empty(T, 4, device="cuda")
     ms = _time(lambda: ops.saliency(grad, 4, out=out), args.warmup, args.reps)
@@ -256,7 +257,9 @@ CASES = {"gram": gram, "gram_weighted": gram_weighted, "chol": chol,
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("case", choices=sorted(CASES))
-    ap.add_argument("--tokens", type=int, default=16384)
+    ap.add_argument("--tokens", type=int, default=None,
+                    help="tokens of a fold / loss / saliency case (16384), of the sweep's "
+                         "Hessians (262144)")
     ap.add_argument("--columns", type=int, default=4096)
     ap.add_argument("--rows", type=int, default=4096)
     ap.add_argument("--vocab", type=int, default=128256)

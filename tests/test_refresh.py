@@ -381,3 +381,35 @@ def test_refresh_kernels_on_empty_inputs():
         loss = G.block_loss(kind, x, target=t, labels=lab)
         loss.backward()
         assert float(loss.detach()) == 0.0 and x.grad.shape == (0, 40)
+
+
+@pytest.mark.gpu
+def test_mse_gradient_loss_promotes_mixed_dtypes():
+    """A bf16 block output against an fp32 target: the gradient loss compares
+    them in fp32 (F.mse_loss's type promotion, g2ptq_utils.py:1025), the
+    target not rounded to bf16, and the gradient reaches the bf16 output."""
+    import types
+    g = torch.Generator(device="cuda").manual_seed(9)
+    h0 = torch.randn(6, 48, device="cuda", generator=g).to(torch.bfloat16)
+    hfp = h0.float() + 1e-3 * torch.randn(6, 48, device="cuda", generator=g)
+    lin = torch.nn.Linear(48, 48, bias=False, device="cuda")
+    sc = G.SaliencyCache(["l"], 4)
+    gc = G.GradientCache(["l"], 4)
+    full = {"l": lin}
+    sc.set_forward_hook(full)
+    gc.set_forward_hook(full)
+    with torch.enable_grad():
+        h = h0.clone().requires_grad_(True)
+        torch.manual_seed(1)
+        loss = G.compute_mse_grad_hessian(h, hfp, sc, gc, full, types.SimpleNamespace(),
+                                          loss_type="block")
+    sc.clear_hook()
+    gc.clear_hook()
+    want, dh = OR.mse_head(h0.float().cpu().numpy(), hfp.cpu().numpy())
+    rounded, _ = OR.mse_head(h0.float().cpu().numpy(),
+                             hfp.to(torch.bfloat16).float().cpu().numpy())
+    assert abs(float(loss) - want) <= 1e-5 * want
+    assert abs(rounded - want) > 1e-3 * want  # the bf16-rounded target would be detected
+    assert h.grad is not None and h.grad.dtype == torch.bfloat16
+    ref = torch.from_numpy(dh).float().reshape(h.shape).to(torch.bfloat16)
+    torch.testing.assert_close(h.grad.cpu(), ref, rtol=1e-2, atol=1e-6)
