@@ -2,6 +2,7 @@
 
     python kernel_cases.py gram --tokens 16384 --columns 4096
     python kernel_cases.py gram_weighted --tokens 16384 --columns 4096
+    python kernel_cases.py gram_grouped --tokens 16384 --columns 4096
     python kernel_cases.py chol --columns 4096 [--batch 64]
     python kernel_cases.py compensate --rows 4096 --columns 4096 [--bits 4 --groupsize 128]
     python kernel_cases.py sweep [--tokens 262144]
@@ -85,6 +86,24 @@ def _hessian(C, g, batch=1):
     return H
 
 
+def gram_grouped(args, g):
+    """One G2PTQ fold as the quantizer object runs it: the four row groups'
+    Grams H[k] <- a H[k] + b X^T diag(s_k) X in one grouped launch (one split
+    pass of X into the scaled bf16 pairs of all groups, one batched CTA-pair
+    launch).  Algorithmic work: four upper-triangle Grams."""
+    T, C = args.tokens or 16384, args.columns
+    X = torch.randn(T, C, device="cuda", generator=g)
+    X[:, :4] *= 20
+    X = X.to(torch.bfloat16)
+    S = torch.rand(T, 4, device="cuda", generator=g)
+    H = torch.zeros(4, C, C, device="cuda")
+    ms = _time(lambda: ops.gram_update_grouped(H, X, S, alpha=0.5, beta=1.0 / T, precision=1),
+               args.warmup, args.reps)
+    flops = 4 * T * C * (C + 1)
+    return dict(case="gram_grouped", tokens=T, columns=C, ms=ms, tflops=flops / ms / 1e9,
+                flops=flops)
+
+
 def chol(args, g):
     """Damped inverse-Cholesky factors of ``batch`` C x C Hessians in one call
     (a layer-batched object's factorization)."""
@@ -95,23 +114,28 @@ def chol(args, g):
     return dict(case="chol", columns=C, batch=B, ms=ms, tflops=flops / ms / 1e9, flops=flops)
 
 
-def _compensate_pass(R, C, bits, gs, U, g, warmup, reps):
-    """One GPTQ compensation pass (symmetric, static groups of ``gs``) of an
-    R x C weight with the factor U: average ms over ``reps``."""
+def _compensate_pass(R, C, bits, gs, U, g, warmup, reps, dynamic=False):
+    """One GPTQ compensation pass (symmetric, groups of ``gs``) of an R x C
+    weight with the factor U: average ms over ``reps``.  Static groups take
+    their parameters before the pass; dynamic groups (act-order off, the
+    reference's default) find them inside it at each group's first column."""
     W = torch.randn(1, R, C, device="cuda", generator=g) * 0.02
     ng = C // gs
     scale = torch.empty(R, ng, device="cuda")
     zero = torch.empty_like(scale)
-    for gi in range(ng):
-        ops.find_params(scale, zero, W[0][:, gi * gs:(gi + 1) * gs], bits, True, param_col=gi)
+    if not dynamic:
+        for gi in range(ng):
+            ops.find_params(scale, zero, W[0][:, gi * gs:(gi + 1) * gs], bits, True,
+                            param_col=gi)
     colgroup = (torch.arange(C, device="cuda") // gs).to(torch.int32)
     codes = torch.empty(1, R, C, dtype=torch.int8, device="cuda")
     Wp = W.clone()
 
     def run():
         Wp.copy_(W)
-        ops.compensate(_lib.METHOD_GPTQ, Wp, U, scale, zero, colgroup, False, 128, bits, True,
-                       gs, codes, precision=1)
+        # block size 128, as the reference
+        ops.compensate(_lib.METHOD_GPTQ, Wp, U, scale, zero, colgroup, dynamic, gs, bits, True,
+                       128, codes, precision=1)
 
     return _time(run, warmup, reps)
 
@@ -149,9 +173,10 @@ def sweep(args, g):
     """The operator sweep: per column count, the Hessian of ``tokens`` fp32
     tokens (~N(0, 1), 1% Student-t channels) folded chunk by chunk (Gram
     TFLOP/s), its damped inverse-Cholesky factor (ms), and GPTQ compensation
-    passes at bits 2/3/4 x group 64/128 for each row count of the column count
-    (GB/s of the 11 B per weight, and the trailing updates' TFLOP/s).  One
-    JSON line per measurement."""
+    passes (act-order off: groups found inside the pass) at bits 2/3/4 x group
+    64/128 for each row count of the column count (GB/s of the 11 B per
+    weight, and the trailing updates' TFLOP/s).  One JSON line per
+    measurement."""
     T, chunk = args.tokens or 262144, 16384
     out = []
     for C in sorted({c for c, _ in SWEEP_SHAPES}):
@@ -193,10 +218,10 @@ def sweep(args, g):
                 continue
             for bits in (2, 3, 4):
                 for gs in (64, 128):
-                    ms = _compensate_pass(R, C, bits, gs, U, g, 1, 3)
+                    ms = _compensate_pass(R, C, bits, gs, U, g, 1, 3, dynamic=True)
                     b, flops = _compensate_units(R, C)
                     line = dict(case="sweep_compensate", columns=C, rows=R, bits=bits,
-                                groupsize=gs, ms=ms, gbs=b / ms / 1e6,
+                                groupsize=gs, groups="dynamic", ms=ms, gbs=b / ms / 1e6,
                                 tflops=flops / ms / 1e9)
                     print(json.dumps(line), flush=True)
                     out.append(line)
@@ -249,7 +274,8 @@ def running_mean(args, g):
     return dict(case="running_mean", rows=R, columns=C, ms=ms, bytes=b, gbs=b / ms / 1e6)
 
 
-CASES = {"gram": gram, "gram_weighted": gram_weighted, "chol": chol,
+CASES = {"gram": gram, "gram_weighted": gram_weighted, "gram_grouped": gram_grouped,
+         "chol": chol,
          "compensate": compensate, "block_loss": block_loss, "saliency": saliency,
          "running_mean": running_mean, "sweep": sweep}
 
