@@ -63,8 +63,7 @@ template <int QT_, int QROWS_>
 struct BlockShape {
   static constexpr int QT = QT_;            // threads per row
   static constexpr int SEG = BLK / QT;      // block columns per thread
-  static constexpr int USEG = SEG + 4;      // padded segment: a row's segments start on distinct banks
-  static constexpr int LDU = QT * USEG;     // shared-memory row of the U (and P) block
+  static constexpr int LDU = QT * SEG;      // shared-memory row of the U (and P) block
   static constexpr int QROWS = QROWS_;      // rows per CTA
   static constexpr int LDE = BLK + 1;       // staged error row
   static constexpr int THREADS = QT * QROWS;
@@ -75,8 +74,18 @@ struct BlockShape {
 };
 // Sixteen threads per row (eight columns each), sixteen rows per CTA: twice the
 // warps of an eight-thread split for the same rows, which the latency-bound
-// column loop needs to hide its dependent chains; two CTAs fit on an SM.
+// column loop needs to hide its dependent chains.  GPTQ's block (64 KB of U,
+// 8 KB of errors, 80 registers) fits three CTAs on an SM, G2PTQ's two.
 using BlockCfg = BlockShape<16, 16>;
+
+// Offset of column k of thread t's segment in a U (or P) row.  The segment's
+// two 4-column halves are swapped when bit 2 of t is set, so that the 16-byte
+// loads of eight consecutive segments of one row cover all 32 banks (the same
+// as padding each segment by four floats, without the padding's third more
+// shared memory).
+__device__ __forceinline__ int useg(int t, int k) {
+  return t * BlockCfg::SEG + ((((k >> 2) ^ (t >> 2)) & 1) << 2) + (k & 3);
+}
 
 // rint(x / s) of the correctly rounded quotient, from a multiply by rs = 1 / s:
 // x * rs lies within two units in the last place of the rounded quotient, so
@@ -99,11 +108,12 @@ __device__ __forceinline__ float div_rn(float num, float d, float rd) {
 }
 
 template <int METHOD>
-__global__ void __launch_bounds__(BlockCfg::THREADS, 2) block_kernel(BlockParams P) {
-  constexpr int QT = BlockCfg::QT, SEG = BlockCfg::SEG, USEG = BlockCfg::USEG;
+__global__ void __launch_bounds__(BlockCfg::THREADS, METHOD == G2Q_METHOD_GPTQ ? 3 : 2)
+    block_kernel(BlockParams P) {
+  constexpr int QT = BlockCfg::QT, SEG = BlockCfg::SEG;
   constexpr int LDU = BlockCfg::LDU, QROWS = BlockCfg::QROWS, LDE = BlockCfg::LDE;
   extern __shared__ __align__(16) float smem[];
-  float* Us = smem;              // [BLK][LDU], segment-padded
+  float* Us = smem;              // [BLK][LDU], segment halves swizzled (useg)
   float* Ps = Us + BLK * LDU;    // GPTAQ P block, same layout
   float* Es = smem + BLK * LDU * (METHOD == G2Q_METHOD_GPTAQ ? 2 : 1);  // [QROWS][LDE] errors
   float* EAs = Es + QROWS * LDE;  // G2PTQ trailing-update errors
@@ -127,7 +137,7 @@ __global__ void __launch_bounds__(BlockCfg::THREADS, 2) block_kernel(BlockParams
 #pragma unroll 8
     for (int q = tid; q < BLK * BLK / 4; q += QT * QROWS) {
       const int i = q / (BLK / 4), j = (q % (BLK / 4)) * 4;
-      const int o = i * LDU + (j / SEG) * USEG + (j % SEG);
+      const int o = i * LDU + useg(j / SEG, j % SEG);
       *reinterpret_cast<float4*>(&Us[o]) = *reinterpret_cast<const float4*>(hb + i * P.ldh + j);
       if (METHOD == G2Q_METHOD_GPTAQ)
         *reinterpret_cast<float4*>(&Ps[o]) =
@@ -137,7 +147,7 @@ __global__ void __launch_bounds__(BlockCfg::THREADS, 2) block_kernel(BlockParams
 #pragma unroll 4
     for (int idx = tid; idx < BLK * BLK; idx += QT * QROWS) {
       const int i = idx / BLK, j = idx % BLK;
-      const int o = i * LDU + (j / SEG) * USEG + (j % SEG);
+      const int o = i * LDU + useg(j / SEG, j % SEG);
       const bool in = i < nc && j < nc;
       Us[o] = in ? hb[i * P.ldh + j] : 0.f;
       if (METHOD == G2Q_METHOD_GPTAQ) Ps[o] = in ? pb[i * P.ldh + j] : 0.f;
@@ -176,7 +186,7 @@ __global__ void __launch_bounds__(BlockCfg::THREADS, 2) block_kernel(BlockParams
   for (int k = 0; k < SEG; ++k) {
     const int col = t * SEG + k;
     rsv[k] = 1.f / sv[k];
-    dv[k] = col < nc ? Us[col * LDU + t * USEG + k] : 1.f;
+    dv[k] = col < nc ? Us[col * LDU + useg(t, k)] : 1.f;
     rdv[k] = 1.f / dv[k];
   }
 
@@ -238,15 +248,15 @@ __global__ void __launch_bounds__(BlockCfg::THREADS, 2) block_kernel(BlockParams
       // column i - 1's update of this thread's columns after i (the owner's
       // column i received it through wn)
       if (k > 0) {
-        const float* urow = Us + (i - 1) * LDU + t * USEG;
-        const float* prow_s = Ps + (i - 1) * LDU + t * USEG;
+        const float* urow = Us + (i - 1) * LDU;
+        const float* prow_s = Ps + (i - 1) * LDU;
 #pragma unroll
         for (int j4 = 0; j4 < SEG; j4 += 4) {
-          const float4 u4 = *reinterpret_cast<const float4*>(urow + j4);
+          const float4 u4 = *reinterpret_cast<const float4*>(urow + useg(t, j4));
           const float uu[4] = {u4.x, u4.y, u4.z, u4.w};
           float pp[4] = {0.f, 0.f, 0.f, 0.f};
           if (METHOD == G2Q_METHOD_GPTAQ) {
-            const float4 p4 = *reinterpret_cast<const float4*>(prow_s + j4);
+            const float4 p4 = *reinterpret_cast<const float4*>(prow_s + useg(t, j4));
             pp[0] = p4.x; pp[1] = p4.y; pp[2] = p4.z; pp[3] = p4.w;
           }
 #pragma unroll
@@ -267,13 +277,13 @@ __global__ void __launch_bounds__(BlockCfg::THREADS, 2) block_kernel(BlockParams
       }
       // the owner's next column with column i's own update
       if (k + 1 < SEG) {
-        const float u1 = Us[i * LDU + tw * USEG + k + 1];
+        const float u1 = Us[i * LDU + useg(tw, k + 1)];
         if (METHOD == G2Q_METHOD_G2PTQ) {
           wn = fmaf(-e, u1, wv[k + 1] - gv[k + 1]);
           if (approx) wn = __fsub_rn(wn, __fmul_rn(__fsub_rn(wn, rv[k + 1]), P.beta));
           gn = fmaf(-aux, u1, gv[k + 1]);
         } else if (METHOD == G2Q_METHOD_GPTAQ) {
-          wn = fmaf(Ps[i * LDU + tw * USEG + k + 1], aux, fmaf(-e, u1, wv[k + 1]));
+          wn = fmaf(Ps[i * LDU + useg(tw, k + 1)], aux, fmaf(-e, u1, wv[k + 1]));
         } else {
           wn = fmaf(-e, u1, wv[k + 1]);
         }
@@ -284,15 +294,15 @@ __global__ void __launch_bounds__(BlockCfg::THREADS, 2) block_kernel(BlockParams
     // the segment's last column updates every column of the threads after it
     if (later) {
       const int i = tw * SEG + klast;
-      const float* urow = Us + i * LDU + t * USEG;
-      const float* prow_s = Ps + i * LDU + t * USEG;
+      const float* urow = Us + i * LDU;
+      const float* prow_s = Ps + i * LDU;
 #pragma unroll
       for (int j4 = 0; j4 < SEG; j4 += 4) {
-        const float4 u4 = *reinterpret_cast<const float4*>(urow + j4);
+        const float4 u4 = *reinterpret_cast<const float4*>(urow + useg(t, j4));
         const float uu[4] = {u4.x, u4.y, u4.z, u4.w};
         float pp[4] = {0.f, 0.f, 0.f, 0.f};
         if (METHOD == G2Q_METHOD_GPTAQ) {
-          const float4 p4 = *reinterpret_cast<const float4*>(prow_s + j4);
+          const float4 p4 = *reinterpret_cast<const float4*>(prow_s + useg(t, j4));
           pp[0] = p4.x; pp[1] = p4.y; pp[2] = p4.z; pp[3] = p4.w;
         }
 #pragma unroll
@@ -378,7 +388,10 @@ static int launch_block_t(const BlockParams& P, long long batch, cudaStream_t st
   const size_t smem = block_smem(METHOD);
   if (dev >= 64 || !attr_done[dev]) {
     if (cudaFuncSetAttribute(block_kernel<METHOD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem) != cudaSuccess)
+                             (int)smem) != cudaSuccess ||
+        cudaFuncSetAttribute(block_kernel<METHOD>,
+                             cudaFuncAttributePreferredSharedMemoryCarveout,
+                             cudaSharedmemCarveoutMaxShared) != cudaSuccess)
       return G2Q_ERR_CUDA;
     if (dev < 64) attr_done[dev] = 1;
   }
