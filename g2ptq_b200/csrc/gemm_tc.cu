@@ -526,6 +526,9 @@ __global__ void __launch_bounds__((Cfg<NA, NB, SMALL, WIDE>::THREADS),
       // two swizzled 4 KB buffers and the TMA unit adds them into D.
       static_assert(K::STAGES * K::STAGE_BYTES >= 4 * 8192, "staging does not fit");
       uint8_t* stg = smem + q * 8192;
+      // the row's operand scale, loaded once; the chunk's 32 column scales,
+      // one per lane and passed around by shuffles (no global load per element)
+      const float sa_row = (p.sa && gm < p.M) ? p.sa[bz * p.sa_bs + gm] : 1.f;
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
@@ -535,6 +538,8 @@ __global__ void __launch_bounds__((Cfg<NA, NB, SMALL, WIDE>::THREADS),
 #pragma unroll
           for (int j = 0; j < 32; ++j) r[j] = 0u;
         }
+        const long long gn_lane = n0 + c * 32 + lane;
+        const float sb_lane = (p.sa && gn_lane < p.N) ? p.sb[bz * p.sb_bs + gn_lane] : 1.f;
         if (c >= 2) {
           if (lane == 0) bulk_wait_read_1();
           __syncwarp();
@@ -547,9 +552,8 @@ __global__ void __launch_bounds__((Cfg<NA, NB, SMALL, WIDE>::THREADS),
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             v[u] = p.beta * __uint_as_float(r[4 * j4 + u]);
-            if (p.sa)
-              v[u] *= (gm < p.M ? p.sa[bz * p.sa_bs + gm] : 1.f) *
-                      (gn + u < p.N ? p.sb[bz * p.sb_bs + gn + u] : 1.f);
+            const float sb_col = __shfl_sync(0xffffffffu, sb_lane, 4 * j4 + u);
+            if (p.sa) v[u] *= sa_row * sb_col;
             // leave the other triangle as it is
             if ((p.lower && gn + u > gm) || (p.supper && gn + u <= gm)) v[u] = 0.f;
           }
