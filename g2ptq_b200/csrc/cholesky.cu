@@ -13,9 +13,11 @@
 //           Y_i: -= L_ik X_k:                (i > k)             (GEMM)
 // potrf + trtri = 2C^3/3 flops, where the reference chain
 // potrf -> cholesky_inverse -> potrf(upper) costs 4C^3/3.
-// The factorization (panel, TRSM, SYRK) runs on the caller's stream; the
-// inverse chain (X_k, Y update), which no later panel depends on, runs on a
+// The inverse chain (X_k, Y update), which no later panel depends on, runs on a
 // library-owned side stream ordered by per-step events and joined at the end.
+// On tensor cores the panels and the update of the next panel's column block
+// run ahead on a high-priority stream while the rest of each SYRK runs on the
+// caller's stream (look-ahead, see chol_batched).
 #include <cuda_fp16.h>
 
 #include "gemm_simt.cuh"
@@ -490,8 +492,6 @@ __global__ void extract_u_kernel(const float* X, long long C, float* U, int* inf
 
 
 
-int split2h(const float* src, long long lds, long long n, int K, __half* hi, __half* lo,
-            long long ldd, float* scale, int transpose, cudaStream_t st);
 int tc_update2h(float* D, long long ldd, long long M, long long N, long long K,
                 __half* const* a2, const float* sa, long long lda, __half* const* b2,
                 const float* sb, long long ldb, int lower, float alpha, float beta,
@@ -508,7 +508,8 @@ struct SideState {
   int dev = -1;
   cudaStream_t main = nullptr;
   cudaStream_t side = nullptr;
-  cudaEvent_t* ev = nullptr;  // [2 * cap]: factor-step-done, inverse-step-done
+  cudaStream_t crit = nullptr;  // the factorization's critical path, highest priority
+  cudaEvent_t* ev = nullptr;    // [4 * cap + 1]: per step four, then one fork event
   int cap = 0;
 };
 
@@ -527,18 +528,24 @@ static int side_state(cudaStream_t main, int steps, SideState** out) {
     if (s->side && s->dev != dev) {
       *s = SideState();  // slot held a stream of another device: start over
     }
-    // the inverse chain runs at the caller's stream priority
-    int prio = 0;
+    // the inverse chain runs at the caller's stream priority, the panels and
+    // their look-ahead updates at the device's highest, so that their single
+    // CTAs take the first SM a trailing update frees
+    int prio = 0, least = 0, greatest = 0;
     if (!s->side && (cudaStreamGetPriority(main, &prio) != cudaSuccess ||
                      cudaStreamCreateWithPriority(&s->side, cudaStreamNonBlocking, prio) !=
                          cudaSuccess))
+      return G2Q_ERR_CUDA;
+    if (!s->crit &&
+        (cudaDeviceGetStreamPriorityRange(&least, &greatest) != cudaSuccess ||
+         cudaStreamCreateWithPriority(&s->crit, cudaStreamNonBlocking, greatest) != cudaSuccess))
       return G2Q_ERR_CUDA;
     s->dev = dev;
     s->main = main;
   }
   if (s->cap < steps + 1) {
-    cudaEvent_t* ev = new cudaEvent_t[2 * (steps + 1)];
-    for (int i = 0; i < 2 * (steps + 1); ++i)
+    cudaEvent_t* ev = new cudaEvent_t[4 * (steps + 1) + 1];
+    for (int i = 0; i < 4 * (steps + 1) + 1; ++i)
       if (cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming) != cudaSuccess)
         return G2Q_ERR_CUDA;
     // events of the previous set may still be referenced by queued work; keep them
@@ -551,13 +558,10 @@ static int side_state(cudaStream_t main, int steps, SideState** out) {
 
 static bool tc_ok(long long C) { return C % 8 == 0; }
 
-// Workspace layout (floats unless noted): A [C*C], Y [C*C], diagonal inverses
-// [nblk][NB*NB], mean diag [64], then fp16: L21^T splits [2 buffers][2][NB*C],
-// X_k splits [2][NB*C], then the splits' scales: L21 [2 buffers][C], X_k [C].
+// Workspace of the CUDA-core chain (floats): A [C*C], Y [C*C], diagonal
+// inverses [nblk][NB*NB], mean diag [64].
 struct CholWs {
   float *A, *Y, *linv, *mdiag;
-  __half *lt, *xk;
-  float *lsc, *xsc;
 };
 
 static CholWs carve(float* ws, long long C) {
@@ -567,10 +571,6 @@ static CholWs carve(float* ws, long long C) {
   w.Y = w.A + C * C;
   w.linv = w.Y + C * C;
   w.mdiag = w.linv + nblk * NB * NB;
-  w.lt = reinterpret_cast<__half*>(w.mdiag + 64);
-  w.xk = w.lt + 2 * 2 * (long long)NB * C;
-  w.lsc = reinterpret_cast<float*>(w.xk + 2 * (long long)NB * C);
-  w.xsc = w.lsc + 2 * C;
   return w;
 }
 
@@ -586,14 +586,16 @@ static int panel_attr() {
   return G2Q_OK;
 }
 
+// One factorization on fp32 CUDA cores (precision 0, or C not a multiple of 8),
+// 128-column steps: the factorization on the caller's stream, the inverse
+// chain on the side stream.
 static int chol_one(float* U, const float* H, long long C, long long ldh, float damp_percent,
-                    int* info, float* ws, int precision, cudaStream_t st) {
+                    int* info, float* ws, cudaStream_t st) {
   G2Q_TRY(panel_attr());
   CholWs w = carve(ws, C);
   float* A = w.A;
   float* Y = w.Y;
   const long long nblk = (C + NB - 1) / NB;
-  const bool use_tc = precision == 1 && tc_ok(C);
   SideState* ss = nullptr;
   G2Q_TRY(side_state(st, (int)nblk, &ss));
   cudaStream_t side = ss->side;
@@ -605,51 +607,29 @@ static int chol_one(float* U, const float* H, long long C, long long ldh, float 
   ds.pct[0] = damp_percent;
   reverse_damp_kernel<<<grid_rows2(C, C), 256, 0, st>>>(H, C, ldh, w.mdiag, ds, A, Y, 0, 0);
   G2Q_CHECK_LAUNCH();
-  const long long tsz = (long long)NB * C;
   for (long long kb = 0; kb < nblk; ++kb) {
     const long long k0 = kb * NB;
     const int nb = (int)((C - k0) < NB ? (C - k0) : NB);
     const long long rest = C - k0 - nb;
     float* linv = w.linv + kb * NB * NB;
-    __half* lt = w.lt + (kb & 1) * 2 * tsz;
-    __half* l2[2] = {lt, lt + tsz};
-    float* lsc = w.lsc + (kb & 1) * C;
-    __half* x2[2] = {w.xk, w.xk + tsz};
-    // ---- factorization (caller's stream): panel, TRSM, split, SYRK
+    // ---- factorization (caller's stream): panel, TRSM, SYRK
     panel_kernel<<<1, PANEL_THREADS, panel_smem_floats() * sizeof(float), st>>>(A, C, k0, nb,
                                                                                 linv, info, 0, 0);
     G2Q_CHECK_LAUNCH();
     if (rest > 0) {
       // L_ik = A_ik Linv_kk^T, in place in A
       G2Q_TRY(linv_apply<false>(A + (k0 + nb) * C + k0, C, rest, linv, nb, st));
-      if (use_tc) {
-        // the inverse chain of step kb-2 used this L21^T buffer
-        if (kb >= 2 && cudaStreamWaitEvent(st, ev[2 * (kb - 2) + 1], 0) != cudaSuccess)
-          return G2Q_ERR_CUDA;
-        G2Q_TRY(split2h(A + (k0 + nb) * C + k0, C, rest, nb, l2[0], l2[1], C, lsc, 1, st));
-        // a tensor-core wait that gives up records G2Q_ERR_TIMEOUT in info
-        G2Q_TRY(tc_update2h(A + (k0 + nb) * C + (k0 + nb), C, rest, rest, nb, l2, lsc, C, l2,
-                            lsc, C, 1, 1.f, -1.f, info, st));
-      } else {
-        G2Q_TRY(simt_gemm_f32(A + (k0 + nb) * C + (k0 + nb), C, A + (k0 + nb) * C + k0, C, false,
-                              A + (k0 + nb) * C + k0, C, true, rest, rest, nb, 1.f, -1.f,
-                              G2Q_MASK_LOWER, st));
-      }
+      G2Q_TRY(simt_gemm_f32(A + (k0 + nb) * C + (k0 + nb), C, A + (k0 + nb) * C + k0, C, false,
+                            A + (k0 + nb) * C + k0, C, true, rest, rest, nb, 1.f, -1.f,
+                            G2Q_MASK_LOWER, st));
     }
     if (cudaEventRecord(ev[2 * kb], st) != cudaSuccess) return G2Q_ERR_CUDA;
     // ---- inverse chain (side stream): X_k: = Linv_kk Y_k:, then Y_i: -= L_ik X_k:
     if (cudaStreamWaitEvent(side, ev[2 * kb], 0) != cudaSuccess) return G2Q_ERR_CUDA;
     G2Q_TRY(linv_apply<true>(Y + k0 * C, C, k0 + nb, linv, nb, side));
-    if (rest > 0) {
-      if (use_tc) {
-        G2Q_TRY(split2h(Y + k0 * C, C, k0 + nb, nb, x2[0], x2[1], C, w.xsc, 0, side));
-        G2Q_TRY(tc_update2h(Y + (k0 + nb) * C, C, rest, k0 + nb, nb, l2, lsc, C, x2, w.xsc, C, 0,
-                            1.f, -1.f, info, side));
-      } else {
-        G2Q_TRY(simt_gemm_f32(Y + (k0 + nb) * C, C, A + (k0 + nb) * C + k0, C, false, Y + k0 * C,
-                              C, false, rest, k0 + nb, nb, 1.f, -1.f, G2Q_MASK_FULL, side));
-      }
-    }
+    if (rest > 0)
+      G2Q_TRY(simt_gemm_f32(Y + (k0 + nb) * C, C, A + (k0 + nb) * C + k0, C, false, Y + k0 * C,
+                            C, false, rest, k0 + nb, nb, 1.f, -1.f, G2Q_MASK_FULL, side));
     if (cudaEventRecord(ev[2 * kb + 1], side) != cudaSuccess) return G2Q_ERR_CUDA;
   }
   if (cudaStreamWaitEvent(st, ev[2 * (nblk - 1) + 1], 0) != cudaSuccess) return G2Q_ERR_CUDA;
@@ -659,19 +639,32 @@ static int chol_one(float* U, const float* H, long long C, long long ldh, float 
 }
 
 // ---------------------------------------------------------------------------
-// Batched chain: n factorizations of one size advance panel by panel together,
-// every launch of a step covering all n (grid z, or one panel CTA each), so a
-// layer-batched object (n same-shape linears or experts) costs one chain of
-// launches instead of n.  Workspace as arrays over the batch, each 256-byte
-// aligned: A [n][C][C], Y [n][C][C], diagonal inverses [n][nblk][NB][NB], mean
-// diagonals [n], then fp16: L21^T splits [2 buffers][2][n][NB][C], X_k splits
-// [2][n][NB][C], then the splits' scales: L21 [2 buffers][n][C], X_k [n][C].
+// Tensor-core chain, n factorizations of one size (n = 1 for a single matrix)
+// advancing panel by panel together, every launch of a step covering all n
+// (grid z, or one panel CTA each): a layer-batched object (n same-shape
+// linears or experts) costs one chain of launches instead of n.
+//
+// Look-ahead over three streams.  The critical path (library stream at the
+// device's highest priority): panel k, L_ik = A_ik Linv_k^T, the split of that
+// strip, and the update of column block k+1 alone (the next panel's input).
+// The bulk of the trailing update (rows and columns past block k+1) runs on
+// the caller's stream, so panel k+1 overlaps the bulk update of step k; the
+// inverse chain (X_k: = Linv_k Y_k:, Y_i: -= L_ik X_k:) runs on the side stream.
+// Every element receives the same K = 128 products in the same order as with
+// one update per step (the same 128 x 128 tiles), so the split changes no bit.
+//
+// Workspace as arrays over the batch, each 256-byte aligned: A [n][C][C],
+// Y [n][C][C], diagonal inverses [n][nblk][NB][NB], mean diagonals [n], then
+// fp16: L21^T splits [2 buffers][2][n][NB][C], X_k splits [2][n][NB][C], then
+// the splits' scales: L21 [2 buffers][n][C], X_k [n][C].
 struct CholWsB {
   float *A, *Y, *linv, *mdiag;
   __half *lt, *xk;
   float *lsc, *xsc;
   size_t bytes;
 };
+
+constexpr int kCholArrays = 8;
 
 static CholWsB carve_batched(void* base, long long C, long long n) {
   const long long nblk = (C + NB - 1) / NB;
@@ -713,8 +706,12 @@ static int chol_batched(float* U, const float* H, long long C, long long ldh, lo
   const long long tsz = n * NB * C;                   // one fp16 term of a strip set
   SideState* ss = nullptr;
   G2Q_TRY(side_state(st, (int)nblk, &ss));
-  cudaStream_t side = ss->side;
+  cudaStream_t side = ss->side, crit = ss->crit;
+  // per step k: [4k] strip (or, for the last panel, its inverse) ready, [4k+1]
+  // bulk update done, [4k+2] inverse step done, [4k+3] critical step done
   cudaEvent_t* ev = ss->ev;
+  auto E = [&](long long k, int which) { return ev[4 * k + which]; };
+  cudaEvent_t fork = ev[4 * ss->cap];
   if (info && cudaMemsetAsync(info, 0, n * sizeof(int), st) != cudaSuccess) return G2Q_ERR_CUDA;
   mean_diag_kernel<<<(unsigned)n, 1024, 0, st>>>(H, C, ldh, w.mdiag, C * ldh);
   G2Q_CHECK_LAUNCH();
@@ -727,31 +724,57 @@ static int chol_batched(float* U, const float* H, long long C, long long ldh, lo
                                                           w.Y + z0 * CC, C * ldh, CC);
     G2Q_CHECK_LAUNCH();
   }
+  if (cudaEventRecord(fork, st) != cudaSuccess || cudaStreamWaitEvent(crit, fork, 0) != cudaSuccess)
+    return G2Q_ERR_CUDA;
+  const size_t psmem = panel_smem_floats() * sizeof(float);
   for (long long kb = 0; kb < nblk; ++kb) {
     const long long k0 = kb * NB;
     const int nb = (int)((C - k0) < NB ? (C - k0) : NB);
-    const long long rest = C - k0 - nb;  // > 0 only for full panels (nb == NB)
+    const long long rest = C - k0 - nb;                 // rows past panel kb
+    const long long nbn = rest < NB ? rest : NB;        // width of column block kb + 1
+    const long long rest2 = rest - nbn;                 // rows past column block kb + 1
     float* linv = w.linv + kb * NB * NB;
     __half* lt = w.lt + (kb & 1) * 2 * tsz;
     __half* l2[2] = {lt, lt + tsz};
     float* lsc = w.lsc + (kb & 1) * n * C;
     __half* x2[2] = {w.xk, w.xk + tsz};
-    // ---- factorization: panel, TRSM, split, SYRK for all n
-    panel_kernel<<<(unsigned)n, PANEL_THREADS, panel_smem_floats() * sizeof(float), st>>>(
-        w.A, C, k0, nb, linv, info, CC, lbs);
+    // ---- critical path
+    // column block kb took its last update from the bulk update of step kb - 2
+    // (and from the look-ahead update of step kb - 1, earlier on this stream)
+    if (kb >= 2 && cudaStreamWaitEvent(crit, E(kb - 2, 1), 0) != cudaSuccess)
+      return G2Q_ERR_CUDA;
+    panel_kernel<<<(unsigned)n, PANEL_THREADS, psmem, crit>>>(w.A, C, k0, nb, linv, info, CC,
+                                                              lbs);
     G2Q_CHECK_LAUNCH();
     if (rest > 0) {
-      G2Q_TRY(linv_apply<false>(w.A + (k0 + nb) * C + k0, C, rest, linv, nb, st, n, CC, lbs));
-      if (kb >= 2 && cudaStreamWaitEvent(st, ev[2 * (kb - 2) + 1], 0) != cudaSuccess)
+      G2Q_TRY(linv_apply<false>(w.A + (k0 + nb) * C + k0, C, rest, linv, nb, crit, n, CC, lbs));
+      // the inverse step kb - 2 read this strip buffer (the bulk update kb - 2
+      // did too: waited for above)
+      if (kb >= 2 && cudaStreamWaitEvent(crit, E(kb - 2, 2), 0) != cudaSuccess)
         return G2Q_ERR_CUDA;
       G2Q_TRY(split2h_strips(w.A + (k0 + nb) * C + k0, C, rest, nb, l2[0], l2[1], C, lsc, 1, 1,
-                             0, 0, 0, (int)n, CC, (long long)NB * C, C, st));
-      G2Q_TRY(tc_update2h(w.A + (k0 + nb) * C + (k0 + nb), C, rest, rest, nb, l2, lsc, C, l2,
-                          lsc, C, 1, 1.f, -1.f, info, st, n, NB, CC, C, C));
+                             0, 0, 0, (int)n, CC, (long long)NB * C, C, crit));
     }
-    if (cudaEventRecord(ev[2 * kb], st) != cudaSuccess) return G2Q_ERR_CUDA;
+    if (cudaEventRecord(E(kb, 0), crit) != cudaSuccess) return G2Q_ERR_CUDA;
+    if (rest > 0) {
+      // column block kb + 1 next: the bulk update of step kb - 1 adds into it too
+      if (kb >= 1 && cudaStreamWaitEvent(crit, E(kb - 1, 1), 0) != cudaSuccess)
+        return G2Q_ERR_CUDA;
+      G2Q_TRY(tc_update2h(w.A + (k0 + nb) * C + (k0 + nb), C, rest, nbn, nb, l2, lsc, C, l2, lsc,
+                          C, 1, 1.f, -1.f, info, crit, n, NB, CC, C, C));
+    }
+    if (cudaEventRecord(E(kb, 3), crit) != cudaSuccess) return G2Q_ERR_CUDA;
+    // ---- bulk trailing update (caller's stream): rows and columns past block kb + 1
+    if (rest2 > 0) {
+      if (cudaStreamWaitEvent(st, E(kb, 0), 0) != cudaSuccess) return G2Q_ERR_CUDA;
+      const long long r2 = k0 + nb + nbn;
+      __half* b2[2] = {l2[0] + nbn, l2[1] + nbn};  // the strip from row r2 on
+      G2Q_TRY(tc_update2h(w.A + r2 * C + r2, C, rest2, rest2, nb, b2, lsc + nbn, C, b2,
+                          lsc + nbn, C, 1, 1.f, -1.f, info, st, n, NB, CC, C, C));
+    }
+    if (cudaEventRecord(E(kb, 1), st) != cudaSuccess) return G2Q_ERR_CUDA;
     // ---- inverse chain (side stream)
-    if (cudaStreamWaitEvent(side, ev[2 * kb], 0) != cudaSuccess) return G2Q_ERR_CUDA;
+    if (cudaStreamWaitEvent(side, E(kb, 0), 0) != cudaSuccess) return G2Q_ERR_CUDA;
     G2Q_TRY(linv_apply<true>(w.Y + k0 * C, C, k0 + nb, linv, nb, side, n, CC, lbs));
     if (rest > 0) {
       G2Q_TRY(split2h_strips(w.Y + k0 * C, C, k0 + nb, nb, x2[0], x2[1], C, w.xsc, 0, 1, 0, 0, 0,
@@ -759,9 +782,11 @@ static int chol_batched(float* U, const float* H, long long C, long long ldh, lo
       G2Q_TRY(tc_update2h(w.Y + (k0 + nb) * C, C, rest, k0 + nb, nb, l2, lsc, C, x2, w.xsc, C, 0,
                           1.f, -1.f, info, side, n, NB, CC, C, C));
     }
-    if (cudaEventRecord(ev[2 * kb + 1], side) != cudaSuccess) return G2Q_ERR_CUDA;
+    if (cudaEventRecord(E(kb, 2), side) != cudaSuccess) return G2Q_ERR_CUDA;
   }
-  if (cudaStreamWaitEvent(st, ev[2 * (nblk - 1) + 1], 0) != cudaSuccess) return G2Q_ERR_CUDA;
+  if (cudaStreamWaitEvent(st, E(nblk - 1, 2), 0) != cudaSuccess ||
+      cudaStreamWaitEvent(st, E(nblk - 1, 3), 0) != cudaSuccess)
+    return G2Q_ERR_CUDA;
   extract_u_kernel<<<batch_grid(C, n), 256, 0, st>>>(w.Y, C, U, info, CC, CC);
   G2Q_CHECK_LAUNCH();
   return G2Q_OK;
@@ -770,9 +795,11 @@ static int chol_batched(float* U, const float* H, long long C, long long ldh, lo
 }  // namespace g2q
 
 extern "C" size_t g2q_chol_workspace_bytes(int64_t C) {
-  const int64_t nblk = (C + g2q::NB - 1) / g2q::NB;
-  const size_t b = (size_t)(2 * C * C + nblk * g2q::NB * g2q::NB + 64) * sizeof(float) +
-                   (size_t)6 * g2q::NB * C * sizeof(__half) + (size_t)3 * C * sizeof(float) + 256;
+  if (C <= 0) return 0;
+  // one factorization of the tensor-core chain plus the alignment slack its
+  // arrays may take in a chain of several (k chains: k times this); covers the
+  // CUDA-core chain's layout too
+  const size_t b = g2q::carve_batched(nullptr, C, 1).bytes + g2q::kCholArrays * 256;
   return (b + 255) / 256 * 256;  // a multiple of 256: concurrent lanes take aligned slices
 }
 
@@ -834,24 +861,18 @@ extern "C" int g2q_chol_upper_inverse(float* U, const float* H, int64_t C, int64
   if (workspace_bytes < per) return G2Q_ERR_INVALID_ARG;
   if (precision != 0 && precision != 1) return G2Q_ERR_INVALID_ARG;
   cudaStream_t st = (cudaStream_t)stream;
-  if (precision == 1 && g2q::tc_ok(C) && batch >= 2 && batch <= 65535) {
-    // batched chains of as many factorizations as the workspace holds
+  if (precision == 1 && g2q::tc_ok(C)) {
+    // tensor-core chains of as many factorizations as the workspace holds
     long long n = (long long)(workspace_bytes / per);
     if (n > batch) n = batch;
+    if (n > 65535) n = 65535;
     while (n >= 2 && g2q::carve_batched(nullptr, C, n).bytes > workspace_bytes) --n;
-    if (n >= 2) {
-      for (int64_t b = 0; b < batch; b += n) {
-        const long long m = batch - b < n ? batch - b : n;
-        if (m == 1)
-          G2Q_TRY(g2q::chol_one(U + b * C * C, H + b * C * ldh, C, ldh, damp_percent_host[b],
-                                info ? info + b : nullptr, (float*)workspace, precision, st));
-        else
-          G2Q_TRY(g2q::chol_batched(U + b * C * C, H + b * C * ldh, C, ldh, m,
-                                    damp_percent_host + b, info ? info + b : nullptr, workspace,
-                                    st));
-      }
-      return G2Q_OK;
+    for (int64_t b = 0; b < batch; b += n) {
+      const long long m = batch - b < n ? batch - b : n;
+      G2Q_TRY(g2q::chol_batched(U + b * C * C, H + b * C * ldh, C, ldh, m, damp_percent_host + b,
+                                info ? info + b : nullptr, workspace, st));
     }
+    return G2Q_OK;
   }
   long long lanes = (long long)(workspace_bytes / per);
   if (lanes > g2q::CHOL_LANES) lanes = g2q::CHOL_LANES;
@@ -859,7 +880,7 @@ extern "C" int g2q_chol_upper_inverse(float* U, const float* H, int64_t C, int64
   if (lanes <= 1) {
     for (int64_t b = 0; b < batch; ++b)
       G2Q_TRY(g2q::chol_one(U + b * C * C, H + b * C * ldh, C, ldh, damp_percent_host[b],
-                            info ? info + b : nullptr, (float*)workspace, precision, st));
+                            info ? info + b : nullptr, (float*)workspace, st));
     return G2Q_OK;
   }
   g2q::LaneSet* ls = nullptr;
@@ -872,7 +893,7 @@ extern "C" int g2q_chol_upper_inverse(float* U, const float* H, int64_t C, int64
     const long long l = b % lanes;
     float* ws = (float*)((char*)workspace + l * per);
     status = g2q::chol_one(U + b * C * C, H + b * C * ldh, C, ldh, damp_percent_host[b],
-                           info ? info + b : nullptr, ws, precision, ls->s[l]);
+                           info ? info + b : nullptr, ws, ls->s[l]);
   }
   // join every lane, also after an error, so that no lane's work outlives the call's stream
   for (long long l = 0; l < lanes; ++l) {

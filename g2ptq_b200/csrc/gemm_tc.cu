@@ -1730,17 +1730,7 @@ __global__ void __launch_bounds__(256) split2h_kernel(const float* __restrict__ 
   }
 }
 
-int split2h(const float* src, long long lds, long long n, int K, __half* hi, __half* lo,
-            long long ldd, float* scale, int transpose, cudaStream_t st) {
-  if (n <= 0 || K <= 0) return G2Q_OK;
-  if (K > 128) return G2Q_ERR_INVALID_ARG;
-  split2h_kernel<<<cdiv(n, 32), dim3(32, 8), 0, st>>>(src, lds, n, K, hi, lo, ldd, scale,
-                                                      transpose, 0, 0, 0, 0, 0, 0);
-  G2Q_CHECK_LAUNCH();
-  return G2Q_OK;
-}
-
-// split2h over ny x nz strips in one launch (strip (y, z) at the given strides).
+// The split of ny x nz strips in one launch (strip (y, z) at the given strides).
 int split2h_strips(const float* src, long long lds, long long n, int K, __half* hi, __half* lo,
                    long long ldd, float* scale, int transpose, int ny, long long src_by,
                    long long dst_by, long long sc_by, int nz, long long src_bz,
