@@ -771,6 +771,20 @@ def cpu_sample():
     return step, parts, time.perf_counter() - wall0, threads
 
 
+def cpu_warmup():
+    """An untimed warm-up step of the CPU arm: the same torch operations at
+    C = 1024 (thread pools and allocator warmed in well under a second; the
+    full-size sample of a timed step takes tens of seconds)."""
+    import torch
+    from oracle import torch_port as tp
+    cpu_threads()
+    g = torch.Generator().manual_seed(1)
+    X = torch.randn(1, 2048, 1024, generator=g).to(torch.bfloat16)
+    H, _ = tp.add_batch(torch.zeros(1024, 1024), 0, X)
+    W = (torch.randn(1, 256, 1024, generator=g) * 0.02).to(torch.bfloat16)
+    tp.fasterquant(W, H[None], BITS, True, GROUPSIZE, True, True, PERCDAMP, BLOCKSIZE)
+
+
 def _sample_text(parts, wall):
     p = ", ".join(f"{k} {v:.3f} s" for k, v in parts.items())
     return (f"reference torch ops on the host (oracle/torch_port.py): one 2048-token add_batch "
@@ -791,7 +805,7 @@ def reference(args):
     if rank != 0:
         return
     for _ in range(args.warmup):
-        cpu_sample()
+        cpu_warmup()
     vals, parts, wall, threads = [], None, 0.0, 1
     for _ in range(args.steps):
         s, parts, wall, threads = cpu_sample()
