@@ -152,9 +152,22 @@ class GPTQ(_engine.StagingMixin):
         ops.prepare_hessian(H, W)
         perm = None
         if actorder:
-            perm, _ = _engine.act_order_perm(ops.mean_diag(H))
-            W = ops.permute_cols(W, perm)
-            H = ops.permute_sym(H, perm)
+            if factor_in is not None:
+                # the owner's Hessian is bit-identical: so is its permutation,
+                # and only the owner factors the permuted Hessian
+                stream = torch.cuda.current_stream(self.dev)
+                stream.wait_event(factor_in["perm_event"])
+                perm = factor_in["perm"]
+                perm.record_stream(stream)
+                W = ops.permute_cols(W, perm)
+            else:
+                perm, _ = _engine.act_order_perm(ops.mean_diag(H))
+                if factor_out is not None:
+                    ev = torch.cuda.Event()
+                    ev.record(torch.cuda.current_stream(self.dev))
+                    factor_out.update(perm=perm, perm_event=ev)
+                W = ops.permute_cols(W, perm)
+                H = ops.permute_sym(H, perm)
         clip, clip_hd = _engine.dynamic_clip(q0, H_diag, perm, B * R, C) if dynamic else (None,
                                                                                           None)
         if factor_in is not None:

@@ -547,3 +547,20 @@ def test_moe_experts_layer_batched_vs_oracle():
                                    proxy_loss(W[e:e + 1], Qo[e:e + 1], Hd[e:e + 1].cpu().numpy()),
                                    rtol=1e-3)
         assert layers[e]._export_qparams["weight_packed"].shape[0] == R
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.int8])
+@pytest.mark.parametrize("nl,rows,C", [(1, 37, 4096), (3, 16, 768), (2, 5, 600), (1, 3, 14336)])
+def test_permute_cols_matches_indexing(dtype, nl, rows, C):
+    """Act-order column permutation and its inverse, exact against indexing:
+    the shared-memory staged kernel (C a multiple of 16) and the direct one."""
+    g = torch.Generator(device=DEV).manual_seed(C + rows)
+    if dtype == torch.float32:
+        src = torch.randn(nl, rows, C, device=DEV, generator=g)
+    else:
+        src = torch.randint(-8, 8, (nl, rows, C), device=DEV, generator=g).to(torch.int8)
+    perm = torch.randperm(C, device=DEV, generator=g)
+    fwd = ops.permute_cols(src, perm)
+    assert torch.equal(fwd, src[:, :, perm])
+    back = ops.permute_cols(fwd, perm, inverse=True)
+    assert torch.equal(back, src)
