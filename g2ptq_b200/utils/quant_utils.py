@@ -6,6 +6,7 @@ with every computation done by the sm_100a kernels of ``libg2ptq_b200``.
 Tensors must live on a CUDA device.
 """
 
+import collections
 import copy
 
 import torch
@@ -35,6 +36,11 @@ def sym_quant(x, scale, maxq):
 
 def sym_dequant(q, scale):
     return scale * q
+
+
+# value types __deepcopy__ shares as they are / rebuilds as containers
+_PLAIN = (bool, int, float, str, type(None))
+_CONTAINERS = (dict, collections.OrderedDict, set)
 
 
 class WeightQuantizer(torch.nn.Module):
@@ -76,21 +82,25 @@ class WeightQuantizer(torch.nn.Module):
         memo[id(self)] = new
         d = {}
         for k, v in self.__dict__.items():
-            if k == "_status":
+            t = type(v)
+            if t in _PLAIN:
+                pass
+            elif k == "_status":
                 v = None
+            elif t in _CONTAINERS:
+                if not v:
+                    v = t()
+                elif t is set:
+                    v = copy.deepcopy(v, memo)
+                else:
+                    v = t((kk, vv.clone() if isinstance(vv, torch.Tensor)
+                           else copy.deepcopy(vv, memo)) for kk, vv in v.items())
             elif isinstance(v, torch.Tensor):
                 v = v.clone()
-            elif isinstance(v, (dict, set)):
-                if v:
-                    v = (type(v)((kk, vv.clone() if isinstance(vv, torch.Tensor)
-                                  else copy.deepcopy(vv, memo)) for kk, vv in v.items())
-                         if isinstance(v, dict) else copy.deepcopy(v, memo))
-                else:
-                    v = type(v)()
-            elif not isinstance(v, (bool, int, float, str, type(None))):
+            else:
                 v = copy.deepcopy(v, memo)
             d[k] = v
-        new.__dict__.update(d)
+        new.__dict__ = d
         return new
 
     def status_tensor(self, device):
