@@ -34,6 +34,7 @@ import torch.distributed as dist
 from .common_utils import (broadcast_quantized_param, build_chunk_specs, make_group_quantizers,
                            partition_layers)
 from . import gptq_utils, g2ptq_utils
+from .. import ops
 from ..utils.quant_utils import WeightQuantizer
 
 SEQUENTIAL_GROUPS = (("self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj"),
@@ -93,8 +94,8 @@ def _synthetic_g2ptq_inputs(cal, names, subset, stage_inputs, layer_idx):
             t = x.shape[0] * x.shape[1]
             go = (torch.randn(t, rows, device=x.device, generator=g) * cal.grad_std).to(
                 torch.bfloat16)
-            gf = go.float()
-            sal[name].append((gf * gf).reshape(t, G, rows // G).mean(-1))
+            # what SaliencyCache.grad_hook computes from the output gradient
+            sal[name].append(ops.saliency(go, G))
             acc += (go.T @ x.reshape(t, -1)).float() / t
         grad[name] = acc / max(1, len(stage_inputs))
     return sal, grad
