@@ -405,9 +405,11 @@ def native(args):
     gram_ms = timer.total_ms() / args.steps
     gram_tflops = timer.flops / args.steps / (gram_ms * 1e-3) / 1e12 if gram_ms > 0 else 0.0
 
-    e2e = None
+    e2e = e2e_dev = None
     if not args.no_e2e:
         e2e = native_e2e(torch, dist, args, layers, world, rank, dev, n_local, acts, g2)
+        e2e_dev = native_e2e(torch, dist, args, layers, world, rank, dev, n_local, acts, g2,
+                             host_inputs=False)
     del acts
     hbm, bf16, peak_kind = load_peaks()
     value = len(LINEARS) / (ms * 1e-3)
@@ -447,6 +449,9 @@ def native(args):
     }
     if e2e is not None:
         line["e2e"] = e2e
+        # the same API path with the activations already on the device (where a
+        # calibration forward produces them) and the results read back
+        line["e2e_activations_on_device"] = e2e_dev
     if rank == 0 and world == 1 and not args.no_cpu_baseline and args.method == "gptq":
         line["cpu_baseline"] = cpu_baseline()
     if rank == 0:
@@ -456,19 +461,25 @@ def native(args):
         dist.destroy_process_group()
 
 
-def native_e2e(torch, dist, args, layers, world, rank, dev, n_local, dev_acts, g2=None):
+def native_e2e(torch, dist, args, layers, world, rank, dev, n_local, dev_acts, g2=None,
+               host_inputs=True):
     """Same steps through the public API with host-resident inputs: every step
     copies its activations from pinned host memory and reads the quantized
     weights and packed codes back to the host.  The copies stream through a ring
     of sequence buffers on a side stream (as the reference's prefetch_generator
     overlaps its H2D copies), running ahead into the next step's sequences while
-    the current step factors and compensates."""
-    host = {grp: torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
-            for grp, x in dev_acts.items()}
+    the current step factors and compensates.  ``host_inputs=False``: the
+    activations stay where a calibration forward leaves them, on the device,
+    and only the results cross to the host."""
+    if not host_inputs:
+        def device_feed(s):
+            return {grp: x[s:s + 1] for grp, x in dev_acts.items()}
+    host = ({grp: torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
+             for grp, x in dev_acts.items()} if host_inputs else {})
     for grp in host:
         host[grp].copy_(dev_acts[grp])
     side = torch.cuda.Stream(device=dev)
-    ring = max(2, min(n_local, E2E_RING))
+    ring = max(2, min(n_local, E2E_RING)) if host_inputs else 0
     bufs = [{grp: torch.empty(1, args.seq_len, C, dtype=torch.bfloat16, device=dev)
              for grp, C in GROUP_COLS.items()} for _ in range(ring)]
     ready = [torch.cuda.Event() for _ in range(ring)]
@@ -500,11 +511,12 @@ def native_e2e(torch, dist, args, layers, world, rank, dev, n_local, dev_acts, g
         return bufs[g % ring]
 
     def step():
-        one_step(torch, layers, feed, n_local, world, rank, dist, args.method, g2,
-                 multi=args.multi)
-        # free the last buffer and keep the copies running into the next step
-        free_ev[(state["consumed"] - 1) % ring].record()
-        prefetch_upto(state["consumed"] + ring)
+        one_step(torch, layers, feed if host_inputs else device_feed, n_local, world, rank,
+                 dist, args.method, g2, multi=args.multi)
+        if host_inputs:
+            # free the last buffer and keep the copies running into the next step
+            free_ev[(state["consumed"] - 1) % ring].record()
+            prefetch_upto(state["consumed"] + ring)
         d2h = 0
         for name, rows, cols, _ in LINEARS:
             outs[name].copy_(layers[name].weight.data, non_blocking=True)
