@@ -171,17 +171,36 @@ def _init(rank, world, port):
     collectives.unpack_upper = cpu_unpack_upper
 
 
+class _Reply:
+    """A rank's channel to the parent: ``put`` hands over the rank's result
+    and returns once the parent holds every rank's result.  Tensors cross
+    the queue as shared file descriptors that the sending process must keep
+    open until the parent has rebuilt them, so no rank may exit before."""
+
+    def __init__(self, q, done):
+        self.q, self.done = q, done
+
+    def put(self, item):
+        self.q.put(item)
+        self.done.wait(120)
+
+
 def _run_ranks(target, world=2):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
+    done = ctx.Event()
     port = _free_port()
-    procs = [ctx.Process(target=target, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=target, args=(r, world, port, _Reply(q, done)))
+             for r in range(world)]
     for p in procs:
         p.start()
     res = {}
-    for _ in range(world):
-        r, payload = q.get(timeout=120)
-        res[r] = payload
+    try:
+        for _ in range(world):
+            r, payload = q.get(timeout=120)
+            res[r] = payload
+    finally:
+        done.set()
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
