@@ -288,6 +288,23 @@ def test_broadcast_quantized_param_two_ranks():
         assert qp["weight_shape"].tolist() == [17, 24]
 
 
+def test_broadcast_quantized_param_with_an_idle_rank():
+    """Three ranks for two objects (one LPT bin stays empty, as with seven
+    linears on eight GPUs): the rank that owns nothing still ends with every
+    owner's weights and export buffers."""
+    res = _run_ranks(_rank_broadcast, world=3)
+    for r in (0, 1, 2):
+        out, n_staged = res[r]
+        assert n_staged == 3
+        for k in range(2):
+            w, qp = out[0][k]
+            assert torch.all(w == 10 + k)
+            assert torch.all(qp["weight_packed"] == 7 + k)
+        w, qp = out[1][0]
+        assert torch.all(w == 100)
+        assert qp["weight_shape"].tolist() == [17, 24]
+
+
 def _rank_gather(rank, world, port, q):
     _init(rank, world, port)
     from g2ptq_b200.gptq_utils import collectives
